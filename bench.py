@@ -1,0 +1,488 @@
+#!/usr/bin/env python
+"""Benchmark of the light-vllm hot path on B200.
+
+Workload: one paged-attention decode step of the
+Qwen2.5-7B head geometry -- 64 sequences, one query token each, contexts
+uniform in [512, 4096], 28 query / 4 KV heads, head_dim 128, bf16 K/V pages
+N(0, 1), block_size 16, block tables carved from a random permutation of a
+40,000-block pool, softmax scale 1/sqrt(128).  A step is the K/V write of the
+64 new tokens plus the attention over every page.
+
+Reported (one JSON line on rank 0):
+  value      attention HBM GB/s over the whole job: algorithmic bytes (K and V
+             pages read, Q read, O written, block tables, new K/V rows written)
+             / device time of K steps replayed back to back from a CUDA graph,
+             inputs resident in HBM.  The 302 MB of K/V per step exceed the
+             126 MB L2, so no flush is needed between steps.
+  e2e        the same bytes / time through the public API per step:
+             H2D of q/k/v from pinned host memory, backend.create(cache,
+             metadata) (block-table validation + one staged metadata copy),
+             forward(), D2H of the output.
+  roofline   the decode-attention launch (split-context kernel + merge) timed
+             alone with CUDA events; peak = measured HBM copy bandwidth.
+  cpu_baseline  the CPU oracle (a restatement of the reference's
+             TorchPagedAttention) on this host's cores over the same batch.
+  awq        (detail) the W4A16 kernel on config 1 and model-scale shapes.
+
+Multi-GPU (torchrun): attention shards over requests with no exchange, so each
+rank runs its own copy of the batch ("weak" scaling, replicas); value sums the
+ranks' bytes over the slowest rank's time.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "decode tok/s + AWQ GEMM/attn HBM GB/s (% roofline) at 1/2/4/8 B200 vs host CPU"
+UNIT = "GB/s"
+CFG = dict(num_seqs=64, ctx_lo=512, ctx_hi=4096, hq=28, hkv=4, d=128, block_size=16, num_blocks=40000,
+           seed=20261201)
+WORKLOAD = ("paged-attention decode (BASELINE config 2): 64 seqs x 1 query, ctx U[512,4096], "
+            "28q/4kv heads, head_dim 128, bf16 K/V, block 16, 40k-block pool")
+
+
+def measured_peaks() -> dict:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.is_file():
+        data = json.loads(path.read_text())
+        return {"hbm_gbs": float(data["hbm_gbs"]), "bf16_tflops": float(data["bf16_tflops"]),
+                "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+# ----------------------------------------------------------------------------
+# workload
+# ----------------------------------------------------------------------------
+def make_workload(torch, device):
+    from light_vllm_b200.kv_cache import (
+        AttentionLayerSpec,
+        ModelKVCacheSpec,
+        PagedAttentionMetadata,
+        PagedKVCache,
+        PagedKVCacheConfig,
+        linear_query_layout,
+    )
+
+    c = CFG
+    gen = torch.Generator().manual_seed(c["seed"])
+    ctx = torch.randint(c["ctx_lo"], c["ctx_hi"] + 1, (c["num_seqs"],), generator=gen).tolist()
+    perm = torch.randperm(c["num_blocks"], generator=gen).tolist()
+    tables, off = [], 0
+    for n_ctx in ctx:
+        n = -(-n_ctx // c["block_size"])
+        tables.append(tuple(perm[off:off + n]))
+        off += n
+    md = PagedAttentionMetadata(block_tables=tuple(tables), num_computed_tokens=tuple(x - 1 for x in ctx),
+                                query_layouts=tuple(linear_query_layout(1) for _ in ctx))
+    spec = ModelKVCacheSpec((AttentionLayerSpec("layer0", c["hq"], c["hkv"], c["d"]),))
+    cache = PagedKVCache(spec, PagedKVCacheConfig(c["num_blocks"], c["block_size"], dtype=torch.bfloat16,
+                                                  device=device))
+    torch.manual_seed(c["seed"])
+    layer = cache.layer("layer0")
+    layer.keys.normal_()
+    layer.values.normal_()
+    q = torch.randn(c["num_seqs"], c["hq"], c["d"], device=device, dtype=torch.bfloat16)
+    k = torch.randn(c["num_seqs"], c["hkv"], c["d"], device=device, dtype=torch.bfloat16)
+    v = torch.randn(c["num_seqs"], c["hkv"], c["d"], device=device, dtype=torch.bfloat16)
+    return cache, md, q, k, v, ctx
+
+
+def algorithmic_bytes(ctx) -> dict:
+    c = CFG
+    kv_read = sum(ctx) * c["hkv"] * c["d"] * 2 * 2
+    q_bytes = c["num_seqs"] * c["hq"] * c["d"] * 2
+    tables = sum(-(-x // c["block_size"]) for x in ctx) * 4
+    attention = kv_read + 2 * q_bytes + tables
+    kv_write = c["num_seqs"] * c["hkv"] * c["d"] * 2 * 2 * 2  # read new rows + write slots, K and V
+    return {"attention": attention, "step": attention + kv_write, "kv_read": kv_read}
+
+
+# ----------------------------------------------------------------------------
+# clocks
+# ----------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu_index = gpu_index
+        self.proc = None
+        self.path = Path(os.environ.get("TMPDIR", "/tmp")) / f"lvb_clocks_{os.getpid()}.csv"
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu_index}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.2)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        if self.proc is None or not self.path.is_file():
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        for line in self.path.read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), parts[5:9]))
+            except ValueError:
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        reasons = sorted({n for _, _, flags in rows for n, f in zip(names, flags) if f.lower().startswith("active")})
+        loaded = sorted(r[0] for r in rows)
+        upper = loaded[len(loaded) // 2:] or loaded
+        return {"sm_mhz": statistics.median(upper), "sm_max_mhz": max(r[1] for r in rows),
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ----------------------------------------------------------------------------
+# timing helpers
+# ----------------------------------------------------------------------------
+def time_graph(torch, graph, steps: int, warmup: int, dist=None) -> float:
+    """Average device ms per replay, max over ranks."""
+
+    for _ in range(warmup):
+        graph.replay()
+    stream = torch.cuda.current_stream()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    start.record(stream)
+    for _ in range(steps):
+        graph.replay()
+    end.record(stream)
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(end) / steps
+    if dist is not None:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms
+
+
+def capture(torch, fn):
+    fn()  # eager warm-up: kernel attributes are set outside the capture
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        fn()
+    torch.cuda.synchronize()
+    return graph
+
+
+# ----------------------------------------------------------------------------
+# AWQ detail
+# ----------------------------------------------------------------------------
+def awq_detail(torch, peaks, steps: int) -> list[dict]:
+    import numpy as np
+
+    from light_vllm_b200.awq import B200AWQScheme
+    from oracle import awq as oawq  # input generator only (packing of random codes)
+
+    shapes = [
+        ("config1 0.5B up-proj", 16, 896, 4864, 128),
+        ("7B gate_up", 1, 3584, 37888, 128),
+        ("7B gate_up", 16, 3584, 37888, 128),
+        ("7B gate_up", 64, 3584, 37888, 128),
+        ("7B down", 16, 18944, 3584, 128),
+        ("7B gate_up prefill", 2048, 3584, 37888, 128),
+    ]
+    out = []
+    l2 = 126 * 1024 * 1024
+    for name, m, k, n, g in shapes:
+        qweight, qzeros, scales = oawq.random_checkpoint(k, n, g, seed=m + k + n)
+        weight_bytes = qweight.nbytes + qzeros.nbytes + scales.nbytes
+        copies = max(1, math.ceil(2 * l2 / weight_bytes)) if m <= 256 else 1
+        dev = torch.device("cuda")
+        base = [torch.from_numpy(a).to(dev) for a in (qweight, qzeros, scales)]
+        ops = []
+        for i in range(copies):
+            ts = [t.clone() for t in base] if i else base
+            ops.append(B200AWQScheme().prepare(*ts, g, None))
+        x = torch.randn(m, k, dtype=torch.float16, device=dev)
+
+        def run():
+            for op in ops:
+                op(x)
+
+        graph = capture(torch, run)
+        ms = time_graph(torch, graph, max(3, steps // 4), 2) / copies
+        io_bytes = weight_bytes + m * k * 2 + m * n * 2
+        flops = 2.0 * m * k * n
+        gbs = io_bytes / (ms * 1e-3) / 1e9
+        tflops = flops / (ms * 1e-3) / 1e12
+        out.append({"shape": name, "m": m, "k": k, "n": n, "group": g, "us_per_call": round(ms * 1e3, 2),
+                    "gbs": round(gbs, 1), "tflops": round(tflops, 2),
+                    "hbm_frac": round(gbs / peaks["hbm_gbs"], 3),
+                    "tensor_frac": round(tflops / peaks["bf16_tflops"], 3),
+                    "rotating_copies": copies})
+        del ops, graph, base
+        torch.cuda.empty_cache()
+    return out
+
+
+# ----------------------------------------------------------------------------
+# CPU baseline (the oracle restating the reference's Torch path)
+# ----------------------------------------------------------------------------
+def cpu_baseline(torch, cache, md, q, k, v, ctx, budget_s: float = 20.0) -> dict:
+    from oracle import paged_attention as opa
+
+    layer = cache.layer("layer0")
+    kc, vc = layer.keys.cpu(), layer.values.cpu()
+    qc, kk, vv = q.cpu(), k.cpu(), v.cpu()
+    threads = torch.get_num_threads()
+    scale = 1.0 / math.sqrt(CFG["d"])
+    n_total = len(ctx)
+    # Grow the sample until it takes a few seconds (bounded by the budget).
+    n = 1
+    elapsed = 0.0
+    while True:
+        tables = md.block_tables[:n]
+        t0 = time.perf_counter()
+        opa.attend(qc[:n], kk[:n], vv[:n], kc, vc, tables, md.num_computed_tokens[:n],
+                   [(-1,)] * n, scale=scale)
+        elapsed = time.perf_counter() - t0
+        if n >= n_total or elapsed * (2 * n if 2 * n <= n_total else n_total) / n > budget_s or elapsed > 3.0:
+            break
+        n = min(n_total, 2 * n)
+    sample_ctx = ctx[:n]
+    c = CFG
+    nbytes = (sum(sample_ctx) * c["hkv"] * c["d"] * 4 + n * c["hq"] * c["d"] * 4
+              + sum(-(-x // c["block_size"]) for x in sample_ctx) * 4 + n * c["hkv"] * c["d"] * 8)
+    return {"value": round(nbytes / elapsed / 1e9, 4), "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"first {n} of {n_total} sequences ({sum(sample_ctx)} context tokens), one step, "
+                      f"{elapsed:.2f} s"}
+
+
+# ----------------------------------------------------------------------------
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    ap.add_argument("--no-awq", action="store_true", help="skip the AWQ detail measurements")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        return reference_arm(torch, args, rank, world)
+
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as tdist
+
+        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+        dist = tdist
+
+    from light_vllm_b200 import _native
+    from light_vllm_b200.paged_attention import B200PagedAttentionBackend
+
+    peaks = measured_peaks()
+    cache, md, q, k, v, ctx = make_workload(torch, device)
+    nbytes = algorithmic_bytes(ctx)
+    scale = 1.0 / math.sqrt(CFG["d"])
+    backend = B200PagedAttentionBackend()
+    step_ctx = backend.create(cache, md)
+    out = torch.empty_like(q)
+
+    step_graph = capture(torch, lambda: step_ctx.launch("layer0", q, k, v, scale=scale, out=out))
+    attn_graph = capture(torch, lambda: step_ctx.launch("layer0", q, k, v, scale=scale, out=out,
+                                                        write_kv=False))
+
+    gpu_index = int(os.environ.get("CUDA_VISIBLE_DEVICES", str(local_rank)).split(",")[local_rank]) \
+        if os.environ.get("CUDA_VISIBLE_DEVICES") else local_rank
+    with ClockSampler(gpu_index) as clocks:
+        step_ms = time_graph(torch, step_graph, args.steps, args.warmup, dist)
+        attn_ms = time_graph(torch, attn_graph, args.steps, args.warmup, dist)
+    clock_summary = clocks.summary()
+
+    # End to end through the public API with host buffers.
+    pinned = [t.cpu().pin_memory() for t in (q, k, v)]
+    host_out = torch.empty(q.shape, dtype=q.dtype, pin_memory=True)
+    staged = [torch.empty_like(t) for t in (q, k, v)]
+    stream = torch.cuda.current_stream()
+
+    def e2e_step():
+        for dst, src in zip(staged, pinned):
+            dst.copy_(src, non_blocking=True)
+        o = backend.create(cache, md).forward("layer0", *staged, scale=scale)
+        host_out.copy_(o, non_blocking=True)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    e2e_steps = max(3, args.steps // 5)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = ev0.elapsed_time(ev1) / e2e_steps
+    if dist is not None:
+        t = torch.tensor([e2e_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    dev_err = _native.device_error()
+    if dev_err:
+        raise RuntimeError(f"device error word {dev_err:#x}")
+
+    meta_bytes = 4 * (sum(len(t) for t in md.block_tables) + 3 * len(ctx) + 1)
+    h2d = sum(t.numel() * t.element_size() for t in (q, k, v)) + meta_bytes
+    d2h = q.numel() * q.element_size()
+    value = world * nbytes["step"] / (step_ms * 1e-3) / 1e9
+    attn_gbs = nbytes["attention"] / (attn_ms * 1e-3) / 1e9
+    e2e_value = world * nbytes["step"] / (e2e_ms * 1e-3) / 1e9
+
+    result = {
+        "metric": METRIC,
+        "value": round(value, 1),
+        "unit": UNIT,
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(step_ms, 5),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) K/V pages, random-permutation block tables)",
+        "config": {
+            "workload": WORKLOAD,
+            "global_batch": CFG["num_seqs"] * world,
+            "parallelism": f"replicas x{world} (attention shards over requests, no collective)",
+            "l2": "no flush: 302 MB of K/V pages per step exceed the 126 MB L2",
+            "timing": "CUDA graph replays, CUDA events on the launching stream, max over ranks",
+            "algorithmic_bytes_per_step": nbytes["step"],
+            "decode_tokens_per_step": CFG["num_seqs"] * world,
+            "decode_attention_tok_s": round(world * CFG["num_seqs"] / (step_ms * 1e-3), 1),
+        },
+        "roofline": {
+            "bound": "hbm",
+            "achieved": round(attn_gbs, 1),
+            "peak": peaks["hbm_gbs"],
+            "unit": "GB/s",
+            "frac": round(attn_gbs / peaks["hbm_gbs"], 4),
+            "traffic": None,
+            "kernel": "paged_decode_kernel + paged_merge_kernel (one lvb_paged_attention call)",
+            "peak_source": peaks["source"],
+            "algorithmic_bytes_per_launch": nbytes["attention"],
+            "launch_us": round(attn_ms * 1e3, 2),
+        },
+        "e2e": {"value": round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4),
+                "path": "backend.create(cache, metadata).forward(...) with pinned host q/k/v and output"},
+        "gpu_launches": 3 * args.steps,
+        "clocks": clock_summary,
+    }
+    if rank == 0 and world == 1:
+        result["cpu_baseline"] = cpu_baseline(torch, cache, md, q, k, v, ctx)
+        if not args.no_awq:
+            del cache
+            torch.cuda.empty_cache()
+            result["awq"] = awq_detail(torch, peaks, args.steps)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+    return 0
+
+
+def reference_arm(torch, args, rank: int, world: int) -> int:
+    """The reference's CPU implementation of the path (the oracle port of
+    TorchPagedAttention) on this host's cores, same workload and metric."""
+
+    if rank != 0:
+        return 0
+    torch.set_num_threads(os.cpu_count() or 1)
+    cache, md, q, k, v, ctx = make_workload(torch, torch.device("cuda", 0) if torch.cuda.is_available()
+                                            else torch.device("cpu"))
+    from oracle import paged_attention as opa
+
+    layer = cache.layer("layer0")
+    kc, vc = layer.keys.cpu(), layer.values.cpu()
+    qc, kk, vv = q.cpu(), k.cpu(), v.cpu()
+    n = len(ctx)
+    scale = 1.0 / math.sqrt(CFG["d"])
+    # Each step covers a bounded slice of the batch so the run ends in minutes.
+    per_step = 8
+    times = []
+    total_bytes = 0
+    steps = args.warmup + args.steps
+    for i in range(steps):
+        lo = (i * per_step) % n
+        sl = slice(lo, min(n, lo + per_step))
+        sample_ctx = ctx[sl]
+        t0 = time.perf_counter()
+        opa.attend(qc[sl], kk[sl], vv[sl], kc, vc, md.block_tables[sl], md.num_computed_tokens[sl],
+                   [(-1,)] * len(sample_ctx), scale=scale)
+        dt = time.perf_counter() - t0
+        if i >= args.warmup:
+            times.append(dt)
+            c = CFG
+            total_bytes += (sum(sample_ctx) * c["hkv"] * c["d"] * 4 + len(sample_ctx) * c["hq"] * c["d"] * 4
+                            + sum(-(-x // c["block_size"]) for x in sample_ctx) * 4
+                            + len(sample_ctx) * c["hkv"] * c["d"] * 8)
+    secs = sum(times)
+    value = total_bytes / secs / 1e9
+    result = {
+        "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(secs / len(times) * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "impl": "reference",
+        "config": {"workload": WORKLOAD, "global_batch": CFG["num_seqs"], "parallelism": "host CPU",
+                   "step": f"{per_step} sequences of the batch per step (bounded sample)"},
+        "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": torch.get_num_threads(),
+                         "kind": "port",
+                         "sample": f"{per_step} of {n} sequences per step, {args.steps} timed steps"},
+        "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(result), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

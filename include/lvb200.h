@@ -1,0 +1,164 @@
+/*
+ * lvb200.h -- C ABI of the B200 (sm_100a) hot-path library for light-vllm.
+ *
+ * The library implements the two GPU pieces of light-vllm's decode/prefill
+ * path behind plain C entry points: the AutoAWQ W4A16 linear (the work of the
+ * reference's `awq_gemm` / `awq_dequantize` extension) and the paged K/V write
+ * plus paged attention (the work of the reference's Triton backend).  Every
+ * entry point takes raw device pointers, element counts, strides and a CUDA
+ * stream, enqueues work on that stream and returns a status code; none of them
+ * synchronises the device or allocates device memory.  No torch types appear
+ * here: any FFI (ctypes, cffi, pybind11, a C++ host) can bind it.
+ *
+ * Reference paths below are relative to the light-vllm repository.
+ *
+ * Data types: `uint16_t` buffers hold IEEE fp16 or bf16 bit patterns as named
+ * by a `dtype` argument (LVB_DTYPE_F16 / LVB_DTYPE_BF16).  AWQ activations,
+ * scales, bias and outputs are always fp16 (the reference hard-wires fp16 for
+ * AWQ: modeling/quantization/awq.py:673-675, cuda_awq.py:65-66).
+ *
+ * Errors: a non-zero status means nothing was enqueued.  `lvb_last_error()`
+ * returns a thread-local message for the most recent failure on the calling
+ * thread.  Kernels never trap: a device-side wait that exceeds its time limit
+ * records a code that `lvb_device_error()` returns (and clears).
+ */
+#ifndef LVB200_H_
+#define LVB200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define LVB_API __attribute__((visibility("default")))
+#else
+#define LVB_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st *lvb_stream_t; /* same handle as cudaStream_t */
+
+enum lvb_status {
+  LVB_OK = 0,
+  LVB_ERR_INVALID = 1,     /* bad shape, size, alignment or pointer (ValueError) */
+  LVB_ERR_UNSUPPORTED = 2, /* valid request outside what the kernels cover   */
+  LVB_ERR_CUDA = 3,        /* a CUDA runtime call failed (RuntimeError)      */
+  LVB_ERR_WORKSPACE = 4    /* caller's workspace smaller than required       */
+};
+
+enum lvb_dtype { LVB_DTYPE_F16 = 0, LVB_DTYPE_BF16 = 1 };
+
+/* Library identification: ABI version (bumped on any signature change). */
+LVB_API int lvb_abi_version(void);
+
+/* Message for the last non-zero status returned on this thread. */
+LVB_API const char *lvb_last_error(void);
+
+/* Device-side error word for the current device (0 = none), cleared on read.
+ * Bit 0: a pipeline wait timed out; bit 1: an index check failed.
+ * Synchronises the current device. */
+LVB_API int lvb_device_error(uint32_t *error_out);
+
+/* ------------------------------------------------------------------------ */
+/* AWQ W4A16 linear                                                          */
+/* ------------------------------------------------------------------------ */
+
+/* Bytes of workspace `lvb_awq_linear` needs for an m x k x n call on the
+ * current device: split-K reduction semaphores followed by fp32 partial
+ * tiles.  A workspace must be zero-filled once before its first use; every
+ * call leaves its semaphores zero again, so one buffer serves all later calls
+ * of the same or smaller size.  Replaces the fp16 split partial planes that
+ * `awq_gemm` allocates per call
+ * (modeling/quantization/csrc/awq/gemm_kernels.cu:456-457). */
+LVB_API size_t lvb_awq_workspace_bytes(int64_t m, int64_t k, int64_t n, int64_t group_size);
+
+/* y[m, n] = x[m, :k] @ W + bias, W[k, n] = fp16(q - z) * s dequantised on the
+ * fly from the AutoAWQ GEMM layout (qweight int32 [k, n/8], qzeros int32
+ * [k/group, n/8], scales fp16 [k/group, n]; nibble p of a word holds column
+ * 8j + (0,2,4,6,1,3,5,7)[p]).  fp32 accumulation on tcgen05 tensor cores.
+ * x and y are row-major with row strides k and n; `bias` may be NULL.
+ * Requirements: n % 32 == 0, k % 8 == 0, group_size % 8 == 0,
+ * k % group_size == 0, 16-byte aligned x / qweight / scales / workspace.  Replaces `awq_gemm`
+ * (csrc/awq/bindings.cpp:10-13, gemm_kernels.cu:444-501) together with the
+ * M>255 dequantise + cuBLAS path and the bias add of
+ * `CudaAWQOperation.__call__` (cuda_awq.py:96-122). */
+LVB_API int lvb_awq_linear(const uint16_t *x, const int32_t *qweight, const int32_t *qzeros,
+                   const uint16_t *scales, const uint16_t *bias, uint16_t *y, int64_t m,
+                   int64_t k, int64_t n, int64_t group_size, void *workspace,
+                   size_t workspace_bytes, lvb_stream_t stream);
+
+/* w[k, n] = fp16(q - z) * s, the full fp16 weight.  Replaces `awq_dequantize`
+ * (csrc/awq/bindings.cpp:10-13, gemm_kernels.cu:391-439). */
+LVB_API int lvb_awq_dequantize(const int32_t *qweight, const int32_t *qzeros, const uint16_t *scales,
+                       uint16_t *w, int64_t k, int64_t n, int64_t group_size,
+                       lvb_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
+/* Paged K/V cache                                                           */
+/* ------------------------------------------------------------------------ */
+/* Cache layout (runtime/execution/paged_cache.py:328-338): per layer, K and V
+ * are separate contiguous tensors [num_blocks, block_size, num_kv_heads,
+ * head_size].  Per-step metadata (runtime/execution/paged_attention.py:18-206):
+ *   block_tables     int32 [num_seqs, table_stride], row r = request r's
+ *                    physical block ids (rows padded with any valid id);
+ *   num_computed     int32 [num_seqs], tokens already in the cache;
+ *   query_start_loc  int32 [num_seqs + 1], prefix sums of query lengths;
+ *   request_indices  int32 [num_tokens], request of each packed token.
+ * Token t of request r (offset o = t - query_start_loc[r]) is written to slot
+ * block_tables[r][(c + o) / bs] * bs + (c + o) % bs, c = num_computed[r]. */
+
+/* Scatter this step's K/V rows into their slots.  key/value rows: token
+ * stride in elements, heads contiguous at stride head_size.  Replaces the
+ * Triton `_write_paged_kv_kernel` launch
+ * (runtime/execution/triton_paged_attention.py:31-104, 498-517). */
+LVB_API int lvb_paged_kv_write(const uint16_t *key, int64_t key_token_stride, const uint16_t *value,
+                       int64_t value_token_stride, uint16_t *key_cache, uint16_t *value_cache,
+                       const int32_t *block_tables, int64_t table_stride,
+                       const int32_t *num_computed, const int32_t *query_start_loc,
+                       const int32_t *request_indices, int64_t num_tokens, int64_t num_kv_heads,
+                       int64_t head_size, int64_t block_size, int dtype, lvb_stream_t stream);
+
+/* Scatter rows into explicit flat slots (slot = block * block_size + offset).
+ * Replaces `PagedKVCache.write_prepared`'s index_copy_
+ * (runtime/execution/paged_cache.py:208-248). */
+LVB_API int lvb_kv_scatter(const uint16_t *key, int64_t key_token_stride, const uint16_t *value,
+                   int64_t value_token_stride, uint16_t *key_cache, uint16_t *value_cache,
+                   const int64_t *slots, int64_t num_tokens, int64_t num_kv_heads,
+                   int64_t head_size, int64_t num_slots, int dtype, lvb_stream_t stream);
+
+/* Bytes of workspace `lvb_paged_attention` needs (split-context partials). */
+LVB_API size_t lvb_paged_attention_workspace_bytes(int64_t num_seqs, int64_t num_q_heads,
+                                           int64_t num_kv_heads, int64_t head_size,
+                                           int64_t max_seq_len);
+
+/* out[t, h, :] = softmax(scale * q[t, h] . K_visible^T) V_visible over the
+ * pages of token t's request.  Visible positions: every computed position,
+ * plus, among this step's queries of the request, the query itself and its
+ * ancestors.  visibility == NULL means linear (causal) layouts; otherwise
+ * visibility is the packed boolean matrix per request (row-major, qlen x qlen)
+ * starting at visibility_start[r].  The query heads of one KV head are
+ * num_q_heads / num_kv_heads consecutive heads (GQA).  fp32 accumulation.
+ * The K/V of this step must already be in the cache (lvb_paged_kv_write).
+ * head_size must be a multiple of 8 and at most 256.  Decode batches (every
+ * query length 1, linear) take a split-context path that needs `workspace`.
+ * Replaces the Triton attention launches
+ * (runtime/execution/triton_paged_attention.py:106-391, 519-559). */
+LVB_API int lvb_paged_attention(const uint16_t *query, int64_t query_token_stride,
+                        const uint16_t *key_cache, const uint16_t *value_cache, uint16_t *out,
+                        int64_t out_token_stride, const int32_t *block_tables,
+                        int64_t table_stride, const int32_t *num_computed,
+                        const int32_t *query_start_loc, const int32_t *request_indices,
+                        const uint8_t *visibility, const int32_t *visibility_start,
+                        int64_t num_seqs, int64_t num_tokens, int64_t max_query_len,
+                        int64_t max_seq_len, int64_t num_q_heads, int64_t num_kv_heads,
+                        int64_t head_size, int64_t block_size, int64_t num_blocks, float scale,
+                        int dtype, void *workspace, size_t workspace_bytes,
+                        lvb_stream_t stream);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* LVB200_H_ */

@@ -1,0 +1,44 @@
+"""B200-native (sm_100a) hot path for light-vllm.
+
+Two drop-in plugins behind light-vllm's own extension points:
+
+* ``B200AWQScheme`` -- an ``AWQScheme`` whose ``LinearOperation`` runs the
+  AutoAWQ W4A16 linear on tcgen05 tensor cores (``light_vllm_b200.awq``);
+* ``B200PagedAttentionBackend`` -- a ``PagedAttentionBackend`` that writes
+  paged K/V and attends with sm_100a kernels (``light_vllm_b200.paged_attention``);
+
+plus ``TensorParallelCollectives`` for the row-parallel all-reduce on the
+caller's stream (``light_vllm_b200.collectives``).  All GPU work goes through
+the C-ABI library ``_lib/liblvb200.so`` (``include/lvb200.h``); there is no
+CPU or Triton fallback.
+"""
+
+from light_vllm_b200.awq import B200AWQOperation, B200AWQScheme, b200_awq_dequantize, b200_awq_linear
+from light_vllm_b200.kv_cache import (
+    AttentionLayerSpec,
+    KVCacheError,
+    ModelKVCacheSpec,
+    PagedAttentionMetadata,
+    PagedKVCache,
+    PagedKVCacheConfig,
+    QueryLayout,
+    linear_query_layout,
+)
+from light_vllm_b200.paged_attention import B200PagedAttention, B200PagedAttentionBackend
+
+__all__ = [
+    "AttentionLayerSpec",
+    "B200AWQOperation",
+    "B200AWQScheme",
+    "B200PagedAttention",
+    "B200PagedAttentionBackend",
+    "KVCacheError",
+    "ModelKVCacheSpec",
+    "PagedAttentionMetadata",
+    "PagedKVCache",
+    "PagedKVCacheConfig",
+    "QueryLayout",
+    "b200_awq_dequantize",
+    "b200_awq_linear",
+    "linear_query_layout",
+]

@@ -1,0 +1,108 @@
+"""ctypes binding of the sm_100a library ``_lib/liblvb200.so`` (C ABI in
+``include/lvb200.h``).
+
+There is no fallback: if the library is missing or cannot be loaded, every
+entry point raises ``RuntimeError`` naming the build command.  Status codes map
+to the exception types the reference uses at the same boundary
+(``modeling/quantization/cuda_awq.py:53-80`` raises ``ValueError`` for bad
+shapes, ``RuntimeError`` for toolchain/runtime failures).
+"""
+
+from __future__ import annotations
+
+import ctypes
+import functools
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "_lib" / "liblvb200.so"
+ABI_VERSION = 1
+
+LVB_OK = 0
+LVB_ERR_INVALID = 1
+LVB_ERR_UNSUPPORTED = 2
+LVB_ERR_CUDA = 3
+LVB_ERR_WORKSPACE = 4
+
+DTYPE_F16 = 0
+DTYPE_BF16 = 1
+
+_c_ptr = ctypes.c_void_p
+_i64 = ctypes.c_int64
+_int = ctypes.c_int
+_size = ctypes.c_size_t
+_f32 = ctypes.c_float
+
+# name -> (restype, argtypes); every symbol declared in include/lvb200.h.
+PROTOTYPES: dict[str, tuple[object, tuple[object, ...]]] = {
+    "lvb_abi_version": (_int, ()),
+    "lvb_last_error": (ctypes.c_char_p, ()),
+    "lvb_device_error": (_int, (ctypes.POINTER(ctypes.c_uint32),)),
+    "lvb_awq_workspace_bytes": (_size, (_i64, _i64, _i64, _i64)),
+    "lvb_awq_linear": (
+        _int,
+        (_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _i64, _i64, _i64, _i64, _c_ptr, _size, _c_ptr),
+    ),
+    "lvb_awq_dequantize": (_int, (_c_ptr, _c_ptr, _c_ptr, _c_ptr, _i64, _i64, _i64, _c_ptr)),
+    "lvb_paged_kv_write": (
+        _int,
+        (_c_ptr, _i64, _c_ptr, _i64, _c_ptr, _c_ptr, _c_ptr, _i64, _c_ptr, _c_ptr, _c_ptr, _i64, _i64,
+         _i64, _i64, _int, _c_ptr),
+    ),
+    "lvb_kv_scatter": (
+        _int,
+        (_c_ptr, _i64, _c_ptr, _i64, _c_ptr, _c_ptr, _c_ptr, _i64, _i64, _i64, _i64, _int, _c_ptr),
+    ),
+    "lvb_paged_attention_workspace_bytes": (_size, (_i64, _i64, _i64, _i64, _i64)),
+    "lvb_paged_attention": (
+        _int,
+        (_c_ptr, _i64, _c_ptr, _c_ptr, _c_ptr, _i64, _c_ptr, _i64, _c_ptr, _c_ptr, _c_ptr, _c_ptr,
+         _c_ptr, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _int, _c_ptr, _size,
+         _c_ptr),
+    ),
+}
+
+
+class NativeLibraryError(RuntimeError):
+    """The sm_100a library is missing, stale or failed to load."""
+
+
+@functools.lru_cache(maxsize=1)
+def library() -> ctypes.CDLL:
+    """Load the library once and declare every prototype; raise if absent."""
+
+    if not LIB_PATH.is_file():
+        raise NativeLibraryError(
+            f"{LIB_PATH} is not built; run `python -m light_vllm_b200.build` (needs nvcc 12.8+)"
+        )
+    try:
+        lib = ctypes.CDLL(str(LIB_PATH))
+    except OSError as exc:
+        raise NativeLibraryError(f"cannot load {LIB_PATH}: {exc}") from exc
+    for name, (restype, argtypes) in PROTOTYPES.items():
+        fn = getattr(lib, name)
+        fn.restype = restype
+        fn.argtypes = list(argtypes)
+    version = lib.lvb_abi_version()
+    if version != ABI_VERSION:
+        raise NativeLibraryError(f"{LIB_PATH} has ABI {version}, expected {ABI_VERSION}; rebuild it")
+    return lib
+
+
+def check(status: int, what: str) -> None:
+    """Raise the exception type matching a non-zero C status."""
+
+    if status == LVB_OK:
+        return
+    message = library().lvb_last_error().decode(errors="replace")
+    text = f"{what}: {message}"
+    if status in (LVB_ERR_INVALID, LVB_ERR_UNSUPPORTED, LVB_ERR_WORKSPACE):
+        raise ValueError(text)
+    raise RuntimeError(text)
+
+
+def device_error() -> int:
+    """Read and clear the device-side error word (synchronises the device)."""
+
+    value = ctypes.c_uint32(0)
+    check(library().lvb_device_error(ctypes.byref(value)), "lvb_device_error")
+    return int(value.value)

@@ -1,0 +1,144 @@
+"""B200 AWQ W4A16 scheme (drop-in ``AWQScheme``).
+
+``B200AWQScheme().prepare(qweight, qzeros, scales, group_size, bias)`` returns
+a ``LinearOperation`` -- the contract of ``AWQScheme.prepare``
+(modeling/quantization/awq.py:468-486) and ``LinearOperation.__call__``
+(modeling/quantization/interfaces.py:23-26).  It replaces ``CudaAWQScheme`` /
+``CudaAWQOperation`` (modeling/quantization/awq_schemes.py:56-73,
+cuda_awq.py:96-146) and consumes the same AutoAWQ GEMM tensors in place: no
+repacking, no second resident copy of the weight.  Every call runs one sm_100a
+kernel (``lvb_awq_linear``) for any number of rows: tcgen05 tensor cores with
+the weight dequantised on the fly, bias fused into the epilogue, and split-K
+for decode-sized batches, whose workspace is allocated once here.
+
+Inject it without touching Engine, Scheduler or Worker, e.g.
+``AWQLinearMethod(AWQConfig.from_mapping(cfg), B200AWQScheme())`` passed as a
+prebuilt ``ModelSpec.linear_method`` (modeling/loaders/safetensors.py:101-102).
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+from torch import Tensor
+
+from light_vllm_b200 import _native
+
+_PACK_FACTOR = 8
+# Row counts that take the split-K path; the workspace covers the largest.
+_SPLIT_K_ROWS = (1, 16, 32, 64)
+
+
+def _validate_static_weights(qweight: Tensor, qzeros: Tensor, scales: Tensor,
+                             group_size: int) -> tuple[int, int]:
+    """Same rules and messages as the reference CUDA scheme (cuda_awq.py:53-80),
+    except that output widths need only be multiples of 32."""
+
+    if qweight.device.type != "cuda":
+        raise ValueError("CUDA AWQ weights must be on CUDA")
+    if torch.cuda.get_device_capability(qweight.device) < (10, 0):
+        raise ValueError("B200 AWQ requires compute capability 10.0 (sm_100a)")
+    if qweight.dtype != torch.int32 or qzeros.dtype != torch.int32:
+        raise ValueError("CUDA AWQ packed weights and zeros must use int32")
+    if scales.dtype != torch.float16:
+        raise ValueError("CUDA AWQ first-stage scales must use float16")
+    if any(t.device != qweight.device for t in (qzeros, scales)):
+        raise ValueError("CUDA AWQ tensors must share one CUDA device")
+    if not all(t.is_contiguous() for t in (qweight, qzeros, scales)):
+        raise ValueError("CUDA AWQ checkpoint tensors must be contiguous")
+    inner = qweight.shape[0]
+    output = qweight.shape[1] * _PACK_FACTOR
+    if group_size <= 0 or inner % group_size or group_size % 32:
+        raise ValueError("CUDA AWQ group_size must divide K and be a multiple of 32")
+    if output % 32:
+        raise ValueError("CUDA AWQ output width must be divisible by 32")
+    expected = (inner // group_size, output // _PACK_FACTOR)
+    if tuple(qzeros.shape) != expected or tuple(scales.shape) != (expected[0], output):
+        raise ValueError("CUDA AWQ qzeros/scales do not match qweight and group_size")
+    return inner, output
+
+
+@dataclass(frozen=True, slots=True)
+class B200AWQOperation:
+    """A prepared W4A16 linear over the model-owned AutoAWQ tensors."""
+
+    qweight: Tensor
+    qzeros: Tensor
+    scales: Tensor
+    group_size: int
+    bias: Tensor | None
+    inner: int
+    output_width: int
+    workspace: Tensor
+
+    def __call__(self, inputs: Tensor) -> Tensor:
+        flat = inputs.reshape(-1, self.inner)
+        if flat.dtype != torch.float16:
+            raise ValueError("B200 AWQ activations must be float16")
+        if not flat.is_contiguous() or flat.data_ptr() % 16:
+            flat = flat.contiguous()
+        rows = flat.shape[0]
+        out = torch.empty((rows, self.output_width), dtype=torch.float16, device=flat.device)
+        _native.check(
+            _native.library().lvb_awq_linear(
+                flat.data_ptr(), self.qweight.data_ptr(), self.qzeros.data_ptr(),
+                self.scales.data_ptr(), None if self.bias is None else self.bias.data_ptr(),
+                out.data_ptr(), rows, self.inner, self.output_width, self.group_size,
+                self.workspace.data_ptr(), self.workspace.numel(),
+                torch.cuda.current_stream(flat.device).cuda_stream,
+            ),
+            "lvb_awq_linear",
+        )
+        return out.reshape(*inputs.shape[:-1], self.output_width)
+
+
+def prepare_b200_awq_operation(qweight: Tensor, qzeros: Tensor, scales: Tensor, group_size: int,
+                               bias: Tensor | None) -> B200AWQOperation:
+    inner, output = _validate_static_weights(qweight, qzeros, scales, group_size)
+    if bias is not None and (bias.device != qweight.device or bias.dtype != scales.dtype
+                             or tuple(bias.shape) != (output,)):
+        raise ValueError("CUDA AWQ bias must match output width, dtype, and device")
+    if bias is not None and not bias.is_contiguous():
+        bias = bias.contiguous()
+    lib = _native.library()
+    with torch.cuda.device(qweight.device):
+        need = max(int(lib.lvb_awq_workspace_bytes(m, inner, output, group_size)) for m in _SPLIT_K_ROWS)
+        # Split-K semaphores must start at zero; every call leaves them zero.
+        workspace = torch.zeros(max(need, 256), dtype=torch.uint8, device=qweight.device)
+    return B200AWQOperation(qweight, qzeros, scales, group_size, bias, inner, output, workspace)
+
+
+class B200AWQScheme:
+    """AWQ Scheme whose operations run the sm_100a W4A16 kernel."""
+
+    name = "b200"
+
+    def __init__(self) -> None:
+        _native.library()  # fail loudly when the library is missing
+
+    def prepare(self, qweight: Tensor, qzeros: Tensor, scales: Tensor, group_size: int,
+                bias: Tensor | None) -> B200AWQOperation:
+        return prepare_b200_awq_operation(qweight, qzeros, scales, group_size, bias)
+
+
+def b200_awq_linear(inputs: Tensor, qweight: Tensor, qzeros: Tensor, scales: Tensor,
+                    group_size: int, bias: Tensor | None) -> Tensor:
+    """One-shot entry for tests and microbenchmarks (mirrors cuda_awq.py:245-255)."""
+
+    return prepare_b200_awq_operation(qweight, qzeros, scales, group_size, bias)(inputs)
+
+
+def b200_awq_dequantize(qweight: Tensor, qzeros: Tensor, scales: Tensor, group_size: int) -> Tensor:
+    """Full fp16 weight [K, N] (the reference's ``awq_dequantize``)."""
+
+    inner, output = _validate_static_weights(qweight, qzeros, scales, group_size)
+    w = torch.empty((inner, output), dtype=torch.float16, device=qweight.device)
+    _native.check(
+        _native.library().lvb_awq_dequantize(
+            qweight.data_ptr(), qzeros.data_ptr(), scales.data_ptr(), w.data_ptr(), inner, output,
+            group_size, torch.cuda.current_stream(qweight.device).cuda_stream,
+        ),
+        "lvb_awq_dequantize",
+    )
+    return w

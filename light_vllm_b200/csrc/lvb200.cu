@@ -1,0 +1,497 @@
+// C-ABI entry points of the B200 hot-path library (declared in include/lvb200.h).
+//
+// One translation unit: the kernels live in the .cuh files included below.
+// Entry points validate arguments, pick a kernel configuration, encode TMA
+// tensor maps on the host (pure host computation, no device traffic) and
+// enqueue on the caller's stream.  They never synchronise and never allocate.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <climits>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/lvb200.h"
+#include "awq_gemm.cuh"
+#include "lvb_common.cuh"
+#include "paged_attention.cuh"
+
+namespace {
+
+constexpr int kAbiVersion = 1;
+constexpr int kMaxDevices = 64;
+
+thread_local char g_last_error[512] = "";
+
+int fail(int code, const char *fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char *what) {
+  return fail(LVB_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Streaming-multiprocessor count of the current device, queried once per device.
+int current_device(int *dev) {
+  cudaError_t e = cudaGetDevice(dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (*dev < 0 || *dev >= kMaxDevices) return fail(LVB_ERR_UNSUPPORTED, "device index %d", *dev);
+  return LVB_OK;
+}
+
+int sm_count(int dev) {
+  static int counts[kMaxDevices] = {0};
+  if (counts[dev] == 0) {
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0)
+      v = 148;
+    counts[dev] = v;
+  }
+  return counts[dev];
+}
+
+// Opt a kernel into large dynamic shared memory once per (kernel, device).
+template <typename Kernel>
+int ensure_smem(Kernel kernel, int bytes, int dev, bool *done_flags) {
+  if (done_flags[dev]) return LVB_OK;
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
+  done_flags[dev] = true;
+  return LVB_OK;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+int encode_map(CUtensorMap *map, CUtensorMapDataType type, cuuint32_t rank, const void *base,
+               const cuuint64_t *dims, const cuuint64_t *strides_bytes, const cuuint32_t *box,
+               CUtensorMapSwizzle swizzle) {
+  auto encode = tensor_map_encoder();
+  if (encode == nullptr) return fail(LVB_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint32_t elem_strides[5] = {1, 1, 1, 1, 1};
+  CUresult r = encode(map, type, rank, const_cast<void *>(base), dims, strides_bytes, box,
+                      elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(LVB_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+  return LVB_OK;
+}
+
+// ------------------------------------------------------------------------
+// AWQ planning
+// ------------------------------------------------------------------------
+struct AwqPlan {
+  int bn, m_tiles, n_tiles, k_tiles, splits;
+  size_t sem_bytes, part_bytes;
+};
+
+AwqPlan awq_plan(int64_t m, int64_t k, int64_t n, int sms) {
+  AwqPlan p{};
+  p.bn = m <= 16 ? 16 : m <= 32 ? 32 : m <= 64 ? 64 : m <= 128 ? 128 : 256;
+  p.m_tiles = static_cast<int>((m + p.bn - 1) / p.bn);
+  p.n_tiles = static_cast<int>((n + lvb::awq::kTileN - 1) / lvb::awq::kTileN);
+  p.k_tiles = static_cast<int>((k + lvb::awq::kTileK - 1) / lvb::awq::kTileK);
+  const int tiles = p.m_tiles * p.n_tiles;
+  p.splits = 1;
+  if (p.bn <= 64 && tiles < sms) {
+    int s = sms / tiles;
+    const int cap = p.k_tiles / 2 > 1 ? p.k_tiles / 2 : 1;
+    p.splits = s < cap ? s : cap;
+    if (p.splits < 1) p.splits = 1;
+  }
+  p.sem_bytes = p.splits > 1 ? (static_cast<size_t>(tiles) * 4 + 255) & ~static_cast<size_t>(255) : 0;
+  p.part_bytes = p.splits > 1
+                     ? static_cast<size_t>(tiles) * p.splits * p.bn * lvb::awq::kTileN * sizeof(float)
+                     : 0;
+  return p;
+}
+
+template <int BN>
+int launch_awq(const AwqPlan &plan, const uint16_t *x, const int32_t *qweight,
+               const int32_t *qzeros, const uint16_t *scales, const uint16_t *bias, uint16_t *y,
+               int64_t m, int64_t k, int64_t n, int64_t g, uint8_t *ws, int dev,
+               cudaStream_t stream) {
+  using C = lvb::awq::Config<BN>;
+  static bool smem_done[kMaxDevices] = {false};
+  auto kernel = lvb::awq::awq_gemm_kernel<BN>;
+  int rc = ensure_smem(kernel, C::kSmemBytes, dev, smem_done);
+  if (rc != LVB_OK) return rc;
+
+  CUtensorMap qmap, xmap;
+  {
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(n / 8), static_cast<cuuint64_t>(k)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(n / 8) * 4};
+    const cuuint32_t box[2] = {lvb::awq::kWordsPerRow, lvb::awq::kTileK};
+    rc = encode_map(&qmap, CU_TENSOR_MAP_DATA_TYPE_INT32, 2, qweight, dims, strides, box,
+                    CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc != LVB_OK) return rc;
+  }
+  {
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(m)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(k) * 2};
+    const cuuint32_t box[2] = {lvb::awq::kTileK, static_cast<cuuint32_t>(BN)};
+    rc = encode_map(&xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, x, dims, strides, box,
+                    CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc != LVB_OK) return rc;
+  }
+  lvb::awq::Params p{};
+  p.qzeros = qzeros;
+  p.scales = scales;
+  p.bias = bias;
+  p.y = y;
+  p.semaphores = reinterpret_cast<uint32_t *>(ws);
+  p.partials = plan.splits > 1 ? reinterpret_cast<float *>(ws + plan.sem_bytes) : nullptr;
+  p.M = static_cast<int>(m);
+  p.K = static_cast<int>(k);
+  p.N = static_cast<int>(n);
+  p.G = static_cast<int>(g);
+  p.k_tiles = plan.k_tiles;
+  p.splits = plan.splits;
+  p.n_tiles = plan.n_tiles;
+  dim3 grid(plan.n_tiles, plan.m_tiles, plan.splits);
+  kernel<<<grid, lvb::awq::kThreads, C::kSmemBytes, stream>>>(qmap, xmap, p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "awq_gemm_kernel launch");
+  return LVB_OK;
+}
+
+// ------------------------------------------------------------------------
+// Attention planning
+// ------------------------------------------------------------------------
+struct DecodePlan {
+  int max_splits, chunk_tokens;
+  size_t o_bytes, lse_bytes;
+};
+
+DecodePlan decode_plan(int64_t num_seqs, int64_t hq, int64_t hkv, int64_t d, int64_t max_seq_len,
+                       int sms) {
+  DecodePlan p{};
+  const int64_t max_pages = (max_seq_len + lvb::attn::kPageTokens - 1) / lvb::attn::kPageTokens;
+  const int64_t pairs = num_seqs * hkv > 0 ? num_seqs * hkv : 1;
+  const int64_t target = 8LL * sms;  // ~4 waves at 2 CTAs per SM
+  int64_t splits = (target + pairs - 1) / pairs;
+  if (splits < 1) splits = 1;
+  if (splits > max_pages) splits = max_pages > 0 ? max_pages : 1;
+  const int64_t chunk_pages = (max_pages + splits - 1) / splits > 0 ? (max_pages + splits - 1) / splits : 1;
+  splits = (max_pages + chunk_pages - 1) / chunk_pages;
+  if (splits < 1) splits = 1;
+  p.max_splits = static_cast<int>(splits);
+  p.chunk_tokens = static_cast<int>(chunk_pages * lvb::attn::kPageTokens);
+  p.o_bytes = (static_cast<size_t>(num_seqs * hq * splits * d) * 4 + 255) & ~static_cast<size_t>(255);
+  p.lse_bytes = (static_cast<size_t>(num_seqs * hq * splits) * 4 + 255) & ~static_cast<size_t>(255);
+  return p;
+}
+
+bool decode_eligible(const uint8_t *vis, int64_t max_query_len, int64_t num_seqs, int64_t num_tokens,
+                     int64_t hq, int64_t hkv, int64_t d, int64_t bs) {
+  return vis == nullptr && max_query_len == 1 && num_tokens == num_seqs && bs == lvb::attn::kPageTokens &&
+         (d == 64 || d == 128) && hq % hkv == 0 && hq / hkv <= 16;
+}
+
+template <bool kBf16, int D>
+int launch_decode(const lvb::attn::AttnArgs &a, int64_t num_seqs, int64_t num_blocks, int dev,
+                  cudaStream_t stream) {
+  using Cfg = lvb::attn::DecodeCfg<D>;
+  static bool smem_done[kMaxDevices] = {false};
+  auto kernel = lvb::attn::paged_decode_kernel<kBf16, D>;
+  int rc = ensure_smem(kernel, Cfg::kSmemBytes, dev, smem_done);
+  if (rc != LVB_OK) return rc;
+  const CUtensorMapDataType type = kBf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(a.Hkv),
+                              static_cast<cuuint64_t>(num_blocks) * lvb::attn::kPageTokens};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(D) * 2,
+                                 static_cast<cuuint64_t>(a.Hkv) * D * 2};
+  const cuuint32_t box[3] = {64, 1, lvb::attn::kPageTokens};
+  CUtensorMap kmap, vmap;
+  rc = encode_map(&kmap, type, 3, a.kc, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc != LVB_OK) return rc;
+  rc = encode_map(&vmap, type, 3, a.vc, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc != LVB_OK) return rc;
+  dim3 grid(a.max_splits, a.Hkv, static_cast<unsigned>(num_seqs));
+  kernel<<<grid, lvb::attn::kDecodeThreads, Cfg::kSmemBytes, stream>>>(kmap, vmap, a);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "paged_decode_kernel launch");
+  dim3 mgrid(static_cast<unsigned>(num_seqs), a.Hq);
+  lvb::attn::paged_merge_kernel<kBf16><<<mgrid, D, 0, stream>>>(a);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "paged_merge_kernel launch");
+  return LVB_OK;
+}
+
+template <bool kBf16>
+int launch_general(const lvb::attn::AttnArgs &a, int64_t num_tokens, cudaStream_t stream) {
+  dim3 grid(static_cast<unsigned>(num_tokens), a.Hq);
+  const int dpl = (a.D + 31) / 32;
+  if (dpl <= 1)
+    lvb::attn::paged_attn_general_kernel<kBf16, 1><<<grid, 128, 0, stream>>>(a);
+  else if (dpl == 2)
+    lvb::attn::paged_attn_general_kernel<kBf16, 2><<<grid, 128, 0, stream>>>(a);
+  else if (dpl == 3)
+    lvb::attn::paged_attn_general_kernel<kBf16, 3><<<grid, 128, 0, stream>>>(a);
+  else if (dpl == 4)
+    lvb::attn::paged_attn_general_kernel<kBf16, 4><<<grid, 128, 0, stream>>>(a);
+  else
+    lvb::attn::paged_attn_general_kernel<kBf16, 8><<<grid, 128, 0, stream>>>(a);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "paged_attn_general_kernel launch");
+  return LVB_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int lvb_abi_version(void) { return kAbiVersion; }
+
+const char *lvb_last_error(void) { return g_last_error; }
+
+int lvb_device_error(uint32_t *error_out) {
+  if (error_out == nullptr) return fail(LVB_ERR_INVALID, "error_out is null");
+  unsigned int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, lvb::g_device_error, sizeof(v));
+  if (e != cudaSuccess) return cuda_fail(e, "reading the device error word");
+  const unsigned int zero = 0;
+  e = cudaMemcpyToSymbol(lvb::g_device_error, &zero, sizeof(zero));
+  if (e != cudaSuccess) return cuda_fail(e, "clearing the device error word");
+  *error_out = v;
+  return LVB_OK;
+}
+
+size_t lvb_awq_workspace_bytes(int64_t m, int64_t k, int64_t n, int64_t group_size) {
+  (void)group_size;
+  if (m <= 0 || k <= 0 || n <= 0) return 0;
+  int dev = 0;
+  if (current_device(&dev) != LVB_OK) return 0;
+  const AwqPlan p = awq_plan(m, k, n, sm_count(dev));
+  return p.sem_bytes + p.part_bytes;
+}
+
+int lvb_awq_linear(const uint16_t *x, const int32_t *qweight, const int32_t *qzeros,
+                   const uint16_t *scales, const uint16_t *bias, uint16_t *y, int64_t m,
+                   int64_t k, int64_t n, int64_t group_size, void *workspace,
+                   size_t workspace_bytes, lvb_stream_t stream) {
+  if (m < 0 || k <= 0 || n <= 0) return fail(LVB_ERR_INVALID, "invalid AWQ shape m=%lld k=%lld n=%lld",
+                                              (long long)m, (long long)k, (long long)n);
+  if (m == 0) return LVB_OK;
+  if (m > INT_MAX || k > INT_MAX || n > INT_MAX) return fail(LVB_ERR_UNSUPPORTED, "AWQ dimension exceeds int32");
+  if (group_size <= 0 || group_size % 8 != 0 || k % group_size != 0)
+    return fail(LVB_ERR_INVALID, "AWQ group_size %lld must be a positive multiple of 8 dividing k=%lld",
+                (long long)group_size, (long long)k);
+  if (n % 32 != 0) return fail(LVB_ERR_INVALID, "AWQ output width %lld must be divisible by 32", (long long)n);
+  if (k % 8 != 0) return fail(LVB_ERR_INVALID, "AWQ input width %lld must be divisible by 8", (long long)k);
+  if (!x || !qweight || !qzeros || !scales || !y) return fail(LVB_ERR_INVALID, "AWQ null pointer argument");
+  if (!aligned16(x) || !aligned16(qweight) || !aligned16(scales) || (workspace && !aligned16(workspace)))
+    return fail(LVB_ERR_INVALID, "AWQ x, qweight, scales and workspace must be 16-byte aligned");
+  int dev = 0;
+  int rc = current_device(&dev);
+  if (rc != LVB_OK) return rc;
+  const AwqPlan plan = awq_plan(m, k, n, sm_count(dev));
+  if ((plan.sem_bytes + plan.part_bytes) > 0 && (workspace == nullptr || workspace_bytes < plan.sem_bytes + plan.part_bytes))
+    return fail(LVB_ERR_WORKSPACE, "AWQ workspace of %zu bytes is below the %zu required", workspace_bytes,
+                plan.sem_bytes + plan.part_bytes);
+  uint8_t *ws = static_cast<uint8_t *>(workspace);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  switch (plan.bn) {
+    case 16: return launch_awq<16>(plan, x, qweight, qzeros, scales, bias, y, m, k, n, group_size, ws, dev, s);
+    case 32: return launch_awq<32>(plan, x, qweight, qzeros, scales, bias, y, m, k, n, group_size, ws, dev, s);
+    case 64: return launch_awq<64>(plan, x, qweight, qzeros, scales, bias, y, m, k, n, group_size, ws, dev, s);
+    case 128: return launch_awq<128>(plan, x, qweight, qzeros, scales, bias, y, m, k, n, group_size, ws, dev, s);
+    default: return launch_awq<256>(plan, x, qweight, qzeros, scales, bias, y, m, k, n, group_size, ws, dev, s);
+  }
+}
+
+int lvb_awq_dequantize(const int32_t *qweight, const int32_t *qzeros, const uint16_t *scales,
+                       uint16_t *w, int64_t k, int64_t n, int64_t group_size, lvb_stream_t stream) {
+  if (k <= 0 || n <= 0 || n % 8 != 0 || group_size <= 0 || k % group_size != 0)
+    return fail(LVB_ERR_INVALID, "invalid AWQ dequantize shape k=%lld n=%lld group=%lld", (long long)k,
+                (long long)n, (long long)group_size);
+  if (k > INT_MAX || n > INT_MAX) return fail(LVB_ERR_UNSUPPORTED, "AWQ dimension exceeds int32");
+  if (!qweight || !qzeros || !scales || !w) return fail(LVB_ERR_INVALID, "AWQ null pointer argument");
+  if (!aligned16(scales) || !aligned16(w)) return fail(LVB_ERR_INVALID, "scales and w must be 16-byte aligned");
+  int dev = 0;
+  int rc = current_device(&dev);
+  if (rc != LVB_OK) return rc;
+  const long long words = k * (n / 8);
+  long long blocks = (words + 255) / 256;
+  const long long cap = static_cast<long long>(sm_count(dev)) * 8;
+  if (blocks > cap) blocks = cap;
+  lvb::awq::awq_dequantize_kernel<<<static_cast<unsigned>(blocks), 256, 0,
+                                    reinterpret_cast<cudaStream_t>(stream)>>>(
+      qweight, qzeros, scales, w, static_cast<int>(k), static_cast<int>(n), static_cast<int>(group_size));
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "awq_dequantize_kernel launch");
+  return LVB_OK;
+}
+
+static int kv_write_common(const lvb::attn::KVWriteArgs &a, int dtype, lvb_stream_t stream) {
+  if (dtype != LVB_DTYPE_F16 && dtype != LVB_DTYPE_BF16) return fail(LVB_ERR_INVALID, "unknown dtype %d", dtype);
+  if (a.num_tokens < 0 || a.Hkv <= 0 || a.D <= 0 || a.D % 8 != 0)
+    return fail(LVB_ERR_INVALID, "invalid K/V shape tokens=%d heads=%d head_size=%d", a.num_tokens, a.Hkv, a.D);
+  if (a.num_tokens == 0) return LVB_OK;
+  if (a.key_stride % 8 != 0 || a.value_stride % 8 != 0)
+    return fail(LVB_ERR_INVALID, "K/V token strides must be multiples of 8 elements");
+  if (!aligned16(a.key) || !aligned16(a.value) || !aligned16(a.key_cache) || !aligned16(a.value_cache))
+    return fail(LVB_ERR_INVALID, "K/V tensors and caches must be 16-byte aligned");
+  const int chunks = a.Hkv * (a.D / 8);
+  const int threads = chunks < 256 ? ((chunks + 31) / 32) * 32 : 256;
+  lvb::attn::paged_kv_write_kernel<<<a.num_tokens, threads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "paged_kv_write_kernel launch");
+  return LVB_OK;
+}
+
+int lvb_paged_kv_write(const uint16_t *key, int64_t key_token_stride, const uint16_t *value,
+                       int64_t value_token_stride, uint16_t *key_cache, uint16_t *value_cache,
+                       const int32_t *block_tables, int64_t table_stride,
+                       const int32_t *num_computed, const int32_t *query_start_loc,
+                       const int32_t *request_indices, int64_t num_tokens, int64_t num_kv_heads,
+                       int64_t head_size, int64_t block_size, int dtype, lvb_stream_t stream) {
+  if (num_tokens > INT_MAX || block_size <= 0 || block_size > INT_MAX)
+    return fail(LVB_ERR_INVALID, "invalid token count or block size");
+  if (num_tokens > 0 && (!key || !value || !key_cache || !value_cache || !block_tables || !num_computed ||
+                         !query_start_loc || !request_indices))
+    return fail(LVB_ERR_INVALID, "paged K/V write null pointer argument");
+  lvb::attn::KVWriteArgs a{};
+  a.key = key;
+  a.key_stride = key_token_stride;
+  a.value = value;
+  a.value_stride = value_token_stride;
+  a.key_cache = key_cache;
+  a.value_cache = value_cache;
+  a.tables = block_tables;
+  a.table_stride = table_stride;
+  a.computed = num_computed;
+  a.qsl = query_start_loc;
+  a.req = request_indices;
+  a.slots = nullptr;
+  a.num_tokens = static_cast<int>(num_tokens);
+  a.Hkv = static_cast<int>(num_kv_heads);
+  a.D = static_cast<int>(head_size);
+  a.bs = static_cast<int>(block_size);
+  return kv_write_common(a, dtype, stream);
+}
+
+int lvb_kv_scatter(const uint16_t *key, int64_t key_token_stride, const uint16_t *value,
+                   int64_t value_token_stride, uint16_t *key_cache, uint16_t *value_cache,
+                   const int64_t *slots, int64_t num_tokens, int64_t num_kv_heads,
+                   int64_t head_size, int64_t num_slots, int dtype, lvb_stream_t stream) {
+  (void)num_slots;
+  if (num_tokens > INT_MAX) return fail(LVB_ERR_INVALID, "token count exceeds int32");
+  if (num_tokens > 0 && (!key || !value || !key_cache || !value_cache || !slots))
+    return fail(LVB_ERR_INVALID, "K/V scatter null pointer argument");
+  lvb::attn::KVWriteArgs a{};
+  a.key = key;
+  a.key_stride = key_token_stride;
+  a.value = value;
+  a.value_stride = value_token_stride;
+  a.key_cache = key_cache;
+  a.value_cache = value_cache;
+  a.slots = slots;
+  a.num_tokens = static_cast<int>(num_tokens);
+  a.Hkv = static_cast<int>(num_kv_heads);
+  a.D = static_cast<int>(head_size);
+  a.bs = 1;
+  return kv_write_common(a, dtype, stream);
+}
+
+size_t lvb_paged_attention_workspace_bytes(int64_t num_seqs, int64_t num_q_heads,
+                                           int64_t num_kv_heads, int64_t head_size,
+                                           int64_t max_seq_len) {
+  if (num_seqs <= 0 || num_q_heads <= 0 || num_kv_heads <= 0 || head_size <= 0 || max_seq_len <= 0) return 0;
+  int dev = 0;
+  if (current_device(&dev) != LVB_OK) return 0;
+  const DecodePlan p = decode_plan(num_seqs, num_q_heads, num_kv_heads, head_size, max_seq_len, sm_count(dev));
+  return p.o_bytes + p.lse_bytes;
+}
+
+int lvb_paged_attention(const uint16_t *query, int64_t query_token_stride,
+                        const uint16_t *key_cache, const uint16_t *value_cache, uint16_t *out,
+                        int64_t out_token_stride, const int32_t *block_tables,
+                        int64_t table_stride, const int32_t *num_computed,
+                        const int32_t *query_start_loc, const int32_t *request_indices,
+                        const uint8_t *visibility, const int32_t *visibility_start,
+                        int64_t num_seqs, int64_t num_tokens, int64_t max_query_len,
+                        int64_t max_seq_len, int64_t num_q_heads, int64_t num_kv_heads,
+                        int64_t head_size, int64_t block_size, int64_t num_blocks, float scale,
+                        int dtype, void *workspace, size_t workspace_bytes,
+                        lvb_stream_t stream) {
+  if (dtype != LVB_DTYPE_F16 && dtype != LVB_DTYPE_BF16) return fail(LVB_ERR_INVALID, "unknown dtype %d", dtype);
+  if (num_tokens < 0 || num_seqs <= 0 || num_q_heads <= 0 || num_kv_heads <= 0 ||
+      num_q_heads % num_kv_heads != 0 || block_size <= 0 || num_blocks <= 0)
+    return fail(LVB_ERR_INVALID, "invalid paged attention shape");
+  if (head_size <= 0 || head_size % 8 != 0 || head_size > 256)
+    return fail(LVB_ERR_UNSUPPORTED, "head_size %lld must be a multiple of 8 up to 256", (long long)head_size);
+  if (num_tokens == 0) return LVB_OK;
+  if (num_tokens > INT_MAX || num_seqs > INT_MAX || max_seq_len > INT_MAX || num_q_heads > 65535)
+    return fail(LVB_ERR_UNSUPPORTED, "paged attention size exceeds the launch limits");
+  if (!query || !key_cache || !value_cache || !out || !block_tables || !num_computed || !query_start_loc ||
+      !request_indices || (visibility != nullptr && visibility_start == nullptr))
+    return fail(LVB_ERR_INVALID, "paged attention null pointer argument");
+  if (!aligned16(key_cache) || !aligned16(value_cache)) return fail(LVB_ERR_INVALID, "caches must be 16-byte aligned");
+  if (query_token_stride % 2 != 0 || (reinterpret_cast<uintptr_t>(query) & 3u) != 0)
+    return fail(LVB_ERR_INVALID, "query rows must be 4-byte aligned");
+  int dev = 0;
+  int rc = current_device(&dev);
+  if (rc != LVB_OK) return rc;
+
+  lvb::attn::AttnArgs a{};
+  a.q = query;
+  a.q_stride = query_token_stride;
+  a.kc = key_cache;
+  a.vc = value_cache;
+  a.out = out;
+  a.o_stride = out_token_stride;
+  a.tables = block_tables;
+  a.table_stride = table_stride;
+  a.computed = num_computed;
+  a.qsl = query_start_loc;
+  a.req = request_indices;
+  a.vis = visibility;
+  a.vis_start = visibility_start;
+  a.Hq = static_cast<int>(num_q_heads);
+  a.Hkv = static_cast<int>(num_kv_heads);
+  a.D = static_cast<int>(head_size);
+  a.bs = static_cast<int>(block_size);
+  a.scale_log2 = scale * 1.4426950408889634f;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const bool bf16 = dtype == LVB_DTYPE_BF16;
+
+  if (decode_eligible(visibility, max_query_len, num_seqs, num_tokens, num_q_heads, num_kv_heads, head_size,
+                      block_size)) {
+    const DecodePlan plan = decode_plan(num_seqs, num_q_heads, num_kv_heads, head_size, max_seq_len, sm_count(dev));
+    if (workspace == nullptr || workspace_bytes < plan.o_bytes + plan.lse_bytes || !aligned16(workspace))
+      return fail(LVB_ERR_WORKSPACE, "paged attention workspace of %zu bytes is below the %zu required",
+                  workspace_bytes, plan.o_bytes + plan.lse_bytes);
+    a.part_o = static_cast<float *>(workspace);
+    a.part_lse = reinterpret_cast<float *>(static_cast<uint8_t *>(workspace) + plan.o_bytes);
+    a.max_splits = plan.max_splits;
+    a.chunk_tokens = plan.chunk_tokens;
+    if (bf16) {
+      return head_size == 128 ? launch_decode<true, 128>(a, num_seqs, num_blocks, dev, s)
+                              : launch_decode<true, 64>(a, num_seqs, num_blocks, dev, s);
+    }
+    return head_size == 128 ? launch_decode<false, 128>(a, num_seqs, num_blocks, dev, s)
+                            : launch_decode<false, 64>(a, num_seqs, num_blocks, dev, s);
+  }
+  return bf16 ? launch_general<true>(a, num_tokens, s) : launch_general<false>(a, num_tokens, s);
+}
+
+}  // extern "C"

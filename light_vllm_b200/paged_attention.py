@@ -1,0 +1,201 @@
+"""B200 paged-attention backend (drop-in ``PagedAttentionBackend``).
+
+``B200PagedAttentionBackend().create(cache, metadata)`` returns a context whose
+``forward(layer_id, query, key, value, *, scale)`` writes this step's K/V into
+the paged cache and attends, exactly the contract of
+``PagedAttentionBackend`` / ``AttentionContext.forward``
+(runtime/execution/paged_attention.py:209-223, modeling/attention/interfaces.py:48-62).
+It replaces ``TritonPagedAttentionBackend``
+(runtime/execution/triton_paged_attention.py:399-581) with the sm_100a kernels
+of ``lvb_paged_kv_write`` and ``lvb_paged_attention``:
+
+* per step, the block tables, computed counts, query starts and request
+  indices go to the GPU in one pinned copy and are shared by every layer;
+* decode steps (one linear query per request) take the split-context kernel;
+  every other batch (prefill chunks, mixed batches, tree visibility) the
+  general kernel;
+* errors follow the reference: ``KVCacheError`` for a repeated layer, a shape,
+  dtype or device mismatch, and any block-table violation.
+
+Nothing here computes on the CPU.
+"""
+
+from __future__ import annotations
+
+import torch
+from torch import Tensor
+
+from light_vllm_b200 import _native
+from light_vllm_b200.kv_cache import KVCacheError
+from light_vllm_b200.staging import SingleStepStaging
+
+_SUPPORTED_DTYPES = (torch.float16, torch.bfloat16)
+
+
+def _validate_tensors(cache, metadata, layer_id: str, query: Tensor, key: Tensor, value: Tensor):
+    """Shape rules shared with the reference backends (paged_attention.py:226-247)."""
+
+    spec = cache.layer_spec(layer_id)
+    if query.ndim != 3:
+        raise KVCacheError("paged attention query must have three dimensions")
+    if query.shape[0] != key.shape[0] or value.shape != key.shape:
+        raise KVCacheError("paged attention Q/K/V token dimensions must match")
+    if query.shape[0] != metadata.num_query_tokens:
+        raise KVCacheError("paged attention metadata token count does not match query")
+    if tuple(query.shape[1:]) != (spec.num_query_heads, spec.head_size):
+        raise KVCacheError("paged attention query shape does not match the layer spec")
+    if tuple(key.shape[1:]) != (spec.num_kv_heads, spec.head_size):
+        raise KVCacheError("paged attention K/V shape does not match the layer spec")
+    return spec
+
+
+def _heads_contiguous(t: Tensor, *, align: int) -> Tensor:
+    """A [tokens, heads, dim] view usable by the kernels without a copy when
+    heads and dims are dense and rows keep ``align``-element alignment."""
+
+    if (t.stride(2) == 1 and t.stride(1) == t.shape[2] and t.stride(0) % align == 0
+            and t.data_ptr() % (2 * align) == 0):
+        return t
+    return t.contiguous()
+
+
+class B200PagedAttention:
+    """Per-step attention context; one ``forward`` per layer."""
+
+    def __init__(self, cache, metadata, staging: SingleStepStaging, backend: "B200PagedAttentionBackend"):
+        config = cache.config
+        if torch.device(config.device).type != "cuda":
+            raise KVCacheError("B200 paged attention requires a CUDA KV cache")
+        if config.dtype not in _SUPPORTED_DTYPES:
+            raise KVCacheError("B200 paged attention supports fp16 and bf16 KV caches")
+        metadata.validate_block_tables(num_blocks=config.num_blocks, block_size=config.block_size)
+        self._cache = cache
+        self._metadata = metadata
+        self._backend = backend
+        self._layer_ids: set[str] = set()
+        self._device = torch.device(config.device)
+        lengths = metadata.query_lengths
+        max_blocks = max(len(table) for table in metadata.block_tables)
+        flat_tables = []
+        for table in metadata.block_tables:
+            flat_tables.extend(table)
+            flat_tables.extend((table[0] if table else 0,) * (max_blocks - len(table)))
+        (tables, self._computed, self._query_start, self._request_indices) = staging.copy_groups(
+            flat_tables,
+            metadata.num_computed_tokens,
+            metadata.query_start_loc,
+            metadata.request_indices,
+        )
+        self._tables = tables
+        self._table_stride = max_blocks
+        self._num_seqs = metadata.batch_size
+        self._num_tokens = metadata.num_query_tokens
+        self._max_query_len = max(lengths)
+        self._max_seq_len = max(c + n for c, n in zip(metadata.num_computed_tokens, lengths))
+        self._linear = metadata.has_only_linear_queries
+        self._visibility: Tensor | None = None
+        self._visibility_start: Tensor | None = None
+
+    @property
+    def layer_ids(self) -> frozenset[str]:
+        return frozenset(self._layer_ids)
+
+    def forward(self, layer_id: str, query: Tensor, key: Tensor, value: Tensor, *, scale: float) -> Tensor:
+        """Write this step's K/V for ``layer_id`` and return the attention output."""
+
+        if layer_id in self._layer_ids:
+            raise KVCacheError(f"paged attention layer {layer_id!r} ran more than once")
+        self._layer_ids.add(layer_id)
+        spec = _validate_tensors(self._cache, self._metadata, layer_id, query, key, value)
+        config = self._cache.config
+        for t in (query, key, value):
+            if t.device != self._device or t.dtype != config.dtype:
+                raise KVCacheError("B200 query/key/value dtype and device must match the KV cache")
+        if spec.head_size % 8 or spec.head_size > 256:
+            raise KVCacheError("B200 paged attention supports head sizes that are multiples of 8 up to 256")
+        out = torch.empty((query.shape[0], spec.num_query_heads, spec.head_size),
+                          dtype=query.dtype, device=self._device)
+        return self.launch(layer_id, query, key, value, scale=scale, out=out)
+
+    def launch(self, layer_id: str, query: Tensor, key: Tensor, value: Tensor, *, scale: float,
+               out: Tensor, write_kv: bool = True) -> Tensor:
+        """Enqueue the K/V write and the attention into ``out`` without the
+        once-per-layer bookkeeping of ``forward`` (no allocation, no host
+        synchronisation), so repeated steps can be captured in a CUDA graph.
+        Shapes must already satisfy ``forward``'s checks."""
+
+        spec = self._cache.layer_spec(layer_id)
+        config = self._cache.config
+        lib = _native.library()
+        stream = torch.cuda.current_stream(self._device).cuda_stream
+        dtype_code = _native.DTYPE_BF16 if config.dtype == torch.bfloat16 else _native.DTYPE_F16
+        layer = self._cache.layer(layer_id)
+        if write_kv:
+            key = _heads_contiguous(key, align=8)
+            value = _heads_contiguous(value, align=8)
+            _native.check(
+                lib.lvb_paged_kv_write(
+                    key.data_ptr(), key.stride(0), value.data_ptr(), value.stride(0),
+                    layer.keys.data_ptr(), layer.values.data_ptr(),
+                    self._tables.data_ptr(), self._table_stride, self._computed.data_ptr(),
+                    self._query_start.data_ptr(), self._request_indices.data_ptr(),
+                    self._num_tokens, spec.num_kv_heads, spec.head_size, config.block_size,
+                    dtype_code, stream,
+                ),
+                "lvb_paged_kv_write",
+            )
+        if not self._linear and self._visibility is None:
+            vis, starts = self._metadata.visibility_tensor(device=self._device)
+            self._visibility = vis.to(torch.uint8)
+            self._visibility_start = starts
+        query = _heads_contiguous(query, align=2)
+        workspace, workspace_bytes = self._backend._workspace(
+            self._device, self._num_seqs, spec.num_query_heads, spec.num_kv_heads,
+            spec.head_size, self._max_seq_len)
+        _native.check(
+            lib.lvb_paged_attention(
+                query.data_ptr(), query.stride(0), layer.keys.data_ptr(), layer.values.data_ptr(),
+                out.data_ptr(), out.stride(0), self._tables.data_ptr(), self._table_stride,
+                self._computed.data_ptr(), self._query_start.data_ptr(),
+                self._request_indices.data_ptr(),
+                None if self._visibility is None else self._visibility.data_ptr(),
+                None if self._visibility_start is None else self._visibility_start.data_ptr(),
+                self._num_seqs, self._num_tokens, self._max_query_len, self._max_seq_len,
+                spec.num_query_heads, spec.num_kv_heads, spec.head_size, config.block_size,
+                config.num_blocks, float(scale), dtype_code, workspace, workspace_bytes, stream,
+            ),
+            "lvb_paged_attention",
+        )
+        return out
+
+
+class B200PagedAttentionBackend:
+    """Creates one ``B200PagedAttention`` per model step.
+
+    Owns the pinned metadata staging buffer and the split-context workspace;
+    both grow on demand and are reused by later steps.
+    """
+
+    name = "b200"
+
+    def __init__(self) -> None:
+        _native.library()  # fail loudly at construction when the library is missing
+        self._staging: SingleStepStaging | None = None
+        self._workspaces: dict[torch.device, Tensor] = {}
+
+    def create(self, cache, metadata) -> B200PagedAttention:
+        device = torch.device(cache.config.device)
+        if device.type != "cuda":
+            raise KVCacheError("B200 paged attention requires a CUDA KV cache")
+        if self._staging is None:
+            self._staging = SingleStepStaging(device)
+        return B200PagedAttention(cache, metadata, self._staging, self)
+
+    def _workspace(self, device: torch.device, num_seqs: int, hq: int, hkv: int, d: int,
+                   max_seq_len: int) -> tuple[int, int]:
+        need = int(_native.library().lvb_paged_attention_workspace_bytes(num_seqs, hq, hkv, d, max_seq_len))
+        buf = self._workspaces.get(device)
+        if buf is None or buf.numel() < need:
+            buf = torch.empty(max(need, 1 << 20), dtype=torch.uint8, device=device)
+            self._workspaces[device] = buf
+        return buf.data_ptr(), buf.numel()

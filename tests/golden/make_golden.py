@@ -1,0 +1,256 @@
+"""Generate golden vectors for the hot path by running the reference itself.
+
+Run in a container that has the light-vllm source tree (read-only is fine):
+
+    LIGHT_VLLM_SRC=/path/to/light-vllm/src python tests/golden/make_golden.py
+
+It imports the reference's own correctness implementations (the Torch AWQ
+scheme, ``PagedAttentionMetadata`` and ``TorchPagedAttention``), runs them on
+seeded inputs and writes the inputs and outputs as small fixtures next to this
+script.  The fixtures are committed; the GPU box never needs the reference.
+
+Fixtures:
+  awq_golden.npz     pack/unpack vectors, quantize_awq_weight outputs and
+                     Torch-scheme linear outputs.
+  paged_meta.json    slot mappings, request indices, tree visibility and
+                     block-table validation outcomes for metadata cases.
+  paged_attn.npz     TorchPagedAttention outputs and post-write cache contents.
+"""
+
+from __future__ import annotations
+
+import json
+import os
+import sys
+from pathlib import Path
+
+import numpy as np
+import torch
+
+HERE = Path(__file__).resolve().parent
+
+
+def _import_reference():
+    src = os.environ.get("LIGHT_VLLM_SRC")
+    if not src or not Path(src).is_dir():
+        raise SystemExit("set LIGHT_VLLM_SRC to the light-vllm 'src' directory")
+    sys.path.insert(0, src)
+    from light_vllm.modeling.attention import AttentionLayerSpec, ModelKVCacheSpec
+    from light_vllm.modeling.quantization import awq
+    from light_vllm.runtime.execution.interfaces import QueryLayout
+    from light_vllm.runtime.execution.paged_attention import (
+        PagedAttentionMetadata,
+        TorchPagedAttention,
+    )
+    from light_vllm.runtime.execution.paged_cache import PagedKVCache, PagedKVCacheConfig
+
+    return dict(
+        AttentionLayerSpec=AttentionLayerSpec,
+        ModelKVCacheSpec=ModelKVCacheSpec,
+        awq=awq,
+        QueryLayout=QueryLayout,
+        PagedAttentionMetadata=PagedAttentionMetadata,
+        TorchPagedAttention=TorchPagedAttention,
+        PagedKVCache=PagedKVCache,
+        PagedKVCacheConfig=PagedKVCacheConfig,
+    )
+
+
+def _as_storable(t: torch.Tensor) -> np.ndarray:
+    if t.dtype == torch.bfloat16:
+        return t.contiguous().view(torch.int16).numpy().view(np.uint16)
+    return t.contiguous().numpy()
+
+
+def make_awq(ref) -> None:
+    awq = ref["awq"]
+    out: dict[str, np.ndarray] = {}
+    # Known answer from the reference's own test (tests/test_awq.py:149-163).
+    values = torch.tensor([[0, 1, 2, 3, 4, 5, 6, 7], [15, 14, 13, 12, 11, 10, 9, 8]],
+                          dtype=torch.int32)
+    out["pack_small_values"] = values.numpy()
+    out["pack_small_packed"] = awq.pack_awq(values).numpy()
+    gen = torch.Generator().manual_seed(11)
+    values = torch.randint(0, 16, (6, 32), generator=gen, dtype=torch.int32)
+    out["pack_rand_values"] = values.numpy()
+    out["pack_rand_packed"] = awq.pack_awq(values).numpy()
+
+    cases = [
+        ("q16x24g8", (16, 24), 8, 3),
+        ("q64x256g32", (64, 256), 32, 5),
+        ("q128x384g128", (128, 384), 128, 9),
+    ]
+    for name, shape, group, seed in cases:
+        torch.manual_seed(seed)
+        weight = torch.randn(*shape, dtype=torch.float16)
+        quant = awq.quantize_awq_weight(weight, group_size=group)
+        out[f"{name}_weight"] = weight.numpy()
+        out[f"{name}_qweight"] = quant.qweight.numpy()
+        out[f"{name}_qzeros"] = quant.qzeros.numpy()
+        out[f"{name}_scales"] = quant.scales.numpy()
+        out[f"{name}_dequant"] = quant.dequantized.numpy()
+        x = torch.randn(5, shape[1], dtype=torch.float16)
+        bias = torch.randn(shape[0], dtype=torch.float16)
+        y = awq._torch_awq_linear(x, quant.qweight, quant.qzeros, quant.scales, group, bias)
+        out[f"{name}_x"] = x.numpy()
+        out[f"{name}_bias"] = bias.numpy()
+        out[f"{name}_y"] = y.numpy()
+        xf = x.float()
+        yf = awq._torch_awq_linear(xf, quant.qweight, quant.qzeros, quant.scales, group, None)
+        out[f"{name}_y_fp32"] = yf.numpy()
+    np.savez_compressed(HERE / "awq_golden.npz", **out)
+
+
+def _meta_cases(ref):
+    QL = ref["QueryLayout"]
+
+    def linear(n):
+        return tuple(-1 if i == 0 else i - 1 for i in range(n))
+
+    return [
+        # tests/test_paged_attention.py:121-130 known answer [4, 5, 0, 3, 6]
+        dict(name="slots_noncontiguous", tables=((2, 0), (1, 3)), computed=(0, 1),
+             layouts=(linear(3), linear(2)), num_blocks=4, block_size=2),
+        # tests/test_paged_attention.py:149-175 visibility known answer
+        dict(name="tree_visibility", tables=((0, 1), (2,)), computed=(0, 0),
+             layouts=((-1, 0, 0), linear(2)), num_blocks=3, block_size=2),
+        dict(name="lookahead", tables=((0, 1, 2),), computed=(0,), layouts=(linear(1),),
+             reserved=(3,), num_blocks=3, block_size=1),
+        dict(name="readonly_shared", tables=((0, 1), (0, 2)), computed=(2, 2),
+             layouts=(linear(1), linear(1)), readonly=(1, 1), num_blocks=4, block_size=2),
+        dict(name="err_not_covered", tables=((0,),), computed=(1,), layouts=(linear(2),),
+             num_blocks=4, block_size=2),
+        dict(name="err_out_of_range", tables=((4, 0),), computed=(2,), layouts=(linear(1),),
+             num_blocks=4, block_size=2),
+        dict(name="err_alias_within", tables=((0, 0),), computed=(2,), layouts=(linear(1),),
+             num_blocks=4, block_size=2),
+        dict(name="err_alias_across", tables=((0,), (0,)), computed=(0, 1),
+             layouts=(linear(1), linear(1)), num_blocks=4, block_size=2),
+        dict(name="err_one_sided_prefix", tables=((0, 1), (0, 2)), computed=(2, 2),
+             layouts=(linear(1), linear(1)), readonly=(1, 0), num_blocks=5, block_size=2),
+        dict(name="err_misaligned_prefix", tables=((0, 1, 2), (3, 0, 4)), computed=(4, 4),
+             layouts=(linear(1), linear(1)), readonly=(1, 2), num_blocks=5, block_size=2),
+        dict(name="err_readonly_beyond", tables=((0,),), computed=(1,), layouts=(linear(1),),
+             readonly=(1,), num_blocks=2, block_size=2),
+        dict(name="err_unused_trailing_a", tables=((0, 0),), computed=(0,), layouts=(linear(1),),
+             num_blocks=4, block_size=2),
+        dict(name="err_unused_trailing_b", tables=((0,), (1, 0)), computed=(0, 0),
+             layouts=(linear(1), linear(1)), num_blocks=4, block_size=2),
+        dict(name="tree_chain", tables=((1, 3, 0, 2),), computed=(2,),
+             layouts=((-1, 0, 0, 2, 3),), readonly=(1,), num_blocks=4, block_size=2),
+    ], QL
+
+
+def make_meta(ref) -> None:
+    PagedAttentionMetadata = ref["PagedAttentionMetadata"]
+    cases, QL = _meta_cases(ref)
+    results = []
+    for case in cases:
+        md = PagedAttentionMetadata(
+            block_tables=case["tables"],
+            num_computed_tokens=case["computed"],
+            query_layouts=tuple(QL(p) for p in case["layouts"]),
+            num_reserved_query_tokens=case.get("reserved", ()),
+            num_readonly_prefix_blocks=case.get("readonly", ()),
+        )
+        record = {k: v for k, v in case.items()}
+        record["query_start_loc"] = list(md.query_start_loc)
+        record["request_indices"] = list(md.request_indices)
+        vis, starts = md.visibility_tensor(device=torch.device("cpu"))
+        record["visibility"] = [bool(v) for v in vis.tolist()]
+        record["visibility_start"] = starts.tolist()
+        record["has_only_linear_queries"] = md.has_only_linear_queries
+        try:
+            md.validate_block_tables(num_blocks=case["num_blocks"], block_size=case["block_size"])
+            record["validate_error"] = None
+        except Exception as exc:  # the reference raises KVCacheError
+            record["validate_error"] = str(exc)
+        try:
+            record["slot_mapping"] = md.slot_mapping(
+                block_size=case["block_size"], device=torch.device("cpu")).tolist()
+            record["slot_error"] = None
+        except Exception as exc:
+            record["slot_mapping"] = None
+            record["slot_error"] = str(exc)
+        results.append(record)
+    (HERE / "paged_meta.json").write_text(json.dumps(results, indent=1) + "\n")
+
+
+def make_attention(ref) -> None:
+    AttentionLayerSpec = ref["AttentionLayerSpec"]
+    ModelKVCacheSpec = ref["ModelKVCacheSpec"]
+    PagedKVCache = ref["PagedKVCache"]
+    PagedKVCacheConfig = ref["PagedKVCacheConfig"]
+    PagedAttentionMetadata = ref["PagedAttentionMetadata"]
+    TorchPagedAttention = ref["TorchPagedAttention"]
+    QL = ref["QueryLayout"]
+
+    def linear(n):
+        return tuple(-1 if i == 0 else i - 1 for i in range(n))
+
+    cases = [
+        dict(name="gqa_prefill_f32", dtype=torch.float32, hq=4, hkv=2, d=8, bs=4, nb=16,
+             tables=((7, 1), (4,)), computed=(0, 0), layouts=(linear(6), linear(3))),
+        dict(name="tree_f16", dtype=torch.float16, hq=4, hkv=2, d=16, bs=2, nb=16,
+             tables=((7, 1), (4, 6)), computed=(0, 0), layouts=((-1, 0, 0, 2), (-1, 0, 0))),
+        dict(name="history_bf16", dtype=torch.bfloat16, hq=28, hkv=4, d=32, bs=16, nb=12,
+             tables=(tuple(range(9)),), computed=(130,), layouts=(linear(1),), prefix=130),
+        dict(name="lookahead_f16", dtype=torch.float16, hq=4, hkv=2, d=16, bs=2, nb=16,
+             tables=((8, 3, 12), (10, 14)), computed=(0, 0), layouts=(linear(3), linear(1)),
+             reserved=(5, 4)),
+        dict(name="readonly_prefix_f16", dtype=torch.float16, hq=4, hkv=2, d=16, bs=2, nb=16,
+             tables=((0, 5), (0, 7)), computed=(2, 2), layouts=(linear(1), linear(1)),
+             readonly=(1, 1), prefix=2),
+        dict(name="mixed_decode_prefill_f32", dtype=torch.float32, hq=6, hkv=2, d=8, bs=4, nb=20,
+             tables=((3, 9, 1), (5,), (11, 2, 0, 17)), computed=(9, 0, 13),
+             layouts=(linear(1), linear(3), linear(2))),
+    ]
+    out: dict[str, np.ndarray] = {}
+    index = []
+    for ci, case in enumerate(cases):
+        torch.manual_seed(1000 + ci)
+        spec = ModelKVCacheSpec((AttentionLayerSpec("attention", case["hq"], case["hkv"], case["d"]),))
+        cache = PagedKVCache(spec, PagedKVCacheConfig(case["nb"], case["bs"], dtype=case["dtype"]))
+        layer = cache.layer("attention")
+        layer.keys.copy_(torch.randn(layer.keys.shape).to(case["dtype"]))
+        layer.values.copy_(torch.randn(layer.values.shape).to(case["dtype"]))
+        before_k = layer.keys.clone()
+        before_v = layer.values.clone()
+        md = PagedAttentionMetadata(
+            block_tables=case["tables"],
+            num_computed_tokens=case["computed"],
+            query_layouts=tuple(QL(p) for p in case["layouts"]),
+            num_reserved_query_tokens=case.get("reserved", ()),
+            num_readonly_prefix_blocks=case.get("readonly", ()),
+        )
+        t = md.num_query_tokens
+        q = torch.randn(t, case["hq"], case["d"]).to(case["dtype"])
+        k = torch.randn(t, case["hkv"], case["d"]).to(case["dtype"])
+        v = torch.randn(t, case["hkv"], case["d"]).to(case["dtype"])
+        scale = 1.0 / case["d"] ** 0.5
+        o = TorchPagedAttention(cache, md).forward("attention", q, k, v, scale=scale)
+        name = case["name"]
+        for key, tensor in (("q", q), ("k", k), ("v", v), ("o", o), ("k_before", before_k),
+                            ("v_before", before_v), ("k_after", layer.keys),
+                            ("v_after", layer.values)):
+            out[f"{name}_{key}"] = _as_storable(tensor)
+        meta = {kk: vv for kk, vv in case.items() if kk != "dtype"}
+        meta["dtype"] = str(case["dtype"]).replace("torch.", "")
+        meta["scale"] = scale
+        index.append(meta)
+    out["index_json"] = np.frombuffer(json.dumps(index).encode(), dtype=np.uint8)
+    np.savez_compressed(HERE / "paged_attn.npz", **out)
+
+
+def main() -> None:
+    torch.set_num_threads(1)
+    ref = _import_reference()
+    make_awq(ref)
+    make_meta(ref)
+    make_attention(ref)
+    for name in ("awq_golden.npz", "paged_meta.json", "paged_attn.npz"):
+        print(name, (HERE / name).stat().st_size, "bytes")
+
+
+if __name__ == "__main__":
+    main()

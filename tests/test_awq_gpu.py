@@ -1,0 +1,143 @@
+"""GPU parity of the B200 AWQ scheme against the CPU oracle.
+
+Matrix:
+  * the reference's own CUDA test matrix (tests/test_cuda_awq.py:19-57):
+    M in {1, 7, 64, 256}, K in {128, 384}, G=32, N=128 with bias, against
+    F.linear(x, dequantized, bias), atol 3e-2 / rtol 2e-2; and the TP shard
+    narrower than a group (K=896, G=128, N=64, M=7);
+  * the BASELINE config-1 shape (M=16, K=896, N=4864, G=128, scales in
+    [0.002, 0.02]) and tile-boundary shapes, against the fp64-accumulated
+    oracle with the north-star tolerance: max-abs <= 2e-2 and rel-L2 <= 1e-3;
+  * bit-exact dequantisation, determinism of the split-K reduction.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+from torch.nn import functional as F
+
+from light_vllm_b200 import _native
+from light_vllm_b200.awq import B200AWQScheme, b200_awq_dequantize, b200_awq_linear
+from oracle import awq as oawq
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda:0")
+MAX_ABS = 2e-2
+REL_L2 = 1e-3
+
+
+def _gpu(*arrays):
+    return [torch.from_numpy(np.ascontiguousarray(a)).to(DEV) for a in arrays]
+
+
+def _quantized(out_features: int, in_features: int, group: int, seed: int):
+    torch.manual_seed(seed)
+    weight = torch.randn(out_features, in_features, dtype=torch.float16)
+    qweight, qzeros, scales, deq = oawq.quantize_weight(weight, group)
+    return qweight, qzeros, scales, deq
+
+
+@pytest.mark.parametrize("num_tokens", [1, 7, 64, 256])
+@pytest.mark.parametrize("inner", [128, 384])
+def test_matches_dequantized_linear(num_tokens, inner):
+    qweight, qzeros, scales, deq = _quantized(128, inner, 32, 3)
+    torch.manual_seed(3)
+    x = torch.randn(num_tokens, inner, dtype=torch.float16, device=DEV)
+    bias = torch.randn(128, dtype=torch.float16, device=DEV)
+    qw, qz, sc, w = _gpu(qweight, qzeros, scales, deq)
+    expected = F.linear(x, w, bias)
+    actual = b200_awq_linear(x, qw, qz, sc, 32, bias)
+    torch.cuda.synchronize()
+    torch.testing.assert_close(actual, expected, atol=3e-2, rtol=2e-2)
+
+
+def test_tp_shard_narrower_than_group():
+    qweight, qzeros, scales, deq = _quantized(64, 896, 128, 7)
+    torch.manual_seed(7)
+    x = torch.randn(7, 896, dtype=torch.float16, device=DEV)
+    qw, qz, sc, w = _gpu(qweight, qzeros, scales, deq)
+    actual = b200_awq_linear(x, qw, qz, sc, 128, None)
+    torch.testing.assert_close(actual, F.linear(x, w), atol=3e-2, rtol=2e-2)
+
+
+def _check_against_oracle(m, k, n, g, seed, with_bias=True):
+    qweight, qzeros, scales = oawq.random_checkpoint(k, n, g, seed=seed)
+    rng = np.random.default_rng(seed + 1)
+    x = rng.standard_normal((m, k)).astype(np.float16)
+    bias = rng.standard_normal(n).astype(np.float16) if with_bias else None
+    expected = oawq.linear_fp32(x, qweight, qzeros, scales, g, bias)
+    qw, qz, sc, xg = _gpu(qweight, qzeros, scales, x)
+    bg = _gpu(bias)[0] if bias is not None else None
+    op = B200AWQScheme().prepare(qw, qz, sc, g, bg)
+    y = op(xg)
+    torch.cuda.synchronize()
+    assert _native.device_error() == 0
+    max_abs, rel = oawq.error_metrics(y.float().cpu().numpy(), expected)
+    assert max_abs <= MAX_ABS and rel <= REL_L2, (m, k, n, g, max_abs, rel)
+    return op, xg, y
+
+
+def test_baseline_config1_shape():
+    _check_against_oracle(16, 896, 4864, 128, seed=20261201)
+
+
+@pytest.mark.parametrize(
+    "m,k,n,g",
+    [
+        (1, 896, 4864, 128),
+        (2, 1024, 2112, 128),     # partial last n tile
+        (15, 96, 256, 32),        # k not a multiple of the 64-wide k tile
+        (17, 896, 4864, 128),     # BN=32 split-K
+        (33, 512, 1024, 64),      # BN=64
+        (65, 640, 512, 128),      # BN=128, no split
+        (129, 384, 768, 128),     # BN=256
+        (300, 256, 384, 32),      # two m tiles
+        (513, 1024, 1280, 128),   # three m tiles, 72B TP=8 QKV width
+        (16, 3584, 4608, 128),    # 7B merged QKV
+    ],
+)
+def test_shapes_against_oracle(m, k, n, g):
+    _check_against_oracle(m, k, n, g, seed=m * 7919 + k)
+
+
+def test_split_k_reduction_is_deterministic_and_reusable():
+    op, x, y = _check_against_oracle(16, 896, 4864, 128, seed=11)
+    for _ in range(3):
+        again = op(x)
+        assert torch.equal(again, y)
+    torch.cuda.synchronize()
+    assert _native.device_error() == 0
+
+
+def test_dequantize_is_bit_exact():
+    k, n, g = 256, 512, 64
+    qweight, qzeros, scales = oawq.random_checkpoint(k, n, g, seed=5)
+    expected = oawq.dequantize(qweight, qzeros, scales, g)
+    qw, qz, sc = _gpu(qweight, qzeros, scales)
+    w = b200_awq_dequantize(qw, qz, sc, g)
+    np.testing.assert_array_equal(w.cpu().numpy().view(np.uint16), expected.view(np.uint16))
+
+
+def test_multi_dim_inputs_keep_leading_shape():
+    qweight, qzeros, scales = oawq.random_checkpoint(256, 512, 128, seed=9)
+    qw, qz, sc = _gpu(qweight, qzeros, scales)
+    x = torch.randn(2, 3, 256, dtype=torch.float16, device=DEV)
+    y = B200AWQScheme().prepare(qw, qz, sc, 128, None)(x)
+    assert y.shape == (2, 3, 512)
+    flat = B200AWQScheme().prepare(qw, qz, sc, 128, None)(x.reshape(6, 256))
+    assert torch.equal(y.reshape(6, 512), flat)
+
+
+def test_prepare_rejects_bad_layouts():
+    qweight, qzeros, scales = oawq.random_checkpoint(256, 512, 128, seed=9)
+    qw, qz, sc = _gpu(qweight, qzeros, scales)
+    with pytest.raises(ValueError, match="group_size"):
+        B200AWQScheme().prepare(qw, qz, sc, 48, None)
+    with pytest.raises(ValueError, match="float16"):
+        B200AWQScheme().prepare(qw, qz, sc.float(), 128, None)
+    with pytest.raises(ValueError, match="bias"):
+        B200AWQScheme().prepare(qw, qz, sc, 128, torch.zeros(7, dtype=torch.float16, device=DEV))
+    with pytest.raises(ValueError, match="activations must be float16"):
+        B200AWQScheme().prepare(qw, qz, sc, 128, None)(torch.zeros(1, 256, device=DEV))

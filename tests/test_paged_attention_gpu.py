@@ -1,0 +1,291 @@
+"""GPU parity of the B200 paged-attention backend.
+
+* The reference's Triton test matrix (tests/test_triton_paged_attention.py):
+  packed GQA prefill for head sizes 32/80/128/256 in fp16/bf16, the Qwen
+  28q/4kv group, history across chunks, tree visibility, decode after
+  prefill, a shared read-only prefix and unused lookahead slots -- against the
+  CPU oracle with the reference's tolerances (fp16 3e-3, bf16 2e-2) and
+  bit-exact cache slots.
+* The golden fixtures produced by the reference's own TorchPagedAttention.
+* Decode batches on the split-context kernel up to the BASELINE config-2 shape
+  (64 sequences, contexts 512..4096, 28q/4kv, D=128, bf16) against a float64
+  evaluation of the same visible positions: max-abs <= 2e-2 and rel-L2 <= 1e-3
+  after rounding to the cache dtype.
+"""
+
+from __future__ import annotations
+
+import json
+from math import sqrt
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from light_vllm_b200 import _native
+from light_vllm_b200.kv_cache import (
+    AttentionLayerSpec,
+    KVCacheError,
+    ModelKVCacheSpec,
+    PagedAttentionMetadata,
+    PagedKVCache,
+    PagedKVCacheConfig,
+    QueryLayout,
+    linear_query_layout,
+)
+from light_vllm_b200.paged_attention import B200PagedAttentionBackend
+from oracle import awq as oawq
+from oracle import paged_attention as opa
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda:0")
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+def _layouts(*lengths):
+    return tuple(linear_query_layout(n) for n in lengths)
+
+
+def _cache(head_size, dtype, *, block_size=2, hq=4, hkv=2, num_blocks=16):
+    spec = ModelKVCacheSpec((AttentionLayerSpec("attention", hq, hkv, head_size),))
+    return PagedKVCache(spec, PagedKVCacheConfig(num_blocks, block_size, dtype=dtype, device=DEV))
+
+
+def _run_and_compare(cache, md, q, k, v, *, tol=None):
+    """Run the B200 backend and the CPU oracle on copies of the same cache."""
+
+    layer = cache.layer("attention")
+    k_before = layer.keys.cpu()
+    v_before = layer.values.cpu()
+    scale = 1.0 / sqrt(q.shape[-1])
+    actual = B200PagedAttentionBackend().create(cache, md).forward("attention", q, k, v, scale=scale)
+    torch.cuda.synchronize()
+    assert _native.device_error() == 0
+    kc, vc = k_before.clone(), v_before.clone()
+    expected = opa.attend(q.cpu(), k.cpu(), v.cpu(), kc, vc,
+                          md.block_tables, md.num_computed_tokens,
+                          [layout.parent_indices for layout in md.query_layouts],
+                          scale=scale, reserved=md.num_reserved_query_tokens)
+    if tol is None:
+        tol = 3e-3 if q.dtype == torch.float16 else 2e-2
+    torch.testing.assert_close(actual.cpu(), expected, atol=tol, rtol=tol)
+    # Bit-exact slot contents (every slot, not only the written ones).
+    assert torch.equal(layer.keys.cpu(), kc)
+    assert torch.equal(layer.values.cpu(), vc)
+    return actual
+
+
+def _randomise(cache):
+    layer = cache.layer("attention")
+    layer.keys.copy_(torch.randn(layer.keys.shape, device=DEV).to(layer.keys.dtype))
+    layer.values.copy_(torch.randn(layer.values.shape, device=DEV).to(layer.values.dtype))
+
+
+@pytest.mark.parametrize("head_size", (32, 80, 128, 256))
+@pytest.mark.parametrize("dtype", (torch.float16, torch.bfloat16))
+def test_packed_gqa_prefill(head_size, dtype):
+    torch.manual_seed(20260817)
+    cache = _cache(head_size, dtype, block_size=4)
+    _randomise(cache)
+    md = PagedAttentionMetadata(block_tables=((7, 1), (4,)), num_computed_tokens=(0, 0),
+                                query_layouts=_layouts(6, 3))
+    q = torch.randn(9, 4, head_size, device=DEV, dtype=dtype)
+    k = torch.randn(9, 2, head_size, device=DEV, dtype=dtype)
+    v = torch.randn(9, 2, head_size, device=DEV, dtype=dtype)
+    _run_and_compare(cache, md, q, k, v)
+
+
+def test_qwen_gqa_group():
+    torch.manual_seed(20260822)
+    cache = _cache(128, torch.bfloat16, block_size=4, hq=28, hkv=4)
+    _randomise(cache)
+    md = PagedAttentionMetadata(block_tables=((7, 1), (4,)), num_computed_tokens=(0, 0),
+                                query_layouts=_layouts(6, 3))
+    q = torch.randn(9, 28, 128, device=DEV, dtype=torch.bfloat16)
+    k = torch.randn(9, 4, 128, device=DEV, dtype=torch.bfloat16)
+    v = torch.randn(9, 4, 128, device=DEV, dtype=torch.bfloat16)
+    _run_and_compare(cache, md, q, k, v)
+
+
+def test_qwen_gqa_across_history_chunks():
+    torch.manual_seed(20260822)
+    cache = _cache(128, torch.bfloat16, block_size=16, hq=28, hkv=4)
+    prefix = 130
+    pk = torch.randn(prefix, 4, 128, device=DEV, dtype=torch.bfloat16)
+    pv = torch.randn(prefix, 4, 128, device=DEV, dtype=torch.bfloat16)
+    cache.write("attention", pk, pv, torch.arange(prefix, device=DEV))
+    md = PagedAttentionMetadata(block_tables=(tuple(range(9)),), num_computed_tokens=(prefix,),
+                                query_layouts=_layouts(1))
+    q = torch.randn(1, 28, 128, device=DEV, dtype=torch.bfloat16)
+    k = torch.randn(1, 4, 128, device=DEV, dtype=torch.bfloat16)
+    v = torch.randn(1, 4, 128, device=DEV, dtype=torch.bfloat16)
+    _run_and_compare(cache, md, q, k, v)
+
+
+def test_packed_tree_visibility():
+    torch.manual_seed(20260819)
+    cache = _cache(64, torch.float16)
+    _randomise(cache)
+    md = PagedAttentionMetadata(block_tables=((7, 1), (4, 6)), num_computed_tokens=(0, 0),
+                                query_layouts=(QueryLayout((-1, 0, 0, 2)), QueryLayout((-1, 0, 0))))
+    q = torch.randn(7, 4, 64, device=DEV, dtype=torch.float16)
+    k = torch.randn(7, 2, 64, device=DEV, dtype=torch.float16)
+    v = torch.randn(7, 2, 64, device=DEV, dtype=torch.float16)
+    _run_and_compare(cache, md, q, k, v)
+
+
+def test_decode_after_prefill():
+    torch.manual_seed(20260817)
+    cache = _cache(64, torch.float16)
+    _randomise(cache)
+    pre = PagedAttentionMetadata(block_tables=((3, 0, 5), (2, 6)), num_computed_tokens=(0, 0),
+                                 query_layouts=_layouts(5, 3))
+    _run_and_compare(cache, pre, *(torch.randn(8, h, 64, device=DEV, dtype=torch.float16)
+                                   for h in (4, 2, 2)))
+    dec = PagedAttentionMetadata(block_tables=((3, 0, 5), (2, 6)), num_computed_tokens=(5, 3),
+                                 query_layouts=_layouts(1, 1))
+    _run_and_compare(cache, dec, *(torch.randn(2, h, 64, device=DEV, dtype=torch.float16)
+                                   for h in (4, 2, 2)))
+
+
+def test_shared_readonly_prefix():
+    torch.manual_seed(20260817)
+    cache = _cache(64, torch.float16)
+    _randomise(cache)
+    cache.write("attention", torch.randn(2, 2, 64, device=DEV, dtype=torch.float16),
+                torch.randn(2, 2, 64, device=DEV, dtype=torch.float16), torch.tensor([0, 1], device=DEV))
+    md = PagedAttentionMetadata(block_tables=((0, 5), (0, 7)), num_computed_tokens=(2, 2),
+                                query_layouts=_layouts(1, 1), num_readonly_prefix_blocks=(1, 1))
+    _run_and_compare(cache, md, *(torch.randn(2, h, 64, device=DEV, dtype=torch.float16)
+                                  for h in (4, 2, 2)))
+
+
+def test_unused_lookahead_slots():
+    torch.manual_seed(20260817)
+    cache = _cache(64, torch.float16)
+    _randomise(cache)
+    md = PagedAttentionMetadata(block_tables=((8, 3, 12), (10, 14)), num_computed_tokens=(0, 0),
+                                query_layouts=_layouts(3, 1), num_reserved_query_tokens=(5, 4))
+    _run_and_compare(cache, md, *(torch.randn(4, h, 64, device=DEV, dtype=torch.float16)
+                                  for h in (4, 2, 2)))
+
+
+ATTN = np.load(GOLDEN / "paged_attn.npz")
+ATTN_INDEX = json.loads(bytes(ATTN["index_json"]).decode())
+
+
+def _golden(name, key, dtype):
+    arr = ATTN[f"{name}_{key}"]
+    if dtype == "bfloat16":
+        return torch.from_numpy(arr.view(np.int16)).view(torch.bfloat16)
+    return torch.from_numpy(arr)
+
+
+@pytest.mark.parametrize("case", [c for c in ATTN_INDEX if c["dtype"] != "float32"],
+                         ids=[c["name"] for c in ATTN_INDEX if c["dtype"] != "float32"])
+def test_reference_golden_outputs(case):
+    dtype = getattr(torch, case["dtype"])
+    cache = _cache(case["d"], dtype, block_size=case["bs"], hq=case["hq"], hkv=case["hkv"],
+                   num_blocks=case["nb"])
+    layer = cache.layer("attention")
+    layer.keys.copy_(_golden(case["name"], "k_before", case["dtype"]).to(DEV))
+    layer.values.copy_(_golden(case["name"], "v_before", case["dtype"]).to(DEV))
+    md = PagedAttentionMetadata(
+        block_tables=tuple(tuple(t) for t in case["tables"]),
+        num_computed_tokens=tuple(case["computed"]),
+        query_layouts=tuple(QueryLayout(tuple(p)) for p in case["layouts"]),
+        num_reserved_query_tokens=tuple(case.get("reserved") or ()),
+        num_readonly_prefix_blocks=tuple(case.get("readonly") or ()),
+    )
+    q, k, v = (_golden(case["name"], key, case["dtype"]).to(DEV) for key in ("q", "k", "v"))
+    out = B200PagedAttentionBackend().create(cache, md).forward("attention", q, k, v, scale=case["scale"])
+    tol = 3e-3 if dtype == torch.float16 else 2e-2
+    torch.testing.assert_close(out.cpu(), _golden(case["name"], "o", case["dtype"]), atol=tol, rtol=tol)
+    assert torch.equal(layer.keys.cpu(), _golden(case["name"], "k_after", case["dtype"]))
+    assert torch.equal(layer.values.cpu(), _golden(case["name"], "v_after", case["dtype"]))
+
+
+def decode_batch(num_seqs, ctx_lo, ctx_hi, hq, hkv, d, dtype, *, num_blocks, seed, block_size=16):
+    """Seeded decode workload: contexts ~ U[ctx_lo, ctx_hi], tables carved from
+    a random permutation of the block pool, K/V pages ~ N(0, 1)."""
+
+    gen = torch.Generator().manual_seed(seed)
+    ctx = torch.randint(ctx_lo, ctx_hi + 1, (num_seqs,), generator=gen).tolist()
+    perm = torch.randperm(num_blocks, generator=gen).tolist()
+    tables, offset = [], 0
+    for c in ctx:
+        n = -(-c // block_size)
+        tables.append(tuple(perm[offset:offset + n]))
+        offset += n
+    assert offset <= num_blocks
+    md = PagedAttentionMetadata(block_tables=tuple(tables), num_computed_tokens=tuple(c - 1 for c in ctx),
+                                query_layouts=_layouts(*([1] * num_seqs)))
+    spec = ModelKVCacheSpec((AttentionLayerSpec("attention", hq, hkv, d),))
+    cache = PagedKVCache(spec, PagedKVCacheConfig(num_blocks, block_size, dtype=dtype, device=DEV))
+    layer = cache.layer("attention")
+    torch.manual_seed(seed)
+    layer.keys.normal_()
+    layer.values.normal_()
+    q = torch.randn(num_seqs, hq, d, device=DEV, dtype=dtype)
+    k = torch.randn(num_seqs, hkv, d, device=DEV, dtype=dtype)
+    v = torch.randn(num_seqs, hkv, d, device=DEV, dtype=dtype)
+    return cache, md, q, k, v
+
+
+def _check_decode(cache, md, q, k, v):
+    scale = 1.0 / sqrt(q.shape[-1])
+    out = B200PagedAttentionBackend().create(cache, md).forward("attention", q, k, v, scale=scale)
+    torch.cuda.synchronize()
+    assert _native.device_error() == 0
+    layer = cache.layer("attention")
+    slots = md.slot_mapping(block_size=cache.config.block_size, device=DEV)
+    flat_k = layer.keys.view(-1, *k.shape[1:])
+    assert torch.equal(flat_k.index_select(0, slots), k)
+    expected = opa.attend_dense_fp64(
+        q.cpu(), layer.keys.cpu(), layer.values.cpu(), md.block_tables, md.num_computed_tokens,
+        [layout.parent_indices for layout in md.query_layouts], scale=scale)
+    rounded = expected.to(q.dtype).double()
+    max_abs, rel = oawq.error_metrics(out.double().cpu().numpy(), rounded.numpy())
+    assert max_abs <= 2e-2 and rel <= 1e-3, (max_abs, rel)
+    return out
+
+
+@pytest.mark.parametrize("dtype", (torch.bfloat16, torch.float16))
+@pytest.mark.parametrize("hq,hkv,d", [(28, 4, 128), (8, 8, 128), (32, 2, 64), (16, 1, 128)])
+def test_decode_split_context(dtype, hq, hkv, d):
+    cache, md, q, k, v = decode_batch(6, 1, 700, hq, hkv, d, dtype, num_blocks=512, seed=hq * 31 + d)
+    _check_decode(cache, md, q, k, v)
+
+
+def test_decode_baseline_config2():
+    cache, md, q, k, v = decode_batch(64, 512, 4096, 28, 4, 128, torch.bfloat16, num_blocks=40000,
+                                      seed=20261201)
+    _check_decode(cache, md, q, k, v)
+
+
+def test_decode_single_token_context():
+    cache, md, q, k, v = decode_batch(3, 1, 1, 28, 4, 128, torch.bfloat16, num_blocks=8, seed=3)
+    _check_decode(cache, md, q, k, v)
+
+
+def test_layer_runs_once_and_dtype_is_checked():
+    cache, md, q, k, v = decode_batch(2, 5, 40, 28, 4, 128, torch.bfloat16, num_blocks=16, seed=4)
+    ctx = B200PagedAttentionBackend().create(cache, md)
+    ctx.forward("attention", q, k, v, scale=0.1)
+    with pytest.raises(KVCacheError, match="ran more than once"):
+        ctx.forward("attention", q, k, v, scale=0.1)
+    ctx2 = B200PagedAttentionBackend().create(cache, md)
+    with pytest.raises(KVCacheError, match="dtype and device"):
+        ctx2.forward("attention", q.half(), k.half(), v.half(), scale=0.1)
+    assert ctx.layer_ids == frozenset({"attention"})
+
+
+def test_strided_qkv_views_are_accepted():
+    """Q/K/V as views of one fused QKV row, as the model produces them."""
+
+    cache, md, q, k, v = decode_batch(4, 20, 90, 28, 4, 128, torch.bfloat16, num_blocks=64, seed=8)
+    fused = torch.cat([q.reshape(4, -1), k.reshape(4, -1), v.reshape(4, -1)], dim=1)
+    qv, kv_, vv = fused.split([28 * 128, 4 * 128, 4 * 128], dim=1)
+    out = _check_decode(cache, md, qv.view(4, 28, 128), kv_.view(4, 4, 128), vv.view(4, 4, 128))
+    assert out.shape == (4, 28, 128)
