@@ -70,10 +70,15 @@ def _run_and_compare(cache, md, q, k, v, *, tol=None):
     if tol is None:
         tol = 3e-3 if q.dtype == torch.float16 else 2e-2
     torch.testing.assert_close(actual.cpu(), expected, atol=tol, rtol=tol)
-    # Bit-exact slot contents (every slot, not only the written ones).
-    assert torch.equal(layer.keys.cpu(), kc)
-    assert torch.equal(layer.values.cpu(), vc)
+    # Bit-exact slot contents (every slot, not only the written ones); compared
+    # as bit patterns because never-written slots may hold NaN encodings.
+    assert torch.equal(_bits(layer.keys.cpu()), _bits(kc))
+    assert torch.equal(_bits(layer.values.cpu()), _bits(vc))
     return actual
+
+
+def _bits(t):
+    return t.view(torch.int16)
 
 
 def _randomise(cache):
@@ -202,8 +207,8 @@ def test_reference_golden_outputs(case):
     out = B200PagedAttentionBackend().create(cache, md).forward("attention", q, k, v, scale=case["scale"])
     tol = 3e-3 if dtype == torch.float16 else 2e-2
     torch.testing.assert_close(out.cpu(), _golden(case["name"], "o", case["dtype"]), atol=tol, rtol=tol)
-    assert torch.equal(layer.keys.cpu(), _golden(case["name"], "k_after", case["dtype"]))
-    assert torch.equal(layer.values.cpu(), _golden(case["name"], "v_after", case["dtype"]))
+    assert torch.equal(_bits(layer.keys.cpu()), _bits(_golden(case["name"], "k_after", case["dtype"])))
+    assert torch.equal(_bits(layer.values.cpu()), _bits(_golden(case["name"], "v_after", case["dtype"])))
 
 
 def decode_batch(num_seqs, ctx_lo, ctx_hi, hq, hkv, d, dtype, *, num_blocks, seed, block_size=16):
@@ -241,7 +246,7 @@ def _check_decode(cache, md, q, k, v):
     layer = cache.layer("attention")
     slots = md.slot_mapping(block_size=cache.config.block_size, device=DEV)
     flat_k = layer.keys.view(-1, *k.shape[1:])
-    assert torch.equal(flat_k.index_select(0, slots), k)
+    assert torch.equal(_bits(flat_k.index_select(0, slots)), _bits(k.contiguous()))
     expected = opa.attend_dense_fp64(
         q.cpu(), layer.keys.cpu(), layer.values.cpu(), md.block_tables, md.num_computed_tokens,
         [layout.parent_indices for layout in md.query_layouts], scale=scale)
