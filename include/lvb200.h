@@ -89,6 +89,25 @@ LVB_API int lvb_awq_linear(const uint16_t *x, const int32_t *qweight, const int3
                    int64_t k, int64_t n, int64_t group_size, void *workspace,
                    size_t workspace_bytes, lvb_stream_t stream);
 
+/* Same computation as lvb_awq_linear, for callers that cannot allocate
+ * device memory: hosts whose device memory is wholly owned by another
+ * allocator that they may not grow, or threads on a latency-critical path where
+ * the device-wide synchronisation of cudaMalloc is not acceptable.  It takes no
+ * workspace; the split-K scratch is a fixed 6 MiB array inside the library
+ * (every GPU that loads the library holds it until exit), so calls whose plan
+ * needs more than that are rejected with LVB_ERR_UNSUPPORTED (no call on a
+ * GPU with up to 192 SMs does).  It calls no cudaMalloc/cudaFree.  The first
+ * call on a device looks up the array's device address (set-up, once per
+ * device, on the calling thread's current device); make that first call before
+ * any stream capture.  Every call on a device shares the one array, so calls
+ * that overlap on the GPU (different streams, no ordering between them) race
+ * and may produce wrong results; order them on one stream.  No counterpart in
+ * the reference. */
+LVB_API int lvb_awq_linear_static(const uint16_t *x, const int32_t *qweight,
+                                  const int32_t *qzeros, const uint16_t *scales,
+                                  const uint16_t *bias, uint16_t *y, int64_t m, int64_t k,
+                                  int64_t n, int64_t group_size, lvb_stream_t stream);
+
 /* w[k, n] = fp16(q - z) * s, the full fp16 weight.  Replaces `awq_dequantize`
  * (csrc/awq/bindings.cpp:10-13, gemm_kernels.cu:391-439). */
 LVB_API int lvb_awq_dequantize(const int32_t *qweight, const int32_t *qzeros, const uint16_t *scales,

@@ -42,6 +42,9 @@ PROTOTYPES: dict[str, tuple[object, tuple[object, ...]]] = {
         _int,
         (_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _i64, _i64, _i64, _i64, _c_ptr, _size, _c_ptr),
     ),
+    "lvb_awq_linear_static": (
+        _int, (_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _i64, _i64, _i64, _i64, _c_ptr),
+    ),
     "lvb_awq_dequantize": (_int, (_c_ptr, _c_ptr, _c_ptr, _c_ptr, _i64, _i64, _i64, _c_ptr)),
     "lvb_paged_kv_write": (
         _int,

@@ -255,6 +255,35 @@ int launch_general(const lvb::attn::AttnArgs &a, int64_t num_tokens, cudaStream_
   return LVB_OK;
 }
 
+// ------------------------------------------------------------------------
+// Fixed scratch for lvb_awq_linear_static
+// ------------------------------------------------------------------------
+// Callers that cannot allocate device memory get the split-K scratch from this
+// file-scope array instead.  6 MiB covers every split-K plan on GPUs with up to
+// 192 SMs (at most SMs x 64 x 128 fp32 partials plus one semaphore per tile).
+// It is part of the module image: every device that loads the library holds it
+// until the process exits.
+constexpr size_t kAwqStaticScratchBytes = size_t(6) << 20;
+__device__ __align__(256) unsigned char g_awq_static_scratch[kAwqStaticScratchBytes];
+
+// Device address of the array on each device.  In host code the symbol is a
+// host-side stand-in, not a device address, so it is looked up once per device
+// (with that device current) and only the looked-up pointer reaches a kernel.
+void *g_awq_static_scratch_addr[kMaxDevices] = {nullptr};
+std::mutex g_awq_static_scratch_mu;
+
+int awq_static_scratch(int dev, void **out) {
+  std::lock_guard<std::mutex> lock(g_awq_static_scratch_mu);
+  if (g_awq_static_scratch_addr[dev] == nullptr) {
+    void *p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_awq_static_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_awq_static_scratch)");
+    g_awq_static_scratch_addr[dev] = p;
+  }
+  *out = g_awq_static_scratch_addr[dev];
+  return LVB_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -492,6 +521,51 @@ int lvb_paged_attention(const uint16_t *query, int64_t query_token_stride,
                             : launch_decode<false, 64>(a, num_seqs, num_blocks, dev, s);
   }
   return bf16 ? launch_general<true>(a, num_tokens, s) : launch_general<false>(a, num_tokens, s);
+}
+
+int lvb_awq_linear_static(const uint16_t *x, const int32_t *qweight, const int32_t *qzeros,
+                          const uint16_t *scales, const uint16_t *bias, uint16_t *y, int64_t m,
+                          int64_t k, int64_t n, int64_t group_size, lvb_stream_t stream) {
+  if (m < 0 || k <= 0 || n <= 0) return fail(LVB_ERR_INVALID, "invalid AWQ shape m=%lld k=%lld n=%lld",
+                                              (long long)m, (long long)k, (long long)n);
+  if (m == 0) return LVB_OK;
+  if (m > INT_MAX || k > INT_MAX || n > INT_MAX) return fail(LVB_ERR_UNSUPPORTED, "AWQ dimension exceeds int32");
+  if (group_size <= 0 || group_size % 8 != 0 || k % group_size != 0)
+    return fail(LVB_ERR_INVALID, "AWQ group_size %lld must be a positive multiple of 8 dividing k=%lld",
+                (long long)group_size, (long long)k);
+  if (n % 32 != 0) return fail(LVB_ERR_INVALID, "AWQ output width %lld must be divisible by 32", (long long)n);
+  if (k % 8 != 0) return fail(LVB_ERR_INVALID, "AWQ input width %lld must be divisible by 8", (long long)k);
+  if (!x || !qweight || !qzeros || !scales || !y) return fail(LVB_ERR_INVALID, "AWQ null pointer argument");
+  if (!aligned16(x) || !aligned16(qweight) || !aligned16(scales))
+    return fail(LVB_ERR_INVALID, "AWQ x, qweight and scales must be 16-byte aligned");
+  int dev = 0;
+  int rc = current_device(&dev);
+  if (rc != LVB_OK) return rc;
+  const AwqPlan plan = awq_plan(m, k, n, sm_count(dev));
+  const size_t need = plan.sem_bytes + plan.part_bytes;
+  if (need > kAwqStaticScratchBytes)
+    return fail(LVB_ERR_UNSUPPORTED,
+                "lvb_awq_linear_static: m=%lld k=%lld n=%lld needs %zu bytes of split-K scratch, above its "
+                "fixed %zu-byte buffer; call lvb_awq_linear with a workspace instead",
+                (long long)m, (long long)k, (long long)n, need, kAwqStaticScratchBytes);
+  void *scratch = nullptr;
+  rc = awq_static_scratch(dev, &scratch);
+  if (rc != LVB_OK) return rc;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (plan.sem_bytes > 0) {
+    // The semaphores must start at zero; a completed call leaves them zero, and
+    // clearing them here also covers a previous call that was aborted.
+    cudaError_t e = cudaMemsetAsync(scratch, 0, plan.sem_bytes, s);
+    if (e != cudaSuccess) return cuda_fail(e, "clearing the static split-K semaphores");
+  }
+  uint8_t *ws = static_cast<uint8_t *>(scratch);
+  switch (plan.bn) {
+    case 16: return launch_awq<16>(plan, x, qweight, qzeros, scales, bias, y, m, k, n, group_size, ws, dev, s);
+    case 32: return launch_awq<32>(plan, x, qweight, qzeros, scales, bias, y, m, k, n, group_size, ws, dev, s);
+    case 64: return launch_awq<64>(plan, x, qweight, qzeros, scales, bias, y, m, k, n, group_size, ws, dev, s);
+    case 128: return launch_awq<128>(plan, x, qweight, qzeros, scales, bias, y, m, k, n, group_size, ws, dev, s);
+    default: return launch_awq<256>(plan, x, qweight, qzeros, scales, bias, y, m, k, n, group_size, ws, dev, s);
+  }
 }
 
 }  // extern "C"
