@@ -203,7 +203,7 @@ def capture(torch, fn):
 # ----------------------------------------------------------------------------
 # AWQ detail
 # ----------------------------------------------------------------------------
-def awq_detail(torch, peaks, steps: int) -> list[dict]:
+def awq_detail(torch, peaks, steps: int, shapes_arg: str | None = None) -> list[dict]:
     import numpy as np
 
     from light_vllm_b200.awq import B200AWQScheme
@@ -217,6 +217,9 @@ def awq_detail(torch, peaks, steps: int) -> list[dict]:
         ("7B down", 16, 18944, 3584, 128),
         ("7B gate_up prefill", 2048, 3584, 37888, 128),
     ]
+    if shapes_arg:
+        shapes = [("custom",) + tuple(int(v) for v in item.split(",")) + (128,)
+                  for item in shapes_arg.split(";") if item]
     out = []
     l2 = 126 * 1024 * 1024
     for name, m, k, n, g in shapes:
@@ -292,6 +295,11 @@ def main() -> int:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
     ap.add_argument("--no-awq", action="store_true", help="skip the AWQ detail measurements")
+    ap.add_argument("--only", choices=("all", "attention", "awq"), default="all",
+                    help="run one part (profiling); 'awq' prints only the AWQ detail")
+    ap.add_argument("--awq-shapes", default=None,
+                    help="AWQ detail shapes as 'm,k,n[;m,k,n...]' (group 128)")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline (profiling)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -319,6 +327,13 @@ def main() -> int:
     from light_vllm_b200.paged_attention import B200PagedAttentionBackend
 
     peaks = measured_peaks()
+    if args.only == "awq":
+        detail = awq_detail(torch, peaks, args.steps, args.awq_shapes)
+        if rank == 0:
+            print(json.dumps({"awq": detail}), flush=True)
+        if dist is not None:
+            dist.destroy_process_group()
+        return 0
     cache, md, q, k, v, ctx = make_workload(torch, device)
     nbytes = algorithmic_bytes(ctx)
     scale = 1.0 / math.sqrt(CFG["d"])
@@ -419,11 +434,12 @@ def main() -> int:
         "clocks": clock_summary,
     }
     if rank == 0 and world == 1:
-        result["cpu_baseline"] = cpu_baseline(torch, cache, md, q, k, v, ctx)
-        if not args.no_awq:
+        if not args.no_cpu:
+            result["cpu_baseline"] = cpu_baseline(torch, cache, md, q, k, v, ctx)
+        if not args.no_awq and args.only == "all":
             del cache
             torch.cuda.empty_cache()
-            result["awq"] = awq_detail(torch, peaks, args.steps)
+            result["awq"] = awq_detail(torch, peaks, args.steps, args.awq_shapes)
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()

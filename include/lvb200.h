@@ -45,7 +45,8 @@ enum lvb_status {
   LVB_ERR_INVALID = 1,     /* bad shape, size, alignment or pointer (ValueError) */
   LVB_ERR_UNSUPPORTED = 2, /* valid request outside what the kernels cover   */
   LVB_ERR_CUDA = 3,        /* a CUDA runtime call failed (RuntimeError)      */
-  LVB_ERR_WORKSPACE = 4    /* caller's workspace smaller than required       */
+  LVB_ERR_WORKSPACE = 4,   /* caller's workspace smaller than required       */
+  LVB_ERR_METADATA = 5     /* block tables violate the paged-cache contract (KVCacheError) */
 };
 
 enum lvb_dtype { LVB_DTYPE_F16 = 0, LVB_DTYPE_BF16 = 1 };
@@ -79,7 +80,7 @@ LVB_API size_t lvb_awq_workspace_bytes(int64_t m, int64_t k, int64_t n, int64_t 
  * [k/group, n/8], scales fp16 [k/group, n]; nibble p of a word holds column
  * 8j + (0,2,4,6,1,3,5,7)[p]).  fp32 accumulation on tcgen05 tensor cores.
  * x and y are row-major with row strides k and n; `bias` may be NULL.
- * Requirements: n % 32 == 0, k % 8 == 0, group_size % 8 == 0,
+ * Requirements: n % 32 == 0, k % 8 == 0, group_size % 32 == 0,
  * k % group_size == 0, 16-byte aligned x / qweight / scales / workspace.  Replaces `awq_gemm`
  * (csrc/awq/bindings.cpp:10-13, gemm_kernels.cu:444-501) together with the
  * M>255 dequantise + cuBLAS path and the bias add of
@@ -147,7 +148,31 @@ LVB_API int lvb_kv_scatter(const uint16_t *key, int64_t key_token_stride, const 
                    const int64_t *slots, int64_t num_tokens, int64_t num_kv_heads,
                    int64_t head_size, int64_t num_slots, int dtype, lvb_stream_t stream);
 
-/* Bytes of workspace `lvb_paged_attention` needs (split-context partials). */
+/* Host-only (no device work): validate one step's block tables and pack the
+ * int32 payload the K/V-write and attention kernels read.  Inputs: the
+ * concatenated block ids of every request with table_offsets[num_seqs + 1]
+ * row offsets, and per request the computed-token count, the query length,
+ * the reserved query slots (>= query length) and the read-only prefix block
+ * count.  The rules, their order and the messages are those of
+ * PagedAttentionMetadata.validate_block_tables
+ * (runtime/execution/paged_attention.py:138-172); a violation returns
+ * LVB_ERR_METADATA with the reference's message.  On success `out` holds
+ * [block tables padded to *table_stride_out columns | num_computed |
+ * query_start_loc (num_seqs + 1) | request_indices (*num_tokens_out)], the
+ * payload of one host-to-device copy (triton_paged_attention.py:422-440).
+ * out_capacity (int32 elements) must be at least
+ * num_seqs * max_table + 2 * num_seqs + 1 + num_tokens. */
+LVB_API int lvb_pack_step_metadata(const int32_t *block_ids, const int64_t *table_offsets,
+                                   const int32_t *num_computed, const int32_t *query_lengths,
+                                   const int32_t *reserved, const int32_t *readonly,
+                                   int64_t num_seqs, int64_t num_blocks, int64_t block_size,
+                                   int32_t *out, int64_t out_capacity,
+                                   int64_t *table_stride_out, int64_t *num_tokens_out);
+
+/* Bytes of workspace `lvb_paged_attention` needs: split-context partial
+ * outputs and log-sum-exps, then one merge semaphore per (request, KV head).
+ * A workspace must be zero-filled once before its first use; every call
+ * leaves its semaphores zero again. */
 LVB_API size_t lvb_paged_attention_workspace_bytes(int64_t num_seqs, int64_t num_q_heads,
                                            int64_t num_kv_heads, int64_t head_size,
                                            int64_t max_seq_len);

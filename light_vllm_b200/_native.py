@@ -22,6 +22,7 @@ LVB_ERR_INVALID = 1
 LVB_ERR_UNSUPPORTED = 2
 LVB_ERR_CUDA = 3
 LVB_ERR_WORKSPACE = 4
+LVB_ERR_METADATA = 5
 
 DTYPE_F16 = 0
 DTYPE_BF16 = 1
@@ -56,6 +57,11 @@ PROTOTYPES: dict[str, tuple[object, tuple[object, ...]]] = {
         (_c_ptr, _i64, _c_ptr, _i64, _c_ptr, _c_ptr, _c_ptr, _i64, _i64, _i64, _i64, _int, _c_ptr),
     ),
     "lvb_paged_attention_workspace_bytes": (_size, (_i64, _i64, _i64, _i64, _i64)),
+    "lvb_pack_step_metadata": (
+        _int,
+        (_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _i64, _i64, _i64, _c_ptr, _i64,
+         ctypes.POINTER(_i64), ctypes.POINTER(_i64)),
+    ),
     "lvb_paged_attention": (
         _int,
         (_c_ptr, _i64, _c_ptr, _c_ptr, _c_ptr, _i64, _c_ptr, _i64, _c_ptr, _c_ptr, _c_ptr, _c_ptr,
@@ -98,6 +104,10 @@ def check(status: int, what: str) -> None:
         return
     message = library().lvb_last_error().decode(errors="replace")
     text = f"{what}: {message}"
+    if status == LVB_ERR_METADATA:
+        from light_vllm_b200.kv_cache import KVCacheError
+
+        raise KVCacheError(message)
     if status in (LVB_ERR_INVALID, LVB_ERR_UNSUPPORTED, LVB_ERR_WORKSPACE):
         raise ValueError(text)
     raise RuntimeError(text)

@@ -16,8 +16,10 @@
 
 #include "../../include/lvb200.h"
 #include "awq_gemm.cuh"
+#include "awq_gemv.cuh"
 #include "lvb_common.cuh"
 #include "paged_attention.cuh"
+#include "step_metadata.cuh"
 
 namespace {
 
@@ -135,24 +137,9 @@ int launch_awq(const AwqPlan &plan, const uint16_t *x, const int32_t *qweight,
   int rc = ensure_smem(kernel, C::kSmemBytes, dev, smem_done);
   if (rc != LVB_OK) return rc;
 
-  CUtensorMap qmap, xmap;
-  {
-    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(n / 8), static_cast<cuuint64_t>(k)};
-    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(n / 8) * 4};
-    const cuuint32_t box[2] = {lvb::awq::kWordsPerRow, lvb::awq::kTileK};
-    rc = encode_map(&qmap, CU_TENSOR_MAP_DATA_TYPE_INT32, 2, qweight, dims, strides, box,
-                    CU_TENSOR_MAP_SWIZZLE_NONE);
-    if (rc != LVB_OK) return rc;
-  }
-  {
-    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(m)};
-    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(k) * 2};
-    const cuuint32_t box[2] = {lvb::awq::kTileK, static_cast<cuuint32_t>(BN)};
-    rc = encode_map(&xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, x, dims, strides, box,
-                    CU_TENSOR_MAP_SWIZZLE_128B);
-    if (rc != LVB_OK) return rc;
-  }
   lvb::awq::Params p{};
+  p.x = x;
+  p.qweight = qweight;
   p.qzeros = qzeros;
   p.scales = scales;
   p.bias = bias;
@@ -167,10 +154,62 @@ int launch_awq(const AwqPlan &plan, const uint16_t *x, const int32_t *qweight,
   p.splits = plan.splits;
   p.n_tiles = plan.n_tiles;
   dim3 grid(plan.n_tiles, plan.m_tiles, plan.splits);
-  kernel<<<grid, lvb::awq::kThreads, C::kSmemBytes, stream>>>(qmap, xmap, p);
+  kernel<<<grid, lvb::awq::kThreads, C::kSmemBytes, stream>>>(p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "awq_gemm_kernel launch");
   return LVB_OK;
+}
+
+template <int BN, bool kSingleGroup>
+int launch_awq_gemv(const AwqPlan &plan, const uint16_t *x, const int32_t *qweight,
+                    const int32_t *qzeros, const uint16_t *scales, const uint16_t *bias, uint16_t *y,
+                    int64_t m, int64_t k, int64_t n, int64_t g, uint8_t *ws, int dev,
+                    cudaStream_t stream) {
+  using C = lvb::awq::GvConfig<BN>;
+  static bool smem_done[kMaxDevices] = {false};
+  auto kernel = lvb::awq::awq_gemv_kernel<BN, kSingleGroup>;
+  int rc = ensure_smem(kernel, C::kSmemBytes, dev, smem_done);
+  if (rc != LVB_OK) return rc;
+  lvb::awq::Params p{};
+  p.x = x;
+  p.qweight = qweight;
+  p.qzeros = qzeros;
+  p.scales = scales;
+  p.bias = bias;
+  p.y = y;
+  p.semaphores = reinterpret_cast<uint32_t *>(ws);
+  p.partials = plan.splits > 1 ? reinterpret_cast<float *>(ws + plan.sem_bytes) : nullptr;
+  p.M = static_cast<int>(m);
+  p.K = static_cast<int>(k);
+  p.N = static_cast<int>(n);
+  p.G = static_cast<int>(g);
+  p.k_tiles = plan.k_tiles;
+  p.splits = plan.splits;
+  p.n_tiles = plan.n_tiles;
+  dim3 grid(plan.n_tiles, plan.m_tiles, plan.splits);
+  kernel<<<grid, lvb::awq::kGvThreads, C::kSmemBytes, stream>>>(p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "awq_gemv_kernel launch");
+  return LVB_OK;
+}
+
+// Decode-sized batches (BN <= 64) take the group-scaled integer kernel,
+// larger ones the fp16-dequantising GEMM.
+int dispatch_awq(const AwqPlan &plan, const uint16_t *x, const int32_t *qweight, const int32_t *qzeros,
+                 const uint16_t *scales, const uint16_t *bias, uint16_t *y, int64_t m, int64_t k, int64_t n,
+                 int64_t g, uint8_t *ws, int dev, cudaStream_t s) {
+  const bool single = g % 64 == 0;
+#define LVB_GV(BN)                                                                                       \
+  return single ? launch_awq_gemv<BN, true>(plan, x, qweight, qzeros, scales, bias, y, m, k, n, g, ws, dev, s) \
+                : launch_awq_gemv<BN, false>(plan, x, qweight, qzeros, scales, bias, y, m, k, n, g, ws, dev, s)
+  switch (plan.bn) {
+    case 16: LVB_GV(16);
+    case 32: LVB_GV(32);
+    case 64: LVB_GV(64);
+    case 128: return launch_awq<128>(plan, x, qweight, qzeros, scales, bias, y, m, k, n, g, ws, dev, s);
+    default: return launch_awq<256>(plan, x, qweight, qzeros, scales, bias, y, m, k, n, g, ws, dev, s);
+  }
+#undef LVB_GV
 }
 
 // ------------------------------------------------------------------------
@@ -178,18 +217,21 @@ int launch_awq(const AwqPlan &plan, const uint16_t *x, const int32_t *qweight,
 // ------------------------------------------------------------------------
 struct DecodePlan {
   int max_splits, chunk_tokens;
-  size_t o_bytes, lse_bytes;
+  size_t o_bytes, lse_bytes, count_bytes;
+  size_t total() const { return o_bytes + lse_bytes + count_bytes; }
 };
 
 DecodePlan decode_plan(int64_t num_seqs, int64_t hq, int64_t hkv, int64_t d, int64_t max_seq_len,
                        int sms) {
   DecodePlan p{};
   const int64_t max_pages = (max_seq_len + lvb::attn::kPageTokens - 1) / lvb::attn::kPageTokens;
-  const int64_t pairs = num_seqs * hkv > 0 ? num_seqs * hkv : 1;
-  const int64_t target = 8LL * sms;  // ~4 waves at 2 CTAs per SM
+  const int64_t hpc = hkv % 4 == 0 ? 4 : hkv % 2 == 0 ? 2 : 1;
+  const int64_t pairs = num_seqs * (hkv / hpc) > 0 ? num_seqs * (hkv / hpc) : 1;
+  const int64_t target = 12LL * sms;  // ~5 waves at 2 CTAs per SM
   int64_t splits = (target + pairs - 1) / pairs;
   if (splits < 1) splits = 1;
   if (splits > max_pages) splits = max_pages > 0 ? max_pages : 1;
+  if (splits > 256) splits = 256;  // merge weights: (heads per CTA) x splits floats in shared memory
   const int64_t chunk_pages = (max_pages + splits - 1) / splits > 0 ? (max_pages + splits - 1) / splits : 1;
   splits = (max_pages + chunk_pages - 1) / chunk_pages;
   if (splits < 1) splits = 1;
@@ -197,6 +239,7 @@ DecodePlan decode_plan(int64_t num_seqs, int64_t hq, int64_t hkv, int64_t d, int
   p.chunk_tokens = static_cast<int>(chunk_pages * lvb::attn::kPageTokens);
   p.o_bytes = (static_cast<size_t>(num_seqs * hq * splits * d) * 4 + 255) & ~static_cast<size_t>(255);
   p.lse_bytes = (static_cast<size_t>(num_seqs * hq * splits) * 4 + 255) & ~static_cast<size_t>(255);
+  p.count_bytes = (static_cast<size_t>(num_seqs * hkv) * 4 + 255) & ~static_cast<size_t>(255);
   return p;
 }
 
@@ -206,34 +249,32 @@ bool decode_eligible(const uint8_t *vis, int64_t max_query_len, int64_t num_seqs
          (d == 64 || d == 128) && hq % hkv == 0 && hq / hkv <= 16;
 }
 
-template <bool kBf16, int D>
+template <bool kBf16, int D, int HPC>
 int launch_decode(const lvb::attn::AttnArgs &a, int64_t num_seqs, int64_t num_blocks, int dev,
                   cudaStream_t stream) {
-  using Cfg = lvb::attn::DecodeCfg<D>;
+  (void)num_blocks;
+  using Cfg = lvb::attn::DecodeCfg<D, HPC>;
   static bool smem_done[kMaxDevices] = {false};
-  auto kernel = lvb::attn::paged_decode_kernel<kBf16, D>;
+  auto kernel = lvb::attn::paged_decode_kernel<kBf16, D, HPC>;
   int rc = ensure_smem(kernel, Cfg::kSmemBytes, dev, smem_done);
   if (rc != LVB_OK) return rc;
-  const CUtensorMapDataType type = kBf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(a.Hkv),
-                              static_cast<cuuint64_t>(num_blocks) * lvb::attn::kPageTokens};
-  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(D) * 2,
-                                 static_cast<cuuint64_t>(a.Hkv) * D * 2};
-  const cuuint32_t box[3] = {64, 1, lvb::attn::kPageTokens};
-  CUtensorMap kmap, vmap;
-  rc = encode_map(&kmap, type, 3, a.kc, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
-  if (rc != LVB_OK) return rc;
-  rc = encode_map(&vmap, type, 3, a.vc, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
-  if (rc != LVB_OK) return rc;
-  dim3 grid(a.max_splits, a.Hkv, static_cast<unsigned>(num_seqs));
-  kernel<<<grid, lvb::attn::kDecodeThreads, Cfg::kSmemBytes, stream>>>(kmap, vmap, a);
+  dim3 grid(a.max_splits, a.Hkv / HPC, static_cast<unsigned>(num_seqs));
+  kernel<<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(a);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "paged_decode_kernel launch");
-  dim3 mgrid(static_cast<unsigned>(num_seqs), a.Hq);
-  lvb::attn::paged_merge_kernel<kBf16><<<mgrid, D, 0, stream>>>(a);
-  e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "paged_merge_kernel launch");
   return LVB_OK;
+}
+
+int decode_heads_per_cta(int64_t hkv) { return hkv % 4 == 0 ? 4 : hkv % 2 == 0 ? 2 : 1; }
+
+template <bool kBf16, int D>
+int launch_decode_any(const lvb::attn::AttnArgs &a, int64_t num_seqs, int64_t num_blocks, int dev,
+                      cudaStream_t stream) {
+  switch (decode_heads_per_cta(a.Hkv)) {
+    case 4: return launch_decode<kBf16, D, 4>(a, num_seqs, num_blocks, dev, stream);
+    case 2: return launch_decode<kBf16, D, 2>(a, num_seqs, num_blocks, dev, stream);
+    default: return launch_decode<kBf16, D, 1>(a, num_seqs, num_blocks, dev, stream);
+  }
 }
 
 template <bool kBf16>
@@ -321,13 +362,14 @@ int lvb_awq_linear(const uint16_t *x, const int32_t *qweight, const int32_t *qze
                                               (long long)m, (long long)k, (long long)n);
   if (m == 0) return LVB_OK;
   if (m > INT_MAX || k > INT_MAX || n > INT_MAX) return fail(LVB_ERR_UNSUPPORTED, "AWQ dimension exceeds int32");
-  if (group_size <= 0 || group_size % 8 != 0 || k % group_size != 0)
-    return fail(LVB_ERR_INVALID, "AWQ group_size %lld must be a positive multiple of 8 dividing k=%lld",
+  if (group_size <= 0 || group_size % 32 != 0 || k % group_size != 0)
+    return fail(LVB_ERR_INVALID, "AWQ group_size %lld must be a positive multiple of 32 dividing k=%lld",
                 (long long)group_size, (long long)k);
   if (n % 32 != 0) return fail(LVB_ERR_INVALID, "AWQ output width %lld must be divisible by 32", (long long)n);
   if (k % 8 != 0) return fail(LVB_ERR_INVALID, "AWQ input width %lld must be divisible by 8", (long long)k);
   if (!x || !qweight || !qzeros || !scales || !y) return fail(LVB_ERR_INVALID, "AWQ null pointer argument");
-  if (!aligned16(x) || !aligned16(qweight) || !aligned16(scales) || (workspace && !aligned16(workspace)))
+  if (!aligned16(x) || !aligned16(qweight) || !aligned16(qzeros) || !aligned16(scales) ||
+      (workspace && !aligned16(workspace)))
     return fail(LVB_ERR_INVALID, "AWQ x, qweight, scales and workspace must be 16-byte aligned");
   int dev = 0;
   int rc = current_device(&dev);
@@ -338,13 +380,7 @@ int lvb_awq_linear(const uint16_t *x, const int32_t *qweight, const int32_t *qze
                 plan.sem_bytes + plan.part_bytes);
   uint8_t *ws = static_cast<uint8_t *>(workspace);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  switch (plan.bn) {
-    case 16: return launch_awq<16>(plan, x, qweight, qzeros, scales, bias, y, m, k, n, group_size, ws, dev, s);
-    case 32: return launch_awq<32>(plan, x, qweight, qzeros, scales, bias, y, m, k, n, group_size, ws, dev, s);
-    case 64: return launch_awq<64>(plan, x, qweight, qzeros, scales, bias, y, m, k, n, group_size, ws, dev, s);
-    case 128: return launch_awq<128>(plan, x, qweight, qzeros, scales, bias, y, m, k, n, group_size, ws, dev, s);
-    default: return launch_awq<256>(plan, x, qweight, qzeros, scales, bias, y, m, k, n, group_size, ws, dev, s);
-  }
+  return dispatch_awq(plan, x, qweight, qzeros, scales, bias, y, m, k, n, group_size, ws, dev, s);
 }
 
 int lvb_awq_dequantize(const int32_t *qweight, const int32_t *qzeros, const uint16_t *scales,
@@ -448,7 +484,7 @@ size_t lvb_paged_attention_workspace_bytes(int64_t num_seqs, int64_t num_q_heads
   int dev = 0;
   if (current_device(&dev) != LVB_OK) return 0;
   const DecodePlan p = decode_plan(num_seqs, num_q_heads, num_kv_heads, head_size, max_seq_len, sm_count(dev));
-  return p.o_bytes + p.lse_bytes;
+  return p.total();
 }
 
 int lvb_paged_attention(const uint16_t *query, int64_t query_token_stride,
@@ -506,19 +542,20 @@ int lvb_paged_attention(const uint16_t *query, int64_t query_token_stride,
   if (decode_eligible(visibility, max_query_len, num_seqs, num_tokens, num_q_heads, num_kv_heads, head_size,
                       block_size)) {
     const DecodePlan plan = decode_plan(num_seqs, num_q_heads, num_kv_heads, head_size, max_seq_len, sm_count(dev));
-    if (workspace == nullptr || workspace_bytes < plan.o_bytes + plan.lse_bytes || !aligned16(workspace))
+    if (workspace == nullptr || workspace_bytes < plan.total() || !aligned16(workspace))
       return fail(LVB_ERR_WORKSPACE, "paged attention workspace of %zu bytes is below the %zu required",
-                  workspace_bytes, plan.o_bytes + plan.lse_bytes);
+                  workspace_bytes, plan.total());
     a.part_o = static_cast<float *>(workspace);
     a.part_lse = reinterpret_cast<float *>(static_cast<uint8_t *>(workspace) + plan.o_bytes);
+    a.merge_count = reinterpret_cast<uint32_t *>(static_cast<uint8_t *>(workspace) + plan.o_bytes + plan.lse_bytes);
     a.max_splits = plan.max_splits;
     a.chunk_tokens = plan.chunk_tokens;
     if (bf16) {
-      return head_size == 128 ? launch_decode<true, 128>(a, num_seqs, num_blocks, dev, s)
-                              : launch_decode<true, 64>(a, num_seqs, num_blocks, dev, s);
+      return head_size == 128 ? launch_decode_any<true, 128>(a, num_seqs, num_blocks, dev, s)
+                              : launch_decode_any<true, 64>(a, num_seqs, num_blocks, dev, s);
     }
-    return head_size == 128 ? launch_decode<false, 128>(a, num_seqs, num_blocks, dev, s)
-                            : launch_decode<false, 64>(a, num_seqs, num_blocks, dev, s);
+    return head_size == 128 ? launch_decode_any<false, 128>(a, num_seqs, num_blocks, dev, s)
+                            : launch_decode_any<false, 64>(a, num_seqs, num_blocks, dev, s);
   }
   return bf16 ? launch_general<true>(a, num_tokens, s) : launch_general<false>(a, num_tokens, s);
 }
@@ -530,14 +567,14 @@ int lvb_awq_linear_static(const uint16_t *x, const int32_t *qweight, const int32
                                               (long long)m, (long long)k, (long long)n);
   if (m == 0) return LVB_OK;
   if (m > INT_MAX || k > INT_MAX || n > INT_MAX) return fail(LVB_ERR_UNSUPPORTED, "AWQ dimension exceeds int32");
-  if (group_size <= 0 || group_size % 8 != 0 || k % group_size != 0)
-    return fail(LVB_ERR_INVALID, "AWQ group_size %lld must be a positive multiple of 8 dividing k=%lld",
+  if (group_size <= 0 || group_size % 32 != 0 || k % group_size != 0)
+    return fail(LVB_ERR_INVALID, "AWQ group_size %lld must be a positive multiple of 32 dividing k=%lld",
                 (long long)group_size, (long long)k);
   if (n % 32 != 0) return fail(LVB_ERR_INVALID, "AWQ output width %lld must be divisible by 32", (long long)n);
   if (k % 8 != 0) return fail(LVB_ERR_INVALID, "AWQ input width %lld must be divisible by 8", (long long)k);
   if (!x || !qweight || !qzeros || !scales || !y) return fail(LVB_ERR_INVALID, "AWQ null pointer argument");
-  if (!aligned16(x) || !aligned16(qweight) || !aligned16(scales))
-    return fail(LVB_ERR_INVALID, "AWQ x, qweight and scales must be 16-byte aligned");
+  if (!aligned16(x) || !aligned16(qweight) || !aligned16(qzeros) || !aligned16(scales))
+    return fail(LVB_ERR_INVALID, "AWQ x, qweight, qzeros and scales must be 16-byte aligned");
   int dev = 0;
   int rc = current_device(&dev);
   if (rc != LVB_OK) return rc;
@@ -559,13 +596,58 @@ int lvb_awq_linear_static(const uint16_t *x, const int32_t *qweight, const int32
     if (e != cudaSuccess) return cuda_fail(e, "clearing the static split-K semaphores");
   }
   uint8_t *ws = static_cast<uint8_t *>(scratch);
-  switch (plan.bn) {
-    case 16: return launch_awq<16>(plan, x, qweight, qzeros, scales, bias, y, m, k, n, group_size, ws, dev, s);
-    case 32: return launch_awq<32>(plan, x, qweight, qzeros, scales, bias, y, m, k, n, group_size, ws, dev, s);
-    case 64: return launch_awq<64>(plan, x, qweight, qzeros, scales, bias, y, m, k, n, group_size, ws, dev, s);
-    case 128: return launch_awq<128>(plan, x, qweight, qzeros, scales, bias, y, m, k, n, group_size, ws, dev, s);
-    default: return launch_awq<256>(plan, x, qweight, qzeros, scales, bias, y, m, k, n, group_size, ws, dev, s);
+  return dispatch_awq(plan, x, qweight, qzeros, scales, bias, y, m, k, n, group_size, ws, dev, s);
+}
+
+int lvb_pack_step_metadata(const int32_t *block_ids, const int64_t *table_offsets,
+                           const int32_t *num_computed, const int32_t *query_lengths,
+                           const int32_t *reserved, const int32_t *readonly, int64_t num_seqs,
+                           int64_t num_blocks, int64_t block_size, int32_t *out,
+                           int64_t out_capacity, int64_t *table_stride_out,
+                           int64_t *num_tokens_out) {
+  if (num_seqs <= 0 || num_blocks <= 0 || block_size <= 0 || num_blocks > INT_MAX)
+    return fail(LVB_ERR_INVALID, "invalid step metadata sizes");
+  if (!block_ids || !table_offsets || !num_computed || !query_lengths || !reserved || !readonly || !out ||
+      !table_stride_out || !num_tokens_out)
+    return fail(LVB_ERR_INVALID, "step metadata null pointer argument");
+  int64_t max_blocks = 0, num_tokens = 0;
+  for (int64_t r = 0; r < num_seqs; ++r) {
+    const int64_t len = table_offsets[r + 1] - table_offsets[r];
+    if (len < 0 || query_lengths[r] < 0 || reserved[r] < query_lengths[r] || num_computed[r] < 0 || readonly[r] < 0)
+      return fail(LVB_ERR_INVALID, "step metadata row %lld is malformed", (long long)r);
+    if (len > max_blocks) max_blocks = len;
+    num_tokens += query_lengths[r];
   }
+  static thread_local lvb::meta::OwnerTable owners;
+  const char *violation = lvb::meta::validate(block_ids, table_offsets, num_computed, reserved, readonly,
+                                              num_seqs, num_blocks, block_size, owners);
+  if (violation != nullptr) return fail(LVB_ERR_METADATA, "%s", violation);
+  const int64_t need = num_seqs * max_blocks + 2 * num_seqs + 1 + num_tokens;
+  if (need > out_capacity || num_tokens > INT_MAX)
+    return fail(LVB_ERR_WORKSPACE, "step metadata needs %lld int32 slots, buffer has %lld", (long long)need,
+                (long long)out_capacity);
+  int32_t *tables = out;
+  for (int64_t r = 0; r < num_seqs; ++r) {
+    const int64_t begin = table_offsets[r];
+    const int64_t len = table_offsets[r + 1] - begin;
+    int32_t *row = tables + r * max_blocks;
+    for (int64_t i = 0; i < len; ++i) row[i] = block_ids[begin + i];
+    const int32_t pad = len > 0 ? block_ids[begin] : 0;
+    for (int64_t i = len; i < max_blocks; ++i) row[i] = pad;
+  }
+  int32_t *computed = tables + num_seqs * max_blocks;
+  int32_t *qsl = computed + num_seqs;
+  int32_t *req = qsl + num_seqs + 1;
+  int64_t t = 0;
+  qsl[0] = 0;
+  for (int64_t r = 0; r < num_seqs; ++r) {
+    computed[r] = num_computed[r];
+    qsl[r + 1] = static_cast<int32_t>(qsl[r] + query_lengths[r]);
+    for (int32_t i = 0; i < query_lengths[r]; ++i) req[t++] = static_cast<int32_t>(r);
+  }
+  *table_stride_out = max_blocks;
+  *num_tokens_out = num_tokens;
+  return LVB_OK;
 }
 
 }  // extern "C"

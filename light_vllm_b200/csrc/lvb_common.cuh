@@ -57,14 +57,19 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t by
                : "memory");
 }
 
+// One potentially blocking probe: the hardware suspends the thread until the
+// phase completes or about kSuspendHintNs pass, so a waiting warp does not spin
+// on the issue slots its neighbours need.
+constexpr uint32_t kSuspendHintNs = 20000;
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
   uint32_t done;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(done)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "n"(kSuspendHintNs)
       : "memory");
   return done != 0;
 }
@@ -78,7 +83,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity,
   const long long start = clock64();
   uint32_t spins = 0;
   while (!mbar_try_wait(bar, parity)) {
-    if ((++spins & 63u) == 0) {
+    if ((++spins & 3u) == 0) {
       if (abort_flag != nullptr && *abort_flag) return false;
       if (clock64() - start > budget) {
         if (abort_flag != nullptr) *abort_flag = 1;
@@ -118,6 +123,25 @@ __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, u
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
+
+// ------------------------------------------------------------------------
+// cp.async (per-thread asynchronous global -> shared copies)
+// ------------------------------------------------------------------------
+// 16-byte copy; `src_bytes` < 16 zero-fills the rest (0 = write zeros only).
+__device__ __forceinline__ void cp_async_16(uint32_t dst, const void *src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes)
+               : "memory");
+}
+
+// Arrive on `bar` once every cp.async this thread issued so far has landed
+// (the barrier's expected count includes this thread; no increment here).
+__device__ __forceinline__ void cp_async_arrive_noinc(uint64_t *bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 // ------------------------------------------------------------------------
 // tcgen05 (5th-generation tensor cores, accumulators in tensor memory)

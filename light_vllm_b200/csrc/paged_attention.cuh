@@ -13,16 +13,18 @@
 //     32 positions at a time, an fp32 online softmax runs per warp and the four
 //     warps merge at the end.
 //   * paged_decode_kernel -- decode batches (one linear query per request):
-//     one CTA per (request, KV head, context split).  A producer warp streams
-//     the split's pages with TMA (K and V boxes of 16 tokens x 64 dims,
-//     128-byte swizzle) through an 8-stage shared-memory ring; four consumer
-//     warps each take every fourth page and run QK^T and PV for the whole GQA
-//     group as 16-row warp MMAs (the group of up to 16 query heads is the MMA's
-//     M dimension), with an fp32 online softmax in registers.  P is fed to the
-//     PV product as a hi + lo pair of 16-bit values so the probabilities keep
-//     fp32-like precision.  The warps merge through shared memory and each
-//     split writes its normalised output and log2-sum-exp; paged_merge_kernel
-//     combines the splits.
+//     one CTA per (request, group of up to 4 KV heads, context split).  Warp h
+//     owns KV head h of the group for every page of the split: its 32 lanes
+//     stream the head's 16-token K and V pages with 16-byte cp.async copies
+//     (two rows of 256 contiguous bytes per instruction) into the warp's own
+//     shared-memory ring, in the 128-byte-swizzled layout that ldmatrix reads
+//     without bank conflicts; completion is tracked per slot by an mbarrier
+//     that the copies themselves arrive on.  The warp runs QK^T and PV for its
+//     whole GQA group as 16-row warp MMAs (the up-to-16 query heads are the
+//     MMA's M dimension), with an fp32 online softmax in registers.  P enters the PV product as a hi + lo pair
+//     of 16-bit values so the probabilities keep fp32-like precision.  Each
+//     split writes its normalised output and log2-sum-exp; the last split of a
+//     request (per-request semaphore) merges them.
 #pragma once
 
 #include "lvb_common.cuh"
@@ -95,6 +97,7 @@ struct AttnArgs {
   // split-context decode
   float *part_o;    // [num_seqs][Hq][max_splits][D]
   float *part_lse;  // [num_seqs][Hq][max_splits]
+  uint32_t *merge_count;  // [num_seqs][Hkv], zero between calls
   int max_splits;
   int chunk_tokens;  // multiple of 16
 };
@@ -217,42 +220,44 @@ __global__ void __launch_bounds__(128) paged_attn_general_kernel(const AttnArgs 
 // ------------------------------------------------------------------------
 // Split-context decode kernel
 // ------------------------------------------------------------------------
-constexpr int kDecodeStages = 8;
-constexpr int kDecodeConsumerWarps = 4;
-constexpr int kDecodeThreads = (kDecodeConsumerWarps + 1) * 32;
 constexpr int kPageTokens = 16;
-constexpr int kBoxBytes = kPageTokens * 128;  // 16 tokens x 64 dims x 2 B
+constexpr int kBoxBytes = kPageTokens * 128;  // one TMA box: 16 tokens x 64 dims of one head
 
-template <int D>
+// HPC = KV heads per CTA (one warp each), D = head size.
+template <int D, int HPC>
 struct DecodeCfg {
-  static constexpr int kBoxes = D / 64;                    // boxes per K (and per V) page
-  static constexpr int kStageBytes = 2 * kBoxes * kBoxBytes;
-  static constexpr int kRingBytes = kDecodeStages * kStageBytes;
-  static constexpr int kMergeBytes = kDecodeConsumerWarps * 16 * D * 4;
-  static constexpr int kDataBytes = kRingBytes > kMergeBytes ? kRingBytes : kMergeBytes;
-  static constexpr int kBarOff = kDataBytes;
-  static constexpr int kStatOff = kBarOff + 2 * kDecodeStages * 8 + 16;
-  static constexpr int kSmemBytes = kStatOff + 2 * kDecodeConsumerWarps * 16 * 4 + 1024;
+  static constexpr int kBoxes = D / 64;                  // 64-dim halves of a head's row
+  static constexpr int kHeadBytes = kBoxes * kBoxBytes;  // one head's 16-token K (or V) page
+  static constexpr int kPageBytes = 2 * kHeadBytes;      // K then V
+  static constexpr int kFit = (96 * 1024) / (HPC * kPageBytes);
+  static constexpr int kStages = kFit < 2 ? 2 : (kFit > 8 ? 8 : kFit);  // per-warp ring depth
+  static constexpr int kWarpRing = kStages * kPageBytes;
+  static constexpr int kThreads = HPC * 32;
+  static constexpr int kBarOff = HPC * kWarpRing;
+  static constexpr int kSmemBytes = kBarOff + HPC * kStages * 8 + 16 + 1024;
 };
 
-template <bool kBf16, int D>
-__global__ void __launch_bounds__(kDecodeThreads, 2)
-    paged_decode_kernel(const __grid_constant__ CUtensorMap kmap,
-                        const __grid_constant__ CUtensorMap vmap, const AttnArgs a) {
-  using Cfg = DecodeCfg<D>;
-  constexpr int kSteps = D / 16;   // k-steps of QK^T, and dim pairs of PV
-  constexpr int kNTiles = D / 8;   // 8-dim output tiles
+template <bool kBf16, int D, int HPC>
+__global__ void __launch_bounds__(DecodeCfg<D, HPC>::kThreads, 2)
+    paged_decode_kernel(const AttnArgs a) {
+  using Cfg = DecodeCfg<D, HPC>;
+  constexpr int kStages = Cfg::kStages;
+  constexpr int kSteps = D / 16;  // k-steps of QK^T, and dim pairs of PV
+  constexpr int kNTiles = D / 8;  // 8-dim output tiles
+  constexpr int kConsumers = HPC * 32;
+  constexpr int kChunksPerLane = Cfg::kHeadBytes / 16 / 32;  // 16-byte copies per lane for K (and V)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  uint64_t *full = reinterpret_cast<uint64_t *>(smem + Cfg::kBarOff);
-  uint64_t *empty = full + kDecodeStages;
-  volatile int *abort_flag = reinterpret_cast<volatile int *>(empty + kDecodeStages);
-  float *m_sm = reinterpret_cast<float *>(smem + Cfg::kStatOff);
-  float *l_sm = m_sm + kDecodeConsumerWarps * 16;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  uint64_t *ready = reinterpret_cast<uint64_t *>(smem + Cfg::kBarOff) + warp * kStages;
+  volatile int *abort_flag =
+      reinterpret_cast<volatile int *>(reinterpret_cast<uint64_t *>(smem + Cfg::kBarOff) + HPC * kStages);
+  volatile int *last_flag = abort_flag + 1;
 
   const int seq = blockIdx.z;
-  const int kvh = blockIdx.y;
+  const int hg = blockIdx.y;  // group of HPC KV heads
   const int split = blockIdx.x;
   const int ctx = a.computed[seq] + 1;
   const int start = split * a.chunk_tokens;
@@ -261,53 +266,64 @@ __global__ void __launch_bounds__(kDecodeThreads, 2)
   const int p_begin = start / kPageTokens;
   const int npages = (end + kPageTokens - 1) / kPageTokens - p_begin;
   const int group = a.Hq / a.Hkv;
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
   const int32_t *table = a.tables + static_cast<int64_t>(seq) * a.table_stride;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kDecodeStages; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
-    }
+    for (int s = 0; s < HPC * kStages; ++s)
+      mbar_init(reinterpret_cast<uint64_t *>(smem + Cfg::kBarOff) + s, 32);
     *abort_flag = 0;
+    *last_flag = 0;
     fence_barrier_init();
   }
   __syncthreads();
 
-  if (warp == kDecodeConsumerWarps) {
-    // ---------------- producer ----------------
-    if (lane == 0) {
-      tma_prefetch_desc(&kmap);
-      tma_prefetch_desc(&vmap);
-      int issued = 0;
-      for (int i = 0; i < npages; ++i) {
-        const int s = i % kDecodeStages;
-        const uint32_t ph = (i / kDecodeStages) & 1;
-        if (!mbar_wait(&empty[s], ph ^ 1, abort_flag)) break;
-        const int row = table[p_begin + i] * kPageTokens;
-        uint8_t *stage = smem + s * Cfg::kStageBytes;
-        mbar_arrive_expect_tx(&full[s], Cfg::kStageBytes);
-#pragma unroll
-        for (int b = 0; b < Cfg::kBoxes; ++b) {
-          tma_load_3d(stage + b * kBoxBytes, &kmap, &full[s], b * 64, kvh, row);
-          tma_load_3d(stage + (Cfg::kBoxes + b) * kBoxBytes, &vmap, &full[s], b * 64, kvh, row);
-        }
-        issued = i + 1;
-      }
-      if (*abort_flag) {
-        for (int i = issued - kDecodeStages < 0 ? 0 : issued - kDecodeStages; i < issued; ++i)
-          mbar_wait(&full[i % kDecodeStages], (i / kDecodeStages) & 1, nullptr, kDrainBudgetCycles);
-      }
-    }
-    asm volatile("bar.sync 1, %0;" ::"n"(kDecodeThreads) : "memory");
-    return;
-  }
+  // ---------------- each warp: KV head hg * HPC + warp, every page ----------------
+  const int kvh = hg * HPC + warp;
+  const uint32_t ring = smem_u32(smem) + warp * Cfg::kWarpRing;
+  const int64_t head_off = static_cast<int64_t>(kvh) * D;
+  const int64_t row_elems = static_cast<int64_t>(a.Hkv) * D;  // elements per cache token row
+  // Block ids: one per lane, 32 pages at a time, passed around by shuffle.
+  int blk_cur = lane < npages ? table[p_begin + lane] : 0;
+  int blk_next = 32 + lane < npages ? table[p_begin + 32 + lane] : 0;
+  int blk_base = 0;  // page index of blk_cur's lane 0
 
-  // ---------------- consumers ----------------
-  const int g = lane >> 2;   // MMA row (query head within the group), and +8
-  const int cq = lane & 3;   // MMA column pair
-  const int t = a.qsl[seq];  // packed token of this request's query
+  // Issue the K and V copies of one page (block id `block`) into `slot`: lane
+  // l copies 16-byte chunks l, l + 32, ... of the head's 16 token rows.
+  auto load_page = [&](int block, int slot) {
+    const uint32_t kdst = ring + slot * Cfg::kPageBytes;
+    const uint32_t vdst = kdst + Cfg::kHeadBytes;
+    const int64_t base = static_cast<int64_t>(block) * kPageTokens * row_elems + head_off;
+#pragma unroll
+    for (int u = 0; u < kChunksPerLane; ++u) {
+      const int q = lane + 32 * u;                  // chunk of this head's page
+      const int tok = q / (D / 8);                   // D / 8 chunks per token row
+      const int c16 = q - tok * (D / 8);
+      const int half = c16 >> 3;
+      const int c = c16 & 7;
+      const uint32_t off = half * kBoxBytes + tok * 128 + ((c ^ (tok & 7)) << 4);
+      const int64_t src = base + tok * row_elems + c16 * 8;
+      cp_async_16(kdst + off, a.kc + src, 16u);
+      cp_async_16(vdst + off, a.vc + src, 16u);
+    }
+    cp_async_arrive_noinc(&ready[slot]);
+  };
+  auto block_of = [&](int pg) {
+    // Pages are requested in increasing order; refill the per-lane batch when
+    // the request moves past it (the batch after it was prefetched).
+    while (pg >= blk_base + 32) {
+      blk_cur = blk_next;
+      blk_base += 32;
+      blk_next = blk_base + 32 + lane < npages ? table[p_begin + blk_base + 32 + lane] : 0;
+    }
+    return __shfl_sync(0xffffffffu, blk_cur, pg - blk_base);
+  };
+
+#pragma unroll 1
+  for (int pg = 0; pg < kStages - 1 && pg < npages; ++pg) load_page(block_of(pg), pg % kStages);
+
+  const int g = lane >> 2;  // MMA row (query head within the group), and +8
+  const int cq = lane & 3;  // MMA column pair
+  const int t = a.qsl[seq];
   const uint16_t *qrow = a.q + t * a.q_stride + static_cast<int64_t>(kvh) * group * D;
   uint32_t qa[kSteps][4];
 #pragma unroll
@@ -323,18 +339,19 @@ __global__ void __launch_bounds__(kDecodeThreads, 2)
   for (int i = 0; i < kNTiles; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
   float m_run[2] = {-INFINITY, -INFINITY};
   float l_run[2] = {0.f, 0.f};
-  const uint32_t ring = smem_u32(smem);
-  // ldmatrix row assignment: matrix mi = lane / 8, row rr = lane % 8.
-  const int mi = lane >> 3;
+  const int mi = lane >> 3;  // ldmatrix: matrix index and row within it
   const int rr = lane & 7;
   bool ok = true;
 
-  for (int i = warp; i < npages; i += kDecodeConsumerWarps) {
-    const int s = i % kDecodeStages;
-    const uint32_t ph = (i / kDecodeStages) & 1;
-    if (!__all_sync(0xffffffffu, mbar_wait(&full[s], ph, abort_flag))) { ok = false; break; }
-    const uint32_t kbase = ring + s * Cfg::kStageBytes;
-    const uint32_t vbase = kbase + Cfg::kBoxes * kBoxBytes;
+  for (int i = 0; i < npages; ++i) {
+    // Keep kStages - 1 pages in flight: the slot refilled here held page
+    // i - 1, which this warp finished in the previous iteration.
+    if (i + kStages - 1 < npages) load_page(block_of(i + kStages - 1), (i + kStages - 1) % kStages);
+    const int s = i % kStages;
+    const uint32_t ph = (i / kStages) & 1;
+    if (!__all_sync(0xffffffffu, mbar_wait(&ready[s], ph, abort_flag))) { ok = false; break; }
+    const uint32_t kbase = ring + s * Cfg::kPageBytes;
+    const uint32_t vbase = kbase + Cfg::kHeadBytes;
 
     // S = Q K^T for the 16 tokens of the page (two 8-token MMA tiles).
     float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
@@ -414,8 +431,8 @@ __global__ void __launch_bounds__(kDecodeThreads, 2)
       mma_16816<kBf16>(o[2 * dp + 1], pa_lo, b2, b3);
     }
     __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[s]);
   }
+  cp_async_wait_all();
 
   // Row sums are spread over the 4 lanes of a row group.
 #pragma unroll
@@ -423,73 +440,89 @@ __global__ void __launch_bounds__(kDecodeThreads, 2)
     l_run[hr] += __shfl_xor_sync(0xffffffffu, l_run[hr], 1);
     l_run[hr] += __shfl_xor_sync(0xffffffffu, l_run[hr], 2);
   }
-  // All consumers and the producer meet before the ring is reused.
-  asm volatile("bar.sync 1, %0;" ::"n"(kDecodeThreads) : "memory");
-  ok = ok && !*abort_flag;
+  asm volatile("bar.sync 1, %0;" ::"n"(kConsumers) : "memory");
+  if (!ok || *abort_flag) return;
 
-  float *o_sm = reinterpret_cast<float *>(smem);  // [warp][16 rows][D]
-  if (cq == 0) {
-    m_sm[warp * 16 + g] = m_run[0];
-    m_sm[warp * 16 + g + 8] = m_run[1];
-    l_sm[warp * 16 + g] = l_run[0];
-    l_sm[warp * 16 + g + 8] = l_run[1];
-  }
+  // Each warp writes its own heads: the final output when the request has one
+  // split, else this split's normalised output and log2-sum-exp; the last split
+  // to finish (per-(request, head group) semaphore) combines the splits.
+  const int nsplit = (ctx + a.chunk_tokens - 1) / a.chunk_tokens;
 #pragma unroll
-  for (int n = 0; n < kNTiles; ++n) {
-    const int d = n * 8 + 2 * cq;
-    float *row0 = o_sm + (warp * 16 + g) * D;
-    float *row1 = o_sm + (warp * 16 + g + 8) * D;
-    row0[d] = o[n][0];
-    row0[d + 1] = o[n][1];
-    row1[d] = o[n][2];
-    row1[d + 1] = o[n][3];
+  for (int hr = 0; hr < 2; ++hr) {
+    const int row = g + 8 * hr;
+    if (row >= group) continue;
+    const int h = kvh * group + row;
+    const float inv = 1.f / l_run[hr];
+    if (nsplit == 1) {
+      uint16_t *dst = a.out + t * a.o_stride + static_cast<int64_t>(h) * D;
+#pragma unroll
+      for (int n = 0; n < kNTiles; ++n)
+        *reinterpret_cast<uint32_t *>(dst + n * 8 + 2 * cq) =
+            pack2<kBf16>(o[n][2 * hr] * inv, o[n][2 * hr + 1] * inv);
+    } else {
+      const int64_t base = (static_cast<int64_t>(seq) * a.Hq + h) * a.max_splits + split;
+      float *dst = a.part_o + base * D;
+#pragma unroll
+      for (int n = 0; n < kNTiles; ++n)
+        __stcg(reinterpret_cast<float2 *>(dst + n * 8 + 2 * cq),
+               make_float2(o[n][2 * hr] * inv, o[n][2 * hr + 1] * inv));
+      if (cq == 0) __stcg(a.part_lse + base, m_run[hr] + log2f(l_run[hr]));
+    }
   }
-  asm volatile("bar.sync 2, %0;" ::"n"(kDecodeConsumerWarps * 32) : "memory");
-  if (!ok) return;
-
-  // Merge the four warps; write this split's normalised output and lse.
+  if (nsplit == 1) return;
+  __threadfence();
+  asm volatile("bar.sync 2, %0;" ::"n"(kConsumers) : "memory");
   const int tid = threadIdx.x;
-  for (int idx = tid; idx < group * D; idx += kDecodeConsumerWarps * 32) {
+  uint32_t *counter = a.merge_count + seq * (a.Hkv / HPC) + hg;
+  if (tid == 0) {
+    const unsigned int prev = atomicAdd(counter, 1u);
+    *last_flag = prev == static_cast<unsigned int>(nsplit - 1) ? 1 : 0;
+  }
+  asm volatile("bar.sync 2, %0;" ::"n"(kConsumers) : "memory");
+  if (!*last_flag) return;
+  __threadfence();
+  // Split weights first (log2-sum-exp -> normalised weights, in shared memory
+  // reused from the ring), then the weighted sum with independent loads.
+  const int rows = HPC * group;
+  float *w_sm = reinterpret_cast<float *>(smem);  // [rows][nsplit]
+  const int64_t head0 = static_cast<int64_t>(seq) * a.Hq + hg * HPC * group;
+  for (int idx = tid; idx < rows * nsplit; idx += kConsumers) {
+    const int row = idx / nsplit;
+    const int sp = idx - row * nsplit;
+    w_sm[idx] = __ldcg(a.part_lse + (head0 + row) * a.max_splits + sp);
+  }
+  asm volatile("bar.sync 2, %0;" ::"n"(kConsumers) : "memory");
+  for (int row = tid; row < rows; row += kConsumers) {
+    float m_all = -INFINITY;
+    for (int sp = 0; sp < nsplit; ++sp) m_all = fmaxf(m_all, w_sm[row * nsplit + sp]);
+    float wsum = 0.f;
+    for (int sp = 0; sp < nsplit; ++sp) {
+      const float wt = exp2f(w_sm[row * nsplit + sp] - m_all);
+      w_sm[row * nsplit + sp] = wt;
+      wsum += wt;
+    }
+    const float inv = 1.f / wsum;
+    for (int sp = 0; sp < nsplit; ++sp) w_sm[row * nsplit + sp] *= inv;
+  }
+  asm volatile("bar.sync 2, %0;" ::"n"(kConsumers) : "memory");
+  for (int idx = tid; idx < rows * D; idx += kConsumers) {
     const int row = idx / D;
     const int d = idx - row * D;
-    float m_all = -INFINITY;
-#pragma unroll
-    for (int w = 0; w < kDecodeConsumerWarps; ++w) m_all = fmaxf(m_all, m_sm[w * 16 + row]);
-    float l_all = 0.f, acc = 0.f;
-#pragma unroll
-    for (int w = 0; w < kDecodeConsumerWarps; ++w) {
-      const float mw = m_sm[w * 16 + row];
-      const float wt = mw == -INFINITY ? 0.f : exp2f(mw - m_all);
-      l_all += wt * l_sm[w * 16 + row];
-      acc += wt * o_sm[(w * 16 + row) * D + d];
+    const float *src = a.part_o + (head0 + row) * a.max_splits * D + d;
+    const float *wrow = w_sm + row * nsplit;
+    float acc0 = 0.f, acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
+    int sp = 0;
+    for (; sp + 4 <= nsplit; sp += 4) {
+      acc0 = fmaf(wrow[sp], __ldcg(src + (sp + 0) * D), acc0);
+      acc1 = fmaf(wrow[sp + 1], __ldcg(src + (sp + 1) * D), acc1);
+      acc2 = fmaf(wrow[sp + 2], __ldcg(src + (sp + 2) * D), acc2);
+      acc3 = fmaf(wrow[sp + 3], __ldcg(src + (sp + 3) * D), acc3);
     }
-    const int h = kvh * group + row;
-    const int64_t base = (static_cast<int64_t>(seq) * a.Hq + h) * a.max_splits + split;
-    a.part_o[base * D + d] = acc / l_all;
-    if (d == 0) a.part_lse[base] = m_all + log2f(l_all);
+    for (; sp < nsplit; ++sp) acc0 = fmaf(wrow[sp], __ldcg(src + sp * D), acc0);
+    a.out[t * a.o_stride + (static_cast<int64_t>(hg) * HPC * group + row) * D + d] =
+        from_float<kBf16>((acc0 + acc1) + (acc2 + acc3));
   }
-}
-
-// Combine the context splits of each (request, query head).
-template <bool kBf16>
-__global__ void paged_merge_kernel(const AttnArgs a) {
-  const int seq = blockIdx.x;
-  const int h = blockIdx.y;
-  const int ctx = a.computed[seq] + 1;
-  const int nsplit = (ctx + a.chunk_tokens - 1) / a.chunk_tokens;
-  const int64_t base = (static_cast<int64_t>(seq) * a.Hq + h) * a.max_splits;
-  float m_all = -INFINITY;
-  for (int s = 0; s < nsplit; ++s) m_all = fmaxf(m_all, a.part_lse[base + s]);
-  float wsum = 0.f;
-  for (int s = 0; s < nsplit; ++s) wsum += exp2f(a.part_lse[base + s] - m_all);
-  const float inv = 1.f / wsum;
-  const int t = a.qsl[seq];
-  for (int d = threadIdx.x; d < a.D; d += blockDim.x) {
-    float acc = 0.f;
-    for (int s = 0; s < nsplit; ++s)
-      acc += exp2f(a.part_lse[base + s] - m_all) * a.part_o[(base + s) * a.D + d];
-    a.out[t * a.o_stride + static_cast<int64_t>(h) * a.D + d] = from_float<kBf16>(acc * inv);
-  }
+  if (tid == 0) *counter = 0u;
 }
 
 }  // namespace attn

@@ -22,6 +22,10 @@ Nothing here computes on the CPU.
 
 from __future__ import annotations
 
+import ctypes
+import itertools
+
+import numpy as np
 import torch
 from torch import Tensor
 
@@ -68,25 +72,45 @@ class B200PagedAttention:
             raise KVCacheError("B200 paged attention requires a CUDA KV cache")
         if config.dtype not in _SUPPORTED_DTYPES:
             raise KVCacheError("B200 paged attention supports fp16 and bf16 KV caches")
-        metadata.validate_block_tables(num_blocks=config.num_blocks, block_size=config.block_size)
         self._cache = cache
         self._metadata = metadata
         self._backend = backend
         self._layer_ids: set[str] = set()
         self._device = torch.device(config.device)
         lengths = metadata.query_lengths
-        max_blocks = max(len(table) for table in metadata.block_tables)
-        flat_tables = []
-        for table in metadata.block_tables:
-            flat_tables.extend(table)
-            flat_tables.extend((table[0] if table else 0,) * (max_blocks - len(table)))
-        (tables, self._computed, self._query_start, self._request_indices) = staging.copy_groups(
-            flat_tables,
-            metadata.num_computed_tokens,
-            metadata.query_start_loc,
-            metadata.request_indices,
-        )
-        self._tables = tables
+        # Validation (the reference's block-table rules, same order and
+        # messages) and packing of the per-step int32 payload run in native
+        # code; one pinned copy moves the payload to the device.
+        tables = metadata.block_tables
+        offsets = np.zeros(len(tables) + 1, dtype=np.int64)
+        np.cumsum([len(t) for t in tables], out=offsets[1:])
+        flat = np.fromiter(itertools.chain.from_iterable(tables), dtype=np.int32, count=int(offsets[-1]))
+        computed = np.asarray(metadata.num_computed_tokens, dtype=np.int32)
+        qlens = np.asarray(lengths, dtype=np.int32)
+        reserved = np.asarray(metadata.num_reserved_query_tokens, dtype=np.int32)
+        readonly = np.asarray(metadata.num_readonly_prefix_blocks, dtype=np.int32)
+        n = len(tables)
+        max_blocks = int(np.max(np.diff(offsets))) if n else 0
+        capacity = n * max_blocks + 2 * n + 1 + int(qlens.sum())
+        stride = ctypes.c_int64(0)
+        ntok = ctypes.c_int64(0)
+        lib = _native.library()
+
+        def fill(host: Tensor) -> int:
+            _native.check(
+                lib.lvb_pack_step_metadata(
+                    flat.ctypes.data, offsets.ctypes.data, computed.ctypes.data, qlens.ctypes.data,
+                    reserved.ctypes.data, readonly.ctypes.data, n, config.num_blocks, config.block_size,
+                    host.data_ptr(), host.numel(), ctypes.byref(stride), ctypes.byref(ntok)),
+                "lvb_pack_step_metadata")
+            return capacity
+
+        packed = staging.copy_packed(capacity, fill)
+        max_blocks = int(stride.value)
+        self._tables = packed[: n * max_blocks]
+        self._computed = packed[n * max_blocks : n * max_blocks + n]
+        self._query_start = packed[n * max_blocks + n : n * max_blocks + 2 * n + 1]
+        self._request_indices = packed[n * max_blocks + 2 * n + 1 :]
         self._table_stride = max_blocks
         self._num_seqs = metadata.batch_size
         self._num_tokens = metadata.num_query_tokens
@@ -196,6 +220,8 @@ class B200PagedAttentionBackend:
         need = int(_native.library().lvb_paged_attention_workspace_bytes(num_seqs, hq, hkv, d, max_seq_len))
         buf = self._workspaces.get(device)
         if buf is None or buf.numel() < need:
-            buf = torch.empty(max(need, 1 << 20), dtype=torch.uint8, device=device)
+            # Zero once: the split-merge semaphores start at zero and every call
+            # leaves them zero.
+            buf = torch.zeros(max(need, 1 << 20), dtype=torch.uint8, device=device)
             self._workspaces[device] = buf
         return buf.data_ptr(), buf.numel()

@@ -51,6 +51,22 @@ class SingleStepStaging:
             offset += length
         return tuple(views)
 
+    def copy_packed(self, capacity: int, fill) -> Tensor:
+        """Let ``fill(host_int32_view)`` write up to ``capacity`` values into the
+        pinned buffer and return how many it wrote; one H2D copy follows.  The
+        returned device view stays valid until the next copy."""
+
+        if self._copied is not None:
+            self._copied.synchronize()
+        self._reserve(capacity)
+        assert self._host is not None and self._dev is not None
+        total = int(fill(self._host))
+        self._dev[:total].copy_(self._host[:total], non_blocking=True)
+        if self._copied is None:
+            self._copied = torch.cuda.Event(blocking=True)
+        self._copied.record(torch.cuda.current_stream(self._device))
+        return self._dev[:total]
+
     def _reserve(self, required: int) -> None:
         if self._dev is not None and self._dev.numel() >= required:
             return
