@@ -185,8 +185,10 @@ LVB_API size_t lvb_paged_attention_workspace_bytes(int64_t num_seqs, int64_t num
  * starting at visibility_start[r].  The query heads of one KV head are
  * num_q_heads / num_kv_heads consecutive heads (GQA).  fp32 accumulation.
  * The K/V of this step must already be in the cache (lvb_paged_kv_write).
- * head_size must be a multiple of 8 and at most 256.  Decode batches (every
- * query length 1, linear) take a split-context path that needs `workspace`.
+ * head_size must be a multiple of 8 and at most 256; query and out rows are
+ * 4-byte aligned (even token strides, in elements), the caches 16-byte
+ * aligned.  Decode batches (every query length 1, linear) take a
+ * split-context path that needs `workspace`.
  * Replaces the Triton attention launches
  * (runtime/execution/triton_paged_attention.py:106-391, 519-559). */
 LVB_API int lvb_paged_attention(const uint16_t *query, int64_t query_token_stride,

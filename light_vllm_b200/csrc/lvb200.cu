@@ -227,7 +227,7 @@ DecodePlan decode_plan(int64_t num_seqs, int64_t hq, int64_t hkv, int64_t d, int
   const int64_t max_pages = (max_seq_len + lvb::attn::kPageTokens - 1) / lvb::attn::kPageTokens;
   const int64_t hpc = hkv % 4 == 0 ? 4 : hkv % 2 == 0 ? 2 : 1;
   const int64_t pairs = num_seqs * (hkv / hpc) > 0 ? num_seqs * (hkv / hpc) : 1;
-  const int64_t target = 12LL * sms;  // ~5 waves at 2 CTAs per SM
+  const int64_t target = 8LL * sms;  // ~4 waves of 2 CTAs per SM (measured best of 4/8/12/24)
   int64_t splits = (target + pairs - 1) / pairs;
   if (splits < 1) splits = 1;
   if (splits > max_pages) splits = max_pages > 0 ? max_pages : 1;
@@ -513,6 +513,8 @@ int lvb_paged_attention(const uint16_t *query, int64_t query_token_stride,
   if (!aligned16(key_cache) || !aligned16(value_cache)) return fail(LVB_ERR_INVALID, "caches must be 16-byte aligned");
   if (query_token_stride % 2 != 0 || (reinterpret_cast<uintptr_t>(query) & 3u) != 0)
     return fail(LVB_ERR_INVALID, "query rows must be 4-byte aligned");
+  if (out_token_stride % 2 != 0 || (reinterpret_cast<uintptr_t>(out) & 3u) != 0)
+    return fail(LVB_ERR_INVALID, "output rows must be 4-byte aligned");
   int dev = 0;
   int rc = current_device(&dev);
   if (rc != LVB_OK) return rc;

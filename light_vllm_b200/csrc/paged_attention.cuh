@@ -505,22 +505,58 @@ __global__ void __launch_bounds__(DecodeCfg<D, HPC>::kThreads, 2)
     for (int sp = 0; sp < nsplit; ++sp) w_sm[row * nsplit + sp] *= inv;
   }
   asm volatile("bar.sync 2, %0;" ::"n"(kConsumers) : "memory");
-  for (int idx = tid; idx < rows * D; idx += kConsumers) {
-    const int row = idx / D;
-    const int d = idx - row * D;
-    const float *src = a.part_o + (head0 + row) * a.max_splits * D + d;
-    const float *wrow = w_sm + row * nsplit;
-    float acc0 = 0.f, acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
-    int sp = 0;
-    for (; sp + 4 <= nsplit; sp += 4) {
-      acc0 = fmaf(wrow[sp], __ldcg(src + (sp + 0) * D), acc0);
-      acc1 = fmaf(wrow[sp + 1], __ldcg(src + (sp + 1) * D), acc1);
-      acc2 = fmaf(wrow[sp + 2], __ldcg(src + (sp + 2) * D), acc2);
-      acc3 = fmaf(wrow[sp + 3], __ldcg(src + (sp + 3) * D), acc3);
+  // Weighted sum over the splits.  The partials sit in L2 (written moments
+  // ago), so the cost is round trips, not bytes: each thread keeps
+  // kMergeOuts float4 outputs x kMergeSplits splits = 16 independent loads in
+  // flight per round trip.  Splits are summed in order for every output, so
+  // the result does not depend on the thread mapping.
+  constexpr int kMergeOuts = 4;
+  constexpr int kMergeSplits = 4;
+  constexpr int kQuads = D / 4;
+  const int total4 = rows * kQuads;
+  uint16_t *out_row = a.out + t * a.o_stride + static_cast<int64_t>(hg) * HPC * group * D;
+  for (int base = tid; base < total4; base += kConsumers * kMergeOuts) {
+    float4 acc[kMergeOuts];
+    const float4 *src[kMergeOuts];
+    const float *wrow[kMergeOuts];
+#pragma unroll
+    for (int j = 0; j < kMergeOuts; ++j) {
+      acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+      const int idx = base + j * kConsumers;
+      const int row = (idx < total4 ? idx : 0) / kQuads;
+      const int q4 = (idx < total4 ? idx : 0) - row * kQuads;
+      src[j] = reinterpret_cast<const float4 *>(a.part_o + (head0 + row) * a.max_splits * D) + q4;
+      wrow[j] = w_sm + row * nsplit;
     }
-    for (; sp < nsplit; ++sp) acc0 = fmaf(wrow[sp], __ldcg(src + sp * D), acc0);
-    a.out[t * a.o_stride + (static_cast<int64_t>(hg) * HPC * group + row) * D + d] =
-        from_float<kBf16>((acc0 + acc1) + (acc2 + acc3));
+    for (int sp0 = 0; sp0 < nsplit; sp0 += kMergeSplits) {
+      float4 v[kMergeOuts][kMergeSplits];
+#pragma unroll
+      for (int j = 0; j < kMergeOuts; ++j)
+#pragma unroll
+        for (int s = 0; s < kMergeSplits; ++s)
+          v[j][s] = (sp0 + s < nsplit && base + j * kConsumers < total4) ? __ldcg(src[j] + (sp0 + s) * kQuads)
+                                                                          : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int j = 0; j < kMergeOuts; ++j)
+#pragma unroll
+        for (int s = 0; s < kMergeSplits; ++s) {
+          const float wt = sp0 + s < nsplit ? wrow[j][sp0 + s] : 0.f;
+          acc[j].x = fmaf(wt, v[j][s].x, acc[j].x);
+          acc[j].y = fmaf(wt, v[j][s].y, acc[j].y);
+          acc[j].z = fmaf(wt, v[j][s].z, acc[j].z);
+          acc[j].w = fmaf(wt, v[j][s].w, acc[j].w);
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < kMergeOuts; ++j) {
+      const int idx = base + j * kConsumers;
+      if (idx >= total4) continue;
+      const int row = idx / kQuads;
+      const int q4 = idx - row * kQuads;
+      uint32_t *dst = reinterpret_cast<uint32_t *>(out_row + row * D + 4 * q4);
+      dst[0] = pack2<kBf16>(acc[j].x, acc[j].y);
+      dst[1] = pack2<kBf16>(acc[j].z, acc[j].w);
+    }
   }
   if (tid == 0) *counter = 0u;
 }
