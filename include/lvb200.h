@@ -66,8 +66,8 @@ LVB_API int lvb_device_error(uint32_t *error_out);
 /* AWQ W4A16 linear                                                          */
 /* ------------------------------------------------------------------------ */
 
-/* Bytes of workspace `lvb_awq_linear` needs for an m x k x n call on the
- * current device: split-K reduction semaphores followed by fp32 partial
+/* Bytes of workspace `lvb_awq_linear` (and `lvb_awq_linear_packed`) needs for
+ * an m x k x n call on the current device: split-K reduction semaphores followed by fp32 partial
  * tiles.  A workspace must be zero-filled once before its first use; every
  * call leaves its semaphores zero again, so one buffer serves all later calls
  * of the same or smaller size.  Replaces the fp16 split partial planes that
@@ -114,6 +114,37 @@ LVB_API int lvb_awq_linear_static(const uint16_t *x, const int32_t *qweight,
 LVB_API int lvb_awq_dequantize(const int32_t *qweight, const int32_t *qzeros, const uint16_t *scales,
                        uint16_t *w, int64_t k, int64_t n, int64_t group_size,
                        lvb_stream_t stream);
+
+/* Packed decode layout.  AWQScheme.prepare (modeling/quantization/awq.py:
+ * 468-486) hands a backend the checkpoint once, after loading, so that it can
+ * convert it (the protocol names Marlin-style backends, which repack); the
+ * B200 scheme repacks into a layout the decode kernel streams with one bulk
+ * copy per 256-k stage:
+ *   codes   [ceil(n/128) column tiles][ceil(k/64)*2 runs][128 columns][16 B]:
+ *           the 32 int4 codes of one column for k = 32r .. 32r+31; word w of
+ *           the 16 bytes holds k = 4w, 4w+1, 4w+2, 4w+3 in nibbles 0, 4, 2, 6
+ *           and k = 16+4w .. 16+4w+3 in nibbles 1, 5, 3, 7 (codes past k or
+ *           n are 0);
+ *   groups  [ceil(n/128)][k/group_size][128] uint32: fp16 scale bits in the
+ *           low half, the int4 zero point in bits 16..19 (0 past n).
+ * lvb_awq_pack_bytes reports both sizes; lvb_awq_pack writes them on `stream`
+ * from the arrays lvb_awq_linear takes (same requirements). */
+LVB_API int lvb_awq_pack_bytes(int64_t k, int64_t n, int64_t group_size, size_t *codes_bytes,
+                               size_t *groups_bytes);
+LVB_API int lvb_awq_pack(const int32_t *qweight, const int32_t *qzeros, const uint16_t *scales,
+                         int64_t k, int64_t n, int64_t group_size, void *codes, void *groups,
+                         lvb_stream_t stream);
+
+/* y[m, n] = x[m, :k] @ W + bias from the packed layout, for m <= 64 (larger m
+ * returns LVB_ERR_UNSUPPORTED: use lvb_awq_linear).  Same arithmetic and
+ * requirements as lvb_awq_linear; the workspace is sized by
+ * lvb_awq_workspace_bytes.  Replaces `awq_gemm` for decode batches
+ * (csrc/awq/bindings.cpp:10-13, gemm_kernels.cu:444-501, called from
+ * `CudaAWQOperation.__call__`, cuda_awq.py:96-122). */
+LVB_API int lvb_awq_linear_packed(const uint16_t *x, const void *codes, const void *groups,
+                                  const uint16_t *bias, uint16_t *y, int64_t m, int64_t k,
+                                  int64_t n, int64_t group_size, void *workspace,
+                                  size_t workspace_bytes, lvb_stream_t stream);
 
 /* ------------------------------------------------------------------------ */
 /* Paged K/V cache                                                           */

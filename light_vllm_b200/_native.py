@@ -15,7 +15,7 @@ import functools
 from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().parent / "_lib" / "liblvb200.so"
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 LVB_OK = 0
 LVB_ERR_INVALID = 1
@@ -47,6 +47,11 @@ PROTOTYPES: dict[str, tuple[object, tuple[object, ...]]] = {
         _int, (_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _i64, _i64, _i64, _i64, _c_ptr),
     ),
     "lvb_awq_dequantize": (_int, (_c_ptr, _c_ptr, _c_ptr, _c_ptr, _i64, _i64, _i64, _c_ptr)),
+    "lvb_awq_pack_bytes": (_int, (_i64, _i64, _i64, ctypes.POINTER(_size), ctypes.POINTER(_size))),
+    "lvb_awq_pack": (_int, (_c_ptr, _c_ptr, _c_ptr, _i64, _i64, _i64, _c_ptr, _c_ptr, _c_ptr)),
+    "lvb_awq_linear_packed": (
+        _int, (_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _i64, _i64, _i64, _i64, _c_ptr, _size, _c_ptr),
+    ),
     "lvb_paged_kv_write": (
         _int,
         (_c_ptr, _i64, _c_ptr, _i64, _c_ptr, _c_ptr, _c_ptr, _i64, _c_ptr, _c_ptr, _c_ptr, _i64, _i64,

@@ -5,11 +5,16 @@ a ``LinearOperation`` -- the contract of ``AWQScheme.prepare``
 (modeling/quantization/awq.py:468-486) and ``LinearOperation.__call__``
 (modeling/quantization/interfaces.py:23-26).  It replaces ``CudaAWQScheme`` /
 ``CudaAWQOperation`` (modeling/quantization/awq_schemes.py:56-73,
-cuda_awq.py:96-146) and consumes the same AutoAWQ GEMM tensors in place: no
-repacking, no second resident copy of the weight.  Every call runs one sm_100a
-kernel (``lvb_awq_linear``) for any number of rows: tcgen05 tensor cores with
-the weight dequantised on the fly, bias fused into the epilogue, and split-K
-for decode-sized batches, whose workspace is allocated once here.
+cuda_awq.py:96-146) and consumes the same AutoAWQ GEMM tensors.  ``prepare``
+also repacks the codes once into the decode layout (``lvb_awq_pack``; the
+``AWQScheme`` protocol leaves such one-time conversion to the backend, as its
+Marlin-style backends do), which costs a second copy of the int4 codes (half a
+byte per weight) plus one (scale, zero) word per group and column.  Every call
+runs one sm_100a kernel: up to 64 rows the decode kernel over the packed codes
+(``lvb_awq_linear_packed``: weights dequantised into tensor memory), above
+that the general GEMM over the checkpoint layout (``lvb_awq_linear``); both
+run tcgen05 tensor cores with the bias fused into the epilogue and split-K
+for small grids, whose workspace is allocated once here.
 
 Inject it without touching Engine, Scheduler or Worker, e.g.
 ``AWQLinearMethod(AWQConfig.from_mapping(cfg), B200AWQScheme())`` passed as a
@@ -18,6 +23,7 @@ prebuilt ``ModelSpec.linear_method`` (modeling/loaders/safetensors.py:101-102).
 
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass
 
 import torch
@@ -28,6 +34,8 @@ from light_vllm_b200 import _native
 _PACK_FACTOR = 8
 # Row counts that take the split-K path; the workspace covers the largest.
 _SPLIT_K_ROWS = (1, 16, 32, 64)
+# Rows served by the packed decode kernel (lvb_awq_linear_packed).
+_PACKED_MAX_ROWS = 64
 
 
 def _validate_static_weights(qweight: Tensor, qzeros: Tensor, scales: Tensor,
@@ -71,6 +79,8 @@ class B200AWQOperation:
     inner: int
     output_width: int
     workspace: Tensor
+    codes: Tensor
+    groups: Tensor
 
     def __call__(self, inputs: Tensor) -> Tensor:
         flat = inputs.reshape(-1, self.inner)
@@ -80,6 +90,17 @@ class B200AWQOperation:
             flat = flat.contiguous()
         rows = flat.shape[0]
         out = torch.empty((rows, self.output_width), dtype=torch.float16, device=flat.device)
+        if rows <= _PACKED_MAX_ROWS:
+            _native.check(
+                _native.library().lvb_awq_linear_packed(
+                    flat.data_ptr(), self.codes.data_ptr(), self.groups.data_ptr(),
+                    None if self.bias is None else self.bias.data_ptr(), out.data_ptr(), rows,
+                    self.inner, self.output_width, self.group_size, self.workspace.data_ptr(),
+                    self.workspace.numel(), torch.cuda.current_stream(flat.device).cuda_stream,
+                ),
+                "lvb_awq_linear_packed",
+            )
+            return out.reshape(*inputs.shape[:-1], self.output_width)
         _native.check(
             _native.library().lvb_awq_linear(
                 flat.data_ptr(), self.qweight.data_ptr(), self.qzeros.data_ptr(),
@@ -106,7 +127,30 @@ def prepare_b200_awq_operation(qweight: Tensor, qzeros: Tensor, scales: Tensor, 
         need = max(int(lib.lvb_awq_workspace_bytes(m, inner, output, group_size)) for m in _SPLIT_K_ROWS)
         # Split-K semaphores must start at zero; every call leaves them zero.
         workspace = torch.zeros(max(need, 256), dtype=torch.uint8, device=qweight.device)
-    return B200AWQOperation(qweight, qzeros, scales, group_size, bias, inner, output, workspace)
+        codes, groups = pack_awq_decode_layout(qweight, qzeros, scales, group_size)
+    return B200AWQOperation(qweight, qzeros, scales, group_size, bias, inner, output, workspace, codes,
+                            groups)
+
+
+def pack_awq_decode_layout(qweight: Tensor, qzeros: Tensor, scales: Tensor,
+                           group_size: int) -> tuple[Tensor, Tensor]:
+    """Packed codes and (scale, zero) words of the decode kernel (``lvb_awq_pack``)."""
+
+    inner, output = _validate_static_weights(qweight, qzeros, scales, group_size)
+    lib = _native.library()
+    codes_bytes = ctypes.c_size_t()
+    groups_bytes = ctypes.c_size_t()
+    _native.check(lib.lvb_awq_pack_bytes(inner, output, group_size, ctypes.byref(codes_bytes),
+                                         ctypes.byref(groups_bytes)), "lvb_awq_pack_bytes")
+    codes = torch.empty(codes_bytes.value, dtype=torch.uint8, device=qweight.device)
+    groups = torch.empty(groups_bytes.value // 4, dtype=torch.int32, device=qweight.device)
+    _native.check(
+        lib.lvb_awq_pack(qweight.data_ptr(), qzeros.data_ptr(), scales.data_ptr(), inner, output,
+                         group_size, codes.data_ptr(), groups.data_ptr(),
+                         torch.cuda.current_stream(qweight.device).cuda_stream),
+        "lvb_awq_pack",
+    )
+    return codes, groups
 
 
 class B200AWQScheme:

@@ -16,14 +16,14 @@
 
 #include "../../include/lvb200.h"
 #include "awq_gemm.cuh"
-#include "awq_gemv.cuh"
+#include "awq_decode.cuh"
 #include "lvb_common.cuh"
 #include "paged_attention.cuh"
 #include "step_metadata.cuh"
 
 namespace {
 
-constexpr int kAbiVersion = 1;
+constexpr int kAbiVersion = 2;
 constexpr int kMaxDevices = 64;
 
 thread_local char g_last_error[512] = "";
@@ -160,21 +160,92 @@ int launch_awq(const AwqPlan &plan, const uint16_t *x, const int32_t *qweight,
   return LVB_OK;
 }
 
-template <int BN, bool kSingleGroup>
-int launch_awq_gemv(const AwqPlan &plan, const uint16_t *x, const int32_t *qweight,
-                    const int32_t *qzeros, const uint16_t *scales, const uint16_t *bias, uint16_t *y,
-                    int64_t m, int64_t k, int64_t n, int64_t g, uint8_t *ws, int dev,
-                    cudaStream_t stream) {
-  using C = lvb::awq::GvConfig<BN>;
+// The standard-layout entry points run the fp16-dequantising GEMM for every
+// batch size; decode-sized batches are fastest through the packed layout
+// (lvb_awq_pack + lvb_awq_linear_packed).
+int dispatch_awq(const AwqPlan &plan, const uint16_t *x, const int32_t *qweight, const int32_t *qzeros,
+                 const uint16_t *scales, const uint16_t *bias, uint16_t *y, int64_t m, int64_t k, int64_t n,
+                 int64_t g, uint8_t *ws, int dev, cudaStream_t s) {
+  switch (plan.bn) {
+    case 16: return launch_awq<16>(plan, x, qweight, qzeros, scales, bias, y, m, k, n, g, ws, dev, s);
+    case 32: return launch_awq<32>(plan, x, qweight, qzeros, scales, bias, y, m, k, n, g, ws, dev, s);
+    case 64: return launch_awq<64>(plan, x, qweight, qzeros, scales, bias, y, m, k, n, g, ws, dev, s);
+    case 128: return launch_awq<128>(plan, x, qweight, qzeros, scales, bias, y, m, k, n, g, ws, dev, s);
+    default: return launch_awq<256>(plan, x, qweight, qzeros, scales, bias, y, m, k, n, g, ws, dev, s);
+  }
+}
+
+// ------------------------------------------------------------------------
+// Packed-layout decode path
+// ------------------------------------------------------------------------
+constexpr int64_t kPackedMaxM = 64;
+
+struct PackedShape {
+  int n_tiles, k_chunks, k_blocks, groups;
+  size_t codes_bytes, groups_bytes;
+};
+
+PackedShape packed_shape(int64_t k, int64_t n, int64_t g) {
+  PackedShape s{};
+  s.n_tiles = static_cast<int>((n + lvb::awqd::kTileN - 1) / lvb::awqd::kTileN);
+  s.k_blocks = static_cast<int>((k + lvb::awqd::kBlockK - 1) / lvb::awqd::kBlockK);
+  s.k_chunks = 2 * s.k_blocks;
+  s.groups = static_cast<int>(k / g);
+  s.codes_bytes = static_cast<size_t>(s.n_tiles) * s.k_chunks * lvb::awqd::kChunkBytes;
+  s.groups_bytes = static_cast<size_t>(s.n_tiles) * s.groups * lvb::awqd::kSzRowBytes;
+  return s;
+}
+
+struct PackedPlan {
+  int bn, splits;
+  size_t sem_bytes, part_bytes;
+};
+
+// K splits for a one-wave-per-SM grid: the split count that minimises
+// (waves of CTAs) x (64-k blocks per CTA), fewest splits on ties.
+PackedPlan packed_plan(int64_t m, const PackedShape &sh, int sms) {
+  PackedPlan p{};
+  p.bn = m <= 16 ? 16 : m <= 32 ? 32 : 64;
+  int best = 1;
+  long long best_cost = -1;
+  const int max_splits = sh.k_blocks < 16 ? sh.k_blocks : 16;
+  for (int sp = 1; sp <= max_splits; ++sp) {
+    const long long ctas = static_cast<long long>(sh.n_tiles) * sp;
+    const long long waves = (ctas + sms - 1) / sms;
+    const long long cost = waves * ((sh.k_blocks + sp - 1) / sp);
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
+      best = sp;
+    }
+  }
+  p.splits = best;
+  p.sem_bytes = p.splits > 1 ? (static_cast<size_t>(sh.n_tiles) * 4 + 255) & ~static_cast<size_t>(255) : 0;
+  p.part_bytes =
+      p.splits > 1 ? static_cast<size_t>(sh.n_tiles) * p.splits * p.bn * lvb::awqd::kTileN * sizeof(float) : 0;
+  return p;
+}
+
+template <int BN>
+int launch_awq_packed(const PackedPlan &plan, const PackedShape &sh, const uint16_t *x, const uint8_t *codes,
+                      const uint32_t *groups, const uint16_t *bias, uint16_t *y, int64_t m, int64_t k,
+                      int64_t n, int64_t g, uint8_t *ws, int dev, cudaStream_t stream) {
+  using C = lvb::awqd::DecodeConfig<BN>;
   static bool smem_done[kMaxDevices] = {false};
-  auto kernel = lvb::awq::awq_gemv_kernel<BN, kSingleGroup>;
+  auto kernel = lvb::awqd::awq_decode_kernel<BN>;
   int rc = ensure_smem(kernel, C::kSmemBytes, dev, smem_done);
   if (rc != LVB_OK) return rc;
-  lvb::awq::Params p{};
-  p.x = x;
-  p.qweight = qweight;
-  p.qzeros = qzeros;
-  p.scales = scales;
+  // Activations as [k / 32 chunks][m rows][32 k]: one box per stage fetches
+  // eight 64-byte-swizzled [BN x 32] tiles, rows past m and chunks past k
+  // read as zeros.
+  CUtensorMap xmap;
+  const cuuint64_t dims[3] = {32, static_cast<cuuint64_t>(m), static_cast<cuuint64_t>(k / 32)};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(k) * 2, 64};
+  const cuuint32_t box[3] = {32, static_cast<cuuint32_t>(BN), static_cast<cuuint32_t>(lvb::awqd::kStageChunks)};
+  rc = encode_map(&xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, x, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B);
+  if (rc != LVB_OK) return rc;
+  lvb::awqd::DecodeParams p{};
+  p.qpack = codes;
+  p.szpack = groups;
   p.bias = bias;
   p.y = y;
   p.semaphores = reinterpret_cast<uint32_t *>(ws);
@@ -183,33 +254,28 @@ int launch_awq_gemv(const AwqPlan &plan, const uint16_t *x, const int32_t *qweig
   p.K = static_cast<int>(k);
   p.N = static_cast<int>(n);
   p.G = static_cast<int>(g);
-  p.k_tiles = plan.k_tiles;
+  p.groups = sh.groups;
+  p.k_chunks = sh.k_chunks;
+  p.k_blocks = sh.k_blocks;
+  p.n_tiles = sh.n_tiles;
   p.splits = plan.splits;
-  p.n_tiles = plan.n_tiles;
-  dim3 grid(plan.n_tiles, plan.m_tiles, plan.splits);
-  kernel<<<grid, lvb::awq::kGvThreads, C::kSmemBytes, stream>>>(p);
+  dim3 grid(sh.n_tiles, plan.splits);
+  kernel<<<grid, lvb::awqd::kThreads, C::kSmemBytes, stream>>>(xmap, p);
   cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "awq_gemv_kernel launch");
+  if (e != cudaSuccess) return cuda_fail(e, "awq_decode_kernel launch");
   return LVB_OK;
 }
 
-// Decode-sized batches (BN <= 64) take the group-scaled integer kernel,
-// larger ones the fp16-dequantising GEMM.
-int dispatch_awq(const AwqPlan &plan, const uint16_t *x, const int32_t *qweight, const int32_t *qzeros,
-                 const uint16_t *scales, const uint16_t *bias, uint16_t *y, int64_t m, int64_t k, int64_t n,
-                 int64_t g, uint8_t *ws, int dev, cudaStream_t s) {
-  const bool single = g % 64 == 0;
-#define LVB_GV(BN)                                                                                       \
-  return single ? launch_awq_gemv<BN, true>(plan, x, qweight, qzeros, scales, bias, y, m, k, n, g, ws, dev, s) \
-                : launch_awq_gemv<BN, false>(plan, x, qweight, qzeros, scales, bias, y, m, k, n, g, ws, dev, s)
-  switch (plan.bn) {
-    case 16: LVB_GV(16);
-    case 32: LVB_GV(32);
-    case 64: LVB_GV(64);
-    case 128: return launch_awq<128>(plan, x, qweight, qzeros, scales, bias, y, m, k, n, g, ws, dev, s);
-    default: return launch_awq<256>(plan, x, qweight, qzeros, scales, bias, y, m, k, n, g, ws, dev, s);
-  }
-#undef LVB_GV
+int check_awq_shape(int64_t m, int64_t k, int64_t n, int64_t group_size) {
+  if (m < 0 || k <= 0 || n <= 0)
+    return fail(LVB_ERR_INVALID, "invalid AWQ shape m=%lld k=%lld n=%lld", (long long)m, (long long)k, (long long)n);
+  if (m > INT_MAX || k > INT_MAX || n > INT_MAX) return fail(LVB_ERR_UNSUPPORTED, "AWQ dimension exceeds int32");
+  if (group_size <= 0 || group_size % 32 != 0 || k % group_size != 0)
+    return fail(LVB_ERR_INVALID, "AWQ group_size %lld must be a positive multiple of 32 dividing k=%lld",
+                (long long)group_size, (long long)k);
+  if (n % 32 != 0) return fail(LVB_ERR_INVALID, "AWQ output width %lld must be divisible by 32", (long long)n);
+  if (k % 8 != 0) return fail(LVB_ERR_INVALID, "AWQ input width %lld must be divisible by 8", (long long)k);
+  return LVB_OK;
 }
 
 // ------------------------------------------------------------------------
@@ -346,12 +412,16 @@ int lvb_device_error(uint32_t *error_out) {
 }
 
 size_t lvb_awq_workspace_bytes(int64_t m, int64_t k, int64_t n, int64_t group_size) {
-  (void)group_size;
   if (m <= 0 || k <= 0 || n <= 0) return 0;
   int dev = 0;
   if (current_device(&dev) != LVB_OK) return 0;
   const AwqPlan p = awq_plan(m, k, n, sm_count(dev));
-  return p.sem_bytes + p.part_bytes;
+  size_t need = p.sem_bytes + p.part_bytes;
+  if (m <= kPackedMaxM && group_size > 0 && group_size % 32 == 0 && k % group_size == 0) {
+    const PackedPlan pp = packed_plan(m, packed_shape(k, n, group_size), sm_count(dev));
+    if (pp.sem_bytes + pp.part_bytes > need) need = pp.sem_bytes + pp.part_bytes;
+  }
+  return need;
 }
 
 int lvb_awq_linear(const uint16_t *x, const int32_t *qweight, const int32_t *qzeros,
@@ -404,6 +474,71 @@ int lvb_awq_dequantize(const int32_t *qweight, const int32_t *qzeros, const uint
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "awq_dequantize_kernel launch");
   return LVB_OK;
+}
+
+int lvb_awq_pack_bytes(int64_t k, int64_t n, int64_t group_size, size_t *codes_bytes, size_t *groups_bytes) {
+  int rc = check_awq_shape(0, k, n, group_size);
+  if (rc != LVB_OK) return rc;
+  if (!codes_bytes || !groups_bytes) return fail(LVB_ERR_INVALID, "AWQ pack null pointer argument");
+  const PackedShape sh = packed_shape(k, n, group_size);
+  *codes_bytes = sh.codes_bytes;
+  *groups_bytes = sh.groups_bytes;
+  return LVB_OK;
+}
+
+int lvb_awq_pack(const int32_t *qweight, const int32_t *qzeros, const uint16_t *scales, int64_t k, int64_t n,
+                 int64_t group_size, void *codes, void *groups, lvb_stream_t stream) {
+  int rc = check_awq_shape(0, k, n, group_size);
+  if (rc != LVB_OK) return rc;
+  if (!qweight || !qzeros || !scales || !codes || !groups) return fail(LVB_ERR_INVALID, "AWQ pack null pointer argument");
+  if (!aligned16(codes) || !aligned16(groups)) return fail(LVB_ERR_INVALID, "packed AWQ buffers must be 16-byte aligned");
+  int dev = 0;
+  rc = current_device(&dev);
+  if (rc != LVB_OK) return rc;
+  const PackedShape sh = packed_shape(k, n, group_size);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const long long code_threads = static_cast<long long>(sh.n_tiles) * sh.k_chunks * lvb::awqd::kTileN;
+  lvb::awqd::awq_pack_codes_kernel<<<static_cast<unsigned>((code_threads + 255) / 256), 256, 0, s>>>(
+      qweight, static_cast<uint8_t *>(codes), static_cast<int>(k), static_cast<int>(n), sh.k_chunks, sh.n_tiles);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "awq_pack_codes_kernel launch");
+  const long long group_threads = static_cast<long long>(sh.n_tiles) * sh.groups * lvb::awqd::kTileN;
+  lvb::awqd::awq_pack_groups_kernel<<<static_cast<unsigned>((group_threads + 255) / 256), 256, 0, s>>>(
+      qzeros, scales, static_cast<uint32_t *>(groups), static_cast<int>(n), sh.groups, sh.n_tiles);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "awq_pack_groups_kernel launch");
+  return LVB_OK;
+}
+
+int lvb_awq_linear_packed(const uint16_t *x, const void *codes, const void *groups, const uint16_t *bias,
+                          uint16_t *y, int64_t m, int64_t k, int64_t n, int64_t group_size, void *workspace,
+                          size_t workspace_bytes, lvb_stream_t stream) {
+  int rc = check_awq_shape(m, k, n, group_size);
+  if (rc != LVB_OK) return rc;
+  if (m == 0) return LVB_OK;
+  if (m > kPackedMaxM)
+    return fail(LVB_ERR_UNSUPPORTED, "lvb_awq_linear_packed takes at most %lld rows, got %lld", (long long)kPackedMaxM,
+                (long long)m);
+  if (!x || !codes || !groups || !y) return fail(LVB_ERR_INVALID, "AWQ null pointer argument");
+  if (!aligned16(x) || !aligned16(codes) || !aligned16(groups) || (workspace && !aligned16(workspace)))
+    return fail(LVB_ERR_INVALID, "AWQ x, packed buffers and workspace must be 16-byte aligned");
+  int dev = 0;
+  rc = current_device(&dev);
+  if (rc != LVB_OK) return rc;
+  const PackedShape sh = packed_shape(k, n, group_size);
+  const PackedPlan plan = packed_plan(m, sh, sm_count(dev));
+  const size_t need = plan.sem_bytes + plan.part_bytes;
+  if (need > 0 && (workspace == nullptr || workspace_bytes < need))
+    return fail(LVB_ERR_WORKSPACE, "AWQ workspace of %zu bytes is below the %zu required", workspace_bytes, need);
+  uint8_t *ws = static_cast<uint8_t *>(workspace);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const uint8_t *c = static_cast<const uint8_t *>(codes);
+  const uint32_t *g = static_cast<const uint32_t *>(groups);
+  switch (plan.bn) {
+    case 16: return launch_awq_packed<16>(plan, sh, x, c, g, bias, y, m, k, n, group_size, ws, dev, s);
+    case 32: return launch_awq_packed<32>(plan, sh, x, c, g, bias, y, m, k, n, group_size, ws, dev, s);
+    default: return launch_awq_packed<64>(plan, sh, x, c, g, bias, y, m, k, n, group_size, ws, dev, s);
+  }
 }
 
 static int kv_write_common(const lvb::attn::KVWriteArgs &a, int dtype, lvb_stream_t stream) {

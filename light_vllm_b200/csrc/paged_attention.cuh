@@ -287,9 +287,13 @@ __global__ void __launch_bounds__(DecodeCfg<D, HPC>::kThreads, 2)
   int blk_next = 32 + lane < npages ? table[p_begin + 32 + lane] : 0;
   int blk_base = 0;  // page index of blk_cur's lane 0
 
-  // Issue the K and V copies of one page (block id `block`) into `slot`: lane
-  // l copies 16-byte chunks l, l + 32, ... of the head's 16 token rows.
-  auto load_page = [&](int block, int slot) {
+  // Issue the K and V copies of page `pg` (block id `block`) into `slot`: lane
+  // l copies 16-byte chunks l, l + 32, ... of the head's 16 token rows.  Rows
+  // at or past the split's end are zero-filled instead of read: their scores
+  // are masked, but their V rows still enter P V with weight 0, and a cache
+  // slot that was never written may hold NaN bit patterns.
+  auto load_page = [&](int pg, int block, int slot) {
+    const int valid = end - (p_begin + pg) * kPageTokens;
     const uint32_t kdst = ring + slot * Cfg::kPageBytes;
     const uint32_t vdst = kdst + Cfg::kHeadBytes;
     const int64_t base = static_cast<int64_t>(block) * kPageTokens * row_elems + head_off;
@@ -302,8 +306,9 @@ __global__ void __launch_bounds__(DecodeCfg<D, HPC>::kThreads, 2)
       const int c = c16 & 7;
       const uint32_t off = half * kBoxBytes + tok * 128 + ((c ^ (tok & 7)) << 4);
       const int64_t src = base + tok * row_elems + c16 * 8;
-      cp_async_16(kdst + off, a.kc + src, 16u);
-      cp_async_16(vdst + off, a.vc + src, 16u);
+      const uint32_t bytes = tok < valid ? 16u : 0u;
+      cp_async_16(kdst + off, a.kc + (bytes ? src : head_off), bytes);
+      cp_async_16(vdst + off, a.vc + (bytes ? src : head_off), bytes);
     }
     cp_async_arrive_noinc(&ready[slot]);
   };
@@ -319,7 +324,7 @@ __global__ void __launch_bounds__(DecodeCfg<D, HPC>::kThreads, 2)
   };
 
 #pragma unroll 1
-  for (int pg = 0; pg < kStages - 1 && pg < npages; ++pg) load_page(block_of(pg), pg % kStages);
+  for (int pg = 0; pg < kStages - 1 && pg < npages; ++pg) load_page(pg, block_of(pg), pg % kStages);
 
   const int g = lane >> 2;  // MMA row (query head within the group), and +8
   const int cq = lane & 3;  // MMA column pair
@@ -346,7 +351,7 @@ __global__ void __launch_bounds__(DecodeCfg<D, HPC>::kThreads, 2)
   for (int i = 0; i < npages; ++i) {
     // Keep kStages - 1 pages in flight: the slot refilled here held page
     // i - 1, which this warp finished in the previous iteration.
-    if (i + kStages - 1 < npages) load_page(block_of(i + kStages - 1), (i + kStages - 1) % kStages);
+    if (i + kStages - 1 < npages) load_page(i + kStages - 1, block_of(i + kStages - 1), (i + kStages - 1) % kStages);
     const int s = i % kStages;
     const uint32_t ph = (i / kStages) & 1;
     if (!__all_sync(0xffffffffu, mbar_wait(&ready[s], ph, abort_flag))) { ok = false; break; }

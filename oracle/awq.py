@@ -213,3 +213,45 @@ def error_metrics(actual: np.ndarray, expected: np.ndarray) -> tuple[float, floa
     denom = float(np.linalg.norm(e))
     rel_l2 = float(np.linalg.norm(diff) / denom) if denom > 0 else float(np.linalg.norm(diff))
     return max_abs, rel_l2
+
+
+# Nibble slot of k offset e (0..3) within a 4-k quad of the packed decode
+# layout's lower half; the upper half (k + 16) uses the next nibble.
+_DECODE_SLOT = (0, 4, 2, 6)
+
+
+def pack_decode_layout(qweight: np.ndarray, qzeros: np.ndarray, scales: np.ndarray,
+                       group_size: int) -> tuple[np.ndarray, np.ndarray]:
+    """The B200 decode layout (``lvb_awq_pack``), restated with numpy.
+
+    Not a reference function: this is the layout the B200 scheme converts the
+    AutoAWQ checkpoint into once at ``AWQScheme.prepare`` time
+    (``modeling/quantization/awq.py:468-486``).  Used only to check the pack
+    kernel bit for bit.  Returns ``(codes uint8 [tiles, runs, 128, 16],
+    groups uint32 [tiles, K/G, 128])``.
+    """
+
+    codes = unpack(qweight)  # [K, N] natural order
+    zeros = unpack(qzeros)   # [K/G, N]
+    k, n = codes.shape
+    tiles = -(-n // 128)
+    runs = 2 * (-(-k // 64))
+    padded = np.zeros((runs * 32, tiles * 128), dtype=np.uint32)
+    padded[:k, :n] = codes
+    # [tiles, 128 cols, runs, 32 k]
+    per_col = padded.reshape(runs, 32, tiles, 128).transpose(2, 3, 0, 1)
+    words = np.zeros((tiles, 128, runs, 4), dtype=np.uint32)
+    for w in range(4):
+        for e in range(4):
+            words[..., w] |= per_col[..., 4 * w + e] << (4 * _DECODE_SLOT[e])
+            words[..., w] |= per_col[..., 16 + 4 * w + e] << (4 * (_DECODE_SLOT[e] + 1))
+    packed_codes = words.transpose(0, 2, 1, 3).astype("<u4").view(np.uint8).reshape(tiles, runs, 128, 16)
+
+    groups = k // group_size
+    scale_bits = np.zeros((groups, tiles * 128), dtype=np.uint32)
+    scale_bits[:, :n] = np.asarray(scales, dtype=np.float16).view(np.uint16)
+    zero_vals = np.zeros((groups, tiles * 128), dtype=np.uint32)
+    zero_vals[:, :n] = zeros
+    words_g = scale_bits | (zero_vals << 16)
+    packed_groups = words_g.reshape(groups, tiles, 128).transpose(1, 0, 2).copy()
+    return packed_codes, packed_groups

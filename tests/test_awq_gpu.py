@@ -141,3 +141,44 @@ def test_prepare_rejects_bad_layouts():
         B200AWQScheme().prepare(qw, qz, sc, 128, torch.zeros(7, dtype=torch.float16, device=DEV))
     with pytest.raises(ValueError, match="activations must be float16"):
         B200AWQScheme().prepare(qw, qz, sc, 128, None)(torch.zeros(1, 256, device=DEV))
+
+
+@pytest.mark.parametrize("m,k,n,g", [(1, 896, 4864, 128), (16, 512, 1024, 64), (40, 96, 256, 32)])
+def test_checkpoint_layout_entry_for_small_batches(m, k, n, g):
+    """lvb_awq_linear (AutoAWQ layout, no packing) also serves decode sizes."""
+
+    qweight, qzeros, scales = oawq.random_checkpoint(k, n, g, seed=m + k + n)
+    rng = np.random.default_rng(m)
+    x = rng.standard_normal((m, k)).astype(np.float16)
+    expected = oawq.linear_fp32(x, qweight, qzeros, scales, g, None)
+    qw, qz, sc, xg = _gpu(qweight, qzeros, scales, x)
+    lib = _native.library()
+    ws = torch.zeros(max(int(lib.lvb_awq_workspace_bytes(m, k, n, g)), 256), dtype=torch.uint8, device=DEV)
+    y = torch.empty(m, n, dtype=torch.float16, device=DEV)
+    _native.check(lib.lvb_awq_linear(xg.data_ptr(), qw.data_ptr(), qz.data_ptr(), sc.data_ptr(), None,
+                                     y.data_ptr(), m, k, n, g, ws.data_ptr(), ws.numel(),
+                                     torch.cuda.current_stream().cuda_stream), "lvb_awq_linear")
+    torch.cuda.synchronize()
+    max_abs, rel = oawq.error_metrics(y.float().cpu().numpy(), expected)
+    assert max_abs <= MAX_ABS and rel <= REL_L2, (max_abs, rel)
+
+
+@pytest.mark.parametrize("m,k,n,g", [(3, 896, 256, 896), (64, 3584, 512, 128), (8, 7168, 384, 128)])
+def test_packed_decode_shapes(m, k, n, g):
+    """Per-column groups (group = k), the largest packed batch, long k."""
+
+    _check_against_oracle(m, k, n, g, seed=m * 31 + n)
+
+
+def test_packed_entry_rejects_large_batches():
+    from light_vllm_b200.awq import pack_awq_decode_layout
+
+    qweight, qzeros, scales = oawq.random_checkpoint(256, 512, 128, seed=9)
+    qw, qz, sc = _gpu(qweight, qzeros, scales)
+    codes, groups = pack_awq_decode_layout(qw, qz, sc, 128)
+    x = torch.zeros(65, 256, dtype=torch.float16, device=DEV)
+    y = torch.empty(65, 512, dtype=torch.float16, device=DEV)
+    status = _native.library().lvb_awq_linear_packed(x.data_ptr(), codes.data_ptr(), groups.data_ptr(), None,
+                                                     y.data_ptr(), 65, 256, 512, 128, None, 0,
+                                                     torch.cuda.current_stream().cuda_stream)
+    assert status == _native.LVB_ERR_UNSUPPORTED

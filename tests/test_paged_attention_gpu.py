@@ -128,6 +128,29 @@ def test_qwen_gqa_across_history_chunks():
     _run_and_compare(cache, md, q, k, v)
 
 
+@pytest.mark.parametrize("dtype", (torch.float16, torch.bfloat16))
+@pytest.mark.parametrize("prefix", (130, 15, 511))
+def test_decode_ignores_unwritten_slots(dtype, prefix):
+    """Slots past the context end (never written, here NaN) do not leak into
+    the output: the split-context kernel must not weight them even by zero."""
+
+    torch.manual_seed(prefix)
+    cache = _cache(128, dtype, block_size=16, hq=28, hkv=4, num_blocks=40)
+    layer = cache.layer("attention")
+    layer.keys.fill_(float("nan"))
+    layer.values.fill_(float("nan"))
+    pk = torch.randn(prefix, 4, 128, device=DEV, dtype=dtype)
+    pv = torch.randn(prefix, 4, 128, device=DEV, dtype=dtype)
+    cache.write("attention", pk, pv, torch.arange(prefix, device=DEV))
+    pages = -(-(prefix + 1) // 16)
+    md = PagedAttentionMetadata(block_tables=(tuple(range(pages)),), num_computed_tokens=(prefix,),
+                                query_layouts=_layouts(1))
+    q = torch.randn(1, 28, 128, device=DEV, dtype=dtype)
+    k = torch.randn(1, 4, 128, device=DEV, dtype=dtype)
+    v = torch.randn(1, 4, 128, device=DEV, dtype=dtype)
+    _run_and_compare(cache, md, q, k, v)
+
+
 def test_packed_tree_visibility():
     torch.manual_seed(20260819)
     cache = _cache(64, torch.float16)
