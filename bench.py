@@ -18,11 +18,15 @@ Reported (one JSON line on rank 0):
              H2D of q/k/v from pinned host memory, backend.create(cache,
              metadata) (block-table validation + one staged metadata copy),
              forward(), D2H of the output.
-  roofline   the decode-attention launch (split-context kernel + merge) timed
-             alone with CUDA events; peak = measured HBM copy bandwidth.
+  roofline   the decode-attention launch (one split-context kernel whose last
+             split per request merges the partials) timed alone with CUDA
+             events; peak = measured HBM copy bandwidth; traffic = DRAM bytes
+             per launch from the committed ncu summary of this workload.
   cpu_baseline  the CPU oracle (a restatement of the reference's
              TorchPagedAttention) on this host's cores over the same batch.
-  awq        (detail) the W4A16 kernel on config 1 and model-scale shapes.
+  awq        (detail) the W4A16 linear through B200AWQScheme on config 1 and
+             model-scale shapes: decode sizes (m <= 64) run the packed
+             tensor-memory kernel, prefill sizes the dequantising GEMM.
 
 Multi-GPU (torchrun): attention shards over requests with no exchange, so each
 rank runs its own copy of the batch ("weak" scaling, replicas); value sums the
@@ -50,6 +54,18 @@ CFG = dict(num_seqs=64, ctx_lo=512, ctx_hi=4096, hq=28, hkv=4, d=128, block_size
            seed=20261201)
 WORKLOAD = ("paged-attention decode (BASELINE config 2): 64 seqs x 1 query, ctx U[512,4096], "
             "28q/4kv heads, head_dim 128, bf16 K/V, block 16, 40k-block pool")
+
+
+def profiled_traffic(name: str) -> int | None:
+    """DRAM bytes per launch (read + write) from a committed ncu summary, if any."""
+
+    path = ROOT / "profiles" / name
+    if not path.is_file():
+        return None
+    for line in path.read_text().splitlines():
+        if line.strip().startswith("traffic_bytes_per_launch:"):
+            return int(line.split(":", 1)[1])
+    return None
 
 
 def measured_peaks() -> dict:
@@ -421,8 +437,11 @@ def main() -> int:
             "peak": peaks["hbm_gbs"],
             "unit": "GB/s",
             "frac": round(attn_gbs / peaks["hbm_gbs"], 4),
-            "traffic": None,
-            "kernel": "paged_decode_kernel + paged_merge_kernel (one lvb_paged_attention call)",
+            "traffic": profiled_traffic("paged_decode_cfg2.txt"),
+            "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch "
+                              "of this workload (profiles/paged_decode_cfg2.txt)",
+            "kernel": "paged_decode_kernel (split-context decode with in-kernel merge; one "
+                      "lvb_paged_attention call)",
             "peak_source": peaks["source"],
             "algorithmic_bytes_per_launch": nbytes["attention"],
             "launch_us": round(attn_ms * 1e3, 2),

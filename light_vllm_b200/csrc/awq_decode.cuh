@@ -84,7 +84,10 @@ struct DecodeConfig {
   // full, empty (per stage), a_full, a_empty (per A stage), acc_full.
   static constexpr int kNumBars = 2 * kStages + 2 * kAStages + 1;
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;
-  static constexpr int kSmemBytes = kMiscOff + 64 + 1024;  // + base alignment slack
+  // Per stage slot: the (scale, zero) row of each of its 8 chunks, one byte
+  // each, written by the producer so that dequantisers need no division.
+  static constexpr int kRowTableOff = kMiscOff + 64;
+  static constexpr int kSmemBytes = kRowTableOff + kStages * 8 + 1024;  // + base alignment slack
   static_assert(kStages >= 3, "pipeline depth");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
   static_assert(BN % 16 == 0 && BN <= 64, "UMMA N for M = 128");
@@ -192,6 +195,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + C::kMiscOff);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + C::kMiscOff + 8);
   volatile int *last_flag = reinterpret_cast<volatile int *>(smem + C::kMiscOff + 16);
+  uint32_t *row_table = reinterpret_cast<uint32_t *>(smem + C::kRowTableOff);  // [kStages][2]
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -252,6 +256,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int g_first = min(k_first / p.G, p.groups - 1);
           const int g_last = min(k_last / p.G, p.groups - 1);
           const uint32_t sz_bytes = static_cast<uint32_t>((g_last - g_first + 1) * kSzRowBytes);
+          uint32_t rows[2] = {0u, 0u};
+          for (int cl = 0; cl < kStageChunks; ++cl) {
+            const int g = min((chunk0 + cl) * kChunkK / p.G, p.groups - 1) - g_first;
+            rows[cl >> 2] |= static_cast<uint32_t>(g) << (8 * (cl & 3));
+          }
+          // Plain stores, published to the dequantisers by the arrive below.
+          row_table[2 * slot] = rows[0];
+          row_table[2 * slot + 1] = rows[1];
           mbar_arrive_expect_tx(&full[slot], static_cast<uint32_t>(C::kXBytes) + sz_bytes);
           tma_load_3d(stage + C::kXOff, &xmap, &full[slot], 0, 0, chunk0);
           bulk_load(stage + C::kSzOff,
@@ -319,8 +331,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       const uint8_t *stage = smem + slot * C::kStageBytes;
-      const int chunk0 = 2 * (b_begin + ls * kStageBlocks);
-      const int g_first = min(chunk0 * kChunkK / p.G, p.groups - 1);
+      const uint32_t rows_lo = row_table[2 * slot];
+      const uint32_t rows_hi = row_table[2 * slot + 1];
       uint4 q[kBlocksPerGroup][2];
       uint32_t sz[kBlocksPerGroup][2];
 #pragma unroll
@@ -331,7 +343,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int c = 0; c < 2; ++c) {
             const int cl = 2 * b + c;
             q[bi][c] = *reinterpret_cast<const uint4 *>(stage + C::kQOff + cl * kChunkBytes + col * 16);
-            const int g = min((chunk0 + cl) * kChunkK / p.G, p.groups - 1) - g_first;
+            const uint32_t g = ((cl < 4 ? rows_lo : rows_hi) >> (8 * (cl & 3))) & 0xFFu;
             sz[bi][c] = *reinterpret_cast<const uint32_t *>(stage + C::kSzOff + g * kSzRowBytes + col * 4);
           }
         }
