@@ -135,10 +135,13 @@ LVB_API int lvb_awq_pack(const int32_t *qweight, const int32_t *qzeros, const ui
                          int64_t k, int64_t n, int64_t group_size, void *codes, void *groups,
                          lvb_stream_t stream);
 
-/* y[m, n] = x[m, :k] @ W + bias from the packed layout, for m <= 64 (larger m
- * returns LVB_ERR_UNSUPPORTED: use lvb_awq_linear).  Same arithmetic and
- * requirements as lvb_awq_linear; the workspace is sized by
- * lvb_awq_workspace_bytes.  Replaces `awq_gemm` for decode batches
+/* y[m, n] = x[m, :k] @ W + bias from the packed layout, any m.  Same
+ * arithmetic and requirements as lvb_awq_linear.  The split-K plan uses at
+ * most `workspace_bytes` of workspace (NULL or 0: no split), so a smaller
+ * workspace only costs speed; lvb_awq_workspace_bytes gives the size of the
+ * fastest plan.  `codes` may be the checkpoint's own qweight buffer
+ * after repacking it in place (same byte size when n % 128 == 0 and
+ * k % 64 == 0).  Replaces `awq_gemm` and the M>255 dequantise + cuBLAS path
  * (csrc/awq/bindings.cpp:10-13, gemm_kernels.cu:444-501, called from
  * `CudaAWQOperation.__call__`, cuda_awq.py:96-122). */
 LVB_API int lvb_awq_linear_packed(const uint16_t *x, const void *codes, const void *groups,

@@ -5,16 +5,22 @@ a ``LinearOperation`` -- the contract of ``AWQScheme.prepare``
 (modeling/quantization/awq.py:468-486) and ``LinearOperation.__call__``
 (modeling/quantization/interfaces.py:23-26).  It replaces ``CudaAWQScheme`` /
 ``CudaAWQOperation`` (modeling/quantization/awq_schemes.py:56-73,
-cuda_awq.py:96-146) and consumes the same AutoAWQ GEMM tensors.  ``prepare``
-also repacks the codes once into the decode layout (``lvb_awq_pack``; the
-``AWQScheme`` protocol leaves such one-time conversion to the backend, as its
-Marlin-style backends do), which costs a second copy of the int4 codes (half a
-byte per weight) plus one (scale, zero) word per group and column.  Every call
-runs one sm_100a kernel: up to 64 rows the decode kernel over the packed codes
-(``lvb_awq_linear_packed``: weights dequantised into tensor memory), above
-that the general GEMM over the checkpoint layout (``lvb_awq_linear``); both
-run tcgen05 tensor cores with the bias fused into the epilogue and split-K
-for small grids, whose workspace is allocated once here.
+cuda_awq.py:96-146) and consumes the same AutoAWQ GEMM tensors.
+
+Ownership: ``prepare`` repacks the int4 codes once, in place, into the
+layout the tensor-memory kernel streams (``lvb_awq_pack``; the ``AWQScheme``
+protocol leaves one-time conversion to the backend, and a repack replaces the
+checkpoint layout rather than adding a second resident copy of the codes,
+awq.py:506-535, cuda_awq.py:101-102).  After ``prepare`` the layer's
+``qweight`` buffer holds the packed codes; ``qzeros`` and ``scales`` are left
+as they are and one (scale, zero) word per group and column is added (1/32 of
+the code bytes).  Preparing the same storage again reuses the packing.  Shapes
+that do not tile (n % 128 or k % 64 non-zero) keep the checkpoint layout and
+run the checkpoint-layout GEMM (``lvb_awq_linear``).
+
+Every call runs one sm_100a kernel on tcgen05 tensor cores with the bias
+fused into the epilogue and split-K for small grids, whose workspace is
+allocated once here.
 
 Inject it without touching Engine, Scheduler or Worker, e.g.
 ``AWQLinearMethod(AWQConfig.from_mapping(cfg), B200AWQScheme())`` passed as a
@@ -24,6 +30,7 @@ prebuilt ``ModelSpec.linear_method`` (modeling/loaders/safetensors.py:101-102).
 from __future__ import annotations
 
 import ctypes
+import weakref
 from dataclasses import dataclass
 
 import torch
@@ -32,10 +39,13 @@ from torch import Tensor
 from light_vllm_b200 import _native
 
 _PACK_FACTOR = 8
-# Row counts that take the split-K path; the workspace covers the largest.
-_SPLIT_K_ROWS = (1, 16, 32, 64)
-# Rows served by the packed decode kernel (lvb_awq_linear_packed).
-_PACKED_MAX_ROWS = 64
+# Row counts whose fastest plans the prepared split-K workspace covers (one
+# per token-tile class); other sizes run the best plan that fits in it.
+_SPLIT_K_ROWS = (1, 16, 32, 64, 128, 256)
+# Storages already repacked in place: (device index, data_ptr, bytes) -> weak
+# reference to a checkpoint tensor over that storage (the model's buffer keeps
+# it alive; the entry dies with it).
+_PACKED_STORAGES: dict[tuple[int, int, int], weakref.ref] = {}
 
 
 def _validate_static_weights(qweight: Tensor, qzeros: Tensor, scales: Tensor,
@@ -79,8 +89,8 @@ class B200AWQOperation:
     inner: int
     output_width: int
     workspace: Tensor
-    codes: Tensor
-    groups: Tensor
+    codes: Tensor | None   # packed codes (a view of qweight's storage), or None
+    groups: Tensor | None  # packed (scale, zero) words, or None
 
     def __call__(self, inputs: Tensor) -> Tensor:
         flat = inputs.reshape(-1, self.inner)
@@ -90,7 +100,7 @@ class B200AWQOperation:
             flat = flat.contiguous()
         rows = flat.shape[0]
         out = torch.empty((rows, self.output_width), dtype=torch.float16, device=flat.device)
-        if rows <= _PACKED_MAX_ROWS:
+        if self.codes is not None:
             _native.check(
                 _native.library().lvb_awq_linear_packed(
                     flat.data_ptr(), self.codes.data_ptr(), self.groups.data_ptr(),
@@ -127,14 +137,36 @@ def prepare_b200_awq_operation(qweight: Tensor, qzeros: Tensor, scales: Tensor, 
         need = max(int(lib.lvb_awq_workspace_bytes(m, inner, output, group_size)) for m in _SPLIT_K_ROWS)
         # Split-K semaphores must start at zero; every call leaves them zero.
         workspace = torch.zeros(max(need, 256), dtype=torch.uint8, device=qweight.device)
-        codes, groups = pack_awq_decode_layout(qweight, qzeros, scales, group_size)
+        codes = groups = None
+        if output % 128 == 0 and inner % 64 == 0:
+            codes, groups = _pack_in_place(qweight, qzeros, scales, group_size)
     return B200AWQOperation(qweight, qzeros, scales, group_size, bias, inner, output, workspace, codes,
                             groups)
 
 
+def _pack_in_place(qweight: Tensor, qzeros: Tensor, scales: Tensor,
+                   group_size: int) -> tuple[Tensor, Tensor]:
+    """Replace ``qweight``'s contents by the packed codes (same byte size when
+    n % 128 == 0 and k % 64 == 0) and return (codes view, group words)."""
+
+    key = (qweight.device.index or 0, qweight.data_ptr(), qweight.numel() * qweight.element_size())
+    ref = _PACKED_STORAGES.get(key)
+    already = ref is not None and ref() is not None
+    codes, groups = pack_awq_decode_layout(qweight, qzeros, scales, group_size)
+    target = qweight.view(torch.uint8).reshape(-1)
+    if already:
+        return target, groups  # repacked earlier: the fresh codes read packed bytes
+    if target.numel() != codes.numel():
+        raise ValueError("packed AWQ codes must have the checkpoint's byte size")
+    target.copy_(codes)
+    _PACKED_STORAGES[key] = weakref.ref(qweight, lambda _r, k=key: _PACKED_STORAGES.pop(k, None))
+    return target, groups
+
+
 def pack_awq_decode_layout(qweight: Tensor, qzeros: Tensor, scales: Tensor,
                            group_size: int) -> tuple[Tensor, Tensor]:
-    """Packed codes and (scale, zero) words of the decode kernel (``lvb_awq_pack``)."""
+    """Packed codes and (scale, zero) words (``lvb_awq_pack``) in new buffers;
+    the checkpoint tensors are left untouched."""
 
     inner, output = _validate_static_weights(qweight, qzeros, scales, group_size)
     lib = _native.library()

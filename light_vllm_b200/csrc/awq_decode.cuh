@@ -1,47 +1,44 @@
-// AutoAWQ W4A16 linear for decode-sized batches (m <= 64) on sm_100a, with
-// the dequantised weight written straight into tensor memory.
+// AutoAWQ W4A16 linear on sm_100a with the dequantised weight written
+// straight into tensor memory, over the packed weight layout.
 //
 // y[m, n] = sum_k x[m, k] * W[k, n] (+ bias[n]),  W[k, n] = fp16(q - z) * s.
 //
 // The weight is the UMMA "A" operand (M = 128 output columns per CTA) and the
-// activations are "B" (N = BN tokens).  Unlike the general GEMM, A never goes
-// through shared memory: every thread owns one output column (one TMEM lane),
-// turns 32 of its int4 codes into fp16 in registers and stores them with
-// tcgen05.st into an A buffer in tensor memory; tcgen05.mma then reads A from
-// tensor memory and B from shared memory.  Shared memory only carries the
-// streamed int4 codes (0.5 byte per weight) and the small activation tiles, so
-// the kernel is bound by HBM and by dequantisation issue rate, not by
-// shared-memory bandwidth.
+// activations are "B" (N = BN tokens).  A never goes through shared memory:
+// every dequantiser thread owns one output column (one TMEM lane), turns 32 of
+// its int4 codes into fp16 in registers and stores them with tcgen05.st into
+// an A stage in tensor memory; tcgen05.mma then reads A from tensor memory and
+// B from shared memory.  Shared memory only carries the streamed int4 codes
+// (0.5 byte per weight) and the activation tiles.
 //
-// Weights are read in the packed layout written once by `awq_pack_kernel`
+// Weights are read in the packed layout written once by the pack kernels below
 // (column-major int4 runs, 16 bytes = 32 k of one column, 2 KB per 128-column
-// x 32-k chunk) so that one contiguous bulk copy fetches a stage and a thread's
-// 16 bytes hold exactly the codes its TMEM lane needs.  Within a 16-byte run,
-// word w holds k = 4w..4w+3 in nibbles (0, 4, 2, 6) and k = 16+4w..16+4w+3 in
-// nibbles (1, 5, 3, 7).  Masking a word with 0x000F000F and OR-ing 0x6400
-// gives the half2 of 1024 + q for (k, k+1); masking with 0x00F000F0 gives
-// 1024 + 16 q for the upper half of the run.  Differences with the zero point
-// in the same biased form are the exact integers q - z and 16 (q - z); one
+// x 32-k chunk) so that one contiguous bulk copy fetches a stage and a
+// thread's 16 bytes hold exactly the codes its TMEM lane needs.  Within a
+// 16-byte run, word w holds k = 4w..4w+3 in nibbles (0, 4, 2, 6) and
+// k = 16+4w..16+4w+3 in nibbles (1, 5, 3, 7).  Masking a word with 0x000F000F
+// and OR-ing 0x6400 gives the half2 of 1024 + q for (k, k+1); differences with
+// the zero point in the same biased form are the exact integers q - z, and one
 // fp16 multiply by the scale rounds like the reference's dequantised weight
-// (modeling/quantization/awq.py:433-450), the 16x values exactly 16 times that
-// (|scale| < 273).  The two halves accumulate into separate TMEM accumulators
-// D_lo and D_hi (K = 16 per MMA, so every MMA reads one half only), and the
-// epilogue forms D_lo + D_hi / 16 in fp32.
+// (modeling/quantization/awq.py:433-450).  With DUAL, the upper 16 k of a run
+// come from the mask 0x00F000F0 as 1024 + 16 q, i.e. 16 (q - z) * s = exactly
+// 16 W (|scale| < 273); they accumulate into a second TMEM accumulator (K = 16
+// per MMA, so every MMA reads one half only) and the epilogue forms
+// D_lo + D_hi / 16 in fp32.  Without DUAL (large N, where the two
+// accumulators would not fit next to the A stages) the upper half is shifted
+// down first and a single accumulator holds exact W products.
 //
 // Roles (one CTA per SM):
-//   warp 0        bulk copies of the packed codes, one per 256-k stage
+//   warp 0        bulk copies of the packed codes, one per stage
 //   warp 1        activation tile (TMA, 64-byte swizzle, zero fill past m and
-//                 k) and the stage's (scale, zero) rows
+//                 k), the stage's (scale, zero) rows and their row table
 //   warp 2        TMEM allocator and the single thread issuing tcgen05.mma
-//   warps 3..     kDqGroups warpgroups of dequantisers; warpgroup w handles
-//                 the 64-k blocks w, w + kDqGroups, ... of every stage into
-//                 one of three TMEM A stages; the first warpgroup also runs
-//                 the epilogue.
-// The MMA issuer waits once per stage and issues its 16 MMAs back to back:
-// a tcgen05.mma with N <= 128 occupies the tensor pipe for a fixed ~70
-// cycles, so per-block waits between them would cost more than the MMAs.
-// Small grids split K across CTAs; partial fp32 tiles are summed in split
-// order by the last CTA of a tile, so results are deterministic.
+//   warps 3..     DG warpgroups of dequantisers; warpgroup w handles the 64-k
+//                 blocks w, w + DG, ... of every stage into one of the TMEM A
+//                 stages; the first warpgroup also runs the epilogue.
+// Grid: (m tiles, column tiles, K splits), m tiles fastest.  Small grids split
+// K across CTAs; partial fp32 tiles are summed in split order by the last CTA
+// of a tile, so results are deterministic.
 #pragma once
 
 #include "lvb_common.cuh"
@@ -53,44 +50,50 @@ constexpr int kTileN = 128;                       // output columns per CTA (UMM
 constexpr int kChunkK = 32;                       // k per packed run (16 bytes per column)
 constexpr int kChunkBytes = kTileN * 16;          // 2048
 constexpr int kBlockK = 64;                       // k per dequantiser work unit
-constexpr int kStageBlocks = 4;                   // 64-k blocks per pipeline stage
-constexpr int kStageChunks = 2 * kStageBlocks;    // 8 packed chunks per stage
-constexpr int kQStageBytes = kStageChunks * kChunkBytes;  // 16384
 constexpr int kSzRowBytes = kTileN * 4;           // (scale, zero) words of one group
-constexpr int kSzStageBytes = kStageChunks * kSzRowBytes;  // at most 8 groups per stage
-constexpr int kDqGroups = 2;                      // dequantiser warpgroups (2 measured faster than 1 or 4)
-constexpr int kBlocksPerGroup = kStageBlocks / kDqGroups;
-constexpr int kDqWarps = 4 * kDqGroups;
 constexpr int kFirstDqWarp = 3;
-constexpr int kThreads = (kFirstDqWarp + kDqWarps) * 32;
 constexpr int kEpilogueThreads = 128;             // the first dequantiser warpgroup
-constexpr int kAStages = 3;                       // TMEM A stages (4 blocks x 32 columns each)
-constexpr int kDLoCol = 0;
-constexpr int kDHiCol = 64;
-constexpr int kACol = 128;
 constexpr int kTmemCols = 512;
 constexpr int kSmemBudget = 216 * 1024;
 
-template <int BN>
-struct DecodeConfig {
-  static constexpr int kXChunkBytes = BN * 64;                 // BN rows x 32 k (64-byte swizzle)
-  static constexpr int kXBytes = kStageChunks * kXChunkBytes;  // TMA box bytes per stage
+// BN: token rows per CTA (UMMA N).  SB: 64-k blocks per pipeline stage.  DG:
+// dequantiser warpgroups (warpgroup w takes blocks w, w + DG, ... of a stage).
+// DUAL: the upper 16 k of every 32-k run are dequantised as 16 W and
+// accumulate into a second accumulator (one instruction less per code pair);
+// otherwise one accumulator and exact W throughout.
+template <int BN, int SB, int DG, bool DUAL>
+struct PackedConfig {
+  static constexpr int kStageChunks = 2 * SB;
+  static constexpr int kQStageBytes = kStageChunks * kChunkBytes;
+  static constexpr int kSzStageBytes = kStageChunks * kSzRowBytes;  // at most one group per chunk
+  static constexpr int kXChunkBytes = BN * 64;                       // BN rows x 32 k (64-byte swizzle)
+  static constexpr int kXBytes = kStageChunks * kXChunkBytes;        // TMA box bytes per stage
   static constexpr int kXOff = 0;
   static constexpr int kQOff = kXBytes;
   static constexpr int kSzOff = kQOff + kQStageBytes;
   static constexpr int kStageBytes = ((kSzOff + kSzStageBytes) + 1023) / 1024 * 1024;
   static constexpr int kStages = kSmemBudget / kStageBytes > 8 ? 8 : kSmemBudget / kStageBytes;
+  // Tensor memory: D_lo [0, BN), D_hi [BN, 2 BN) when DUAL, then the A stages.
+  static constexpr int kDHiCol = BN;
+  static constexpr int kACol = ((DUAL ? 2 * BN : BN) + 31) / 32 * 32;
+  static constexpr int kAStageCols = SB * 32;
+  static constexpr int kAStages = (kTmemCols - kACol) / kAStageCols > 4 ? 4 : (kTmemCols - kACol) / kAStageCols;
+  static constexpr int kBlocksPerGroup = SB / DG;
+  static constexpr int kDqWarps = 4 * DG;
+  static constexpr int kThreads = (kFirstDqWarp + kDqWarps) * 32;
   static constexpr int kBarOff = kStages * kStageBytes;
   // full, empty (per stage), a_full, a_empty (per A stage), acc_full.
   static constexpr int kNumBars = 2 * kStages + 2 * kAStages + 1;
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;
-  // Per stage slot: the (scale, zero) row of each of its 8 chunks, one byte
-  // each, written by the producer so that dequantisers need no division.
+  // Per stage slot: the (scale, zero) row of each chunk, one byte each,
+  // written by the producer so that dequantisers need no division.
   static constexpr int kRowTableOff = kMiscOff + 64;
   static constexpr int kSmemBytes = kRowTableOff + kStages * 8 + 1024;  // + base alignment slack
+  static_assert(SB % DG == 0 && kStageChunks <= 8, "stage blocks per warpgroup");
   static_assert(kStages >= 3, "pipeline depth");
+  static_assert(kAStages >= 2, "tensor-memory A stages");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
-  static_assert(BN % 16 == 0 && BN <= 64, "UMMA N for M = 128");
+  static_assert(BN % 16 == 0 && BN <= 256, "UMMA N for M = 128");
 };
 
 struct DecodeParams {
@@ -99,12 +102,12 @@ struct DecodeParams {
   const uint16_t *bias;    // may be null
   uint16_t *y;
   uint32_t *semaphores;    // per output tile, zero between calls
-  float *partials;         // [n_tiles][splits][BN][128] when splits > 1
+  float *partials;         // [tiles][splits][BN][128] when splits > 1
   int M, K, N, G;
   int groups;
   int k_chunks;            // packed chunks per column tile (K rounded up to 64, / 32)
   int k_blocks;            // k_chunks / 2
-  int n_tiles, splits;
+  int n_tiles, m_tiles, splits;
 };
 
 __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
@@ -160,8 +163,10 @@ __device__ __forceinline__ uint32_t hsub_hmul(uint32_t a, uint32_t b, uint32_t c
   return *reinterpret_cast<uint32_t *>(&r);
 }
 
-// Dequantise one 16-byte run (32 k of one column) into 16 half2 words:
-// out[0..7] = W for k 0..15 (pairs), out[8..15] = 16 W for k 16..31.
+// Dequantise one 16-byte run (32 k of one column) into 16 half2 words in k
+// order: out[0..7] = W for k 0..15, out[8..15] = k 16..31, as W (exact) or,
+// when DUAL, as 16 W (exact multiple of W for |scale| < 273).
+template <bool DUAL>
 __device__ __forceinline__ void dequant_run(const uint4 q, uint32_t sz, uint32_t *out) {
   const uint32_t s2 = __byte_perm(sz, 0, 0x1010);  // (scale, scale)
   const uint32_t z = sz >> 16;
@@ -174,15 +179,21 @@ __device__ __forceinline__ void dequant_run(const uint4 q, uint32_t sz, uint32_t
     const uint32_t w8 = w[i] >> 8;
     out[2 * i] = hsub_hmul((w[i] & 0x000F000Fu) | 0x64006400u, zlo, s2);
     out[2 * i + 1] = hsub_hmul((w8 & 0x000F000Fu) | 0x64006400u, zlo, s2);
-    out[8 + 2 * i] = hsub_hmul((w[i] & 0x00F000F0u) | 0x64006400u, zhi, s2);
-    out[8 + 2 * i + 1] = hsub_hmul((w8 & 0x00F000F0u) | 0x64006400u, zhi, s2);
+    if constexpr (DUAL) {
+      out[8 + 2 * i] = hsub_hmul((w[i] & 0x00F000F0u) | 0x64006400u, zhi, s2);
+      out[8 + 2 * i + 1] = hsub_hmul((w8 & 0x00F000F0u) | 0x64006400u, zhi, s2);
+    } else {
+      out[8 + 2 * i] = hsub_hmul(((w[i] >> 4) & 0x000F000Fu) | 0x64006400u, zlo, s2);
+      out[8 + 2 * i + 1] = hsub_hmul(((w[i] >> 12) & 0x000F000Fu) | 0x64006400u, zlo, s2);
+    }
   }
 }
 
-template <int BN>
-__global__ void __launch_bounds__(kThreads, 1)
-    awq_decode_kernel(const __grid_constant__ CUtensorMap xmap, const DecodeParams p) {
-  using C = DecodeConfig<BN>;
+template <int BN, int SB, int DG, bool DUAL>
+__global__ void __launch_bounds__(PackedConfig<BN, SB, DG, DUAL>::kThreads, 1)
+    awq_packed_kernel(const __grid_constant__ CUtensorMap xmap, const DecodeParams p) {
+  using C = PackedConfig<BN, SB, DG, DUAL>;
+  constexpr int kAStages = C::kAStages;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -199,20 +210,24 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int tile = blockIdx.x;
-  const int split = blockIdx.y;
+  // m tiles vary fastest across the grid, so the CTAs sharing a column tile
+  // of weights run together and read it from HBM once.
+  const int m_tile = blockIdx.x;
+  const int tile = blockIdx.y;
+  const int split = blockIdx.z;
+  const int tile_id = tile * p.m_tiles + m_tile;
   const int b_begin = static_cast<int>((static_cast<long long>(split) * p.k_blocks) / p.splits);
   const int b_end = static_cast<int>((static_cast<long long>(split + 1) * p.k_blocks) / p.splits);
   const int nblocks = b_end - b_begin;
-  const int nstages = (nblocks + kStageBlocks - 1) / kStageBlocks;
+  const int nstages = (nblocks + SB - 1) / SB;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::kStages; ++s) {
       mbar_init(&full[s], 2);
-      mbar_init(&empty[s], kDqWarps + 1);
+      mbar_init(&empty[s], C::kDqWarps + 1);
     }
     for (int j = 0; j < kAStages; ++j) {
-      mbar_init(&a_full[j], kDqWarps);
+      mbar_init(&a_full[j], C::kDqWarps);
       mbar_init(&a_empty[j], 1);
     }
     mbar_init(acc_full, 1);
@@ -241,8 +256,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         uint8_t *stage = smem + slot * C::kStageBytes;
-        const int blk0 = b_begin + ls * kStageBlocks;
-        const int nb = min(kStageBlocks, b_end - blk0);
+        const int blk0 = b_begin + ls * SB;
+        const int nb = min(SB, b_end - blk0);
         const int chunk0 = 2 * blk0;
         if (warp == 0) {
           const uint32_t bytes = static_cast<uint32_t>(2 * nb * kChunkBytes);
@@ -257,7 +272,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int g_last = min(k_last / p.G, p.groups - 1);
           const uint32_t sz_bytes = static_cast<uint32_t>((g_last - g_first + 1) * kSzRowBytes);
           uint32_t rows[2] = {0u, 0u};
-          for (int cl = 0; cl < kStageChunks; ++cl) {
+          for (int cl = 0; cl < C::kStageChunks; ++cl) {
             const int g = min((chunk0 + cl) * kChunkK / p.G, p.groups - 1) - g_first;
             rows[cl >> 2] |= static_cast<uint32_t>(g) << (8 * (cl & 3));
           }
@@ -265,7 +280,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           row_table[2 * slot] = rows[0];
           row_table[2 * slot + 1] = rows[1];
           mbar_arrive_expect_tx(&full[slot], static_cast<uint32_t>(C::kXBytes) + sz_bytes);
-          tma_load_3d(stage + C::kXOff, &xmap, &full[slot], 0, 0, chunk0);
+          tma_load_3d(stage + C::kXOff, &xmap, &full[slot], 0, m_tile * BN, chunk0);
           bulk_load(stage + C::kSzOff,
                     p.szpack + (static_cast<size_t>(tile) * p.groups + g_first) * kTileN, sz_bytes,
                     &full[slot]);
@@ -281,6 +296,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else if (warp == 2) {
     // ---------------- tcgen05.mma issuer ----------------
+    // Every dequantiser warp arrives once per stage, so one wait covers the
+    // stage and its MMAs issue back to back: a tcgen05.mma with N <= 128
+    // occupies the tensor pipe for a fixed ~70 cycles, so per-block waits
+    // between them would cost more than the MMAs.
     if (lane == 0) {
       constexpr uint32_t idesc = umma_idesc_f16(kTileN, BN, 0, 0, 0, 0);
       bool ok = true;
@@ -289,22 +308,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!mbar_wait(&full[slot], (ls / C::kStages) & 1, abort_flag)) { ok = false; break; }
         tc_fence_after();
         const uint32_t x_base = smem_u32(smem + slot * C::kStageBytes + C::kXOff);
-        const int nb = min(kStageBlocks, nblocks - ls * kStageBlocks);
-        // Every dequantiser warp arrives once per stage, so one wait covers the
-        // stage's blocks and its MMAs issue back to back.
+        const int nb = min(SB, nblocks - ls * SB);
         const int as = ls % kAStages;
         if (!mbar_wait(&a_full[as], (ls / kAStages) & 1, abort_flag)) { ok = false; break; }
         tc_fence_after();
         for (int b = 0; b < nb; ++b) {
-          const uint32_t a_blk = tmem + kACol + (as * kStageBlocks + b) * 32;
+          const uint32_t a_blk = tmem + C::kACol + as * C::kAStageCols + b * 32;
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
               const uint64_t bdesc =
                   umma_desc_kmajor_sw64(x_base + (2 * b + c) * C::kXChunkBytes + h * 32);
-              umma_f16_ts(tmem + (h ? kDHiCol : kDLoCol), a_blk + c * 16 + h * 8, bdesc, idesc,
-                          (ls | b | c) != 0 ? 1u : 0u);
+              const uint32_t d_addr = tmem + ((DUAL && h) ? C::kDHiCol : 0);
+              const bool first = (ls | b | c) == 0 && (DUAL || h == 0);
+              umma_f16_ts(d_addr, a_blk + c * 16 + h * 8, bdesc, idesc, first ? 0u : 1u);
             }
           }
         }
@@ -325,7 +343,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     for (int ls = 0; ls < nstages; ++ls) {
       const int slot = ls % C::kStages;
-      const int nb = min(kStageBlocks, nblocks - ls * kStageBlocks);
+      const int nb = min(SB, nblocks - ls * SB);
       if (!__all_sync(0xffffffffu, mbar_wait(&full[slot], (ls / C::kStages) & 1, abort_flag))) {
         ok = false;
         break;
@@ -333,11 +351,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint8_t *stage = smem + slot * C::kStageBytes;
       const uint32_t rows_lo = row_table[2 * slot];
       const uint32_t rows_hi = row_table[2 * slot + 1];
-      uint4 q[kBlocksPerGroup][2];
-      uint32_t sz[kBlocksPerGroup][2];
+      uint4 q[C::kBlocksPerGroup][2];
+      uint32_t sz[C::kBlocksPerGroup][2];
 #pragma unroll
-      for (int bi = 0; bi < kBlocksPerGroup; ++bi) {
-        const int b = wg + bi * kDqGroups;
+      for (int bi = 0; bi < C::kBlocksPerGroup; ++bi) {
+        const int b = wg + bi * DG;
         if (b < nb) {
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
@@ -350,12 +368,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[slot]);
-      uint32_t a[kBlocksPerGroup][32];
+      uint32_t a[C::kBlocksPerGroup][32];
 #pragma unroll
-      for (int bi = 0; bi < kBlocksPerGroup; ++bi) {
-        if (wg + bi * kDqGroups < nb) {
-          dequant_run(q[bi][0], sz[bi][0], a[bi]);
-          dequant_run(q[bi][1], sz[bi][1], a[bi] + 16);
+      for (int bi = 0; bi < C::kBlocksPerGroup; ++bi) {
+        if (wg + bi * DG < nb) {
+          dequant_run<DUAL>(q[bi][0], sz[bi][0], a[bi]);
+          dequant_run<DUAL>(q[bi][1], sz[bi][1], a[bi] + 16);
         }
       }
       const int as = ls % kAStages;
@@ -366,9 +384,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_after();
 #pragma unroll
-      for (int bi = 0; bi < kBlocksPerGroup; ++bi) {
-        const int b = wg + bi * kDqGroups;
-        if (b < nb) tmem_st_32x32b_x32(tmem + lane_base + kACol + (as * kStageBlocks + b) * 32, a[bi]);
+      for (int bi = 0; bi < C::kBlocksPerGroup; ++bi) {
+        const int b = wg + bi * DG;
+        if (b < nb) tmem_st_32x32b_x32(tmem + lane_base + C::kACol + as * C::kAStageCols + b * 32, a[bi]);
       }
       tmem_wait_st();
       tc_fence_before();
@@ -382,22 +400,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       ok = __all_sync(0xffffffffu, ok) && nblocks > 0;
       tc_fence_after();
       const int n = tile * kTileN + col;
+      const int m0 = m_tile * BN;
       const bool n_ok = n < p.N;
       const float bias_n = (p.bias != nullptr && n_ok) ? __half2float(__ushort_as_half(p.bias[n])) : 0.f;
-      float *part = p.partials + static_cast<size_t>(tile) * p.splits * BN * kTileN;
+      float *part = p.partials + static_cast<size_t>(tile_id) * p.splits * BN * kTileN;
       if (ok) {
 #pragma unroll 1
         for (int c0 = 0; c0 < BN; c0 += 8) {
           float lo[8], hi[8];
-          tmem_ld_32x32b_x8(tmem + lane_base + kDLoCol + c0, lo);
-          tmem_ld_32x32b_x8(tmem + lane_base + kDHiCol + c0, hi);
+          tmem_ld_32x32b_x8(tmem + lane_base + c0, lo);
+          if constexpr (DUAL) tmem_ld_32x32b_x8(tmem + lane_base + C::kDHiCol + c0, hi);
           tmem_wait_ld();
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
-            const float v = fmaf(hi[c], 0.0625f, lo[c]);
+            const float v = DUAL ? fmaf(hi[c], 0.0625f, lo[c]) : lo[c];
             const int m = c0 + c;
             if (p.splits == 1) {
-              if (n_ok && m < p.M) p.y[static_cast<size_t>(m) * p.N + n] = __half_as_ushort(__float2half_rn(v + bias_n));
+              if (n_ok && m0 + m < p.M)
+                p.y[static_cast<size_t>(m0 + m) * p.N + n] = __half_as_ushort(__float2half_rn(v + bias_n));
             } else {
               __stcg(part + (static_cast<size_t>(split) * BN + m) * kTileN + col, v);
             }
@@ -408,7 +428,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         __threadfence();
         asm volatile("bar.sync 1, %0;" ::"n"(kEpilogueThreads) : "memory");
         if (dw == 0 && lane == 0) {
-          const unsigned int prev = ok ? atomicAdd(p.semaphores + tile, 1u) : 0u;
+          const unsigned int prev = ok ? atomicAdd(p.semaphores + tile_id, 1u) : 0u;
           *last_flag = (ok && prev == static_cast<unsigned int>(p.splits - 1)) ? 1 : 0;
         }
         asm volatile("bar.sync 1, %0;" ::"n"(kEpilogueThreads) : "memory");
@@ -417,25 +437,25 @@ __global__ void __launch_bounds__(kThreads, 1)
           // Sum the splits in order, 16 rows at a time; the loads of one split
           // are independent of each other.
 #pragma unroll 1
-          for (int m0 = 0; m0 < BN; m0 += 16) {
+          for (int r0 = 0; r0 < BN; r0 += 16) {
             float sum[16];
 #pragma unroll
             for (int m = 0; m < 16; ++m) sum[m] = 0.f;
             for (int s = 0; s < p.splits; ++s) {
               float v[16];
 #pragma unroll
-              for (int m = 0; m < 16; ++m) v[m] = __ldcg(part + (static_cast<size_t>(s) * BN + m0 + m) * kTileN + col);
+              for (int m = 0; m < 16; ++m) v[m] = __ldcg(part + (static_cast<size_t>(s) * BN + r0 + m) * kTileN + col);
 #pragma unroll
               for (int m = 0; m < 16; ++m) sum[m] += v[m];
             }
             if (n_ok) {
 #pragma unroll
               for (int m = 0; m < 16; ++m)
-                if (m0 + m < p.M)
-                  p.y[static_cast<size_t>(m0 + m) * p.N + n] = __half_as_ushort(__float2half_rn(sum[m] + bias_n));
+                if (m0 + r0 + m < p.M)
+                  p.y[static_cast<size_t>(m0 + r0 + m) * p.N + n] = __half_as_ushort(__float2half_rn(sum[m] + bias_n));
             }
           }
-          if (dw == 0 && lane == 0) p.semaphores[tile] = 0u;
+          if (dw == 0 && lane == 0) p.semaphores[tile_id] = 0u;
         }
       }
       tc_fence_before();

@@ -178,8 +178,6 @@ int dispatch_awq(const AwqPlan &plan, const uint16_t *x, const int32_t *qweight,
 // ------------------------------------------------------------------------
 // Packed-layout decode path
 // ------------------------------------------------------------------------
-constexpr int64_t kPackedMaxM = 64;
-
 struct PackedShape {
   int n_tiles, k_chunks, k_blocks, groups;
   size_t codes_bytes, groups_bytes;
@@ -197,20 +195,31 @@ PackedShape packed_shape(int64_t k, int64_t n, int64_t g) {
 }
 
 struct PackedPlan {
-  int bn, splits;
+  int bn, m_tiles, splits;
   size_t sem_bytes, part_bytes;
 };
 
-// K splits for a one-wave-per-SM grid: the split count that minimises
-// (waves of CTAs) x (64-k blocks per CTA), fewest splits on ties.
-PackedPlan packed_plan(int64_t m, const PackedShape &sh, int sms) {
+// Token tile per batch size: the decode configurations (two accumulators,
+// 256-k stages) up to 64 rows, 128 rows with two accumulators, then 256-row
+// tiles with one accumulator.
+int packed_bn(int64_t m) { return m <= 16 ? 16 : m <= 32 ? 32 : m <= 64 ? 64 : m <= 128 ? 128 : 256; }
+
+// K splits for grids smaller than the SM count: the split count that
+// minimises (waves of CTAs) x (64-k blocks per CTA), fewest splits on ties,
+// among the plans whose split-K workspace fits in `max_ws` bytes.
+PackedPlan packed_plan(int64_t m, const PackedShape &sh, int sms, size_t max_ws = SIZE_MAX) {
   PackedPlan p{};
-  p.bn = m <= 16 ? 16 : m <= 32 ? 32 : 64;
+  p.bn = packed_bn(m);
+  p.m_tiles = static_cast<int>((m + p.bn - 1) / p.bn);
+  const long long tiles = static_cast<long long>(sh.n_tiles) * p.m_tiles;
   int best = 1;
   long long best_cost = -1;
   const int max_splits = sh.k_blocks < 16 ? sh.k_blocks : 16;
+  const size_t sem = (static_cast<size_t>(tiles) * 4 + 255) & ~static_cast<size_t>(255);
   for (int sp = 1; sp <= max_splits; ++sp) {
-    const long long ctas = static_cast<long long>(sh.n_tiles) * sp;
+    const size_t need = sp > 1 ? sem + static_cast<size_t>(tiles) * sp * p.bn * lvb::awqd::kTileN * sizeof(float) : 0;
+    if (need > max_ws) continue;
+    const long long ctas = tiles * sp;
     const long long waves = (ctas + sms - 1) / sms;
     const long long cost = waves * ((sh.k_blocks + sp - 1) / sp);
     if (best_cost < 0 || cost < best_cost) {
@@ -219,28 +228,28 @@ PackedPlan packed_plan(int64_t m, const PackedShape &sh, int sms) {
     }
   }
   p.splits = best;
-  p.sem_bytes = p.splits > 1 ? (static_cast<size_t>(sh.n_tiles) * 4 + 255) & ~static_cast<size_t>(255) : 0;
+  p.sem_bytes = p.splits > 1 ? sem : 0;
   p.part_bytes =
-      p.splits > 1 ? static_cast<size_t>(sh.n_tiles) * p.splits * p.bn * lvb::awqd::kTileN * sizeof(float) : 0;
+      p.splits > 1 ? static_cast<size_t>(tiles) * p.splits * p.bn * lvb::awqd::kTileN * sizeof(float) : 0;
   return p;
 }
 
-template <int BN>
+template <int BN, int SB, int DG, bool DUAL>
 int launch_awq_packed(const PackedPlan &plan, const PackedShape &sh, const uint16_t *x, const uint8_t *codes,
                       const uint32_t *groups, const uint16_t *bias, uint16_t *y, int64_t m, int64_t k,
                       int64_t n, int64_t g, uint8_t *ws, int dev, cudaStream_t stream) {
-  using C = lvb::awqd::DecodeConfig<BN>;
+  using C = lvb::awqd::PackedConfig<BN, SB, DG, DUAL>;
   static bool smem_done[kMaxDevices] = {false};
-  auto kernel = lvb::awqd::awq_decode_kernel<BN>;
+  auto kernel = lvb::awqd::awq_packed_kernel<BN, SB, DG, DUAL>;
   int rc = ensure_smem(kernel, C::kSmemBytes, dev, smem_done);
   if (rc != LVB_OK) return rc;
   // Activations as [k / 32 chunks][m rows][32 k]: one box per stage fetches
-  // eight 64-byte-swizzled [BN x 32] tiles, rows past m and chunks past k
-  // read as zeros.
+  // the stage's 64-byte-swizzled [BN x 32] tiles; rows past m and chunks past
+  // k read as zeros.
   CUtensorMap xmap;
   const cuuint64_t dims[3] = {32, static_cast<cuuint64_t>(m), static_cast<cuuint64_t>(k / 32)};
   const cuuint64_t strides[2] = {static_cast<cuuint64_t>(k) * 2, 64};
-  const cuuint32_t box[3] = {32, static_cast<cuuint32_t>(BN), static_cast<cuuint32_t>(lvb::awqd::kStageChunks)};
+  const cuuint32_t box[3] = {32, static_cast<cuuint32_t>(BN), static_cast<cuuint32_t>(C::kStageChunks)};
   rc = encode_map(&xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, x, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B);
   if (rc != LVB_OK) return rc;
   lvb::awqd::DecodeParams p{};
@@ -258,11 +267,12 @@ int launch_awq_packed(const PackedPlan &plan, const PackedShape &sh, const uint1
   p.k_chunks = sh.k_chunks;
   p.k_blocks = sh.k_blocks;
   p.n_tiles = sh.n_tiles;
+  p.m_tiles = plan.m_tiles;
   p.splits = plan.splits;
-  dim3 grid(sh.n_tiles, plan.splits);
-  kernel<<<grid, lvb::awqd::kThreads, C::kSmemBytes, stream>>>(xmap, p);
+  dim3 grid(plan.m_tiles, sh.n_tiles, plan.splits);
+  kernel<<<grid, C::kThreads, C::kSmemBytes, stream>>>(xmap, p);
   cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "awq_decode_kernel launch");
+  if (e != cudaSuccess) return cuda_fail(e, "awq_packed_kernel launch");
   return LVB_OK;
 }
 
@@ -417,7 +427,7 @@ size_t lvb_awq_workspace_bytes(int64_t m, int64_t k, int64_t n, int64_t group_si
   if (current_device(&dev) != LVB_OK) return 0;
   const AwqPlan p = awq_plan(m, k, n, sm_count(dev));
   size_t need = p.sem_bytes + p.part_bytes;
-  if (m <= kPackedMaxM && group_size > 0 && group_size % 32 == 0 && k % group_size == 0) {
+  if (group_size > 0 && group_size % 32 == 0 && k % group_size == 0) {
     const PackedPlan pp = packed_plan(m, packed_shape(k, n, group_size), sm_count(dev));
     if (pp.sem_bytes + pp.part_bytes > need) need = pp.sem_bytes + pp.part_bytes;
   }
@@ -516,9 +526,6 @@ int lvb_awq_linear_packed(const uint16_t *x, const void *codes, const void *grou
   int rc = check_awq_shape(m, k, n, group_size);
   if (rc != LVB_OK) return rc;
   if (m == 0) return LVB_OK;
-  if (m > kPackedMaxM)
-    return fail(LVB_ERR_UNSUPPORTED, "lvb_awq_linear_packed takes at most %lld rows, got %lld", (long long)kPackedMaxM,
-                (long long)m);
   if (!x || !codes || !groups || !y) return fail(LVB_ERR_INVALID, "AWQ null pointer argument");
   if (!aligned16(x) || !aligned16(codes) || !aligned16(groups) || (workspace && !aligned16(workspace)))
     return fail(LVB_ERR_INVALID, "AWQ x, packed buffers and workspace must be 16-byte aligned");
@@ -526,18 +533,18 @@ int lvb_awq_linear_packed(const uint16_t *x, const void *codes, const void *grou
   rc = current_device(&dev);
   if (rc != LVB_OK) return rc;
   const PackedShape sh = packed_shape(k, n, group_size);
-  const PackedPlan plan = packed_plan(m, sh, sm_count(dev));
-  const size_t need = plan.sem_bytes + plan.part_bytes;
-  if (need > 0 && (workspace == nullptr || workspace_bytes < need))
-    return fail(LVB_ERR_WORKSPACE, "AWQ workspace of %zu bytes is below the %zu required", workspace_bytes, need);
+  // The plan never needs more split-K workspace than the caller passed.
+  const PackedPlan plan = packed_plan(m, sh, sm_count(dev), workspace != nullptr ? workspace_bytes : 0);
   uint8_t *ws = static_cast<uint8_t *>(workspace);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const uint8_t *c = static_cast<const uint8_t *>(codes);
   const uint32_t *g = static_cast<const uint32_t *>(groups);
   switch (plan.bn) {
-    case 16: return launch_awq_packed<16>(plan, sh, x, c, g, bias, y, m, k, n, group_size, ws, dev, s);
-    case 32: return launch_awq_packed<32>(plan, sh, x, c, g, bias, y, m, k, n, group_size, ws, dev, s);
-    default: return launch_awq_packed<64>(plan, sh, x, c, g, bias, y, m, k, n, group_size, ws, dev, s);
+    case 16: return launch_awq_packed<16, 4, 2, true>(plan, sh, x, c, g, bias, y, m, k, n, group_size, ws, dev, s);
+    case 32: return launch_awq_packed<32, 4, 2, true>(plan, sh, x, c, g, bias, y, m, k, n, group_size, ws, dev, s);
+    case 64: return launch_awq_packed<64, 4, 2, true>(plan, sh, x, c, g, bias, y, m, k, n, group_size, ws, dev, s);
+    case 128: return launch_awq_packed<128, 2, 2, true>(plan, sh, x, c, g, bias, y, m, k, n, group_size, ws, dev, s);
+    default: return launch_awq_packed<256, 1, 1, false>(plan, sh, x, c, g, bias, y, m, k, n, group_size, ws, dev, s);
   }
 }
 

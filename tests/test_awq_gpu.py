@@ -170,15 +170,54 @@ def test_packed_decode_shapes(m, k, n, g):
     _check_against_oracle(m, k, n, g, seed=m * 31 + n)
 
 
-def test_packed_entry_rejects_large_batches():
+@pytest.mark.parametrize("m,k,n", [(100, 512, 1024), (300, 640, 768), (2048, 1024, 1280)])
+def test_packed_entry_prefill_sizes(m, k, n):
+    """lvb_awq_linear_packed on 128- and 256-row tiles (several m tiles)."""
+
     from light_vllm_b200.awq import pack_awq_decode_layout
 
-    qweight, qzeros, scales = oawq.random_checkpoint(256, 512, 128, seed=9)
+    g = 128
+    qweight, qzeros, scales = oawq.random_checkpoint(k, n, g, seed=m + n)
+    rng = np.random.default_rng(m)
+    x = rng.standard_normal((m, k)).astype(np.float16)
+    bias = rng.standard_normal(n).astype(np.float16)
+    expected = oawq.linear_fp32(x, qweight, qzeros, scales, g, bias)
+    qw, qz, sc, xg, bg = _gpu(qweight, qzeros, scales, x, bias)
+    codes, groups = pack_awq_decode_layout(qw, qz, sc, g)
+    lib = _native.library()
+    ws = torch.zeros(max(int(lib.lvb_awq_workspace_bytes(m, k, n, g)), 256), dtype=torch.uint8, device=DEV)
+    y = torch.empty(m, n, dtype=torch.float16, device=DEV)
+    _native.check(lib.lvb_awq_linear_packed(xg.data_ptr(), codes.data_ptr(), groups.data_ptr(), bg.data_ptr(),
+                                            y.data_ptr(), m, k, n, g, ws.data_ptr(), ws.numel(),
+                                            torch.cuda.current_stream().cuda_stream), "lvb_awq_linear_packed")
+    torch.cuda.synchronize()
+    assert _native.device_error() == 0
+    max_abs, rel = oawq.error_metrics(y.float().cpu().numpy(), expected)
+    assert max_abs <= MAX_ABS and rel <= REL_L2, (max_abs, rel)
+
+
+def test_prepare_repacks_in_place_once():
+    """prepare() replaces qweight's contents with the packed codes (no second
+    resident copy); preparing the same storage again reuses that packing."""
+
+    k, n, g = 512, 1024, 128
+    qweight, qzeros, scales = oawq.random_checkpoint(k, n, g, seed=4)
+    expected_codes, _ = oawq.pack_decode_layout(qweight, qzeros, scales, g)
     qw, qz, sc = _gpu(qweight, qzeros, scales)
-    codes, groups = pack_awq_decode_layout(qw, qz, sc, 128)
-    x = torch.zeros(65, 256, dtype=torch.float16, device=DEV)
-    y = torch.empty(65, 512, dtype=torch.float16, device=DEV)
-    status = _native.library().lvb_awq_linear_packed(x.data_ptr(), codes.data_ptr(), groups.data_ptr(), None,
-                                                     y.data_ptr(), 65, 256, 512, 128, None, 0,
-                                                     torch.cuda.current_stream().cuda_stream)
-    assert status == _native.LVB_ERR_UNSUPPORTED
+    x = torch.randn(5, k, dtype=torch.float16, device=DEV)
+    op1 = B200AWQScheme().prepare(qw, qz, sc, g, None)
+    y1 = op1(x)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(qw.cpu().numpy().view(np.uint8).reshape(-1), expected_codes.reshape(-1))
+    assert op1.codes.data_ptr() == qw.data_ptr()
+    op2 = B200AWQScheme().prepare(qw, qz, sc, g, None)
+    assert torch.equal(op2(x), y1)
+    np.testing.assert_array_equal(qw.cpu().numpy().view(np.uint8).reshape(-1), expected_codes.reshape(-1))
+
+
+def test_ragged_shapes_keep_the_checkpoint_layout():
+    qweight, qzeros, scales = oawq.random_checkpoint(96, 256, 32, seed=2)
+    qw, qz, sc = _gpu(qweight, qzeros, scales)
+    op = B200AWQScheme().prepare(qw, qz, sc, 32, None)
+    assert op.codes is None
+    np.testing.assert_array_equal(qw.cpu().numpy(), qweight)
