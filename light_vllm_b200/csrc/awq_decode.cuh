@@ -129,6 +129,41 @@ __device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, ui
       : "memory");
 }
 
+// The four MMAs of one 64-k block in one asm statement (no instructions
+// between them): runs c = 0, 1 of the block, each as its lower 16 k into D_lo
+// and its upper 16 k into D_hi (DUAL) or D_lo.  `acc_first` = 0 starts the
+// accumulators on the block's first MMAs.
+template <bool DUAL>
+__device__ __forceinline__ void umma_ts_block(uint32_t d_lo, uint32_t d_hi, uint32_t a, uint64_t b0, uint64_t b1,
+                                              uint64_t b2, uint64_t b3, uint32_t idesc, uint32_t acc_first) {
+  const uint32_t a1 = a + 8, a2 = a + 16, a3 = a + 24;
+  if constexpr (DUAL) {
+    asm volatile(
+        "{\n\t.reg .pred pf, pt;\n\t"
+        "setp.ne.b32 pf, %8, 0;\n\t"
+        "setp.eq.b32 pt, %8, %8;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%2], %4, %9, pf;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%1], [%3], %5, %9, pf;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%10], %6, %9, pt;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%1], [%11], %7, %9, pt;\n\t}" ::"r"(d_lo),
+        "r"(d_hi), "r"(a), "r"(a1), "l"(b0), "l"(b1), "l"(b2), "l"(b3), "r"(acc_first), "r"(idesc), "r"(a2),
+        "r"(a3)
+        : "memory");
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred pf, pt;\n\t"
+        "setp.ne.b32 pf, %8, 0;\n\t"
+        "setp.eq.b32 pt, %8, %8;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%2], %4, %9, pf;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%3], %5, %9, pt;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%10], %6, %9, pt;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%11], %7, %9, pt;\n\t}" ::"r"(d_lo),
+        "r"(d_hi), "r"(a), "r"(a1), "l"(b0), "l"(b1), "l"(b2), "l"(b3), "r"(acc_first), "r"(idesc), "r"(a2),
+        "r"(a3)
+        : "memory");
+  }
+}
+
 // K-major SWIZZLE_64B operand: rows of 64 bytes, 8-row groups 512 bytes apart.
 __device__ __forceinline__ uint64_t umma_desc_kmajor_sw64(uint32_t saddr) {
   uint64_t d = 0;
@@ -307,24 +342,32 @@ __global__ void __launch_bounds__(PackedConfig<BN, SB, DG, DUAL>::kThreads, 1)
         const int slot = ls % C::kStages;
         if (!mbar_wait(&full[slot], (ls / C::kStages) & 1, abort_flag)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t x_base = smem_u32(smem + slot * C::kStageBytes + C::kXOff);
         const int nb = min(SB, nblocks - ls * SB);
         const int as = ls % kAStages;
+        // Descriptors and addresses of the whole stage are formed before the
+        // MMAs: tcgen05.mma holds the issuing thread until the pipe accepts it,
+        // so any arithmetic between two MMAs shows up as a gap in the pipe.
+        // The start-address field of a descriptor (bits 0..13, address / 16)
+        // does not overflow for shared-memory offsets, so descriptors of the
+        // stage's tiles differ from the first by (offset / 16).
+        const uint64_t bdesc0 = umma_desc_kmajor_sw64(smem_u32(smem + slot * C::kStageBytes + C::kXOff));
+        const uint32_t a0 = tmem + C::kACol + as * C::kAStageCols;
+        const uint32_t acc0 = ls == 0 ? 0u : 1u;
+        // Descriptors of the stage's four B sub-tiles per block: (run c, half h)
+        // at (2 b + c) * kXChunkBytes + 32 h.
+        uint64_t bd[SB][4];
+#pragma unroll
+        for (int b = 0; b < SB; ++b)
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            bd[b][i] = bdesc0 + static_cast<uint64_t>(((2 * b + (i >> 1)) * C::kXChunkBytes + (i & 1) * 32) >> 4);
         if (!mbar_wait(&a_full[as], (ls / kAStages) & 1, abort_flag)) { ok = false; break; }
         tc_fence_after();
-        for (int b = 0; b < nb; ++b) {
-          const uint32_t a_blk = tmem + C::kACol + as * C::kAStageCols + b * 32;
 #pragma unroll
-          for (int c = 0; c < 2; ++c) {
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              const uint64_t bdesc =
-                  umma_desc_kmajor_sw64(x_base + (2 * b + c) * C::kXChunkBytes + h * 32);
-              const uint32_t d_addr = tmem + ((DUAL && h) ? C::kDHiCol : 0);
-              const bool first = (ls | b | c) == 0 && (DUAL || h == 0);
-              umma_f16_ts(d_addr, a_blk + c * 16 + h * 8, bdesc, idesc, first ? 0u : 1u);
-            }
-          }
+        for (int b = 0; b < SB; ++b) {
+          if (b < nb)
+            umma_ts_block<DUAL>(tmem, tmem + C::kDHiCol, a0 + b * 32, bd[b][0], bd[b][1], bd[b][2], bd[b][3], idesc,
+                                b == 0 ? acc0 : 1u);
         }
         umma_commit(&a_empty[as]);
         umma_commit(&empty[slot]);

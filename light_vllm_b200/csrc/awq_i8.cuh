@@ -1,0 +1,490 @@
+// AutoAWQ W4A16 linear for decode batches (m <= 32) on the int8 tensor-core
+// path: twice the weights per tcgen05.mma of the fp16 path.
+//
+// y[t, n] = sum_k x[t, k] * (q[k, n] - z[g, n]) * s[g, n]   (g = k / G)
+//         = sum_g s[g, n] * (sum_{k in g} q x  -  z[g, n] * sum_{k in g} x).
+//
+// A tcgen05.mma with M = 128 occupies the tensor pipe for a fixed ~70 cycles
+// at small N whatever its kind; with kind::f16 it retires 128 x 16 weights,
+// with kind::i8 128 x 32.  So here the weight operand is the raw int4 code q
+// as an int8 (exact), written into tensor memory by the dequantisers with two
+// logic operations per 8 codes, and the activations enter as int8 "limbs":
+// per (token, group) a power-of-two scale a with |x / a| <= 127, and
+//     x / a = x0 + x1 / 128,  x0 = rint(x / a) in [-127, 127],
+//                             x1 = rint(128 (x / a - x0)) in [-64, 64],
+// i.e. 15 significant bits relative to the group's largest element (the fp16
+// input has 11).  The MMA accumulates, exactly in int32, D0 = sum q x0 and
+// D1 = sum q x1 over one group; the drain warps then form, still exactly in
+// integers,  v = 128 D0 + D1 - z * sum_k (128 x0 + x1)  and add
+// s * (a / 128) * v to an fp32 accumulator.  The only roundings are the limb
+// quantisation of x and the fp32 conversion/accumulation; the zero point and
+// the scale are applied exactly (the reference rounds W to fp16 instead,
+// modeling/quantization/awq.py:433-450).
+//
+// Kernels:
+//   awq_act_limbs_kernel  one warp per (group, token row): the limbs of x, in
+//                         the K-major 64-byte-swizzled tile layout the MMA
+//                         reads (pre-swizzled, so a stage is one bulk copy),
+//                         and per (group, token) the scale a / 128 and the
+//                         integer sum of 128 x0 + x1.
+//   awq_i8_kernel<BN>     one CTA per (128-column tile, K split):
+//     warp 0      bulk copies of the packed codes (16 KB per 256-k stage)
+//     warp 1      bulk copies of the limb tiles (2 BN rows x 256 k)
+//     warp 2      TMEM allocation and the tcgen05.mma.kind::i8 issuer of
+//                 even stages; warp 11 issues the odd stages
+//     warps 3..6  code expanders: q nibbles -> int8 A columns in TMEM
+//     warps 7..10 drain: per group, int32 D -> fp32 accumulators; epilogue
+// The codes use the packed layout of awq_decode.cuh.  Within a 32-k run, word
+// w masked with 0x0F0F0F0F gives the bytes of k = 4w, 4w+2, 4w+1, 4w+3, and
+// the word shifted right by 4 those of k = 16+4w, 16+4w+2, 16+4w+1, 16+4w+3;
+// the limb tiles store x in the same k order, so A and B agree without any
+// byte shuffling.
+#pragma once
+
+#include "awq_decode.cuh"
+#include "lvb_common.cuh"
+
+namespace lvb {
+namespace awqi8 {
+
+using awqd::kChunkBytes;
+using awqd::kTileN;
+
+constexpr int kStageBlocks = 4;                       // 64-k blocks per stage
+constexpr int kStageChunks = 2 * kStageBlocks;        // 32-k runs per stage
+constexpr int kQStageBytes = kStageChunks * kChunkBytes;  // 16 KB of codes
+constexpr int kStages = 4;                            // stages in flight (shared memory and TMEM A)
+constexpr int kAStageCols = kStageBlocks * 16;        // 16 columns (64 int8) per block
+constexpr int kDStages = 2;                           // stage accumulators in flight
+constexpr int kExpandWarp = 3;                        // first code-expander warp
+constexpr int kDrainWarp = 7;                         // first drain warp
+constexpr int kIssuer2Warp = 11;                      // second MMA issuer (odd stages)
+constexpr int kThreads = 12 * 32;
+constexpr int kTmemCols = 512;
+
+// Groups of 128 or 256 k: a 256-k stage holds two groups or one, and the
+// MMA issuer, code expanders and drain synchronise once per stage.
+template <int BN>
+struct I8Config {
+  static constexpr int kLimbRows = 2 * BN;                   // (limb, token) rows of B
+  static constexpr int kLimbChunkBytes = kLimbRows * 64;     // one 64-k chunk of the limb tile
+  static constexpr int kLimbStageBytes = kStageBlocks * kLimbChunkBytes;
+  static constexpr int kQOff = kLimbStageBytes;              // limb tile first (1024-aligned)
+  static constexpr int kStageBytes = ((kQOff + kQStageBytes) + 1023) / 1024 * 1024;
+  static constexpr int kGroupCols = kLimbRows;               // int32 accumulator columns per group
+  static constexpr int kDStageCols = 2 * kGroupCols;         // up to two groups per stage
+  static constexpr int kACol = kDStages * kDStageCols;
+  static constexpr int kBarOff = kStages * kStageBytes;
+  // full, done, a_full (stages), d_full, d_empty (stage accumulators), fin (per issuer).
+  static constexpr int kNumBars = 3 * kStages + 2 * kDStages + 2;
+  static constexpr int kMiscOff = kBarOff + kNumBars * 8;
+  // Per drain warp, two stage slots of per-token scalars (2 groups x BN x 8 bytes).
+  static constexpr int kScalOff = (kMiscOff + 64 + 15) / 16 * 16;
+  static constexpr int kScalSlotBytes = 2 * BN * 8;
+  static constexpr int kScalBytes = 4 * 2 * kScalSlotBytes;
+  static constexpr int kSmemBytes = kScalOff + kScalBytes + 1024;
+  static_assert(BN == 16 || BN == 32, "int8 path covers 16- and 32-row token tiles");
+  static_assert(kACol + kStages * kAStageCols <= kTmemCols, "tensor memory budget");
+  static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
+};
+
+struct I8Params {
+  const uint8_t *qpack;      // packed codes [n_tiles][k_chunks][128][16 B]
+  const uint32_t *szpack;    // [n_tiles][groups][128] (scale bits | zero << 16)
+  const int8_t *limbs;       // [K/64][2 BN][64 B], pre-swizzled
+  const int2 *scal;          // [groups][BN]: (bits of a / 128, sum of 128 x0 + x1)
+  const uint16_t *bias;      // may be null
+  uint16_t *y;
+  uint32_t *semaphores;
+  float *partials;           // [n_tiles][splits][BN][128]
+  int M, K, N, G;
+  int groups, k_chunks, blocks_per_group, bpg_shift;  // blocks per group = 1 << bpg_shift (2 or 4)
+  int n_tiles, splits;
+};
+
+// Byte offset of k within its 64-k chunk row, in the A column order of the
+// code expanders: inside each 4-k quad the order is (0, 2, 1, 3).
+__host__ __device__ __forceinline__ int limb_pos(int k64) {
+  const int e = k64 & 3;
+  return (k64 & ~3) | ((e & 1) << 1) | (e >> 1);
+}
+
+// 64-byte swizzle of a K-major tile: 16-byte chunk c of row r lands at
+// chunk c ^ ((r >> 1) & 3).
+__host__ __device__ __forceinline__ int sw64(int row, int byte) {
+  return row * 64 + ((((byte >> 4) ^ ((row >> 1) & 3)) & 3) << 4) + (byte & 15);
+}
+
+// One warp per (group, token row t < BN); rows t >= M are written as zeros.
+// Each lane handles 4 consecutive k (one quad) per pass and stores the quad's
+// two limbs as one 32-bit word each, bytes in the (0, 2, 1, 3) order.
+template <int BN>
+__global__ void __launch_bounds__(32) awq_act_limbs_kernel(const uint16_t *__restrict__ x, int8_t *__restrict__ limbs,
+                                                           int2 *__restrict__ scal, int M, int K, int G) {
+  const int g = blockIdx.x;
+  const int t = blockIdx.y;
+  const int lane = threadIdx.x;
+  const bool row_ok = t < M;
+  const uint16_t *xrow = x + static_cast<size_t>(row_ok ? t : 0) * K + static_cast<size_t>(g) * G;
+  float amax = 0.f;
+  for (int i = 4 * lane; i < G; i += 128) {
+    const uint2 raw = row_ok ? *reinterpret_cast<const uint2 *>(xrow + i) : make_uint2(0u, 0u);
+    const __half2 h0 = *reinterpret_cast<const __half2 *>(&raw.x);
+    const __half2 h1 = *reinterpret_cast<const __half2 *>(&raw.y);
+    amax = fmaxf(amax, fmaxf(fmaxf(fabsf(__low2float(h0)), fabsf(__high2float(h0))),
+                             fmaxf(fabsf(__low2float(h1)), fabsf(__high2float(h1)))));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  // Smallest power of two a with amax / a <= 127 (a = 1 for an all-zero row).
+  int e = 0;
+  if (amax > 0.f) frexpf(amax / 127.f, &e);
+  const float inv_a = ldexpf(1.f, -e);
+  int isum = 0;
+  for (int i = 4 * lane; i < G; i += 128) {
+    const uint2 raw = row_ok ? *reinterpret_cast<const uint2 *>(xrow + i) : make_uint2(0u, 0u);
+    const __half2 h0 = *reinterpret_cast<const __half2 *>(&raw.x);
+    const __half2 h1 = *reinterpret_cast<const __half2 *>(&raw.y);
+    const float v[4] = {__low2float(h0), __high2float(h0), __low2float(h1), __high2float(h1)};
+    uint32_t w0 = 0, w1 = 0;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float r = v[q] * inv_a;                 // exact: power-of-two scaling of an fp16 value
+      const float x0 = rintf(r);
+      const float x1 = rintf((r - x0) * 128.f);     // r - x0 exact, |r - x0| <= 1/2
+      const int i0 = static_cast<int>(x0), i1 = static_cast<int>(x1);
+      isum += i0 * 128 + i1;
+      const int pos = ((q & 1) << 1) | (q >> 1);    // byte of k-offset q in the quad
+      w0 |= (static_cast<uint32_t>(i0) & 0xFFu) << (8 * pos);
+      w1 |= (static_cast<uint32_t>(i1) & 0xFFu) << (8 * pos);
+    }
+    const int k = g * G + i;
+    int8_t *tile = limbs + static_cast<size_t>(k >> 6) * (2 * BN * 64);
+    *reinterpret_cast<uint32_t *>(tile + sw64(t, k & 63)) = w0;
+    *reinterpret_cast<uint32_t *>(tile + sw64(BN + t, k & 63)) = w1;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) isum += __shfl_xor_sync(0xffffffffu, isum, o);
+  if (lane == 0) scal[static_cast<size_t>(g) * BN + t] = make_int2(__float_as_int(ldexpf(1.f, e - 7)), isum);
+}
+
+// D[tmem] (+)= A[tmem] * B[smem desc]^T, kind::i8 (s8 x s8 -> s32).
+__device__ __forceinline__ void umma_i8_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                           uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Instruction descriptor, kind::i8: signed 8-bit A and B, s32 accumulator.
+__host__ __device__ constexpr uint32_t umma_idesc_i8(int m, int n) {
+  return (2u << 4) |                               // D format: s32
+         (1u << 7) |                               // A: signed 8-bit
+         (1u << 10) |                              // B: signed 8-bit
+         (static_cast<uint32_t>(n >> 3) << 17) |  // N / 8
+         (static_cast<uint32_t>(m >> 4) << 24);   // M / 16
+}
+
+__device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+      "%14, %15, %16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+}
+
+template <int BN>
+__global__ void __launch_bounds__(kThreads, 1) awq_i8_kernel(const I8Params p) {
+  using C = I8Config<BN>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::kBarOff);
+  uint64_t *full = bars;                      // codes and limbs of a stage landed
+  uint64_t *done = full + kStages;            // the stage's MMAs completed (slot and A stage free)
+  uint64_t *a_full = done + kStages;          // the stage's A columns are in tensor memory
+  uint64_t *d_full = a_full + kStages;        // a stage accumulator holds finished groups
+  uint64_t *d_empty = d_full + kDStages;      // the drain has read a stage accumulator
+  uint64_t *fin = d_empty + kDStages;         // [2]: every MMA of each issuer has completed
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + C::kMiscOff);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + C::kMiscOff + 8);
+  volatile int *last_flag = reinterpret_cast<volatile int *>(smem + C::kMiscOff + 16);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int tile = blockIdx.x;
+  const int split = blockIdx.y;
+  // Splits cover whole groups, so every CTA drains complete groups, and its
+  // stages start on a group boundary.
+  const int g_begin = static_cast<int>((static_cast<long long>(split) * p.groups) / p.splits);
+  const int g_end = static_cast<int>((static_cast<long long>(split + 1) * p.groups) / p.splits);
+  const int b_begin = g_begin << p.bpg_shift;
+  const int nblocks = (g_end - g_begin) << p.bpg_shift;
+  const int nstages = (nblocks + kStageBlocks - 1) / kStageBlocks;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 2);
+      mbar_init(&done[s], 1);
+      mbar_init(&a_full[s], 4);
+    }
+    for (int j = 0; j < kDStages; ++j) {
+      mbar_init(&d_full[j], 1);
+      mbar_init(&d_empty[j], 4);
+    }
+    mbar_init(&fin[0], 1);
+    mbar_init(&fin[1], 1);
+    *abort_flag = 0;
+    *last_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 2) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0 || warp == 1) {
+    // ---------------- producers ----------------
+    if (lane == 0) {
+      bool ok = true;
+      int issued = 0;
+      for (int ls = 0; ls < nstages; ++ls) {
+        const int slot = ls % kStages;
+        if (ls >= kStages && !mbar_wait(&done[slot], ((ls / kStages) - 1) & 1, abort_flag)) {
+          ok = false;
+          break;
+        }
+        uint8_t *stage = smem + slot * C::kStageBytes;
+        const int blk0 = b_begin + ls * kStageBlocks;
+        const int nb = min(kStageBlocks, b_begin + nblocks - blk0);
+        if (warp == 0) {
+          const uint32_t bytes = static_cast<uint32_t>(2 * nb * kChunkBytes);
+          mbar_arrive_expect_tx(&full[slot], bytes);
+          awqd::bulk_load(stage + C::kQOff,
+                          p.qpack + (static_cast<size_t>(tile) * p.k_chunks + 2 * blk0) * kChunkBytes, bytes,
+                          &full[slot]);
+        } else {
+          const uint32_t bytes = static_cast<uint32_t>(nb * C::kLimbChunkBytes);
+          mbar_arrive_expect_tx(&full[slot], bytes);
+          awqd::bulk_load(stage, p.limbs + static_cast<size_t>(blk0) * C::kLimbChunkBytes, bytes, &full[slot]);
+        }
+        issued = ls + 1;
+      }
+      if (!ok) {
+        for (int ls = issued > kStages ? issued - kStages : 0; ls < issued; ++ls)
+          mbar_wait(&full[ls % kStages], (ls / kStages) & 1, nullptr, kDrainBudgetCycles);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 2 || warp == kIssuer2Warp) {
+    // ---------------- tcgen05.mma issuers ----------------
+    // Two threads issue alternate stages (stage parity = issuer), each with
+    // one wait set and one commit pair per stage: a stage's waits and
+    // bookkeeping overlap the other issuer's MMAs in the tensor pipe.  Stage
+    // accumulator ds = parity and A stages s = ls % 4 are private to one
+    // issuer, and tcgen05.commit tracks only the issuing thread's MMAs.
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_i8(kTileN, 2 * BN);
+      const int parity = warp == 2 ? 0 : 1;
+      bool ok = true;
+      for (int ls = parity; ls < nstages; ls += 2) {
+        const int s = ls % kStages;
+        const int ds = ls & (kDStages - 1);
+        const int nb = min(kStageBlocks, nblocks - ls * kStageBlocks);
+        const uint64_t bdesc0 = awqd::umma_desc_kmajor_sw64(smem_u32(smem + s * C::kStageBytes));
+        const uint32_t a0 = tmem + C::kACol + s * kAStageCols;
+        const uint32_t d0 = tmem + ds * C::kDStageCols;
+        if (!mbar_wait(&full[s], (ls / kStages) & 1, abort_flag) ||
+            !mbar_wait(&a_full[s], (ls / kStages) & 1, abort_flag) ||
+            (ls >= kDStages && !mbar_wait(&d_empty[ds], ((ls / kDStages) - 1) & 1, abort_flag))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        for (int b = 0; b < nb; ++b) {
+          const uint32_t d = d0 + (b >> p.bpg_shift) * C::kGroupCols;
+          const uint64_t bd = bdesc0 + static_cast<uint64_t>((b * C::kLimbChunkBytes) >> 4);
+          umma_i8_ts(d, a0 + b * 16, bd, idesc, (b & ((1 << p.bpg_shift) - 1)) == 0 ? 0u : 1u);
+          umma_i8_ts(d, a0 + b * 16 + 8, bd + 2, idesc, 1u);  // +32 bytes: the block's second 32-k run
+        }
+        umma_commit(&done[s]);
+        umma_commit(&d_full[ds]);
+      }
+      // Tensor memory is freed only after every issued MMA has completed.
+      umma_commit(&fin[parity]);
+      mbar_wait(&fin[parity], 0, nullptr, ok ? kWaitBudgetCycles : kDrainBudgetCycles);
+    }
+    __syncwarp();
+  } else if (warp < kDrainWarp) {
+    // ---------------- code expanders ----------------
+    // full[s] for stage ls implies done[s] for stage ls - kStages (the
+    // producer waited for it before refilling the slot), so A stage s is free.
+    const int quad = warp & 3;
+    const int col = quad * 32 + lane;
+    const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
+    for (int ls = 0; ls < nstages; ++ls) {
+      const int s = ls % kStages;
+      const int nb = min(kStageBlocks, nblocks - ls * kStageBlocks);
+      if (!__all_sync(0xffffffffu, mbar_wait(&full[s], (ls / kStages) & 1, abort_flag))) break;
+      const uint8_t *stage = smem + s * C::kStageBytes + C::kQOff;
+      uint4 q[kStageChunks];
+#pragma unroll
+      for (int c = 0; c < kStageChunks; ++c)
+        if (c < 2 * nb) q[c] = *reinterpret_cast<const uint4 *>(stage + c * kChunkBytes + col * 16);
+      tc_fence_after();
+#pragma unroll
+      for (int b = 0; b < kStageBlocks; ++b) {
+        if (b < nb) {
+          uint32_t a[16];
+#pragma unroll
+          for (int r = 0; r < 2; ++r) {
+            const uint32_t w[4] = {q[2 * b + r].x, q[2 * b + r].y, q[2 * b + r].z, q[2 * b + r].w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              a[8 * r + j] = w[j] & 0x0F0F0F0Fu;
+              a[8 * r + 4 + j] = (w[j] >> 4) & 0x0F0F0F0Fu;
+            }
+          }
+          tmem_st_32x32b_x16(tmem + lane_base + C::kACol + s * kAStageCols + b * 16, a);
+        }
+      }
+      awqd::tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&a_full[s]);
+    }
+  } else {
+    // ---------------- drain + epilogue ----------------
+    const int quad = warp & 3;
+    const int col = quad * 32 + lane;
+    const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
+    const int n = tile * kTileN + col;
+    const bool n_ok = n < p.N;
+    const int gps_full = kStageBlocks >> p.bpg_shift;  // groups per full stage (2 or 1)
+    float acc[BN];
+#pragma unroll
+    for (int t = 0; t < BN; ++t) acc[t] = 0.f;
+    bool ok = true;
+    const uint32_t *szrow = p.szpack + (static_cast<size_t>(tile) * p.groups) * kTileN + col;
+    // The next stage's (scale, zero) words (registers) and per-token scalars
+    // (cp.async into this warp's shared slots) are fetched one stage ahead.
+    uint8_t *scal_sm = smem + C::kScalOff + (warp - kDrainWarp) * 2 * C::kScalSlotBytes;
+    auto groups_in = [&](int ls) { return min(kStageBlocks, nblocks - ls * kStageBlocks) >> p.bpg_shift; };
+    auto fetch = [&](int ls, uint32_t (&szw)[2]) {
+      const int g0 = g_begin + ls * gps_full;
+      const int ng = groups_in(ls);
+      if (lane < ng * BN / 2)
+        cp_async_16(smem_u32(scal_sm + (ls & 1) * C::kScalSlotBytes + lane * 16),
+                    reinterpret_cast<const uint8_t *>(p.scal + static_cast<size_t>(g0) * BN) + lane * 16, 16u);
+      cp_async_commit();
+      szw[0] = __ldg(szrow + static_cast<size_t>(g0) * kTileN);
+      szw[1] = ng > 1 ? __ldg(szrow + static_cast<size_t>(g0 + 1) * kTileN) : 0u;
+    };
+    uint32_t sz_next[2] = {0u, 0u};
+    if (nstages > 0) fetch(0, sz_next);
+    for (int ls = 0; ls < nstages; ++ls) {
+      const uint32_t sz[2] = {sz_next[0], sz_next[1]};
+      const int ng = groups_in(ls);
+      cp_async_wait_all();
+      __syncwarp();
+      if (ls + 1 < nstages) fetch(ls + 1, sz_next);
+      const int4 *sc = reinterpret_cast<const int4 *>(scal_sm + (ls & 1) * C::kScalSlotBytes);
+      const int ds = ls & (kDStages - 1);
+      if (!__all_sync(0xffffffffu, mbar_wait(&d_full[ds], (ls / kDStages) & 1, abort_flag))) { ok = false; break; }
+      tc_fence_after();
+      for (int j = 0; j < ng; ++j) {
+        const float s = __half2float(__ushort_as_half(static_cast<uint16_t>(sz[j] & 0xFFFFu)));
+        const int z = static_cast<int>(sz[j] >> 16);
+        const uint32_t dcol = tmem + lane_base + ds * C::kDStageCols + j * C::kGroupCols;
+#pragma unroll
+        for (int h = 0; h < BN / 16; ++h) {
+          uint32_t d0[16], d1[16];
+          tmem_ld_32x32b_x16(dcol + h * 16, d0);
+          tmem_ld_32x32b_x16(dcol + BN + h * 16, d1);
+          tmem_wait_ld();
+#pragma unroll
+          for (int t = 0; t < 16; t += 2) {
+            const int4 two = sc[(j * BN + h * 16 + t) / 2];
+            const int v0 = static_cast<int>(d0[t]) * 128 + static_cast<int>(d1[t]) - z * two.y;
+            const int v1 = static_cast<int>(d0[t + 1]) * 128 + static_cast<int>(d1[t + 1]) - z * two.w;
+            acc[h * 16 + t] = fmaf(s * __int_as_float(two.x), static_cast<float>(v0), acc[h * 16 + t]);
+            acc[h * 16 + t + 1] = fmaf(s * __int_as_float(two.z), static_cast<float>(v1), acc[h * 16 + t + 1]);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&d_empty[ds]);
+    }
+    cp_async_wait_all();
+    ok = __all_sync(0xffffffffu, ok) && nstages > 0 && !*abort_flag;
+    const float bias_n = (p.bias != nullptr && n_ok) ? __half2float(__ushort_as_half(p.bias[n])) : 0.f;
+    if (p.splits == 1) {
+      if (ok && n_ok) {
+#pragma unroll
+        for (int t = 0; t < BN; ++t)
+          if (t < p.M) p.y[static_cast<size_t>(t) * p.N + n] = __half_as_ushort(__float2half_rn(acc[t] + bias_n));
+      }
+    } else {
+      float *part = p.partials + static_cast<size_t>(tile) * p.splits * BN * kTileN;
+      if (ok) {
+#pragma unroll
+        for (int t = 0; t < BN; ++t) __stcg(part + (static_cast<size_t>(split) * BN + t) * kTileN + col, acc[t]);
+      }
+      __threadfence();
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (warp == kDrainWarp && lane == 0) {
+        const unsigned int prev = ok ? atomicAdd(p.semaphores + tile, 1u) : 0u;
+        *last_flag = (ok && prev == static_cast<unsigned int>(p.splits - 1)) ? 1 : 0;
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (*last_flag) {
+        __threadfence();
+        float sum[BN];
+#pragma unroll
+        for (int t = 0; t < BN; ++t) sum[t] = 0.f;
+        for (int sp = 0; sp < p.splits; ++sp) {
+          float v[BN];
+#pragma unroll
+          for (int t = 0; t < BN; ++t) v[t] = __ldcg(part + (static_cast<size_t>(sp) * BN + t) * kTileN + col);
+#pragma unroll
+          for (int t = 0; t < BN; ++t) sum[t] += v[t];
+        }
+        if (n_ok) {
+#pragma unroll
+          for (int t = 0; t < BN; ++t)
+            if (t < p.M) p.y[static_cast<size_t>(t) * p.N + n] = __half_as_ushort(__float2half_rn(sum[t] + bias_n));
+        }
+        if (warp == kDrainWarp && lane == 0) p.semaphores[tile] = 0u;
+      }
+    }
+    tc_fence_before();
+  }
+
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+}  // namespace awqi8
+}  // namespace lvb

@@ -17,6 +17,7 @@
 #include "../../include/lvb200.h"
 #include "awq_gemm.cuh"
 #include "awq_decode.cuh"
+#include "awq_i8.cuh"
 #include "lvb_common.cuh"
 #include "paged_attention.cuh"
 #include "step_metadata.cuh"
@@ -276,6 +277,89 @@ int launch_awq_packed(const PackedPlan &plan, const PackedShape &sh, const uint1
   return LVB_OK;
 }
 
+// int8 tensor-core path for decode batches: m <= 32, groups of 128 or 256 k
+// (one or two whole groups per 256-k stage).
+bool i8_eligible(int64_t m, int64_t k, int64_t n, int64_t g) {
+  return m <= 32 && (g == 128 || g == 256) && k % g == 0 && n % 128 == 0;
+}
+
+struct I8Plan {
+  int bn = 0, splits = 1;
+  size_t sem_bytes = 0, part_bytes = 0, limb_bytes = 0, scal_bytes = 0;
+  size_t total() const { return sem_bytes + part_bytes + limb_bytes + scal_bytes; }
+};
+
+size_t round256(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
+
+// bn == 0 when the activation limbs do not fit in `max_ws`.  Splits cover
+// whole groups; same cost model as the packed path.
+I8Plan i8_plan(int64_t m, int64_t k, const PackedShape &sh, int64_t g, int sms, size_t max_ws = SIZE_MAX) {
+  I8Plan p;
+  const int bn = m <= 16 ? 16 : 32;
+  p.limb_bytes = round256(static_cast<size_t>(k) * 2 * bn);
+  p.scal_bytes = round256(static_cast<size_t>(sh.groups) * bn * 8);
+  if (p.limb_bytes + p.scal_bytes > max_ws) return p;
+  p.bn = bn;
+  const int bpg = static_cast<int>(g / 64);
+  const size_t sem = round256(static_cast<size_t>(sh.n_tiles) * 4);
+  long long best_cost = -1;
+  const int max_splits = sh.groups < 16 ? sh.groups : 16;
+  for (int sp = 1; sp <= max_splits; ++sp) {
+    const size_t part = sp > 1 ? static_cast<size_t>(sh.n_tiles) * sp * bn * lvb::awqi8::kTileN * sizeof(float) : 0;
+    if ((sp > 1 ? sem : 0) + part + p.limb_bytes + p.scal_bytes > max_ws) continue;
+    const long long ctas = static_cast<long long>(sh.n_tiles) * sp;
+    const long long waves = (ctas + sms - 1) / sms;
+    const long long cost = waves * ((sh.groups + sp - 1) / sp) * bpg;
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
+      p.splits = sp;
+      p.sem_bytes = sp > 1 ? sem : 0;
+      p.part_bytes = part;
+    }
+  }
+  return p;
+}
+
+template <int BN>
+int launch_awq_i8(const I8Plan &plan, const PackedShape &sh, const uint16_t *x, const uint8_t *codes,
+                  const uint32_t *groups, const uint16_t *bias, uint16_t *y, int64_t m, int64_t k, int64_t n,
+                  int64_t g, uint8_t *ws, int dev, cudaStream_t stream) {
+  using C = lvb::awqi8::I8Config<BN>;
+  static bool smem_done[kMaxDevices] = {false};
+  auto kernel = lvb::awqi8::awq_i8_kernel<BN>;
+  int rc = ensure_smem(kernel, C::kSmemBytes, dev, smem_done);
+  if (rc != LVB_OK) return rc;
+  int8_t *limbs = reinterpret_cast<int8_t *>(ws + plan.sem_bytes + plan.part_bytes);
+  int2 *scal = reinterpret_cast<int2 *>(ws + plan.sem_bytes + plan.part_bytes + plan.limb_bytes);
+  lvb::awqi8::awq_act_limbs_kernel<BN><<<dim3(sh.groups, BN), 32, 0, stream>>>(
+      x, limbs, scal, static_cast<int>(m), static_cast<int>(k), static_cast<int>(g));
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "awq_act_limbs_kernel launch");
+  lvb::awqi8::I8Params p{};
+  p.qpack = codes;
+  p.szpack = groups;
+  p.limbs = limbs;
+  p.scal = scal;
+  p.bias = bias;
+  p.y = y;
+  p.semaphores = reinterpret_cast<uint32_t *>(ws);
+  p.partials = plan.splits > 1 ? reinterpret_cast<float *>(ws + plan.sem_bytes) : nullptr;
+  p.M = static_cast<int>(m);
+  p.K = static_cast<int>(k);
+  p.N = static_cast<int>(n);
+  p.G = static_cast<int>(g);
+  p.groups = sh.groups;
+  p.k_chunks = sh.k_chunks;
+  p.blocks_per_group = static_cast<int>(g / 64);
+  p.bpg_shift = g == 128 ? 1 : 2;
+  p.n_tiles = sh.n_tiles;
+  p.splits = plan.splits;
+  kernel<<<dim3(sh.n_tiles, plan.splits), lvb::awqi8::kThreads, C::kSmemBytes, stream>>>(p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "awq_i8_kernel launch");
+  return LVB_OK;
+}
+
 int check_awq_shape(int64_t m, int64_t k, int64_t n, int64_t group_size) {
   if (m < 0 || k <= 0 || n <= 0)
     return fail(LVB_ERR_INVALID, "invalid AWQ shape m=%lld k=%lld n=%lld", (long long)m, (long long)k, (long long)n);
@@ -428,8 +512,13 @@ size_t lvb_awq_workspace_bytes(int64_t m, int64_t k, int64_t n, int64_t group_si
   const AwqPlan p = awq_plan(m, k, n, sm_count(dev));
   size_t need = p.sem_bytes + p.part_bytes;
   if (group_size > 0 && group_size % 32 == 0 && k % group_size == 0) {
-    const PackedPlan pp = packed_plan(m, packed_shape(k, n, group_size), sm_count(dev));
+    const PackedShape sh = packed_shape(k, n, group_size);
+    const PackedPlan pp = packed_plan(m, sh, sm_count(dev));
     if (pp.sem_bytes + pp.part_bytes > need) need = pp.sem_bytes + pp.part_bytes;
+    if (i8_eligible(m, k, n, group_size)) {
+      const I8Plan ip = i8_plan(m, k, sh, group_size, sm_count(dev));
+      if (ip.total() > need) need = ip.total();
+    }
   }
   return need;
 }
@@ -533,8 +622,18 @@ int lvb_awq_linear_packed(const uint16_t *x, const void *codes, const void *grou
   rc = current_device(&dev);
   if (rc != LVB_OK) return rc;
   const PackedShape sh = packed_shape(k, n, group_size);
+  const size_t max_ws = workspace != nullptr ? workspace_bytes : 0;
+  cudaStream_t stream_ = reinterpret_cast<cudaStream_t>(stream);
+  if (i8_eligible(m, k, n, group_size)) {
+    const I8Plan ip = i8_plan(m, k, sh, group_size, sm_count(dev), max_ws);
+    const uint8_t *c8 = static_cast<const uint8_t *>(codes);
+    const uint32_t *g8 = static_cast<const uint32_t *>(groups);
+    uint8_t *w8 = static_cast<uint8_t *>(workspace);
+    if (ip.bn == 16) return launch_awq_i8<16>(ip, sh, x, c8, g8, bias, y, m, k, n, group_size, w8, dev, stream_);
+    if (ip.bn == 32) return launch_awq_i8<32>(ip, sh, x, c8, g8, bias, y, m, k, n, group_size, w8, dev, stream_);
+  }
   // The plan never needs more split-K workspace than the caller passed.
-  const PackedPlan plan = packed_plan(m, sh, sm_count(dev), workspace != nullptr ? workspace_bytes : 0);
+  const PackedPlan plan = packed_plan(m, sh, sm_count(dev), max_ws);
   uint8_t *ws = static_cast<uint8_t *>(workspace);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const uint8_t *c = static_cast<const uint8_t *>(codes);

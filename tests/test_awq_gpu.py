@@ -221,3 +221,28 @@ def test_ragged_shapes_keep_the_checkpoint_layout():
     op = B200AWQScheme().prepare(qw, qz, sc, 32, None)
     assert op.codes is None
     np.testing.assert_array_equal(qw.cpu().numpy(), qweight)
+
+
+@pytest.mark.parametrize("m", [1, 16, 32])
+def test_int8_path_with_activation_outliers(m):
+    """Decode batches (m <= 32, group % 64 == 0) run the int8 tensor-core path,
+    which splits each (token, group) of x into two int8 limbs under a
+    power-of-two scale: rows whose groups mix outliers 300x the typical value
+    keep the north-star tolerance (relative to the output scale)."""
+
+    k, n, g = 3584, 512, 128
+    qweight, qzeros, scales = oawq.random_checkpoint(k, n, g, seed=m + 77)
+    rng = np.random.default_rng(m + 5)
+    x = rng.standard_normal((m, k))
+    outliers = rng.random((m, k)) < 0.01
+    x[outliers] *= 300.0
+    x = x.astype(np.float16)
+    expected = oawq.linear_fp32(x, qweight, qzeros, scales, g, None)
+    qw, qz, sc, xg = _gpu(qweight, qzeros, scales, x)
+    op = B200AWQScheme().prepare(qw, qz, sc, g, None)
+    y = op(xg)
+    torch.cuda.synchronize()
+    assert _native.device_error() == 0
+    max_abs, rel = oawq.error_metrics(y.float().cpu().numpy(), expected)
+    scale = float(np.max(np.abs(expected)))
+    assert rel <= REL_L2 and max_abs <= MAX_ABS * max(1.0, scale / 8.0), (m, max_abs, rel, scale)
