@@ -27,7 +27,10 @@
 //                         reads (pre-swizzled, so a stage is one bulk copy),
 //                         and per (group, token) the scale a / 128 and the
 //                         integer sum of 128 x0 + x1.
-//   awq_i8_kernel<BN>     one CTA per (128-column tile, K split):
+//   awq_i8_kernel<BN>     persistent, one CTA per SM over (128-column tile,
+//                         K split) units; launched as a programmatic
+//                         dependent of the limb kernel so that its set-up and
+//                         code streaming overlap it:
 //     warp 0      bulk copies of the packed codes (16 KB per 256-k stage)
 //     warp 1      bulk copies of the limb tiles (2 BN rows x 256 k)
 //     warp 2      TMEM allocation and the tcgen05.mma.kind::i8 issuer of
@@ -121,6 +124,9 @@ __host__ __device__ __forceinline__ int sw64(int row, int byte) {
 template <int BN>
 __global__ void __launch_bounds__(32) awq_act_limbs_kernel(const uint16_t *__restrict__ x, int8_t *__restrict__ limbs,
                                                            int2 *__restrict__ scal, int M, int K, int G) {
+  // The AWQ kernel that reads these limbs may start now and overlap this
+  // grid; it waits for its completion before touching the outputs.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int g = blockIdx.x;
   const int t = blockIdx.y;
   const int lane = threadIdx.x;
@@ -207,6 +213,29 @@ __device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)
       : "memory");
 }
 
+// One (column tile, K split) work unit of a persistent CTA: its groups,
+// blocks and 256-k stages.
+struct Unit {
+  int tile, split, g_begin, b_begin, nblocks, nstages;
+};
+
+__device__ __forceinline__ Unit unit_of(int u, const I8Params &p) {
+  Unit w;
+  w.tile = u / p.splits;
+  w.split = u - w.tile * p.splits;
+  // Splits cover whole groups, so every unit drains complete groups and its
+  // stages start on a group boundary.
+  w.g_begin = static_cast<int>((static_cast<long long>(w.split) * p.groups) / p.splits);
+  const int g_end = static_cast<int>((static_cast<long long>(w.split + 1) * p.groups) / p.splits);
+  w.b_begin = w.g_begin << p.bpg_shift;
+  w.nblocks = (g_end - w.g_begin) << p.bpg_shift;
+  w.nstages = (w.nblocks + kStageBlocks - 1) / kStageBlocks;
+  return w;
+}
+
+// Persistent: CTA c runs units c, c + gridDim.x, ...; every role walks the
+// same sequence of stages, numbered gs across units for the rings' slots and
+// phases, so the pipeline does not drain between units.
 template <int BN>
 __global__ void __launch_bounds__(kThreads, 1) awq_i8_kernel(const I8Params p) {
   using C = I8Config<BN>;
@@ -226,15 +255,7 @@ __global__ void __launch_bounds__(kThreads, 1) awq_i8_kernel(const I8Params p) {
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int tile = blockIdx.x;
-  const int split = blockIdx.y;
-  // Splits cover whole groups, so every CTA drains complete groups, and its
-  // stages start on a group boundary.
-  const int g_begin = static_cast<int>((static_cast<long long>(split) * p.groups) / p.splits);
-  const int g_end = static_cast<int>((static_cast<long long>(split + 1) * p.groups) / p.splits);
-  const int b_begin = g_begin << p.bpg_shift;
-  const int nblocks = (g_end - g_begin) << p.bpg_shift;
-  const int nstages = (nblocks + kStageBlocks - 1) / kStageBlocks;
+  const int units = p.n_tiles * p.splits;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -264,33 +285,39 @@ __global__ void __launch_bounds__(kThreads, 1) awq_i8_kernel(const I8Params p) {
   if (warp == 0 || warp == 1) {
     // ---------------- producers ----------------
     if (lane == 0) {
+      // The activation limbs come from the preceding prologue launch, which
+      // this grid may overlap (programmatic dependent launch): wait for it
+      // before the first limb copy.  The codes do not depend on it.
+      if (warp == 1) asm volatile("griddepcontrol.wait;" ::: "memory");
       bool ok = true;
-      int issued = 0;
-      for (int ls = 0; ls < nstages; ++ls) {
-        const int slot = ls % kStages;
-        if (ls >= kStages && !mbar_wait(&done[slot], ((ls / kStages) - 1) & 1, abort_flag)) {
-          ok = false;
-          break;
+      int gs = 0;
+      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+        const Unit w = unit_of(u, p);
+        for (int ls = 0; ls < w.nstages; ++ls, ++gs) {
+          const int slot = gs % kStages;
+          if (gs >= kStages && !mbar_wait(&done[slot], ((gs / kStages) - 1) & 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          uint8_t *stage = smem + slot * C::kStageBytes;
+          const int blk0 = w.b_begin + ls * kStageBlocks;
+          const int nb = min(kStageBlocks, w.b_begin + w.nblocks - blk0);
+          if (warp == 0) {
+            const uint32_t bytes = static_cast<uint32_t>(2 * nb * kChunkBytes);
+            mbar_arrive_expect_tx(&full[slot], bytes);
+            awqd::bulk_load(stage + C::kQOff,
+                            p.qpack + (static_cast<size_t>(w.tile) * p.k_chunks + 2 * blk0) * kChunkBytes, bytes,
+                            &full[slot]);
+          } else {
+            const uint32_t bytes = static_cast<uint32_t>(nb * C::kLimbChunkBytes);
+            mbar_arrive_expect_tx(&full[slot], bytes);
+            awqd::bulk_load(stage, p.limbs + static_cast<size_t>(blk0) * C::kLimbChunkBytes, bytes, &full[slot]);
+          }
         }
-        uint8_t *stage = smem + slot * C::kStageBytes;
-        const int blk0 = b_begin + ls * kStageBlocks;
-        const int nb = min(kStageBlocks, b_begin + nblocks - blk0);
-        if (warp == 0) {
-          const uint32_t bytes = static_cast<uint32_t>(2 * nb * kChunkBytes);
-          mbar_arrive_expect_tx(&full[slot], bytes);
-          awqd::bulk_load(stage + C::kQOff,
-                          p.qpack + (static_cast<size_t>(tile) * p.k_chunks + 2 * blk0) * kChunkBytes, bytes,
-                          &full[slot]);
-        } else {
-          const uint32_t bytes = static_cast<uint32_t>(nb * C::kLimbChunkBytes);
-          mbar_arrive_expect_tx(&full[slot], bytes);
-          awqd::bulk_load(stage, p.limbs + static_cast<size_t>(blk0) * C::kLimbChunkBytes, bytes, &full[slot]);
-        }
-        issued = ls + 1;
       }
       if (!ok) {
-        for (int ls = issued > kStages ? issued - kStages : 0; ls < issued; ++ls)
-          mbar_wait(&full[ls % kStages], (ls / kStages) & 1, nullptr, kDrainBudgetCycles);
+        for (int g = gs > kStages ? gs - kStages : 0; g < gs; ++g)
+          mbar_wait(&full[g % kStages], (g / kStages) & 1, nullptr, kDrainBudgetCycles);
       }
     }
     __syncwarp();
@@ -299,34 +326,39 @@ __global__ void __launch_bounds__(kThreads, 1) awq_i8_kernel(const I8Params p) {
     // Two threads issue alternate stages (stage parity = issuer), each with
     // one wait set and one commit pair per stage: a stage's waits and
     // bookkeeping overlap the other issuer's MMAs in the tensor pipe.  Stage
-    // accumulator ds = parity and A stages s = ls % 4 are private to one
+    // accumulator ds = parity and A stages s = gs % 4 are private to one
     // issuer, and tcgen05.commit tracks only the issuing thread's MMAs.
     if (lane == 0) {
       constexpr uint32_t idesc = umma_idesc_i8(kTileN, 2 * BN);
       const int parity = warp == 2 ? 0 : 1;
       bool ok = true;
-      for (int ls = parity; ls < nstages; ls += 2) {
-        const int s = ls % kStages;
-        const int ds = ls & (kDStages - 1);
-        const int nb = min(kStageBlocks, nblocks - ls * kStageBlocks);
-        const uint64_t bdesc0 = awqd::umma_desc_kmajor_sw64(smem_u32(smem + s * C::kStageBytes));
-        const uint32_t a0 = tmem + C::kACol + s * kAStageCols;
-        const uint32_t d0 = tmem + ds * C::kDStageCols;
-        if (!mbar_wait(&full[s], (ls / kStages) & 1, abort_flag) ||
-            !mbar_wait(&a_full[s], (ls / kStages) & 1, abort_flag) ||
-            (ls >= kDStages && !mbar_wait(&d_empty[ds], ((ls / kDStages) - 1) & 1, abort_flag))) {
-          ok = false;
-          break;
+      int gs = 0;
+      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+        const Unit w = unit_of(u, p);
+        for (int ls = 0; ls < w.nstages; ++ls, ++gs) {
+          if ((gs & 1) != parity) continue;
+          const int s = gs % kStages;
+          const int ds = gs & (kDStages - 1);
+          const int nb = min(kStageBlocks, w.nblocks - ls * kStageBlocks);
+          const uint64_t bdesc0 = awqd::umma_desc_kmajor_sw64(smem_u32(smem + s * C::kStageBytes));
+          const uint32_t a0 = tmem + C::kACol + s * kAStageCols;
+          const uint32_t d0 = tmem + ds * C::kDStageCols;
+          if (!mbar_wait(&full[s], (gs / kStages) & 1, abort_flag) ||
+              !mbar_wait(&a_full[s], (gs / kStages) & 1, abort_flag) ||
+              (gs >= kDStages && !mbar_wait(&d_empty[ds], ((gs / kDStages) - 1) & 1, abort_flag))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          for (int b = 0; b < nb; ++b) {
+            const uint32_t d = d0 + (b >> p.bpg_shift) * C::kGroupCols;
+            const uint64_t bd = bdesc0 + static_cast<uint64_t>((b * C::kLimbChunkBytes) >> 4);
+            umma_i8_ts(d, a0 + b * 16, bd, idesc, (b & ((1 << p.bpg_shift) - 1)) == 0 ? 0u : 1u);
+            umma_i8_ts(d, a0 + b * 16 + 8, bd + 2, idesc, 1u);  // +32 bytes: the block's second 32-k run
+          }
+          umma_commit(&done[s]);
+          umma_commit(&d_full[ds]);
         }
-        tc_fence_after();
-        for (int b = 0; b < nb; ++b) {
-          const uint32_t d = d0 + (b >> p.bpg_shift) * C::kGroupCols;
-          const uint64_t bd = bdesc0 + static_cast<uint64_t>((b * C::kLimbChunkBytes) >> 4);
-          umma_i8_ts(d, a0 + b * 16, bd, idesc, (b & ((1 << p.bpg_shift) - 1)) == 0 ? 0u : 1u);
-          umma_i8_ts(d, a0 + b * 16 + 8, bd + 2, idesc, 1u);  // +32 bytes: the block's second 32-k run
-        }
-        umma_commit(&done[s]);
-        umma_commit(&d_full[ds]);
       }
       // Tensor memory is freed only after every issued MMA has completed.
       umma_commit(&fin[parity]);
@@ -335,147 +367,164 @@ __global__ void __launch_bounds__(kThreads, 1) awq_i8_kernel(const I8Params p) {
     __syncwarp();
   } else if (warp < kDrainWarp) {
     // ---------------- code expanders ----------------
-    // full[s] for stage ls implies done[s] for stage ls - kStages (the
+    // full[s] for stage gs implies done[s] for stage gs - kStages (the
     // producer waited for it before refilling the slot), so A stage s is free.
     const int quad = warp & 3;
     const int col = quad * 32 + lane;
     const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
-    for (int ls = 0; ls < nstages; ++ls) {
-      const int s = ls % kStages;
-      const int nb = min(kStageBlocks, nblocks - ls * kStageBlocks);
-      if (!__all_sync(0xffffffffu, mbar_wait(&full[s], (ls / kStages) & 1, abort_flag))) break;
-      const uint8_t *stage = smem + s * C::kStageBytes + C::kQOff;
-      uint4 q[kStageChunks];
+    bool ok = true;
+    int gs = 0;
+    for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+      const Unit w = unit_of(u, p);
+      for (int ls = 0; ls < w.nstages; ++ls, ++gs) {
+        const int s = gs % kStages;
+        const int nb = min(kStageBlocks, w.nblocks - ls * kStageBlocks);
+        if (!__all_sync(0xffffffffu, mbar_wait(&full[s], (gs / kStages) & 1, abort_flag))) { ok = false; break; }
+        const uint8_t *stage = smem + s * C::kStageBytes + C::kQOff;
+        uint4 q[kStageChunks];
 #pragma unroll
-      for (int c = 0; c < kStageChunks; ++c)
-        if (c < 2 * nb) q[c] = *reinterpret_cast<const uint4 *>(stage + c * kChunkBytes + col * 16);
-      tc_fence_after();
+        for (int c = 0; c < kStageChunks; ++c)
+          if (c < 2 * nb) q[c] = *reinterpret_cast<const uint4 *>(stage + c * kChunkBytes + col * 16);
+        tc_fence_after();
 #pragma unroll
-      for (int b = 0; b < kStageBlocks; ++b) {
-        if (b < nb) {
-          uint32_t a[16];
+        for (int b = 0; b < kStageBlocks; ++b) {
+          if (b < nb) {
+            uint32_t a[16];
 #pragma unroll
-          for (int r = 0; r < 2; ++r) {
-            const uint32_t w[4] = {q[2 * b + r].x, q[2 * b + r].y, q[2 * b + r].z, q[2 * b + r].w};
+            for (int r = 0; r < 2; ++r) {
+              const uint32_t wd[4] = {q[2 * b + r].x, q[2 * b + r].y, q[2 * b + r].z, q[2 * b + r].w};
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              a[8 * r + j] = w[j] & 0x0F0F0F0Fu;
-              a[8 * r + 4 + j] = (w[j] >> 4) & 0x0F0F0F0Fu;
+              for (int j = 0; j < 4; ++j) {
+                a[8 * r + j] = wd[j] & 0x0F0F0F0Fu;
+                a[8 * r + 4 + j] = (wd[j] >> 4) & 0x0F0F0F0Fu;
+              }
             }
+            tmem_st_32x32b_x16(tmem + lane_base + C::kACol + s * kAStageCols + b * 16, a);
           }
-          tmem_st_32x32b_x16(tmem + lane_base + C::kACol + s * kAStageCols + b * 16, a);
         }
+        awqd::tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&a_full[s]);
       }
-      awqd::tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&a_full[s]);
     }
   } else {
     // ---------------- drain + epilogue ----------------
     const int quad = warp & 3;
     const int col = quad * 32 + lane;
     const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
-    const int n = tile * kTileN + col;
-    const bool n_ok = n < p.N;
     const int gps_full = kStageBlocks >> p.bpg_shift;  // groups per full stage (2 or 1)
-    float acc[BN];
-#pragma unroll
-    for (int t = 0; t < BN; ++t) acc[t] = 0.f;
-    bool ok = true;
-    const uint32_t *szrow = p.szpack + (static_cast<size_t>(tile) * p.groups) * kTileN + col;
     // The next stage's (scale, zero) words (registers) and per-token scalars
     // (cp.async into this warp's shared slots) are fetched one stage ahead.
     uint8_t *scal_sm = smem + C::kScalOff + (warp - kDrainWarp) * 2 * C::kScalSlotBytes;
-    auto groups_in = [&](int ls) { return min(kStageBlocks, nblocks - ls * kStageBlocks) >> p.bpg_shift; };
-    auto fetch = [&](int ls, uint32_t (&szw)[2]) {
-      const int g0 = g_begin + ls * gps_full;
-      const int ng = groups_in(ls);
+    auto fetch = [&](const Unit &w, int ls, int gs_, uint32_t (&szw)[2]) {
+      const int g0 = w.g_begin + ls * gps_full;
+      const int ng = min(kStageBlocks, w.nblocks - ls * kStageBlocks) >> p.bpg_shift;
       if (lane < ng * BN / 2)
-        cp_async_16(smem_u32(scal_sm + (ls & 1) * C::kScalSlotBytes + lane * 16),
+        cp_async_16(smem_u32(scal_sm + (gs_ & 1) * C::kScalSlotBytes + lane * 16),
                     reinterpret_cast<const uint8_t *>(p.scal + static_cast<size_t>(g0) * BN) + lane * 16, 16u);
       cp_async_commit();
+      const uint32_t *szrow = p.szpack + (static_cast<size_t>(w.tile) * p.groups) * kTileN + col;
       szw[0] = __ldg(szrow + static_cast<size_t>(g0) * kTileN);
       szw[1] = ng > 1 ? __ldg(szrow + static_cast<size_t>(g0 + 1) * kTileN) : 0u;
     };
+    asm volatile("griddepcontrol.wait;" ::: "memory");  // the scalars come from the prologue launch
+    bool ok = true;
+    int gs = 0;
     uint32_t sz_next[2] = {0u, 0u};
-    if (nstages > 0) fetch(0, sz_next);
-    for (int ls = 0; ls < nstages; ++ls) {
-      const uint32_t sz[2] = {sz_next[0], sz_next[1]};
-      const int ng = groups_in(ls);
-      cp_async_wait_all();
-      __syncwarp();
-      if (ls + 1 < nstages) fetch(ls + 1, sz_next);
-      const int4 *sc = reinterpret_cast<const int4 *>(scal_sm + (ls & 1) * C::kScalSlotBytes);
-      const int ds = ls & (kDStages - 1);
-      if (!__all_sync(0xffffffffu, mbar_wait(&d_full[ds], (ls / kDStages) & 1, abort_flag))) { ok = false; break; }
-      tc_fence_after();
-      for (int j = 0; j < ng; ++j) {
-        const float s = __half2float(__ushort_as_half(static_cast<uint16_t>(sz[j] & 0xFFFFu)));
-        const int z = static_cast<int>(sz[j] >> 16);
-        const uint32_t dcol = tmem + lane_base + ds * C::kDStageCols + j * C::kGroupCols;
+    int u = blockIdx.x;
+    Unit w = unit_of(u, p);
+    if (u < units) fetch(w, 0, 0, sz_next);
+    for (; u < units && ok; u += gridDim.x) {
+      w = unit_of(u, p);
+      const int n = w.tile * kTileN + col;
+      const bool n_ok = n < p.N;
+      float acc[BN];
 #pragma unroll
-        for (int h = 0; h < BN / 16; ++h) {
-          uint32_t d0[16], d1[16];
-          tmem_ld_32x32b_x16(dcol + h * 16, d0);
-          tmem_ld_32x32b_x16(dcol + BN + h * 16, d1);
-          tmem_wait_ld();
+      for (int t = 0; t < BN; ++t) acc[t] = 0.f;
+      for (int ls = 0; ls < w.nstages; ++ls, ++gs) {
+        const uint32_t sz[2] = {sz_next[0], sz_next[1]};
+        const int ng = min(kStageBlocks, w.nblocks - ls * kStageBlocks) >> p.bpg_shift;
+        cp_async_wait_all();
+        __syncwarp();
+        if (ls + 1 < w.nstages) {
+          fetch(w, ls + 1, gs + 1, sz_next);
+        } else if (u + static_cast<int>(gridDim.x) < units) {
+          fetch(unit_of(u + gridDim.x, p), 0, gs + 1, sz_next);
+        }
+        const int4 *sc = reinterpret_cast<const int4 *>(scal_sm + (gs & 1) * C::kScalSlotBytes);
+        const int ds = gs & (kDStages - 1);
+        if (!__all_sync(0xffffffffu, mbar_wait(&d_full[ds], (gs / kDStages) & 1, abort_flag))) { ok = false; break; }
+        tc_fence_after();
+        for (int j = 0; j < ng; ++j) {
+          const float s = __half2float(__ushort_as_half(static_cast<uint16_t>(sz[j] & 0xFFFFu)));
+          const int z = static_cast<int>(sz[j] >> 16);
+          const uint32_t dcol = tmem + lane_base + ds * C::kDStageCols + j * C::kGroupCols;
 #pragma unroll
-          for (int t = 0; t < 16; t += 2) {
-            const int4 two = sc[(j * BN + h * 16 + t) / 2];
-            const int v0 = static_cast<int>(d0[t]) * 128 + static_cast<int>(d1[t]) - z * two.y;
-            const int v1 = static_cast<int>(d0[t + 1]) * 128 + static_cast<int>(d1[t + 1]) - z * two.w;
-            acc[h * 16 + t] = fmaf(s * __int_as_float(two.x), static_cast<float>(v0), acc[h * 16 + t]);
-            acc[h * 16 + t + 1] = fmaf(s * __int_as_float(two.z), static_cast<float>(v1), acc[h * 16 + t + 1]);
+          for (int h = 0; h < BN / 16; ++h) {
+            uint32_t d0[16], d1[16];
+            tmem_ld_32x32b_x16(dcol + h * 16, d0);
+            tmem_ld_32x32b_x16(dcol + BN + h * 16, d1);
+            tmem_wait_ld();
+#pragma unroll
+            for (int t = 0; t < 16; t += 2) {
+              const int4 two = sc[(j * BN + h * 16 + t) / 2];
+              const int v0 = static_cast<int>(d0[t]) * 128 + static_cast<int>(d1[t]) - z * two.y;
+              const int v1 = static_cast<int>(d0[t + 1]) * 128 + static_cast<int>(d1[t + 1]) - z * two.w;
+              acc[h * 16 + t] = fmaf(s * __int_as_float(two.x), static_cast<float>(v0), acc[h * 16 + t]);
+              acc[h * 16 + t + 1] = fmaf(s * __int_as_float(two.z), static_cast<float>(v1), acc[h * 16 + t + 1]);
+            }
           }
         }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&d_empty[ds]);
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&d_empty[ds]);
-    }
-    cp_async_wait_all();
-    ok = __all_sync(0xffffffffu, ok) && nstages > 0 && !*abort_flag;
-    const float bias_n = (p.bias != nullptr && n_ok) ? __half2float(__ushort_as_half(p.bias[n])) : 0.f;
-    if (p.splits == 1) {
-      if (ok && n_ok) {
-#pragma unroll
-        for (int t = 0; t < BN; ++t)
-          if (t < p.M) p.y[static_cast<size_t>(t) * p.N + n] = __half_as_ushort(__float2half_rn(acc[t] + bias_n));
-      }
-    } else {
-      float *part = p.partials + static_cast<size_t>(tile) * p.splits * BN * kTileN;
-      if (ok) {
-#pragma unroll
-        for (int t = 0; t < BN; ++t) __stcg(part + (static_cast<size_t>(split) * BN + t) * kTileN + col, acc[t]);
-      }
-      __threadfence();
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (warp == kDrainWarp && lane == 0) {
-        const unsigned int prev = ok ? atomicAdd(p.semaphores + tile, 1u) : 0u;
-        *last_flag = (ok && prev == static_cast<unsigned int>(p.splits - 1)) ? 1 : 0;
-      }
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (*last_flag) {
-        __threadfence();
-        float sum[BN];
-#pragma unroll
-        for (int t = 0; t < BN; ++t) sum[t] = 0.f;
-        for (int sp = 0; sp < p.splits; ++sp) {
-          float v[BN];
-#pragma unroll
-          for (int t = 0; t < BN; ++t) v[t] = __ldcg(part + (static_cast<size_t>(sp) * BN + t) * kTileN + col);
-#pragma unroll
-          for (int t = 0; t < BN; ++t) sum[t] += v[t];
-        }
+      // ---- epilogue of the unit ----
+      ok = __all_sync(0xffffffffu, ok) && !*abort_flag;
+      if (!ok) break;
+      const float bias_n = (p.bias != nullptr && n_ok) ? __half2float(__ushort_as_half(p.bias[n])) : 0.f;
+      if (p.splits == 1) {
         if (n_ok) {
 #pragma unroll
           for (int t = 0; t < BN; ++t)
-            if (t < p.M) p.y[static_cast<size_t>(t) * p.N + n] = __half_as_ushort(__float2half_rn(sum[t] + bias_n));
+            if (t < p.M) p.y[static_cast<size_t>(t) * p.N + n] = __half_as_ushort(__float2half_rn(acc[t] + bias_n));
         }
-        if (warp == kDrainWarp && lane == 0) p.semaphores[tile] = 0u;
+      } else {
+        float *part = p.partials + static_cast<size_t>(w.tile) * p.splits * BN * kTileN;
+#pragma unroll
+        for (int t = 0; t < BN; ++t) __stcg(part + (static_cast<size_t>(w.split) * BN + t) * kTileN + col, acc[t]);
+        __threadfence();
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (warp == kDrainWarp && lane == 0) {
+          const unsigned int prev = atomicAdd(p.semaphores + w.tile, 1u);
+          *last_flag = prev == static_cast<unsigned int>(p.splits - 1) ? 1 : 0;
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        const bool last = *last_flag != 0;
+        asm volatile("bar.sync 1, 128;" ::: "memory");  // every drain thread has read the flag
+        if (last) {
+          __threadfence();
+          float sum[BN];
+#pragma unroll
+          for (int t = 0; t < BN; ++t) sum[t] = 0.f;
+          for (int sp = 0; sp < p.splits; ++sp) {
+            float v[BN];
+#pragma unroll
+            for (int t = 0; t < BN; ++t) v[t] = __ldcg(part + (static_cast<size_t>(sp) * BN + t) * kTileN + col);
+#pragma unroll
+            for (int t = 0; t < BN; ++t) sum[t] += v[t];
+          }
+          if (n_ok) {
+#pragma unroll
+            for (int t = 0; t < BN; ++t)
+              if (t < p.M) p.y[static_cast<size_t>(t) * p.N + n] = __half_as_ushort(__float2half_rn(sum[t] + bias_n));
+          }
+          if (warp == kDrainWarp && lane == 0) p.semaphores[w.tile] = 0u;
+        }
       }
     }
+    cp_async_wait_all();
     tc_fence_before();
   }
 

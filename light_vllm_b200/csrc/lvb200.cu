@@ -354,8 +354,21 @@ int launch_awq_i8(const I8Plan &plan, const PackedShape &sh, const uint16_t *x, 
   p.bpg_shift = g == 128 ? 1 : 2;
   p.n_tiles = sh.n_tiles;
   p.splits = plan.splits;
-  kernel<<<dim3(sh.n_tiles, plan.splits), lvb::awqi8::kThreads, C::kSmemBytes, stream>>>(p);
-  e = cudaGetLastError();
+  // Persistent grid of at most one CTA per SM, launched as a programmatic
+  // dependent of the limb kernel (it waits for the limbs in-kernel).
+  const int units = sh.n_tiles * plan.splits;
+  const int ctas = units < sm_count(dev) ? units : sm_count(dev);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(ctas));
+  cfg.blockDim = dim3(lvb::awqi8::kThreads);
+  cfg.dynamicSmemBytes = C::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, kernel, p);
   if (e != cudaSuccess) return cuda_fail(e, "awq_i8_kernel launch");
   return LVB_OK;
 }
