@@ -58,7 +58,6 @@ constexpr int kStageChunks = 2 * kStageBlocks;        // 32-k runs per stage
 constexpr int kQStageBytes = kStageChunks * kChunkBytes;  // 16 KB of codes
 constexpr int kStages = 4;                            // stages in flight (shared memory and TMEM A)
 constexpr int kAStageCols = kStageBlocks * 16;        // 16 columns (64 int8) per block
-constexpr int kDStages = 2;                           // stage accumulators in flight
 constexpr int kExpandWarp = 3;                        // first code-expander warp
 constexpr int kDrainWarp = 7;                         // first drain warp
 constexpr int kIssuer2Warp = 11;                      // second MMA issuer (odd stages)
@@ -69,6 +68,9 @@ constexpr int kTmemCols = 512;
 // MMA issuer, code expanders and drain synchronise once per stage.
 template <int BN>
 struct I8Config {
+  // Stage accumulators in flight: the drain of stage s overlaps the MMAs of
+  // the next kDStages - 1 stages (as many as tensor memory holds).
+  static constexpr int kDStages = BN == 16 ? 4 : 2;
   static constexpr int kLimbRows = 2 * BN;                   // (limb, token) rows of B
   static constexpr int kLimbChunkBytes = kLimbRows * 64;     // one 64-k chunk of the limb tile
   static constexpr int kLimbStageBytes = kStageBlocks * kLimbChunkBytes;
@@ -80,12 +82,16 @@ struct I8Config {
   static constexpr int kBarOff = kStages * kStageBytes;
   // full, done, a_full (stages), d_full, d_empty (stage accumulators), fin (per issuer).
   static constexpr int kNumBars = 3 * kStages + 2 * kDStages + 2;
+  static_assert((kDStages & (kDStages - 1)) == 0, "power-of-two accumulator ring");
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;
   // Per drain warp, two stage slots of per-token scalars (2 groups x BN x 8 bytes).
   static constexpr int kScalOff = (kMiscOff + 64 + 15) / 16 * 16;
   static constexpr int kScalSlotBytes = 2 * BN * 8;
   static constexpr int kScalBytes = 4 * 2 * kScalSlotBytes;
-  static constexpr int kSmemBytes = kScalOff + kScalBytes + 1024;
+  // Output tile [BN tokens][128 columns] fp16, written to y by one TMA store.
+  static constexpr int kYOff = (kScalOff + kScalBytes + 127) / 128 * 128;
+  static constexpr int kYBytes = BN * kTileN * 2;
+  static constexpr int kSmemBytes = kYOff + kYBytes + 1024;
   static_assert(BN == 16 || BN == 32, "int8 path covers 16- and 32-row token tiles");
   static_assert(kACol + kStages * kAStageCols <= kTmemCols, "tensor memory budget");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
@@ -174,6 +180,22 @@ __global__ void __launch_bounds__(32) awq_act_limbs_kernel(const uint16_t *__res
   if (lane == 0) scal[static_cast<size_t>(g) * BN + t] = make_int2(__float_as_int(ldexpf(1.f, e - 7)), isum);
 }
 
+// y tile store: shared [BN][128] fp16 -> global y at (column n0, row 0);
+// rows past m are clipped by the tensor map.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, const void *src, int32_t x, int32_t y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(src)), "r"(x), "r"(y)
+               : "memory");
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+__device__ __forceinline__ void tma_store_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+
+__device__ __forceinline__ void tma_store_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 // D[tmem] (+)= A[tmem] * B[smem desc]^T, kind::i8 (s8 x s8 -> s32).
 __device__ __forceinline__ void umma_i8_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
                                            uint32_t accumulate) {
@@ -220,13 +242,16 @@ struct Unit {
 };
 
 __device__ __forceinline__ Unit unit_of(int u, const I8Params &p) {
+  // 32-bit arithmetic throughout (a 64-bit division is a long subroutine on
+  // the path between units): splits <= 16 and groups < 2^20.
   Unit w;
-  w.tile = u / p.splits;
+  const unsigned splits = static_cast<unsigned>(p.splits);
+  w.tile = static_cast<int>(static_cast<unsigned>(u) / splits);
   w.split = u - w.tile * p.splits;
   // Splits cover whole groups, so every unit drains complete groups and its
   // stages start on a group boundary.
-  w.g_begin = static_cast<int>((static_cast<long long>(w.split) * p.groups) / p.splits);
-  const int g_end = static_cast<int>((static_cast<long long>(w.split + 1) * p.groups) / p.splits);
+  w.g_begin = static_cast<int>(static_cast<unsigned>(w.split * p.groups) / splits);
+  const int g_end = static_cast<int>(static_cast<unsigned>((w.split + 1) * p.groups) / splits);
   w.b_begin = w.g_begin << p.bpg_shift;
   w.nblocks = (g_end - w.g_begin) << p.bpg_shift;
   w.nstages = (w.nblocks + kStageBlocks - 1) / kStageBlocks;
@@ -237,7 +262,8 @@ __device__ __forceinline__ Unit unit_of(int u, const I8Params &p) {
 // same sequence of stages, numbered gs across units for the rings' slots and
 // phases, so the pipeline does not drain between units.
 template <int BN>
-__global__ void __launch_bounds__(kThreads, 1) awq_i8_kernel(const I8Params p) {
+__global__ void __launch_bounds__(kThreads, 1)
+    awq_i8_kernel(const __grid_constant__ CUtensorMap ymap, const I8Params p) {
   using C = I8Config<BN>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
@@ -247,8 +273,8 @@ __global__ void __launch_bounds__(kThreads, 1) awq_i8_kernel(const I8Params p) {
   uint64_t *done = full + kStages;            // the stage's MMAs completed (slot and A stage free)
   uint64_t *a_full = done + kStages;          // the stage's A columns are in tensor memory
   uint64_t *d_full = a_full + kStages;        // a stage accumulator holds finished groups
-  uint64_t *d_empty = d_full + kDStages;      // the drain has read a stage accumulator
-  uint64_t *fin = d_empty + kDStages;         // [2]: every MMA of each issuer has completed
+  uint64_t *d_empty = d_full + C::kDStages;      // the drain has read a stage accumulator
+  uint64_t *fin = d_empty + C::kDStages;         // [2]: every MMA of each issuer has completed
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + C::kMiscOff);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + C::kMiscOff + 8);
   volatile int *last_flag = reinterpret_cast<volatile int *>(smem + C::kMiscOff + 16);
@@ -263,7 +289,7 @@ __global__ void __launch_bounds__(kThreads, 1) awq_i8_kernel(const I8Params p) {
       mbar_init(&done[s], 1);
       mbar_init(&a_full[s], 4);
     }
-    for (int j = 0; j < kDStages; ++j) {
+    for (int j = 0; j < C::kDStages; ++j) {
       mbar_init(&d_full[j], 1);
       mbar_init(&d_empty[j], 4);
     }
@@ -338,14 +364,14 @@ __global__ void __launch_bounds__(kThreads, 1) awq_i8_kernel(const I8Params p) {
         for (int ls = 0; ls < w.nstages; ++ls, ++gs) {
           if ((gs & 1) != parity) continue;
           const int s = gs % kStages;
-          const int ds = gs & (kDStages - 1);
+          const int ds = gs & (C::kDStages - 1);
           const int nb = min(kStageBlocks, w.nblocks - ls * kStageBlocks);
           const uint64_t bdesc0 = awqd::umma_desc_kmajor_sw64(smem_u32(smem + s * C::kStageBytes));
           const uint32_t a0 = tmem + C::kACol + s * kAStageCols;
           const uint32_t d0 = tmem + ds * C::kDStageCols;
           if (!mbar_wait(&full[s], (gs / kStages) & 1, abort_flag) ||
               !mbar_wait(&a_full[s], (gs / kStages) & 1, abort_flag) ||
-              (gs >= kDStages && !mbar_wait(&d_empty[ds], ((gs / kDStages) - 1) & 1, abort_flag))) {
+              (gs >= C::kDStages && !mbar_wait(&d_empty[ds], ((gs / C::kDStages) - 1) & 1, abort_flag))) {
             ok = false;
             break;
           }
@@ -417,46 +443,63 @@ __global__ void __launch_bounds__(kThreads, 1) awq_i8_kernel(const I8Params p) {
     // The next stage's (scale, zero) words (registers) and per-token scalars
     // (cp.async into this warp's shared slots) are fetched one stage ahead.
     uint8_t *scal_sm = smem + C::kScalOff + (warp - kDrainWarp) * 2 * C::kScalSlotBytes;
-    auto fetch = [&](const Unit &w, int ls, int gs_, uint32_t (&szw)[2]) {
+    auto fetch_scal = [&](const Unit &w, int ls, int gs_) {
       const int g0 = w.g_begin + ls * gps_full;
       const int ng = min(kStageBlocks, w.nblocks - ls * kStageBlocks) >> p.bpg_shift;
       if (lane < ng * BN / 2)
         cp_async_16(smem_u32(scal_sm + (gs_ & 1) * C::kScalSlotBytes + lane * 16),
                     reinterpret_cast<const uint8_t *>(p.scal + static_cast<size_t>(g0) * BN) + lane * 16, 16u);
       cp_async_commit();
+    };
+    // Returned by value, so the loads stay in registers and are waited for
+    // only where the words are used.
+    auto fetch_sz = [&](const Unit &w, int ls) -> uint2 {
+      const int g0 = w.g_begin + ls * gps_full;
+      const int ng = min(kStageBlocks, w.nblocks - ls * kStageBlocks) >> p.bpg_shift;
       const uint32_t *szrow = p.szpack + (static_cast<size_t>(w.tile) * p.groups) * kTileN + col;
-      szw[0] = __ldg(szrow + static_cast<size_t>(g0) * kTileN);
-      szw[1] = ng > 1 ? __ldg(szrow + static_cast<size_t>(g0 + 1) * kTileN) : 0u;
+      return make_uint2(__ldg(szrow + static_cast<size_t>(g0) * kTileN),
+                        ng > 1 ? __ldg(szrow + static_cast<size_t>(g0 + 1) * kTileN) : 0u);
     };
     asm volatile("griddepcontrol.wait;" ::: "memory");  // the scalars come from the prologue launch
     bool ok = true;
     int gs = 0;
-    uint32_t sz_next[2] = {0u, 0u};
+    uint2 sz_next = make_uint2(0u, 0u);
+    uint2 sz_unit_next = make_uint2(0u, 0u);  // first stage of the next unit, loaded a unit ahead
     int u = blockIdx.x;
     Unit w = unit_of(u, p);
-    if (u < units) fetch(w, 0, 0, sz_next);
+    if (u < units) {
+      fetch_scal(w, 0, 0);
+      sz_next = fetch_sz(w, 0);
+    }
     for (; u < units && ok; u += gridDim.x) {
       w = unit_of(u, p);
+      const bool has_next = u + static_cast<int>(gridDim.x) < units;
+      const Unit wn = unit_of(has_next ? u + static_cast<int>(gridDim.x) : u, p);
+      if (has_next) sz_unit_next = fetch_sz(wn, 0);
       const int n = w.tile * kTileN + col;
       const bool n_ok = n < p.N;
       float acc[BN];
 #pragma unroll
       for (int t = 0; t < BN; ++t) acc[t] = 0.f;
       for (int ls = 0; ls < w.nstages; ++ls, ++gs) {
-        const uint32_t sz[2] = {sz_next[0], sz_next[1]};
+        const uint32_t sz[2] = {sz_next.x, sz_next.y};
         const int ng = min(kStageBlocks, w.nblocks - ls * kStageBlocks) >> p.bpg_shift;
         cp_async_wait_all();
         __syncwarp();
         if (ls + 1 < w.nstages) {
-          fetch(w, ls + 1, gs + 1, sz_next);
-        } else if (u + static_cast<int>(gridDim.x) < units) {
-          fetch(unit_of(u + gridDim.x, p), 0, gs + 1, sz_next);
+          fetch_scal(w, ls + 1, gs + 1);
+          sz_next = fetch_sz(w, ls + 1);
+        } else if (has_next) {
+          fetch_scal(wn, 0, gs + 1);
+          sz_next = sz_unit_next;
         }
         const int4 *sc = reinterpret_cast<const int4 *>(scal_sm + (gs & 1) * C::kScalSlotBytes);
-        const int ds = gs & (kDStages - 1);
-        if (!__all_sync(0xffffffffu, mbar_wait(&d_full[ds], (gs / kDStages) & 1, abort_flag))) { ok = false; break; }
+        const int ds = gs & (C::kDStages - 1);
+        if (!__all_sync(0xffffffffu, mbar_wait(&d_full[ds], (gs / C::kDStages) & 1, abort_flag))) { ok = false; break; }
         tc_fence_after();
-        for (int j = 0; j < ng; ++j) {
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          if (j >= ng) break;
           const float s = __half2float(__ushort_as_half(static_cast<uint16_t>(sz[j] & 0xFFFFu)));
           const int z = static_cast<int>(sz[j] >> 16);
           const uint32_t dcol = tmem + lane_base + ds * C::kDStageCols + j * C::kGroupCols;
@@ -485,11 +528,16 @@ __global__ void __launch_bounds__(kThreads, 1) awq_i8_kernel(const I8Params p) {
       if (!ok) break;
       const float bias_n = (p.bias != nullptr && n_ok) ? __half2float(__ushort_as_half(p.bias[n])) : 0.f;
       if (p.splits == 1) {
-        if (n_ok) {
+        // Stage the tile in shared memory and write it with one TMA store, so
+        // the drain does not wait on BN strided global stores.
+        uint16_t *ytile = reinterpret_cast<uint16_t *>(smem + C::kYOff);
+        if (warp == kDrainWarp && lane == 0) tma_store_wait_read();  // the previous unit's store has read the tile
+        asm volatile("bar.sync 1, 128;" ::: "memory");
 #pragma unroll
-          for (int t = 0; t < BN; ++t)
-            if (t < p.M) p.y[static_cast<size_t>(t) * p.N + n] = __half_as_ushort(__float2half_rn(acc[t] + bias_n));
-        }
+        for (int t = 0; t < BN; ++t) ytile[t * kTileN + col] = __half_as_ushort(__float2half_rn(acc[t] + bias_n));
+        fence_proxy_async_smem();
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (warp == kDrainWarp && lane == 0) tma_store_2d(&ymap, ytile, w.tile * kTileN, 0);
       } else {
         float *part = p.partials + static_cast<size_t>(w.tile) * p.splits * BN * kTileN;
 #pragma unroll
@@ -525,6 +573,7 @@ __global__ void __launch_bounds__(kThreads, 1) awq_i8_kernel(const I8Params p) {
       }
     }
     cp_async_wait_all();
+    if (warp == kDrainWarp && lane == 0) tma_store_wait_all();
     tc_fence_before();
   }
 

@@ -368,7 +368,14 @@ int launch_awq_i8(const I8Plan &plan, const PackedShape &sh, const uint16_t *x, 
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  e = cudaLaunchKernelEx(&cfg, kernel, p);
+  // y as a [m rows][n] fp16 tensor; a box is one [BN][128] output tile.
+  CUtensorMap ymap;
+  const cuuint64_t ydims[2] = {static_cast<cuuint64_t>(n), static_cast<cuuint64_t>(m)};
+  const cuuint64_t ystrides[1] = {static_cast<cuuint64_t>(n) * 2};
+  const cuuint32_t ybox[2] = {static_cast<cuuint32_t>(lvb::awqi8::kTileN), static_cast<cuuint32_t>(BN)};
+  rc = encode_map(&ymap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, y, ydims, ystrides, ybox, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (rc != LVB_OK) return rc;
+  e = cudaLaunchKernelEx(&cfg, kernel, ymap, p);
   if (e != cudaSuccess) return cuda_fail(e, "awq_i8_kernel launch");
   return LVB_OK;
 }
@@ -637,7 +644,7 @@ int lvb_awq_linear_packed(const uint16_t *x, const void *codes, const void *grou
   const PackedShape sh = packed_shape(k, n, group_size);
   const size_t max_ws = workspace != nullptr ? workspace_bytes : 0;
   cudaStream_t stream_ = reinterpret_cast<cudaStream_t>(stream);
-  if (i8_eligible(m, k, n, group_size)) {
+  if (i8_eligible(m, k, n, group_size) && aligned16(y)) {  // y is written by TMA stores
     const I8Plan ip = i8_plan(m, k, sh, group_size, sm_count(dev), max_ws);
     const uint8_t *c8 = static_cast<const uint8_t *>(codes);
     const uint32_t *g8 = static_cast<const uint32_t *>(groups);
