@@ -237,6 +237,43 @@ LVB_API int lvb_paged_attention(const uint16_t *query, int64_t query_token_strid
                         int dtype, void *workspace, size_t workspace_bytes,
                         lvb_stream_t stream);
 
+/* ------------------------------------------------------------------------ */
+/* Tensor-parallel all-reduce + residual add + RMSNorm                        */
+/* ------------------------------------------------------------------------ */
+
+/* Peer workspaces (set-up calls; unlike the compute entry points these
+ * allocate and map device memory).  lvb_ipc_alloc returns zero-filled device
+ * memory on the current device and its 64-byte CUDA IPC handle; every other
+ * rank of the node maps it with lvb_ipc_open.  lvb_ipc_close unmaps a peer's
+ * workspace, lvb_ipc_free releases one's own (after every peer has closed it).
+ * Used by TensorParallelCollectives in place of the NCCL communicator set-up of
+ * `CurrentStreamNCCL` (runtime/distributed/nccl.py:45-120). */
+LVB_API int lvb_ipc_alloc(size_t bytes, void **ptr, void *handle_out);
+LVB_API int lvb_ipc_open(const void *handle, void **ptr);
+LVB_API int lvb_ipc_close(void *ptr);
+LVB_API int lvb_ipc_free(void *ptr);
+
+/* Bytes of one rank's workspace for up to max_tokens rows of `hidden` fp16:
+ * 256 bytes of flags, then two staging buffers. */
+LVB_API size_t lvb_allreduce_workspace_bytes(int64_t max_tokens, int64_t hidden);
+
+/* Row-parallel epilogue of a Qwen2 block in one launch: h = sum over the
+ * world ranks of `partial` (fp32, rounded to fp16 once), v = h + residual
+ * (fp32), residual <- fp16(v), out <- fp16(v * rsqrt(mean(v^2) + eps) *
+ * weight).  Replaces `all_reduce_sum` (modeling/tensor_parallel.py:18-27,
+ * runtime/distributed/distributed.py:190-197, nccl.py:127-139) followed by
+ * `fused_add_rms_norm` (modeling/models/_qwen2_kernels.py:20-43, 145-180).
+ * workspaces[r] = rank r's workspace as mapped in this process (own for r ==
+ * rank); every rank calls with the same tokens, hidden, max_tokens and epoch,
+ * and epoch increases by one per call starting at 1.  Peers are read with
+ * plain loads; waits for peers are bounded (on timeout the device error word
+ * gets LVB_DEVERR_TIMEOUT and the outputs are left unwritten).  hidden is a
+ * multiple of 8 up to 8192; tensors 16-byte aligned; world <= 8. */
+LVB_API int lvb_allreduce_add_rmsnorm(void *const *workspaces, int rank, int world, const uint16_t *partial,
+                                      uint16_t *residual, const uint16_t *weight, uint16_t *out,
+                                      int64_t tokens, int64_t hidden, int64_t max_tokens, float eps,
+                                      uint32_t epoch, lvb_stream_t stream);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

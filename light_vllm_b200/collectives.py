@@ -20,6 +20,10 @@ logits are gathered along the last dimension.
   (modeling/quantization/awq.py:165-198, 272-297), including their alignment
   rules (output partitions aligned to 8 packed values, row partitions aligned
   to the group size).
+* ``PeerWorkspace`` + ``all_reduce_add_rms_norm``: the row-parallel epilogue
+  of a Qwen2 block (all-reduce, residual add, RMSNorm) as one launch that
+  reads the ranks' partial sums over NVLink peer memory; the workspaces are
+  shared through CUDA IPC handles exchanged over the process group.
 """
 
 from __future__ import annotations
@@ -124,3 +128,110 @@ class TensorParallelCollectives:
         dist.all_gather_into_tensor(flat, tensor.view(-1), group=self._group)
         gathered = flat.view(self.world_size, *tensor.shape)
         return torch.cat([gathered[r][..., :size] for r, size in enumerate(partition_sizes)], dim=-1)
+
+
+class PeerWorkspace:
+    """One peer-readable workspace per rank, mapped by every rank of the group.
+
+    Each rank allocates its workspace with ``lvb_ipc_alloc`` and the ranks
+    exchange the CUDA IPC handles over the process group; afterwards
+    ``pointers`` holds every rank's workspace as mapped in this process, the
+    argument of ``lvb_allreduce_add_rmsnorm``.  All ranks must build and close
+    it together (it is a collective).  Without a process group it serves a
+    single rank.
+    """
+
+    def __init__(self, max_tokens: int, hidden: int, device: torch.device,
+                 group: dist.ProcessGroup | None = None, *, distributed: bool = True) -> None:
+        import ctypes
+
+        from light_vllm_b200 import _native
+
+        self._lib = _native.library()
+        self._native = _native
+        self.max_tokens = int(max_tokens)
+        self.hidden = int(hidden)
+        self.device = device
+        self._group = group
+        use_dist = distributed and dist.is_initialized()
+        self.world_size = dist.get_world_size(group) if use_dist else 1
+        self.rank = dist.get_rank(group) if use_dist else 0
+        nbytes = int(self._lib.lvb_allreduce_workspace_bytes(self.max_tokens, self.hidden))
+        if nbytes == 0:
+            raise ValueError("invalid all-reduce workspace shape")
+        own = ctypes.c_void_p()
+        handle = ctypes.create_string_buffer(64)
+        with torch.cuda.device(device):
+            _native.check(self._lib.lvb_ipc_alloc(nbytes, ctypes.byref(own), handle), "lvb_ipc_alloc")
+        self._own = own.value
+        handles = [handle.raw]
+        if self.world_size > 1:
+            handles = [None] * self.world_size
+            dist.all_gather_object(handles, handle.raw, group=group)
+        pointers = []
+        self._opened = []
+        with torch.cuda.device(device):
+            for r, h in enumerate(handles):
+                if r == self.rank:
+                    pointers.append(self._own)
+                    continue
+                ptr = ctypes.c_void_p()
+                _native.check(self._lib.lvb_ipc_open(h, ctypes.byref(ptr)), "lvb_ipc_open")
+                pointers.append(ptr.value)
+                self._opened.append(ptr.value)
+        self.pointers = (ctypes.c_void_p * self.world_size)(*pointers)
+        self.epoch = 0
+
+    def next_epoch(self) -> int:
+        self.epoch += 1
+        return self.epoch
+
+    def close(self) -> None:
+        """Unmap the peers' workspaces and free this rank's (collective)."""
+
+        if self._own is None:
+            return
+        torch.cuda.synchronize(self.device)
+        with torch.cuda.device(self.device):
+            for ptr in self._opened:
+                self._native.check(self._lib.lvb_ipc_close(ptr), "lvb_ipc_close")
+        self._opened = []
+        if self.world_size > 1:
+            dist.barrier(group=self._group)  # every peer has unmapped this rank's workspace
+        with torch.cuda.device(self.device):
+            self._native.check(self._lib.lvb_ipc_free(self._own), "lvb_ipc_free")
+        self._own = None
+
+
+def all_reduce_add_rms_norm(workspace: PeerWorkspace, partial: Tensor, residual: Tensor,
+                            weight: Tensor, eps: float) -> tuple[Tensor, Tensor]:
+    """Sum ``partial`` over the ranks, add ``residual`` and RMSNorm the result,
+    in one sm_100a launch over peer memory (``lvb_allreduce_add_rmsnorm``).
+
+    Returns ``(normed, residual)``; ``residual`` is updated in place, like
+    ``fused_add_rms_norm`` after ``all_reduce_sum`` in the reference
+    (modeling/models/qwen2.py:497-514, _qwen2_kernels.py:145-180).
+    """
+
+    from light_vllm_b200 import _native
+
+    if partial.shape != residual.shape or partial.dim() != 2:
+        raise ValueError("partial and residual must be [tokens, hidden] tensors of one shape")
+    if partial.dtype != torch.float16 or residual.dtype != torch.float16 or weight.dtype != torch.float16:
+        raise ValueError("the fused all-reduce normalises fp16 tensors")
+    if partial.shape[1] != workspace.hidden or weight.shape != (workspace.hidden,):
+        raise ValueError("hidden size does not match the all-reduce workspace")
+    if partial.shape[0] > workspace.max_tokens:
+        raise ValueError("more tokens than the all-reduce workspace holds")
+    if not (partial.is_contiguous() and residual.is_contiguous() and weight.is_contiguous()):
+        raise ValueError("the fused all-reduce requires contiguous tensors")
+    out = torch.empty_like(partial)
+    epoch = workspace.next_epoch()
+    _native.check(
+        _native.library().lvb_allreduce_add_rmsnorm(
+            workspace.pointers, workspace.rank, workspace.world_size, partial.data_ptr(),
+            residual.data_ptr(), weight.data_ptr(), out.data_ptr(), partial.shape[0], partial.shape[1],
+            workspace.max_tokens, float(eps), epoch, torch.cuda.current_stream(partial.device).cuda_stream),
+        "lvb_allreduce_add_rmsnorm",
+    )
+    return out, residual

@@ -18,13 +18,14 @@
 #include "awq_gemm.cuh"
 #include "awq_decode.cuh"
 #include "awq_i8.cuh"
+#include "allreduce.cuh"
 #include "lvb_common.cuh"
 #include "paged_attention.cuh"
 #include "step_metadata.cuh"
 
 namespace {
 
-constexpr int kAbiVersion = 2;
+constexpr int kAbiVersion = 3;
 constexpr int kMaxDevices = 64;
 
 thread_local char g_last_error[512] = "";
@@ -914,3 +915,92 @@ int lvb_pack_step_metadata(const int32_t *block_ids, const int64_t *table_offset
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------------
+// Tensor-parallel all-reduce + residual add + RMSNorm over peer memory
+// ------------------------------------------------------------------------
+int lvb_ipc_alloc(size_t bytes, void **ptr, void *handle_out) {
+  if (bytes == 0 || !ptr || !handle_out) return fail(LVB_ERR_INVALID, "lvb_ipc_alloc: invalid argument");
+  void *p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc (peer workspace)");
+  e = cudaMemset(p, 0, bytes);
+  if (e == cudaSuccess) {
+    cudaIpcMemHandle_t h;
+    e = cudaIpcGetMemHandle(&h, p);
+    if (e == cudaSuccess) {
+      std::memcpy(handle_out, &h, sizeof(h));
+      *ptr = p;
+      return LVB_OK;
+    }
+  }
+  cudaFree(p);
+  return cuda_fail(e, "preparing a peer workspace");
+}
+
+int lvb_ipc_open(const void *handle, void **ptr) {
+  if (!handle || !ptr) return fail(LVB_ERR_INVALID, "lvb_ipc_open: invalid argument");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcOpenMemHandle");
+  return LVB_OK;
+}
+
+int lvb_ipc_close(void *ptr) {
+  cudaError_t e = cudaIpcCloseMemHandle(ptr);
+  return e == cudaSuccess ? LVB_OK : cuda_fail(e, "cudaIpcCloseMemHandle");
+}
+
+int lvb_ipc_free(void *ptr) {
+  cudaError_t e = cudaFree(ptr);
+  return e == cudaSuccess ? LVB_OK : cuda_fail(e, "cudaFree (peer workspace)");
+}
+
+size_t lvb_allreduce_workspace_bytes(int64_t max_tokens, int64_t hidden) {
+  if (max_tokens <= 0 || hidden <= 0) return 0;
+  return lvb::ar::kFlagBytes + 2 * static_cast<size_t>(max_tokens) * hidden * 2;
+}
+
+int lvb_allreduce_add_rmsnorm(void *const *workspaces, int rank, int world, const uint16_t *partial,
+                              uint16_t *residual, const uint16_t *weight, uint16_t *out, int64_t tokens,
+                              int64_t hidden, int64_t max_tokens, float eps, uint32_t epoch,
+                              lvb_stream_t stream) {
+  if (world < 1 || world > lvb::ar::kMaxWorld || rank < 0 || rank >= world)
+    return fail(LVB_ERR_INVALID, "all-reduce rank %d of world %d (at most %d ranks)", rank, world, lvb::ar::kMaxWorld);
+  if (tokens < 0 || tokens > max_tokens || hidden <= 0 || hidden % 8 != 0 || hidden > lvb::ar::kMaxHidden)
+    return fail(LVB_ERR_INVALID, "all-reduce shape %lld x %lld (workspace rows %lld; hidden a multiple of 8 up to %d)",
+                (long long)tokens, (long long)hidden, (long long)max_tokens, lvb::ar::kMaxHidden);
+  if (tokens == 0) return LVB_OK;
+  if (tokens > INT_MAX) return fail(LVB_ERR_UNSUPPORTED, "token count exceeds int32");
+  if (epoch == 0) return fail(LVB_ERR_INVALID, "all-reduce epochs start at 1");
+  if (!workspaces || !partial || !residual || !weight || !out) return fail(LVB_ERR_INVALID, "all-reduce null pointer argument");
+  if (!aligned16(partial) || !aligned16(residual) || !aligned16(weight) || !aligned16(out))
+    return fail(LVB_ERR_INVALID, "all-reduce tensors must be 16-byte aligned");
+  lvb::ar::Args a{};
+  for (int r = 0; r < world; ++r) {
+    if (!workspaces[r] || !aligned16(workspaces[r])) return fail(LVB_ERR_INVALID, "peer workspace %d is null or unaligned", r);
+    a.ws[r] = static_cast<uint8_t *>(workspaces[r]);
+  }
+  int dev = 0;
+  int rc = current_device(&dev);
+  if (rc != LVB_OK) return rc;
+  a.rank = rank;
+  a.world = world;
+  a.partial = partial;
+  a.residual = residual;
+  a.weight = weight;
+  a.out = out;
+  a.tokens = static_cast<int>(tokens);
+  a.hidden = static_cast<int>(hidden);
+  a.buf_bytes = static_cast<size_t>(max_tokens) * hidden * 2;
+  a.eps = eps;
+  a.epoch = epoch;
+  // At most one CTA per SM: every CTA must be resident while it waits.
+  const int sms = sm_count(dev);
+  const int grid = tokens < sms ? static_cast<int>(tokens) : sms;
+  lvb::ar::allreduce_add_rmsnorm_kernel<<<grid, lvb::ar::kThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "allreduce_add_rmsnorm_kernel launch");
+  return LVB_OK;
+}

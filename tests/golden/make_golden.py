@@ -15,6 +15,8 @@ Fixtures:
   paged_meta.json    slot mappings, request indices, tree visibility and
                      block-table validation outcomes for metadata cases.
   paged_attn.npz     TorchPagedAttention outputs and post-write cache contents.
+  fused_norm.npz     fused_add_rms_norm outputs after a rank sum of fp16
+                     partials (the row-parallel epilogue of a Qwen2 block).
 """
 
 from __future__ import annotations
@@ -43,6 +45,7 @@ def _import_reference():
         TorchPagedAttention,
     )
     from light_vllm.runtime.execution.paged_cache import PagedKVCache, PagedKVCacheConfig
+    from light_vllm.modeling.models._qwen2_kernels import fused_add_rms_norm
 
     return dict(
         AttentionLayerSpec=AttentionLayerSpec,
@@ -53,6 +56,7 @@ def _import_reference():
         TorchPagedAttention=TorchPagedAttention,
         PagedKVCache=PagedKVCache,
         PagedKVCacheConfig=PagedKVCacheConfig,
+        fused_add_rms_norm=fused_add_rms_norm,
     )
 
 
@@ -242,13 +246,40 @@ def make_attention(ref) -> None:
     np.savez_compressed(HERE / "paged_attn.npz", **out)
 
 
+def make_fused_norm(ref) -> None:
+    """Rank sums of fp16 partials, then the reference's ``fused_add_rms_norm``.
+
+    The all-reduced tensor is the fp16 rounding of the fp32 rank sum.  The
+    reference function runs on fp32 copies of the fp16 inputs: on CPU that is
+    its ``hidden + residual`` / ``F.rms_norm`` path in fp32, the arithmetic its
+    Triton kernel performs on GPUs before storing fp16.
+    """
+
+    out: dict[str, np.ndarray] = {}
+    cases = [("w2_t5_h64", 2, 5, 64, 1e-6), ("w4_t3_h3584", 4, 3, 3584, 1e-6),
+             ("w8_t2_h896", 8, 2, 896, 1e-5)]
+    for ci, (name, world, tokens, hidden, eps) in enumerate(cases):
+        g = torch.Generator().manual_seed(3000 + ci)
+        partials = (torch.randn(world, tokens, hidden, generator=g) * 4).half()
+        residual = (torch.randn(tokens, hidden, generator=g) * 8).half()
+        weight = (torch.rand(hidden, generator=g) * 2).half()
+        reduced = partials.float().sum(0).half()
+        normed, new_residual = ref["fused_add_rms_norm"](reduced.float(), residual.float(), weight.float(), eps)
+        for key, tensor in (("partials", partials), ("residual", residual), ("weight", weight),
+                            ("normed", normed), ("new_residual", new_residual)):
+            out[f"{name}_{key}"] = _as_storable(tensor)
+        out[f"{name}_eps"] = np.array(eps, dtype=np.float64)
+    np.savez_compressed(HERE / "fused_norm.npz", **out)
+
+
 def main() -> None:
     torch.set_num_threads(1)
     ref = _import_reference()
     make_awq(ref)
     make_meta(ref)
     make_attention(ref)
-    for name in ("awq_golden.npz", "paged_meta.json", "paged_attn.npz"):
+    make_fused_norm(ref)
+    for name in ("awq_golden.npz", "paged_meta.json", "paged_attn.npz", "fused_norm.npz"):
         print(name, (HERE / name).stat().st_size, "bytes")
 
 

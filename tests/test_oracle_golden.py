@@ -128,3 +128,25 @@ def test_attention_matches_reference(case):
     assert torch.equal(vc, _load(case["name"], "v_after", dt))
     expected = _load(case["name"], "o", dt)
     assert torch.equal(out, expected)
+
+
+FUSED = np.load(GOLDEN / "fused_norm.npz")
+FUSED_CASES = ["w2_t5_h64", "w4_t3_h3584", "w8_t2_h896"]
+
+
+@pytest.mark.parametrize("name", FUSED_CASES)
+def test_fused_add_rms_norm_matches_reference(name):
+    """Rank sum + ``fused_add_rms_norm`` (_qwen2_kernels.py:145-180)."""
+
+    from oracle import tensor_parallel as otp
+
+    partials = torch.from_numpy(FUSED[f"{name}_partials"])
+    residual = torch.from_numpy(FUSED[f"{name}_residual"])
+    weight = torch.from_numpy(FUSED[f"{name}_weight"])
+    eps = float(FUSED[f"{name}_eps"])
+    normed, new_residual = otp.all_reduce_add_rms_norm(list(partials), residual, weight, eps)
+    want_res = torch.from_numpy(FUSED[f"{name}_new_residual"])
+    want_norm = torch.from_numpy(FUSED[f"{name}_normed"])
+    # The residual is the fp16 rounding of an exact fp32 sum of two fp16 values.
+    assert torch.equal(new_residual, want_res.half())
+    assert torch.equal(normed, want_norm.half())
