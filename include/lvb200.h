@@ -253,9 +253,15 @@ LVB_API int lvb_ipc_open(const void *handle, void **ptr);
 LVB_API int lvb_ipc_close(void *ptr);
 LVB_API int lvb_ipc_free(void *ptr);
 
-/* Bytes of one rank's workspace for up to max_tokens rows of `hidden` fp16:
- * 256 bytes of flags, then two staging buffers. */
-LVB_API size_t lvb_allreduce_workspace_bytes(int64_t max_tokens, int64_t hidden);
+/* Bytes of one rank's workspace for a group of `world` ranks and up to
+ * max_tokens rows of `hidden` fp16: a 64 KiB header (epoch, arrival counter,
+ * flags), two parities of `world` staging slots and two gather buffers. */
+LVB_API size_t lvb_allreduce_workspace_bytes(int world, int64_t max_tokens, int64_t hidden);
+
+/* Put a freshly allocated workspace in its initial state (header zeroed,
+ * sentinel buffers filled with 0xFFFF); synchronises the device.  Every rank
+ * initialises its own workspace before the handles are exchanged. */
+LVB_API int lvb_allreduce_workspace_init(void *workspace, int world, int64_t max_tokens, int64_t hidden);
 
 /* Row-parallel epilogue of a Qwen2 block in one launch: h = sum over the
  * world ranks of `partial` (fp32, rounded to fp16 once), v = h + residual
@@ -263,16 +269,25 @@ LVB_API size_t lvb_allreduce_workspace_bytes(int64_t max_tokens, int64_t hidden)
  * weight).  Replaces `all_reduce_sum` (modeling/tensor_parallel.py:18-27,
  * runtime/distributed/distributed.py:190-197, nccl.py:127-139) followed by
  * `fused_add_rms_norm` (modeling/models/_qwen2_kernels.py:20-43, 145-180).
+ * With residual and weight both null it is the plain in-place-capable
+ * all-reduce: out <- h (out may equal partial; eps is ignored).
  * workspaces[r] = rank r's workspace as mapped in this process (own for r ==
- * rank); every rank calls with the same tokens, hidden, max_tokens and epoch,
- * and epoch increases by one per call starting at 1.  Peers are read with
- * plain loads; waits for peers are bounded (on timeout the device error word
- * gets LVB_DEVERR_TIMEOUT and the outputs are left unwritten).  hidden is a
- * multiple of 8 up to 8192; tensors 16-byte aligned; world <= 8. */
+ * rank), each sized for this world; every rank calls with the same tokens,
+ * hidden, max_tokens and mode, in the same order.  The call counter lives in
+ * the workspace, so launches may be captured in a CUDA graph.
+ * mode: 1 one-shot (push every row to every peer, then flags), 2 two-shot
+ * (reduce-scatter + all-gather through peer memory), 3 sentinel one-shot
+ * (pushed data carries its own ready marker: no flags, no fences); 0 picks
+ * 3 for small messages and 2 otherwise.  An fp16 lane equal to 0xFFFF (a
+ * NaN) is pushed as 0xFE00 in mode 3, so NaN payloads are not preserved.  Waits for peers are bounded: on timeout the
+ * device error word gets LVB_DEVERR_TIMEOUT, outputs are left unwritten and
+ * the workspaces must be rebuilt.  hidden is a multiple of 8 up to 8192;
+ * tensors 16-byte aligned; residual must not alias partial or out;
+ * world <= 8. */
 LVB_API int lvb_allreduce_add_rmsnorm(void *const *workspaces, int rank, int world, const uint16_t *partial,
                                       uint16_t *residual, const uint16_t *weight, uint16_t *out,
                                       int64_t tokens, int64_t hidden, int64_t max_tokens, float eps,
-                                      uint32_t epoch, lvb_stream_t stream);
+                                      int mode, lvb_stream_t stream);
 
 #ifdef __cplusplus
 } /* extern "C" */

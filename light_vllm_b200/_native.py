@@ -15,7 +15,7 @@ import functools
 from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().parent / "_lib" / "liblvb200.so"
-ABI_VERSION = 3
+ABI_VERSION = 4
 
 LVB_OK = 0
 LVB_ERR_INVALID = 1
@@ -71,10 +71,11 @@ PROTOTYPES: dict[str, tuple[object, tuple[object, ...]]] = {
     "lvb_ipc_open": (_int, (_c_ptr, ctypes.POINTER(_c_ptr))),
     "lvb_ipc_close": (_int, (_c_ptr,)),
     "lvb_ipc_free": (_int, (_c_ptr,)),
-    "lvb_allreduce_workspace_bytes": (_size, (_i64, _i64)),
+    "lvb_allreduce_workspace_bytes": (_size, (_int, _i64, _i64)),
+    "lvb_allreduce_workspace_init": (_int, (_c_ptr, _int, _i64, _i64)),
     "lvb_allreduce_add_rmsnorm": (
         _int,
-        (_c_ptr, _int, _int, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _i64, _i64, _i64, _f32, ctypes.c_uint32, _c_ptr),
+        (_c_ptr, _int, _int, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _i64, _i64, _i64, _f32, _int, _c_ptr),
     ),
     "lvb_paged_attention": (
         _int,

@@ -131,14 +131,15 @@ class TensorParallelCollectives:
 
 
 class PeerWorkspace:
-    """One peer-readable workspace per rank, mapped by every rank of the group.
+    """One peer-writable workspace per rank, mapped by every rank of the group.
 
     Each rank allocates its workspace with ``lvb_ipc_alloc`` and the ranks
     exchange the CUDA IPC handles over the process group; afterwards
     ``pointers`` holds every rank's workspace as mapped in this process, the
     argument of ``lvb_allreduce_add_rmsnorm``.  All ranks must build and close
     it together (it is a collective).  Without a process group it serves a
-    single rank.
+    single rank.  The call counter lives in the workspace itself, so the
+    launches that use it can be captured in CUDA graphs.
     """
 
     def __init__(self, max_tokens: int, hidden: int, device: torch.device,
@@ -151,18 +152,21 @@ class PeerWorkspace:
         self._native = _native
         self.max_tokens = int(max_tokens)
         self.hidden = int(hidden)
-        self.device = device
+        self.device = torch.device(device)
         self._group = group
         use_dist = distributed and dist.is_initialized()
         self.world_size = dist.get_world_size(group) if use_dist else 1
         self.rank = dist.get_rank(group) if use_dist else 0
-        nbytes = int(self._lib.lvb_allreduce_workspace_bytes(self.max_tokens, self.hidden))
+        nbytes = int(self._lib.lvb_allreduce_workspace_bytes(self.world_size, self.max_tokens, self.hidden))
         if nbytes == 0:
             raise ValueError("invalid all-reduce workspace shape")
+        self.nbytes = nbytes
         own = ctypes.c_void_p()
         handle = ctypes.create_string_buffer(64)
-        with torch.cuda.device(device):
+        with torch.cuda.device(self.device):
             _native.check(self._lib.lvb_ipc_alloc(nbytes, ctypes.byref(own), handle), "lvb_ipc_alloc")
+            _native.check(self._lib.lvb_allreduce_workspace_init(own.value, self.world_size, self.max_tokens,
+                                                                 self.hidden), "lvb_allreduce_workspace_init")
         self._own = own.value
         handles = [handle.raw]
         if self.world_size > 1:
@@ -170,7 +174,7 @@ class PeerWorkspace:
             dist.all_gather_object(handles, handle.raw, group=group)
         pointers = []
         self._opened = []
-        with torch.cuda.device(device):
+        with torch.cuda.device(self.device):
             for r, h in enumerate(handles):
                 if r == self.rank:
                     pointers.append(self._own)
@@ -180,11 +184,6 @@ class PeerWorkspace:
                 pointers.append(ptr.value)
                 self._opened.append(ptr.value)
         self.pointers = (ctypes.c_void_p * self.world_size)(*pointers)
-        self.epoch = 0
-
-    def next_epoch(self) -> int:
-        self.epoch += 1
-        return self.epoch
 
     def close(self) -> None:
         """Unmap the peers' workspaces and free this rank's (collective)."""
@@ -192,6 +191,8 @@ class PeerWorkspace:
         if self._own is None:
             return
         torch.cuda.synchronize(self.device)
+        if self.world_size > 1:
+            dist.barrier(group=self._group)  # no rank still pushes into a workspace
         with torch.cuda.device(self.device):
             for ptr in self._opened:
                 self._native.check(self._lib.lvb_ipc_close(ptr), "lvb_ipc_close")
@@ -203,35 +204,93 @@ class PeerWorkspace:
         self._own = None
 
 
+ALL_REDUCE_AUTO, ALL_REDUCE_ONE_SHOT, ALL_REDUCE_TWO_SHOT, ALL_REDUCE_SENTINEL = 0, 1, 2, 3
+
+
+def _check_rows(workspace: PeerWorkspace, tensor: Tensor, what: str) -> None:
+    if tensor.dim() != 2 or tensor.dtype != torch.float16 or not tensor.is_contiguous():
+        raise ValueError(f"{what} must be a contiguous fp16 [tokens, hidden] tensor")
+    if tensor.device != workspace.device:
+        raise ValueError(f"{what} is on {tensor.device}, the workspace on {workspace.device}")
+    if tensor.shape[1] != workspace.hidden:
+        raise ValueError("hidden size does not match the all-reduce workspace")
+    if tensor.shape[0] > workspace.max_tokens:
+        raise ValueError("more tokens than the all-reduce workspace holds")
+
+
+def _launch(workspace: PeerWorkspace, partial: Tensor, residual: Tensor | None, weight: Tensor | None,
+            out: Tensor, eps: float, mode: int) -> None:
+    from light_vllm_b200 import _native
+
+    _native.check(
+        _native.library().lvb_allreduce_add_rmsnorm(
+            workspace.pointers, workspace.rank, workspace.world_size, partial.data_ptr(),
+            0 if residual is None else residual.data_ptr(), 0 if weight is None else weight.data_ptr(),
+            out.data_ptr(), partial.shape[0], partial.shape[1], workspace.max_tokens, float(eps), int(mode),
+            torch.cuda.current_stream(partial.device).cuda_stream),
+        "lvb_allreduce_add_rmsnorm",
+    )
+
+
 def all_reduce_add_rms_norm(workspace: PeerWorkspace, partial: Tensor, residual: Tensor,
-                            weight: Tensor, eps: float) -> tuple[Tensor, Tensor]:
+                            weight: Tensor, eps: float, *, mode: int = ALL_REDUCE_AUTO) -> tuple[Tensor, Tensor]:
     """Sum ``partial`` over the ranks, add ``residual`` and RMSNorm the result,
     in one sm_100a launch over peer memory (``lvb_allreduce_add_rmsnorm``).
 
     Returns ``(normed, residual)``; ``residual`` is updated in place, like
     ``fused_add_rms_norm`` after ``all_reduce_sum`` in the reference
-    (modeling/models/qwen2.py:497-514, _qwen2_kernels.py:145-180).
+    (modeling/models/qwen2.py:497-514, _qwen2_kernels.py:145-180).  Every rank
+    calls it with the same shapes in the same order.
     """
 
-    from light_vllm_b200 import _native
-
-    if partial.shape != residual.shape or partial.dim() != 2:
-        raise ValueError("partial and residual must be [tokens, hidden] tensors of one shape")
-    if partial.dtype != torch.float16 or residual.dtype != torch.float16 or weight.dtype != torch.float16:
-        raise ValueError("the fused all-reduce normalises fp16 tensors")
-    if partial.shape[1] != workspace.hidden or weight.shape != (workspace.hidden,):
-        raise ValueError("hidden size does not match the all-reduce workspace")
-    if partial.shape[0] > workspace.max_tokens:
-        raise ValueError("more tokens than the all-reduce workspace holds")
-    if not (partial.is_contiguous() and residual.is_contiguous() and weight.is_contiguous()):
-        raise ValueError("the fused all-reduce requires contiguous tensors")
+    _check_rows(workspace, partial, "partial")
+    _check_rows(workspace, residual, "residual")
+    if partial.shape != residual.shape:
+        raise ValueError("partial and residual must have one shape")
+    if residual.data_ptr() == partial.data_ptr():
+        raise ValueError("residual must not alias partial")
+    if weight.dtype != torch.float16 or weight.shape != (workspace.hidden,) or not weight.is_contiguous():
+        raise ValueError("weight must be a contiguous fp16 [hidden] tensor")
     out = torch.empty_like(partial)
-    epoch = workspace.next_epoch()
-    _native.check(
-        _native.library().lvb_allreduce_add_rmsnorm(
-            workspace.pointers, workspace.rank, workspace.world_size, partial.data_ptr(),
-            residual.data_ptr(), weight.data_ptr(), out.data_ptr(), partial.shape[0], partial.shape[1],
-            workspace.max_tokens, float(eps), epoch, torch.cuda.current_stream(partial.device).cuda_stream),
-        "lvb_allreduce_add_rmsnorm",
-    )
+    _launch(workspace, partial, residual, weight, out, eps, mode)
     return out, residual
+
+
+def all_reduce_sum_peer(workspace: PeerWorkspace, tensor: Tensor, *, mode: int = ALL_REDUCE_AUTO) -> Tensor:
+    """In-place fp16 sum over the ranks through peer memory (the contract of
+    ``TensorCollectives.all_reduce_sum``, modeling/tensor_parallel.py:18-27)."""
+
+    _check_rows(workspace, tensor, "tensor")
+    _launch(workspace, tensor, None, None, tensor, 0.0, mode)
+    return tensor
+
+
+class PeerCollectives(TensorParallelCollectives):
+    """``TensorParallelCollectives`` whose fp16 row sums run through the
+    peer-memory kernel, plus the fused ``all_reduce_add_rms_norm`` a Qwen2
+    layer uses after its row-parallel projections.  Tensors the workspace
+    does not cover (other dtypes, wider rows, more tokens) take the NCCL
+    path of the base class."""
+
+    def __init__(self, workspace: PeerWorkspace, group: dist.ProcessGroup | None = None) -> None:
+        super().__init__(group)
+        self.workspace = workspace
+
+    def _covers(self, tensor: Tensor) -> bool:
+        ws = self.workspace
+        return (tensor.dtype == torch.float16 and tensor.is_contiguous() and tensor.dim() >= 1
+                and tensor.shape[-1] == ws.hidden and tensor.numel() // ws.hidden <= ws.max_tokens
+                and tensor.device == ws.device)
+
+    def all_reduce_sum(self, tensor: Tensor) -> Tensor:
+        if not self._covers(tensor):
+            return super().all_reduce_sum(tensor)
+        all_reduce_sum_peer(self.workspace, tensor.view(-1, self.workspace.hidden))
+        return tensor
+
+    def all_reduce_add_rms_norm(self, partial: Tensor, residual: Tensor, weight: Tensor,
+                                eps: float) -> tuple[Tensor, Tensor]:
+        shape = partial.shape
+        out, res = all_reduce_add_rms_norm(self.workspace, partial.view(-1, shape[-1]),
+                                           residual.view(-1, shape[-1]), weight, eps)
+        return out.view(shape), residual

@@ -25,7 +25,7 @@
 
 namespace {
 
-constexpr int kAbiVersion = 3;
+constexpr int kAbiVersion = 4;
 constexpr int kMaxDevices = 64;
 
 thread_local char g_last_error[512] = "";
@@ -957,26 +957,69 @@ int lvb_ipc_free(void *ptr) {
   return e == cudaSuccess ? LVB_OK : cuda_fail(e, "cudaFree (peer workspace)");
 }
 
-size_t lvb_allreduce_workspace_bytes(int64_t max_tokens, int64_t hidden) {
-  if (max_tokens <= 0 || hidden <= 0) return 0;
-  return lvb::ar::kFlagBytes + 2 * static_cast<size_t>(max_tokens) * hidden * 2;
+size_t lvb_allreduce_workspace_bytes(int world, int64_t max_tokens, int64_t hidden) {
+  if (world < 1 || world > lvb::ar::kMaxWorld || max_tokens <= 0 || hidden <= 0) return 0;
+  const size_t slot = static_cast<size_t>(max_tokens) * hidden * 2;
+  return lvb::ar::kHeaderBytes + lvb::ar::slots_per_workspace(world) * slot;
 }
+
+int lvb_allreduce_workspace_init(void *workspace, int world, int64_t max_tokens, int64_t hidden) {
+  const size_t total = lvb_allreduce_workspace_bytes(world, max_tokens, hidden);
+  if (!workspace || total == 0) return fail(LVB_ERR_INVALID, "lvb_allreduce_workspace_init: invalid argument");
+  const size_t slot = static_cast<size_t>(max_tokens) * hidden * 2;
+  uint8_t *base = static_cast<uint8_t *>(workspace);
+  const size_t sentinel_begin = lvb::ar::kHeaderBytes + (2 * static_cast<size_t>(world) + 2) * slot;
+  if (max_tokens > INT_MAX || hidden > lvb::ar::kMaxHidden)
+    return fail(LVB_ERR_INVALID, "lvb_allreduce_workspace_init: shape too large");
+  cudaError_t e = cudaMemset(base, 0, sentinel_begin);
+  if (e == cudaSuccess) e = cudaMemset(base + sentinel_begin, 0xFF, total - sentinel_begin);
+  const uint32_t geometry[4] = {lvb::ar::kMagic, static_cast<uint32_t>(world), static_cast<uint32_t>(max_tokens),
+                                static_cast<uint32_t>(hidden)};
+  if (e == cudaSuccess) e = cudaMemcpy(base + lvb::ar::kGeometryOff, geometry, sizeof(geometry), cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  return e == cudaSuccess ? LVB_OK : cuda_fail(e, "initialising an all-reduce workspace");
+}
+
+namespace {
+
+// CTAs of the all-reduce kernel that fit on the GPU at once (its two-shot
+// phase waits on other CTAs of the same grid).
+int allreduce_capacity(int dev) {
+  static int cached[64] = {0};
+  if (dev >= 0 && dev < 64 && cached[dev] > 0) return cached[dev];
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, lvb::ar::allreduce_add_rmsnorm_kernel,
+                                                    lvb::ar::kThreads, 0) != cudaSuccess || per_sm < 1)
+    per_sm = 1;
+  int cap = sm_count(dev) * per_sm;
+  if (cap > lvb::ar::kMaxBlocks) cap = lvb::ar::kMaxBlocks;
+  if (dev >= 0 && dev < 64) cached[dev] = cap;
+  return cap;
+}
+
+constexpr size_t kOneShotMaxPushBytes = 1u << 20;  // (world - 1) x message bytes
+
+}  // namespace
 
 int lvb_allreduce_add_rmsnorm(void *const *workspaces, int rank, int world, const uint16_t *partial,
                               uint16_t *residual, const uint16_t *weight, uint16_t *out, int64_t tokens,
-                              int64_t hidden, int64_t max_tokens, float eps, uint32_t epoch,
-                              lvb_stream_t stream) {
+                              int64_t hidden, int64_t max_tokens, float eps, int mode, lvb_stream_t stream) {
   if (world < 1 || world > lvb::ar::kMaxWorld || rank < 0 || rank >= world)
     return fail(LVB_ERR_INVALID, "all-reduce rank %d of world %d (at most %d ranks)", rank, world, lvb::ar::kMaxWorld);
   if (tokens < 0 || tokens > max_tokens || hidden <= 0 || hidden % 8 != 0 || hidden > lvb::ar::kMaxHidden)
     return fail(LVB_ERR_INVALID, "all-reduce shape %lld x %lld (workspace rows %lld; hidden a multiple of 8 up to %d)",
                 (long long)tokens, (long long)hidden, (long long)max_tokens, lvb::ar::kMaxHidden);
+  if (mode < lvb::ar::kAuto || mode > lvb::ar::kSentinel) return fail(LVB_ERR_INVALID, "all-reduce mode %d", mode);
   if (tokens == 0) return LVB_OK;
-  if (tokens > INT_MAX) return fail(LVB_ERR_UNSUPPORTED, "token count exceeds int32");
-  if (epoch == 0) return fail(LVB_ERR_INVALID, "all-reduce epochs start at 1");
-  if (!workspaces || !partial || !residual || !weight || !out) return fail(LVB_ERR_INVALID, "all-reduce null pointer argument");
-  if (!aligned16(partial) || !aligned16(residual) || !aligned16(weight) || !aligned16(out))
+  if (tokens > INT_MAX / 8) return fail(LVB_ERR_UNSUPPORTED, "token count too large");
+  if (!workspaces || !partial || !out) return fail(LVB_ERR_INVALID, "all-reduce null pointer argument");
+  if ((residual == nullptr) != (weight == nullptr))
+    return fail(LVB_ERR_INVALID, "residual and weight are given together (norm) or both null (plain sum)");
+  if (!aligned16(partial) || !aligned16(out) || (residual && (!aligned16(residual) || !aligned16(weight))))
     return fail(LVB_ERR_INVALID, "all-reduce tensors must be 16-byte aligned");
+  if (residual && (static_cast<const void *>(residual) == static_cast<const void *>(partial) ||
+                   static_cast<const void *>(residual) == static_cast<const void *>(out)))
+    return fail(LVB_ERR_INVALID, "residual must not alias partial or out");
   lvb::ar::Args a{};
   for (int r = 0; r < world; ++r) {
     if (!workspaces[r] || !aligned16(workspaces[r])) return fail(LVB_ERR_INVALID, "peer workspace %d is null or unaligned", r);
@@ -993,12 +1036,22 @@ int lvb_allreduce_add_rmsnorm(void *const *workspaces, int rank, int world, cons
   a.out = out;
   a.tokens = static_cast<int>(tokens);
   a.hidden = static_cast<int>(hidden);
-  a.buf_bytes = static_cast<size_t>(max_tokens) * hidden * 2;
+  a.slot_bytes = static_cast<size_t>(max_tokens) * hidden * 2;
   a.eps = eps;
-  a.epoch = epoch;
-  // At most one CTA per SM: every CTA must be resident while it waits.
-  const int sms = sm_count(dev);
-  const int grid = tokens < sms ? static_cast<int>(tokens) : sms;
+  const size_t bytes = static_cast<size_t>(tokens) * hidden * 2;
+  if (mode == lvb::ar::kAuto)
+    mode = (world <= 2 || bytes * (world - 1) <= kOneShotMaxPushBytes) ? lvb::ar::kSentinel : lvb::ar::kTwoShot;
+  a.mode = mode;
+  const int cap = allreduce_capacity(dev);
+  int grid;
+  if (mode != lvb::ar::kTwoShot) {
+    grid = tokens < cap ? static_cast<int>(tokens) : cap;
+  } else {
+    const int64_t per_owner_vecs = (tokens * hidden / 8 + world - 1) / world;
+    int64_t want = (per_owner_vecs + lvb::ar::kThreads - 1) / lvb::ar::kThreads;
+    if (want < tokens) want = tokens;
+    grid = want < cap ? static_cast<int>(want) : cap;
+  }
   lvb::ar::allreduce_add_rmsnorm_kernel<<<grid, lvb::ar::kThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "allreduce_add_rmsnorm_kernel launch");

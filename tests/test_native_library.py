@@ -64,3 +64,14 @@ def test_invalid_arguments_are_rejected_before_any_launch():
                                      None, 1, 1, 1, 1, 4, 4, 8, 16, 1, 1.0, 7, None, 0, None)
     assert status == _native.LVB_ERR_INVALID
     assert b"unknown dtype" in lib.lvb_last_error()
+
+
+def test_allreduce_workspace_bytes_cover_every_slot():
+    """Header + 2*world staging + 2 gather + 3*world sentinel slots."""
+
+    lib = _native.library()
+    for world, tokens, hidden in ((1, 8, 256), (2, 512, 3584), (8, 128, 8192)):
+        slot = tokens * hidden * 2
+        assert lib.lvb_allreduce_workspace_bytes(world, tokens, hidden) == 65536 + (5 * world + 2) * slot
+    assert lib.lvb_allreduce_workspace_bytes(9, 8, 256) == 0
+    assert lib.lvb_allreduce_workspace_bytes(2, 0, 256) == 0
