@@ -289,6 +289,30 @@ LVB_API int lvb_allreduce_add_rmsnorm(void *const *workspaces, int rank, int wor
                                       int64_t tokens, int64_t hidden, int64_t max_tokens, float eps,
                                       int mode, lvb_stream_t stream);
 
+/* ------------------------------------------------------------------------ */
+/* Qwen2 element-wise layer steps (fp16)                                     */
+/* ------------------------------------------------------------------------ */
+
+/* Qwen2 half-rotation RoPE, in place on the query heads (columns [0, hq*D))
+ * and key heads (the next hkv*D columns) of each row of the merged QKV
+ * projection: x[i] <- x[i]cos[p][i] - x[i+D/2]sin[p][i], x[i+D/2] <-
+ * x[i+D/2]cos[p][i+D/2] + x[i]sin[p][i+D/2], fp32 arithmetic, p =
+ * positions[t] (int32).  cos/sin are fp16 [table_rows][D] tables.  Replaces
+ * `apply_rotary` (modeling/models/_qwen2_kernels.py:66-133, 205-243).  A
+ * position outside the table sets LVB_DEVERR_INDEX and leaves its row. */
+LVB_API int lvb_rope_qk(uint16_t *qkv, int64_t row_stride, int64_t tokens, int64_t num_query_heads,
+                        int64_t num_kv_heads, int64_t head_size, const int32_t *positions,
+                        const uint16_t *cos_table, const uint16_t *sin_table, int64_t table_rows,
+                        lvb_stream_t stream);
+
+/* out[t][c] = silu(g) * u for g = gate_up[t][c], u = gate_up[t][I + c]
+ * (fp32 arithmetic, one fp16 rounding).  Replaces `silu_and_mul`
+ * (modeling/models/_qwen2_kernels.py:45-64, 183-202) on the merged gate/up
+ * output (qwen2.py:237-247).  I and both row strides are multiples of 8;
+ * tensors 16-byte aligned. */
+LVB_API int lvb_silu_mul(const uint16_t *gate_up, int64_t in_stride, int64_t tokens, int64_t intermediate,
+                         uint16_t *out, int64_t out_stride, lvb_stream_t stream);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

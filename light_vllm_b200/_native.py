@@ -77,6 +77,11 @@ PROTOTYPES: dict[str, tuple[object, tuple[object, ...]]] = {
         _int,
         (_c_ptr, _int, _int, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _i64, _i64, _i64, _f32, _int, _c_ptr),
     ),
+    "lvb_rope_qk": (
+        _int,
+        (_c_ptr, _i64, _i64, _i64, _i64, _i64, _c_ptr, _c_ptr, _c_ptr, _i64, _c_ptr),
+    ),
+    "lvb_silu_mul": (_int, (_c_ptr, _i64, _i64, _i64, _c_ptr, _i64, _c_ptr)),
     "lvb_paged_attention": (
         _int,
         (_c_ptr, _i64, _c_ptr, _c_ptr, _c_ptr, _i64, _c_ptr, _i64, _c_ptr, _c_ptr, _c_ptr, _c_ptr,

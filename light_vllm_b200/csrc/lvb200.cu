@@ -16,6 +16,7 @@
 
 #include "../../include/lvb200.h"
 #include "awq_gemm.cuh"
+#include "qwen2_ops.cuh"
 #include "awq_decode.cuh"
 #include "awq_i8.cuh"
 #include "allreduce.cuh"
@@ -1056,4 +1057,64 @@ int lvb_allreduce_add_rmsnorm(void *const *workspaces, int rank, int world, cons
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "allreduce_add_rmsnorm_kernel launch");
   return LVB_OK;
+}
+
+/* ------------------------------------------------------------------------ */
+/* Qwen2 element-wise layer steps                                            */
+/* ------------------------------------------------------------------------ */
+
+int lvb_rope_qk(uint16_t *qkv, int64_t row_stride, int64_t tokens, int64_t num_query_heads, int64_t num_kv_heads,
+                int64_t head_size, const int32_t *positions, const uint16_t *cos_table, const uint16_t *sin_table,
+                int64_t table_rows, lvb_stream_t stream) {
+  if (tokens < 0 || tokens > INT_MAX || num_query_heads <= 0 || num_kv_heads <= 0 || head_size <= 0 ||
+      head_size % 2 || head_size > 1024 || table_rows <= 0 || table_rows > INT_MAX)
+    return fail(LVB_ERR_INVALID, "rope: invalid shape");
+  if (row_stride < (num_query_heads + num_kv_heads) * head_size)
+    return fail(LVB_ERR_INVALID, "rope: row stride %lld shorter than the query and key heads", (long long)row_stride);
+  if (tokens == 0) return LVB_OK;
+  if (!qkv || !positions || !cos_table || !sin_table) return fail(LVB_ERR_INVALID, "rope: null pointer argument");
+  lvb::q2::RopeArgs a{};
+  a.qkv = qkv;
+  a.row_stride = row_stride;
+  a.positions = positions;
+  a.cos = cos_table;
+  a.sin = sin_table;
+  a.tokens = static_cast<int>(tokens);
+  a.hq = static_cast<int>(num_query_heads);
+  a.hkv = static_cast<int>(num_kv_heads);
+  a.D = static_cast<int>(head_size);
+  a.table_rows = static_cast<int>(table_rows);
+  lvb::q2::rope_qk_kernel<<<static_cast<unsigned>(tokens), lvb::q2::kRopeThreads, 0,
+                            reinterpret_cast<cudaStream_t>(stream)>>>(a);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? LVB_OK : cuda_fail(e, "rope_qk_kernel launch");
+}
+
+int lvb_silu_mul(const uint16_t *gate_up, int64_t in_stride, int64_t tokens, int64_t intermediate, uint16_t *out,
+                 int64_t out_stride, lvb_stream_t stream) {
+  if (tokens < 0 || tokens > INT_MAX || intermediate <= 0 || intermediate % 8 || intermediate > INT_MAX / 2)
+    return fail(LVB_ERR_INVALID, "silu_mul: intermediate size must be a positive multiple of 8");
+  if (in_stride < 2 * intermediate || in_stride % 8 || out_stride < intermediate || out_stride % 8)
+    return fail(LVB_ERR_INVALID, "silu_mul: row strides must cover the rows and be multiples of 8");
+  if (tokens == 0) return LVB_OK;
+  if (!gate_up || !out || !aligned16(gate_up) || !aligned16(out))
+    return fail(LVB_ERR_INVALID, "silu_mul: tensors must be non-null and 16-byte aligned");
+  lvb::q2::SiluArgs a{};
+  a.gate_up = gate_up;
+  a.in_stride = in_stride;
+  a.out = out;
+  a.out_stride = out_stride;
+  a.tokens = static_cast<int>(tokens);
+  a.inter = static_cast<int>(intermediate);
+  int dev = 0;
+  int rc = current_device(&dev);
+  if (rc != LVB_OK) return rc;
+  const int64_t vecs = tokens * (intermediate / 8);
+  int64_t blocks = (vecs + lvb::q2::kSiluThreads - 1) / lvb::q2::kSiluThreads;
+  const int64_t cap = 8LL * sm_count(dev);
+  if (blocks > cap) blocks = cap;
+  lvb::q2::silu_mul_kernel<<<static_cast<unsigned>(blocks), lvb::q2::kSiluThreads, 0,
+                             reinterpret_cast<cudaStream_t>(stream)>>>(a);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? LVB_OK : cuda_fail(e, "silu_mul_kernel launch");
 }

@@ -1,0 +1,89 @@
+// Element-wise steps of a Qwen2 decoder layer that sit between the AWQ
+// projections and the attention on sm_100a:
+//   * rope_qk: Qwen2 half-rotation RoPE applied in place to the query and key
+//     heads of the merged QKV projection output (reference Triton kernel
+//     modeling/models/_qwen2_kernels.py:66-133, called from qwen2.py:411):
+//       out[i]       = x[i] * cos[p][i]       - x[i + D/2] * sin[p][i]
+//       out[i + D/2] = x[i + D/2] * cos[p][i + D/2] + x[i] * sin[p][i + D/2]
+//     in fp32 from fp16 x and fp16 cos/sin tables, stored as fp16.
+//   * silu_mul: act = silu(gate) * up over the merged gate/up output
+//     (reference _qwen2_kernels.py:45-64, 183-202): fp32 arithmetic, one
+//     fp16 rounding.
+// Both are HBM-bound and tiny next to the projections; rows are read and
+// written with 16-byte vectors where the layout allows.
+#pragma once
+
+#include "lvb_common.cuh"
+
+namespace lvb {
+namespace q2 {
+
+constexpr int kRopeThreads = 256;
+constexpr int kSiluThreads = 256;
+
+struct RopeArgs {
+  uint16_t *qkv;          // [tokens][row_stride] fp16; query heads at column 0, key heads after them
+  int64_t row_stride;     // elements
+  const int32_t *positions;
+  const uint16_t *cos, *sin;  // [table_rows][D] fp16
+  int tokens, hq, hkv, D, table_rows;
+};
+
+__global__ void __launch_bounds__(kRopeThreads) rope_qk_kernel(const __grid_constant__ RopeArgs a) {
+  const int t = blockIdx.x;
+  const int pos = a.positions[t];
+  if (pos < 0 || pos >= a.table_rows) {
+    if (threadIdx.x == 0) record_device_error(LVB_DEVERR_INDEX);
+    return;
+  }
+  const int half = a.D / 2;
+  const __half *cs = reinterpret_cast<const __half *>(a.cos) + static_cast<size_t>(pos) * a.D;
+  const __half *sn = reinterpret_cast<const __half *>(a.sin) + static_cast<size_t>(pos) * a.D;
+  __half *row = reinterpret_cast<__half *>(a.qkv) + static_cast<size_t>(t) * a.row_stride;
+  const int units = (a.hq + a.hkv) * half;
+  for (int u = threadIdx.x; u < units; u += kRopeThreads) {
+    const int head = u / half, i = u - head * half;
+    __half *x = row + static_cast<size_t>(head) * a.D;
+    const float x1 = __half2float(x[i]);
+    const float x2 = __half2float(x[i + half]);
+    const float o1 = x1 * __half2float(cs[i]) + (-x2) * __half2float(sn[i]);
+    const float o2 = x2 * __half2float(cs[i + half]) + x1 * __half2float(sn[i + half]);
+    x[i] = __float2half_rn(o1);
+    x[i + half] = __float2half_rn(o2);
+  }
+}
+
+struct SiluArgs {
+  const uint16_t *gate_up;  // [tokens][in_stride]: gate in columns [0, I), up in [I, 2I)
+  int64_t in_stride;
+  uint16_t *out;            // [tokens][out_stride], columns [0, I)
+  int64_t out_stride;
+  int tokens, inter;
+};
+
+__device__ __forceinline__ float silu_mul1(float g, float u) { return g / (1.f + expf(-g)) * u; }
+
+// I % 8 == 0 and 16-byte aligned rows: one 16-byte vector per thread-step.
+__global__ void __launch_bounds__(kSiluThreads) silu_mul_kernel(const __grid_constant__ SiluArgs a) {
+  const int vecs = a.inter / 8;
+  const size_t total = static_cast<size_t>(a.tokens) * vecs;
+  for (size_t i = static_cast<size_t>(blockIdx.x) * kSiluThreads + threadIdx.x; i < total;
+       i += static_cast<size_t>(gridDim.x) * kSiluThreads) {
+    const int t = static_cast<int>(i / vecs), c = static_cast<int>(i - static_cast<size_t>(t) * vecs);
+    const uint4 gv = *reinterpret_cast<const uint4 *>(a.gate_up + static_cast<size_t>(t) * a.in_stride + c * 8);
+    const uint4 uv = *reinterpret_cast<const uint4 *>(a.gate_up + static_cast<size_t>(t) * a.in_stride + a.inter + c * 8);
+    const __half2 *g = reinterpret_cast<const __half2 *>(&gv);
+    const __half2 *u = reinterpret_cast<const __half2 *>(&uv);
+    uint4 ov;
+    __half2 *o = reinterpret_cast<__half2 *>(&ov);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 gf = __half22float2(g[e]), uf = __half22float2(u[e]);
+      o[e] = __floats2half2_rn(silu_mul1(gf.x, uf.x), silu_mul1(gf.y, uf.y));
+    }
+    *reinterpret_cast<uint4 *>(a.out + static_cast<size_t>(t) * a.out_stride + c * 8) = ov;
+  }
+}
+
+}  // namespace q2
+}  // namespace lvb

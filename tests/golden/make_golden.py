@@ -17,6 +17,10 @@ Fixtures:
   paged_attn.npz     TorchPagedAttention outputs and post-write cache contents.
   fused_norm.npz     fused_add_rms_norm outputs after a rank sum of fp16
                      partials (the row-parallel epilogue of a Qwen2 block).
+  qwen2_greedy.npz   a random-init AWQ Qwen2ForCausalLM (Torch AWQ scheme,
+                     TorchPagedAttention, fp16, CPU): its weights, two prompts,
+                     the greedy tokens of a prefill plus 64 decode steps and
+                     the top-2 logit margin of every step.
 """
 
 from __future__ import annotations
@@ -46,6 +50,11 @@ def _import_reference():
     )
     from light_vllm.runtime.execution.paged_cache import PagedKVCache, PagedKVCacheConfig
     from light_vllm.modeling.models._qwen2_kernels import fused_add_rms_norm
+    from light_vllm.modeling.models.interfaces import ForwardBatch
+    from light_vllm.modeling.models.qwen2 import Qwen2Config, Qwen2ForCausalLM
+    from light_vllm.modeling.quantization.awq import AWQConfig, AWQLinearMethod
+    from light_vllm.modeling.quantization.awq_schemes import TorchAWQScheme
+    from light_vllm.modeling.tensor_parallel import TensorParallelContext
 
     return dict(
         AttentionLayerSpec=AttentionLayerSpec,
@@ -57,6 +66,13 @@ def _import_reference():
         PagedKVCache=PagedKVCache,
         PagedKVCacheConfig=PagedKVCacheConfig,
         fused_add_rms_norm=fused_add_rms_norm,
+        ForwardBatch=ForwardBatch,
+        Qwen2Config=Qwen2Config,
+        Qwen2ForCausalLM=Qwen2ForCausalLM,
+        AWQConfig=AWQConfig,
+        AWQLinearMethod=AWQLinearMethod,
+        TorchAWQScheme=TorchAWQScheme,
+        TensorParallelContext=TensorParallelContext,
     )
 
 
@@ -272,6 +288,104 @@ def make_fused_norm(ref) -> None:
     np.savez_compressed(HERE / "fused_norm.npz", **out)
 
 
+QWEN2_TINY = dict(vocab_size=512, hidden_size=256, intermediate_size=512, num_hidden_layers=2,
+                  num_attention_heads=4, num_key_value_heads=2, max_position_embeddings=256,
+                  rms_norm_eps=1e-6, rope_theta=1e6)
+QWEN2_PROMPTS = (7, 12)
+QWEN2_STEPS = 64
+QWEN2_BLOCK = 16
+
+
+QWEN2_SEED = 16
+
+
+def make_qwen2(ref, seed: int = QWEN2_SEED, write: bool = True) -> float:
+    """Greedy decoding of a seeded random-init AWQ Qwen2 through the reference.
+
+    The seed is one whose every step has a top-2 logit margin far above fp16
+    rounding noise, so greedy identity is decided by the arithmetic, not by
+    ties.  Returns that smallest margin.
+    """
+
+    awq = ref["awq"]
+    cfg = ref["Qwen2Config"](**QWEN2_TINY)
+    method = ref["AWQLinearMethod"](ref["AWQConfig"](group_size=128), ref["TorchAWQScheme"]())
+    model = ref["Qwen2ForCausalLM"](cfg, ref["TensorParallelContext"](), method, device="cpu",
+                                    dtype=torch.float16)
+    g = torch.Generator().manual_seed(seed)
+    out: dict[str, np.ndarray] = {}
+    with torch.no_grad():
+        for name, module in model.named_modules():
+            if hasattr(module, "qweight") and hasattr(module, "qzeros"):
+                k, n8 = module.qweight.shape
+                groups = module.qzeros.shape[0]
+                q = torch.randint(0, 16, (k, n8 * 8), generator=g, dtype=torch.int32)
+                z = torch.randint(0, 16, (groups, n8 * 8), generator=g, dtype=torch.int32)
+                module.qweight.copy_(awq.pack_awq(q))
+                module.qzeros.copy_(awq.pack_awq(z))
+                module.scales.copy_((torch.rand(groups, n8 * 8, generator=g) * 0.018 + 0.002).half())
+                if module.bias is not None:
+                    module.bias.copy_((torch.randn(module.bias.shape, generator=g) * 0.1).half())
+            elif name.endswith("layernorm") or name.endswith(".norm"):
+                module.weight.copy_((torch.rand(module.weight.shape, generator=g) + 0.5).half())
+        model.model.embed_tokens.weight.copy_((torch.randn(model.model.embed_tokens.weight.shape,
+                                                           generator=g) * 0.5).half())
+        model.lm_head.weight.copy_((torch.randn(model.lm_head.weight.shape, generator=g) * 0.05).half())
+        for key, tensor in model.state_dict().items():
+            out[f"w:{key}"] = _as_storable(tensor)
+        model.prepare_for_inference()
+
+        spec = model.kv_cache_spec
+        cache = ref["PagedKVCache"](spec, ref["PagedKVCacheConfig"](32, QWEN2_BLOCK, dtype=torch.float16))
+        prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=g) for n in QWEN2_PROMPTS]
+        per_seq = -(-(max(QWEN2_PROMPTS) + QWEN2_STEPS) // QWEN2_BLOCK)
+        tables = tuple(tuple(range(i * per_seq, (i + 1) * per_seq)) for i in range(len(prompts)))
+        QL = ref["QueryLayout"]
+
+        def linear(n):
+            return QL(tuple(-1 if i == 0 else i - 1 for i in range(n)))
+
+        def run(ids, positions, computed, lengths):
+            starts = [0]
+            for n in lengths:
+                starts.append(starts[-1] + n)
+            # A table covers exactly the blocks its tokens use.
+            used = tuple(t[: -(-(c + n) // QWEN2_BLOCK)] for t, c, n in zip(tables, computed, lengths))
+            md = ref["PagedAttentionMetadata"](block_tables=used, num_computed_tokens=tuple(computed),
+                                               query_layouts=tuple(linear(n) for n in lengths))
+            batch = ref["ForwardBatch"](input_ids=torch.tensor(ids, dtype=torch.long),
+                                        positions=torch.tensor(positions, dtype=torch.long),
+                                        query_start_loc=tuple(starts),
+                                        attention=ref["TorchPagedAttention"](cache, md),
+                                        logit_query_indices=tuple(s - 1 for s in starts[1:]))
+            logits = model(batch).logits.float()
+            top2 = logits.topk(2, dim=-1).values
+            return logits.argmax(-1).tolist(), (top2[:, 0] - top2[:, 1]).tolist()
+
+        ids = [t for p in prompts for t in p.tolist()]
+        positions = [i for p in prompts for i in range(len(p))]
+        tokens, margins = [], []
+        nxt, marg = run(ids, positions, [0] * len(prompts), [len(p) for p in prompts])
+        tokens.append(nxt)
+        margins.append(marg)
+        ctx = [len(p) for p in prompts]
+        for _ in range(QWEN2_STEPS):
+            nxt, marg = run(nxt, ctx, ctx, [1] * len(prompts))
+            tokens.append(nxt)
+            margins.append(marg)
+            ctx = [c + 1 for c in ctx]
+    for i, p in enumerate(prompts):
+        out[f"prompt{i}"] = p.numpy().astype(np.int64)
+    out["tables"] = np.asarray(tables, dtype=np.int32)
+    out["tokens"] = np.asarray(tokens, dtype=np.int64)      # [1 + steps, requests]
+    out["margins"] = np.asarray(margins, dtype=np.float32)
+    out["config_json"] = np.frombuffer(json.dumps(dict(QWEN2_TINY, group_size=128, block_size=QWEN2_BLOCK,
+                                                       seed=seed)).encode(), dtype=np.uint8)
+    if write:
+        np.savez_compressed(HERE / "qwen2_greedy.npz", **out)
+    return float(np.min(out["margins"]))
+
+
 def main() -> None:
     torch.set_num_threads(1)
     ref = _import_reference()
@@ -279,7 +393,8 @@ def main() -> None:
     make_meta(ref)
     make_attention(ref)
     make_fused_norm(ref)
-    for name in ("awq_golden.npz", "paged_meta.json", "paged_attn.npz", "fused_norm.npz"):
+    make_qwen2(ref)
+    for name in ("awq_golden.npz", "paged_meta.json", "paged_attn.npz", "fused_norm.npz", "qwen2_greedy.npz"):
         print(name, (HERE / name).stat().st_size, "bytes")
 
 

@@ -150,3 +150,24 @@ def test_fused_add_rms_norm_matches_reference(name):
     # The residual is the fp16 rounding of an exact fp32 sum of two fp16 values.
     assert torch.equal(new_residual, want_res.half())
     assert torch.equal(normed, want_norm.half())
+
+
+def test_qwen2_oracle_greedy_matches_reference():
+    """The oracle decoder reproduces the reference model's greedy tokens:
+    a two-request prefill, then 64 decode steps (tests/golden/qwen2_greedy.npz,
+    written by the reference's Qwen2ForCausalLM with the Torch AWQ scheme)."""
+
+    from oracle.qwen2 import Qwen2Oracle
+
+    d = np.load(GOLDEN / "qwen2_greedy.npz")
+    cfg = json.loads(bytes(d["config_json"]).decode())
+    model = Qwen2Oracle({k[2:]: d[k] for k in d.files if k.startswith("w:")}, cfg)
+    prompts = [d["prompt0"].tolist(), d["prompt1"].tolist()]
+    nxt, _ = model.step([(p, 0) for p in prompts])
+    tokens = [nxt]
+    ctx = [len(p) for p in prompts]
+    for _ in range(len(d["tokens"]) - 1):
+        nxt, _ = model.step([([t], c) for t, c in zip(nxt, ctx)])
+        ctx = [c + 1 for c in ctx]
+        tokens.append(nxt)
+    assert np.array_equal(np.asarray(tokens), d["tokens"])
