@@ -304,6 +304,156 @@ def cpu_baseline(torch, cache, md, q, k, v, ctx, budget_s: float = 20.0) -> dict
 
 
 # ----------------------------------------------------------------------------
+# ----------------------------------------------------------------------------
+# Decode-step detail: the Qwen2 AWQ decoder stack on the B200 kernels
+# ----------------------------------------------------------------------------
+QWEN2_7B = dict(vocab_size=152064, hidden_size=3584, intermediate_size=18944, num_hidden_layers=28,
+                num_attention_heads=28, num_key_value_heads=4, rms_norm_eps=1e-6, rope_theta=1e6)
+# Intermediate 29696 = 29568 padded to 232 groups of 128 so that every TP shard is group-aligned.
+QWEN2_72B = dict(vocab_size=152064, hidden_size=8192, intermediate_size=29696, num_hidden_layers=80,
+                 num_attention_heads=64, num_key_value_heads=8, rms_norm_eps=1e-6, rope_theta=1e6)
+
+
+def decode_case(torch, shape, rank: int, world: int, device, batches, ctx: int, steps: int, warmup: int,
+                dist, random_kv: bool) -> list[dict]:
+    """Greedy decode steps of a random-init AWQ model, replayed from a CUDA
+    graph (one graph per batch size), timed with CUDA events, max over ranks."""
+
+    from light_vllm_b200 import PagedKVCache, PagedKVCacheConfig
+    import gc
+
+    from light_vllm_b200.qwen2 import Qwen2AWQRunner, StaticDecodeAttention, random_shard
+
+    gc.collect()
+    torch.cuda.empty_cache()
+    weights = random_shard(shape, rank, world, device, seed=7)
+    runner = Qwen2AWQRunner(shape, weights, device, rank=rank, world=world, max_tokens=max(batches))
+    del weights
+    torch.cuda.empty_cache()
+    spec = runner.kv_cache_spec().layers[0]
+    kv_token_bytes = 2 * spec.num_kv_heads * spec.head_size * 2 * shape.num_hidden_layers
+    def op_bytes(op):  # packed codes + (scale, zero) words, or the checkpoint tensors
+        if op.groups is not None:
+            return op.qweight.numel() * 4 + op.groups.numel() * op.groups.element_size()
+        return op.qweight.numel() * 4 + op.qzeros.numel() * 4 + op.scales.numel() * 2
+
+    awq_bytes = sum(op_bytes(op) for L in runner.layers for op in (L.qkv, L.o, L.gate_up, L.down))
+    lm_bytes = runner.lm_head.numel() * 2
+    out = []
+    try:
+        for b in batches:
+            per = -(-(ctx + steps + warmup + 2) // 16)
+            cache = PagedKVCache(runner.kv_cache_spec(),
+                                 PagedKVCacheConfig(b * per, 16, dtype=torch.float16, device=device))
+            for L in runner.layers:
+                layer = cache.layer(L.layer_id)
+                if random_kv:
+                    layer.keys.normal_()
+                    layer.values.normal_()
+                else:
+                    layer.keys.zero_()
+                    layer.values.zero_()
+            attention = StaticDecodeAttention(cache, [list(range(i * per, (i + 1) * per)) for i in range(b)],
+                                              [ctx] * b, device)
+            ids = torch.randint(0, shape.vocab_size, (b,), device=device)
+            step = runner.capture_decode(attention, ids)
+            for _ in range(warmup):
+                step.replay()
+            torch.cuda.synchronize()
+            if dist is not None:
+                dist.barrier()
+            ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            stream = torch.cuda.current_stream()
+            ev0.record(stream)
+            for _ in range(steps):
+                step.replay()
+            ev1.record(stream)
+            torch.cuda.synchronize()
+            ms = ev0.elapsed_time(ev1) / steps
+            if dist is not None:
+                t = torch.tensor([ms], device=device)
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+                ms = float(t.item())
+            mean_ctx = ctx + warmup + steps / 2
+            step_bytes = awq_bytes + lm_bytes + b * mean_ctx * kv_token_bytes
+            out.append({"batch": b, "ctx": ctx, "ms_per_step": round(ms, 3), "tok_s": round(b / ms * 1e3, 1),
+                        "bytes_per_step_per_rank": int(step_bytes),
+                        "hbm_gbs_per_rank": round(step_bytes / (ms * 1e-3) / 1e9, 1)})
+            del step, attention, cache
+            torch.cuda.empty_cache()
+    finally:
+        torch.cuda.synchronize()
+        runner.close()
+    return out
+
+
+def decode_cpu_baseline(torch, budget_s: float = 20.0) -> dict:
+    """The reference's CPU Torch path for one 7B decoder layer at batch 1
+    (the Torch AWQ scheme dequantises every weight per call, then an fp16
+    matmul), extrapolated to 28 layers; the lm_head GEMV is timed on an
+    eighth of the vocabulary and scaled."""
+
+    import numpy as np
+
+    from oracle import awq as oawq  # CPU baseline leg only
+
+    torch.manual_seed(0)
+    h, inter, g = QWEN2_7B["hidden_size"], QWEN2_7B["intermediate_size"], 128
+    rng = np.random.default_rng(0)
+
+    def proj(k, n):
+        qw = torch.from_numpy(rng.integers(-2**31, 2**31 - 1, (k, n // 8), dtype=np.int32))
+        qz = torch.from_numpy(rng.integers(-2**31, 2**31 - 1, (k // g, n // 8), dtype=np.int32))
+        sc = torch.rand(k // g, n).mul(0.018).add(0.002).half()
+        return qw, qz, sc
+
+    shapes = [(h, 4608), (h, h), (h, 2 * inter), (inter, h)]
+    weights = [proj(k, n) for k, n in shapes]
+    x = torch.randn(1, h).half()
+    threads = torch.get_num_threads()
+    t0 = time.perf_counter()
+    layers = 0
+    while True:
+        for (k, n), (qw, qz, sc) in zip(shapes, weights):
+            oawq.torch_linear(torch.randn(1, k).half(), qw, qz, sc, g, None)
+        layers += 1
+        if time.perf_counter() - t0 > budget_s / 2 or layers >= 3:
+            break
+    layer_s = (time.perf_counter() - t0) / layers
+    lm = torch.randn(QWEN2_7B["vocab_size"] // 8, h).half()
+    t1 = time.perf_counter()
+    torch.mm(x, lm.t())
+    lm_s = (time.perf_counter() - t1) * 8
+    step_s = 28 * layer_s + lm_s
+    return {"value": round(1.0 / step_s, 4), "unit": "decode tok/s (batch 1)", "cores": threads,
+            "kind": "port", "sample": f"{layers} layer(s) of 7B AWQ projections through the Torch-scheme "
+                                      f"restatement (dequantise per call + fp16 matmul) x 28 layers "
+                                      f"extrapolated, plus the lm_head GEMV on 1/8 of the vocabulary x 8"}
+
+
+def decode_detail(torch, device, rank: int, world: int, dist, steps: int, warmup: int, with_cpu: bool) -> dict:
+    from light_vllm_b200.qwen2 import Qwen2Shape
+
+    steps = max(5, min(steps, 20))
+    cfg3 = decode_case(torch, Qwen2Shape(**QWEN2_7B), rank, world, device, (1, 16, 64), 1024, steps, warmup,
+                       dist, random_kv=True)
+    mem_after_cfg3 = round(torch.cuda.memory_allocated(device) / 1e9, 2)
+    out = {"config3_qwen2.5_7b_awq": {"tp": world, "steps": cfg3, "prompt_tokens": 1024,
+                                      "kv": "fp16 pages N(0,1)", "allocated_gb_after": mem_after_cfg3}}
+    if world > 1:  # BASELINE config 4 is a TP = 2 / 4 / 8 configuration
+        cfg4 = decode_case(torch, Qwen2Shape(**QWEN2_72B), rank, world, device, (128,), 2048,
+                           max(5, steps // 4), warmup, dist, random_kv=False)
+        out["config4_qwen2.5_72b_awq"] = {"tp": world, "steps": cfg4, "prompt_tokens": 2048, "intermediate": 29696,
+                                          "kv": "fp16 pages, zero-filled (timing only)"}
+    out.update({
+           "timing": "one CUDA graph per batch size: embedding, 4 AWQ projections, RoPE, K/V write, paged "
+                     "attention, SiLU-mul, 2 fused all-reduce+add+RMSNorm per layer, lm_head, greedy pick; "
+                     "CUDA events over K replays, max over ranks"})
+    if with_cpu and rank == 0 and world == 1:
+        out["cpu_baseline"] = decode_cpu_baseline(torch)
+    return out
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -311,11 +461,12 @@ def main() -> int:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
     ap.add_argument("--no-awq", action="store_true", help="skip the AWQ detail measurements")
-    ap.add_argument("--only", choices=("all", "attention", "awq"), default="all",
+    ap.add_argument("--only", choices=("all", "attention", "awq", "decode"), default="all",
                     help="run one part (profiling); 'awq' prints only the AWQ detail")
     ap.add_argument("--awq-shapes", default=None,
                     help="AWQ detail shapes as 'm,k,n[;m,k,n...]' (group 128)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline (profiling)")
+    ap.add_argument("--no-decode", action="store_true", help="skip the Qwen2 decode-step detail")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -343,6 +494,13 @@ def main() -> int:
     from light_vllm_b200.paged_attention import B200PagedAttentionBackend
 
     peaks = measured_peaks()
+    if args.only == "decode":
+        detail = decode_detail(torch, device, rank, world, dist, args.steps, args.warmup, with_cpu=not args.no_cpu)
+        if rank == 0:
+            print(json.dumps({"decode": detail}), flush=True)
+        if dist is not None:
+            dist.destroy_process_group()
+        return 0
     if args.only == "awq":
         detail = awq_detail(torch, peaks, args.steps, args.awq_shapes)
         if rank == 0:
@@ -456,9 +614,14 @@ def main() -> int:
         if not args.no_cpu:
             result["cpu_baseline"] = cpu_baseline(torch, cache, md, q, k, v, ctx)
         if not args.no_awq and args.only == "all":
-            del cache
+            cache = step_ctx = None
             torch.cuda.empty_cache()
             result["awq"] = awq_detail(torch, peaks, args.steps, args.awq_shapes)
+    if args.only == "all" and not args.no_decode:
+        cache = step_ctx = step_graph = attn_graph = None
+        torch.cuda.empty_cache()
+        result["decode"] = decode_detail(torch, device, rank, world, dist, args.steps, args.warmup,
+                                         with_cpu=not args.no_cpu)
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()

@@ -41,7 +41,7 @@ from light_vllm_b200 import _native
 _PACK_FACTOR = 8
 # Row counts whose fastest plans the prepared split-K workspace covers (one
 # per token-tile class); other sizes run the best plan that fits in it.
-_SPLIT_K_ROWS = (1, 16, 32, 64, 128, 256)
+_SPLIT_K_ROWS = (1, 2, 4, 16, 32, 64, 128, 256)
 # Storages already repacked in place: (device index, data_ptr, bytes) -> weak
 # reference to a checkpoint tensor over that storage (the model's buffer keeps
 # it alive; the entry dies with it).

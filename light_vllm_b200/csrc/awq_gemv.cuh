@@ -1,0 +1,272 @@
+// W4A16 GEMV for the smallest decode batches (m <= 4) on sm_100a CUDA cores.
+//
+// Reference: the decode-sized path of CudaAWQOperation (M <= 255 -> K1
+// `gemm_forward_4bit_cuda_m16nXk32`, csrc/awq/gemm_kernels.cu:29-326, 444-501,
+// called from modeling/quantization/cuda_awq.py:96-122): y = x @ W (+ bias),
+// W[k][n] = (q - z) * s per 128-k group.  At m <= 4 the tensor cores would
+// multiply mostly padding, so each output column is reduced on CUDA cores
+// with integer dot products, exactly like the int8 tensor-core path:
+//
+//   x is split per (token, group) into two int8 limbs, x = a (x0 + x1 / 128)
+//   with a a power of two (awq_act_limbs_kernel, the same prologue as the
+//   int8 path); for each group
+//     D0 = sum q x0,  D1 = sum q x1          (dp4a, exact in int32)
+//     v  = 128 D0 + D1 - z * sum(128 x0 + x1)  = sum (q - z)(128 x0 + x1)
+//     acc += s * (a / 128) * v               (fp32)
+//
+// Layout: the packed codes of awq_decode.cuh ([n_tile][32-k run][128 columns]
+// [16 B]); within a run, word w masked with 0x0F0F0F0F holds k = 4w + (0, 2,
+// 1, 3) and shifted right by 4 holds k = 16 + 4w + (0, 2, 1, 3) -- the byte
+// order of the limb words, so each (code word, limb word) pair is one dp4a.
+//
+// One consumer thread per output column (4 warps, one 128-column tile) and
+// one producer warp; a CTA covers a range of whole groups (split-K).  The
+// producer streams the range's codes -- contiguous in the packed layout --
+// into a ring of shared-memory stages with bulk async copies (mbarrier
+// complete_tx), starting before the limb prologue has finished; consumers
+// read their column's 16 bytes per run from shared memory and the limbs of
+// the range, staged once, as broadcasts.  Splits combine through per-split
+// fp32 partials and a semaphore: the last CTA of a tile sums them in split
+// order (deterministic), adds the bias and writes y.  Every wait is bounded.
+#pragma once
+
+#include "awq_i8.cuh"
+#include "lvb_common.cuh"
+
+namespace lvb {
+namespace awqg {
+
+constexpr int kThreads = 128;      // consumer threads: one output column each
+constexpr int kCtaThreads = 160;   // + one producer warp
+constexpr int kStageRuns = 4;      // 32-k runs per stage (8 KB of codes)
+constexpr int kStages = 4;
+constexpr int kStageBytes = kStageRuns * 128 * 16;
+constexpr int kLimbBN = 4;         // token rows of the prologue's limb tiles
+constexpr int kMaxM = 4;
+
+struct GemvParams {
+  const uint8_t *qpack;    // [n_tiles][k_chunks][128][16 B]
+  const uint32_t *szpack;  // [n_tiles][groups][128]: scale bits | zero << 16
+  const int8_t *limbs;     // [K/64][2 * kLimbBN][64 B], 64-byte swizzled (awq_act_limbs_kernel<4>)
+  const int2 *scal;        // [groups][kLimbBN]: (bits of a / 128, sum of 128 x0 + x1)
+  const uint16_t *bias;    // may be null
+  uint16_t *y;             // [M][N]
+  uint32_t *semaphores;    // [n_tiles], zero between calls
+  float *partials;         // [n_tiles][splits][M][128]
+  int M, K, N, G;
+  int groups, k_chunks, runs_per_group;
+  int n_tiles, splits, groups_per_split;
+};
+
+// Shared memory: code stages, limb words [MT][2][range_quads] (quad q = k
+// offset 4q, bytes in the (0, 2, 1, 3) order), (a / 128, isum) per
+// [group][MT], then the barriers.
+template <int MT>
+struct GemvSmem {
+  static constexpr size_t kLimbOff = static_cast<size_t>(kStages) * kStageBytes;
+  __host__ __device__ static size_t limb_bytes(int gps, int rpg) { return static_cast<size_t>(MT) * 2 * gps * rpg * 8 * 4; }
+  __host__ __device__ static size_t scal_off(int gps, int rpg) { return kLimbOff + limb_bytes(gps, rpg); }
+  __host__ __device__ static size_t bar_off(int gps, int rpg) { return (scal_off(gps, rpg) + static_cast<size_t>(gps) * MT * 8 + 7) / 8 * 8; }
+  __host__ __device__ static size_t bytes(int gps, int rpg) { return bar_off(gps, rpg) + 2 * kStages * 8 + 16; }
+};
+
+__device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kThreads) : "memory"); }
+
+template <int MT>
+__global__ void __launch_bounds__(kCtaThreads) awq_gemv_kernel(const __grid_constant__ GemvParams p) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  using S = GemvSmem<MT>;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int tile = blockIdx.x, split = blockIdx.y;
+  const int rpg = p.runs_per_group;
+  const int g0 = split * p.groups_per_split;
+  const int g1 = min(p.groups, g0 + p.groups_per_split);
+  const int run0 = g0 * rpg, run1 = g1 * rpg;
+  const int nruns = run1 - run0;
+  const int nstages = (nruns + kStageRuns - 1) / kStageRuns;
+  const int range_quads = nruns * 8;
+  uint32_t *limb_sm = reinterpret_cast<uint32_t *>(smem + S::kLimbOff);
+  int2 *scal_sm = reinterpret_cast<int2 *>(smem + S::scal_off(p.groups_per_split, rpg));
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + S::bar_off(p.groups_per_split, rpg));
+  uint64_t *empty = full + kStages;
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(empty + kStages);
+
+  if (tid == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kThreads / 32);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  if (warp == kThreads / 32) {
+    // Producer: codes do not depend on the limb prologue, so this starts at once.
+    if (lane == 0) {
+      const uint8_t *src = p.qpack + (static_cast<size_t>(tile) * p.k_chunks + run0) * 128 * 16;
+      int issued = 0;
+      for (int st = 0; st < nstages; ++st) {
+        const int slot = st % kStages;
+        if (st >= kStages && !mbar_wait(&empty[slot], ((st / kStages) - 1) & 1, abort_flag)) break;
+        const int runs = min(kStageRuns, nruns - st * kStageRuns);
+        const uint32_t bytes = static_cast<uint32_t>(runs) * 128 * 16;
+        mbar_arrive_expect_tx(&full[slot], bytes);
+        awqd::bulk_load(smem + static_cast<size_t>(slot) * kStageBytes,
+                        src + static_cast<size_t>(st) * kStageBytes, bytes, &full[slot]);
+        issued = st + 1;
+      }
+      // Leave only once every copy issued has landed (shared memory must not
+      // be written after the CTA ends).
+      for (int st = max(0, issued - kStages); st < issued; ++st)
+        mbar_wait(&full[st % kStages], (st / kStages) & 1, nullptr);
+    }
+    return;
+  }
+
+  const uint32_t *szp = p.szpack + (static_cast<size_t>(tile) * p.groups + g0) * kThreads + tid;
+  uint32_t sz = szp[0];
+  uint32_t sz_next = g0 + 1 < g1 ? szp[kThreads] : 0u;
+
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  // Limbs of this range: 16-byte chunks of the swizzled tiles, un-swizzled.
+  {
+    const int chunks_per_row = range_quads / 4;  // 16-byte chunks per (token, limb) row
+    const int total = MT * 2 * chunks_per_row;
+    const int k_base = run0 * 32;
+    for (int i = tid; i < total; i += kThreads) {
+      const int row = i / chunks_per_row;           // t * 2 + limb
+      const int c = i - row * chunks_per_row;
+      const int t = row >> 1, limb = row & 1;
+      const int k = k_base + c * 16;                // 16 k per 16-byte chunk (4 quads)
+      const int trow = limb * kLimbBN + t;          // row of the prologue tile
+      const int8_t *tilep = p.limbs + static_cast<size_t>(k >> 6) * (2 * kLimbBN * 64);
+      const uint4 v = *reinterpret_cast<const uint4 *>(tilep + awqi8::sw64(trow, k & 63));
+      reinterpret_cast<uint4 *>(limb_sm)[static_cast<size_t>(row) * chunks_per_row + c] = v;
+    }
+    for (int i = tid; i < (g1 - g0) * MT; i += kThreads) {
+      const int gg = i / MT, t = i - gg * MT;
+      scal_sm[i] = p.scal[static_cast<size_t>(g0 + gg) * kLimbBN + t];
+    }
+  }
+  consumers_sync();
+
+  float acc[MT];
+  int d0[MT], d1[MT];
+#pragma unroll
+  for (int t = 0; t < MT; ++t) acc[t] = 0.f, d0[t] = 0, d1[t] = 0;
+  int group = g0, run_in_group = 0;
+  bool ok = true;
+
+  for (int st = 0; st < nstages && ok; ++st) {
+    const int slot = st % kStages;
+    if (!mbar_wait(&full[slot], (st / kStages) & 1, abort_flag)) {
+      ok = false;
+      break;
+    }
+    const uint4 *stage = reinterpret_cast<const uint4 *>(smem + static_cast<size_t>(slot) * kStageBytes) + tid;
+    const int runs = min(kStageRuns, nruns - st * kStageRuns);
+#pragma unroll
+    for (int r = 0; r < kStageRuns; ++r) {
+      if (r < runs) {
+        const uint4 c = stage[r * kThreads];
+        const uint32_t w[4] = {c.x, c.y, c.z, c.w};
+        uint32_t lo[4], hi[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          lo[j] = w[j] & 0x0F0F0F0Fu;
+          hi[j] = (w[j] >> 4) & 0x0F0F0F0Fu;
+        }
+        const int q0 = (st * kStageRuns + r) * 8;
+#pragma unroll
+        for (int t = 0; t < MT; ++t) {
+          const uint4 *l0 = reinterpret_cast<const uint4 *>(limb_sm + (static_cast<size_t>(t) * 2) * range_quads + q0);
+          const uint4 *l1 = reinterpret_cast<const uint4 *>(limb_sm + (static_cast<size_t>(t) * 2 + 1) * range_quads + q0);
+          const uint4 a0 = l0[0], b0 = l0[1], a1 = l1[0], b1 = l1[1];
+          int s0 = d0[t], s1 = d1[t];
+          s0 = __dp4a(static_cast<int>(lo[0]), static_cast<int>(a0.x), s0);
+          s0 = __dp4a(static_cast<int>(lo[1]), static_cast<int>(a0.y), s0);
+          s0 = __dp4a(static_cast<int>(lo[2]), static_cast<int>(a0.z), s0);
+          s0 = __dp4a(static_cast<int>(lo[3]), static_cast<int>(a0.w), s0);
+          s0 = __dp4a(static_cast<int>(hi[0]), static_cast<int>(b0.x), s0);
+          s0 = __dp4a(static_cast<int>(hi[1]), static_cast<int>(b0.y), s0);
+          s0 = __dp4a(static_cast<int>(hi[2]), static_cast<int>(b0.z), s0);
+          s0 = __dp4a(static_cast<int>(hi[3]), static_cast<int>(b0.w), s0);
+          s1 = __dp4a(static_cast<int>(lo[0]), static_cast<int>(a1.x), s1);
+          s1 = __dp4a(static_cast<int>(lo[1]), static_cast<int>(a1.y), s1);
+          s1 = __dp4a(static_cast<int>(lo[2]), static_cast<int>(a1.z), s1);
+          s1 = __dp4a(static_cast<int>(lo[3]), static_cast<int>(a1.w), s1);
+          s1 = __dp4a(static_cast<int>(hi[0]), static_cast<int>(b1.x), s1);
+          s1 = __dp4a(static_cast<int>(hi[1]), static_cast<int>(b1.y), s1);
+          s1 = __dp4a(static_cast<int>(hi[2]), static_cast<int>(b1.z), s1);
+          s1 = __dp4a(static_cast<int>(hi[3]), static_cast<int>(b1.w), s1);
+          d0[t] = s0;
+          d1[t] = s1;
+        }
+        if (++run_in_group == rpg) {
+          // Group done: fold the exact integer sums into the fp32 accumulators.
+          const float s = __half2float(__ushort_as_half(static_cast<unsigned short>(sz & 0xFFFFu)));
+          const int z = static_cast<int>(sz >> 16);
+#pragma unroll
+          for (int t = 0; t < MT; ++t) {
+            const int2 sc = scal_sm[(group - g0) * MT + t];
+            const int v = 128 * d0[t] + d1[t] - z * sc.y;
+            acc[t] = fmaf(s * __int_as_float(sc.x), static_cast<float>(v), acc[t]);
+            d0[t] = 0;
+            d1[t] = 0;
+          }
+          ++group;
+          run_in_group = 0;
+          sz = sz_next;
+          if (group + 1 < g1) sz_next = szp[static_cast<size_t>(group + 1 - g0) * kThreads];
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[slot]);
+  }
+  // A wait that gave up raised the abort flag (and set the error word): the
+  // CTA then leaves without output.
+  consumers_sync();
+  if (*abort_flag) return;
+
+  const int n = tile * kThreads + tid;
+  if (p.splits == 1) {
+    const float b = p.bias ? __half2float(__ushort_as_half(p.bias[n])) : 0.f;
+#pragma unroll
+    for (int t = 0; t < MT; ++t)
+      if (t < p.M) p.y[static_cast<size_t>(t) * p.N + n] = __half_as_ushort(__float2half_rn(acc[t] + b));
+    return;
+  }
+  float *part = p.partials + (static_cast<size_t>(tile) * p.splits + split) * p.M * kThreads;
+#pragma unroll
+  for (int t = 0; t < MT; ++t)
+    if (t < p.M) part[static_cast<size_t>(t) * kThreads + tid] = acc[t];
+  __shared__ int last_sm;
+  __threadfence();
+  consumers_sync();
+  if (tid == 0) {
+    const unsigned prev = atomicAdd(p.semaphores + tile, 1u);
+    last_sm = prev == static_cast<unsigned>(p.splits - 1);
+  }
+  consumers_sync();
+  if (!last_sm) return;
+  __threadfence();
+  float sum[MT];
+#pragma unroll
+  for (int t = 0; t < MT; ++t) sum[t] = 0.f;
+  const float *tp = p.partials + static_cast<size_t>(tile) * p.splits * p.M * kThreads;
+  for (int sp = 0; sp < p.splits; ++sp) {
+#pragma unroll
+    for (int t = 0; t < MT; ++t)
+      if (t < p.M) sum[t] += __ldcg(tp + (static_cast<size_t>(sp) * p.M + t) * kThreads + tid);
+  }
+  const float b = p.bias ? __half2float(__ushort_as_half(p.bias[n])) : 0.f;
+#pragma unroll
+  for (int t = 0; t < MT; ++t)
+    if (t < p.M) p.y[static_cast<size_t>(t) * p.N + n] = __half_as_ushort(__float2half_rn(sum[t] + b));
+  if (tid == 0) p.semaphores[tile] = 0u;  // ready for the next call
+}
+
+}  // namespace awqg
+}  // namespace lvb

@@ -16,6 +16,7 @@
 
 #include "../../include/lvb200.h"
 #include "awq_gemm.cuh"
+#include "awq_gemv.cuh"
 #include "qwen2_ops.cuh"
 #include "awq_decode.cuh"
 #include "awq_i8.cuh"
@@ -382,6 +383,120 @@ int launch_awq_i8(const I8Plan &plan, const PackedShape &sh, const uint16_t *x, 
   return LVB_OK;
 }
 
+// ------------------------------------------------------------------------
+// GEMV plan (m <= 4, CUDA-core dp4a over the packed layout)
+// ------------------------------------------------------------------------
+// Measured on B200 (7B gate_up / down / QKV): the GEMV beats the int8
+// tensor-core path at one row only (m = 2..4 run it for shapes the int8 path
+// does not take).
+constexpr int64_t kGemvFastRows = 1;
+
+bool gemv_eligible(int64_t m, int64_t k, int64_t n, int64_t g) {
+  return m >= 1 && m <= lvb::awqg::kMaxM && g % 32 == 0 && k % g == 0 && k % 64 == 0 && n % 128 == 0 &&
+         (m <= kGemvFastRows || !(m <= 32 && (g == 128 || g == 256)));
+}
+
+struct GemvPlan {
+  int mt = 0, splits = 1, gps = 1;
+  size_t smem = 0, sem_bytes = 0, part_bytes = 0, limb_bytes = 0, scal_bytes = 0;
+  size_t total() const { return sem_bytes + part_bytes + limb_bytes + scal_bytes; }
+};
+
+constexpr size_t kGemvMaxSmem = 96 * 1024;
+
+// About four 128-thread CTAs per SM, whole groups per split, shared memory
+// for the split's limbs within kGemvMaxSmem; mt == 0 when the limbs do not fit
+// in `max_ws`.
+GemvPlan gemv_plan(int64_t m, int64_t k, const PackedShape &sh, int64_t g, int sms, size_t max_ws = SIZE_MAX) {
+  GemvPlan p;
+  const int mt = m <= 1 ? 1 : m <= 2 ? 2 : 4;
+  p.limb_bytes = round256(static_cast<size_t>(k) * 2 * lvb::awqg::kLimbBN);
+  p.scal_bytes = round256(static_cast<size_t>(sh.groups) * lvb::awqg::kLimbBN * 8);
+  if (p.limb_bytes + p.scal_bytes > max_ws) return p;
+  const int rpg = static_cast<int>(g / 32);
+  auto smem_of = [&](int gps) {
+    return mt == 1 ? lvb::awqg::GemvSmem<1>::bytes(gps, rpg)
+                   : mt == 2 ? lvb::awqg::GemvSmem<2>::bytes(gps, rpg) : lvb::awqg::GemvSmem<4>::bytes(gps, rpg);
+  };
+  const long long target = 4LL * sms;
+  int splits = static_cast<int>((target + sh.n_tiles - 1) / sh.n_tiles);
+  if (splits < 1) splits = 1;
+  if (splits > sh.groups) splits = sh.groups;
+  int gps = (sh.groups + splits - 1) / splits;
+  while (smem_of(gps) > kGemvMaxSmem && gps > 1) --gps;
+  splits = (sh.groups + gps - 1) / gps;
+  const size_t sem = round256(static_cast<size_t>(sh.n_tiles) * 4);
+  // Fewer splits when the partials do not fit the caller's workspace.
+  while (true) {
+    const size_t part = splits > 1 ? static_cast<size_t>(sh.n_tiles) * splits * m * lvb::awqg::kThreads * 4 : 0;
+    if ((splits > 1 ? sem : 0) + part + p.limb_bytes + p.scal_bytes <= max_ws) {
+      p.part_bytes = part;
+      p.sem_bytes = splits > 1 ? sem : 0;
+      break;
+    }
+    if (splits == 1) return p;
+    const int next_gps = gps + 1;
+    if (smem_of(next_gps) > kGemvMaxSmem) return p;
+    gps = next_gps;
+    splits = (sh.groups + gps - 1) / gps;
+  }
+  p.mt = mt;
+  p.splits = splits;
+  p.gps = gps;
+  p.smem = smem_of(gps);
+  return p;
+}
+
+template <int MT>
+int launch_awq_gemv(const GemvPlan &plan, const PackedShape &sh, const uint16_t *x, const uint8_t *codes,
+                    const uint32_t *groups, const uint16_t *bias, uint16_t *y, int64_t m, int64_t k, int64_t n,
+                    int64_t g, uint8_t *ws, int dev, cudaStream_t stream) {
+  static bool smem_done[kMaxDevices] = {false};
+  auto kernel = lvb::awqg::awq_gemv_kernel<MT>;
+  int rc = ensure_smem(kernel, static_cast<int>(kGemvMaxSmem), dev, smem_done);
+  if (rc != LVB_OK) return rc;
+  int8_t *limbs = reinterpret_cast<int8_t *>(ws + plan.sem_bytes + plan.part_bytes);
+  int2 *scal = reinterpret_cast<int2 *>(ws + plan.sem_bytes + plan.part_bytes + plan.limb_bytes);
+  lvb::awqi8::awq_act_limbs_kernel<lvb::awqg::kLimbBN><<<dim3(sh.groups, lvb::awqg::kLimbBN), 32, 0, stream>>>(
+      x, limbs, scal, static_cast<int>(m), static_cast<int>(k), static_cast<int>(g));
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "awq_act_limbs_kernel launch");
+  lvb::awqg::GemvParams p{};
+  p.qpack = codes;
+  p.szpack = groups;
+  p.limbs = limbs;
+  p.scal = scal;
+  p.bias = bias;
+  p.y = y;
+  p.semaphores = reinterpret_cast<uint32_t *>(ws);
+  p.partials = plan.splits > 1 ? reinterpret_cast<float *>(ws + plan.sem_bytes) : nullptr;
+  p.M = static_cast<int>(m);
+  p.K = static_cast<int>(k);
+  p.N = static_cast<int>(n);
+  p.G = static_cast<int>(g);
+  p.groups = sh.groups;
+  p.k_chunks = sh.k_chunks;
+  p.runs_per_group = static_cast<int>(g / 32);
+  p.n_tiles = sh.n_tiles;
+  p.splits = plan.splits;
+  p.groups_per_split = plan.gps;
+  // A programmatic dependent of the limb kernel: it streams its first codes
+  // while the limbs are computed and waits for them in-kernel.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(sh.n_tiles), static_cast<unsigned>(plan.splits));
+  cfg.blockDim = dim3(lvb::awqg::kCtaThreads);
+  cfg.dynamicSmemBytes = plan.smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, kernel, p);
+  if (e != cudaSuccess) return cuda_fail(e, "awq_gemv_kernel launch");
+  return LVB_OK;
+}
+
 int check_awq_shape(int64_t m, int64_t k, int64_t n, int64_t group_size) {
   if (m < 0 || k <= 0 || n <= 0)
     return fail(LVB_ERR_INVALID, "invalid AWQ shape m=%lld k=%lld n=%lld", (long long)m, (long long)k, (long long)n);
@@ -398,27 +513,34 @@ int check_awq_shape(int64_t m, int64_t k, int64_t n, int64_t group_size) {
 // Attention planning
 // ------------------------------------------------------------------------
 struct DecodePlan {
-  int max_splits, chunk_tokens;
+  int max_splits, chunk_tokens, heads_per_cta;
   size_t o_bytes, lse_bytes, count_bytes;
   size_t total() const { return o_bytes + lse_bytes + count_bytes; }
 };
+
+// Fewest pages one split covers: shorter splits only add merge traffic.
+constexpr int64_t kMinSplitPages = 4;
 
 DecodePlan decode_plan(int64_t num_seqs, int64_t hq, int64_t hkv, int64_t d, int64_t max_seq_len,
                        int sms) {
   DecodePlan p{};
   const int64_t max_pages = (max_seq_len + lvb::attn::kPageTokens - 1) / lvb::attn::kPageTokens;
-  const int64_t hpc = hkv % 4 == 0 ? 4 : hkv % 2 == 0 ? 2 : 1;
+  // Small batches: one KV head per CTA, so (request, head) pairs and their
+  // merges spread over more SMs.
+  const int64_t hpc = num_seqs < 32 ? 1 : hkv % 4 == 0 ? 4 : hkv % 2 == 0 ? 2 : 1;
   const int64_t pairs = num_seqs * (hkv / hpc) > 0 ? num_seqs * (hkv / hpc) : 1;
   const int64_t target = 8LL * sms;  // ~4 waves of 2 CTAs per SM (measured best of 4/8/12/24)
   int64_t splits = (target + pairs - 1) / pairs;
   if (splits < 1) splits = 1;
   if (splits > max_pages) splits = max_pages > 0 ? max_pages : 1;
   if (splits > 256) splits = 256;  // merge weights: (heads per CTA) x splits floats in shared memory
-  const int64_t chunk_pages = (max_pages + splits - 1) / splits > 0 ? (max_pages + splits - 1) / splits : 1;
+  int64_t chunk_pages = (max_pages + splits - 1) / splits > 0 ? (max_pages + splits - 1) / splits : 1;
+  if (chunk_pages < kMinSplitPages) chunk_pages = kMinSplitPages;
   splits = (max_pages + chunk_pages - 1) / chunk_pages;
   if (splits < 1) splits = 1;
   p.max_splits = static_cast<int>(splits);
   p.chunk_tokens = static_cast<int>(chunk_pages * lvb::attn::kPageTokens);
+  p.heads_per_cta = static_cast<int>(hpc);
   p.o_bytes = (static_cast<size_t>(num_seqs * hq * splits * d) * 4 + 255) & ~static_cast<size_t>(255);
   p.lse_bytes = (static_cast<size_t>(num_seqs * hq * splits) * 4 + 255) & ~static_cast<size_t>(255);
   p.count_bytes = (static_cast<size_t>(num_seqs * hkv) * 4 + 255) & ~static_cast<size_t>(255);
@@ -447,12 +569,10 @@ int launch_decode(const lvb::attn::AttnArgs &a, int64_t num_seqs, int64_t num_bl
   return LVB_OK;
 }
 
-int decode_heads_per_cta(int64_t hkv) { return hkv % 4 == 0 ? 4 : hkv % 2 == 0 ? 2 : 1; }
-
 template <bool kBf16, int D>
-int launch_decode_any(const lvb::attn::AttnArgs &a, int64_t num_seqs, int64_t num_blocks, int dev,
-                      cudaStream_t stream) {
-  switch (decode_heads_per_cta(a.Hkv)) {
+int launch_decode_any(const lvb::attn::AttnArgs &a, int heads_per_cta, int64_t num_seqs, int64_t num_blocks,
+                      int dev, cudaStream_t stream) {
+  switch (heads_per_cta) {
     case 4: return launch_decode<kBf16, D, 4>(a, num_seqs, num_blocks, dev, stream);
     case 2: return launch_decode<kBf16, D, 2>(a, num_seqs, num_blocks, dev, stream);
     default: return launch_decode<kBf16, D, 1>(a, num_seqs, num_blocks, dev, stream);
@@ -540,6 +660,10 @@ size_t lvb_awq_workspace_bytes(int64_t m, int64_t k, int64_t n, int64_t group_si
     if (i8_eligible(m, k, n, group_size)) {
       const I8Plan ip = i8_plan(m, k, sh, group_size, sm_count(dev));
       if (ip.total() > need) need = ip.total();
+    }
+    if (gemv_eligible(m, k, n, group_size)) {
+      const GemvPlan gp = gemv_plan(m, k, sh, group_size, sm_count(dev));
+      if (gp.total() > need) need = gp.total();
     }
   }
   return need;
@@ -646,6 +770,15 @@ int lvb_awq_linear_packed(const uint16_t *x, const void *codes, const void *grou
   const PackedShape sh = packed_shape(k, n, group_size);
   const size_t max_ws = workspace != nullptr ? workspace_bytes : 0;
   cudaStream_t stream_ = reinterpret_cast<cudaStream_t>(stream);
+  if (gemv_eligible(m, k, n, group_size)) {
+    const GemvPlan gp = gemv_plan(m, k, sh, group_size, sm_count(dev), max_ws);
+    const uint8_t *c8 = static_cast<const uint8_t *>(codes);
+    const uint32_t *g8 = static_cast<const uint32_t *>(groups);
+    uint8_t *w8 = static_cast<uint8_t *>(workspace);
+    if (gp.mt == 1) return launch_awq_gemv<1>(gp, sh, x, c8, g8, bias, y, m, k, n, group_size, w8, dev, stream_);
+    if (gp.mt == 2) return launch_awq_gemv<2>(gp, sh, x, c8, g8, bias, y, m, k, n, group_size, w8, dev, stream_);
+    if (gp.mt == 4) return launch_awq_gemv<4>(gp, sh, x, c8, g8, bias, y, m, k, n, group_size, w8, dev, stream_);
+  }
   if (i8_eligible(m, k, n, group_size) && aligned16(y)) {  // y is written by TMA stores
     const I8Plan ip = i8_plan(m, k, sh, group_size, sm_count(dev), max_ws);
     const uint8_t *c8 = static_cast<const uint8_t *>(codes);
@@ -816,11 +949,11 @@ int lvb_paged_attention(const uint16_t *query, int64_t query_token_stride,
     a.max_splits = plan.max_splits;
     a.chunk_tokens = plan.chunk_tokens;
     if (bf16) {
-      return head_size == 128 ? launch_decode_any<true, 128>(a, num_seqs, num_blocks, dev, s)
-                              : launch_decode_any<true, 64>(a, num_seqs, num_blocks, dev, s);
+      return head_size == 128 ? launch_decode_any<true, 128>(a, plan.heads_per_cta, num_seqs, num_blocks, dev, s)
+                              : launch_decode_any<true, 64>(a, plan.heads_per_cta, num_seqs, num_blocks, dev, s);
     }
-    return head_size == 128 ? launch_decode_any<false, 128>(a, num_seqs, num_blocks, dev, s)
-                            : launch_decode_any<false, 64>(a, num_seqs, num_blocks, dev, s);
+    return head_size == 128 ? launch_decode_any<false, 128>(a, plan.heads_per_cta, num_seqs, num_blocks, dev, s)
+                            : launch_decode_any<false, 64>(a, plan.heads_per_cta, num_seqs, num_blocks, dev, s);
   }
   return bf16 ? launch_general<true>(a, num_tokens, s) : launch_general<false>(a, num_tokens, s);
 }
@@ -1084,8 +1217,14 @@ int lvb_rope_qk(uint16_t *qkv, int64_t row_stride, int64_t tokens, int64_t num_q
   a.hkv = static_cast<int>(num_kv_heads);
   a.D = static_cast<int>(head_size);
   a.table_rows = static_cast<int>(table_rows);
-  lvb::q2::rope_qk_kernel<<<static_cast<unsigned>(tokens), lvb::q2::kRopeThreads, 0,
-                            reinterpret_cast<cudaStream_t>(stream)>>>(a);
+  const bool vec = head_size % 16 == 0 && row_stride % 8 == 0 && aligned16(qkv) && aligned16(cos_table) &&
+                   aligned16(sin_table);
+  if (vec)
+    lvb::q2::rope_qk_kernel<true><<<static_cast<unsigned>(tokens), lvb::q2::kRopeThreads, 0,
+                                    reinterpret_cast<cudaStream_t>(stream)>>>(a);
+  else
+    lvb::q2::rope_qk_kernel<false><<<static_cast<unsigned>(tokens), lvb::q2::kRopeThreads, 0,
+                                     reinterpret_cast<cudaStream_t>(stream)>>>(a);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? LVB_OK : cuda_fail(e, "rope_qk_kernel launch");
 }

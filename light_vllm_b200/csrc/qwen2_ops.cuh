@@ -29,6 +29,9 @@ struct RopeArgs {
   int tokens, hq, hkv, D, table_rows;
 };
 
+// kVec: 8 pairs per step with 16-byte loads (D % 16 == 0, 16-byte aligned
+// rows and tables); otherwise one pair per step.
+template <bool kVec>
 __global__ void __launch_bounds__(kRopeThreads) rope_qk_kernel(const __grid_constant__ RopeArgs a) {
   const int t = blockIdx.x;
   const int pos = a.positions[t];
@@ -40,16 +43,44 @@ __global__ void __launch_bounds__(kRopeThreads) rope_qk_kernel(const __grid_cons
   const __half *cs = reinterpret_cast<const __half *>(a.cos) + static_cast<size_t>(pos) * a.D;
   const __half *sn = reinterpret_cast<const __half *>(a.sin) + static_cast<size_t>(pos) * a.D;
   __half *row = reinterpret_cast<__half *>(a.qkv) + static_cast<size_t>(t) * a.row_stride;
-  const int units = (a.hq + a.hkv) * half;
-  for (int u = threadIdx.x; u < units; u += kRopeThreads) {
-    const int head = u / half, i = u - head * half;
-    __half *x = row + static_cast<size_t>(head) * a.D;
-    const float x1 = __half2float(x[i]);
-    const float x2 = __half2float(x[i + half]);
-    const float o1 = x1 * __half2float(cs[i]) + (-x2) * __half2float(sn[i]);
-    const float o2 = x2 * __half2float(cs[i + half]) + x1 * __half2float(sn[i + half]);
-    x[i] = __float2half_rn(o1);
-    x[i + half] = __float2half_rn(o2);
+  if constexpr (kVec) {
+    const int per_head = half / 8;
+    const int units = (a.hq + a.hkv) * per_head;
+    for (int u = threadIdx.x; u < units; u += kRopeThreads) {
+      const int head = u / per_head, i = (u - head * per_head) * 8;
+      __half *x = row + static_cast<size_t>(head) * a.D;
+      const uint4 xa = *reinterpret_cast<const uint4 *>(x + i);
+      const uint4 xb = *reinterpret_cast<const uint4 *>(x + i + half);
+      const uint4 ca = *reinterpret_cast<const uint4 *>(cs + i);
+      const uint4 cb = *reinterpret_cast<const uint4 *>(cs + i + half);
+      const uint4 sa = *reinterpret_cast<const uint4 *>(sn + i);
+      const uint4 sb = *reinterpret_cast<const uint4 *>(sn + i + half);
+      const __half *x1 = reinterpret_cast<const __half *>(&xa), *x2 = reinterpret_cast<const __half *>(&xb);
+      const __half *c1 = reinterpret_cast<const __half *>(&ca), *c2 = reinterpret_cast<const __half *>(&cb);
+      const __half *s1 = reinterpret_cast<const __half *>(&sa), *s2 = reinterpret_cast<const __half *>(&sb);
+      uint4 oa, ob;
+      __half *o1 = reinterpret_cast<__half *>(&oa), *o2 = reinterpret_cast<__half *>(&ob);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float v1 = __half2float(x1[e]), v2 = __half2float(x2[e]);
+        o1[e] = __float2half_rn(v1 * __half2float(c1[e]) + (-v2) * __half2float(s1[e]));
+        o2[e] = __float2half_rn(v2 * __half2float(c2[e]) + v1 * __half2float(s2[e]));
+      }
+      *reinterpret_cast<uint4 *>(x + i) = oa;
+      *reinterpret_cast<uint4 *>(x + i + half) = ob;
+    }
+  } else {
+    const int units = (a.hq + a.hkv) * half;
+    for (int u = threadIdx.x; u < units; u += kRopeThreads) {
+      const int head = u / half, i = u - head * half;
+      __half *x = row + static_cast<size_t>(head) * a.D;
+      const float x1 = __half2float(x[i]);
+      const float x2 = __half2float(x[i + half]);
+      const float o1 = x1 * __half2float(cs[i]) + (-x2) * __half2float(sn[i]);
+      const float o2 = x2 * __half2float(cs[i + half]) + x1 * __half2float(sn[i + half]);
+      x[i] = __float2half_rn(o1);
+      x[i + half] = __float2half_rn(o2);
+    }
   }
 }
 

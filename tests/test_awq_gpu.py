@@ -223,9 +223,9 @@ def test_ragged_shapes_keep_the_checkpoint_layout():
     np.testing.assert_array_equal(qw.cpu().numpy(), qweight)
 
 
-@pytest.mark.parametrize("m", [1, 16, 32])
+@pytest.mark.parametrize("m", [5, 16, 32])
 def test_int8_path_with_activation_outliers(m):
-    """Decode batches (m <= 32, group % 64 == 0) run the int8 tensor-core path,
+    """Decode batches (4 < m <= 32, group 128 / 256) run the int8 tensor-core path,
     which splits each (token, group) of x into two int8 limbs under a
     power-of-two scale: rows whose groups mix outliers 300x the typical value
     keep the north-star tolerance (relative to the output scale)."""
@@ -241,6 +241,35 @@ def test_int8_path_with_activation_outliers(m):
     qw, qz, sc, xg = _gpu(qweight, qzeros, scales, x)
     op = B200AWQScheme().prepare(qw, qz, sc, g, None)
     y = op(xg)
+    torch.cuda.synchronize()
+    assert _native.device_error() == 0
+    max_abs, rel = oawq.error_metrics(y.float().cpu().numpy(), expected)
+    scale = float(np.max(np.abs(expected)))
+    assert rel <= REL_L2 and max_abs <= MAX_ABS * max(1.0, scale / 8.0), (m, max_abs, rel, scale)
+
+
+@pytest.mark.parametrize("m", [1, 2, 3, 4])
+@pytest.mark.parametrize("k,n,g", [(896, 4864, 128), (3584, 4608, 128), (18944, 384, 128), (512, 1024, 64),
+                                   (1024, 256, 256), (896, 256, 896)])
+def test_gemv_decode_batches(m, k, n, g):
+    """m <= 4 runs the CUDA-core dp4a GEMV over the packed layout (one split
+    or many, group sizes 64 / 128 / 256 / per column); with and without
+    bias."""
+
+    _check_against_oracle(m, k, n, g, seed=1000 * m + k + n, with_bias=(m % 2 == 1))
+
+
+@pytest.mark.parametrize("m", [1, 4])
+def test_gemv_with_activation_outliers(m):
+    k, n, g = 3584, 512, 128
+    qweight, qzeros, scales = oawq.random_checkpoint(k, n, g, seed=m + 91)
+    rng = np.random.default_rng(m + 9)
+    x = rng.standard_normal((m, k))
+    x[rng.random((m, k)) < 0.01] *= 300.0
+    x = x.astype(np.float16)
+    expected = oawq.linear_fp32(x, qweight, qzeros, scales, g, None)
+    qw, qz, sc, xg = _gpu(qweight, qzeros, scales, x)
+    y = B200AWQScheme().prepare(qw, qz, sc, g, None)(xg)
     torch.cuda.synchronize()
     assert _native.device_error() == 0
     max_abs, rel = oawq.error_metrics(y.float().cpu().numpy(), expected)

@@ -152,3 +152,53 @@ def test_tensor_parallel_greedy_matches_reference(world):
         assert status == "ok", f"rank {r}: {tokens}"
         assert err == 0
         np.testing.assert_array_equal(np.asarray(tokens), d["tokens"])
+
+
+@pytest.mark.parametrize("head_size,hq,hkv,stride_pad", [(128, 28, 4, 0), (64, 4, 2, 0), (80, 8, 2, 0), (128, 7, 1, 8)])
+def test_rope_matches_oracle(head_size, hq, hkv, stride_pad):
+    """lvb_rope_qk against the oracle's half rotation (fp32 from fp16, one
+    rounding): within one fp16 ulp; positions up to the table end."""
+
+    from light_vllm_b200 import _native
+    from oracle.qwen2 import apply_rope, rope_tables
+
+    g = torch.Generator().manual_seed(head_size + hq)
+    tokens = 37
+    width = (hq + 2 * hkv) * head_size + stride_pad
+    qkv = torch.randn(tokens, width, generator=g).half()
+    positions = torch.randint(0, 4096, (tokens,), generator=g, dtype=torch.int32)
+    positions[0] = 4095
+    cos, sin = rope_tables(4096, head_size, 1e6)
+    q = qkv[:, :hq * head_size].reshape(tokens, hq, head_size)
+    k = qkv[:, hq * head_size:(hq + hkv) * head_size].reshape(tokens, hkv, head_size)
+    want_q = apply_rope(q, positions.long(), cos, sin)
+    want_k = apply_rope(k, positions.long(), cos, sin)
+    dev = qkv.cuda()
+    pos_d, cos_d, sin_d = positions.cuda(), cos.cuda(), sin.cuda()  # held until the kernel ran
+    lib = _native.library()
+    _native.check(lib.lvb_rope_qk(dev.data_ptr(), dev.stride(0), tokens, hq, hkv, head_size,
+                                  pos_d.data_ptr(), cos_d.data_ptr(), sin_d.data_ptr(),
+                                  4096, torch.cuda.current_stream().cuda_stream), "rope")
+    got = dev.cpu()
+    torch.cuda.synchronize()
+    assert _native.device_error() == 0
+    for got_part, want in ((got[:, :hq * head_size].reshape(want_q.shape), want_q),
+                           (got[:, hq * head_size:(hq + hkv) * head_size].reshape(want_k.shape), want_k)):
+        ulp = torch.clamp(want.float().abs(), min=2.0**-14) * 2.0**-10
+        assert float(((got_part.float() - want.float()).abs() / ulp).max()) <= 1.0
+    # V columns and padding are untouched
+    assert torch.equal(got[:, (hq + hkv) * head_size:], qkv[:, (hq + hkv) * head_size:])
+
+
+def test_silu_mul_matches_fp32_reference():
+    from light_vllm_b200 import _native
+
+    g = torch.Generator().manual_seed(5)
+    gate_up = (torch.randn(19, 2 * 1024, generator=g) * 3).half()
+    want = (torch.nn.functional.silu(gate_up[:, :1024].float()) * gate_up[:, 1024:].float()).half()
+    dev = gate_up.cuda()
+    out = torch.empty(19, 1024, dtype=torch.float16, device="cuda")
+    _native.check(_native.library().lvb_silu_mul(dev.data_ptr(), dev.stride(0), 19, 1024, out.data_ptr(),
+                                                 out.stride(0), torch.cuda.current_stream().cuda_stream), "silu")
+    ulp = torch.clamp(want.float().abs(), min=2.0**-14) * 2.0**-10
+    assert float(((out.cpu().float() - want.float()).abs() / ulp).max()) <= 1.0
