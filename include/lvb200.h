@@ -281,7 +281,9 @@ LVB_API int lvb_allreduce_workspace_init(void *workspace, int world, int64_t max
  * 3 for small messages and 2 otherwise.  An fp16 lane equal to 0xFFFF (a
  * NaN) is pushed as 0xFE00 in mode 3, so NaN payloads are not preserved.  Waits for peers are bounded: on timeout the
  * device error word gets LVB_DEVERR_TIMEOUT, outputs are left unwritten and
- * the workspaces must be rebuilt.  hidden is a multiple of 8 up to 8192;
+ * the workspaces must be rebuilt.  With world == 1 no workspace is touched
+ * (the plain sum is a copy, or nothing when out == partial; the norm is one
+ * add + RMSNorm launch).  hidden is a multiple of 8 up to 8192;
  * tensors 16-byte aligned; residual must not alias partial or out;
  * world <= 8. */
 LVB_API int lvb_allreduce_add_rmsnorm(void *const *workspaces, int rank, int world, const uint16_t *partial,

@@ -516,5 +516,22 @@ __global__ void __launch_bounds__(kThreads) allreduce_add_rmsnorm_kernel(const _
   }
 }
 
+// One rank: no exchange, no workspace -- residual add + RMSNorm of each row,
+// with every input vector loaded before the first reduction.
+__global__ void __launch_bounds__(kThreads) add_rmsnorm_kernel(const __grid_constant__ Args a) {
+  __shared__ float red[kThreads / 32];
+  const int nvec_row = a.hidden / kVec;
+  const uint4 *partial = reinterpret_cast<const uint4 *>(a.partial);
+  for (int row = blockIdx.x; row < a.tokens; row += gridDim.x) {
+    uint4 hv[kMaxVecsPerThread];
+#pragma unroll
+    for (int j = 0; j < kMaxVecsPerThread; ++j) {
+      const int c = threadIdx.x + j * kThreads;
+      if (c < nvec_row) hv[j] = partial[static_cast<size_t>(row) * nvec_row + c];
+    }
+    finish_row(a, row, hv, red);
+  }
+}
+
 }  // namespace ar
 }  // namespace lvb

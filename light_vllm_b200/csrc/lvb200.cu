@@ -208,9 +208,16 @@ struct PackedPlan {
 // tiles with one accumulator.
 int packed_bn(int64_t m) { return m <= 16 ? 16 : m <= 32 ? 32 : m <= 64 ? 64 : m <= 128 ? 128 : 256; }
 
+// Fixed cost of one CTA (TMEM allocation, pipeline fill and drain, partial
+// tile write and merge) in 64-k blocks of main-loop work; without it the
+// model splits a 4096-deep M = 128 GEMM into 16 CTAs of 4 blocks each and
+// runs 4x slower than with 2 splits (ncu: tensor pipe 5 % active).
+constexpr long long kPackedCtaOverheadBlocks = 8;
+
 // K splits for grids smaller than the SM count: the split count that
-// minimises (waves of CTAs) x (64-k blocks per CTA), fewest splits on ties,
-// among the plans whose split-K workspace fits in `max_ws` bytes.
+// minimises (waves of CTAs) x (64-k blocks per CTA + the per-CTA overhead),
+// fewest splits on ties, among the plans whose split-K workspace fits in
+// `max_ws` bytes.
 PackedPlan packed_plan(int64_t m, const PackedShape &sh, int sms, size_t max_ws = SIZE_MAX) {
   PackedPlan p{};
   p.bn = packed_bn(m);
@@ -225,7 +232,7 @@ PackedPlan packed_plan(int64_t m, const PackedShape &sh, int sms, size_t max_ws 
     if (need > max_ws) continue;
     const long long ctas = tiles * sp;
     const long long waves = (ctas + sms - 1) / sms;
-    const long long cost = waves * ((sh.k_blocks + sp - 1) / sp);
+    const long long cost = waves * ((sh.k_blocks + sp - 1) / sp + kPackedCtaOverheadBlocks);
     if (best_cost < 0 || cost < best_cost) {
       best_cost = cost;
       best = sp;
@@ -519,7 +526,7 @@ struct DecodePlan {
 };
 
 // Fewest pages one split covers: shorter splits only add merge traffic.
-constexpr int64_t kMinSplitPages = 4;
+constexpr int64_t kMinSplitPages = 8;
 
 DecodePlan decode_plan(int64_t num_seqs, int64_t hq, int64_t hkv, int64_t d, int64_t max_seq_len,
                        int sms) {
@@ -1155,6 +1162,32 @@ int lvb_allreduce_add_rmsnorm(void *const *workspaces, int rank, int world, cons
                    static_cast<const void *>(residual) == static_cast<const void *>(out)))
     return fail(LVB_ERR_INVALID, "residual must not alias partial or out");
   lvb::ar::Args a{};
+  if (world == 1) {
+    // No exchange: the sum of one partial is the partial itself.
+    if (residual == nullptr) {
+      if (out == partial) return LVB_OK;
+      cudaError_t e = cudaMemcpyAsync(out, partial, static_cast<size_t>(tokens) * hidden * 2, cudaMemcpyDeviceToDevice,
+                                      reinterpret_cast<cudaStream_t>(stream));
+      return e == cudaSuccess ? LVB_OK : cuda_fail(e, "all-reduce copy (one rank)");
+    }
+    int dev1 = 0;
+    int rc1 = current_device(&dev1);
+    if (rc1 != LVB_OK) return rc1;
+    a.rank = 0;
+    a.world = 1;
+    a.partial = partial;
+    a.residual = residual;
+    a.weight = weight;
+    a.out = out;
+    a.tokens = static_cast<int>(tokens);
+    a.hidden = static_cast<int>(hidden);
+    a.eps = eps;
+    const int cap1 = 8 * sm_count(dev1);
+    const int grid1 = tokens < cap1 ? static_cast<int>(tokens) : cap1;
+    lvb::ar::add_rmsnorm_kernel<<<grid1, lvb::ar::kThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? LVB_OK : cuda_fail(e, "add_rmsnorm_kernel launch");
+  }
   for (int r = 0; r < world; ++r) {
     if (!workspaces[r] || !aligned16(workspaces[r])) return fail(LVB_ERR_INVALID, "peer workspace %d is null or unaligned", r);
     a.ws[r] = static_cast<uint8_t *>(workspaces[r]);

@@ -132,28 +132,44 @@ def test_wait_times_out_when_a_peer_never_arrives(mode):
 
 def test_workspace_geometry_mismatch_is_refused_on_the_device():
     """A call whose world / rows / hidden differ from the workspace's
-    initialisation records LVB_DEVERR_INDEX and touches nothing."""
+    initialisation records LVB_DEVERR_INDEX and touches nothing (two local
+    workspaces play the ranks; the check runs before any peer access)."""
 
     from light_vllm_b200 import _native
 
     lib = _native.library()
-    nbytes = lib.lvb_allreduce_workspace_bytes(1, 8, 256)
-    p = ctypes.c_void_p()
-    _native.check(lib.lvb_ipc_alloc(nbytes, ctypes.byref(p), ctypes.create_string_buffer(64)), "alloc")
+    nbytes = lib.lvb_allreduce_workspace_bytes(2, 8, 256)
+    ptrs = []
+    for _ in range(2):
+        p = ctypes.c_void_p()
+        _native.check(lib.lvb_ipc_alloc(nbytes, ctypes.byref(p), ctypes.create_string_buffer(64)), "alloc")
+        ptrs.append(p.value)
+        _native.check(lib.lvb_allreduce_workspace_init(p.value, 2, 8, 256), "init")
     try:
-        _native.check(lib.lvb_allreduce_workspace_init(p.value, 1, 8, 256), "init")
-        arr = (ctypes.c_void_p * 1)(p.value)
+        arr = (ctypes.c_void_p * 2)(*ptrs)
         partial = torch.ones(8, 256, dtype=torch.float16, device="cuda")
         out = torch.full((8, 256), -7.0, dtype=torch.float16, device="cuda")
-        _native.check(lib.lvb_allreduce_add_rmsnorm(arr, 0, 1, partial.data_ptr(), None, None, out.data_ptr(),
-                                                    8, 256, 16, 0.0, 3, torch.cuda.current_stream().cuda_stream),
+        # max_tokens 4 describes a smaller workspace than the one initialised
+        _native.check(lib.lvb_allreduce_add_rmsnorm(arr, 0, 2, partial.data_ptr(), None, None, out.data_ptr(),
+                                                    4, 256, 4, 0.0, 3, torch.cuda.current_stream().cuda_stream),
                       "launch")
         torch.cuda.synchronize()
         assert _native.device_error() == 2  # LVB_DEVERR_INDEX
         assert bool((out == -7.0).all())
     finally:
         torch.cuda.synchronize()
-        _native.check(lib.lvb_ipc_free(p.value), "free")
+        for p in ptrs:
+            _native.check(lib.lvb_ipc_free(p), "free")
+
+
+def test_single_rank_plain_sum_is_a_copy(workspace):
+    from light_vllm_b200.collectives import all_reduce_sum_peer
+
+    t = torch.randn(5, 3584, device="cuda").half()
+    want = t.clone()
+    all_reduce_sum_peer(workspace, t)
+    torch.cuda.synchronize()
+    assert torch.equal(t, want)
 
 
 def _free_port() -> int:
