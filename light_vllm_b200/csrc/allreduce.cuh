@@ -278,6 +278,7 @@ __device__ __forceinline__ void finish_row(const Args &a, int row, const uint4 (
 }
 
 __global__ void __launch_bounds__(kThreads) allreduce_add_rmsnorm_kernel(const __grid_constant__ Args a) {
+  pdl_entry();
   __shared__ float red[kThreads / 32];
   __shared__ int ok_sm;
   __shared__ uint32_t epoch_sm, stale_rows_sm;
@@ -519,6 +520,7 @@ __global__ void __launch_bounds__(kThreads) allreduce_add_rmsnorm_kernel(const _
 // One rank: no exchange, no workspace -- residual add + RMSNorm of each row,
 // with every input vector loaded before the first reduction.
 __global__ void __launch_bounds__(kThreads) add_rmsnorm_kernel(const __grid_constant__ Args a) {
+  pdl_entry();
   __shared__ float red[kThreads / 32];
   const int nvec_row = a.hidden / kVec;
   const uint4 *partial = reinterpret_cast<const uint4 *>(a.partial);

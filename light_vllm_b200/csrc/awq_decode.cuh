@@ -227,6 +227,7 @@ __device__ __forceinline__ void dequant_run(const uint4 q, uint32_t sz, uint32_t
 template <int BN, int SB, int DG, bool DUAL>
 __global__ void __launch_bounds__(PackedConfig<BN, SB, DG, DUAL>::kThreads, 1)
     awq_packed_kernel(const __grid_constant__ CUtensorMap xmap, const DecodeParams p) {
+  pdl_entry();
   using C = PackedConfig<BN, SB, DG, DUAL>;
   constexpr int kAStages = C::kAStages;
   extern __shared__ __align__(1024) uint8_t smem_raw[];

@@ -145,6 +145,7 @@ __device__ __forceinline__ void load_stage(const Params &p, uint32_t stage, int 
 
 template <int BN>
 __global__ void __launch_bounds__(kThreads, 1) awq_gemm_kernel(const Params p) {
+  pdl_entry();
   using C = Config<BN>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(

@@ -131,8 +131,9 @@ template <int BN>
 __global__ void __launch_bounds__(32) awq_act_limbs_kernel(const uint16_t *__restrict__ x, int8_t *__restrict__ limbs,
                                                            int2 *__restrict__ scal, int M, int K, int G) {
   // The AWQ kernel that reads these limbs may start now and overlap this
-  // grid; it waits for its completion before touching the outputs.
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  // grid; it waits for its completion before touching the outputs.  This
+  // grid waits for the kernel that produced x.
+  pdl_entry();
   const int g = blockIdx.x;
   const int t = blockIdx.y;
   const int lane = threadIdx.x;

@@ -13,6 +13,7 @@
 #include <cstdio>
 #include <cstring>
 #include <mutex>
+#include <utility>
 
 #include "../../include/lvb200.h"
 #include "awq_gemm.cuh"
@@ -73,6 +74,25 @@ int ensure_smem(Kernel kernel, int bytes, int dev, bool *done_flags) {
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
   done_flags[dev] = true;
   return LVB_OK;
+}
+
+// Launch with the programmatic-serialisation attribute: the kernel may start
+// while the previous kernel of the stream finishes (each hot-path kernel
+// begins with pdl_entry(), which waits for it before any dependent access).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       Args &&...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
@@ -158,8 +178,7 @@ int launch_awq(const AwqPlan &plan, const uint16_t *x, const int32_t *qweight,
   p.splits = plan.splits;
   p.n_tiles = plan.n_tiles;
   dim3 grid(plan.n_tiles, plan.m_tiles, plan.splits);
-  kernel<<<grid, lvb::awq::kThreads, C::kSmemBytes, stream>>>(p);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_pdl(kernel, grid, dim3(lvb::awq::kThreads), C::kSmemBytes, stream, p);
   if (e != cudaSuccess) return cuda_fail(e, "awq_gemm_kernel launch");
   return LVB_OK;
 }
@@ -281,8 +300,7 @@ int launch_awq_packed(const PackedPlan &plan, const PackedShape &sh, const uint1
   p.m_tiles = plan.m_tiles;
   p.splits = plan.splits;
   dim3 grid(plan.m_tiles, sh.n_tiles, plan.splits);
-  kernel<<<grid, C::kThreads, C::kSmemBytes, stream>>>(xmap, p);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_pdl(kernel, grid, dim3(C::kThreads), C::kSmemBytes, stream, xmap, p);
   if (e != cudaSuccess) return cuda_fail(e, "awq_packed_kernel launch");
   return LVB_OK;
 }
@@ -341,9 +359,8 @@ int launch_awq_i8(const I8Plan &plan, const PackedShape &sh, const uint16_t *x, 
   if (rc != LVB_OK) return rc;
   int8_t *limbs = reinterpret_cast<int8_t *>(ws + plan.sem_bytes + plan.part_bytes);
   int2 *scal = reinterpret_cast<int2 *>(ws + plan.sem_bytes + plan.part_bytes + plan.limb_bytes);
-  lvb::awqi8::awq_act_limbs_kernel<BN><<<dim3(sh.groups, BN), 32, 0, stream>>>(
-      x, limbs, scal, static_cast<int>(m), static_cast<int>(k), static_cast<int>(g));
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_pdl(lvb::awqi8::awq_act_limbs_kernel<BN>, dim3(sh.groups, BN), dim3(32), 0, stream, x,
+                             limbs, scal, static_cast<int>(m), static_cast<int>(k), static_cast<int>(g));
   if (e != cudaSuccess) return cuda_fail(e, "awq_act_limbs_kernel launch");
   lvb::awqi8::I8Params p{};
   p.qpack = codes;
@@ -464,9 +481,9 @@ int launch_awq_gemv(const GemvPlan &plan, const PackedShape &sh, const uint16_t 
   if (rc != LVB_OK) return rc;
   int8_t *limbs = reinterpret_cast<int8_t *>(ws + plan.sem_bytes + plan.part_bytes);
   int2 *scal = reinterpret_cast<int2 *>(ws + plan.sem_bytes + plan.part_bytes + plan.limb_bytes);
-  lvb::awqi8::awq_act_limbs_kernel<lvb::awqg::kLimbBN><<<dim3(sh.groups, lvb::awqg::kLimbBN), 32, 0, stream>>>(
-      x, limbs, scal, static_cast<int>(m), static_cast<int>(k), static_cast<int>(g));
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_pdl(lvb::awqi8::awq_act_limbs_kernel<lvb::awqg::kLimbBN>, dim3(sh.groups, lvb::awqg::kLimbBN),
+                             dim3(32), 0, stream, x, limbs, scal, static_cast<int>(m), static_cast<int>(k),
+                             static_cast<int>(g));
   if (e != cudaSuccess) return cuda_fail(e, "awq_act_limbs_kernel launch");
   lvb::awqg::GemvParams p{};
   p.qpack = codes;
@@ -570,8 +587,7 @@ int launch_decode(const lvb::attn::AttnArgs &a, int64_t num_seqs, int64_t num_bl
   int rc = ensure_smem(kernel, Cfg::kSmemBytes, dev, smem_done);
   if (rc != LVB_OK) return rc;
   dim3 grid(a.max_splits, a.Hkv / HPC, static_cast<unsigned>(num_seqs));
-  kernel<<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(a);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_pdl(kernel, grid, dim3(Cfg::kThreads), Cfg::kSmemBytes, stream, a);
   if (e != cudaSuccess) return cuda_fail(e, "paged_decode_kernel launch");
   return LVB_OK;
 }
@@ -590,17 +606,17 @@ template <bool kBf16>
 int launch_general(const lvb::attn::AttnArgs &a, int64_t num_tokens, cudaStream_t stream) {
   dim3 grid(static_cast<unsigned>(num_tokens), a.Hq);
   const int dpl = (a.D + 31) / 32;
+  cudaError_t e;
   if (dpl <= 1)
-    lvb::attn::paged_attn_general_kernel<kBf16, 1><<<grid, 128, 0, stream>>>(a);
+    e = launch_pdl(lvb::attn::paged_attn_general_kernel<kBf16, 1>, grid, dim3(128), 0, stream, a);
   else if (dpl == 2)
-    lvb::attn::paged_attn_general_kernel<kBf16, 2><<<grid, 128, 0, stream>>>(a);
+    e = launch_pdl(lvb::attn::paged_attn_general_kernel<kBf16, 2>, grid, dim3(128), 0, stream, a);
   else if (dpl == 3)
-    lvb::attn::paged_attn_general_kernel<kBf16, 3><<<grid, 128, 0, stream>>>(a);
+    e = launch_pdl(lvb::attn::paged_attn_general_kernel<kBf16, 3>, grid, dim3(128), 0, stream, a);
   else if (dpl == 4)
-    lvb::attn::paged_attn_general_kernel<kBf16, 4><<<grid, 128, 0, stream>>>(a);
+    e = launch_pdl(lvb::attn::paged_attn_general_kernel<kBf16, 4>, grid, dim3(128), 0, stream, a);
   else
-    lvb::attn::paged_attn_general_kernel<kBf16, 8><<<grid, 128, 0, stream>>>(a);
-  cudaError_t e = cudaGetLastError();
+    e = launch_pdl(lvb::attn::paged_attn_general_kernel<kBf16, 8>, grid, dim3(128), 0, stream, a);
   if (e != cudaSuccess) return cuda_fail(e, "paged_attn_general_kernel launch");
   return LVB_OK;
 }
@@ -820,8 +836,8 @@ static int kv_write_common(const lvb::attn::KVWriteArgs &a, int dtype, lvb_strea
     return fail(LVB_ERR_INVALID, "K/V tensors and caches must be 16-byte aligned");
   const int chunks = a.Hkv * (a.D / 8);
   const int threads = chunks < 256 ? ((chunks + 31) / 32) * 32 : 256;
-  lvb::attn::paged_kv_write_kernel<<<a.num_tokens, threads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_pdl(lvb::attn::paged_kv_write_kernel, dim3(a.num_tokens), dim3(threads), 0,
+                             reinterpret_cast<cudaStream_t>(stream), a);
   if (e != cudaSuccess) return cuda_fail(e, "paged_kv_write_kernel launch");
   return LVB_OK;
 }
@@ -1184,8 +1200,8 @@ int lvb_allreduce_add_rmsnorm(void *const *workspaces, int rank, int world, cons
     a.eps = eps;
     const int cap1 = 8 * sm_count(dev1);
     const int grid1 = tokens < cap1 ? static_cast<int>(tokens) : cap1;
-    lvb::ar::add_rmsnorm_kernel<<<grid1, lvb::ar::kThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_pdl(lvb::ar::add_rmsnorm_kernel, dim3(grid1), dim3(lvb::ar::kThreads), 0,
+                               reinterpret_cast<cudaStream_t>(stream), a);
     return e == cudaSuccess ? LVB_OK : cuda_fail(e, "add_rmsnorm_kernel launch");
   }
   for (int r = 0; r < world; ++r) {
@@ -1219,8 +1235,8 @@ int lvb_allreduce_add_rmsnorm(void *const *workspaces, int rank, int world, cons
     if (want < tokens) want = tokens;
     grid = want < cap ? static_cast<int>(want) : cap;
   }
-  lvb::ar::allreduce_add_rmsnorm_kernel<<<grid, lvb::ar::kThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_pdl(lvb::ar::allreduce_add_rmsnorm_kernel, dim3(grid), dim3(lvb::ar::kThreads), 0,
+                             reinterpret_cast<cudaStream_t>(stream), a);
   if (e != cudaSuccess) return cuda_fail(e, "allreduce_add_rmsnorm_kernel launch");
   return LVB_OK;
 }
@@ -1252,13 +1268,10 @@ int lvb_rope_qk(uint16_t *qkv, int64_t row_stride, int64_t tokens, int64_t num_q
   a.table_rows = static_cast<int>(table_rows);
   const bool vec = head_size % 16 == 0 && row_stride % 8 == 0 && aligned16(qkv) && aligned16(cos_table) &&
                    aligned16(sin_table);
-  if (vec)
-    lvb::q2::rope_qk_kernel<true><<<static_cast<unsigned>(tokens), lvb::q2::kRopeThreads, 0,
-                                    reinterpret_cast<cudaStream_t>(stream)>>>(a);
-  else
-    lvb::q2::rope_qk_kernel<false><<<static_cast<unsigned>(tokens), lvb::q2::kRopeThreads, 0,
-                                     reinterpret_cast<cudaStream_t>(stream)>>>(a);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = vec ? launch_pdl(lvb::q2::rope_qk_kernel<true>, dim3(static_cast<unsigned>(tokens)),
+                                  dim3(lvb::q2::kRopeThreads), 0, reinterpret_cast<cudaStream_t>(stream), a)
+                      : launch_pdl(lvb::q2::rope_qk_kernel<false>, dim3(static_cast<unsigned>(tokens)),
+                                   dim3(lvb::q2::kRopeThreads), 0, reinterpret_cast<cudaStream_t>(stream), a);
   return e == cudaSuccess ? LVB_OK : cuda_fail(e, "rope_qk_kernel launch");
 }
 
@@ -1285,8 +1298,7 @@ int lvb_silu_mul(const uint16_t *gate_up, int64_t in_stride, int64_t tokens, int
   int64_t blocks = (vecs + lvb::q2::kSiluThreads - 1) / lvb::q2::kSiluThreads;
   const int64_t cap = 8LL * sm_count(dev);
   if (blocks > cap) blocks = cap;
-  lvb::q2::silu_mul_kernel<<<static_cast<unsigned>(blocks), lvb::q2::kSiluThreads, 0,
-                             reinterpret_cast<cudaStream_t>(stream)>>>(a);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_pdl(lvb::q2::silu_mul_kernel, dim3(static_cast<unsigned>(blocks)),
+                             dim3(lvb::q2::kSiluThreads), 0, reinterpret_cast<cudaStream_t>(stream), a);
   return e == cudaSuccess ? LVB_OK : cuda_fail(e, "silu_mul_kernel launch");
 }

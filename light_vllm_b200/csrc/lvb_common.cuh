@@ -36,6 +36,23 @@ __device__ __forceinline__ uint32_t smem_u32(const void *p) {
 }
 
 // ------------------------------------------------------------------------
+// Programmatic dependent launch.  Every hot-path kernel is launched with the
+// programmatic-serialisation attribute and starts with pdl_entry(): the next
+// kernel of the stream may launch as soon as every CTA of this one has
+// started (its launch overlaps this kernel's tail), and this kernel waits for
+// the previous one to complete and flush before any access that may depend
+// on it.  Without the attribute both instructions are no-ops.
+// ------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_entry() {
+  pdl_launch_dependents();
+  pdl_wait();
+}
+
+// ------------------------------------------------------------------------
 // mbarrier
 // ------------------------------------------------------------------------
 __device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {

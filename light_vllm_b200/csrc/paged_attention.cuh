@@ -52,6 +52,7 @@ struct KVWriteArgs {
 };
 
 __global__ void paged_kv_write_kernel(const KVWriteArgs a) {
+  pdl_entry();
   const int t = blockIdx.x;
   int64_t slot;
   if (a.slots != nullptr) {
@@ -119,6 +120,7 @@ __device__ __forceinline__ float warp_sum(float v) {
 // ------------------------------------------------------------------------
 template <bool kBf16, int DPL>
 __global__ void __launch_bounds__(128) paged_attn_general_kernel(const AttnArgs a) {
+  pdl_entry();
   constexpr int kWarps = 4;
   __shared__ float q_sm[32 * DPL];
   __shared__ float m_sm[kWarps];
@@ -240,6 +242,7 @@ struct DecodeCfg {
 template <bool kBf16, int D, int HPC>
 __global__ void __launch_bounds__(DecodeCfg<D, HPC>::kThreads, 2)
     paged_decode_kernel(const AttnArgs a) {
+  pdl_entry();
   using Cfg = DecodeCfg<D, HPC>;
   constexpr int kStages = Cfg::kStages;
   constexpr int kSteps = D / 16;  // k-steps of QK^T, and dim pairs of PV

@@ -33,6 +33,7 @@ struct RopeArgs {
 // rows and tables); otherwise one pair per step.
 template <bool kVec>
 __global__ void __launch_bounds__(kRopeThreads) rope_qk_kernel(const __grid_constant__ RopeArgs a) {
+  pdl_entry();
   const int t = blockIdx.x;
   const int pos = a.positions[t];
   if (pos < 0 || pos >= a.table_rows) {
@@ -96,6 +97,7 @@ __device__ __forceinline__ float silu_mul1(float g, float u) { return g / (1.f +
 
 // I % 8 == 0 and 16-byte aligned rows: one 16-byte vector per thread-step.
 __global__ void __launch_bounds__(kSiluThreads) silu_mul_kernel(const __grid_constant__ SiluArgs a) {
+  pdl_entry();
   const int vecs = a.inter / 8;
   const size_t total = static_cast<size_t>(a.tokens) * vecs;
   for (size_t i = static_cast<size_t>(blockIdx.x) * kSiluThreads + threadIdx.x; i < total;
