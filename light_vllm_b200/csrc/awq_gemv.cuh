@@ -60,14 +60,18 @@ struct GemvParams {
 
 // Shared memory: code stages, limb words [MT][2][range_quads] (quad q = k
 // offset 4q, bytes in the (0, 2, 1, 3) order), (a / 128, isum) per
-// [group][MT], then the barriers.
+// [group][MT], the range's (scale, zero) words [group][128], then the
+// barriers (full[kStages], empty[kStages], sz) and the abort flag.
 template <int MT>
 struct GemvSmem {
   static constexpr size_t kLimbOff = static_cast<size_t>(kStages) * kStageBytes;
   __host__ __device__ static size_t limb_bytes(int gps, int rpg) { return static_cast<size_t>(MT) * 2 * gps * rpg * 8 * 4; }
   __host__ __device__ static size_t scal_off(int gps, int rpg) { return kLimbOff + limb_bytes(gps, rpg); }
-  __host__ __device__ static size_t bar_off(int gps, int rpg) { return (scal_off(gps, rpg) + static_cast<size_t>(gps) * MT * 8 + 7) / 8 * 8; }
-  __host__ __device__ static size_t bytes(int gps, int rpg) { return bar_off(gps, rpg) + 2 * kStages * 8 + 16; }
+  __host__ __device__ static size_t sz_off(int gps, int rpg) {
+    return (scal_off(gps, rpg) + static_cast<size_t>(gps) * MT * 8 + 15) / 16 * 16;
+  }
+  __host__ __device__ static size_t bar_off(int gps, int rpg) { return sz_off(gps, rpg) + static_cast<size_t>(gps) * kThreads * 4; }
+  __host__ __device__ static size_t bytes(int gps, int rpg) { return bar_off(gps, rpg) + (2 * kStages + 1) * 8 + 16; }
 };
 
 __device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kThreads) : "memory"); }
@@ -87,15 +91,18 @@ __global__ void __launch_bounds__(kCtaThreads) awq_gemv_kernel(const __grid_cons
   const int range_quads = nruns * 8;
   uint32_t *limb_sm = reinterpret_cast<uint32_t *>(smem + S::kLimbOff);
   int2 *scal_sm = reinterpret_cast<int2 *>(smem + S::scal_off(p.groups_per_split, rpg));
+  const uint32_t *sz_sm = reinterpret_cast<const uint32_t *>(smem + S::sz_off(p.groups_per_split, rpg));
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + S::bar_off(p.groups_per_split, rpg));
   uint64_t *empty = full + kStages;
-  volatile int *abort_flag = reinterpret_cast<volatile int *>(empty + kStages);
+  uint64_t *sz_bar = empty + kStages;
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(sz_bar + 1);
 
   if (tid == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kThreads / 32);
     }
+    mbar_init(sz_bar, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -104,6 +111,11 @@ __global__ void __launch_bounds__(kCtaThreads) awq_gemv_kernel(const __grid_cons
   if (warp == kThreads / 32) {
     // Producer: codes do not depend on the limb prologue, so this starts at once.
     if (lane == 0) {
+      // The range's (scale, zero) rows are contiguous: one copy.
+      const uint32_t sz_bytes = static_cast<uint32_t>(g1 - g0) * kThreads * 4;
+      mbar_arrive_expect_tx(sz_bar, sz_bytes);
+      awqd::bulk_load(smem + S::sz_off(p.groups_per_split, rpg),
+                      p.szpack + (static_cast<size_t>(tile) * p.groups + g0) * kThreads, sz_bytes, sz_bar);
       const uint8_t *src = p.qpack + (static_cast<size_t>(tile) * p.k_chunks + run0) * 128 * 16;
       int issued = 0;
       for (int st = 0; st < nstages; ++st) {
@@ -120,13 +132,10 @@ __global__ void __launch_bounds__(kCtaThreads) awq_gemv_kernel(const __grid_cons
       // be written after the CTA ends).
       for (int st = max(0, issued - kStages); st < issued; ++st)
         mbar_wait(&full[st % kStages], (st / kStages) & 1, nullptr);
+      mbar_wait(sz_bar, 0, nullptr);
     }
     return;
   }
-
-  const uint32_t *szp = p.szpack + (static_cast<size_t>(tile) * p.groups + g0) * kThreads + tid;
-  uint32_t sz = szp[0];
-  uint32_t sz_next = g0 + 1 < g1 ? szp[kThreads] : 0u;
 
   asm volatile("griddepcontrol.wait;" ::: "memory");
   // Limbs of this range: 16-byte chunks of the swizzled tiles, un-swizzled.
@@ -156,7 +165,7 @@ __global__ void __launch_bounds__(kCtaThreads) awq_gemv_kernel(const __grid_cons
 #pragma unroll
   for (int t = 0; t < MT; ++t) acc[t] = 0.f, d0[t] = 0, d1[t] = 0;
   int group = g0, run_in_group = 0;
-  bool ok = true;
+  bool ok = mbar_wait(sz_bar, 0, abort_flag);
 
   for (int st = 0; st < nstages && ok; ++st) {
     const int slot = st % kStages;
@@ -205,6 +214,7 @@ __global__ void __launch_bounds__(kCtaThreads) awq_gemv_kernel(const __grid_cons
         }
         if (++run_in_group == rpg) {
           // Group done: fold the exact integer sums into the fp32 accumulators.
+          const uint32_t sz = sz_sm[(group - g0) * kThreads + tid];
           const float s = __half2float(__ushort_as_half(static_cast<unsigned short>(sz & 0xFFFFu)));
           const int z = static_cast<int>(sz >> 16);
 #pragma unroll
@@ -217,8 +227,6 @@ __global__ void __launch_bounds__(kCtaThreads) awq_gemv_kernel(const __grid_cons
           }
           ++group;
           run_in_group = 0;
-          sz = sz_next;
-          if (group + 1 < g1) sz_next = szp[static_cast<size_t>(group + 1 - g0) * kThreads];
         }
       }
     }

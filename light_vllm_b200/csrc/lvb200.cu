@@ -542,8 +542,13 @@ struct DecodePlan {
   size_t total() const { return o_bytes + lse_bytes + count_bytes; }
 };
 
-// Fewest pages one split covers: shorter splits only add merge traffic.
-constexpr int64_t kMinSplitPages = 8;
+// Fewest pages one split covers (shorter splits only add merge traffic):
+// measured best on B200 at 8 pages for small batches and 16 from 32 requests
+// up (B = 64, ctx 1024: 38.5 -> 34.1 us).
+constexpr int64_t kMinSplitPagesSmall = 8;
+constexpr int64_t kMinSplitPagesLarge = 16;
+// Batches below this many requests run one KV head per CTA.
+constexpr int64_t kAttnSmallBatch = 32;
 
 DecodePlan decode_plan(int64_t num_seqs, int64_t hq, int64_t hkv, int64_t d, int64_t max_seq_len,
                        int sms) {
@@ -551,7 +556,7 @@ DecodePlan decode_plan(int64_t num_seqs, int64_t hq, int64_t hkv, int64_t d, int
   const int64_t max_pages = (max_seq_len + lvb::attn::kPageTokens - 1) / lvb::attn::kPageTokens;
   // Small batches: one KV head per CTA, so (request, head) pairs and their
   // merges spread over more SMs.
-  const int64_t hpc = num_seqs < 32 ? 1 : hkv % 4 == 0 ? 4 : hkv % 2 == 0 ? 2 : 1;
+  const int64_t hpc = num_seqs < kAttnSmallBatch ? 1 : hkv % 4 == 0 ? 4 : hkv % 2 == 0 ? 2 : 1;
   const int64_t pairs = num_seqs * (hkv / hpc) > 0 ? num_seqs * (hkv / hpc) : 1;
   const int64_t target = 8LL * sms;  // ~4 waves of 2 CTAs per SM (measured best of 4/8/12/24)
   int64_t splits = (target + pairs - 1) / pairs;
@@ -559,7 +564,8 @@ DecodePlan decode_plan(int64_t num_seqs, int64_t hq, int64_t hkv, int64_t d, int
   if (splits > max_pages) splits = max_pages > 0 ? max_pages : 1;
   if (splits > 256) splits = 256;  // merge weights: (heads per CTA) x splits floats in shared memory
   int64_t chunk_pages = (max_pages + splits - 1) / splits > 0 ? (max_pages + splits - 1) / splits : 1;
-  if (chunk_pages < kMinSplitPages) chunk_pages = kMinSplitPages;
+  const int64_t min_pages = num_seqs < kAttnSmallBatch ? kMinSplitPagesSmall : kMinSplitPagesLarge;
+  if (chunk_pages < min_pages) chunk_pages = min_pages;
   splits = (max_pages + chunk_pages - 1) / chunk_pages;
   if (splits < 1) splits = 1;
   p.max_splits = static_cast<int>(splits);
