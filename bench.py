@@ -434,17 +434,39 @@ def decode_cpu_baseline(torch, budget_s: float = 20.0) -> dict:
 def decode_detail(torch, device, rank: int, world: int, dist, steps: int, warmup: int, with_cpu: bool) -> dict:
     from light_vllm_b200.qwen2 import Qwen2Shape
 
+    from light_vllm_b200.qwen2 import RankLayout
+
+    def tp_layout_error(shape) -> str | None:
+        try:
+            RankLayout.of(shape, 0, world)
+        except ValueError as exc:
+            return str(exc)
+        if (shape.intermediate_size // world) % shape.group_size:
+            return "per-rank intermediate size is not a multiple of the AWQ group"
+        return None
+
     steps = max(5, min(steps, 20))
-    cfg3 = decode_case(torch, Qwen2Shape(**QWEN2_7B), rank, world, device, (1, 16, 64), 1024, steps, warmup,
-                       dist, random_kv=True)
-    mem_after_cfg3 = round(torch.cuda.memory_allocated(device) / 1e9, 2)
-    out = {"config3_qwen2.5_7b_awq": {"tp": world, "steps": cfg3, "prompt_tokens": 1024,
-                                      "kv": "fp16 pages N(0,1)", "allocated_gb_after": mem_after_cfg3}}
+    out = {}
+    shape3 = Qwen2Shape(**QWEN2_7B)
+    why = tp_layout_error(shape3)
+    if why is None:
+        cfg3 = decode_case(torch, shape3, rank, world, device, (1, 16, 64), 1024, steps, warmup, dist,
+                           random_kv=True)
+        out["config3_qwen2.5_7b_awq"] = {"tp": world, "steps": cfg3, "prompt_tokens": 1024,
+                                         "kv": "fp16 pages N(0,1)",
+                                         "allocated_gb_after": round(torch.cuda.memory_allocated(device) / 1e9, 2)}
+    else:
+        out["config3_qwen2.5_7b_awq"] = {"tp": world, "skipped": f"no TP={world} layout: {why}"}
     if world > 1:  # BASELINE config 4 is a TP = 2 / 4 / 8 configuration
-        cfg4 = decode_case(torch, Qwen2Shape(**QWEN2_72B), rank, world, device, (128,), 2048,
-                           max(5, steps // 4), warmup, dist, random_kv=False)
-        out["config4_qwen2.5_72b_awq"] = {"tp": world, "steps": cfg4, "prompt_tokens": 2048, "intermediate": 29696,
-                                          "kv": "fp16 pages, zero-filled (timing only)"}
+        shape4 = Qwen2Shape(**QWEN2_72B)
+        why = tp_layout_error(shape4)
+        if why is None:
+            cfg4 = decode_case(torch, shape4, rank, world, device, (128,), 2048, max(5, steps // 4), warmup, dist,
+                               random_kv=False)
+            out["config4_qwen2.5_72b_awq"] = {"tp": world, "steps": cfg4, "prompt_tokens": 2048,
+                                              "intermediate": 29696, "kv": "fp16 pages, zero-filled (timing only)"}
+        else:
+            out["config4_qwen2.5_72b_awq"] = {"tp": world, "skipped": f"no TP={world} layout: {why}"}
     out.update({
            "timing": "one CUDA graph per batch size: embedding, 4 AWQ projections, RoPE, K/V write, paged "
                      "attention, SiLU-mul, 2 fused all-reduce+add+RMSNorm per layer, lm_head, greedy pick; "
