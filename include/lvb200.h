@@ -278,7 +278,9 @@ LVB_API int lvb_allreduce_workspace_init(void *workspace, int world, int64_t max
  * mode: 1 one-shot (push every row to every peer, then flags), 2 two-shot
  * (reduce-scatter + all-gather through peer memory), 3 sentinel one-shot
  * (pushed data carries its own ready marker: no flags, no fences); 0 picks
- * 3 for small messages and 2 otherwise.  An fp16 lane equal to 0xFFFF (a
+ * 3 while (world - 1) x message bytes <= 16 MiB and 2 beyond (callers with
+ * a library all-reduce at hand do better with it there: see
+ * lvb_allreduce_peer_max_bytes).  An fp16 lane equal to 0xFFFF (a
  * NaN) is pushed as 0xFE00 in mode 3, so NaN payloads are not preserved.  Waits for peers are bounded: on timeout the
  * device error word gets LVB_DEVERR_TIMEOUT, outputs are left unwritten and
  * the workspaces must be rebuilt.  With world == 1 no workspace is touched
@@ -286,6 +288,11 @@ LVB_API int lvb_allreduce_workspace_init(void *workspace, int world, int64_t max
  * add + RMSNorm launch).  hidden is a multiple of 8 up to 8192;
  * tensors 16-byte aligned; residual must not alias partial or out;
  * world <= 8. */
+/* Message bytes per rank up to which the peer-memory kernel beats a ring
+ * all-reduce at this world size (larger messages: NCCL in place, then this
+ * entry point with world = 1 for the add + RMSNorm). */
+LVB_API size_t lvb_allreduce_peer_max_bytes(int world);
+
 LVB_API int lvb_allreduce_add_rmsnorm(void *const *workspaces, int rank, int world, const uint16_t *partial,
                                       uint16_t *residual, const uint16_t *weight, uint16_t *out,
                                       int64_t tokens, int64_t hidden, int64_t max_tokens, float eps,

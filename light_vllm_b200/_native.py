@@ -73,6 +73,7 @@ PROTOTYPES: dict[str, tuple[object, tuple[object, ...]]] = {
     "lvb_ipc_free": (_int, (_c_ptr,)),
     "lvb_allreduce_workspace_bytes": (_size, (_int, _i64, _i64)),
     "lvb_allreduce_workspace_init": (_int, (_c_ptr, _int, _i64, _i64)),
+    "lvb_allreduce_peer_max_bytes": (_size, (_int,)),
     "lvb_allreduce_add_rmsnorm": (
         _int,
         (_c_ptr, _int, _int, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _i64, _i64, _i64, _f32, _int, _c_ptr),

@@ -154,6 +154,7 @@ class PeerWorkspace:
         self.hidden = int(hidden)
         self.device = torch.device(device)
         self._group = group
+        self.group = group
         use_dist = distributed and dist.is_initialized()
         self.world_size = dist.get_world_size(group) if use_dist else 1
         self.rank = dist.get_rank(group) if use_dist else 0
@@ -218,13 +219,27 @@ def _check_rows(workspace: PeerWorkspace, tensor: Tensor, what: str) -> None:
         raise ValueError("more tokens than the all-reduce workspace holds")
 
 
-def _launch(workspace: PeerWorkspace, partial: Tensor, residual: Tensor | None, weight: Tensor | None,
-            out: Tensor, eps: float, mode: int) -> None:
+def _peer_path(workspace: PeerWorkspace, tensor: Tensor, mode: int) -> bool:
+    """Whether the peer-memory kernel does the exchange (else NCCL does)."""
+
+    if mode != ALL_REDUCE_AUTO or workspace.world_size == 1:
+        return True
     from light_vllm_b200 import _native
 
+    limit = int(_native.library().lvb_allreduce_peer_max_bytes(workspace.world_size))
+    return tensor.numel() * tensor.element_size() <= limit
+
+
+def _launch(workspace: PeerWorkspace, partial: Tensor, residual: Tensor | None, weight: Tensor | None,
+            out: Tensor, eps: float, mode: int, *, local: bool = False) -> None:
+    """``local``: the ranks' sum is already in ``partial`` (world 1 launch)."""
+
+    from light_vllm_b200 import _native
+
+    rank, world = (0, 1) if local else (workspace.rank, workspace.world_size)
     _native.check(
         _native.library().lvb_allreduce_add_rmsnorm(
-            workspace.pointers, workspace.rank, workspace.world_size, partial.data_ptr(),
+            workspace.pointers, rank, world, partial.data_ptr(),
             0 if residual is None else residual.data_ptr(), 0 if weight is None else weight.data_ptr(),
             out.data_ptr(), partial.shape[0], partial.shape[1], workspace.max_tokens, float(eps), int(mode),
             torch.cuda.current_stream(partial.device).cuda_stream),
@@ -252,7 +267,13 @@ def all_reduce_add_rms_norm(workspace: PeerWorkspace, partial: Tensor, residual:
     if weight.dtype != torch.float16 or weight.shape != (workspace.hidden,) or not weight.is_contiguous():
         raise ValueError("weight must be a contiguous fp16 [hidden] tensor")
     out = torch.empty_like(partial)
-    _launch(workspace, partial, residual, weight, out, eps, mode)
+    if _peer_path(workspace, partial, mode):
+        _launch(workspace, partial, residual, weight, out, eps, mode)
+    else:
+        # Large messages: NCCL's ring all-reduce in place (the reference's
+        # all_reduce_sum), then the add + RMSNorm without an exchange.
+        dist.all_reduce(partial, op=dist.ReduceOp.SUM, group=workspace.group)
+        _launch(workspace, partial, residual, weight, out, eps, mode, local=True)
     return out, residual
 
 
@@ -261,7 +282,10 @@ def all_reduce_sum_peer(workspace: PeerWorkspace, tensor: Tensor, *, mode: int =
     ``TensorCollectives.all_reduce_sum``, modeling/tensor_parallel.py:18-27)."""
 
     _check_rows(workspace, tensor, "tensor")
-    _launch(workspace, tensor, None, None, tensor, 0.0, mode)
+    if _peer_path(workspace, tensor, mode):
+        _launch(workspace, tensor, None, None, tensor, 0.0, mode)
+    else:
+        dist.all_reduce(tensor, op=dist.ReduceOp.SUM, group=workspace.group)
     return tensor
 
 
