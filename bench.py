@@ -364,11 +364,13 @@ def decode_case(torch, shape, rank: int, world: int, device, batches, ctx: int, 
                 dist.barrier()
             ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             stream = torch.cuda.current_stream()
+            torch.cuda.nvtx.range_push("decode")  # lets a profiler capture only the timed steps
             ev0.record(stream)
             for _ in range(steps):
                 step.replay()
             ev1.record(stream)
             torch.cuda.synchronize()
+            torch.cuda.nvtx.range_pop()
             ms = ev0.elapsed_time(ev1) / steps
             if dist is not None:
                 t = torch.tensor([ms], device=device)
