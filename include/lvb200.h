@@ -276,11 +276,12 @@ LVB_API int lvb_allreduce_workspace_init(void *workspace, int world, int64_t max
  * hidden, max_tokens and mode, in the same order.  The call counter lives in
  * the workspace, so launches may be captured in a CUDA graph.
  * mode: 1 one-shot (push every row to every peer, then flags), 2 two-shot
- * (reduce-scatter + all-gather through peer memory), 3 sentinel one-shot
- * (pushed data carries its own ready marker: no flags, no fences); 0 picks
- * 3 while (world - 1) x message bytes <= 16 MiB and 2 beyond (callers with
- * a library all-reduce at hand do better with it there: see
- * lvb_allreduce_peer_max_bytes).  An fp16 lane equal to 0xFFFF (a
+ * (reduce-scatter + all-gather through peer memory, flags), 3 sentinel
+ * one-shot (pushed data carries its own ready marker: no flags, no fences),
+ * 4 sentinel two-shot (reduce-scatter + all-gather with sentinel-marked
+ * pushes); 0 picks 3 at world <= 2 or while (world - 1) x message bytes <=
+ * 4 MiB, else 4 (callers with a library all-reduce at hand do better with it
+ * for messages above lvb_allreduce_peer_max_bytes).  An fp16 lane equal to 0xFFFF (a
  * NaN) is pushed as 0xFE00 in mode 3, so NaN payloads are not preserved.  Waits for peers are bounded: on timeout the
  * device error word gets LVB_DEVERR_TIMEOUT, outputs are left unwritten and
  * the workspaces must be rebuilt.  With world == 1 no workspace is touched

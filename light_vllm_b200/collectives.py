@@ -205,7 +205,7 @@ class PeerWorkspace:
         self._own = None
 
 
-ALL_REDUCE_AUTO, ALL_REDUCE_ONE_SHOT, ALL_REDUCE_TWO_SHOT, ALL_REDUCE_SENTINEL = 0, 1, 2, 3
+ALL_REDUCE_AUTO, ALL_REDUCE_ONE_SHOT, ALL_REDUCE_TWO_SHOT, ALL_REDUCE_SENTINEL, ALL_REDUCE_SENTINEL_TWO_SHOT = 0, 1, 2, 3, 4
 
 
 def _check_rows(workspace: PeerWorkspace, tensor: Tensor, what: str) -> None:

@@ -21,8 +21,9 @@
 //           receives the rows (or flat chunks) rank src pushes here
 //   gather  2 parities x max_tokens x hidden fp16 (two-shot only): the
 //           reduced rows every owner pushes to every rank
-//   sentinel buffers  3 x world slots x max_tokens x hidden fp16, filled
-//           with the sentinel 0xFFFF when empty (sentinel one-shot only)
+//   sentinel buffers  3 x world slots x max_tokens x hidden fp16, then 3
+//           gather slots, filled with the sentinel 0xFFFF when empty
+//           (sentinel modes only)
 // Call e (read from the device, so the launch can be graph-captured) uses
 // parity e & 1.  Data moves by plain 16-byte stores into peer memory; flags
 // are system-scope release stores and acquire loads; every wait is bounded
@@ -53,6 +54,18 @@
 // finished writing it (this rank read all of it) and writes it again only at
 // call e + 2, after this call has finished.
 //
+// Sentinel two-shot (larger messages at world > 2): the flat range is cut
+// into world owner ranges and each into grid sub-chunks, as in the two-shot
+// mode, but every exchange is a sentinel-marked push.  Phase 1: CTA b pushes
+// sub-chunk (c, b) of its partial into owner c's slot [rank].  Phase 2: CTA b
+// polls its own sub-chunk from the world - 1 slots, sums, rounds to fp16 and
+// pushes the sums into every rank's gather slot.  Phase 3: every CTA polls
+// the gather slot for its rows and normalises them.  No flags and no grid
+// barrier: each wait is on exactly the data it consumes.  Call e clears, at
+// home, what call e - 1 left in buffer (e + 2) % 3 (its own owner range of
+// the peer slots and the whole gather slot); header words record the rows and
+// the kind of exchange each buffer last received.
+//
 // Reuse of parity e & 1 at call e + 2 is safe: a rank can start call e + 2
 // only after its call e + 1 passed a wait on every peer's call e + 1 pushes,
 // and a peer pushes at call e + 1 only after its call e finished.
@@ -76,13 +89,15 @@ constexpr int kEpochOff = 0;
 constexpr int kCounterOff = 4;
 constexpr int kRowsOff = 16;      // uint32 rows received per sentinel buffer [3]
 constexpr int kGeometryOff = 32;  // uint32 magic, world, max_tokens, hidden (written at initialisation)
+constexpr int kKindOff = 48;      // uint32 kind of data per sentinel buffer [3]: 0 none, 1 one-shot, 2 two-shot
 constexpr uint32_t kMagic = 0x4c564152u;
 constexpr int kFlags2Off = 64;
 constexpr int kFlags1Off = 256;
 constexpr size_t kHeaderBytes = 64 * 1024;
 static_assert(kFlags1Off + kMaxBlocks * kMaxWorld * 4 <= static_cast<int>(kHeaderBytes), "header too small");
 
-enum Mode : int { kAuto = 0, kOneShot = 1, kTwoShot = 2, kSentinel = 3 };
+enum Mode : int { kAuto = 0, kOneShot = 1, kTwoShot = 2, kSentinel = 3, kSentinelTwoShot = 4 };
+enum Kind : uint32_t { kKindNone = 0, kKindOneShot = 1, kKindTwoShot = 2 };
 constexpr uint32_t kSentinelWord = 0xFFFFFFFFu;
 
 struct Args {
@@ -98,8 +113,10 @@ struct Args {
   int mode;                 // kOneShot, kTwoShot or kSentinel
 };
 
-// Staging (2 x world), gather (2) and sentinel (3 x world) slots.
-__host__ __device__ constexpr size_t slots_per_workspace(int world) { return 5 * static_cast<size_t>(world) + 2; }
+// Staging (2 x world), gather (2), sentinel (3 x world) and sentinel gather (3) slots.
+__host__ __device__ constexpr size_t slots_per_workspace(int world) { return 5 * static_cast<size_t>(world) + 5; }
+// Slots before the sentinel region (initialised to zero; the rest to 0xFF).
+__host__ __device__ constexpr size_t slots_before_sentinel(int world) { return 2 * static_cast<size_t>(world) + 2; }
 
 __host__ __device__ __forceinline__ size_t staging_off(const Args &a, uint32_t parity, int src) {
   return kHeaderBytes + (static_cast<size_t>(parity) * a.world + src) * a.slot_bytes;
@@ -111,6 +128,19 @@ __host__ __device__ __forceinline__ size_t gather_off(const Args &a, uint32_t pa
 __host__ __device__ __forceinline__ size_t sentinel_off(const Args &a, uint32_t buf, int src) {
   return kHeaderBytes + (2 * static_cast<size_t>(a.world) + 2 + static_cast<size_t>(buf) * a.world + src) * a.slot_bytes;
 }
+__host__ __device__ __forceinline__ size_t sentinel_gather_off(const Args &a, uint32_t buf) {
+  return kHeaderBytes + (5 * static_cast<size_t>(a.world) + 2 + buf) * a.slot_bytes;
+}
+
+// Owner range [begin, end) of rank c in a flat range of `total` vectors.
+__device__ __forceinline__ void owner_range(size_t total, int world, int c, size_t &begin, size_t &end) {
+  const size_t per = (total + world - 1) / world;
+  begin = min(static_cast<size_t>(c) * per, total);
+  end = min(begin + per, total);
+}
+
+// Poll a 16-byte vector of peer-pushed data until no lane holds the sentinel.
+__device__ __forceinline__ uint4 poll_vec(const void *p, long long start, bool &fail);
 
 __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
   uint32_t v;
@@ -147,6 +177,18 @@ __device__ __forceinline__ uint32_t sanitize_word(uint32_t w) {
 }
 __device__ __forceinline__ uint4 sanitize(uint4 v) {
   return make_uint4(sanitize_word(v.x), sanitize_word(v.y), sanitize_word(v.z), sanitize_word(v.w));
+}
+
+__device__ __forceinline__ uint4 poll_vec(const void *p, long long start, bool &fail) {
+  uint4 v = ld_volatile(p);
+  while (has_sentinel(v) && !fail) {
+    if (clock64() - start > kWaitBudgetCycles) {
+      record_device_error(LVB_DEVERR_TIMEOUT);
+      fail = true;
+    }
+    v = ld_volatile(p);
+  }
+  return v;
 }
 
 // Thread 0: wait until flags[i * stride] reaches epoch for i < n (bounded).
@@ -281,7 +323,7 @@ __global__ void __launch_bounds__(kThreads) allreduce_add_rmsnorm_kernel(const _
   pdl_entry();
   __shared__ float red[kThreads / 32];
   __shared__ int ok_sm;
-  __shared__ uint32_t epoch_sm, stale_rows_sm;
+  __shared__ uint32_t epoch_sm, stale_rows_sm, stale_kind_sm;
   const int tid = threadIdx.x;
   uint8_t *own = a.ws[a.rank];
   uint32_t *counter = reinterpret_cast<uint32_t *>(own + kCounterOff);
@@ -295,6 +337,7 @@ __global__ void __launch_bounds__(kThreads) allreduce_add_rmsnorm_kernel(const _
     if (!ok_sm) record_device_error(LVB_DEVERR_INDEX);
     epoch_sm = *reinterpret_cast<volatile uint32_t *>(own + kEpochOff) + 1u;
     stale_rows_sm = reinterpret_cast<const volatile uint32_t *>(own + kRowsOff)[(epoch_sm + 2u) % 3u];
+    stale_kind_sm = reinterpret_cast<const volatile uint32_t *>(own + kKindOff)[(epoch_sm + 2u) % 3u];
   }
   __syncthreads();
   if (!ok_sm) return;
@@ -310,23 +353,92 @@ __global__ void __launch_bounds__(kThreads) allreduce_add_rmsnorm_kernel(const _
   {
     const int stale_rows = static_cast<int>(stale_rows_sm);
     const uint4 empty = make_uint4(kSentinelWord, kSentinelWord, kSentinelWord, kSentinelWord);
-    for (int row = blockIdx.x; row < stale_rows; row += gridDim.x) {
-      const size_t v0 = static_cast<size_t>(row) * nvec_row;
+    if (stale_kind_sm == kKindOneShot) {
+      for (int row = blockIdx.x; row < stale_rows; row += gridDim.x) {
+        const size_t v0 = static_cast<size_t>(row) * nvec_row;
+        for (int r = 0; r < a.world; ++r) {
+          if (r == a.rank) continue;
+          uint4 *dst = reinterpret_cast<uint4 *>(own + sentinel_off(a, stale, r));
+          for (int c = tid; c < nvec_row; c += kThreads) dst[v0 + c] = empty;
+        }
+      }
+    } else if (stale_kind_sm == kKindTwoShot) {
+      const size_t total = static_cast<size_t>(stale_rows) * nvec_row;
+      size_t ob, oe;
+      owner_range(total, a.world, a.rank, ob, oe);
+      const size_t step = static_cast<size_t>(gridDim.x) * kThreads;
       for (int r = 0; r < a.world; ++r) {
         if (r == a.rank) continue;
         uint4 *dst = reinterpret_cast<uint4 *>(own + sentinel_off(a, stale, r));
-        for (int c = tid; c < nvec_row; c += kThreads) dst[v0 + c] = empty;
+        for (size_t i = ob + static_cast<size_t>(blockIdx.x) * kThreads + tid; i < oe; i += step) dst[i] = empty;
       }
+      uint4 *gdst = reinterpret_cast<uint4 *>(own + sentinel_gather_off(a, stale));
+      for (size_t i = static_cast<size_t>(blockIdx.x) * kThreads + tid; i < total; i += step) gdst[i] = empty;
     }
   }
   // The last CTA to arrive records what this call left in the sentinel
   // buffers and advances the epoch.
   auto advance_epoch = [&]() {
     *counter = 0u;
-    reinterpret_cast<volatile uint32_t *>(own + kRowsOff)[buf] =
-        a.mode == kSentinel ? static_cast<uint32_t>(a.tokens) : 0u;
+    const bool sentinel = a.mode == kSentinel || a.mode == kSentinelTwoShot;
+    reinterpret_cast<volatile uint32_t *>(own + kRowsOff)[buf] = sentinel ? static_cast<uint32_t>(a.tokens) : 0u;
+    reinterpret_cast<volatile uint32_t *>(own + kKindOff)[buf] =
+        a.mode == kSentinel ? kKindOneShot : a.mode == kSentinelTwoShot ? kKindTwoShot : kKindNone;
     *reinterpret_cast<volatile uint32_t *>(own + kEpochOff) = epoch;
   };
+
+  if (a.mode == kSentinelTwoShot) {
+    const size_t total = static_cast<size_t>(a.tokens) * nvec_row;
+    // Phase 1: sub-chunk (c, b) of this rank's partial -> owner c's slot [rank].
+    for (int c = 0; c < a.world; ++c) {
+      if (c == a.rank) continue;
+      size_t ob, oe;
+      owner_range(total, a.world, c, ob, oe);
+      const size_t per_cta = (oe - ob + gridDim.x - 1) / gridDim.x;
+      const size_t b0 = min(ob + static_cast<size_t>(blockIdx.x) * per_cta, oe);
+      const size_t e0 = min(b0 + per_cta, oe);
+      uint4 *dst = reinterpret_cast<uint4 *>(a.ws[c] + sentinel_off(a, buf, a.rank));
+      for (size_t i = b0 + tid; i < e0; i += kThreads) dst[i] = sanitize(partial[i]);
+    }
+    if (tid == 0) {
+      const unsigned int prev = atomicAdd(counter, 1u);
+      if (prev == gridDim.x - 1) advance_epoch();
+    }
+    // Phase 2: own sub-chunk: poll the peers' values, sum, push the sums.
+    bool fail = false;
+    {
+      size_t ob, oe;
+      owner_range(total, a.world, a.rank, ob, oe);
+      const size_t per_cta = (oe - ob + gridDim.x - 1) / gridDim.x;
+      const size_t b0 = min(ob + static_cast<size_t>(blockIdx.x) * per_cta, oe);
+      const size_t e0 = min(b0 + per_cta, oe);
+      const size_t goff = sentinel_gather_off(a, buf);
+      for (size_t i = b0 + tid; i < e0; i += kThreads) {
+        float acc[kVec];
+#pragma unroll
+        for (int e = 0; e < kVec; ++e) acc[e] = 0.f;
+        for (int r = 0; r < a.world; ++r) {
+          const uint4 pv = r == a.rank ? partial[i] : poll_vec(own + sentinel_off(a, buf, r) + i * 16, start, fail);
+          add_vec(acc, pv);
+        }
+        const uint4 hv = sanitize(round_vec(acc));
+        for (int r = 0; r < a.world; ++r) reinterpret_cast<uint4 *>(a.ws[r] + goff)[i] = hv;
+      }
+    }
+    // Phase 3: rows b, b + grid, ... from the home gather slot.
+    const uint8_t *gather = own + sentinel_gather_off(a, buf);
+    for (int row = blockIdx.x; row < a.tokens; row += gridDim.x) {
+      uint4 hv[kMaxVecsPerThread];
+#pragma unroll
+      for (int j = 0; j < kMaxVecsPerThread; ++j) {
+        const int c = tid + j * kThreads;
+        if (c < nvec_row) hv[j] = poll_vec(gather + (static_cast<size_t>(row) * nvec_row + c) * 16, start, fail);
+      }
+      if (__syncthreads_or(fail)) return;
+      finish_row(a, row, hv, red);
+    }
+    return;
+  }
 
   if (a.mode == kSentinel) {
     // ---- sentinel one-shot: rows b, b + grid, ... ----

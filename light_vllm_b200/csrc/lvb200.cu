@@ -1131,7 +1131,7 @@ int lvb_allreduce_workspace_init(void *workspace, int world, int64_t max_tokens,
   if (!workspace || total == 0) return fail(LVB_ERR_INVALID, "lvb_allreduce_workspace_init: invalid argument");
   const size_t slot = static_cast<size_t>(max_tokens) * hidden * 2;
   uint8_t *base = static_cast<uint8_t *>(workspace);
-  const size_t sentinel_begin = lvb::ar::kHeaderBytes + (2 * static_cast<size_t>(world) + 2) * slot;
+  const size_t sentinel_begin = lvb::ar::kHeaderBytes + lvb::ar::slots_before_sentinel(world) * slot;
   if (max_tokens > INT_MAX || hidden > lvb::ar::kMaxHidden)
     return fail(LVB_ERR_INVALID, "lvb_allreduce_workspace_init: shape too large");
   cudaError_t e = cudaMemset(base, 0, sentinel_begin);
@@ -1165,6 +1165,10 @@ int allreduce_capacity(int dev) {
 // and NCCL's all-reduce up to ~16 MiB of pushes (world 2: 1024 x 8192 fp16
 // rows, world 4: 256 rows).
 constexpr size_t kOneShotMaxPushBytes = size_t(16) << 20;
+// (world - 1) x message bytes up to which the one-shot push beats the two-shot
+// exchange (which moves 2 (world - 1) / world of the message per rank instead
+// of world - 1 messages, for one more NVLink round trip).
+constexpr size_t kSentinelOneShotMaxPushBytes = size_t(4) << 20;
 
 }  // namespace
 
@@ -1181,7 +1185,7 @@ int lvb_allreduce_add_rmsnorm(void *const *workspaces, int rank, int world, cons
   if (tokens < 0 || tokens > max_tokens || hidden <= 0 || hidden % 8 != 0 || hidden > lvb::ar::kMaxHidden)
     return fail(LVB_ERR_INVALID, "all-reduce shape %lld x %lld (workspace rows %lld; hidden a multiple of 8 up to %d)",
                 (long long)tokens, (long long)hidden, (long long)max_tokens, lvb::ar::kMaxHidden);
-  if (mode < lvb::ar::kAuto || mode > lvb::ar::kSentinel) return fail(LVB_ERR_INVALID, "all-reduce mode %d", mode);
+  if (mode < lvb::ar::kAuto || mode > lvb::ar::kSentinelTwoShot) return fail(LVB_ERR_INVALID, "all-reduce mode %d", mode);
   if (tokens == 0) return LVB_OK;
   if (tokens > INT_MAX / 8) return fail(LVB_ERR_UNSUPPORTED, "token count too large");
   if (!workspaces || !partial || !out) return fail(LVB_ERR_INVALID, "all-reduce null pointer argument");
@@ -1238,11 +1242,12 @@ int lvb_allreduce_add_rmsnorm(void *const *workspaces, int rank, int world, cons
   a.eps = eps;
   const size_t bytes = static_cast<size_t>(tokens) * hidden * 2;
   if (mode == lvb::ar::kAuto)
-    mode = bytes * (world - 1) <= kOneShotMaxPushBytes ? lvb::ar::kSentinel : lvb::ar::kTwoShot;
+    mode = (world <= 2 || bytes * (world - 1) <= kSentinelOneShotMaxPushBytes) ? lvb::ar::kSentinel
+                                                                               : lvb::ar::kSentinelTwoShot;
   a.mode = mode;
   const int cap = allreduce_capacity(dev);
   int grid;
-  if (mode != lvb::ar::kTwoShot) {
+  if (mode != lvb::ar::kTwoShot && mode != lvb::ar::kSentinelTwoShot) {
     grid = tokens < cap ? static_cast<int>(tokens) : cap;
   } else {
     const int64_t per_owner_vecs = (tokens * hidden / 8 + world - 1) / world;

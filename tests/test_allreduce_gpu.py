@@ -202,7 +202,8 @@ def _rank_worker(rank: int, world: int, port: int, results) -> None:
         dev = torch.device("cuda", rank)
         ws = PeerWorkspace(512, 3584, dev)
         worst = 0.0
-        cases = ((5, 1), (1, 2), (16, 0), (512, 2), (77, 3), (512, 3), (9, 3), (77, 1), (512, 1), (300, 2), (3, 3))
+        cases = ((5, 1), (1, 2), (16, 0), (512, 2), (77, 3), (512, 3), (9, 3), (77, 1), (512, 1), (300, 2), (3, 3),
+                 (1, 4), (77, 4), (512, 4), (9, 3), (300, 4), (13, 1), (100, 4))
         for it, (tokens, mode) in enumerate(cases):
             partials, residual, weight = inputs(100 * it, tokens)
             want_norm, want_res = otp.all_reduce_add_rms_norm(list(partials), residual, weight, 1e-6)
@@ -231,6 +232,7 @@ def _rank_worker(rank: int, world: int, port: int, results) -> None:
                 g_out, _ = all_reduce_add_rms_norm(ws, p_dev, r_dev, w_dev, 1e-6, mode=1)
                 g_out2, _ = all_reduce_add_rms_norm(ws, g_out, r_dev, w_dev, 1e-6, mode=2)
                 g_out3, _ = all_reduce_add_rms_norm(ws, g_out2, r_dev, w_dev, 1e-6, mode=3)
+                g_out4, _ = all_reduce_add_rms_norm(ws, g_out3, r_dev, w_dev, 1e-6, mode=4)
         for _ in range(3):
             graph.replay()
             torch.cuda.synchronize(dev)
@@ -241,6 +243,8 @@ def _rank_worker(rank: int, world: int, port: int, results) -> None:
             worst = max(worst, ulps(g_out2, n2))
             n3, r_ref = otp.all_reduce_add_rms_norm([g_out2.cpu()] * world, r_ref, weight, 1e-6)
             worst = max(worst, ulps(g_out3, n3))
+            n4, r_ref = otp.all_reduce_add_rms_norm([g_out3.cpu()] * world, r_ref, weight, 1e-6)
+            worst = max(worst, ulps(g_out4, n4))
             if not torch.equal(r_dev.cpu(), r_ref):
                 raise AssertionError("graph replay residual mismatch")
         del graph

@@ -67,11 +67,11 @@ def test_invalid_arguments_are_rejected_before_any_launch():
 
 
 def test_allreduce_workspace_bytes_cover_every_slot():
-    """Header + 2*world staging + 2 gather + 3*world sentinel slots."""
+    """Header + 2*world staging + 2 gather + 3*world sentinel + 3 sentinel gather slots."""
 
     lib = _native.library()
     for world, tokens, hidden in ((1, 8, 256), (2, 512, 3584), (8, 128, 8192)):
         slot = tokens * hidden * 2
-        assert lib.lvb_allreduce_workspace_bytes(world, tokens, hidden) == 65536 + (5 * world + 2) * slot
+        assert lib.lvb_allreduce_workspace_bytes(world, tokens, hidden) == 65536 + (5 * world + 5) * slot
     assert lib.lvb_allreduce_workspace_bytes(9, 8, 256) == 0
     assert lib.lvb_allreduce_workspace_bytes(2, 0, 256) == 0
