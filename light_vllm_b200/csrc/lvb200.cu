@@ -1160,21 +1160,23 @@ int allreduce_capacity(int dev) {
   return cap;
 }
 
-// (world - 1) x message bytes up to which the sentinel one-shot is the
-// default: measured on B200 it beats the two-shot mode at every size tried
-// and NCCL's all-reduce up to ~16 MiB of pushes (world 2: 1024 x 8192 fp16
-// rows, world 4: 256 rows).
-constexpr size_t kOneShotMaxPushBytes = size_t(16) << 20;
+// Message bytes up to which the peer-memory kernel beats NCCL's ring
+// all-reduce (measured on B200, add + RMSNorm included on our side): world 2
+// one-shot up to ~16 MiB (1024 x 8192 fp16 rows); world 4 sentinel two-shot up
+// to ~32 MiB (2048 rows, where both reach ~415 GB/s bus bandwidth).
+constexpr size_t kPeerMaxBytesWorld2 = size_t(16) << 20;
+constexpr size_t kPeerMaxBytes = size_t(32) << 20;
 // (world - 1) x message bytes up to which the one-shot push beats the two-shot
 // exchange (which moves 2 (world - 1) / world of the message per rank instead
-// of world - 1 messages, for one more NVLink round trip).
+// of world - 1 messages, for one more NVLink round trip); world 4 crossover
+// near 64 x 8192 rows.
 constexpr size_t kSentinelOneShotMaxPushBytes = size_t(4) << 20;
 
 }  // namespace
 
 size_t lvb_allreduce_peer_max_bytes(int world) {
   if (world <= 1) return SIZE_MAX;
-  return kOneShotMaxPushBytes / static_cast<size_t>(world - 1);
+  return world == 2 ? kPeerMaxBytesWorld2 : kPeerMaxBytes;
 }
 
 int lvb_allreduce_add_rmsnorm(void *const *workspaces, int rank, int world, const uint16_t *partial,
