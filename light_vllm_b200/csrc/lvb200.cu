@@ -537,7 +537,7 @@ int check_awq_shape(int64_t m, int64_t k, int64_t n, int64_t group_size) {
 // Attention planning
 // ------------------------------------------------------------------------
 struct DecodePlan {
-  int max_splits, chunk_tokens, heads_per_cta;
+  int max_splits, chunk_tokens, heads_per_cta, warps_per_head;
   size_t o_bytes, lse_bytes, count_bytes;
   size_t total() const { return o_bytes + lse_bytes + count_bytes; }
 };
@@ -556,9 +556,14 @@ DecodePlan decode_plan(int64_t num_seqs, int64_t hq, int64_t hkv, int64_t d, int
   const int64_t max_pages = (max_seq_len + lvb::attn::kPageTokens - 1) / lvb::attn::kPageTokens;
   // Small batches: one KV head per CTA, so (request, head) pairs and their
   // merges spread over more SMs.
-  const int64_t hpc = num_seqs < kAttnSmallBatch ? 1 : hkv % 4 == 0 ? 4 : hkv % 2 == 0 ? 2 : 1;
+  const bool small = num_seqs < kAttnSmallBatch;
+  const int64_t hpc = small ? 1 : hkv % 4 == 0 ? 4 : hkv % 2 == 0 ? 2 : 1;
+  // Very small batches: four warps share each (request, head) split, cutting
+  // the serial per-warp page work and widening the split merge (B200, ctx
+  // 1024: B = 1 14.0 -> 10.4 us; at B = 16 it loses, 17.1 -> 20.7 us).
+  const int64_t kw = small && num_seqs * hkv <= 32 ? 4 : 1;
   const int64_t pairs = num_seqs * (hkv / hpc) > 0 ? num_seqs * (hkv / hpc) : 1;
-  const int64_t target = 8LL * sms;  // ~4 waves of 2 CTAs per SM (measured best of 4/8/12/24)
+  const int64_t target = (kw > 1 ? 2LL : 8LL) * sms;  // CTAs: ~8 warps per SM either way
   int64_t splits = (target + pairs - 1) / pairs;
   if (splits < 1) splits = 1;
   if (splits > max_pages) splits = max_pages > 0 ? max_pages : 1;
@@ -571,6 +576,7 @@ DecodePlan decode_plan(int64_t num_seqs, int64_t hq, int64_t hkv, int64_t d, int
   p.max_splits = static_cast<int>(splits);
   p.chunk_tokens = static_cast<int>(chunk_pages * lvb::attn::kPageTokens);
   p.heads_per_cta = static_cast<int>(hpc);
+  p.warps_per_head = static_cast<int>(kw);
   p.o_bytes = (static_cast<size_t>(num_seqs * hq * splits * d) * 4 + 255) & ~static_cast<size_t>(255);
   p.lse_bytes = (static_cast<size_t>(num_seqs * hq * splits) * 4 + 255) & ~static_cast<size_t>(255);
   p.count_bytes = (static_cast<size_t>(num_seqs * hkv) * 4 + 255) & ~static_cast<size_t>(255);
@@ -583,13 +589,13 @@ bool decode_eligible(const uint8_t *vis, int64_t max_query_len, int64_t num_seqs
          (d == 64 || d == 128) && hq % hkv == 0 && hq / hkv <= 16;
 }
 
-template <bool kBf16, int D, int HPC>
+template <bool kBf16, int D, int HPC, int KW = 1>
 int launch_decode(const lvb::attn::AttnArgs &a, int64_t num_seqs, int64_t num_blocks, int dev,
                   cudaStream_t stream) {
   (void)num_blocks;
-  using Cfg = lvb::attn::DecodeCfg<D, HPC>;
+  using Cfg = lvb::attn::DecodeCfg<D, HPC, KW>;
   static bool smem_done[kMaxDevices] = {false};
-  auto kernel = lvb::attn::paged_decode_kernel<kBf16, D, HPC>;
+  auto kernel = lvb::attn::paged_decode_kernel<kBf16, D, HPC, KW>;
   int rc = ensure_smem(kernel, Cfg::kSmemBytes, dev, smem_done);
   if (rc != LVB_OK) return rc;
   dim3 grid(a.max_splits, a.Hkv / HPC, static_cast<unsigned>(num_seqs));
@@ -599,8 +605,9 @@ int launch_decode(const lvb::attn::AttnArgs &a, int64_t num_seqs, int64_t num_bl
 }
 
 template <bool kBf16, int D>
-int launch_decode_any(const lvb::attn::AttnArgs &a, int heads_per_cta, int64_t num_seqs, int64_t num_blocks,
-                      int dev, cudaStream_t stream) {
+int launch_decode_any(const lvb::attn::AttnArgs &a, int heads_per_cta, int warps_per_head, int64_t num_seqs,
+                      int64_t num_blocks, int dev, cudaStream_t stream) {
+  if (warps_per_head == 4) return launch_decode<kBf16, D, 1, 4>(a, num_seqs, num_blocks, dev, stream);
   switch (heads_per_cta) {
     case 4: return launch_decode<kBf16, D, 4>(a, num_seqs, num_blocks, dev, stream);
     case 2: return launch_decode<kBf16, D, 2>(a, num_seqs, num_blocks, dev, stream);
@@ -978,11 +985,13 @@ int lvb_paged_attention(const uint16_t *query, int64_t query_token_stride,
     a.max_splits = plan.max_splits;
     a.chunk_tokens = plan.chunk_tokens;
     if (bf16) {
-      return head_size == 128 ? launch_decode_any<true, 128>(a, plan.heads_per_cta, num_seqs, num_blocks, dev, s)
-                              : launch_decode_any<true, 64>(a, plan.heads_per_cta, num_seqs, num_blocks, dev, s);
+      return head_size == 128
+                 ? launch_decode_any<true, 128>(a, plan.heads_per_cta, plan.warps_per_head, num_seqs, num_blocks, dev, s)
+                 : launch_decode_any<true, 64>(a, plan.heads_per_cta, plan.warps_per_head, num_seqs, num_blocks, dev, s);
     }
-    return head_size == 128 ? launch_decode_any<false, 128>(a, plan.heads_per_cta, num_seqs, num_blocks, dev, s)
-                            : launch_decode_any<false, 64>(a, plan.heads_per_cta, num_seqs, num_blocks, dev, s);
+    return head_size == 128
+               ? launch_decode_any<false, 128>(a, plan.heads_per_cta, plan.warps_per_head, num_seqs, num_blocks, dev, s)
+               : launch_decode_any<false, 64>(a, plan.heads_per_cta, plan.warps_per_head, num_seqs, num_blocks, dev, s);
   }
   return bf16 ? launch_general<true>(a, num_tokens, s) : launch_general<false>(a, num_tokens, s);
 }

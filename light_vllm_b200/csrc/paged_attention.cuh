@@ -225,33 +225,41 @@ __global__ void __launch_bounds__(128) paged_attn_general_kernel(const AttnArgs 
 constexpr int kPageTokens = 16;
 constexpr int kBoxBytes = kPageTokens * 128;  // one TMA box: 16 tokens x 64 dims of one head
 
-// HPC = KV heads per CTA (one warp each), D = head size.
-template <int D, int HPC>
+// HPC = KV heads per CTA, KW = warps per head (KW > 1 only with HPC = 1:
+// the warps of a CTA share one head's pages round-robin and merge their
+// partial softmax results in shared memory), D = head size.
+template <int D, int HPC, int KW = 1>
 struct DecodeCfg {
+  static_assert(KW == 1 || HPC == 1, "several warps per head only with one head per CTA");
   static constexpr int kBoxes = D / 64;                  // 64-dim halves of a head's row
   static constexpr int kHeadBytes = kBoxes * kBoxBytes;  // one head's 16-token K (or V) page
   static constexpr int kPageBytes = 2 * kHeadBytes;      // K then V
-  // Page ring per CTA: 96 KB for 2-4 heads; a one-head CTA (small batches)
-  // keeps 32 KB so that more of them fit on an SM (B = 16, ctx 1024:
+  static constexpr int kWarps = HPC * KW;
+  // Page ring per CTA: 96 KB for 2-4 heads or 4 warps on one head; a one-warp
+  // CTA keeps 32 KB so that more of them fit on an SM (B = 16, ctx 1024:
   // 21.9 -> 17.1 us on B200).
-  static constexpr int kRingBudget = HPC == 1 ? 32 * 1024 : 96 * 1024;
-  static constexpr int kFit = kRingBudget / (HPC * kPageBytes);
+  static constexpr int kRingBudget = kWarps == 1 ? 32 * 1024 : 96 * 1024;
+  static constexpr int kFit = kRingBudget / (kWarps * kPageBytes);
   static constexpr int kStages = kFit < 2 ? 2 : (kFit > 8 ? 8 : kFit);  // per-warp ring depth
   static constexpr int kWarpRing = kStages * kPageBytes;
-  static constexpr int kThreads = HPC * 32;
-  static constexpr int kBarOff = HPC * kWarpRing;
-  static constexpr int kSmemBytes = kBarOff + HPC * kStages * 8 + 16 + 1024;
+  static constexpr int kThreads = kWarps * 32;
+  static constexpr int kBarOff = kWarps * kWarpRing;
+  static constexpr int kSmemBytes = kBarOff + kWarps * kStages * 8 + 16 + 1024;
+  // Cross-warp merge scratch (KW > 1), reusing the ring: (m, l) per warp and
+  // row, then the scaled outputs [KW][16 rows][D] fp32.
+  static constexpr int kMergeObufOff = 1024;
+  static_assert(KW == 1 || kMergeObufOff + KW * 16 * D * 4 <= kBarOff, "merge scratch fits in the ring");
 };
 
-template <bool kBf16, int D, int HPC>
-__global__ void __launch_bounds__(DecodeCfg<D, HPC>::kThreads, 2)
+template <bool kBf16, int D, int HPC, int KW = 1>
+__global__ void __launch_bounds__(DecodeCfg<D, HPC, KW>::kThreads, 2)
     paged_decode_kernel(const AttnArgs a) {
   pdl_entry();
-  using Cfg = DecodeCfg<D, HPC>;
+  using Cfg = DecodeCfg<D, HPC, KW>;
   constexpr int kStages = Cfg::kStages;
   constexpr int kSteps = D / 16;  // k-steps of QK^T, and dim pairs of PV
   constexpr int kNTiles = D / 8;  // 8-dim output tiles
-  constexpr int kConsumers = HPC * 32;
+  constexpr int kConsumers = Cfg::kThreads;
   constexpr int kChunksPerLane = Cfg::kHeadBytes / 16 / 32;  // 16-byte copies per lane for K (and V)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
@@ -260,7 +268,7 @@ __global__ void __launch_bounds__(DecodeCfg<D, HPC>::kThreads, 2)
   const int lane = threadIdx.x & 31;
   uint64_t *ready = reinterpret_cast<uint64_t *>(smem + Cfg::kBarOff) + warp * kStages;
   volatile int *abort_flag =
-      reinterpret_cast<volatile int *>(reinterpret_cast<uint64_t *>(smem + Cfg::kBarOff) + HPC * kStages);
+      reinterpret_cast<volatile int *>(reinterpret_cast<uint64_t *>(smem + Cfg::kBarOff) + Cfg::kWarps * kStages);
   volatile int *last_flag = abort_flag + 1;
 
   const int seq = blockIdx.z;
@@ -276,7 +284,7 @@ __global__ void __launch_bounds__(DecodeCfg<D, HPC>::kThreads, 2)
   const int32_t *table = a.tables + static_cast<int64_t>(seq) * a.table_stride;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < HPC * kStages; ++s)
+    for (int s = 0; s < Cfg::kWarps * kStages; ++s)
       mbar_init(reinterpret_cast<uint64_t *>(smem + Cfg::kBarOff) + s, 32);
     *abort_flag = 0;
     *last_flag = 0;
@@ -285,7 +293,10 @@ __global__ void __launch_bounds__(DecodeCfg<D, HPC>::kThreads, 2)
   __syncthreads();
 
   // ---------------- each warp: KV head hg * HPC + warp, every page ----------------
-  const int kvh = hg * HPC + warp;
+  // (KW > 1: every warp on head hg, pages wsub, wsub + KW, ...)
+  const int kvh = KW == 1 ? hg * HPC + warp : hg;
+  const int wsub = KW == 1 ? 0 : warp;
+  const int my_pages = npages > wsub ? (npages - wsub + KW - 1) / KW : 0;
   const uint32_t ring = smem_u32(smem) + warp * Cfg::kWarpRing;
   const int64_t head_off = static_cast<int64_t>(kvh) * D;
   const int64_t row_elems = static_cast<int64_t>(a.Hkv) * D;  // elements per cache token row
@@ -331,7 +342,10 @@ __global__ void __launch_bounds__(DecodeCfg<D, HPC>::kThreads, 2)
   };
 
 #pragma unroll 1
-  for (int pg = 0; pg < kStages - 1 && pg < npages; ++pg) load_page(pg, block_of(pg), pg % kStages);
+  for (int j = 0; j < kStages - 1 && j < my_pages; ++j) {
+    const int pg = wsub + j * KW;
+    load_page(pg, block_of(pg), j % kStages);
+  }
 
   const int g = lane >> 2;  // MMA row (query head within the group), and +8
   const int cq = lane & 3;  // MMA column pair
@@ -355,10 +369,14 @@ __global__ void __launch_bounds__(DecodeCfg<D, HPC>::kThreads, 2)
   const int rr = lane & 7;
   bool ok = true;
 
-  for (int i = 0; i < npages; ++i) {
-    // Keep kStages - 1 pages in flight: the slot refilled here held page
-    // i - 1, which this warp finished in the previous iteration.
-    if (i + kStages - 1 < npages) load_page(i + kStages - 1, block_of(i + kStages - 1), (i + kStages - 1) % kStages);
+  for (int i = 0; i < my_pages; ++i) {
+    // Keep kStages - 1 pages in flight: the slot refilled here held this
+    // warp's previous page, which it finished in the previous iteration.
+    if (i + kStages - 1 < my_pages) {
+      const int pg_next = wsub + (i + kStages - 1) * KW;
+      load_page(pg_next, block_of(pg_next), (i + kStages - 1) % kStages);
+    }
+    const int pg = wsub + i * KW;
     const int s = i % kStages;
     const uint32_t ph = (i / kStages) & 1;
     if (!__all_sync(0xffffffffu, mbar_wait(&ready[s], ph, abort_flag))) { ok = false; break; }
@@ -378,7 +396,7 @@ __global__ void __launch_bounds__(DecodeCfg<D, HPC>::kThreads, 2)
       mma_16816<kBf16>(sc[1], qa[ks], b2, b3);
     }
     // Online softmax (rows g and g + 8; columns = tokens 8 * nt + 2 * cq + {0, 1}).
-    const int pos0 = (p_begin + i) * kPageTokens + 2 * cq;
+    const int pos0 = (p_begin + pg) * kPageTokens + 2 * cq;
     float mx[2] = {-INFINITY, -INFINITY};
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt) {
@@ -453,7 +471,71 @@ __global__ void __launch_bounds__(DecodeCfg<D, HPC>::kThreads, 2)
     l_run[hr] += __shfl_xor_sync(0xffffffffu, l_run[hr], 2);
   }
   asm volatile("bar.sync 1, %0;" ::"n"(kConsumers) : "memory");
-  if (!ok || *abort_flag) return;
+  if (!ok || *abort_flag) return;  // a failed wait raised the (CTA-wide) abort flag
+
+  if constexpr (KW > 1) {
+    // Merge the warps' partial softmax results: rescale each to the rows'
+    // common maximum, sum in shared memory; warp 0 carries the result.
+    float *ml = reinterpret_cast<float *>(smem);  // [KW][16][2]: (m, l)
+    float *obuf = reinterpret_cast<float *>(smem + Cfg::kMergeObufOff);
+    if (cq == 0) {
+#pragma unroll
+      for (int hr = 0; hr < 2; ++hr) {
+        ml[(warp * 16 + g + 8 * hr) * 2] = m_run[hr];
+        ml[(warp * 16 + g + 8 * hr) * 2 + 1] = l_run[hr];
+      }
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(kConsumers) : "memory");
+    float scale[2], m_all[2], l_all[2];
+#pragma unroll
+    for (int hr = 0; hr < 2; ++hr) {
+      const int row = g + 8 * hr;
+      m_all[hr] = -INFINITY;
+#pragma unroll
+      for (int w = 0; w < KW; ++w) m_all[hr] = fmaxf(m_all[hr], ml[(w * 16 + row) * 2]);
+      l_all[hr] = 0.f;
+#pragma unroll
+      for (int w = 0; w < KW; ++w) {
+        const float mw = ml[(w * 16 + row) * 2];
+        l_all[hr] += mw == -INFINITY ? 0.f : ml[(w * 16 + row) * 2 + 1] * exp2f(mw - m_all[hr]);
+      }
+      scale[hr] = m_run[hr] == -INFINITY ? 0.f : exp2f(m_run[hr] - m_all[hr]);
+    }
+#pragma unroll
+    for (int n = 0; n < kNTiles; ++n) {
+      const int col = n * 8 + 2 * cq;
+      *reinterpret_cast<float2 *>(obuf + (warp * 16 + g) * D + col) = make_float2(o[n][0] * scale[0], o[n][1] * scale[0]);
+      *reinterpret_cast<float2 *>(obuf + (warp * 16 + g + 8) * D + col) =
+          make_float2(o[n][2] * scale[1], o[n][3] * scale[1]);
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(kConsumers) : "memory");
+    if (warp == 0) {
+#pragma unroll
+      for (int n = 0; n < kNTiles; ++n) {
+        const int col = n * 8 + 2 * cq;
+        float2 s0 = make_float2(0.f, 0.f), s1 = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int w = 0; w < KW; ++w) {
+          const float2 v0 = *reinterpret_cast<const float2 *>(obuf + (w * 16 + g) * D + col);
+          const float2 v1 = *reinterpret_cast<const float2 *>(obuf + (w * 16 + g + 8) * D + col);
+          s0.x += v0.x;
+          s0.y += v0.y;
+          s1.x += v1.x;
+          s1.y += v1.y;
+        }
+        o[n][0] = s0.x;
+        o[n][1] = s0.y;
+        o[n][2] = s1.x;
+        o[n][3] = s1.y;
+      }
+#pragma unroll
+      for (int hr = 0; hr < 2; ++hr) {
+        m_run[hr] = m_all[hr];
+        l_run[hr] = l_all[hr];
+      }
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(kConsumers) : "memory");  // scratch free again
+  }
 
   // Each warp writes its own heads: the final output when the request has one
   // split, else this split's normalised output and log2-sum-exp; the last split
@@ -462,7 +544,7 @@ __global__ void __launch_bounds__(DecodeCfg<D, HPC>::kThreads, 2)
 #pragma unroll
   for (int hr = 0; hr < 2; ++hr) {
     const int row = g + 8 * hr;
-    if (row >= group) continue;
+    if (row >= group || (KW > 1 && warp != 0)) continue;
     const int h = kvh * group + row;
     const float inv = 1.f / l_run[hr];
     if (nsplit == 1) {
