@@ -442,6 +442,8 @@ GemvPlan gemv_plan(int64_t m, int64_t k, const PackedShape &sh, int64_t g, int s
     return mt == 1 ? lvb::awqg::GemvSmem<1>::bytes(gps, rpg)
                    : mt == 2 ? lvb::awqg::GemvSmem<2>::bytes(gps, rpg) : lvb::awqg::GemvSmem<4>::bytes(gps, rpg);
   };
+  // Four CTAs per SM: best or tied among 2 / 3 / 4 / 6 on every 7B shape
+  // (B200); the 16 MB QKV / o shapes sit at an ~8 us latency floor anyway.
   const long long target = 4LL * sms;
   int splits = static_cast<int>((target + sh.n_tiles - 1) / sh.n_tiles);
   if (splits < 1) splits = 1;
