@@ -149,6 +149,19 @@ LVB_API int lvb_awq_linear_packed(const uint16_t *x, const void *codes, const vo
                                   int64_t n, int64_t group_size, void *workspace,
                                   size_t workspace_bytes, lvb_stream_t stream);
 
+/* y = (silu(gate) * up) @ W (+ bias) on the packed layout, with the SiLU-mul
+ * computed inside the activation prologue of the decode kernels (fp32, one
+ * fp16 rounding, as lvb_silu_mul): gate_up holds m rows of [gate (k values) |
+ * up (k values)], gate_up_stride elements apart.  Replaces `silu_and_mul`
+ * followed by the down projection (modeling/models/qwen2.py:237-247,
+ * _qwen2_kernels.py:45-64).  Covers the decode batches of the one-row GEMV
+ * and the int8 path (m <= 32, groups of 128 / 256); other shapes return
+ * LVB_ERR_UNSUPPORTED and the caller runs lvb_silu_mul + lvb_awq_linear_packed. */
+LVB_API int lvb_awq_silu_linear_packed(const uint16_t *gate_up, int64_t gate_up_stride, const void *codes,
+                                       const void *groups, const uint16_t *bias, uint16_t *y, int64_t m, int64_t k,
+                                       int64_t n, int64_t group_size, void *workspace, size_t workspace_bytes,
+                                       lvb_stream_t stream);
+
 /* ------------------------------------------------------------------------ */
 /* Paged K/V cache                                                           */
 /* ------------------------------------------------------------------------ */

@@ -123,6 +123,36 @@ class B200AWQOperation:
         )
         return out.reshape(*inputs.shape[:-1], self.output_width)
 
+    def silu_mul_linear(self, gate_up: Tensor) -> Tensor:
+        """``self(silu(gate) * up)`` for merged [gate | up] rows of 2 x inner
+        values (the Qwen2 MLP's down projection after ``silu_and_mul``,
+        qwen2.py:237-247).  Decode batches run the SiLU-mul inside the
+        projection's activation prologue (``lvb_awq_silu_linear_packed``);
+        other shapes run ``lvb_silu_mul`` and then the projection."""
+
+        flat = gate_up.reshape(-1, 2 * self.inner)
+        if flat.dtype != torch.float16:
+            raise ValueError("B200 AWQ activations must be float16")
+        if not flat.is_contiguous() or flat.data_ptr() % 16:
+            flat = flat.contiguous()
+        rows = flat.shape[0]
+        lib = _native.library()
+        stream = torch.cuda.current_stream(flat.device).cuda_stream
+        if self.codes is not None:
+            out = torch.empty((rows, self.output_width), dtype=torch.float16, device=flat.device)
+            status = lib.lvb_awq_silu_linear_packed(
+                flat.data_ptr(), flat.stride(0), self.codes.data_ptr(), self.groups.data_ptr(),
+                None if self.bias is None else self.bias.data_ptr(), out.data_ptr(), rows, self.inner,
+                self.output_width, self.group_size, self.workspace.data_ptr(), self.workspace.numel(), stream)
+            if status == _native.LVB_OK:
+                return out.reshape(*gate_up.shape[:-1], self.output_width)
+            if status != _native.LVB_ERR_UNSUPPORTED:
+                _native.check(status, "lvb_awq_silu_linear_packed")
+        act = torch.empty((rows, self.inner), dtype=torch.float16, device=flat.device)
+        _native.check(lib.lvb_silu_mul(flat.data_ptr(), flat.stride(0), rows, self.inner, act.data_ptr(),
+                                       act.stride(0), stream), "lvb_silu_mul")
+        return self(act).reshape(*gate_up.shape[:-1], self.output_width)
+
 
 def prepare_b200_awq_operation(qweight: Tensor, qzeros: Tensor, scales: Tensor, group_size: int,
                                bias: Tensor | None) -> B200AWQOperation:

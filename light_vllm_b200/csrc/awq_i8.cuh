@@ -127,9 +127,13 @@ __host__ __device__ __forceinline__ int sw64(int row, int byte) {
 // One warp per (group, token row t < BN); rows t >= M are written as zeros.
 // Each lane handles 4 consecutive k (one quad) per pass and stores the quad's
 // two limbs as one 32-bit word each, bytes in the (0, 2, 1, 3) order.
+// x rows are x_stride elements apart.  gated: x holds merged [gate | up] rows
+// of 2K values and the activation is fp16(silu(gate) * up), rounded exactly as
+// lvb_silu_mul rounds it (the SiLU-mul fused into the down projection).
 template <int BN>
-__global__ void __launch_bounds__(32) awq_act_limbs_kernel(const uint16_t *__restrict__ x, int8_t *__restrict__ limbs,
-                                                           int2 *__restrict__ scal, int M, int K, int G) {
+__global__ void __launch_bounds__(32) awq_act_limbs_kernel(const uint16_t *__restrict__ x, int64_t x_stride, int gated,
+                                                           int8_t *__restrict__ limbs, int2 *__restrict__ scal,
+                                                           int M, int K, int G) {
   // The AWQ kernel that reads these limbs may start now and overlap this
   // grid; it waits for its completion before touching the outputs.  This
   // grid waits for the kernel that produced x.
@@ -138,10 +142,24 @@ __global__ void __launch_bounds__(32) awq_act_limbs_kernel(const uint16_t *__res
   const int t = blockIdx.y;
   const int lane = threadIdx.x;
   const bool row_ok = t < M;
-  const uint16_t *xrow = x + static_cast<size_t>(row_ok ? t : 0) * K + static_cast<size_t>(g) * G;
+  const uint16_t *xrow = x + static_cast<size_t>(row_ok ? t : 0) * x_stride + static_cast<size_t>(g) * G;
+  // Four consecutive activations at k = g * G + i.
+  auto load4 = [&](int i) -> uint2 {
+    if (!row_ok) return make_uint2(0u, 0u);
+    const uint2 gv = *reinterpret_cast<const uint2 *>(xrow + i);
+    if (!gated) return gv;
+    const uint2 uv = *reinterpret_cast<const uint2 *>(xrow + K + i);
+    const float2 g0 = __half22float2(*reinterpret_cast<const __half2 *>(&gv.x));
+    const float2 g1 = __half22float2(*reinterpret_cast<const __half2 *>(&gv.y));
+    const float2 u0 = __half22float2(*reinterpret_cast<const __half2 *>(&uv.x));
+    const float2 u1 = __half22float2(*reinterpret_cast<const __half2 *>(&uv.y));
+    const __half2 a0 = __floats2half2_rn(silu_times(g0.x, u0.x), silu_times(g0.y, u0.y));
+    const __half2 a1 = __floats2half2_rn(silu_times(g1.x, u1.x), silu_times(g1.y, u1.y));
+    return make_uint2(*reinterpret_cast<const uint32_t *>(&a0), *reinterpret_cast<const uint32_t *>(&a1));
+  };
   float amax = 0.f;
   for (int i = 4 * lane; i < G; i += 128) {
-    const uint2 raw = row_ok ? *reinterpret_cast<const uint2 *>(xrow + i) : make_uint2(0u, 0u);
+    const uint2 raw = load4(i);
     const __half2 h0 = *reinterpret_cast<const __half2 *>(&raw.x);
     const __half2 h1 = *reinterpret_cast<const __half2 *>(&raw.y);
     amax = fmaxf(amax, fmaxf(fmaxf(fabsf(__low2float(h0)), fabsf(__high2float(h0))),
@@ -155,7 +173,7 @@ __global__ void __launch_bounds__(32) awq_act_limbs_kernel(const uint16_t *__res
   const float inv_a = ldexpf(1.f, -e);
   int isum = 0;
   for (int i = 4 * lane; i < G; i += 128) {
-    const uint2 raw = row_ok ? *reinterpret_cast<const uint2 *>(xrow + i) : make_uint2(0u, 0u);
+    const uint2 raw = load4(i);
     const __half2 h0 = *reinterpret_cast<const __half2 *>(&raw.x);
     const __half2 h1 = *reinterpret_cast<const __half2 *>(&raw.y);
     const float v[4] = {__low2float(h0), __high2float(h0), __low2float(h1), __high2float(h1)};

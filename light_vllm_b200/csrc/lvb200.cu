@@ -351,7 +351,7 @@ I8Plan i8_plan(int64_t m, int64_t k, const PackedShape &sh, int64_t g, int sms, 
 template <int BN>
 int launch_awq_i8(const I8Plan &plan, const PackedShape &sh, const uint16_t *x, const uint8_t *codes,
                   const uint32_t *groups, const uint16_t *bias, uint16_t *y, int64_t m, int64_t k, int64_t n,
-                  int64_t g, uint8_t *ws, int dev, cudaStream_t stream) {
+                  int64_t g, uint8_t *ws, int dev, cudaStream_t stream, int64_t x_stride, int gated) {
   using C = lvb::awqi8::I8Config<BN>;
   static bool smem_done[kMaxDevices] = {false};
   auto kernel = lvb::awqi8::awq_i8_kernel<BN>;
@@ -360,7 +360,8 @@ int launch_awq_i8(const I8Plan &plan, const PackedShape &sh, const uint16_t *x, 
   int8_t *limbs = reinterpret_cast<int8_t *>(ws + plan.sem_bytes + plan.part_bytes);
   int2 *scal = reinterpret_cast<int2 *>(ws + plan.sem_bytes + plan.part_bytes + plan.limb_bytes);
   cudaError_t e = launch_pdl(lvb::awqi8::awq_act_limbs_kernel<BN>, dim3(sh.groups, BN), dim3(32), 0, stream, x,
-                             limbs, scal, static_cast<int>(m), static_cast<int>(k), static_cast<int>(g));
+                             x_stride, gated, limbs, scal, static_cast<int>(m), static_cast<int>(k),
+                             static_cast<int>(g));
   if (e != cudaSuccess) return cuda_fail(e, "awq_act_limbs_kernel launch");
   lvb::awqi8::I8Params p{};
   p.qpack = codes;
@@ -476,7 +477,7 @@ GemvPlan gemv_plan(int64_t m, int64_t k, const PackedShape &sh, int64_t g, int s
 template <int MT>
 int launch_awq_gemv(const GemvPlan &plan, const PackedShape &sh, const uint16_t *x, const uint8_t *codes,
                     const uint32_t *groups, const uint16_t *bias, uint16_t *y, int64_t m, int64_t k, int64_t n,
-                    int64_t g, uint8_t *ws, int dev, cudaStream_t stream) {
+                    int64_t g, uint8_t *ws, int dev, cudaStream_t stream, int64_t x_stride, int gated) {
   static bool smem_done[kMaxDevices] = {false};
   auto kernel = lvb::awqg::awq_gemv_kernel<MT>;
   int rc = ensure_smem(kernel, static_cast<int>(kGemvMaxSmem), dev, smem_done);
@@ -484,8 +485,8 @@ int launch_awq_gemv(const GemvPlan &plan, const PackedShape &sh, const uint16_t 
   int8_t *limbs = reinterpret_cast<int8_t *>(ws + plan.sem_bytes + plan.part_bytes);
   int2 *scal = reinterpret_cast<int2 *>(ws + plan.sem_bytes + plan.part_bytes + plan.limb_bytes);
   cudaError_t e = launch_pdl(lvb::awqi8::awq_act_limbs_kernel<lvb::awqg::kLimbBN>, dim3(sh.groups, lvb::awqg::kLimbBN),
-                             dim3(32), 0, stream, x, limbs, scal, static_cast<int>(m), static_cast<int>(k),
-                             static_cast<int>(g));
+                             dim3(32), 0, stream, x, x_stride, gated, limbs, scal, static_cast<int>(m),
+                             static_cast<int>(k), static_cast<int>(g));
   if (e != cudaSuccess) return cuda_fail(e, "awq_act_limbs_kernel launch");
   lvb::awqg::GemvParams p{};
   p.qpack = codes;
@@ -813,17 +814,17 @@ int lvb_awq_linear_packed(const uint16_t *x, const void *codes, const void *grou
     const uint8_t *c8 = static_cast<const uint8_t *>(codes);
     const uint32_t *g8 = static_cast<const uint32_t *>(groups);
     uint8_t *w8 = static_cast<uint8_t *>(workspace);
-    if (gp.mt == 1) return launch_awq_gemv<1>(gp, sh, x, c8, g8, bias, y, m, k, n, group_size, w8, dev, stream_);
-    if (gp.mt == 2) return launch_awq_gemv<2>(gp, sh, x, c8, g8, bias, y, m, k, n, group_size, w8, dev, stream_);
-    if (gp.mt == 4) return launch_awq_gemv<4>(gp, sh, x, c8, g8, bias, y, m, k, n, group_size, w8, dev, stream_);
+    if (gp.mt == 1) return launch_awq_gemv<1>(gp, sh, x, c8, g8, bias, y, m, k, n, group_size, w8, dev, stream_, k, 0);
+    if (gp.mt == 2) return launch_awq_gemv<2>(gp, sh, x, c8, g8, bias, y, m, k, n, group_size, w8, dev, stream_, k, 0);
+    if (gp.mt == 4) return launch_awq_gemv<4>(gp, sh, x, c8, g8, bias, y, m, k, n, group_size, w8, dev, stream_, k, 0);
   }
   if (i8_eligible(m, k, n, group_size) && aligned16(y)) {  // y is written by TMA stores
     const I8Plan ip = i8_plan(m, k, sh, group_size, sm_count(dev), max_ws);
     const uint8_t *c8 = static_cast<const uint8_t *>(codes);
     const uint32_t *g8 = static_cast<const uint32_t *>(groups);
     uint8_t *w8 = static_cast<uint8_t *>(workspace);
-    if (ip.bn == 16) return launch_awq_i8<16>(ip, sh, x, c8, g8, bias, y, m, k, n, group_size, w8, dev, stream_);
-    if (ip.bn == 32) return launch_awq_i8<32>(ip, sh, x, c8, g8, bias, y, m, k, n, group_size, w8, dev, stream_);
+    if (ip.bn == 16) return launch_awq_i8<16>(ip, sh, x, c8, g8, bias, y, m, k, n, group_size, w8, dev, stream_, k, 0);
+    if (ip.bn == 32) return launch_awq_i8<32>(ip, sh, x, c8, g8, bias, y, m, k, n, group_size, w8, dev, stream_, k, 0);
   }
   // The plan never needs more split-K workspace than the caller passed.
   const PackedPlan plan = packed_plan(m, sh, sm_count(dev), max_ws);
@@ -838,6 +839,41 @@ int lvb_awq_linear_packed(const uint16_t *x, const void *codes, const void *grou
     case 128: return launch_awq_packed<128, 2, 2, true>(plan, sh, x, c, g, bias, y, m, k, n, group_size, ws, dev, s);
     default: return launch_awq_packed<256, 1, 1, false>(plan, sh, x, c, g, bias, y, m, k, n, group_size, ws, dev, s);
   }
+}
+
+int lvb_awq_silu_linear_packed(const uint16_t *gate_up, int64_t gate_up_stride, const void *codes,
+                               const void *groups, const uint16_t *bias, uint16_t *y, int64_t m, int64_t k, int64_t n,
+                               int64_t group_size, void *workspace, size_t workspace_bytes, lvb_stream_t stream) {
+  int rc = check_awq_shape(m, k, n, group_size);
+  if (rc != LVB_OK) return rc;
+  if (m == 0) return LVB_OK;
+  if (!gate_up || !codes || !groups || !y) return fail(LVB_ERR_INVALID, "AWQ null pointer argument");
+  if (gate_up_stride < 2 * k || gate_up_stride % 8 != 0)
+    return fail(LVB_ERR_INVALID, "gate/up row stride %lld must cover 2 x %lld values and be a multiple of 8",
+                (long long)gate_up_stride, (long long)k);
+  if (!aligned16(gate_up) || !aligned16(codes) || !aligned16(groups) || (workspace && !aligned16(workspace)))
+    return fail(LVB_ERR_INVALID, "AWQ gate/up, packed buffers and workspace must be 16-byte aligned");
+  int dev = 0;
+  rc = current_device(&dev);
+  if (rc != LVB_OK) return rc;
+  const PackedShape sh = packed_shape(k, n, group_size);
+  const size_t max_ws = workspace != nullptr ? workspace_bytes : 0;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const uint8_t *c8 = static_cast<const uint8_t *>(codes);
+  const uint32_t *g8 = static_cast<const uint32_t *>(groups);
+  uint8_t *w8 = static_cast<uint8_t *>(workspace);
+  if (gemv_eligible(m, k, n, group_size)) {
+    const GemvPlan gp = gemv_plan(m, k, sh, group_size, sm_count(dev), max_ws);
+    if (gp.mt == 1) return launch_awq_gemv<1>(gp, sh, gate_up, c8, g8, bias, y, m, k, n, group_size, w8, dev, st, gate_up_stride, 1);
+    if (gp.mt == 2) return launch_awq_gemv<2>(gp, sh, gate_up, c8, g8, bias, y, m, k, n, group_size, w8, dev, st, gate_up_stride, 1);
+    if (gp.mt == 4) return launch_awq_gemv<4>(gp, sh, gate_up, c8, g8, bias, y, m, k, n, group_size, w8, dev, st, gate_up_stride, 1);
+  }
+  if (i8_eligible(m, k, n, group_size) && aligned16(y)) {
+    const I8Plan ip = i8_plan(m, k, sh, group_size, sm_count(dev), max_ws);
+    if (ip.bn == 16) return launch_awq_i8<16>(ip, sh, gate_up, c8, g8, bias, y, m, k, n, group_size, w8, dev, st, gate_up_stride, 1);
+    if (ip.bn == 32) return launch_awq_i8<32>(ip, sh, gate_up, c8, g8, bias, y, m, k, n, group_size, w8, dev, st, gate_up_stride, 1);
+  }
+  return fail(LVB_ERR_UNSUPPORTED, "fused SiLU-mul linear covers decode batches (m <= 32, groups of 128 / 256) only");
 }
 
 static int kv_write_common(const lvb::attn::KVWriteArgs &a, int dtype, lvb_stream_t stream) {

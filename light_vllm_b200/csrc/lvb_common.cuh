@@ -52,6 +52,10 @@ __device__ __forceinline__ void pdl_entry() {
   pdl_wait();
 }
 
+// silu(g) * u in fp32 (the arithmetic of _qwen2_kernels.py:45-64); callers
+// round the result to fp16 once.
+__device__ __forceinline__ float silu_times(float g, float u) { return g / (1.f + expf(-g)) * u; }
+
 // ------------------------------------------------------------------------
 // mbarrier
 // ------------------------------------------------------------------------

@@ -93,7 +93,6 @@ struct SiluArgs {
   int tokens, inter;
 };
 
-__device__ __forceinline__ float silu_mul1(float g, float u) { return g / (1.f + expf(-g)) * u; }
 
 // I % 8 == 0 and 16-byte aligned rows: one 16-byte vector per thread-step.
 __global__ void __launch_bounds__(kSiluThreads) silu_mul_kernel(const __grid_constant__ SiluArgs a) {
@@ -112,7 +111,7 @@ __global__ void __launch_bounds__(kSiluThreads) silu_mul_kernel(const __grid_con
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       const float2 gf = __half22float2(g[e]), uf = __half22float2(u[e]);
-      o[e] = __floats2half2_rn(silu_mul1(gf.x, uf.x), silu_mul1(gf.y, uf.y));
+      o[e] = __floats2half2_rn(silu_times(gf.x, uf.x), silu_times(gf.y, uf.y));
     }
     *reinterpret_cast<uint4 *>(a.out + static_cast<size_t>(t) * a.out_stride + c * 8) = ov;
   }

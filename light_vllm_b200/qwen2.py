@@ -15,8 +15,9 @@ fewer than ranks: qwen2.py:290-318, tensor_parallel.py:248-330):
     rope(q, k)                            lvb_rope_qk, in place
     attn = attention.forward(q, k, v)     B200PagedAttention (writes K/V)
     x, residual = allreduce_add_rmsnorm(AWQ_o(attn), residual, post_norm)
-    act  = silu(gate) * up                lvb_silu_mul over the merged gate/up
-    x, residual = allreduce_add_rmsnorm(AWQ_down(act), residual, next norm)
+    x, residual = allreduce_add_rmsnorm(AWQ_down(silu(gate) * up), residual, next norm)
+                                          (the SiLU-mul inside the down projection's
+                                          activation prologue at decode sizes)
   logits = x @ lm_head_shard^T            cuBLAS (plain fp16 GEMM)
   next   = argmax over the full vocabulary (per-shard max + index, gathered)
 
@@ -238,14 +239,6 @@ class Qwen2AWQRunner:
             positions.data_ptr(), self.cos.data_ptr(), self.sin.data_ptr(), self.cos.shape[0],
             torch.cuda.current_stream(self.device).cuda_stream), "lvb_rope_qk")
 
-    def _silu_mul(self, gate_up: Tensor) -> Tensor:
-        inter = gate_up.shape[1] // 2
-        out = torch.empty((gate_up.shape[0], inter), dtype=gate_up.dtype, device=self.device)
-        _native.check(self._lib.lvb_silu_mul(
-            gate_up.data_ptr(), gate_up.stride(0), gate_up.shape[0], inter, out.data_ptr(), out.stride(0),
-            torch.cuda.current_stream(self.device).cuda_stream), "lvb_silu_mul")
-        return out
-
     def _greedy(self, hidden: Tensor) -> Tensor:
         logits = torch.mm(hidden, self.lm_head.t())
         if self.world == 1:
@@ -285,9 +278,11 @@ class Qwen2AWQRunner:
             v = qkv[:, qd + kd:qd + 2 * kd].view(t, lay.kv_heads, s.head_size)
             attn = attention.forward(L.layer_id, q, k, v, scale=self.scale)
             x, residual = all_reduce_add_rms_norm(ws, L.o(attn.reshape(t, qd)), residual, L.ln_post, eps)
-            act = self._silu_mul(L.gate_up(x))
+            # SiLU-mul runs inside the down projection's activation prologue
+            # at decode batch sizes (lvb_awq_silu_linear_packed).
+            down = L.down.silu_mul_linear(L.gate_up(x))
             nxt = self.layers[i + 1].ln_in if i + 1 < len(self.layers) else self.final_norm
-            x, residual = all_reduce_add_rms_norm(ws, L.down(act), residual, nxt, eps)
+            x, residual = all_reduce_add_rms_norm(ws, down, residual, nxt, eps)
         if logit_rows is not None:
             x = x.index_select(0, logit_rows)
         return self._greedy(x)

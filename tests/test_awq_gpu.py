@@ -275,3 +275,26 @@ def test_gemv_with_activation_outliers(m):
     max_abs, rel = oawq.error_metrics(y.float().cpu().numpy(), expected)
     scale = float(np.max(np.abs(expected)))
     assert rel <= REL_L2 and max_abs <= MAX_ABS * max(1.0, scale / 8.0), (m, max_abs, rel, scale)
+
+
+@pytest.mark.parametrize("m", [1, 3, 16, 32, 48])
+def test_silu_mul_linear_matches_oracle(m):
+    """down(silu(gate) * up): decode sizes fuse the SiLU-mul into the
+    activation prologue (lvb_awq_silu_linear_packed), larger batches run
+    lvb_silu_mul and the projection; both against the fp32 oracle on the
+    fp16-rounded activation."""
+
+    k, n, g = 1024, 512, 128
+    qweight, qzeros, scales = oawq.random_checkpoint(k, n, g, seed=m + 301)
+    rng = np.random.default_rng(m + 17)
+    gate_up = (rng.standard_normal((m, 2 * k)) * 2).astype(np.float16)
+    gu = torch.from_numpy(gate_up).float()
+    act = (torch.nn.functional.silu(gu[:, :k]) * gu[:, k:]).half().numpy()
+    expected = oawq.linear_fp32(act, qweight, qzeros, scales, g, None)
+    qw, qz, sc, gu_dev = _gpu(qweight, qzeros, scales, gate_up)
+    op = B200AWQScheme().prepare(qw, qz, sc, g, None)
+    y = op.silu_mul_linear(gu_dev)
+    torch.cuda.synchronize()
+    assert _native.device_error() == 0
+    max_abs, rel = oawq.error_metrics(y.float().cpu().numpy(), expected)
+    assert max_abs <= MAX_ABS and rel <= REL_L2, (m, max_abs, rel)
