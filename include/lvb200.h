@@ -328,6 +328,21 @@ LVB_API int lvb_rope_qk(uint16_t *qkv, int64_t row_stride, int64_t tokens, int64
                         const uint16_t *cos_table, const uint16_t *sin_table, int64_t table_rows,
                         lvb_stream_t stream);
 
+/* lvb_rope_qk and the paged K/V write in one launch (fp16 caches): the
+ * query heads of each QKV row are rotated in place, the key heads rotated
+ * into the token's cache slot and the value heads copied there (slot of token
+ * t as in lvb_paged_kv_write; RoPE position positions[t]).  Replaces
+ * `apply_rotary` (_qwen2_kernels.py:66-133) plus the K/V write of the
+ * attention step (triton_paged_attention.py:31-104, 498-517); the attention
+ * then runs without writing K/V.  head_size % 16 == 0, row_stride a multiple
+ * of 8 covering the Q, K and V heads, 16-byte aligned rows, tables, caches. */
+LVB_API int lvb_rope_kv_write(uint16_t *qkv, int64_t row_stride, int64_t tokens, int64_t num_query_heads,
+                              int64_t num_kv_heads, int64_t head_size, const int32_t *positions,
+                              const uint16_t *cos_table, const uint16_t *sin_table, int64_t table_rows,
+                              uint16_t *key_cache, uint16_t *value_cache, const int32_t *block_tables,
+                              int64_t table_stride, const int32_t *num_computed, const int32_t *query_start_loc,
+                              const int32_t *request_indices, int64_t block_size, lvb_stream_t stream);
+
 /* out[t][c] = silu(g) * u for g = gate_up[t][c], u = gate_up[t][I + c]
  * (fp32 arithmetic, one fp16 rounding).  Replaces `silu_and_mul`
  * (modeling/models/_qwen2_kernels.py:45-64, 183-202) on the merged gate/up

@@ -87,6 +87,11 @@ PROTOTYPES: dict[str, tuple[object, tuple[object, ...]]] = {
         (_c_ptr, _i64, _i64, _i64, _i64, _i64, _c_ptr, _c_ptr, _c_ptr, _i64, _c_ptr),
     ),
     "lvb_silu_mul": (_int, (_c_ptr, _i64, _i64, _i64, _c_ptr, _i64, _c_ptr)),
+    "lvb_rope_kv_write": (
+        _int,
+        (_c_ptr, _i64, _i64, _i64, _i64, _i64, _c_ptr, _c_ptr, _c_ptr, _i64, _c_ptr, _c_ptr, _c_ptr, _i64, _c_ptr,
+         _c_ptr, _c_ptr, _i64, _c_ptr),
+    ),
     "lvb_paged_attention": (
         _int,
         (_c_ptr, _i64, _c_ptr, _c_ptr, _c_ptr, _i64, _c_ptr, _i64, _c_ptr, _c_ptr, _c_ptr, _c_ptr,

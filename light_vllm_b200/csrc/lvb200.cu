@@ -1344,6 +1344,49 @@ int lvb_rope_qk(uint16_t *qkv, int64_t row_stride, int64_t tokens, int64_t num_q
   return e == cudaSuccess ? LVB_OK : cuda_fail(e, "rope_qk_kernel launch");
 }
 
+int lvb_rope_kv_write(uint16_t *qkv, int64_t row_stride, int64_t tokens, int64_t num_query_heads,
+                      int64_t num_kv_heads, int64_t head_size, const int32_t *positions, const uint16_t *cos_table,
+                      const uint16_t *sin_table, int64_t table_rows, uint16_t *key_cache, uint16_t *value_cache,
+                      const int32_t *block_tables, int64_t table_stride, const int32_t *num_computed,
+                      const int32_t *query_start_loc, const int32_t *request_indices, int64_t block_size,
+                      lvb_stream_t stream) {
+  if (tokens < 0 || tokens > INT_MAX || num_query_heads <= 0 || num_kv_heads <= 0 || head_size <= 0 ||
+      head_size % 16 || head_size > 1024 || table_rows <= 0 || table_rows > INT_MAX || block_size <= 0 ||
+      block_size > INT_MAX)
+    return fail(LVB_ERR_INVALID, "rope_kv_write: invalid shape (head size a multiple of 16)");
+  if (row_stride < (num_query_heads + 2 * num_kv_heads) * head_size || row_stride % 8)
+    return fail(LVB_ERR_INVALID, "rope_kv_write: row stride must cover the Q, K and V heads and be a multiple of 8");
+  if (tokens == 0) return LVB_OK;
+  if (!qkv || !positions || !cos_table || !sin_table || !key_cache || !value_cache || !block_tables ||
+      !num_computed || !query_start_loc || !request_indices)
+    return fail(LVB_ERR_INVALID, "rope_kv_write: null pointer argument");
+  if (!aligned16(qkv) || !aligned16(cos_table) || !aligned16(sin_table) || !aligned16(key_cache) ||
+      !aligned16(value_cache))
+    return fail(LVB_ERR_INVALID, "rope_kv_write: rows, tables and caches must be 16-byte aligned");
+  lvb::q2::RopeKVArgs a{};
+  a.qkv = qkv;
+  a.row_stride = row_stride;
+  a.positions = positions;
+  a.cos = cos_table;
+  a.sin = sin_table;
+  a.key_cache = key_cache;
+  a.value_cache = value_cache;
+  a.tables = block_tables;
+  a.table_stride = table_stride;
+  a.computed = num_computed;
+  a.qsl = query_start_loc;
+  a.req = request_indices;
+  a.tokens = static_cast<int>(tokens);
+  a.hq = static_cast<int>(num_query_heads);
+  a.hkv = static_cast<int>(num_kv_heads);
+  a.D = static_cast<int>(head_size);
+  a.bs = static_cast<int>(block_size);
+  a.table_rows = static_cast<int>(table_rows);
+  cudaError_t e = launch_pdl(lvb::q2::rope_kv_write_kernel, dim3(static_cast<unsigned>(tokens)),
+                             dim3(lvb::q2::kRopeThreads), 0, reinterpret_cast<cudaStream_t>(stream), a);
+  return e == cudaSuccess ? LVB_OK : cuda_fail(e, "rope_kv_write_kernel launch");
+}
+
 int lvb_silu_mul(const uint16_t *gate_up, int64_t in_stride, int64_t tokens, int64_t intermediate, uint16_t *out,
                  int64_t out_stride, lvb_stream_t stream) {
   if (tokens < 0 || tokens > INT_MAX || intermediate <= 0 || intermediate % 8 || intermediate > INT_MAX / 2)

@@ -85,6 +85,79 @@ __global__ void __launch_bounds__(kRopeThreads) rope_qk_kernel(const __grid_cons
   }
 }
 
+// RoPE fused with the paged K/V write (the QKV epilogue steps of
+// qwen2.py:380-411 and triton_paged_attention.py:31-104): per token, the query
+// heads are rotated in place (the attention reads them from the QKV rows), the
+// key heads are rotated into the token's cache slot, the value heads copied
+// there.  Slot of token t: request r = req[t], position computed[r] + t -
+// qsl[r] in r's block table; RoPE position: positions[t].  D % 16 == 0,
+// 16-byte aligned rows, tables and cache.
+struct RopeKVArgs {
+  uint16_t *qkv;
+  int64_t row_stride;
+  const int32_t *positions;
+  const uint16_t *cos, *sin;
+  uint16_t *key_cache, *value_cache;  // [blocks][bs][hkv][D]
+  const int32_t *tables;
+  int64_t table_stride;
+  const int32_t *computed, *qsl, *req;
+  int tokens, hq, hkv, D, bs, table_rows;
+};
+
+__device__ __forceinline__ void rope8(const uint4 xa, const uint4 xb, const uint4 ca, const uint4 cb, const uint4 sa,
+                                      const uint4 sb, uint4 &oa, uint4 &ob) {
+  const __half *x1 = reinterpret_cast<const __half *>(&xa), *x2 = reinterpret_cast<const __half *>(&xb);
+  const __half *c1 = reinterpret_cast<const __half *>(&ca), *c2 = reinterpret_cast<const __half *>(&cb);
+  const __half *s1 = reinterpret_cast<const __half *>(&sa), *s2 = reinterpret_cast<const __half *>(&sb);
+  __half *o1 = reinterpret_cast<__half *>(&oa), *o2 = reinterpret_cast<__half *>(&ob);
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const float v1 = __half2float(x1[e]), v2 = __half2float(x2[e]);
+    o1[e] = __float2half_rn(v1 * __half2float(c1[e]) + (-v2) * __half2float(s1[e]));
+    o2[e] = __float2half_rn(v2 * __half2float(c2[e]) + v1 * __half2float(s2[e]));
+  }
+}
+
+__global__ void __launch_bounds__(kRopeThreads) rope_kv_write_kernel(const __grid_constant__ RopeKVArgs a) {
+  pdl_entry();
+  const int t = blockIdx.x;
+  const int pos = a.positions[t];
+  if (pos < 0 || pos >= a.table_rows) {
+    if (threadIdx.x == 0) record_device_error(LVB_DEVERR_INDEX);
+    return;
+  }
+  const int r = a.req[t];
+  const int p = a.computed[r] + (t - a.qsl[r]);
+  const int64_t slot = static_cast<int64_t>(a.tables[static_cast<int64_t>(r) * a.table_stride + p / a.bs]) * a.bs + p % a.bs;
+  const int half = a.D / 2;
+  const int per_head = half / 8;
+  const __half *cs = reinterpret_cast<const __half *>(a.cos) + static_cast<size_t>(pos) * a.D;
+  const __half *sn = reinterpret_cast<const __half *>(a.sin) + static_cast<size_t>(pos) * a.D;
+  __half *row = reinterpret_cast<__half *>(a.qkv) + static_cast<size_t>(t) * a.row_stride;
+  __half *kc = reinterpret_cast<__half *>(a.key_cache) + static_cast<size_t>(slot) * a.hkv * a.D;
+  __half *vc = reinterpret_cast<__half *>(a.value_cache) + static_cast<size_t>(slot) * a.hkv * a.D;
+  const int rope_units = (a.hq + a.hkv) * per_head;
+  const int v_units = a.hkv * (a.D / 8);
+  for (int u = threadIdx.x; u < rope_units + v_units; u += kRopeThreads) {
+    if (u < rope_units) {
+      const int head = u / per_head, i = (u - head * per_head) * 8;
+      const __half *x = row + static_cast<size_t>(head) * a.D;
+      uint4 oa, ob;
+      rope8(*reinterpret_cast<const uint4 *>(x + i), *reinterpret_cast<const uint4 *>(x + i + half),
+            *reinterpret_cast<const uint4 *>(cs + i), *reinterpret_cast<const uint4 *>(cs + i + half),
+            *reinterpret_cast<const uint4 *>(sn + i), *reinterpret_cast<const uint4 *>(sn + i + half), oa, ob);
+      __half *dst = head < a.hq ? row + static_cast<size_t>(head) * a.D : kc + static_cast<size_t>(head - a.hq) * a.D;
+      *reinterpret_cast<uint4 *>(dst + i) = oa;
+      *reinterpret_cast<uint4 *>(dst + i + half) = ob;
+    } else {
+      const int v = u - rope_units;
+      const int h = v / (a.D / 8), d = (v - h * (a.D / 8)) * 8;
+      *reinterpret_cast<uint4 *>(vc + static_cast<size_t>(h) * a.D + d) =
+          *reinterpret_cast<const uint4 *>(row + static_cast<size_t>(a.hq + a.hkv + h) * a.D + d);
+    }
+  }
+}
+
 struct SiluArgs {
   const uint16_t *gate_up;  // [tokens][in_stride]: gate in columns [0, I), up in [I, 2I)
   int64_t in_stride;

@@ -124,8 +124,12 @@ class B200PagedAttention:
     def layer_ids(self) -> frozenset[str]:
         return frozenset(self._layer_ids)
 
-    def forward(self, layer_id: str, query: Tensor, key: Tensor, value: Tensor, *, scale: float) -> Tensor:
-        """Write this step's K/V for ``layer_id`` and return the attention output."""
+    def forward(self, layer_id: str, query: Tensor, key: Tensor, value: Tensor, *, scale: float,
+                write_kv: bool = True) -> Tensor:
+        """Write this step's K/V for ``layer_id`` and return the attention output.
+
+        ``write_kv=False``: the step's K/V are already in the cache
+        (``rope_write_kv``)."""
 
         if layer_id in self._layer_ids:
             raise KVCacheError(f"paged attention layer {layer_id!r} ran more than once")
@@ -139,7 +143,17 @@ class B200PagedAttention:
             raise KVCacheError("B200 paged attention supports head sizes that are multiples of 8 up to 256")
         out = torch.empty((query.shape[0], spec.num_query_heads, spec.head_size),
                           dtype=query.dtype, device=self._device)
-        return self.launch(layer_id, query, key, value, scale=scale, out=out)
+        return self.launch(layer_id, query, key, value, scale=scale, out=out, write_kv=write_kv)
+
+    def rope_write_kv(self, layer_id: str, qkv: Tensor, q_heads: int, kv_heads: int, positions: Tensor,
+                      cos: Tensor, sin: Tensor) -> None:
+        """RoPE on the query and key heads of merged QKV rows, fused with this
+        step's K/V write for ``layer_id`` (``lvb_rope_kv_write``); follow with
+        ``forward(..., write_kv=False)``."""
+
+        _rope_write_kv(self._cache, layer_id, qkv, q_heads, kv_heads, positions, cos, sin, self._tables,
+                       self._table_stride, self._computed, self._query_start, self._request_indices,
+                       self._device)
 
     def launch(self, layer_id: str, query: Tensor, key: Tensor, value: Tensor, *, scale: float,
                out: Tensor, write_kv: bool = True) -> Tensor:
@@ -191,6 +205,22 @@ class B200PagedAttention:
             "lvb_paged_attention",
         )
         return out
+
+
+def _rope_write_kv(cache, layer_id, qkv, q_heads, kv_heads, positions, cos, sin, tables, table_stride, computed,
+                   query_start, request_indices, device) -> None:
+    spec = cache.layer_spec(layer_id)
+    config = cache.config
+    if config.dtype != torch.float16 or qkv.dtype != torch.float16:
+        raise KVCacheError("the fused RoPE + K/V write covers fp16 caches")
+    if (q_heads, kv_heads) != (spec.num_query_heads, spec.num_kv_heads) or positions.dtype != torch.int32:
+        raise KVCacheError("QKV heads or positions do not match the layer")
+    layer = cache.layer(layer_id)
+    _native.check(_native.library().lvb_rope_kv_write(
+        qkv.data_ptr(), qkv.stride(0), qkv.shape[0], q_heads, kv_heads, spec.head_size, positions.data_ptr(),
+        cos.data_ptr(), sin.data_ptr(), cos.shape[0], layer.keys.data_ptr(), layer.values.data_ptr(),
+        tables.data_ptr(), table_stride, computed.data_ptr(), query_start.data_ptr(), request_indices.data_ptr(),
+        config.block_size, torch.cuda.current_stream(device).cuda_stream), "lvb_rope_kv_write")
 
 
 class B200PagedAttentionBackend:

@@ -12,8 +12,8 @@ fewer than ranks: qwen2.py:290-318, tensor_parallel.py:248-330):
   x, residual = allreduce_add_rmsnorm(x, 0, input_layernorm)
   per layer:
     qkv  = AWQ(x) + bias                  B200AWQScheme, merged QKV
-    rope(q, k)                            lvb_rope_qk, in place
-    attn = attention.forward(q, k, v)     B200PagedAttention (writes K/V)
+    rope(q, k) + K/V write                lvb_rope_kv_write (q in place, k, v to the pages)
+    attn = attention.forward(q, ...)      B200PagedAttention (K/V already written)
     x, residual = allreduce_add_rmsnorm(AWQ_o(attn), residual, post_norm)
     x, residual = allreduce_add_rmsnorm(AWQ_down(silu(gate) * up), residual, next norm)
                                           (the SiLU-mul inside the down projection's
@@ -49,7 +49,7 @@ from light_vllm_b200.collectives import (
     partition_dimension,
 )
 from light_vllm_b200.kv_cache import AttentionLayerSpec, KVCacheError, ModelKVCacheSpec
-from light_vllm_b200.paged_attention import _heads_contiguous
+from light_vllm_b200.paged_attention import _heads_contiguous, _rope_write_kv
 
 
 @dataclass(frozen=True, slots=True)
@@ -268,15 +268,21 @@ class Qwen2AWQRunner:
         ws = self.workspace
         eps = s.rms_norm_eps
         qd, kd = lay.q_heads * s.head_size, lay.kv_heads * s.head_size
+        fused_rope = s.head_size % 16 == 0 and hasattr(attention, "rope_write_kv")
         residual = torch.zeros((t, s.hidden_size), dtype=torch.float16, device=self.device)
         x, residual = all_reduce_add_rms_norm(ws, self._embed(input_ids), residual, self.layers[0].ln_in, eps)
         for i, L in enumerate(self.layers):
             qkv = L.qkv(x)
-            self._rope(qkv, positions)
             q = qkv[:, :qd].view(t, lay.q_heads, s.head_size)
             k = qkv[:, qd:qd + kd].view(t, lay.kv_heads, s.head_size)
             v = qkv[:, qd + kd:qd + 2 * kd].view(t, lay.kv_heads, s.head_size)
-            attn = attention.forward(L.layer_id, q, k, v, scale=self.scale)
+            if fused_rope:
+                # RoPE fused with the K/V write (the QKV epilogue of qwen2.py:380-411)
+                attention.rope_write_kv(L.layer_id, qkv, lay.q_heads, lay.kv_heads, positions, self.cos, self.sin)
+                attn = attention.forward(L.layer_id, q, k, v, scale=self.scale, write_kv=False)
+            else:
+                self._rope(qkv, positions)
+                attn = attention.forward(L.layer_id, q, k, v, scale=self.scale)
             x, residual = all_reduce_add_rms_norm(ws, L.o(attn.reshape(t, qd)), residual, L.ln_post, eps)
             # SiLU-mul runs inside the down projection's activation prologue
             # at decode batch sizes (lvb_awq_silu_linear_packed).
@@ -377,21 +383,30 @@ class StaticDecodeAttention:
     def advance(self) -> None:
         self.computed.add_(1)
 
-    def forward(self, layer_id: str, query: Tensor, key: Tensor, value: Tensor, *, scale: float) -> Tensor:
+    def rope_write_kv(self, layer_id: str, qkv: Tensor, q_heads: int, kv_heads: int, positions: Tensor,
+                      cos: Tensor, sin: Tensor) -> None:
+        """RoPE fused with this step's K/V write (``lvb_rope_kv_write``)."""
+
+        _rope_write_kv(self.cache, layer_id, qkv, q_heads, kv_heads, positions, cos, sin, self.tables, self.stride,
+                       self.computed, self.query_start, self.request_indices, self.device)
+
+    def forward(self, layer_id: str, query: Tensor, key: Tensor, value: Tensor, *, scale: float,
+                write_kv: bool = True) -> Tensor:
         spec = self.cache.layer_spec(layer_id)
         config = self.cache.config
         layer = self.cache.layer(layer_id)
         stream = torch.cuda.current_stream(self.device).cuda_stream
         dtype_code = _native.DTYPE_BF16 if config.dtype == torch.bfloat16 else _native.DTYPE_F16
-        key = _heads_contiguous(key, align=8)
-        value = _heads_contiguous(value, align=8)
         query = _heads_contiguous(query, align=2)
-        _native.check(self._lib.lvb_paged_kv_write(
-            key.data_ptr(), key.stride(0), value.data_ptr(), value.stride(0),
-            layer.keys.data_ptr(), layer.values.data_ptr(), self.tables.data_ptr(), self.stride,
-            self.computed.data_ptr(), self.query_start.data_ptr(), self.request_indices.data_ptr(),
-            self.num_seqs, spec.num_kv_heads, spec.head_size, config.block_size, dtype_code, stream),
-            "lvb_paged_kv_write")
+        if write_kv:
+            key = _heads_contiguous(key, align=8)
+            value = _heads_contiguous(value, align=8)
+            _native.check(self._lib.lvb_paged_kv_write(
+                key.data_ptr(), key.stride(0), value.data_ptr(), value.stride(0),
+                layer.keys.data_ptr(), layer.values.data_ptr(), self.tables.data_ptr(), self.stride,
+                self.computed.data_ptr(), self.query_start.data_ptr(), self.request_indices.data_ptr(),
+                self.num_seqs, spec.num_kv_heads, spec.head_size, config.block_size, dtype_code, stream),
+                "lvb_paged_kv_write")
         out = torch.empty((self.num_seqs, spec.num_query_heads, spec.head_size), dtype=query.dtype,
                           device=self.device)
         _native.check(self._lib.lvb_paged_attention(

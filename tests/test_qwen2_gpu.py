@@ -202,3 +202,52 @@ def test_silu_mul_matches_fp32_reference():
                                                  out.stride(0), torch.cuda.current_stream().cuda_stream), "silu")
     ulp = torch.clamp(want.float().abs(), min=2.0**-14) * 2.0**-10
     assert float(((out.cpu().float() - want.float()).abs() / ulp).max()) <= 1.0
+
+
+def test_rope_kv_write_equals_rope_then_write():
+    """lvb_rope_kv_write is bit-identical to lvb_rope_qk followed by
+    lvb_paged_kv_write: rotated queries in place, rotated keys and the values
+    in the tokens' cache slots (two requests, mixed query lengths)."""
+
+    from light_vllm_b200 import _native
+    from oracle.qwen2 import rope_tables
+
+    lib = _native.library()
+    hq, hkv, d, bs, nb = 7, 1, 128, 16, 12
+    g = torch.Generator().manual_seed(11)
+    tokens = 5
+    qkv = torch.randn(tokens, (hq + 2 * hkv) * d, generator=g).half().cuda()
+    cos, sin = (t.cuda() for t in rope_tables(512, d, 1e6))
+    tables = torch.tensor([[3, 7, 1], [9, 0, 5]], dtype=torch.int32, device="cuda")
+    computed = torch.tensor([20, 40], dtype=torch.int32, device="cuda")
+    qsl = torch.tensor([0, 3, 5], dtype=torch.int32, device="cuda")
+    req = torch.tensor([0, 0, 0, 1, 1], dtype=torch.int32, device="cuda")
+    positions = torch.tensor([20, 21, 22, 40, 41], dtype=torch.int32, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    caches = []
+    outs = []
+    for fused in (False, True):
+        kc = torch.zeros(nb, bs, hkv, d, dtype=torch.float16, device="cuda")
+        vc = torch.zeros_like(kc)
+        x = qkv.clone()
+        if fused:
+            _native.check(lib.lvb_rope_kv_write(x.data_ptr(), x.stride(0), tokens, hq, hkv, d, positions.data_ptr(),
+                                                cos.data_ptr(), sin.data_ptr(), cos.shape[0], kc.data_ptr(),
+                                                vc.data_ptr(), tables.data_ptr(), 3, computed.data_ptr(),
+                                                qsl.data_ptr(), req.data_ptr(), bs, stream), "rope_kv_write")
+        else:
+            _native.check(lib.lvb_rope_qk(x.data_ptr(), x.stride(0), tokens, hq, hkv, d, positions.data_ptr(),
+                                          cos.data_ptr(), sin.data_ptr(), cos.shape[0], stream), "rope")
+            k = x[:, hq * d:(hq + hkv) * d]
+            v = x[:, (hq + hkv) * d:]
+            _native.check(lib.lvb_paged_kv_write(k.data_ptr(), x.stride(0), v.data_ptr(), x.stride(0), kc.data_ptr(),
+                                                 vc.data_ptr(), tables.data_ptr(), 3, computed.data_ptr(),
+                                                 qsl.data_ptr(), req.data_ptr(), tokens, hkv, d, bs,
+                                                 _native.DTYPE_F16, stream), "kv_write")
+        torch.cuda.synchronize()
+        caches.append((kc, vc))
+        outs.append(x[:, :hq * d].clone())
+    assert _native.device_error() == 0
+    assert torch.equal(outs[0], outs[1])
+    assert torch.equal(caches[0][0], caches[1][0]) and torch.equal(caches[0][1], caches[1][1])
+    assert bool(caches[1][0].abs().sum() > 0)
