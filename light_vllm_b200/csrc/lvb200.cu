@@ -307,8 +307,14 @@ int launch_awq_packed(const PackedPlan &plan, const PackedShape &sh, const uint1
 
 // int8 tensor-core path for decode batches: m <= 32, groups of 128 or 256 k
 // (one or two whole groups per 256-k stage).
+// The int8 path pays a limb prologue and a persistent-kernel start-up that
+// only large weights amortise: measured on B200 at m = 16 it ties the fp16
+// packed path at 6-8 MB of packed weights, wins above (34 MB: 20.3 vs 24.2 us;
+// 68 MB: 26.9 vs 40.6 us) and loses below (config 1, 2.2 MB: 13.0 vs 8.2 us).
+constexpr int64_t kI8MinWeightBytes = int64_t(8) << 20;
+
 bool i8_eligible(int64_t m, int64_t k, int64_t n, int64_t g) {
-  return m <= 32 && (g == 128 || g == 256) && k % g == 0 && n % 128 == 0;
+  return m <= 32 && (g == 128 || g == 256) && k % g == 0 && n % 128 == 0 && k * n / 2 >= kI8MinWeightBytes;
 }
 
 struct I8Plan {
