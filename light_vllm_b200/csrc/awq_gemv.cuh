@@ -39,7 +39,8 @@ namespace awqg {
 constexpr int kThreads = 128;      // consumer threads: one output column each
 constexpr int kCtaThreads = 160;   // + one producer warp
 constexpr int kStageRuns = 4;      // 32-k runs per stage (8 KB of codes)
-constexpr int kStages = 4;
+constexpr int kStages = 5;         // 40 KB ring: 4 CTAs still fit an SM; measured best of 4 / 5 / 6
+                                   // (7B gate_up m = 1: 19.0 / 17.7 / 24.7 us)
 constexpr int kStageBytes = kStageRuns * 128 * 16;
 constexpr int kLimbBN = 4;         // token rows of the prologue's limb tiles
 constexpr int kMaxM = 4;
