@@ -265,10 +265,20 @@ __global__ void __launch_bounds__(kCtaThreads) awq_gemv_kernel(const __grid_cons
 #pragma unroll
   for (int t = 0; t < MT; ++t) sum[t] = 0.f;
   const float *tp = p.partials + static_cast<size_t>(tile) * p.splits * p.M * kThreads;
-  for (int sp = 0; sp < p.splits; ++sp) {
+  // Eight splits' loads in flight per round, summed in split order.
+  constexpr int kBatch = 8;
+  for (int sp0 = 0; sp0 < p.splits; sp0 += kBatch) {
 #pragma unroll
-    for (int t = 0; t < MT; ++t)
-      if (t < p.M) sum[t] += __ldcg(tp + (static_cast<size_t>(sp) * p.M + t) * kThreads + tid);
+    for (int t = 0; t < MT; ++t) {
+      if (t >= p.M) continue;
+      float v[kBatch];
+#pragma unroll
+      for (int b = 0; b < kBatch; ++b)
+        v[b] = sp0 + b < p.splits ? __ldcg(tp + (static_cast<size_t>(sp0 + b) * p.M + t) * kThreads + tid) : 0.f;
+#pragma unroll
+      for (int b = 0; b < kBatch; ++b)
+        if (sp0 + b < p.splits) sum[t] += v[b];
+    }
   }
   const float b = p.bias ? __half2float(__ushort_as_half(p.bias[n])) : 0.f;
 #pragma unroll
