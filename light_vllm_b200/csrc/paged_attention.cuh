@@ -418,6 +418,10 @@ __global__ void __launch_bounds__(DecodeCfg<D, HPC, KW>::kThreads, 2)
       m_run[hr] = m_new;
       l_run[hr] *= alpha[hr];
     }
+    // P enters the MMA in the cache dtype.  bf16 keeps 8 mantissa bits, so its
+    // rounding error is carried by a second MMA on the remainder (hi + lo ~ 16
+    // bits); fp16 P (11 bits) is used as is, as the reference's Triton kernel
+    // does (tl.dot on fp16 p), one MMA per tile.
     uint32_t pa_hi[4], pa_lo[4];
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt) {
@@ -427,17 +431,12 @@ __global__ void __launch_bounds__(DecodeCfg<D, HPC, KW>::kThreads, 2)
         const float p1 = exp2f(sc[nt][2 * hr + 1] - m_run[hr]);
         l_run[hr] += p0 + p1;
         const uint32_t hi = pack2<kBf16>(p0, p1);
-        float h0, h1;
-        if constexpr (kBf16) {
-          h0 = __uint_as_float(hi << 16);
-          h1 = __uint_as_float(hi & 0xFFFF0000u);
-        } else {
-          const __half2 hh = *reinterpret_cast<const __half2 *>(&hi);
-          h0 = __low2float(hh);
-          h1 = __high2float(hh);
-        }
         pa_hi[nt * 2 + hr] = hi;
-        pa_lo[nt * 2 + hr] = pack2<kBf16>(p0 - h0, p1 - h1);
+        if constexpr (kBf16) {
+          const float h0 = __uint_as_float(hi << 16);
+          const float h1 = __uint_as_float(hi & 0xFFFF0000u);
+          pa_lo[nt * 2 + hr] = pack2<kBf16>(p0 - h0, p1 - h1);
+        }
       }
     }
 #pragma unroll
@@ -456,9 +455,11 @@ __global__ void __launch_bounds__(DecodeCfg<D, HPC, KW>::kThreads, 2)
       uint32_t b0, b1, b2, b3;
       ldsm_x4_trans(addr, b0, b1, b2, b3);
       mma_16816<kBf16>(o[2 * dp], pa_hi, b0, b1);
-      mma_16816<kBf16>(o[2 * dp], pa_lo, b0, b1);
       mma_16816<kBf16>(o[2 * dp + 1], pa_hi, b2, b3);
-      mma_16816<kBf16>(o[2 * dp + 1], pa_lo, b2, b3);
+      if constexpr (kBf16) {
+        mma_16816<kBf16>(o[2 * dp], pa_lo, b0, b1);
+        mma_16816<kBf16>(o[2 * dp + 1], pa_lo, b2, b3);
+      }
     }
     __syncwarp();
   }
