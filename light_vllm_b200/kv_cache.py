@@ -270,6 +270,59 @@ class PagedKVCache:
 
         self.write_prepared(layer_id, key, value, self.prepare_write(slot_mapping))
 
+    def compact(self, block_ids: tuple[int, ...], *, num_computed_tokens: int, num_query_tokens: int,
+                num_reserved_query_tokens: int, retained_query_indices: tuple[int, ...],
+                num_readonly_prefix_blocks: int = 0) -> int:
+        """Move the retained query tokens' K/V from their flattened query slots
+        to the contiguous tail after the computed prefix; returns how many
+        tokens moved.  Same checks, order and messages as the reference
+        (runtime/execution/paged_cache.py:257-326); the rows are gathered first
+        and then written with the sm_100a scatter, so overlapping moves are
+        safe."""
+
+        block_ids = tuple(block_ids)
+        retained = tuple(retained_query_indices)
+        values = (num_computed_tokens, num_query_tokens, num_reserved_query_tokens, num_readonly_prefix_blocks)
+        if any(type(v) is not int or v < 0 for v in values):
+            raise ValueError("paged compact counts must be non-negative integers")
+        if num_reserved_query_tokens < num_query_tokens:
+            raise ValueError("reserved query tokens must cover every actual query")
+        if any(type(i) is not int or i < 0 for i in retained):
+            raise ValueError("retained query indices must be non-negative integers")
+        if len(set(retained)) != len(retained):
+            raise ValueError("retained query indices must be unique")
+        if any(i >= num_query_tokens for i in retained):
+            raise KVCacheError("retained query index exceeds the paged KV tail")
+        config = self._config
+        required = (num_computed_tokens + num_reserved_query_tokens + config.block_size - 1) // config.block_size
+        if len(block_ids) != required:
+            raise KVCacheError("block table does not exactly cover the reserved query slots")
+        if any(type(b) is not int or not 0 <= b < config.num_blocks for b in block_ids):
+            raise KVCacheError("block table contains an invalid physical block")
+        if len(set(block_ids)) != len(block_ids):
+            raise KVCacheError("block table aliases a physical block within one request")
+        if num_readonly_prefix_blocks * config.block_size > num_computed_tokens:
+            raise KVCacheError("readonly prefix blocks exceed the computed prefix")
+
+        def physical_slot(pos: int) -> int:
+            return block_ids[pos // config.block_size] * config.block_size + pos % config.block_size
+
+        source_slots = tuple(physical_slot(num_computed_tokens + i) for i in retained)
+        target_slots = tuple(physical_slot(num_computed_tokens + i) for i in range(len(retained)))
+        if source_slots == target_slots:
+            return 0
+        source = torch.tensor(source_slots, dtype=torch.long, device=config.device)
+        mapping = self.prepare_write(torch.tensor(target_slots, dtype=torch.long, device=config.device))
+        num_slots = config.num_blocks * config.block_size
+        for layer_id, layer in self._layers.items():
+            flat_keys = layer.keys.view(num_slots, *layer.keys.shape[2:])
+            flat_values = layer.values.view(num_slots, *layer.values.shape[2:])
+            # every source row is read before any target is written
+            keys = flat_keys.index_select(0, source)
+            values_ = flat_values.index_select(0, source)
+            self.write_prepared(layer_id, keys, values_, mapping)
+        return sum(a != b for a, b in zip(source_slots, target_slots))
+
     def _allocate_layer(self, spec: AttentionLayerSpec) -> PagedLayerCache:
         shape = (self._config.num_blocks, self._config.block_size, spec.num_kv_heads, spec.head_size)
         return PagedLayerCache(

@@ -265,3 +265,18 @@ def attend_dense_fp64(
             probs = torch.softmax(scores, dim=-1)
             out[starts[row] + offset] = torch.einsum("ht,thd->hd", probs, values)
     return out
+
+
+def compact_slots(block_ids: Sequence[int], *, num_computed_tokens: int, retained_query_indices: Sequence[int],
+                  block_size: int) -> tuple[tuple[int, ...], tuple[int, ...]]:
+    """Source and target physical slots of ``PagedKVCache.compact``
+    (runtime/execution/paged_cache.py:304-311): the retained query tokens move
+    from their flattened query slots to the contiguous tail after the
+    computed prefix."""
+
+    def physical_slot(pos: int) -> int:
+        return block_ids[pos // block_size] * block_size + pos % block_size
+
+    source = tuple(physical_slot(num_computed_tokens + i) for i in retained_query_indices)
+    target = tuple(physical_slot(num_computed_tokens + i) for i in range(len(retained_query_indices)))
+    return source, target

@@ -99,3 +99,64 @@ def test_backend_refuses_cpu_cache():
                                    query_layouts=(kv.linear_query_layout(1),))
     with pytest.raises(kv.KVCacheError, match="requires a CUDA KV cache"):
         B200PagedAttentionBackend().create(cache, md)
+
+
+def test_reference_known_answers_for_metadata():
+    """Known answers of the reference's tests/test_paged_attention.py:121-175:
+    slot mapping across non-contiguous blocks, packed request indices and the
+    tree visibility vector."""
+
+    from oracle import paged_attention as opa
+
+    md = kv.PagedAttentionMetadata(block_tables=((2, 0), (1, 3)), num_computed_tokens=(0, 1),
+                                   query_layouts=(kv.linear_query_layout(3), kv.linear_query_layout(2)))
+    assert md.slot_mapping(block_size=2, device=torch.device("cpu")).tolist() == [4, 5, 0, 3, 6]
+    assert list(opa.slot_mapping(((2, 0), (1, 3)), (0, 1), (3, 2), (3, 2), 2)) == [4, 5, 0, 3, 6]
+
+    tree = kv.PagedAttentionMetadata(block_tables=((0, 1), (2,)), num_computed_tokens=(0, 0),
+                                     query_layouts=(kv.QueryLayout((-1, 0, 0)), kv.linear_query_layout(2)))
+    vis, starts = tree.visibility_tensor(device=torch.device("cpu"))
+    expected = [True, False, False, True, True, False, True, False, True, True, False, True, True]
+    assert tree.query_start_loc == (0, 3, 5)
+    assert tree.request_indices_tensor(device=torch.device("cpu")).tolist() == [0, 0, 0, 1, 1]
+    assert starts.tolist() == [0, 9, 13]
+    assert vis.tolist() == expected
+    ovis, ostarts = opa.visibility_tensor([(-1, 0, 0), (-1, 0)])
+    assert list(ovis) == expected and list(ostarts) == [0, 9, 13]
+
+
+def test_reference_known_answer_for_compaction_slots():
+    """tests/test_paged_attention.py:178-228: retained queries (0, 2, 4) of a
+    5-token tree over blocks (1, 3, 0, 2) move to slots (6, 7, 0)."""
+
+    from oracle import paged_attention as opa
+
+    source, target = opa.compact_slots((1, 3, 0, 2), num_computed_tokens=2, retained_query_indices=(0, 2, 4),
+                                       block_size=2)
+    assert target == (6, 7, 0)
+    assert source == (6, 0, 4)
+
+
+def test_compaction_checks_match_the_reference_order():
+    spec = kv.ModelKVCacheSpec((kv.AttentionLayerSpec("attention", 2, 2, 8),))
+    cache = kv.PagedKVCache.__new__(kv.PagedKVCache)  # checks run before any device work
+    cache._config = kv.PagedKVCacheConfig(4, 2, dtype=torch.float16)
+    cache._layers = {}
+    with pytest.raises(ValueError, match="reserved query tokens must cover"):
+        cache.compact((1, 3, 0), num_computed_tokens=2, num_query_tokens=5, num_reserved_query_tokens=4,
+                      retained_query_indices=(0,))
+    with pytest.raises(ValueError, match="unique"):
+        cache.compact((1, 3, 0), num_computed_tokens=2, num_query_tokens=3, num_reserved_query_tokens=3,
+                      retained_query_indices=(0, 0))
+    with pytest.raises(kv.KVCacheError, match="exceeds the paged KV tail"):
+        cache.compact((1, 3, 0), num_computed_tokens=2, num_query_tokens=3, num_reserved_query_tokens=3,
+                      retained_query_indices=(3,))
+    with pytest.raises(kv.KVCacheError, match="exactly cover"):
+        cache.compact((1, 3), num_computed_tokens=2, num_query_tokens=3, num_reserved_query_tokens=3,
+                      retained_query_indices=(0,))
+    with pytest.raises(kv.KVCacheError, match="aliases"):
+        cache.compact((1, 1, 0), num_computed_tokens=2, num_query_tokens=3, num_reserved_query_tokens=3,
+                      retained_query_indices=(0,))
+    with pytest.raises(kv.KVCacheError, match="readonly prefix"):
+        cache.compact((1, 3, 0), num_computed_tokens=2, num_query_tokens=3, num_reserved_query_tokens=3,
+                      retained_query_indices=(0,), num_readonly_prefix_blocks=2)

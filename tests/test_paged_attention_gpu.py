@@ -317,3 +317,34 @@ def test_strided_qkv_views_are_accepted():
     qv, kv_, vv = fused.split([28 * 128, 4 * 128, 4 * 128], dim=1)
     out = _check_decode(cache, md, qv.view(4, 28, 128), kv_.view(4, 4, 128), vv.view(4, 4, 128))
     assert out.shape == (4, 28, 128)
+
+
+def test_compaction_moves_retained_queries_like_the_reference():
+    """The reference's compaction test (tests/test_paged_attention.py:178-228)
+    on the B200 cache (head size 8 instead of 4: the scatter kernel moves
+    16-byte rows): retained queries (0, 2, 4) land in slots (6, 7, 0) and the
+    readonly prefix block is untouched."""
+
+    spec = ModelKVCacheSpec((AttentionLayerSpec("attention", 2, 2, 8),))
+    cache = PagedKVCache(spec, PagedKVCacheConfig(4, 2, dtype=torch.float16, device=torch.device("cuda")))
+    layer = cache.layer("attention")
+    layer.keys.zero_()
+    layer.values.zero_()
+    prefix_keys = torch.arange(32, dtype=torch.float32).reshape(2, 2, 8).half().cuda()
+    prefix_values = prefix_keys + 100
+    cache.write("attention", prefix_keys, prefix_values, torch.tensor([2, 3], device="cuda"))
+    md = PagedAttentionMetadata(block_tables=((1, 3, 0, 2),), num_computed_tokens=(2,),
+                                query_layouts=(QueryLayout((-1, 0, 0, 2, 3)),), num_readonly_prefix_blocks=(1,))
+    query_keys = (torch.arange(80, dtype=torch.float32).reshape(5, 2, 8) + 40).half().cuda()
+    query_values = query_keys + 200
+    cache.write("attention", query_keys, query_values, md.slot_mapping(block_size=2, device=torch.device("cuda")))
+    moved = cache.compact(md.block_tables[0], num_computed_tokens=2, num_query_tokens=5, num_reserved_query_tokens=5,
+                          retained_query_indices=(0, 2, 4), num_readonly_prefix_blocks=1)
+    torch.cuda.synchronize()
+    assert moved == 2
+    assert torch.equal(layer.keys[1], prefix_keys)
+    flat_k = layer.keys.view(8, 2, 8)
+    flat_v = layer.values.view(8, 2, 8)
+    assert torch.equal(flat_k[[6, 7, 0]], query_keys[[0, 2, 4]])
+    assert torch.equal(flat_v[[6, 7, 0]], query_values[[0, 2, 4]])
+    assert _native.device_error() == 0
