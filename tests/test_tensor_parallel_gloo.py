@@ -126,3 +126,25 @@ def test_partition_and_alignment_rules():
         awq_column_shard(q, q[:2], torch.zeros(2, 192), None, partition_dimension(192, 0, 5))
     with pytest.raises(ValueError, match="align to group_size"):
         awq_row_shard(q, q[:2], torch.zeros(2, 192), 128, partition_dimension(256, 0, 4))
+
+
+def test_qwen2_rank_layout_matches_the_reference_shard_declarations():
+    """The runner's tensor-parallel layout against the reference's declared
+    checkpoint slices (tests/test_tensor_parallel.py:231-256): 4 query / 2 KV
+    heads at TP=2 give 2 / 1 per rank, rank 1's vocabulary shard starts at 5;
+    with 1 KV head both ranks hold the whole KV head (start 0, length 2)."""
+
+    from light_vllm_b200.qwen2 import Qwen2Shape, RankLayout
+
+    cfg = dict(vocab_size=10, hidden_size=8, intermediate_size=12, num_hidden_layers=1, num_attention_heads=4,
+               num_key_value_heads=2, max_position_embeddings=16)
+    lay = RankLayout.of(Qwen2Shape(**cfg), 1, 2)
+    assert (lay.q_heads, lay.kv_heads) == (2, 1)
+    assert lay.vocab_part.start == 5
+    assert (lay.q_part.start, lay.q_part.local_size) == (4, 4)
+    for rank in range(2):
+        rep = RankLayout.of(Qwen2Shape(**dict(cfg, num_key_value_heads=1)), rank, 2)
+        assert rep.kv_heads == 1
+        assert (rep.kv_part.start, rep.kv_part.local_size) == (0, 2)
+    with pytest.raises(ValueError, match="query heads"):
+        RankLayout.of(Qwen2Shape(**dict(cfg, num_attention_heads=6, num_key_value_heads=3)), 0, 4)
