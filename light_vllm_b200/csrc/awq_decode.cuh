@@ -60,9 +60,13 @@ constexpr int kSmemBudget = 216 * 1024;
 // dequantiser warpgroups (warpgroup w takes blocks w, w + DG, ... of a stage).
 // DUAL: the upper 16 k of every 32-k run are dequantised as 16 W and
 // accumulate into a second accumulator (one instruction less per code pair);
-// otherwise one accumulator and exact W throughout.
-template <int BN, int SB, int DG, bool DUAL>
+// otherwise one accumulator and exact W throughout.  TMEM / SMEM_KB: the
+// tensor-memory columns and shared-memory bytes one CTA takes (half of each
+// lets two CTAs share an SM).
+template <int BN, int SB, int DG, bool DUAL, int TMEM = kTmemCols, int SMEM_KB = kSmemBudget / 1024>
 struct PackedConfig {
+  static constexpr int kTmemAlloc = TMEM;
+  static constexpr int kCtasPerSm = TMEM == kTmemCols ? 1 : 2;
   static constexpr int kStageChunks = 2 * SB;
   static constexpr int kQStageBytes = kStageChunks * kChunkBytes;
   static constexpr int kSzStageBytes = kStageChunks * kSzRowBytes;  // at most one group per chunk
@@ -72,12 +76,12 @@ struct PackedConfig {
   static constexpr int kQOff = kXBytes;
   static constexpr int kSzOff = kQOff + kQStageBytes;
   static constexpr int kStageBytes = ((kSzOff + kSzStageBytes) + 1023) / 1024 * 1024;
-  static constexpr int kStages = kSmemBudget / kStageBytes > 8 ? 8 : kSmemBudget / kStageBytes;
+  static constexpr int kStages = SMEM_KB * 1024 / kStageBytes > 8 ? 8 : SMEM_KB * 1024 / kStageBytes;
   // Tensor memory: D_lo [0, BN), D_hi [BN, 2 BN) when DUAL, then the A stages.
   static constexpr int kDHiCol = BN;
   static constexpr int kACol = ((DUAL ? 2 * BN : BN) + 31) / 32 * 32;
   static constexpr int kAStageCols = SB * 32;
-  static constexpr int kAStages = (kTmemCols - kACol) / kAStageCols > 4 ? 4 : (kTmemCols - kACol) / kAStageCols;
+  static constexpr int kAStages = (TMEM - kACol) / kAStageCols > 4 ? 4 : (TMEM - kACol) / kAStageCols;
   static constexpr int kBlocksPerGroup = SB / DG;
   static constexpr int kDqWarps = 4 * DG;
   static constexpr int kThreads = (kFirstDqWarp + kDqWarps) * 32;
@@ -224,11 +228,12 @@ __device__ __forceinline__ void dequant_run(const uint4 q, uint32_t sz, uint32_t
   }
 }
 
-template <int BN, int SB, int DG, bool DUAL>
-__global__ void __launch_bounds__(PackedConfig<BN, SB, DG, DUAL>::kThreads, 1)
+template <int BN, int SB, int DG, bool DUAL, int TMEM = kTmemCols, int SMEM_KB = kSmemBudget / 1024>
+__global__ void __launch_bounds__(PackedConfig<BN, SB, DG, DUAL, TMEM, SMEM_KB>::kThreads,
+                                  PackedConfig<BN, SB, DG, DUAL, TMEM, SMEM_KB>::kCtasPerSm)
     awq_packed_kernel(const __grid_constant__ CUtensorMap xmap, const DecodeParams p) {
   pdl_entry();
-  using C = PackedConfig<BN, SB, DG, DUAL>;
+  using C = PackedConfig<BN, SB, DG, DUAL, TMEM, SMEM_KB>;
   constexpr int kAStages = C::kAStages;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
@@ -272,7 +277,7 @@ __global__ void __launch_bounds__(PackedConfig<BN, SB, DG, DUAL>::kThreads, 1)
     fence_barrier_init();
   }
   if (warp == 2) {
-    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_alloc(tmem_slot, C::kTmemAlloc);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -509,7 +514,7 @@ __global__ void __launch_bounds__(PackedConfig<BN, SB, DG, DUAL>::kThreads, 1)
   __syncthreads();
   if (warp == 2) {
     tc_fence_after();
-    tmem_dealloc(tmem, kTmemCols);
+    tmem_dealloc(tmem, C::kTmemAlloc);
   }
 }
 

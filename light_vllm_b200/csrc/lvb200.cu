@@ -227,6 +227,16 @@ struct PackedPlan {
 // tiles with one accumulator.
 int packed_bn(int64_t m) { return m <= 16 ? 16 : m <= 32 ? 32 : m <= 64 ? 64 : m <= 128 ? 128 : 256; }
 
+// Two CTAs per SM (half the tensor and shared memory each: 128-k or 64-k
+// stages, one dequantiser warpgroup) for the 64- and 128-row token tiles when
+// the output tiles alone fill the GPU: measured on B200 they win without
+// split-K (m = 64, 3584 x 37888: 46.0 -> 38.5 us; m = 128, 8192 x 29696:
+// 136.6 -> 101.8 us) and lose with it (m = 128, 4096 x 8192: 27.6 -> 34.0).
+int packed_ctas_per_sm(int bn, const PackedShape &sh, int64_t m, int sms) {
+  const int64_t tiles = static_cast<int64_t>(sh.n_tiles) * ((m + bn - 1) / bn);
+  return (bn == 64 || bn == 128) && tiles >= sms ? 2 : 1;
+}
+
 // Fixed cost of one CTA (TMEM allocation, pipeline fill and drain, partial
 // tile write and merge) in 64-k blocks of main-loop work; without it the
 // model splits a 4096-deep M = 128 GEMM into 16 CTAs of 4 blocks each and
@@ -264,13 +274,14 @@ PackedPlan packed_plan(int64_t m, const PackedShape &sh, int sms, size_t max_ws 
   return p;
 }
 
-template <int BN, int SB, int DG, bool DUAL>
+template <int BN, int SB, int DG, bool DUAL, int TMEM = lvb::awqd::kTmemCols,
+          int SMEM_KB = lvb::awqd::kSmemBudget / 1024>
 int launch_awq_packed(const PackedPlan &plan, const PackedShape &sh, const uint16_t *x, const uint8_t *codes,
                       const uint32_t *groups, const uint16_t *bias, uint16_t *y, int64_t m, int64_t k,
                       int64_t n, int64_t g, uint8_t *ws, int dev, cudaStream_t stream) {
-  using C = lvb::awqd::PackedConfig<BN, SB, DG, DUAL>;
+  using C = lvb::awqd::PackedConfig<BN, SB, DG, DUAL, TMEM, SMEM_KB>;
   static bool smem_done[kMaxDevices] = {false};
-  auto kernel = lvb::awqd::awq_packed_kernel<BN, SB, DG, DUAL>;
+  auto kernel = lvb::awqd::awq_packed_kernel<BN, SB, DG, DUAL, TMEM, SMEM_KB>;
   int rc = ensure_smem(kernel, C::kSmemBytes, dev, smem_done);
   if (rc != LVB_OK) return rc;
   // Activations as [k / 32 chunks][m rows][32 k]: one box per stage fetches
@@ -700,7 +711,7 @@ size_t lvb_awq_workspace_bytes(int64_t m, int64_t k, int64_t n, int64_t group_si
   size_t need = p.sem_bytes + p.part_bytes;
   if (group_size > 0 && group_size % 32 == 0 && k % group_size == 0) {
     const PackedShape sh = packed_shape(k, n, group_size);
-    const PackedPlan pp = packed_plan(m, sh, sm_count(dev));
+    const PackedPlan pp = packed_plan(m, sh, sm_count(dev) * packed_ctas_per_sm(packed_bn(m), sh, m, sm_count(dev)));
     if (pp.sem_bytes + pp.part_bytes > need) need = pp.sem_bytes + pp.part_bytes;
     if (i8_eligible(m, k, n, group_size)) {
       const I8Plan ip = i8_plan(m, k, sh, group_size, sm_count(dev));
@@ -833,7 +844,8 @@ int lvb_awq_linear_packed(const uint16_t *x, const void *codes, const void *grou
     if (ip.bn == 32) return launch_awq_i8<32>(ip, sh, x, c8, g8, bias, y, m, k, n, group_size, w8, dev, stream_, k, 0);
   }
   // The plan never needs more split-K workspace than the caller passed.
-  const PackedPlan plan = packed_plan(m, sh, sm_count(dev), max_ws);
+  const int per_sm = packed_ctas_per_sm(packed_bn(m), sh, m, sm_count(dev));
+  const PackedPlan plan = packed_plan(m, sh, sm_count(dev) * per_sm, max_ws);
   uint8_t *ws = static_cast<uint8_t *>(workspace);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const uint8_t *c = static_cast<const uint8_t *>(codes);
@@ -841,8 +853,14 @@ int lvb_awq_linear_packed(const uint16_t *x, const void *codes, const void *grou
   switch (plan.bn) {
     case 16: return launch_awq_packed<16, 4, 2, true>(plan, sh, x, c, g, bias, y, m, k, n, group_size, ws, dev, s);
     case 32: return launch_awq_packed<32, 4, 2, true>(plan, sh, x, c, g, bias, y, m, k, n, group_size, ws, dev, s);
-    case 64: return launch_awq_packed<64, 4, 2, true>(plan, sh, x, c, g, bias, y, m, k, n, group_size, ws, dev, s);
-    case 128: return launch_awq_packed<128, 2, 2, true>(plan, sh, x, c, g, bias, y, m, k, n, group_size, ws, dev, s);
+    case 64:
+      if (per_sm == 2)
+        return launch_awq_packed<64, 2, 1, true, 256, 108>(plan, sh, x, c, g, bias, y, m, k, n, group_size, ws, dev, s);
+      return launch_awq_packed<64, 4, 2, true>(plan, sh, x, c, g, bias, y, m, k, n, group_size, ws, dev, s);
+    case 128:
+      if (per_sm == 2)
+        return launch_awq_packed<128, 1, 1, false, 256, 108>(plan, sh, x, c, g, bias, y, m, k, n, group_size, ws, dev, s);
+      return launch_awq_packed<128, 2, 2, true>(plan, sh, x, c, g, bias, y, m, k, n, group_size, ws, dev, s);
     default: return launch_awq_packed<256, 1, 1, false>(plan, sh, x, c, g, bias, y, m, k, n, group_size, ws, dev, s);
   }
 }

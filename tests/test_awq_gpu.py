@@ -300,3 +300,12 @@ def test_silu_mul_linear_matches_oracle(m):
     # fp16 outputs: the absolute bound grows with the output scale (as in the outlier test)
     scale = float(np.max(np.abs(expected)))
     assert rel <= REL_L2 and max_abs <= MAX_ABS * max(1.0, scale / 8.0), (m, max_abs, rel, scale)
+
+
+@pytest.mark.parametrize("m,k,n", [(40, 512, 18944), (64, 768, 18944), (100, 512, 18944), (128, 1024, 19200)])
+def test_packed_two_ctas_per_sm_configs(m, k, n):
+    """64- and 128-row token tiles with at least one output tile per SM run
+    two CTAs per SM (half the tensor and shared memory each, the 128-row
+    tile without the second accumulator)."""
+
+    _check_against_oracle(m, k, n, 128, seed=m + k, with_bias=(m % 2 == 0))
