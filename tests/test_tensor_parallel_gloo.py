@@ -80,7 +80,7 @@ def _shard_worker(rank: int, world: int, port: int, results) -> None:
 def test_awq_shards_and_collectives_match_the_full_linear():
     world = 2
     port = _free_port()
-    with mp.Manager() as manager:
+    with mp.get_context("spawn").Manager() as manager:
         results = manager.dict()
         mp.start_processes(_shard_worker, args=(world, port, results), nprocs=world, start_method="spawn")
         for rank in range(world):
@@ -107,7 +107,7 @@ def _leaving_worker(rank: int, world: int, port: int, results) -> None:
 def test_a_rank_that_leaves_makes_the_next_collective_fail():
     world = 2
     port = _free_port()
-    with mp.Manager() as manager:
+    with mp.get_context("spawn").Manager() as manager:
         results = manager.dict()
         ctx = mp.start_processes(_leaving_worker, args=(world, port, results), nprocs=world,
                                  start_method="spawn", join=False)
