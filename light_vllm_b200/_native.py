@@ -12,9 +12,13 @@ from __future__ import annotations
 
 import ctypes
 import functools
+import importlib.machinery
+import importlib.util
+import sysconfig
 from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().parent / "_lib" / "liblvb200.so"
+HOSTPACK_PATH = Path(__file__).resolve().parent / "_lib" / ("_hostpack" + sysconfig.get_config_var("EXT_SUFFIX"))
 ABI_VERSION = 4
 
 LVB_OK = 0
@@ -125,6 +129,19 @@ def library() -> ctypes.CDLL:
     if version != ABI_VERSION:
         raise NativeLibraryError(f"{LIB_PATH} has ABI {version}, expected {ABI_VERSION}; rebuild it")
     return lib
+
+
+@functools.lru_cache(maxsize=1)
+def hostpack():
+    """The CPython module that reads step metadata out of Python objects."""
+
+    if not HOSTPACK_PATH.is_file():
+        raise NativeLibraryError(f"{HOSTPACK_PATH} is not built; run `python -m light_vllm_b200.build`")
+    loader = importlib.machinery.ExtensionFileLoader("light_vllm_b200._hostpack", str(HOSTPACK_PATH))
+    spec = importlib.util.spec_from_file_location("light_vllm_b200._hostpack", str(HOSTPACK_PATH), loader=loader)
+    module = importlib.util.module_from_spec(spec)
+    loader.exec_module(module)
+    return module
 
 
 def check(status: int, what: str) -> None:

@@ -3,7 +3,9 @@
 One nvcc invocation compiles ``csrc/lvb200.cu`` (which includes every kernel)
 into ``_lib/liblvb200.so`` for ``compute_100a``/``sm_100a`` only, with the CUDA
 runtime linked statically so the library does not depend on which libcudart
-the host process loaded first.
+the host process loaded first.  The small CPython module ``csrc/hostpack.c``
+(step metadata read out of Python objects) is compiled by the C compiler into
+``_lib/_hostpack<suffix>``.
 """
 
 from __future__ import annotations
@@ -12,11 +14,14 @@ import os
 import shutil
 import subprocess
 import sys
+import sysconfig
 from pathlib import Path
 
 PACKAGE = Path(__file__).resolve().parent
 SOURCE = PACKAGE / "csrc" / "lvb200.cu"
 OUTPUT = PACKAGE / "_lib" / "liblvb200.so"
+HOSTPACK_SOURCE = PACKAGE / "csrc" / "hostpack.c"
+HOSTPACK_OUTPUT = PACKAGE / "_lib" / ("_hostpack" + sysconfig.get_config_var("EXT_SUFFIX"))
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
@@ -41,6 +46,26 @@ def sources() -> list[Path]:
     return sorted((PACKAGE / "csrc").glob("*.cu*")) + [PACKAGE.parent / "include" / "lvb200.h"]
 
 
+def build_hostpack(force: bool = False) -> Path:
+    """Compile the CPython step-metadata module if missing or stale."""
+
+    if (not force and HOSTPACK_OUTPUT.is_file()
+            and HOSTPACK_OUTPUT.stat().st_mtime >= HOSTPACK_SOURCE.stat().st_mtime):
+        return HOSTPACK_OUTPUT
+    HOSTPACK_OUTPUT.parent.mkdir(parents=True, exist_ok=True)
+    cc = os.environ.get("CC") or shutil.which("gcc") or shutil.which("cc")
+    if not cc:
+        raise RuntimeError("no C compiler found for csrc/hostpack.c")
+    tmp = HOSTPACK_OUTPUT.with_name(HOSTPACK_OUTPUT.name + ".tmp")
+    cmd = [cc, "-O2", "-shared", "-fPIC", "-fvisibility=hidden", "-Wall",
+           "-I", sysconfig.get_paths()["include"], "-o", str(tmp), str(HOSTPACK_SOURCE)]
+    result = subprocess.run(cmd, capture_output=True, text=True)
+    if result.returncode != 0:
+        raise RuntimeError(f"{cc} failed ({result.returncode}):\n{result.stderr}")
+    os.replace(tmp, HOSTPACK_OUTPUT)
+    return HOSTPACK_OUTPUT
+
+
 def is_stale() -> bool:
     if not OUTPUT.is_file():
         return True
@@ -51,6 +76,7 @@ def is_stale() -> bool:
 def build(force: bool = False, verbose: bool = False) -> Path:
     """Compile the library if it is missing or older than its sources."""
 
+    build_hostpack(force)
     if not force and not is_stale():
         return OUTPUT
     OUTPUT.parent.mkdir(parents=True, exist_ok=True)

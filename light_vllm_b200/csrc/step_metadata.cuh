@@ -10,8 +10,8 @@
 //     runtime/execution/triton_paged_attention.py:422-440): block tables padded
 //     to the longest table, computed counts, query start offsets, and the
 //     request index of every packed query token.
-// Ownership of physical blocks across requests is tracked in thread-local
-// arrays indexed by block id and stamped per call, so a call costs
+// Ownership of physical blocks across requests is tracked in a thread-local
+// table indexed by block id and stamped per call, so a call costs
 // O(total blocks) without clearing anything.
 #pragma once
 
@@ -23,71 +23,99 @@
 namespace lvb {
 namespace meta {
 
+// Per physical block: the call that last touched it, its first owner's
+// logical index and read-only mark, and the (call, row) stamp used to find
+// duplicates inside one row.  One 16-byte record, so a block costs one cache
+// line touch per check.
+struct Owner {
+  uint32_t stamp;
+  uint32_t row_stamp;
+  int32_t logical;
+  uint32_t readonly;
+};
+
 struct OwnerTable {
-  std::vector<uint32_t> stamp;     // call id that last touched the block
-  std::vector<int32_t> logical;    // logical index of its first owner
-  std::vector<uint8_t> readonly;   // whether that owner marked it read-only
-  std::vector<uint32_t> row_stamp; // (call, row) stamp for in-row duplicates
-  uint32_t call = 0;
+  std::vector<Owner> blocks;
+  uint32_t call = 0;  // stamp of the current call
+  uint32_t row = 0;   // last (call, row) stamp handed out
 
   void reserve(int64_t num_blocks) {
-    if (static_cast<int64_t>(stamp.size()) < num_blocks) {
-      stamp.assign(num_blocks, 0);
-      logical.assign(num_blocks, 0);
-      readonly.assign(num_blocks, 0);
-      row_stamp.assign(num_blocks, 0);
+    if (static_cast<int64_t>(blocks.size()) < num_blocks) {
+      blocks.assign(num_blocks, Owner{0, 0, 0, 0});
       call = 0;
+      row = 0;
     }
   }
 };
 
-// Returns nullptr when valid, otherwise the reference's message.
+// The rules of one row in the reference's order, without the fast path's
+// shortcuts; called only once the fused pass has seen a violation in row r
+// (rows before r passed).  Cross-row ownership stamps of rows < r are intact;
+// row r's own stamps may be partly written, which only the in-row duplicate
+// rule could notice, and that rule uses a fresh row stamp here.
+inline const char *row_violation(const int32_t *ids, int64_t len, int64_t needed, int32_t computed,
+                                 int32_t readonly, int64_t num_blocks, int64_t block_size, OwnerTable &owners,
+                                 uint32_t row_stamp) {
+  if (len < needed) return "block table does not cover all scheduled tokens";
+  if (len > needed) return "block table contains unused physical blocks";
+  for (int64_t i = 0; i < len; ++i)
+    if (ids[i] >= num_blocks || ids[i] < 0) return "block table contains an out-of-range physical block";
+  if (readonly > len || static_cast<int64_t>(readonly) * block_size > computed)
+    return "readonly prefix blocks exceed the computed prefix";
+  Owner *own = owners.blocks.data();
+  for (int64_t i = 0; i < len; ++i) {
+    if (own[ids[i]].row_stamp == row_stamp) return "block table aliases a physical block within one request";
+    own[ids[i]].row_stamp = row_stamp;
+  }
+  return "block tables alias a physical block across requests";
+}
+
+// Returns nullptr when valid, otherwise the reference's message.  Valid rows
+// take one fused pass per entry (range, in-row duplicate, cross-row
+// ownership); the first violation sends its row through row_violation, which
+// applies the rules in the reference's order and so reports the same message.
 inline const char *validate(const int32_t *block_ids, const int64_t *offsets, const int32_t *computed,
                             const int32_t *reserved, const int32_t *readonly, int64_t num_seqs,
                             int64_t num_blocks, int64_t block_size, OwnerTable &owners) {
   owners.reserve(num_blocks);
-  // Stamps: one per call for ownership, one per (call, row) for duplicates.
-  owners.call += 1;
-  if (owners.call == 0) {  // wrapped: clear once
-    std::fill(owners.stamp.begin(), owners.stamp.end(), 0u);
-    std::fill(owners.row_stamp.begin(), owners.row_stamp.end(), 0u);
-    owners.call = 1;
+  // Stamps (uint32): wrap-around clears the table once.
+  if (owners.call == UINT32_MAX || owners.row > UINT32_MAX - static_cast<uint32_t>(num_seqs) - 2) {
+    std::fill(owners.blocks.begin(), owners.blocks.end(), Owner{0, 0, 0, 0});
+    owners.call = 0;
+    owners.row = 0;
   }
-  static thread_local uint32_t row_counter = 0;
-  for (int64_t r = 0; r < num_seqs; ++r) {
-    const int64_t begin = offsets[r];
-    const int64_t len = offsets[r + 1] - begin;
+  const uint32_t call = ++owners.call;
+  uint32_t row = owners.row;
+  Owner *own = owners.blocks.data();
+  const char *violation = nullptr;
+  for (int64_t r = 0; r < num_seqs && violation == nullptr; ++r) {
+    const int32_t *ids = block_ids + offsets[r];
+    const int64_t len = offsets[r + 1] - offsets[r];
     const int64_t needed = (static_cast<int64_t>(computed[r]) + reserved[r] + block_size - 1) / block_size;
-    if (len < needed) return "block table does not cover all scheduled tokens";
-    if (len > needed) return "block table contains unused physical blocks";
-    for (int64_t i = 0; i < len; ++i)
-      if (block_ids[begin + i] >= num_blocks || block_ids[begin + i] < 0)
-        return "block table contains an out-of-range physical block";
-    if (readonly[r] > len || static_cast<int64_t>(readonly[r]) * block_size > computed[r])
-      return "readonly prefix blocks exceed the computed prefix";
-    row_counter += 1;
-    if (row_counter == 0) {
-      std::fill(owners.row_stamp.begin(), owners.row_stamp.end(), 0u);
-      row_counter = 1;
-    }
-    for (int64_t i = 0; i < len; ++i) {
-      const int32_t b = block_ids[begin + i];
-      if (owners.row_stamp[b] == row_counter) return "block table aliases a physical block within one request";
-      owners.row_stamp[b] = row_counter;
-    }
-    for (int64_t i = 0; i < len; ++i) {
-      const int32_t b = block_ids[begin + i];
-      const bool ro = i < readonly[r];
-      if (owners.stamp[b] == owners.call) {
-        if (owners.logical[b] != i || !owners.readonly[b] || !ro)
-          return "block tables alias a physical block across requests";
+    const int32_t ro_len = readonly[r];
+    const uint32_t rs = ++row;
+    bool ok = len == needed && ro_len <= len && static_cast<int64_t>(ro_len) * block_size <= computed[r];
+    for (int64_t i = 0; ok && i < len; ++i) {
+      const int32_t b = ids[i];
+      if (b < 0 || b >= num_blocks) {
+        ok = false;
+        break;
       }
-      owners.stamp[b] = owners.call;
-      owners.logical[b] = static_cast<int32_t>(i);
-      owners.readonly[b] = ro ? 1 : 0;
+      Owner &o = own[b];
+      const bool ro = i < ro_len;
+      if (o.row_stamp == rs || (o.stamp == call && (o.logical != i || !o.readonly || !ro))) {
+        ok = false;
+        break;
+      }
+      o.row_stamp = rs;
+      o.stamp = call;
+      o.logical = static_cast<int32_t>(i);
+      o.readonly = ro ? 1u : 0u;
     }
+    if (!ok) violation = row_violation(ids, len, needed, computed[r], ro_len, num_blocks, block_size, owners, ++row);
   }
-  return nullptr;
+  owners.row = row;
+  return violation;
 }
 
 }  // namespace meta

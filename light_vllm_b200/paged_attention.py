@@ -23,7 +23,7 @@ Nothing here computes on the CPU.
 from __future__ import annotations
 
 import ctypes
-import itertools
+from typing import NamedTuple
 
 import numpy as np
 import torch
@@ -36,7 +36,7 @@ from light_vllm_b200.staging import SingleStepStaging
 _SUPPORTED_DTYPES = (torch.float16, torch.bfloat16)
 
 
-def _validate_tensors(cache, metadata, layer_id: str, query: Tensor, key: Tensor, value: Tensor):
+def _validate_tensors(cache, num_query_tokens: int, layer_id: str, query: Tensor, key: Tensor, value: Tensor):
     """Shape rules shared with the reference backends (paged_attention.py:226-247)."""
 
     spec = cache.layer_spec(layer_id)
@@ -44,7 +44,7 @@ def _validate_tensors(cache, metadata, layer_id: str, query: Tensor, key: Tensor
         raise KVCacheError("paged attention query must have three dimensions")
     if query.shape[0] != key.shape[0] or value.shape != key.shape:
         raise KVCacheError("paged attention Q/K/V token dimensions must match")
-    if query.shape[0] != metadata.num_query_tokens:
+    if query.shape[0] != num_query_tokens:
         raise KVCacheError("paged attention metadata token count does not match query")
     if tuple(query.shape[1:]) != (spec.num_query_heads, spec.head_size):
         raise KVCacheError("paged attention query shape does not match the layer spec")
@@ -63,6 +63,80 @@ def _heads_contiguous(t: Tensor, *, align: int) -> Tensor:
     return t.contiguous()
 
 
+class StepShape(NamedTuple):
+    num_seqs: int
+    total_blocks: int
+    max_blocks: int
+    num_tokens: int
+    max_query_len: int
+    max_seq_len: int
+    linear: bool
+
+    @property
+    def packed_size(self) -> int:
+        """int32 values of the packed payload: padded tables, computed counts,
+        query starts, request indices."""
+        return self.num_seqs * self.max_blocks + 2 * self.num_seqs + 1 + self.num_tokens
+
+
+class StepMetadataPacker:
+    """Host half of a step's metadata, with buffers reused across steps.
+
+    ``gather`` reads a ``PagedAttentionMetadata`` (its tuples of Python ints)
+    into flat C arrays through the ``_hostpack`` module; ``pack`` runs
+    ``lvb_pack_step_metadata`` on them: the reference's block-table checks
+    (runtime/execution/paged_attention.py:138-172, same order and messages),
+    then the padded tables, computed counts, query starts and request indices
+    written into the caller's int32 buffer.  Both are native; the Python here
+    only sizes buffers.
+    """
+
+    def __init__(self) -> None:
+        self._hostpack = _native.hostpack()
+        self._lib = _native.library()
+        self._ids = np.empty(0, dtype=np.int32)
+        self._offsets = np.empty(0, dtype=np.int64)
+        self._rows = np.empty(0, dtype=np.int32)
+        self._stride = ctypes.c_int64(0)
+        self._ntok = ctypes.c_int64(0)
+        self._step: StepShape | None = None
+
+    def _reserve(self, num_seqs: int, total_blocks: int) -> None:
+        if self._ids.size < max(total_blocks, 1):
+            self._ids = np.empty(1 << max(total_blocks - 1, 1).bit_length(), dtype=np.int32)
+        if self._offsets.size < num_seqs + 1:
+            self._offsets = np.empty(1 << num_seqs.bit_length(), dtype=np.int64)
+            self._rows = np.empty(4 * self._offsets.size, dtype=np.int32)
+
+    def gather(self, metadata) -> StepShape:
+        tables = metadata.block_tables
+        n = len(tables)
+        self._reserve(n, sum(map(len, tables)))
+        total, max_blocks, ntok, max_q, max_seq, linear = self._hostpack.gather_step(
+            tables, metadata.num_computed_tokens, metadata.query_layouts,
+            metadata.num_reserved_query_tokens, metadata.num_readonly_prefix_blocks,
+            self._ids.ctypes.data, self._ids.size, self._offsets.ctypes.data, self._rows.ctypes.data)
+        self._step = StepShape(n, total, max_blocks, ntok, max_q, max_seq, linear)
+        return self._step
+
+    def pack(self, num_blocks: int, block_size: int, out_ptr: int, out_capacity: int) -> None:
+        """Validate the gathered step and write its payload (``packed_size``
+        int32 values) at ``out_ptr``; raises ``KVCacheError`` with the
+        reference's message for a block-table violation."""
+
+        step = self._step
+        if step is None:
+            raise RuntimeError("StepMetadataPacker.pack before gather")
+        n = step.num_seqs
+        rows = self._rows.ctypes.data
+        _native.check(
+            self._lib.lvb_pack_step_metadata(
+                self._ids.ctypes.data, self._offsets.ctypes.data, rows, rows + 4 * n, rows + 8 * n,
+                rows + 12 * n, n, num_blocks, block_size, out_ptr, out_capacity,
+                ctypes.byref(self._stride), ctypes.byref(self._ntok)),
+            "lvb_pack_step_metadata")
+
+
 class B200PagedAttention:
     """Per-step attention context; one ``forward`` per layer."""
 
@@ -77,46 +151,29 @@ class B200PagedAttention:
         self._backend = backend
         self._layer_ids: set[str] = set()
         self._device = torch.device(config.device)
-        lengths = metadata.query_lengths
         # Validation (the reference's block-table rules, same order and
         # messages) and packing of the per-step int32 payload run in native
         # code; one pinned copy moves the payload to the device.
-        tables = metadata.block_tables
-        offsets = np.zeros(len(tables) + 1, dtype=np.int64)
-        np.cumsum([len(t) for t in tables], out=offsets[1:])
-        flat = np.fromiter(itertools.chain.from_iterable(tables), dtype=np.int32, count=int(offsets[-1]))
-        computed = np.asarray(metadata.num_computed_tokens, dtype=np.int32)
-        qlens = np.asarray(lengths, dtype=np.int32)
-        reserved = np.asarray(metadata.num_reserved_query_tokens, dtype=np.int32)
-        readonly = np.asarray(metadata.num_readonly_prefix_blocks, dtype=np.int32)
-        n = len(tables)
-        max_blocks = int(np.max(np.diff(offsets))) if n else 0
-        capacity = n * max_blocks + 2 * n + 1 + int(qlens.sum())
-        stride = ctypes.c_int64(0)
-        ntok = ctypes.c_int64(0)
-        lib = _native.library()
+        packer = backend._packer
+        step = packer.gather(metadata)
+        capacity = step.packed_size
 
         def fill(host: Tensor) -> int:
-            _native.check(
-                lib.lvb_pack_step_metadata(
-                    flat.ctypes.data, offsets.ctypes.data, computed.ctypes.data, qlens.ctypes.data,
-                    reserved.ctypes.data, readonly.ctypes.data, n, config.num_blocks, config.block_size,
-                    host.data_ptr(), host.numel(), ctypes.byref(stride), ctypes.byref(ntok)),
-                "lvb_pack_step_metadata")
+            packer.pack(config.num_blocks, config.block_size, host.data_ptr(), host.numel())
             return capacity
 
         packed = staging.copy_packed(capacity, fill)
-        max_blocks = int(stride.value)
+        n, max_blocks = step.num_seqs, step.max_blocks
         self._tables = packed[: n * max_blocks]
         self._computed = packed[n * max_blocks : n * max_blocks + n]
         self._query_start = packed[n * max_blocks + n : n * max_blocks + 2 * n + 1]
         self._request_indices = packed[n * max_blocks + 2 * n + 1 :]
         self._table_stride = max_blocks
-        self._num_seqs = metadata.batch_size
-        self._num_tokens = metadata.num_query_tokens
-        self._max_query_len = max(lengths)
-        self._max_seq_len = max(c + n for c, n in zip(metadata.num_computed_tokens, lengths))
-        self._linear = metadata.has_only_linear_queries
+        self._num_seqs = n
+        self._num_tokens = step.num_tokens
+        self._max_query_len = step.max_query_len
+        self._max_seq_len = step.max_seq_len
+        self._linear = step.linear
         self._visibility: Tensor | None = None
         self._visibility_start: Tensor | None = None
 
@@ -134,7 +191,7 @@ class B200PagedAttention:
         if layer_id in self._layer_ids:
             raise KVCacheError(f"paged attention layer {layer_id!r} ran more than once")
         self._layer_ids.add(layer_id)
-        spec = _validate_tensors(self._cache, self._metadata, layer_id, query, key, value)
+        spec = _validate_tensors(self._cache, self._num_tokens, layer_id, query, key, value)
         config = self._cache.config
         for t in (query, key, value):
             if t.device != self._device or t.dtype != config.dtype:
@@ -235,6 +292,7 @@ class B200PagedAttentionBackend:
     def __init__(self) -> None:
         _native.library()  # fail loudly at construction when the library is missing
         self._staging: SingleStepStaging | None = None
+        self._packer = StepMetadataPacker()
         self._workspaces: dict[torch.device, Tensor] = {}
 
     def create(self, cache, metadata) -> B200PagedAttention:

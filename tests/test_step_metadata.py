@@ -13,11 +13,14 @@ import ctypes
 import json
 import random
 from pathlib import Path
+from types import SimpleNamespace
 
 import numpy as np
 import pytest
 
 from light_vllm_b200 import _native
+from light_vllm_b200.kv_cache import KVCacheError, PagedAttentionMetadata, QueryLayout, linear_query_layout
+from light_vllm_b200.paged_attention import StepMetadataPacker
 from oracle import paged_attention as opa
 
 META = json.loads((Path(__file__).resolve().parent / "golden" / "paged_meta.json").read_text())
@@ -40,6 +43,22 @@ def native_pack(tables, computed, qlens, reserved, readonly, num_blocks, block_s
         return lib.lvb_last_error().decode(), None
     assert status == _native.LVB_OK, lib.lvb_last_error()
     return None, (out, int(stride.value), int(ntok.value))
+
+
+def packer_pack(packer, tables, computed, qlens, reserved, readonly, num_blocks, block_size):
+    """The product path: Python objects -> ``_hostpack.gather_step`` ->
+    ``lvb_pack_step_metadata`` through ``StepMetadataPacker``."""
+
+    md = SimpleNamespace(block_tables=tuple(tuple(t) for t in tables), num_computed_tokens=tuple(computed),
+                         query_layouts=tuple(linear_query_layout(q) for q in qlens),
+                         num_reserved_query_tokens=tuple(reserved), num_readonly_prefix_blocks=tuple(readonly))
+    step = packer.gather(md)
+    out = np.zeros(step.packed_size, dtype=np.int32)
+    try:
+        packer.pack(num_blocks, block_size, out.ctypes.data, out.size)
+    except KVCacheError as exc:
+        return str(exc), None, step
+    return None, (out, step.max_blocks, step.num_tokens), step
 
 
 def oracle_error(tables, computed, reserved, readonly, num_blocks, block_size):
@@ -108,15 +127,21 @@ def _random_case(rng: random.Random):
 
 def test_random_cases_agree_with_the_oracle():
     rng = random.Random(20261201)
+    packer = StepMetadataPacker()
     seen_errors = set()
     for _ in range(3000):
         tables, computed, qlens, reserved, readonly, nb, bs = _random_case(rng)
         expected = oracle_error(tables, computed, reserved, readonly, nb, bs)
         error, payload = native_pack(tables, computed, qlens, reserved, readonly, nb, bs)
         assert error == expected, (tables, computed, reserved, readonly, nb, bs)
+        error2, payload2, step = packer_pack(packer, tables, computed, qlens, reserved, readonly, nb, bs)
+        assert error2 == expected, (tables, computed, reserved, readonly, nb, bs)
+        assert step.num_tokens == sum(qlens) and step.max_query_len == max(qlens) and step.linear
+        assert step.max_seq_len == max(c + q for c, q in zip(computed, qlens))
         seen_errors.add(expected)
         if error is None:
             check_payload(payload, tables, computed, qlens)
+            check_payload(payload2, tables, computed, qlens)
     # The fuzzing reached every rule.
     assert len(seen_errors) >= 6, seen_errors
 
@@ -133,3 +158,56 @@ def test_small_buffer_is_rejected():
                                         one.ctypes.data, one.ctypes.data, zero.ctypes.data, 1, 4, 1,
                                         out.ctypes.data, out.size, ctypes.byref(stride), ctypes.byref(ntok))
     assert status == _native.LVB_ERR_WORKSPACE
+
+
+def test_packer_reads_the_metadata_objects():
+    """Gathering from the metadata mirror: tuples and lists, tree layouts
+    (not linear), ids beyond int32 (reported as out of range, as the
+    reference reports any id >= num_blocks), counts beyond int32 refused."""
+
+    packer = StepMetadataPacker()
+    md = PagedAttentionMetadata(block_tables=((3, 1), (0,)), num_computed_tokens=(16, 3),
+                                query_layouts=(linear_query_layout(2), QueryLayout((-1, 0, 0))))
+    step = packer.gather(md)
+    assert step == (2, 3, 2, 5, 3, 18, False)
+    out = np.zeros(step.packed_size, dtype=np.int32)
+    packer.pack(4, 16, out.ctypes.data, out.size)
+    assert out.tolist() == [3, 1, 0, 0, 16, 3, 0, 2, 5, 0, 0, 1, 1, 1]
+
+    lists = SimpleNamespace(block_tables=[[3, 1], [0]], num_computed_tokens=[16, 3],
+                            query_layouts=[linear_query_layout(2), linear_query_layout(1)],
+                            num_reserved_query_tokens=[2, 1], num_readonly_prefix_blocks=[0, 0])
+    assert packer.gather(lists).linear
+
+    huge = SimpleNamespace(block_tables=((1 << 40,),), num_computed_tokens=(0,),
+                           query_layouts=(linear_query_layout(1),), num_reserved_query_tokens=(1,),
+                           num_readonly_prefix_blocks=(0,))
+    step = packer.gather(huge)
+    out = np.zeros(step.packed_size, dtype=np.int32)
+    with pytest.raises(KVCacheError, match="out-of-range physical block"):
+        packer.pack(4, 16, out.ctypes.data, out.size)
+
+    bad = SimpleNamespace(block_tables=((0,),), num_computed_tokens=(1 << 40,),
+                          query_layouts=(linear_query_layout(1),), num_reserved_query_tokens=(1,),
+                          num_readonly_prefix_blocks=(0,))
+    with pytest.raises(OverflowError):
+        packer.gather(bad)
+    short = SimpleNamespace(block_tables=((0,), (1,)), num_computed_tokens=(0,),
+                            query_layouts=(linear_query_layout(1),) * 2, num_reserved_query_tokens=(1, 1),
+                            num_readonly_prefix_blocks=(0, 0))
+    with pytest.raises(ValueError, match="one entry per request"):
+        packer.gather(short)
+
+
+def test_packer_grows_its_buffers_and_reuses_them():
+    packer = StepMetadataPacker()
+    rng = random.Random(7)
+    for n in (1, 64, 3, 200, 5):
+        tables = tuple(tuple(range(i * 50, i * 50 + rng.randint(1, 40))) for i in range(n))
+        computed = tuple(16 * len(t) - 1 for t in tables)
+        md = PagedAttentionMetadata(block_tables=tables, num_computed_tokens=computed,
+                                    query_layouts=tuple(linear_query_layout(1) for _ in tables))
+        step = packer.gather(md)
+        out = np.zeros(step.packed_size, dtype=np.int32)
+        packer.pack(n * 50, 16, out.ctypes.data, out.size)
+        check_payload((out, step.max_blocks, step.num_tokens), tables, computed, [1] * n)
