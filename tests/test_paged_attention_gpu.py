@@ -326,18 +326,19 @@ def test_compaction_moves_retained_queries_like_the_reference():
     readonly prefix block is untouched."""
 
     spec = ModelKVCacheSpec((AttentionLayerSpec("attention", 2, 2, 8),))
-    cache = PagedKVCache(spec, PagedKVCacheConfig(4, 2, dtype=torch.float16, device=torch.device("cuda")))
+    device = torch.device("cuda", 0)
+    cache = PagedKVCache(spec, PagedKVCacheConfig(4, 2, dtype=torch.float16, device=device))
     layer = cache.layer("attention")
     layer.keys.zero_()
     layer.values.zero_()
-    prefix_keys = torch.arange(32, dtype=torch.float32).reshape(2, 2, 8).half().cuda()
+    prefix_keys = torch.arange(32, dtype=torch.float32).reshape(2, 2, 8).half().to(device)
     prefix_values = prefix_keys + 100
-    cache.write("attention", prefix_keys, prefix_values, torch.tensor([2, 3], device="cuda"))
+    cache.write("attention", prefix_keys, prefix_values, torch.tensor([2, 3], device=device))
     md = PagedAttentionMetadata(block_tables=((1, 3, 0, 2),), num_computed_tokens=(2,),
                                 query_layouts=(QueryLayout((-1, 0, 0, 2, 3)),), num_readonly_prefix_blocks=(1,))
-    query_keys = (torch.arange(80, dtype=torch.float32).reshape(5, 2, 8) + 40).half().cuda()
+    query_keys = (torch.arange(80, dtype=torch.float32).reshape(5, 2, 8) + 40).half().to(device)
     query_values = query_keys + 200
-    cache.write("attention", query_keys, query_values, md.slot_mapping(block_size=2, device=torch.device("cuda")))
+    cache.write("attention", query_keys, query_values, md.slot_mapping(block_size=2, device=device))
     moved = cache.compact(md.block_tables[0], num_computed_tokens=2, num_query_tokens=5, num_reserved_query_tokens=5,
                           retained_query_indices=(0, 2, 4), num_readonly_prefix_blocks=1)
     torch.cuda.synchronize()
