@@ -19,7 +19,7 @@ from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().parent / "_lib" / "liblvb200.so"
 HOSTPACK_PATH = Path(__file__).resolve().parent / "_lib" / ("_hostpack" + sysconfig.get_config_var("EXT_SUFFIX"))
-ABI_VERSION = 4
+ABI_VERSION = 5
 
 LVB_OK = 0
 LVB_ERR_INVALID = 1
@@ -98,7 +98,7 @@ PROTOTYPES: dict[str, tuple[object, tuple[object, ...]]] = {
     ),
     "lvb_paged_attention": (
         _int,
-        (_c_ptr, _i64, _c_ptr, _c_ptr, _c_ptr, _i64, _c_ptr, _i64, _c_ptr, _c_ptr, _c_ptr, _c_ptr,
+        (_c_ptr, _i64, _c_ptr, _c_ptr, _c_ptr, _i64, _c_ptr, _i64, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr,
          _c_ptr, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _int, _c_ptr, _size,
          _c_ptr),
     ),

@@ -8,6 +8,7 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <climits>
 #include <cstdarg>
 #include <cstdio>
@@ -28,7 +29,7 @@
 
 namespace {
 
-constexpr int kAbiVersion = 4;
+constexpr int kAbiVersion = 5;
 constexpr int kMaxDevices = 64;
 
 thread_local char g_last_error[512] = "";
@@ -986,6 +987,7 @@ int lvb_paged_attention(const uint16_t *query, int64_t query_token_stride,
                         int64_t out_token_stride, const int32_t *block_tables,
                         int64_t table_stride, const int32_t *num_computed,
                         const int32_t *query_start_loc, const int32_t *request_indices,
+                        const int32_t *request_order,
                         const uint8_t *visibility, const int32_t *visibility_start,
                         int64_t num_seqs, int64_t num_tokens, int64_t max_query_len,
                         int64_t max_seq_len, int64_t num_q_heads, int64_t num_kv_heads,
@@ -1025,6 +1027,7 @@ int lvb_paged_attention(const uint16_t *query, int64_t query_token_stride,
   a.computed = num_computed;
   a.qsl = query_start_loc;
   a.req = request_indices;
+  a.order = request_order;
   a.vis = visibility;
   a.vis_start = visibility_start;
   a.Hq = static_cast<int>(num_q_heads);
@@ -1120,7 +1123,7 @@ int lvb_pack_step_metadata(const int32_t *block_ids, const int64_t *table_offset
   const char *violation = lvb::meta::validate(block_ids, table_offsets, num_computed, reserved, readonly,
                                               num_seqs, num_blocks, block_size, owners);
   if (violation != nullptr) return fail(LVB_ERR_METADATA, "%s", violation);
-  const int64_t need = num_seqs * max_blocks + 2 * num_seqs + 1 + num_tokens;
+  const int64_t need = num_seqs * max_blocks + 3 * num_seqs + 1 + num_tokens;
   if (need > out_capacity || num_tokens > INT_MAX)
     return fail(LVB_ERR_WORKSPACE, "step metadata needs %lld int32 slots, buffer has %lld", (long long)need,
                 (long long)out_capacity);
@@ -1136,13 +1139,18 @@ int lvb_pack_step_metadata(const int32_t *block_ids, const int64_t *table_offset
   int32_t *computed = tables + num_seqs * max_blocks;
   int32_t *qsl = computed + num_seqs;
   int32_t *req = qsl + num_seqs + 1;
+  int32_t *order = req + num_tokens;
   int64_t t = 0;
   qsl[0] = 0;
   for (int64_t r = 0; r < num_seqs; ++r) {
     computed[r] = num_computed[r];
     qsl[r + 1] = static_cast<int32_t>(qsl[r] + query_lengths[r]);
     for (int32_t i = 0; i < query_lengths[r]; ++i) req[t++] = static_cast<int32_t>(r);
+    order[r] = static_cast<int32_t>(r);
   }
+  // Launch order for the decode kernel: longest context first, ties by index.
+  std::stable_sort(order, order + num_seqs,
+                   [num_computed](int32_t x, int32_t y) { return num_computed[x] > num_computed[y]; });
   *table_stride_out = max_blocks;
   *num_tokens_out = num_tokens;
   return LVB_OK;

@@ -75,8 +75,8 @@ class StepShape(NamedTuple):
     @property
     def packed_size(self) -> int:
         """int32 values of the packed payload: padded tables, computed counts,
-        query starts, request indices."""
-        return self.num_seqs * self.max_blocks + 2 * self.num_seqs + 1 + self.num_tokens
+        query starts, request indices, launch order (longest context first)."""
+        return self.num_seqs * self.max_blocks + 3 * self.num_seqs + 1 + self.num_tokens
 
 
 class StepMetadataPacker:
@@ -167,7 +167,9 @@ class B200PagedAttention:
         self._tables = packed[: n * max_blocks]
         self._computed = packed[n * max_blocks : n * max_blocks + n]
         self._query_start = packed[n * max_blocks + n : n * max_blocks + 2 * n + 1]
-        self._request_indices = packed[n * max_blocks + 2 * n + 1 :]
+        req_end = n * max_blocks + 2 * n + 1 + step.num_tokens
+        self._request_indices = packed[n * max_blocks + 2 * n + 1 : req_end]
+        self._request_order = packed[req_end:]
         self._table_stride = max_blocks
         self._num_seqs = n
         self._num_tokens = step.num_tokens
@@ -252,7 +254,7 @@ class B200PagedAttention:
                 query.data_ptr(), query.stride(0), layer.keys.data_ptr(), layer.values.data_ptr(),
                 out.data_ptr(), out.stride(0), self._tables.data_ptr(), self._table_stride,
                 self._computed.data_ptr(), self._query_start.data_ptr(),
-                self._request_indices.data_ptr(),
+                self._request_indices.data_ptr(), self._request_order.data_ptr(),
                 None if self._visibility is None else self._visibility.data_ptr(),
                 None if self._visibility_start is None else self._visibility_start.data_ptr(),
                 self._num_seqs, self._num_tokens, self._max_query_len, self._max_seq_len,

@@ -412,7 +412,7 @@ class StaticDecodeAttention:
         _native.check(self._lib.lvb_paged_attention(
             query.data_ptr(), query.stride(0), layer.keys.data_ptr(), layer.values.data_ptr(),
             out.data_ptr(), out.stride(0), self.tables.data_ptr(), self.stride, self.computed.data_ptr(),
-            self.query_start.data_ptr(), self.request_indices.data_ptr(), None, None,
+            self.query_start.data_ptr(), self.request_indices.data_ptr(), None, None, None,
             self.num_seqs, self.num_seqs, 1, self.capacity, spec.num_query_heads, spec.num_kv_heads,
             spec.head_size, config.block_size, config.num_blocks, float(scale), dtype_code,
             self.workspace.data_ptr(), self.workspace.numel(), stream), "lvb_paged_attention")

@@ -292,6 +292,79 @@ def test_decode_baseline_config2():
     _check_decode(cache, md, q, k, v)
 
 
+def decode_batch_ctx(ctx, hq, hkv, d, dtype, *, seed, block_size=16):
+    """Decode workload with the given context lengths (tables carved from a
+    random permutation of a pool that just holds them)."""
+
+    gen = torch.Generator().manual_seed(seed)
+    pages = sum(-(-c // block_size) for c in ctx)
+    perm = torch.randperm(pages + 7, generator=gen).tolist()
+    tables, offset = [], 0
+    for c in ctx:
+        n = -(-c // block_size)
+        tables.append(tuple(perm[offset:offset + n]))
+        offset += n
+    md = PagedAttentionMetadata(block_tables=tuple(tables), num_computed_tokens=tuple(c - 1 for c in ctx),
+                                query_layouts=_layouts(*([1] * len(ctx))))
+    spec = ModelKVCacheSpec((AttentionLayerSpec("attention", hq, hkv, d),))
+    cache = PagedKVCache(spec, PagedKVCacheConfig(pages + 7, block_size, dtype=dtype, device=DEV))
+    layer = cache.layer("attention")
+    torch.manual_seed(seed)
+    layer.keys.normal_()
+    layer.values.normal_()
+    n = len(ctx)
+    q = torch.randn(n, hq, d, device=DEV, dtype=dtype)
+    k = torch.randn(n, hkv, d, device=DEV, dtype=dtype)
+    v = torch.randn(n, hkv, d, device=DEV, dtype=dtype)
+    return cache, md, q, k, v
+
+
+_BALANCED_CASES = {
+    # 32+ requests with 2 or 4 KV heads per CTA run the balanced decode: one
+    # wave of CTAs over the requests' pages laid end to end.
+    "short_contexts_many_per_cta": (dict(n=32, lo=1, hi=40), (28, 4, 128)),
+    "300_requests": (dict(n=300, lo=1, hi=100), (28, 4, 128)),
+    "two_head_groups_long": (dict(n=48, lo=1, hi=12000), (16, 8, 64)),
+    "extreme_mix": (dict(n=40, choices=(1, 16, 17, 1000, 9000)), (32, 2, 64)),
+}
+
+
+@pytest.mark.parametrize("dtype", (torch.bfloat16, torch.float16))
+@pytest.mark.parametrize("name", sorted(_BALANCED_CASES))
+def test_decode_balanced_ranges(dtype, name):
+    shape, (hq, hkv, d) = _BALANCED_CASES[name]
+    rng = np.random.default_rng(len(name) * 7 + (dtype == torch.float16))
+    if "choices" in shape:
+        ctx = [int(x) for x in rng.choice(shape["choices"], size=shape["n"])]
+    else:
+        ctx = [int(x) for x in rng.integers(shape["lo"], shape["hi"] + 1, size=shape["n"])]
+    cache, md, q, k, v = decode_batch_ctx(ctx, hq, hkv, d, dtype, seed=len(ctx))
+    _check_decode(cache, md, q, k, v)
+
+
+def test_decode_balanced_replays_are_identical():
+    """Graph replays of the balanced decode (merge semaphores reset by the
+    merging CTA) give bit-identical outputs, equal to the eager call."""
+
+    cache, md, q, k, v = decode_batch(64, 512, 4096, 28, 4, 128, torch.bfloat16, num_blocks=40000,
+                                      seed=20261201)
+    scale = 1.0 / sqrt(q.shape[-1])
+    eager = _check_decode(cache, md, q, k, v)
+    ctx = B200PagedAttentionBackend().create(cache, md)
+    out = torch.empty_like(q)
+    ctx.launch("attention", q, k, v, scale=scale, out=out, write_kv=False)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        ctx.launch("attention", q, k, v, scale=scale, out=out, write_kv=False)
+    for _ in range(3):
+        out.zero_()
+        graph.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(_bits(out), _bits(eager))
+    assert _native.device_error() == 0
+
+
 def test_decode_single_token_context():
     cache, md, q, k, v = decode_batch(3, 1, 1, 28, 4, 128, torch.bfloat16, num_blocks=8, seed=3)
     _check_decode(cache, md, q, k, v)
