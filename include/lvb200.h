@@ -218,6 +218,31 @@ LVB_API int lvb_pack_step_metadata(const int32_t *block_ids, const int64_t *tabl
                                    int32_t *out, int64_t out_capacity,
                                    int64_t *table_stride_out, int64_t *num_tokens_out);
 
+/* One step's metadata staged for the device in one call: waits on the host
+ * until `slot_event` (NULL: no wait) has passed, i.e. the copy last issued
+ * from `pinned_out` finished; packs exactly as lvb_pack_step_metadata into
+ * the page-locked `pinned_out`; copies the payload to `device_out`
+ * (device_capacity int32 elements) on `stream`; records `slot_event` on
+ * `stream` after the copy.  The native form of the reference's
+ * SingleStepCudaStagingBuffer.copy_groups (runtime/execution/cuda_staging.py:11-70)
+ * for the packed payload; a block-table violation returns LVB_ERR_METADATA
+ * before anything is copied. */
+LVB_API int lvb_stage_step_metadata(const int32_t *block_ids, const int64_t *table_offsets,
+                                    const int32_t *num_computed, const int32_t *query_lengths,
+                                    const int32_t *reserved, const int32_t *readonly, int64_t num_seqs,
+                                    int64_t num_blocks, int64_t block_size, int32_t *pinned_out,
+                                    int64_t out_capacity, int32_t *device_out, int64_t device_capacity,
+                                    void *slot_event, lvb_stream_t stream, int64_t *table_stride_out,
+                                    int64_t *num_tokens_out);
+
+/* Events for staging slots (cudaEventDisableTiming): create, destroy, record
+ * on a stream, and wait on the host (a poll, then a synchronize only if the
+ * event is still pending; an event never recorded counts as passed). */
+LVB_API int lvb_event_create(void **event);
+LVB_API int lvb_event_destroy(void *event);
+LVB_API int lvb_event_record(void *event, lvb_stream_t stream);
+LVB_API int lvb_event_wait_host(void *event);
+
 /* Bytes of workspace `lvb_paged_attention` needs: split-context partial
  * outputs and log-sum-exps, then one merge semaphore per (request, KV head).
  * A workspace must be zero-filled once before its first use; every call

@@ -75,6 +75,15 @@ PROTOTYPES: dict[str, tuple[object, tuple[object, ...]]] = {
         (_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _i64, _i64, _i64, _c_ptr, _i64,
          ctypes.POINTER(_i64), ctypes.POINTER(_i64)),
     ),
+    "lvb_stage_step_metadata": (
+        _int,
+        (_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _i64, _i64, _i64, _c_ptr, _i64, _c_ptr, _i64,
+         _c_ptr, _c_ptr, ctypes.POINTER(_i64), ctypes.POINTER(_i64)),
+    ),
+    "lvb_event_create": (_int, (ctypes.POINTER(_c_ptr),)),
+    "lvb_event_destroy": (_int, (_c_ptr,)),
+    "lvb_event_record": (_int, (_c_ptr, _c_ptr)),
+    "lvb_event_wait_host": (_int, (_c_ptr,)),
     "lvb_ipc_alloc": (_int, (_size, ctypes.POINTER(_c_ptr), _c_ptr)),
     "lvb_ipc_open": (_int, (_c_ptr, ctypes.POINTER(_c_ptr))),
     "lvb_ipc_close": (_int, (_c_ptr,)),

@@ -1156,6 +1156,62 @@ int lvb_pack_step_metadata(const int32_t *block_ids, const int64_t *table_offset
   return LVB_OK;
 }
 
+int lvb_event_create(void **event) {
+  if (!event) return fail(LVB_ERR_INVALID, "lvb_event_create: null argument");
+  cudaEvent_t e = nullptr;
+  cudaError_t err = cudaEventCreateWithFlags(&e, cudaEventDisableTiming);
+  if (err != cudaSuccess) return cuda_fail(err, "cudaEventCreateWithFlags");
+  *event = e;
+  return LVB_OK;
+}
+
+int lvb_event_destroy(void *event) {
+  if (!event) return LVB_OK;
+  cudaError_t err = cudaEventDestroy(static_cast<cudaEvent_t>(event));
+  return err == cudaSuccess ? LVB_OK : cuda_fail(err, "cudaEventDestroy");
+}
+
+int lvb_event_record(void *event, lvb_stream_t stream) {
+  if (!event) return fail(LVB_ERR_INVALID, "lvb_event_record: null event");
+  cudaError_t err = cudaEventRecord(static_cast<cudaEvent_t>(event), reinterpret_cast<cudaStream_t>(stream));
+  return err == cudaSuccess ? LVB_OK : cuda_fail(err, "cudaEventRecord");
+}
+
+int lvb_event_wait_host(void *event) {
+  if (!event) return LVB_OK;
+  cudaEvent_t e = static_cast<cudaEvent_t>(event);
+  cudaError_t err = cudaEventQuery(e);
+  if (err == cudaErrorNotReady) err = cudaEventSynchronize(e);
+  return err == cudaSuccess ? LVB_OK : cuda_fail(err, "waiting for a staging copy");
+}
+
+int lvb_stage_step_metadata(const int32_t *block_ids, const int64_t *table_offsets,
+                            const int32_t *num_computed, const int32_t *query_lengths,
+                            const int32_t *reserved, const int32_t *readonly, int64_t num_seqs,
+                            int64_t num_blocks, int64_t block_size, int32_t *pinned_out,
+                            int64_t out_capacity, int32_t *device_out, int64_t device_capacity,
+                            void *slot_event, lvb_stream_t stream, int64_t *table_stride_out,
+                            int64_t *num_tokens_out) {
+  if (!device_out || !table_stride_out || !num_tokens_out)
+    return fail(LVB_ERR_INVALID, "step metadata staging null pointer argument");
+  // The pinned slot may still feed the copy issued the last time it was used.
+  int rc = lvb_event_wait_host(slot_event);
+  if (rc != LVB_OK) return rc;
+  rc = lvb_pack_step_metadata(block_ids, table_offsets, num_computed, query_lengths, reserved, readonly,
+                              num_seqs, num_blocks, block_size, pinned_out, out_capacity, table_stride_out,
+                              num_tokens_out);
+  if (rc != LVB_OK) return rc;
+  const int64_t total = num_seqs * *table_stride_out + 3 * num_seqs + 1 + *num_tokens_out;
+  if (total > device_capacity)
+    return fail(LVB_ERR_WORKSPACE, "step metadata needs %lld int32 slots on the device, buffer has %lld",
+                (long long)total, (long long)device_capacity);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  cudaError_t err = cudaMemcpyAsync(device_out, pinned_out, static_cast<size_t>(total) * sizeof(int32_t),
+                                    cudaMemcpyHostToDevice, s);
+  if (err != cudaSuccess) return cuda_fail(err, "cudaMemcpyAsync (step metadata)");
+  return slot_event ? lvb_event_record(slot_event, stream) : LVB_OK;
+}
+
 }  // extern "C"
 
 // ------------------------------------------------------------------------

@@ -97,16 +97,22 @@ class StepMetadataPacker:
         self._ids = np.empty(0, dtype=np.int32)
         self._offsets = np.empty(0, dtype=np.int64)
         self._rows = np.empty(0, dtype=np.int32)
+        self._ids_ptr = self._offsets_ptr = self._rows_ptr = 0
         self._stride = ctypes.c_int64(0)
         self._ntok = ctypes.c_int64(0)
+        self._stride_ref = ctypes.byref(self._stride)
+        self._ntok_ref = ctypes.byref(self._ntok)
         self._step: StepShape | None = None
 
     def _reserve(self, num_seqs: int, total_blocks: int) -> None:
         if self._ids.size < max(total_blocks, 1):
             self._ids = np.empty(1 << max(total_blocks - 1, 1).bit_length(), dtype=np.int32)
+            self._ids_ptr = self._ids.ctypes.data
         if self._offsets.size < num_seqs + 1:
             self._offsets = np.empty(1 << num_seqs.bit_length(), dtype=np.int64)
             self._rows = np.empty(4 * self._offsets.size, dtype=np.int32)
+            self._offsets_ptr = self._offsets.ctypes.data
+            self._rows_ptr = self._rows.ctypes.data
 
     def gather(self, metadata) -> StepShape:
         tables = metadata.block_tables
@@ -115,7 +121,7 @@ class StepMetadataPacker:
         total, max_blocks, ntok, max_q, max_seq, linear = self._hostpack.gather_step(
             tables, metadata.num_computed_tokens, metadata.query_layouts,
             metadata.num_reserved_query_tokens, metadata.num_readonly_prefix_blocks,
-            self._ids.ctypes.data, self._ids.size, self._offsets.ctypes.data, self._rows.ctypes.data)
+            self._ids_ptr, self._ids.size, self._offsets_ptr, self._rows_ptr)
         self._step = StepShape(n, total, max_blocks, ntok, max_q, max_seq, linear)
         return self._step
 
@@ -128,13 +134,37 @@ class StepMetadataPacker:
         if step is None:
             raise RuntimeError("StepMetadataPacker.pack before gather")
         n = step.num_seqs
-        rows = self._rows.ctypes.data
+        rows = self._rows_ptr
         _native.check(
             self._lib.lvb_pack_step_metadata(
-                self._ids.ctypes.data, self._offsets.ctypes.data, rows, rows + 4 * n, rows + 8 * n,
+                self._ids_ptr, self._offsets_ptr, rows, rows + 4 * n, rows + 8 * n,
                 rows + 12 * n, n, num_blocks, block_size, out_ptr, out_capacity,
-                ctypes.byref(self._stride), ctypes.byref(self._ntok)),
+                self._stride_ref, self._ntok_ref),
             "lvb_pack_step_metadata")
+
+    def stage(self, staging: SingleStepStaging, num_blocks: int, block_size: int) -> Tensor:
+        """Validate, pack and copy the gathered step to the device in one
+        native call (``lvb_stage_step_metadata``) through a staging slot;
+        returns the device payload (``packed_size`` int32 values)."""
+
+        step = self._step
+        if step is None:
+            raise RuntimeError("StepMetadataPacker.stage before gather")
+        n = step.num_seqs
+        rows = self._rows_ptr
+        lib = self._lib
+
+        def run(host_ptr: int, host_capacity: int, dev_ptr: int, dev_capacity: int, event: int,
+                stream: int) -> int:
+            _native.check(
+                lib.lvb_stage_step_metadata(
+                    self._ids_ptr, self._offsets_ptr, rows, rows + 4 * n, rows + 8 * n, rows + 12 * n, n,
+                    num_blocks, block_size, host_ptr, host_capacity, dev_ptr, dev_capacity, event, stream,
+                    self._stride_ref, self._ntok_ref),
+                "lvb_stage_step_metadata")
+            return step.packed_size
+
+        return staging.stage(step.packed_size, run)
 
 
 class B200PagedAttention:
@@ -156,13 +186,7 @@ class B200PagedAttention:
         # code; one pinned copy moves the payload to the device.
         packer = backend._packer
         step = packer.gather(metadata)
-        capacity = step.packed_size
-
-        def fill(host: Tensor) -> int:
-            packer.pack(config.num_blocks, config.block_size, host.data_ptr(), host.numel())
-            return capacity
-
-        packed = staging.copy_packed(capacity, fill)
+        packed = packer.stage(staging, config.num_blocks, config.block_size)
         n, max_blocks = step.num_seqs, step.max_blocks
         self._tables = packed[: n * max_blocks]
         self._computed = packed[n * max_blocks : n * max_blocks + n]

@@ -422,3 +422,19 @@ def test_compaction_moves_retained_queries_like_the_reference():
     assert torch.equal(flat_k[[6, 7, 0]], query_keys[[0, 2, 4]])
     assert torch.equal(flat_v[[6, 7, 0]], query_values[[0, 2, 4]])
     assert _native.device_error() == 0
+
+
+def test_staging_ring_copies_groups_and_grows():
+    """The pinned ring (native slot events): group copies land intact across
+    ring wrap-around and buffer growth; each view is read before the next copy."""
+
+    from light_vllm_b200.staging import SingleStepStaging
+
+    staging = SingleStepStaging(DEV)
+    for i in range(11):
+        tail = np.arange(i * 97 + 1, dtype=np.int32)
+        head, rest = staging.copy_groups([i, i + 1, i + 2], tail)
+        assert head.tolist() == [i, i + 1, i + 2]
+        assert torch.equal(rest.cpu(), torch.from_numpy(tail))
+        packed = staging.copy_packed(5, lambda host: host[:5].copy_(torch.arange(5, dtype=torch.int32) + i).numel())
+        assert packed.tolist() == [i, i + 1, i + 2, i + 3, i + 4]

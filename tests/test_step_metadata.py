@@ -214,3 +214,27 @@ def test_packer_grows_its_buffers_and_reuses_them():
         out = np.zeros(step.packed_size, dtype=np.int32)
         packer.pack(n * 50, 16, out.ctypes.data, out.size)
         check_payload((out, step.max_blocks, step.num_tokens), tables, computed, [1] * n)
+
+
+def test_stage_rejects_violations_before_any_copy():
+    """lvb_stage_step_metadata validates (host code) before its device copy:
+    a block-table violation returns the reference's message and a missing
+    device buffer is refused, with no CUDA call made."""
+
+    lib = _native.library()
+    flat = np.array([0, 0], dtype=np.int32)  # one request aliasing block 0 twice
+    offsets = np.array([0, 2], dtype=np.int64)
+    computed = np.array([17], dtype=np.int32)
+    one = np.array([1], dtype=np.int32)
+    zero = np.array([0], dtype=np.int32)
+    host = np.zeros(16, dtype=np.int32)
+    stride, ntok = ctypes.c_int64(0), ctypes.c_int64(0)
+    args = (flat.ctypes.data, offsets.ctypes.data, computed.ctypes.data, one.ctypes.data, one.ctypes.data,
+            zero.ctypes.data, 1, 4, 16, host.ctypes.data, host.size)
+    status = lib.lvb_stage_step_metadata(*args, 8, 16, None, None, ctypes.byref(stride), ctypes.byref(ntok))
+    assert status == _native.LVB_ERR_METADATA
+    assert lib.lvb_last_error() == b"block table aliases a physical block within one request"
+    status = lib.lvb_stage_step_metadata(*args, None, 16, None, None, ctypes.byref(stride), ctypes.byref(ntok))
+    assert status == _native.LVB_ERR_INVALID
+    assert lib.lvb_event_wait_host(None) == _native.LVB_OK
+    assert lib.lvb_event_destroy(None) == _native.LVB_OK
