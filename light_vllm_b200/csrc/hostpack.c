@@ -190,8 +190,13 @@ static PyMethodDef methods[] = {
     {NULL, NULL, 0, NULL},
 };
 
-static struct PyModuleDef module = {PyModuleDef_HEAD_INIT, "_hostpack",
-                                    "Step-metadata gathering from Python objects into C arrays.", -1, methods};
+static struct PyModuleDef module = {
+    PyModuleDef_HEAD_INIT,
+    .m_name = "_hostpack",
+    .m_doc = "Step-metadata gathering from Python objects into C arrays.",
+    .m_size = -1,
+    .m_methods = methods,
+};
 
 PyMODINIT_FUNC PyInit__hostpack(void) {
   parent_indices_name = PyUnicode_InternFromString("parent_indices");
