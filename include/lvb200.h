@@ -206,11 +206,11 @@ LVB_API int lvb_kv_scatter(const uint16_t *key, int64_t key_token_stride, const 
  * LVB_ERR_METADATA with the reference's message.  On success `out` holds
  * [block tables padded to *table_stride_out columns | num_computed |
  * query_start_loc (num_seqs + 1) | request_indices (*num_tokens_out) |
- * request_order (num_seqs: requests by descending num_computed, ties in index
- * order)], the payload of one host-to-device copy
- * (triton_paged_attention.py:422-440, plus the launch order that
- * lvb_paged_attention takes).  out_capacity (int32 elements) must be at least
- * num_seqs * max_table + 3 * num_seqs + 1 + num_tokens. */
+ * request_order (2 * num_seqs: the requests by descending num_computed, ties
+ * in index order, then their num_computed in that order)], the payload of one
+ * host-to-device copy (triton_paged_attention.py:422-440, plus the launch
+ * order that lvb_paged_attention takes).  out_capacity (int32 elements) must
+ * be at least num_seqs * max_table + 4 * num_seqs + 1 + num_tokens. */
 LVB_API int lvb_pack_step_metadata(const int32_t *block_ids, const int64_t *table_offsets,
                                    const int32_t *num_computed, const int32_t *query_lengths,
                                    const int32_t *reserved, const int32_t *readonly,
@@ -263,9 +263,10 @@ LVB_API size_t lvb_paged_attention_workspace_bytes(int64_t num_seqs, int64_t num
  * 4-byte aligned (even token strides, in elements), the caches 16-byte
  * aligned.  Decode batches (every query length 1, linear) take a
  * split-context path that needs `workspace`; request_order (optional, NULL =
- * index order) is a permutation of the requests in which that path launches
- * them: longest context first (the order lvb_pack_step_metadata writes)
- * shortens the tail of the launch.  The results do not depend on it.
+ * index order: 2 * num_seqs int32, a permutation of the requests followed by
+ * their num_computed in that order, as lvb_pack_step_metadata writes it) is
+ * the order in which that path launches them: longest context first shortens
+ * the tail of the launch.  The results do not depend on it.
  * Replaces the Triton attention launches
  * (runtime/execution/triton_paged_attention.py:106-391, 519-559). */
 LVB_API int lvb_paged_attention(const uint16_t *query, int64_t query_token_stride,

@@ -1028,6 +1028,7 @@ int lvb_paged_attention(const uint16_t *query, int64_t query_token_stride,
   a.qsl = query_start_loc;
   a.req = request_indices;
   a.order = request_order;
+  a.num_seqs = static_cast<int>(num_seqs);
   a.vis = visibility;
   a.vis_start = visibility_start;
   a.Hq = static_cast<int>(num_q_heads);
@@ -1123,7 +1124,7 @@ int lvb_pack_step_metadata(const int32_t *block_ids, const int64_t *table_offset
   const char *violation = lvb::meta::validate(block_ids, table_offsets, num_computed, reserved, readonly,
                                               num_seqs, num_blocks, block_size, owners);
   if (violation != nullptr) return fail(LVB_ERR_METADATA, "%s", violation);
-  const int64_t need = num_seqs * max_blocks + 3 * num_seqs + 1 + num_tokens;
+  const int64_t need = num_seqs * max_blocks + 4 * num_seqs + 1 + num_tokens;
   if (need > out_capacity || num_tokens > INT_MAX)
     return fail(LVB_ERR_WORKSPACE, "step metadata needs %lld int32 slots, buffer has %lld", (long long)need,
                 (long long)out_capacity);
@@ -1148,9 +1149,11 @@ int lvb_pack_step_metadata(const int32_t *block_ids, const int64_t *table_offset
     for (int32_t i = 0; i < query_lengths[r]; ++i) req[t++] = static_cast<int32_t>(r);
     order[r] = static_cast<int32_t>(r);
   }
-  // Launch order for the decode kernel: longest context first, ties by index.
+  // Launch order for the decode kernel: longest context first, ties by index;
+  // then the listed requests' computed counts.
   std::stable_sort(order, order + num_seqs,
                    [num_computed](int32_t x, int32_t y) { return num_computed[x] > num_computed[y]; });
+  for (int64_t r = 0; r < num_seqs; ++r) order[num_seqs + r] = num_computed[order[r]];
   *table_stride_out = max_blocks;
   *num_tokens_out = num_tokens;
   return LVB_OK;
@@ -1201,7 +1204,7 @@ int lvb_stage_step_metadata(const int32_t *block_ids, const int64_t *table_offse
                               num_seqs, num_blocks, block_size, pinned_out, out_capacity, table_stride_out,
                               num_tokens_out);
   if (rc != LVB_OK) return rc;
-  const int64_t total = num_seqs * *table_stride_out + 3 * num_seqs + 1 + *num_tokens_out;
+  const int64_t total = num_seqs * *table_stride_out + 4 * num_seqs + 1 + *num_tokens_out;
   if (total > device_capacity)
     return fail(LVB_ERR_WORKSPACE, "step metadata needs %lld int32 slots on the device, buffer has %lld",
                 (long long)total, (long long)device_capacity);

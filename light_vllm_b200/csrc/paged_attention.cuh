@@ -91,7 +91,9 @@ struct AttnArgs {
   const int32_t *computed;
   const int32_t *qsl;
   const int32_t *req;
-  const int32_t *order;      // decode: requests in launch order (longest first), null = index order
+  // decode launch order, null = index order: [num_seqs] requests (longest
+  // context first), then [num_seqs] their num_computed in that order
+  const int32_t *order;
   const uint8_t *vis;        // null = linear layouts
   const int32_t *vis_start;  // per request
   int Hq, Hkv, D, bs;
@@ -102,6 +104,7 @@ struct AttnArgs {
   uint32_t *merge_count;  // [num_seqs][Hkv], zero between calls
   int max_splits;
   int chunk_tokens;  // multiple of 16
+  int num_seqs;
 };
 
 __device__ __forceinline__ float warp_max(float v) {
@@ -277,10 +280,13 @@ __global__ void __launch_bounds__(DecodeCfg<D, HPC, KW>::kThreads, 2)
   // splits for the end, where they fill the SMs that free up (B200, BASELINE
   // config 2, same data: index order 65.1 us, longest first 62.8, shortest
   // first 66.5).
-  const int seq = a.order != nullptr ? a.order[blockIdx.z] : static_cast<int>(blockIdx.z);
+  // With an order, the request and its context length are two independent
+  // loads (the packed order carries the lengths), not a dependent pair.
+  const int z = blockIdx.z;
+  const int seq = a.order != nullptr ? a.order[z] : z;
+  const int ctx = (a.order != nullptr ? a.order[a.num_seqs + z] : a.computed[z]) + 1;
   const int hg = blockIdx.y;  // group of HPC KV heads
   const int split = blockIdx.x;
-  const int ctx = a.computed[seq] + 1;
   const int start = split * a.chunk_tokens;
   if (start >= ctx) return;  // uniform for the whole CTA
   const int end = min(ctx, start + a.chunk_tokens);

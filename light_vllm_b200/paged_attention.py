@@ -75,8 +75,9 @@ class StepShape(NamedTuple):
     @property
     def packed_size(self) -> int:
         """int32 values of the packed payload: padded tables, computed counts,
-        query starts, request indices, launch order (longest context first)."""
-        return self.num_seqs * self.max_blocks + 3 * self.num_seqs + 1 + self.num_tokens
+        query starts, request indices, launch order (longest context first)
+        with the listed requests' computed counts."""
+        return self.num_seqs * self.max_blocks + 4 * self.num_seqs + 1 + self.num_tokens
 
 
 class StepMetadataPacker:

@@ -33,7 +33,7 @@ def native_pack(tables, computed, qlens, reserved, readonly, num_blocks, block_s
     flat = np.array([b for t in tables for b in t] or [0], dtype=np.int32)
     arrs = [np.asarray(v, dtype=np.int32) for v in (computed, qlens, reserved, readonly)]
     n = len(tables)
-    cap = n * max(len(t) for t in tables) + 3 * n + 1 + sum(qlens)
+    cap = n * max(len(t) for t in tables) + 4 * n + 1 + sum(qlens)
     out = np.zeros(max(cap, 1), dtype=np.int32)
     stride, ntok = ctypes.c_int64(0), ctypes.c_int64(0)
     status = lib.lvb_pack_step_metadata(flat.ctypes.data, offsets.ctypes.data,
@@ -83,6 +83,7 @@ def check_payload(payload, tables, computed, qlens):
     # Launch order for the decode kernel: descending computed count, ties by index.
     order = list(out[base + 2 * n + 1 + ntok : base + 3 * n + 1 + ntok])
     assert order == sorted(range(n), key=lambda r: -computed[r])
+    assert list(out[base + 3 * n + 1 + ntok : base + 4 * n + 1 + ntok]) == [computed[r] for r in order]
 
 
 @pytest.mark.parametrize("case", META, ids=[c["name"] for c in META])
@@ -175,7 +176,7 @@ def test_packer_reads_the_metadata_objects():
     assert step == (2, 3, 2, 5, 3, 18, False)
     out = np.zeros(step.packed_size, dtype=np.int32)
     packer.pack(4, 16, out.ctypes.data, out.size)
-    assert out.tolist() == [3, 1, 0, 0, 16, 3, 0, 2, 5, 0, 0, 1, 1, 1, 0, 1]
+    assert out.tolist() == [3, 1, 0, 0, 16, 3, 0, 2, 5, 0, 0, 1, 1, 1, 0, 1, 16, 3]
 
     lists = SimpleNamespace(block_tables=[[3, 1], [0]], num_computed_tokens=[16, 3],
                             query_layouts=[linear_query_layout(2), linear_query_layout(1)],
