@@ -140,6 +140,25 @@ def library() -> ctypes.CDLL:
     return lib
 
 
+def stream_handle(device) -> int:
+    """The raw ``cudaStream_t`` of the current stream on ``device`` (what
+    ``torch.cuda.current_stream(device).cuda_stream`` returns, without
+    building a Stream object: ~0.1 instead of ~2 us per call)."""
+
+    index = device.index
+    if index is None:
+        import torch
+
+        index = torch.cuda.current_device()
+    return _raw_stream(index)
+
+
+def _raw_stream(index: int) -> int:
+    import torch
+
+    return torch._C._cuda_getCurrentRawStream(index)
+
+
 @functools.lru_cache(maxsize=1)
 def hostpack():
     """The CPython module that reads step metadata out of Python objects."""

@@ -106,7 +106,7 @@ class B200AWQOperation:
                     flat.data_ptr(), self.codes.data_ptr(), self.groups.data_ptr(),
                     None if self.bias is None else self.bias.data_ptr(), out.data_ptr(), rows,
                     self.inner, self.output_width, self.group_size, self.workspace.data_ptr(),
-                    self.workspace.numel(), torch.cuda.current_stream(flat.device).cuda_stream,
+                    self.workspace.numel(), _native.stream_handle(flat.device),
                 ),
                 "lvb_awq_linear_packed",
             )
@@ -117,7 +117,7 @@ class B200AWQOperation:
                 self.scales.data_ptr(), None if self.bias is None else self.bias.data_ptr(),
                 out.data_ptr(), rows, self.inner, self.output_width, self.group_size,
                 self.workspace.data_ptr(), self.workspace.numel(),
-                torch.cuda.current_stream(flat.device).cuda_stream,
+                _native.stream_handle(flat.device),
             ),
             "lvb_awq_linear",
         )
@@ -137,7 +137,7 @@ class B200AWQOperation:
             flat = flat.contiguous()
         rows = flat.shape[0]
         lib = _native.library()
-        stream = torch.cuda.current_stream(flat.device).cuda_stream
+        stream = _native.stream_handle(flat.device)
         if self.codes is not None:
             out = torch.empty((rows, self.output_width), dtype=torch.float16, device=flat.device)
             status = lib.lvb_awq_silu_linear_packed(
@@ -209,7 +209,7 @@ def pack_awq_decode_layout(qweight: Tensor, qzeros: Tensor, scales: Tensor,
     _native.check(
         lib.lvb_awq_pack(qweight.data_ptr(), qzeros.data_ptr(), scales.data_ptr(), inner, output,
                          group_size, codes.data_ptr(), groups.data_ptr(),
-                         torch.cuda.current_stream(qweight.device).cuda_stream),
+                         _native.stream_handle(qweight.device)),
         "lvb_awq_pack",
     )
     return codes, groups
@@ -243,7 +243,7 @@ def b200_awq_dequantize(qweight: Tensor, qzeros: Tensor, scales: Tensor, group_s
     _native.check(
         _native.library().lvb_awq_dequantize(
             qweight.data_ptr(), qzeros.data_ptr(), scales.data_ptr(), w.data_ptr(), inner, output,
-            group_size, torch.cuda.current_stream(qweight.device).cuda_stream,
+            group_size, _native.stream_handle(qweight.device),
         ),
         "lvb_awq_dequantize",
     )

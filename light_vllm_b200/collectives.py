@@ -242,7 +242,7 @@ def _launch(workspace: PeerWorkspace, partial: Tensor, residual: Tensor | None, 
             workspace.pointers, rank, world, partial.data_ptr(),
             0 if residual is None else residual.data_ptr(), 0 if weight is None else weight.data_ptr(),
             out.data_ptr(), partial.shape[0], partial.shape[1], workspace.max_tokens, float(eps), int(mode),
-            torch.cuda.current_stream(partial.device).cuda_stream),
+            _native.stream_handle(partial.device)),
         "lvb_allreduce_add_rmsnorm",
     )
 

@@ -252,7 +252,7 @@ class PagedKVCache:
         key = _rows_for_kernel(key)
         value = _rows_for_kernel(value)
         slots = mapping.slots.contiguous()
-        stream = torch.cuda.current_stream(key.device).cuda_stream
+        stream = _native.stream_handle(key.device)
         _native.check(
             _native.library().lvb_kv_scatter(
                 key.data_ptr(), key.stride(0), value.data_ptr(), value.stride(0),

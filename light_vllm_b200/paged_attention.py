@@ -249,7 +249,7 @@ class B200PagedAttention:
         spec = self._cache.layer_spec(layer_id)
         config = self._cache.config
         lib = _native.library()
-        stream = torch.cuda.current_stream(self._device).cuda_stream
+        stream = _native.stream_handle(self._device)
         dtype_code = _native.DTYPE_BF16 if config.dtype == torch.bfloat16 else _native.DTYPE_F16
         layer = self._cache.layer(layer_id)
         if write_kv:
@@ -304,7 +304,7 @@ def _rope_write_kv(cache, layer_id, qkv, q_heads, kv_heads, positions, cos, sin,
         qkv.data_ptr(), qkv.stride(0), qkv.shape[0], q_heads, kv_heads, spec.head_size, positions.data_ptr(),
         cos.data_ptr(), sin.data_ptr(), cos.shape[0], layer.keys.data_ptr(), layer.values.data_ptr(),
         tables.data_ptr(), table_stride, computed.data_ptr(), query_start.data_ptr(), request_indices.data_ptr(),
-        config.block_size, torch.cuda.current_stream(device).cuda_stream), "lvb_rope_kv_write")
+        config.block_size, _native.stream_handle(device)), "lvb_rope_kv_write")
 
 
 class B200PagedAttentionBackend:

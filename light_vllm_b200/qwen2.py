@@ -237,7 +237,7 @@ class Qwen2AWQRunner:
         _native.check(self._lib.lvb_rope_qk(
             qkv.data_ptr(), qkv.stride(0), qkv.shape[0], self.layout.q_heads, self.layout.kv_heads, s.head_size,
             positions.data_ptr(), self.cos.data_ptr(), self.sin.data_ptr(), self.cos.shape[0],
-            torch.cuda.current_stream(self.device).cuda_stream), "lvb_rope_qk")
+            _native.stream_handle(self.device)), "lvb_rope_qk")
 
     def _greedy(self, hidden: Tensor) -> Tensor:
         logits = torch.mm(hidden, self.lm_head.t())
@@ -395,7 +395,7 @@ class StaticDecodeAttention:
         spec = self.cache.layer_spec(layer_id)
         config = self.cache.config
         layer = self.cache.layer(layer_id)
-        stream = torch.cuda.current_stream(self.device).cuda_stream
+        stream = _native.stream_handle(self.device)
         dtype_code = _native.DTYPE_BF16 if config.dtype == torch.bfloat16 else _native.DTYPE_F16
         query = _heads_contiguous(query, align=2)
         if write_kv:

@@ -81,7 +81,7 @@ class SingleStepStaging:
         return slot, host, self._dev
 
     def _stream(self) -> int:
-        return torch.cuda.current_stream(self._device).cuda_stream
+        return _native.stream_handle(self._device)
 
     def copy_groups(self, *groups: Sequence[int] | np.ndarray) -> tuple[Tensor, ...]:
         lengths = [len(group) for group in groups]
