@@ -239,3 +239,30 @@ def test_stage_rejects_violations_before_any_copy():
     assert status == _native.LVB_ERR_INVALID
     assert lib.lvb_event_wait_host(None) == _native.LVB_OK
     assert lib.lvb_event_destroy(None) == _native.LVB_OK
+
+
+def test_packer_input_types():
+    """The gatherer takes any integer-like ids (numpy scalars included),
+    refuses non-integers and layouts without ``parent_indices``, and hands
+    negative ids to the validator, which reports them as out of range."""
+
+    packer = StepMetadataPacker()
+
+    def md(tables, layouts=None):
+        return SimpleNamespace(block_tables=tables, num_computed_tokens=(15,) * len(tables),
+                               query_layouts=layouts or (linear_query_layout(1),) * len(tables),
+                               num_reserved_query_tokens=(1,) * len(tables),
+                               num_readonly_prefix_blocks=(0,) * len(tables))
+
+    step = packer.gather(md(((np.int64(2),), (np.int32(3),))))
+    out = np.zeros(step.packed_size, dtype=np.int32)
+    packer.pack(4, 16, out.ctypes.data, out.size)
+    assert out[:2].tolist() == [2, 3]
+    with pytest.raises(TypeError):
+        packer.gather(md(((2.0,),)))
+    with pytest.raises(AttributeError):
+        packer.gather(md(((2,),), layouts=((-1,),)))  # has a length, no parent_indices
+    step = packer.gather(md(((-5,),)))
+    out = np.zeros(step.packed_size, dtype=np.int32)
+    with pytest.raises(KVCacheError, match="out-of-range physical block"):
+        packer.pack(4, 16, out.ctypes.data, out.size)
