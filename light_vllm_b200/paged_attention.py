@@ -9,15 +9,17 @@ It replaces ``TritonPagedAttentionBackend``
 (runtime/execution/triton_paged_attention.py:399-581) with the sm_100a kernels
 of ``lvb_paged_kv_write`` and ``lvb_paged_attention``:
 
-* per step, the block tables, computed counts, query starts and request
-  indices go to the GPU in one pinned copy and are shared by every layer;
+* per step, the block tables, computed counts, query starts, request
+  indices and the decode launch order (longest context first) go to the GPU
+  in one pinned copy and are shared by every layer;
 * decode steps (one linear query per request) take the split-context kernel;
   every other batch (prefill chunks, mixed batches, tree visibility) the
   general kernel;
 * errors follow the reference: ``KVCacheError`` for a repeated layer, a shape,
   dtype or device mismatch, and any block-table violation.
 
-Nothing here computes on the CPU.
+No attention arithmetic runs on the CPU; the host side only gathers,
+validates and stages the step metadata, in native code.
 """
 
 from __future__ import annotations
@@ -182,9 +184,10 @@ class B200PagedAttention:
         self._backend = backend
         self._layer_ids: set[str] = set()
         self._device = torch.device(config.device)
-        # Validation (the reference's block-table rules, same order and
-        # messages) and packing of the per-step int32 payload run in native
-        # code; one pinned copy moves the payload to the device.
+        # Gathering from the metadata objects, validation (the reference's
+        # block-table rules, same order and messages), packing and the one
+        # pinned host-to-device copy of the per-step int32 payload all run in
+        # native code (_hostpack.gather_step, lvb_stage_step_metadata).
         packer = backend._packer
         step = packer.gather(metadata)
         packed = packer.stage(staging, config.num_blocks, config.block_size)
