@@ -89,9 +89,11 @@ class StepMetadataPacker:
     into flat C arrays through the ``_hostpack`` module; ``pack`` runs
     ``lvb_pack_step_metadata`` on them: the reference's block-table checks
     (runtime/execution/paged_attention.py:138-172, same order and messages),
-    then the padded tables, computed counts, query starts and request indices
-    written into the caller's int32 buffer.  Both are native; the Python here
-    only sizes buffers.
+    then the padded tables, computed counts, query starts, request indices
+    and decode launch order written into the caller's int32 buffer; ``stage``
+    does the same into a pinned staging slot and issues the device copy
+    (``lvb_stage_step_metadata``).  All of it is native; the Python here only
+    sizes buffers.
     """
 
     def __init__(self) -> None:
