@@ -23,26 +23,23 @@
 namespace lvb {
 namespace meta {
 
-// Per physical block: the call that last touched it, its first owner's
-// logical index and read-only mark, and the (call, row) stamp used to find
-// duplicates inside one row.  One 16-byte record, so a block costs one cache
-// line touch per check.
+// Per physical block: the (call, row) stamp of the row that last listed it
+// and that row's logical index for it, shifted left once, with the row's
+// read-only mark in bit 0.  Stamps grow monotonically across calls, so "listed
+// earlier in this call" is "stamp >= the call's first row stamp"; one 8-byte
+// record per block, read and written once per id.
 struct Owner {
-  uint32_t stamp;
   uint32_t row_stamp;
-  int32_t logical;
-  uint32_t readonly;
+  uint32_t logical_ro;
 };
 
 struct OwnerTable {
   std::vector<Owner> blocks;
-  uint32_t call = 0;  // stamp of the current call
-  uint32_t row = 0;   // last (call, row) stamp handed out
+  uint32_t row = 0;  // last (call, row) stamp handed out
 
   void reserve(int64_t num_blocks) {
     if (static_cast<int64_t>(blocks.size()) < num_blocks) {
-      blocks.assign(num_blocks, Owner{0, 0, 0, 0});
-      call = 0;
+      blocks.assign(num_blocks, Owner{0, 0});
       row = 0;
     }
   }
@@ -50,9 +47,9 @@ struct OwnerTable {
 
 // The rules of one row in the reference's order, without the fast path's
 // shortcuts; called only once the fused pass has seen a violation in row r
-// (rows before r passed).  Cross-row ownership stamps of rows < r are intact;
-// row r's own stamps may be partly written, which only the in-row duplicate
-// rule could notice, and that rule uses a fresh row stamp here.
+// (rows before r passed, so their stamps are intact).  Row r's own records
+// may be partly rewritten, which only the in-row duplicate rule could notice,
+// and that rule uses a fresh stamp here.
 inline const char *row_violation(const int32_t *ids, int64_t len, int64_t needed, int32_t computed,
                                  int32_t readonly, int64_t num_blocks, int64_t block_size, OwnerTable &owners,
                                  uint32_t row_stamp) {
@@ -71,21 +68,23 @@ inline const char *row_violation(const int32_t *ids, int64_t len, int64_t needed
 }
 
 // Returns nullptr when valid, otherwise the reference's message.  Valid rows
-// take one fused pass per entry (range, in-row duplicate, cross-row
-// ownership); the first violation sends its row through row_violation, which
-// applies the rules in the reference's order and so reports the same message.
+// take one fused pass per id (range, in-row duplicate, cross-row ownership);
+// the first violation sends its row through row_violation, which applies the
+// rules in the reference's order and so reports the same message.  A block
+// may appear in several rows only inside their read-only prefixes, at the
+// same logical index.
 inline const char *validate(const int32_t *block_ids, const int64_t *offsets, const int32_t *computed,
                             const int32_t *reserved, const int32_t *readonly, int64_t num_seqs,
                             int64_t num_blocks, int64_t block_size, OwnerTable &owners) {
   owners.reserve(num_blocks);
-  // Stamps (uint32): wrap-around clears the table once.
-  if (owners.call == UINT32_MAX || owners.row > UINT32_MAX - static_cast<uint32_t>(num_seqs) - 2) {
-    std::fill(owners.blocks.begin(), owners.blocks.end(), Owner{0, 0, 0, 0});
-    owners.call = 0;
+  // Stamps are uint32: a call needs num_seqs + 2 of them; wrap-around clears
+  // the table once.
+  if (owners.row > UINT32_MAX - static_cast<uint32_t>(num_seqs) - 2) {
+    std::fill(owners.blocks.begin(), owners.blocks.end(), Owner{0, 0});
     owners.row = 0;
   }
-  const uint32_t call = ++owners.call;
   uint32_t row = owners.row;
+  const uint32_t first = row + 1;  // stamps >= first were handed out in this call
   Owner *own = owners.blocks.data();
   const char *violation = nullptr;
   for (int64_t r = 0; r < num_seqs && violation == nullptr; ++r) {
@@ -101,16 +100,15 @@ inline const char *validate(const int32_t *block_ids, const int64_t *offsets, co
         ok = false;
         break;
       }
-      Owner &o = own[b];
-      const bool ro = i < ro_len;
-      if (o.row_stamp == rs || (o.stamp == call && (o.logical != i || !o.readonly || !ro))) {
+      const Owner o = own[b];
+      const uint32_t mine = (static_cast<uint32_t>(i) << 1) | (i < ro_len ? 1u : 0u);
+      // Listed before in this call: a duplicate in this row, or another row's
+      // block that may be shared only as the same read-only prefix block.
+      if (o.row_stamp >= first && (o.row_stamp == rs || (mine & 1u) == 0u || o.logical_ro != mine)) {
         ok = false;
         break;
       }
-      o.row_stamp = rs;
-      o.stamp = call;
-      o.logical = static_cast<int32_t>(i);
-      o.readonly = ro ? 1u : 0u;
+      own[b] = Owner{rs, mine};
     }
     if (!ok) violation = row_violation(ids, len, needed, computed[r], ro_len, num_blocks, block_size, owners, ++row);
   }
