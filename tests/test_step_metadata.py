@@ -266,3 +266,22 @@ def test_packer_input_types():
     out = np.zeros(step.packed_size, dtype=np.int32)
     with pytest.raises(KVCacheError, match="out-of-range physical block"):
         packer.pack(4, 16, out.ctypes.data, out.size)
+
+
+def test_ownership_stamps_reset_between_calls():
+    """Ownership is per call: a block listed in one call may be listed again
+    by any request of the next call; within a call only a read-only prefix
+    block at the same logical index may be shared."""
+
+    shared_ok = ([[7, 1], [7, 2]], [16, 16], [1, 1], [1, 1], [1, 1])
+    wrong_index = ([[7, 1], [2, 7]], [16, 16], [1, 1], [1, 1], [1, 1])
+    not_readonly = ([[7, 1], [7, 2]], [16, 16], [1, 1], [1, 1], [1, 0])
+    for _ in range(3):
+        for tables, computed, qlens, reserved, readonly in (shared_ok, ([[7, 1]], [16], [1], [1], [0])):
+            error, payload = native_pack(tables, computed, qlens, reserved, readonly, 8, 16)
+            assert error is None
+        error, _ = native_pack(*wrong_index, 8, 16)
+        assert error == "block tables alias a physical block across requests"
+        error, _ = native_pack(*not_readonly, 8, 16)
+        assert error == "block tables alias a physical block across requests"
+        assert oracle_error(wrong_index[0], wrong_index[1], wrong_index[3], wrong_index[4], 8, 16) == error
