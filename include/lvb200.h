@@ -94,16 +94,20 @@ LVB_API int lvb_awq_linear(const uint16_t *x, const int32_t *qweight, const int3
  * device memory: hosts whose device memory is wholly owned by another
  * allocator that they may not grow, or threads on a latency-critical path where
  * the device-wide synchronisation of cudaMalloc is not acceptable.  It takes no
- * workspace; the split-K scratch is a fixed 6 MiB array inside the library
- * (every GPU that loads the library holds it until exit), so calls whose plan
- * needs more than that are rejected with LVB_ERR_UNSUPPORTED (no call on a
- * GPU with up to 192 SMs does).  It calls no cudaMalloc/cudaFree.  The first
- * call on a device looks up the array's device address (set-up, once per
- * device, on the calling thread's current device); make that first call before
- * any stream capture.  Every call on a device shares the one array, so calls
- * that overlap on the GPU (different streams, no ordering between them) race
- * and may produce wrong results; order them on one stream.  No counterpart in
- * the reference. */
+ * workspace; the split-K scratch is a fixed array of 6 MiB + 4 KiB inside the
+ * library (every GPU that loads the library holds it until exit), so calls
+ * whose plan needs more than that are rejected with LVB_ERR_UNSUPPORTED (no
+ * call on a GPU with up to 192 SMs does).  It calls no cudaMalloc/cudaFree.
+ * The first call on a device looks up the array's device address (set-up,
+ * once per device, on the calling thread's current device); make that first
+ * call before any stream capture.  The address is cached for the process and
+ * is not valid after cudaDeviceReset.  Every call on a device shares the one
+ * array, which keeps the previous call's contents: each call clears the
+ * split-K semaphores it will use (cudaMemsetAsync on its stream) before its
+ * kernel, so a call that follows one aborted by a wait timeout starts clean.
+ * Calls that overlap on the GPU (different streams, no ordering between them)
+ * race and may produce wrong results; order them on one stream.  No
+ * counterpart in the reference. */
 LVB_API int lvb_awq_linear_static(const uint16_t *x, const int32_t *qweight,
                                   const int32_t *qzeros, const uint16_t *scales,
                                   const uint16_t *bias, uint16_t *y, int64_t m, int64_t k,
@@ -292,7 +296,7 @@ LVB_API int lvb_paged_attention(const uint16_t *query, int64_t query_token_strid
  * rank of the node maps it with lvb_ipc_open.  lvb_ipc_close unmaps a peer's
  * workspace, lvb_ipc_free releases one's own (after every peer has closed it).
  * Used by TensorParallelCollectives in place of the NCCL communicator set-up of
- * `CurrentStreamNCCL` (runtime/distributed/nccl.py:45-120). */
+ * `CurrentStreamNCCL` (runtime/execution/nccl.py:45-120). */
 LVB_API int lvb_ipc_alloc(size_t bytes, void **ptr, void *handle_out);
 LVB_API int lvb_ipc_open(const void *handle, void **ptr);
 LVB_API int lvb_ipc_close(void *ptr);
@@ -312,7 +316,7 @@ LVB_API int lvb_allreduce_workspace_init(void *workspace, int world, int64_t max
  * world ranks of `partial` (fp32, rounded to fp16 once), v = h + residual
  * (fp32), residual <- fp16(v), out <- fp16(v * rsqrt(mean(v^2) + eps) *
  * weight).  Replaces `all_reduce_sum` (modeling/tensor_parallel.py:18-27,
- * runtime/distributed/distributed.py:190-197, nccl.py:127-139) followed by
+ * runtime/execution/distributed.py:190-197, nccl.py:127-139) followed by
  * `fused_add_rms_norm` (modeling/models/_qwen2_kernels.py:20-43, 145-180).
  * With residual and weight both null it is the plain in-place-capable
  * all-reduce: out <- h (out may equal partial; eps is ignored).

@@ -9,6 +9,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <atomic>
 #include <climits>
 #include <cstdarg>
 #include <cstdio>
@@ -659,28 +660,35 @@ int launch_general(const lvb::attn::AttnArgs &a, int64_t num_tokens, cudaStream_
 // Fixed scratch for lvb_awq_linear_static
 // ------------------------------------------------------------------------
 // Callers that cannot allocate device memory get the split-K scratch from this
-// file-scope array instead.  6 MiB covers every split-K plan on GPUs with up to
-// 192 SMs (at most SMs x 64 x 128 fp32 partials plus one semaphore per tile).
-// It is part of the module image: every device that loads the library holds it
-// until the process exits.
-constexpr size_t kAwqStaticScratchBytes = size_t(6) << 20;
+// file-scope array instead.  6 MiB + 4 KiB covers every split-K plan on GPUs
+// with up to 192 SMs: at most SMs x 64 x 128 fp32 partials (6 MiB at 192 SMs)
+// plus the semaphore block in front of them (one uint32 per output tile,
+// rounded to 256 bytes).  It is part of the module image: every device that
+// loads the library holds it until the process exits.
+constexpr size_t kAwqStaticScratchBytes = (size_t(6) << 20) + 4096;
 __device__ __align__(256) unsigned char g_awq_static_scratch[kAwqStaticScratchBytes];
 
 // Device address of the array on each device.  In host code the symbol is a
 // host-side stand-in, not a device address, so it is looked up once per device
 // (with that device current) and only the looked-up pointer reaches a kernel.
-void *g_awq_static_scratch_addr[kMaxDevices] = {nullptr};
+// Double-checked: the lock is taken only while a device's address is still
+// unknown, so later calls read one atomic.  The cached address belongs to the
+// device's primary context; after cudaDeviceReset it is stale.
+std::atomic<void *> g_awq_static_scratch_addr[kMaxDevices];
 std::mutex g_awq_static_scratch_mu;
 
 int awq_static_scratch(int dev, void **out) {
-  std::lock_guard<std::mutex> lock(g_awq_static_scratch_mu);
-  if (g_awq_static_scratch_addr[dev] == nullptr) {
-    void *p = nullptr;
-    cudaError_t e = cudaGetSymbolAddress(&p, g_awq_static_scratch);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_awq_static_scratch)");
-    g_awq_static_scratch_addr[dev] = p;
+  void *p = g_awq_static_scratch_addr[dev].load(std::memory_order_acquire);
+  if (p == nullptr) {
+    std::lock_guard<std::mutex> lock(g_awq_static_scratch_mu);
+    p = g_awq_static_scratch_addr[dev].load(std::memory_order_relaxed);
+    if (p == nullptr) {
+      cudaError_t e = cudaGetSymbolAddress(&p, g_awq_static_scratch);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_awq_static_scratch)");
+      g_awq_static_scratch_addr[dev].store(p, std::memory_order_release);
+    }
   }
-  *out = g_awq_static_scratch_addr[dev];
+  *out = p;
   return LVB_OK;
 }
 

@@ -386,6 +386,114 @@ def make_qwen2(ref, seed: int = QWEN2_SEED, write: bool = True) -> float:
     return float(np.min(out["margins"]))
 
 
+QWEN2_PIN = dict(vocab_size=512, hidden_size=2048, intermediate_size=8192, num_hidden_layers=2,
+                 num_attention_heads=16, num_key_value_heads=2, max_position_embeddings=512,
+                 rms_norm_eps=1e-6, rope_theta=1e6)
+QWEN2_PIN_PROMPTS = (6, 11, 17, 23)
+QWEN2_PIN_STEPS = 64
+QWEN2_PIN_MARGIN = 0.02
+QWEN2_PIN_SEED = 1
+
+
+def make_qwen2_pin(ref, seed: int = QWEN2_PIN_SEED, threshold: float = float("-inf"),
+                   write: bool = True) -> float | None:
+    """Greedy tokens of a random-init AWQ Qwen2 whose MLP projections are
+    large enough (>= 8 MiB of int4 codes) for the B200 decode paths that the
+    7B/72B numbers run: one request alone (one-row decode) and four requests
+    together (small-batch decode), each a prefill plus 64 decode steps,
+    through the reference's own ``Qwen2ForCausalLM`` with the Torch AWQ scheme
+    and ``TorchPagedAttention`` (fp16, CPU).
+
+    Only the seed, prompts, tables, tokens, runner-up tokens and top-2 logit
+    margins are stored; the weights come from
+    ``qwen2_weights.random_awq_state``.  A model this size has steps whose
+    top-2 margin is one fp16 ulp of the logits, so the GPU test feeds the
+    reference's tokens back (teacher forcing) and requires its greedy pick to
+    equal the reference's at every step whose margin is at least
+    ``QWEN2_PIN_MARGIN`` and to be one of the reference's top two at the
+    others.  Returns the smallest margin (None if ``threshold`` is given and a
+    step falls below it).
+    """
+
+    sys.path.insert(0, str(HERE.parent.parent))
+    from tests.golden.qwen2_weights import checksum, random_awq_state
+
+    cfg = ref["Qwen2Config"](**QWEN2_PIN)
+    method = ref["AWQLinearMethod"](ref["AWQConfig"](group_size=128), ref["TorchAWQScheme"]())
+    model = ref["Qwen2ForCausalLM"](cfg, ref["TensorParallelContext"](), method, device="cpu",
+                                    dtype=torch.float16)
+    state = random_awq_state(QWEN2_PIN, seed)
+    out: dict[str, np.ndarray] = {}
+    with torch.no_grad():
+        sd = model.state_dict()
+        if set(sd) != set(state):
+            raise SystemExit(f"state dict keys differ: {sorted(set(sd) ^ set(state))[:8]}")
+        for key, tensor in state.items():
+            sd[key].copy_(tensor)
+        model.prepare_for_inference()
+        g = torch.Generator().manual_seed(seed + 7919)
+        prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in QWEN2_PIN_PROMPTS]
+        per_seq = -(-(max(QWEN2_PIN_PROMPTS) + QWEN2_PIN_STEPS) // QWEN2_BLOCK)
+        tables = tuple(tuple(range(i * per_seq, (i + 1) * per_seq)) for i in range(len(prompts)))
+        QL = ref["QueryLayout"]
+
+        def linear(n):
+            return QL(tuple(-1 if i == 0 else i - 1 for i in range(n)))
+
+        smallest = float("inf")
+        for run_name, members in (("single", (0,)), ("batch", tuple(range(len(prompts))))):
+            cache = ref["PagedKVCache"](model.kv_cache_spec,
+                                        ref["PagedKVCacheConfig"](len(prompts) * per_seq, QWEN2_BLOCK,
+                                                                  dtype=torch.float16))
+            run_tables = [tables[i] for i in members]
+
+            def run(ids, positions, computed, lengths):
+                starts = [0]
+                for n in lengths:
+                    starts.append(starts[-1] + n)
+                used = tuple(t[: -(-(c + n) // QWEN2_BLOCK)] for t, c, n in zip(run_tables, computed, lengths))
+                md = ref["PagedAttentionMetadata"](block_tables=used, num_computed_tokens=tuple(computed),
+                                                   query_layouts=tuple(linear(n) for n in lengths))
+                batch = ref["ForwardBatch"](input_ids=torch.tensor(ids, dtype=torch.long),
+                                            positions=torch.tensor(positions, dtype=torch.long),
+                                            query_start_loc=tuple(starts),
+                                            attention=ref["TorchPagedAttention"](cache, md),
+                                            logit_query_indices=tuple(s - 1 for s in starts[1:]))
+                logits = model(batch).logits.float()
+                top2 = logits.topk(2, dim=-1)
+                second.append(top2.indices[:, 1].tolist())
+                return logits.argmax(-1).tolist(), (top2.values[:, 0] - top2.values[:, 1]).tolist()
+
+            second: list[list[int]] = []
+            ps = [prompts[i] for i in members]
+            nxt, marg = run([t for p in ps for t in p], [i for p in ps for i in range(len(p))],
+                            [0] * len(ps), [len(p) for p in ps])
+            tokens, margins = [nxt], [marg]
+            ctx = [len(p) for p in ps]
+            for _ in range(QWEN2_PIN_STEPS):
+                if min(marg) < threshold:
+                    return None
+                nxt, marg = run(nxt, ctx, ctx, [1] * len(ps))
+                tokens.append(nxt)
+                margins.append(marg)
+                ctx = [c + 1 for c in ctx]
+            out[f"{run_name}_second"] = np.asarray(second, dtype=np.int64)
+            if min(marg) < threshold:
+                return None
+            smallest = min(smallest, float(np.min(margins)))
+            out[f"{run_name}_tokens"] = np.asarray(tokens, dtype=np.int64)   # [1 + steps, requests]
+            out[f"{run_name}_margins"] = np.asarray(margins, dtype=np.float32)
+    for i, p in enumerate(prompts):
+        out[f"prompt{i}"] = np.asarray(p, dtype=np.int64)
+    out["tables"] = np.asarray(tables, dtype=np.int32)
+    out["config_json"] = np.frombuffer(json.dumps(dict(QWEN2_PIN, group_size=128, block_size=QWEN2_BLOCK,
+                                                       seed=seed, weights_sha256=checksum(state))).encode(),
+                                       dtype=np.uint8)
+    if write:
+        np.savez_compressed(HERE / "qwen2_decode_pin.npz", **out)
+    return smallest
+
+
 def main() -> None:
     torch.set_num_threads(1)
     ref = _import_reference()
@@ -394,7 +502,9 @@ def main() -> None:
     make_attention(ref)
     make_fused_norm(ref)
     make_qwen2(ref)
-    for name in ("awq_golden.npz", "paged_meta.json", "paged_attn.npz", "fused_norm.npz", "qwen2_greedy.npz"):
+    make_qwen2_pin(ref)
+    for name in ("awq_golden.npz", "paged_meta.json", "paged_attn.npz", "fused_norm.npz", "qwen2_greedy.npz",
+                 "qwen2_decode_pin.npz"):
         print(name, (HERE / name).stat().st_size, "bytes")
 
 

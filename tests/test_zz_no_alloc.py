@@ -4,11 +4,13 @@
 memory for a workspace (their device memory belongs to another allocator, or
 cudaMalloc's device-wide synchronisation is off limits on their path); it uses
 a fixed scratch array inside the library instead.  This test calls both entry
-points through the C ABI on the same inputs, twice in a row with different
-shapes (so the second call reuses scratch the first one left behind), and
-checks each static result against the workspace result with the tolerance the
-AWQ tests use (max-abs 2e-2, relative L2 1e-3).  This file is named to be
-collected last.
+points through the C ABI on the same inputs: three shapes in a row (two
+split-K plans, whose semaphores live in the shared array, and one plan without
+split-K), each shape called twice back to back on the static entry point, so
+later calls reuse scratch that earlier ones left behind.  Every static result
+must equal the workspace result within the tolerance the AWQ tests use
+(max-abs 2e-2, relative L2 1e-3), and both must meet that tolerance against
+the fp32-accumulated CPU oracle.  This file is named to be collected last.
 """
 
 from __future__ import annotations
@@ -58,13 +60,23 @@ def _static(lib, x, qw, qz, sc, bias, g):
 
 def test_static_scratch_entry_point_matches_workspace_entry_point():
     lib = _native.library()
-    # Config-1 shape (split-K, BN=16), then a BN=64 split-K shape.
-    for m, k, n, g, seed in ((16, 896, 4864, 128, 101), (40, 1024, 2048, 64, 202)):
+    # Config-1 shape (split-K, BN=16), a BN=64 split-K shape, then m = 128
+    # with enough output tiles that the plan has no split-K.
+    shapes = ((16, 896, 4864, 128, 101), (40, 1024, 2048, 64, 202), (128, 1024, 4096, 128, 303))
+    for m, k, n, g, seed in shapes:
         x, qw, qz, sc, bias = _inputs(m, k, n, g, seed)
-        static_y = _static(lib, x, qw, qz, sc, bias, g)
+        first = _static(lib, x, qw, qz, sc, bias, g)
+        second = _static(lib, x, qw, qz, sc, bias, g)
         reference_y = _with_workspace(lib, x, qw, qz, sc, bias, g)
         torch.cuda.synchronize()
         assert _native.device_error() == 0
-        max_abs, rel = oawq.error_metrics(static_y.float().cpu().numpy(),
-                                          reference_y.float().cpu().numpy())
-        assert max_abs <= 2e-2 and rel <= 1e-3, (m, k, n, max_abs, rel)
+        want = reference_y.float().cpu().numpy()
+        oracle_y = oawq.linear_fp32(x.cpu().numpy(), qw.cpu().numpy(), qz.cpu().numpy(), sc.cpu().numpy(), g,
+                                    bias.cpu().numpy())
+        for got in (first, second):
+            max_abs, rel = oawq.error_metrics(got.float().cpu().numpy(), want)
+            assert max_abs <= 2e-2 and rel <= 1e-3, (m, k, n, max_abs, rel)
+            max_abs, rel = oawq.error_metrics(got.float().cpu().numpy(), oracle_y)
+            assert max_abs <= 2e-2 and rel <= 1e-3, ("oracle", m, k, n, max_abs, rel)
+        max_abs, rel = oawq.error_metrics(want, oracle_y)
+        assert max_abs <= 2e-2 and rel <= 1e-3, ("workspace vs oracle", m, k, n, max_abs, rel)
