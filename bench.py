@@ -80,15 +80,22 @@ def measured_peaks() -> dict:
 # ----------------------------------------------------------------------------
 # workload
 # ----------------------------------------------------------------------------
+def cache_types():
+    """light-vllm's own PagedKVCache / PagedAttentionMetadata classes (the
+    offline install under baseline/_ref, or LIGHT_VLLM_SRC) -- the objects the
+    backend receives in a real deployment -- else the oracle's stand-ins with
+    the same surface (input construction only; nothing timed runs in them)."""
+
+    from oracle.paged_cache import reference_types
+
+    return reference_types()
+
+
 def make_workload(torch, device):
-    from light_vllm_b200.kv_cache import (
-        AttentionLayerSpec,
-        ModelKVCacheSpec,
-        PagedAttentionMetadata,
-        PagedKVCache,
-        PagedKVCacheConfig,
-        linear_query_layout,
-    )
+    T = cache_types()
+    AttentionLayerSpec, ModelKVCacheSpec = T.AttentionLayerSpec, T.ModelKVCacheSpec
+    PagedAttentionMetadata, PagedKVCache, PagedKVCacheConfig = T.PagedAttentionMetadata, T.PagedKVCache, T.PagedKVCacheConfig
+    linear_query_layout = T.linear_query_layout
 
     c = CFG
     gen = torch.Generator().manual_seed(c["seed"])
@@ -319,8 +326,11 @@ def decode_case(torch, shape, rank: int, world: int, device, batches, ctx: int, 
     """Greedy decode steps of a random-init AWQ model, replayed from a CUDA
     graph (one graph per batch size), timed with CUDA events, max over ranks."""
 
-    from light_vllm_b200 import PagedKVCache, PagedKVCacheConfig
     import gc
+
+    from oracle.paged_cache import model_spec
+    T = cache_types()
+    PagedKVCache, PagedKVCacheConfig = T.PagedKVCache, T.PagedKVCacheConfig
 
     from light_vllm_b200.qwen2 import Qwen2AWQRunner, StaticDecodeAttention, random_shard
 
@@ -330,8 +340,8 @@ def decode_case(torch, shape, rank: int, world: int, device, batches, ctx: int, 
     runner = Qwen2AWQRunner(shape, weights, device, rank=rank, world=world, max_tokens=max(batches))
     del weights
     torch.cuda.empty_cache()
-    spec = runner.kv_cache_spec().layers[0]
-    kv_token_bytes = 2 * spec.num_kv_heads * spec.head_size * 2 * shape.num_hidden_layers
+    _, _, kv_heads, head_size = runner.kv_layers()[0]
+    kv_token_bytes = 2 * kv_heads * head_size * 2 * shape.num_hidden_layers
     def op_bytes(op):  # packed codes + (scale, zero) words, or the checkpoint tensors
         if op.groups is not None:
             return op.qweight.numel() * 4 + op.groups.numel() * op.groups.element_size()
@@ -343,7 +353,7 @@ def decode_case(torch, shape, rank: int, world: int, device, batches, ctx: int, 
     try:
         for b in batches:
             per = -(-(ctx + steps + warmup + 2) // 16)
-            cache = PagedKVCache(runner.kv_cache_spec(),
+            cache = PagedKVCache(model_spec(T, runner.kv_layers()),
                                  PagedKVCacheConfig(b * per, 16, dtype=torch.float16, device=device))
             for L in runner.layers:
                 layer = cache.layer(L.layer_id)

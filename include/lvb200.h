@@ -199,6 +199,27 @@ LVB_API int lvb_kv_scatter(const uint16_t *key, int64_t key_token_stride, const 
                    const int64_t *slots, int64_t num_tokens, int64_t num_kv_heads,
                    int64_t head_size, int64_t num_slots, int dtype, lvb_stream_t stream);
 
+/* Plan of the tree-acceptance compaction `PagedKVCache.compact`
+ * (runtime/execution/paged_cache.py:257-326): checks its argument rules in
+ * the reference's order (LVB_ERR_INVALID where it raises ValueError,
+ * LVB_ERR_METADATA where it raises KVCacheError, same messages) and writes
+ * the (source, target) slot of each retained query token; *moved = how many
+ * pairs differ (0: nothing to move).  counts = {num_computed_tokens,
+ * num_query_tokens, num_reserved_query_tokens, num_readonly_prefix_blocks};
+ * callers pass -1 for a value that is not an integer.  Host only. */
+LVB_API int lvb_kv_compact_plan(const int64_t *block_ids, int64_t num_table_blocks, const int64_t *counts,
+                                const int64_t *retained, int64_t num_retained, int64_t num_blocks,
+                                int64_t block_size, int32_t *src_slots, int32_t *dst_slots, int64_t *moved);
+
+/* Move K and V rows of one layer from src_slots[i] to dst_slots[i] (every
+ * KV head); every source row is read before any target is written, so the
+ * pairs may overlap.  The device half of `PagedKVCache.compact`'s
+ * index_select + index_copy_ (paged_cache.py:312-325).  Rows x head_size x 2
+ * bytes must fit 96 KiB. */
+LVB_API int lvb_kv_move_rows(uint16_t *key_cache, uint16_t *value_cache, const int32_t *src_slots,
+                             const int32_t *dst_slots, int64_t num_rows, int64_t num_kv_heads, int64_t head_size,
+                             int64_t num_slots, int dtype, lvb_stream_t stream);
+
 /* Host-only (no device work): validate one step's block tables and pack the
  * int32 payload the K/V-write and attention kernels read.  Inputs: the
  * concatenated block ids of every request with table_offsets[num_seqs + 1]

@@ -8,37 +8,25 @@ Two drop-in plugins behind light-vllm's own extension points:
   paged K/V and attends with sm_100a kernels (``light_vllm_b200.paged_attention``);
 
 plus ``TensorParallelCollectives`` for the row-parallel all-reduce on the
-caller's stream (``light_vllm_b200.collectives``).  All GPU work goes through
+caller's stream (``light_vllm_b200.collectives``) and ``compact_kv``, the
+tree-acceptance K/V compaction on the device (``light_vllm_b200.kv_cache``).
+Both plugins take light-vllm's own ``PagedKVCache`` and
+``PagedAttentionMetadata`` objects; this package defines no copies of them.  All GPU work goes through
 the C-ABI library ``_lib/liblvb200.so`` (``include/lvb200.h``); there is no
 CPU or Triton fallback.
 """
 
 from light_vllm_b200.awq import B200AWQOperation, B200AWQScheme, b200_awq_dequantize, b200_awq_linear
-from light_vllm_b200.kv_cache import (
-    AttentionLayerSpec,
-    KVCacheError,
-    ModelKVCacheSpec,
-    PagedAttentionMetadata,
-    PagedKVCache,
-    PagedKVCacheConfig,
-    QueryLayout,
-    linear_query_layout,
-)
+from light_vllm_b200.kv_cache import KVCacheError, compact_kv
 from light_vllm_b200.paged_attention import B200PagedAttention, B200PagedAttentionBackend
 
 __all__ = [
-    "AttentionLayerSpec",
     "B200AWQOperation",
     "B200AWQScheme",
     "B200PagedAttention",
     "B200PagedAttentionBackend",
     "KVCacheError",
-    "ModelKVCacheSpec",
-    "PagedAttentionMetadata",
-    "PagedKVCache",
-    "PagedKVCacheConfig",
-    "QueryLayout",
     "b200_awq_dequantize",
     "b200_awq_linear",
-    "linear_query_layout",
+    "compact_kv",
 ]

@@ -19,7 +19,7 @@ from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().parent / "_lib" / "liblvb200.so"
 HOSTPACK_PATH = Path(__file__).resolve().parent / "_lib" / ("_hostpack" + sysconfig.get_config_var("EXT_SUFFIX"))
-ABI_VERSION = 5
+ABI_VERSION = 6
 
 LVB_OK = 0
 LVB_ERR_INVALID = 1
@@ -69,6 +69,10 @@ PROTOTYPES: dict[str, tuple[object, tuple[object, ...]]] = {
         _int,
         (_c_ptr, _i64, _c_ptr, _i64, _c_ptr, _c_ptr, _c_ptr, _i64, _i64, _i64, _i64, _int, _c_ptr),
     ),
+    "lvb_kv_compact_plan": (
+        _int, (_c_ptr, _i64, _c_ptr, _c_ptr, _i64, _i64, _i64, _c_ptr, _c_ptr, ctypes.POINTER(_i64)),
+    ),
+    "lvb_kv_move_rows": (_int, (_c_ptr, _c_ptr, _c_ptr, _c_ptr, _i64, _i64, _i64, _i64, _int, _c_ptr)),
     "lvb_paged_attention_workspace_bytes": (_size, (_i64, _i64, _i64, _i64, _i64)),
     "lvb_pack_step_metadata": (
         _int,

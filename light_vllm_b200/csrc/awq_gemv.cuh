@@ -5,14 +5,16 @@
 // called from modeling/quantization/cuda_awq.py:96-122): y = x @ W (+ bias),
 // W[k][n] = (q - z) * s per 128-k group.  At m <= 4 the tensor cores would
 // multiply mostly padding, so each output column is reduced on CUDA cores
-// with integer dot products, exactly like the int8 tensor-core path:
+// with integer dot products, with the limb arithmetic of the int8 path
+// (awq_i8.cuh):
 //
-//   x is split per (token, group) into two int8 limbs, x = a (x0 + x1 / 128)
-//   with a a power of two (awq_act_limbs_kernel, the same prologue as the
-//   int8 path); for each group
-//     D0 = sum q x0,  D1 = sum q x1          (dp4a, exact in int32)
-//     v  = 128 D0 + D1 - z * sum(128 x0 + x1)  = sum (q - z)(128 x0 + x1)
-//     acc += s * (a / 128) * v               (fp32)
+//   x is split per (token, group) into four int8 limbs,
+//   x = a (x0 + x1 / 128 + x2 / 128^2 + x3 / 128^3), a a power of two
+//   (exact for every fp16 value within 2^17 of the group's largest); for
+//   each group
+//     D_l  = sum q x_l                               (dp4a, exact in int32)
+//     v_hi = 128 D0 + D1 - z * sum(128 x0 + x1),  v_lo = 128 D2 + D3 - z * sum(128 x2 + x3)
+//     acc += s * (a / 128) * (v_hi + v_lo / 128^2)   (fp32)
 //
 // Layout: the packed codes of awq_decode.cuh ([n_tile][32-k run][128 columns]
 // [16 B]); within a run, word w masked with 0x0F0F0F0F holds k = 4w + (0, 2,
@@ -23,11 +25,15 @@
 // one producer warp; a CTA covers a range of whole groups (split-K).  The
 // producer streams the range's codes -- contiguous in the packed layout --
 // into a ring of shared-memory stages with bulk async copies (mbarrier
-// complete_tx), starting before the limb prologue has finished; consumers
-// read their column's 16 bytes per run from shared memory and the limbs of
-// the range, staged once, as broadcasts.  Splits combine through per-split
-// fp32 partials and a semaphore: the last CTA of a tile sums them in split
-// order (deterministic), adds the bias and writes y.  Every wait is bounded.
+// complete_tx) from the moment the CTA starts; meanwhile the consumers wait
+// for the kernel that produced x (programmatic dependent launch), read the
+// range's activations (a few KB, L2-resident) and write their limbs into
+// shared memory -- one warp per (group, token) -- so no separate prologue
+// launch and no global limb buffer exist.  Consumers then read their
+// column's 16 bytes per run from shared memory and the limbs as broadcasts.
+// Splits combine through per-split fp32 partials and a semaphore: the last
+// CTA of a tile sums them in split order (deterministic), adds the bias and
+// writes y.  Every wait is bounded.
 #pragma once
 
 #include "awq_i8.cuh"
@@ -42,14 +48,15 @@ constexpr int kStageRuns = 4;      // 32-k runs per stage (8 KB of codes)
 constexpr int kStages = 5;         // 40 KB ring: 4 CTAs still fit an SM; measured best of 4 / 5 / 6
                                    // (7B gate_up m = 1: 19.0 / 17.7 / 24.7 us)
 constexpr int kStageBytes = kStageRuns * 128 * 16;
-constexpr int kLimbBN = 4;         // token rows of the prologue's limb tiles
 constexpr int kMaxM = 4;
+using awqi8::kLimbs;
 
 struct GemvParams {
   const uint8_t *qpack;    // [n_tiles][k_chunks][128][16 B]
   const uint32_t *szpack;  // [n_tiles][groups][128]: scale bits | zero << 16
-  const int8_t *limbs;     // [K/64][2 * kLimbBN][64 B], 64-byte swizzled (awq_act_limbs_kernel<4>)
-  const int2 *scal;        // [groups][kLimbBN]: (bits of a / 128, sum of 128 x0 + x1)
+  const uint16_t *x;       // [M] rows of x_stride fp16 (gated: merged [gate | up] rows of 2K)
+  int64_t x_stride;
+  int gated;               // activation = fp16(silu(gate) * up), as lvb_silu_mul rounds it
   const uint16_t *bias;    // may be null
   uint16_t *y;             // [M][N]
   uint32_t *semaphores;    // [n_tiles], zero between calls
@@ -59,17 +66,20 @@ struct GemvParams {
   int n_tiles, splits, groups_per_split;
 };
 
-// Shared memory: code stages, limb words [MT][2][range_quads] (quad q = k
-// offset 4q, bytes in the (0, 2, 1, 3) order), (a / 128, isum) per
-// [group][MT], the range's (scale, zero) words [group][128], then the
-// barriers (full[kStages], empty[kStages], sz) and the abort flag.
+// Shared memory: code stages, limb words [MT][kLimbs][range_quads] (quad q =
+// k offset 4q of the range, bytes in the (0, 2, 1, 3) order), per [group][MT]
+// (a / 128, sum of 128 x0 + x1, sum of 128 x2 + x3, 0), the range's (scale,
+// zero) words [group][128], then the barriers (full[kStages],
+// empty[kStages], sz) and the abort flag.
 template <int MT>
 struct GemvSmem {
   static constexpr size_t kLimbOff = static_cast<size_t>(kStages) * kStageBytes;
-  __host__ __device__ static size_t limb_bytes(int gps, int rpg) { return static_cast<size_t>(MT) * 2 * gps * rpg * 8 * 4; }
+  __host__ __device__ static size_t limb_bytes(int gps, int rpg) {
+    return static_cast<size_t>(MT) * kLimbs * gps * rpg * 8 * 4;
+  }
   __host__ __device__ static size_t scal_off(int gps, int rpg) { return kLimbOff + limb_bytes(gps, rpg); }
   __host__ __device__ static size_t sz_off(int gps, int rpg) {
-    return (scal_off(gps, rpg) + static_cast<size_t>(gps) * MT * 8 + 15) / 16 * 16;
+    return scal_off(gps, rpg) + static_cast<size_t>(gps) * MT * 16;
   }
   __host__ __device__ static size_t bar_off(int gps, int rpg) { return sz_off(gps, rpg) + static_cast<size_t>(gps) * kThreads * 4; }
   __host__ __device__ static size_t bytes(int gps, int rpg) { return bar_off(gps, rpg) + (2 * kStages + 1) * 8 + 16; }
@@ -91,13 +101,16 @@ __global__ void __launch_bounds__(kCtaThreads) awq_gemv_kernel(const __grid_cons
   const int nstages = (nruns + kStageRuns - 1) / kStageRuns;
   const int range_quads = nruns * 8;
   uint32_t *limb_sm = reinterpret_cast<uint32_t *>(smem + S::kLimbOff);
-  int2 *scal_sm = reinterpret_cast<int2 *>(smem + S::scal_off(p.groups_per_split, rpg));
+  int4 *scal_sm = reinterpret_cast<int4 *>(smem + S::scal_off(p.groups_per_split, rpg));
   const uint32_t *sz_sm = reinterpret_cast<const uint32_t *>(smem + S::sz_off(p.groups_per_split, rpg));
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + S::bar_off(p.groups_per_split, rpg));
   uint64_t *empty = full + kStages;
   uint64_t *sz_bar = empty + kStages;
   volatile int *abort_flag = reinterpret_cast<volatile int *>(sz_bar + 1);
 
+  // The next kernel of the stream may launch now; it waits for this grid's
+  // completion before touching y.
+  pdl_launch_dependents();
   if (tid == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], 1);
@@ -110,7 +123,7 @@ __global__ void __launch_bounds__(kCtaThreads) awq_gemv_kernel(const __grid_cons
   __syncthreads();
 
   if (warp == kThreads / 32) {
-    // Producer: codes do not depend on the limb prologue, so this starts at once.
+    // Producer: the codes do not depend on the previous kernel, so this starts at once.
     if (lane == 0) {
       // The range's (scale, zero) rows are contiguous: one copy.
       const uint32_t sz_bytes = static_cast<uint32_t>(g1 - g0) * kThreads * 4;
@@ -138,33 +151,81 @@ __global__ void __launch_bounds__(kCtaThreads) awq_gemv_kernel(const __grid_cons
     return;
   }
 
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-  // Limbs of this range: 16-byte chunks of the swizzled tiles, un-swizzled.
+  // Activations come from the previous kernel of the stream (this grid may
+  // have started during its tail): wait for it, then build this range's limbs.
+  pdl_wait();
   {
-    const int chunks_per_row = range_quads / 4;  // 16-byte chunks per (token, limb) row
-    const int total = MT * 2 * chunks_per_row;
-    const int k_base = run0 * 32;
-    for (int i = tid; i < total; i += kThreads) {
-      const int row = i / chunks_per_row;           // t * 2 + limb
-      const int c = i - row * chunks_per_row;
-      const int t = row >> 1, limb = row & 1;
-      const int k = k_base + c * 16;                // 16 k per 16-byte chunk (4 quads)
-      const int trow = limb * kLimbBN + t;          // row of the prologue tile
-      const int8_t *tilep = p.limbs + static_cast<size_t>(k >> 6) * (2 * kLimbBN * 64);
-      const uint4 v = *reinterpret_cast<const uint4 *>(tilep + awqi8::sw64(trow, k & 63));
-      reinterpret_cast<uint4 *>(limb_sm)[static_cast<size_t>(row) * chunks_per_row + c] = v;
-    }
-    for (int i = tid; i < (g1 - g0) * MT; i += kThreads) {
-      const int gg = i / MT, t = i - gg * MT;
-      scal_sm[i] = p.scal[static_cast<size_t>(g0 + gg) * kLimbBN + t];
+    const int G = p.G;
+    const int ng = g1 - g0;
+    for (int pr = warp; pr < ng * MT; pr += kThreads / 32) {
+      const int gg = pr / MT, t = pr - gg * MT;
+      const bool row_ok = t < p.M;
+      const uint16_t *xrow = p.x + static_cast<size_t>(row_ok ? t : 0) * p.x_stride + static_cast<size_t>(g0 + gg) * G;
+      auto load4 = [&](int i) -> uint2 {
+        if (!row_ok) return make_uint2(0u, 0u);
+        const uint2 gv = *reinterpret_cast<const uint2 *>(xrow + i);
+        if (!p.gated) return gv;
+        const uint2 uv = *reinterpret_cast<const uint2 *>(xrow + p.K + i);
+        const float2 ga = __half22float2(*reinterpret_cast<const __half2 *>(&gv.x));
+        const float2 gb = __half22float2(*reinterpret_cast<const __half2 *>(&gv.y));
+        const float2 ua = __half22float2(*reinterpret_cast<const __half2 *>(&uv.x));
+        const float2 ub = __half22float2(*reinterpret_cast<const __half2 *>(&uv.y));
+        const __half2 a0 = __floats2half2_rn(silu_times(ga.x, ua.x), silu_times(ga.y, ua.y));
+        const __half2 a1 = __floats2half2_rn(silu_times(gb.x, ub.x), silu_times(gb.y, ub.y));
+        return make_uint2(*reinterpret_cast<const uint32_t *>(&a0), *reinterpret_cast<const uint32_t *>(&a1));
+      };
+      float amax = 0.f;
+      for (int i = 4 * lane; i < G; i += 128) {
+        const uint2 raw = load4(i);
+        const __half2 h0 = *reinterpret_cast<const __half2 *>(&raw.x);
+        const __half2 h1 = *reinterpret_cast<const __half2 *>(&raw.y);
+        amax = fmaxf(amax, fmaxf(fmaxf(fabsf(__low2float(h0)), fabsf(__high2float(h0))),
+                                 fmaxf(fabsf(__low2float(h1)), fabsf(__high2float(h1)))));
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      const int e = awqi8::limb_exponent(amax);
+      const float inv_a = ldexpf(1.f, -e);
+      int s01 = 0, s23 = 0;
+      uint32_t *trow = limb_sm + static_cast<size_t>(t) * kLimbs * range_quads;
+      for (int i = 4 * lane; i < G; i += 128) {
+        const uint2 raw = load4(i);
+        const __half2 h0 = *reinterpret_cast<const __half2 *>(&raw.x);
+        const __half2 h1 = *reinterpret_cast<const __half2 *>(&raw.y);
+        const float v[4] = {__low2float(h0), __high2float(h0), __low2float(h1), __high2float(h1)};
+        uint32_t w[kLimbs] = {};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          int l[kLimbs];
+          awqi8::split_limbs(v[q] * inv_a, l);
+          s01 += l[0] * 128 + l[1];
+          s23 += l[2] * 128 + l[3];
+          const int pos = ((q & 1) << 1) | (q >> 1);  // byte of k-offset q in the quad
+#pragma unroll
+          for (int j = 0; j < kLimbs; ++j) w[j] |= (static_cast<uint32_t>(l[j]) & 0xFFu) << (8 * pos);
+        }
+        const int quad = (gg * G + i) >> 2;
+#pragma unroll
+        for (int j = 0; j < kLimbs; ++j) trow[static_cast<size_t>(j) * range_quads + quad] = w[j];
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        s01 += __shfl_xor_sync(0xffffffffu, s01, o);
+        s23 += __shfl_xor_sync(0xffffffffu, s23, o);
+      }
+      if (lane == 0) scal_sm[pr] = make_int4(__float_as_int(ldexpf(1.f, e - 7)), s01, s23, 0);
     }
   }
   consumers_sync();
 
   float acc[MT];
-  int d0[MT], d1[MT];
+  int d[MT][kLimbs];
 #pragma unroll
-  for (int t = 0; t < MT; ++t) acc[t] = 0.f, d0[t] = 0, d1[t] = 0;
+  for (int t = 0; t < MT; ++t) {
+    acc[t] = 0.f;
+#pragma unroll
+    for (int j = 0; j < kLimbs; ++j) d[t][j] = 0;
+  }
   int group = g0, run_in_group = 0;
   bool ok = mbar_wait(sz_bar, 0, abort_flag);
 
@@ -190,28 +251,21 @@ __global__ void __launch_bounds__(kCtaThreads) awq_gemv_kernel(const __grid_cons
         const int q0 = (st * kStageRuns + r) * 8;
 #pragma unroll
         for (int t = 0; t < MT; ++t) {
-          const uint4 *l0 = reinterpret_cast<const uint4 *>(limb_sm + (static_cast<size_t>(t) * 2) * range_quads + q0);
-          const uint4 *l1 = reinterpret_cast<const uint4 *>(limb_sm + (static_cast<size_t>(t) * 2 + 1) * range_quads + q0);
-          const uint4 a0 = l0[0], b0 = l0[1], a1 = l1[0], b1 = l1[1];
-          int s0 = d0[t], s1 = d1[t];
-          s0 = __dp4a(static_cast<int>(lo[0]), static_cast<int>(a0.x), s0);
-          s0 = __dp4a(static_cast<int>(lo[1]), static_cast<int>(a0.y), s0);
-          s0 = __dp4a(static_cast<int>(lo[2]), static_cast<int>(a0.z), s0);
-          s0 = __dp4a(static_cast<int>(lo[3]), static_cast<int>(a0.w), s0);
-          s0 = __dp4a(static_cast<int>(hi[0]), static_cast<int>(b0.x), s0);
-          s0 = __dp4a(static_cast<int>(hi[1]), static_cast<int>(b0.y), s0);
-          s0 = __dp4a(static_cast<int>(hi[2]), static_cast<int>(b0.z), s0);
-          s0 = __dp4a(static_cast<int>(hi[3]), static_cast<int>(b0.w), s0);
-          s1 = __dp4a(static_cast<int>(lo[0]), static_cast<int>(a1.x), s1);
-          s1 = __dp4a(static_cast<int>(lo[1]), static_cast<int>(a1.y), s1);
-          s1 = __dp4a(static_cast<int>(lo[2]), static_cast<int>(a1.z), s1);
-          s1 = __dp4a(static_cast<int>(lo[3]), static_cast<int>(a1.w), s1);
-          s1 = __dp4a(static_cast<int>(hi[0]), static_cast<int>(b1.x), s1);
-          s1 = __dp4a(static_cast<int>(hi[1]), static_cast<int>(b1.y), s1);
-          s1 = __dp4a(static_cast<int>(hi[2]), static_cast<int>(b1.z), s1);
-          s1 = __dp4a(static_cast<int>(hi[3]), static_cast<int>(b1.w), s1);
-          d0[t] = s0;
-          d1[t] = s1;
+#pragma unroll
+          for (int j = 0; j < kLimbs; ++j) {
+            const uint4 *l = reinterpret_cast<const uint4 *>(limb_sm + (static_cast<size_t>(t) * kLimbs + j) * range_quads + q0);
+            const uint4 a = l[0], b = l[1];
+            int acc_l = d[t][j];
+            acc_l = __dp4a(static_cast<int>(lo[0]), static_cast<int>(a.x), acc_l);
+            acc_l = __dp4a(static_cast<int>(lo[1]), static_cast<int>(a.y), acc_l);
+            acc_l = __dp4a(static_cast<int>(lo[2]), static_cast<int>(a.z), acc_l);
+            acc_l = __dp4a(static_cast<int>(lo[3]), static_cast<int>(a.w), acc_l);
+            acc_l = __dp4a(static_cast<int>(hi[0]), static_cast<int>(b.x), acc_l);
+            acc_l = __dp4a(static_cast<int>(hi[1]), static_cast<int>(b.y), acc_l);
+            acc_l = __dp4a(static_cast<int>(hi[2]), static_cast<int>(b.z), acc_l);
+            acc_l = __dp4a(static_cast<int>(hi[3]), static_cast<int>(b.w), acc_l);
+            d[t][j] = acc_l;
+          }
         }
         if (++run_in_group == rpg) {
           // Group done: fold the exact integer sums into the fp32 accumulators.
@@ -220,11 +274,13 @@ __global__ void __launch_bounds__(kCtaThreads) awq_gemv_kernel(const __grid_cons
           const int z = static_cast<int>(sz >> 16);
 #pragma unroll
           for (int t = 0; t < MT; ++t) {
-            const int2 sc = scal_sm[(group - g0) * MT + t];
-            const int v = 128 * d0[t] + d1[t] - z * sc.y;
-            acc[t] = fmaf(s * __int_as_float(sc.x), static_cast<float>(v), acc[t]);
-            d0[t] = 0;
-            d1[t] = 0;
+            const int4 sc = scal_sm[(group - g0) * MT + t];
+            const int v_hi = 128 * d[t][0] + d[t][1] - z * sc.y;
+            const int v_lo = 128 * d[t][2] + d[t][3] - z * sc.z;
+            const float v = fmaf(static_cast<float>(v_lo), 1.f / 16384.f, static_cast<float>(v_hi));
+            acc[t] = fmaf(s * __int_as_float(sc.x), v, acc[t]);
+#pragma unroll
+            for (int j = 0; j < kLimbs; ++j) d[t][j] = 0;
           }
           ++group;
           run_in_group = 0;

@@ -1,4 +1,4 @@
-// AutoAWQ W4A16 linear for decode batches (m <= 32) on the int8 tensor-core
+// AutoAWQ W4A16 linear for decode batches (m <= 16) on the int8 tensor-core
 // path: twice the weights per tcgen05.mma of the fp16 path.
 //
 // y[t, n] = sum_k x[t, k] * (q[k, n] - z[g, n]) * s[g, n]   (g = k / G)
@@ -8,17 +8,25 @@
 // at small N whatever its kind; with kind::f16 it retires 128 x 16 weights,
 // with kind::i8 128 x 32.  So here the weight operand is the raw int4 code q
 // as an int8 (exact), written into tensor memory by the dequantisers with two
-// logic operations per 8 codes, and the activations enter as int8 "limbs":
-// per (token, group) a power-of-two scale a with |x / a| <= 127, and
-//     x / a = x0 + x1 / 128,  x0 = rint(x / a) in [-127, 127],
-//                             x1 = rint(128 (x / a - x0)) in [-64, 64],
-// i.e. 15 significant bits relative to the group's largest element (the fp16
-// input has 11).  The MMA accumulates, exactly in int32, D0 = sum q x0 and
-// D1 = sum q x1 over one group; the drain warps then form, still exactly in
-// integers,  v = 128 D0 + D1 - z * sum_k (128 x0 + x1)  and add
-// s * (a / 128) * v to an fp32 accumulator.  The only roundings are the limb
-// quantisation of x and the fp32 conversion/accumulation; the zero point and
-// the scale are applied exactly (the reference rounds W to fp16 instead,
+// logic operations per 8 codes, and the activations enter as four int8
+// "limbs": per (token, group) a power-of-two scale a with |x / a| <= 127, and
+//     x / a = x0 + x1 / 128 + x2 / 128^2 + x3 / 128^3,
+//     x0 = rint(x / a) in [-127, 127], each later limb the rounded residual
+//     times 128, in [-64, 64]
+// (every residual is exact in fp32).  Relative to the group's largest
+// element a, this keeps 29 significant bits: every fp16 value within a
+// factor 2^17 of the group's largest is represented exactly, so a group that
+// mixes an activation outlier of 10^4 with N(0, 1) values keeps the small
+// values' precision (with two limbs they lost it all).  The four limbs are
+// four row blocks of the MMA's B operand (N = 4 x 16 = 64), so they cost no
+// extra MMA: its time is the same for every N <= 128.  The MMA accumulates,
+// exactly in int32, D_l = sum q x_l over one group; the drain warps form
+//     v_hi = 128 D0 + D1 - z * sum_k (128 x0 + x1),
+//     v_lo = 128 D2 + D3 - z * sum_k (128 x2 + x3)          (exact integers)
+// and add s * (a / 128) * (v_hi + v_lo / 128^2) to an fp32 accumulator.  The
+// only roundings are the fp32 conversion and accumulation (the limbs are
+// exact for the inputs above); the zero point and the scale are applied
+// exactly (the reference rounds W to fp16 instead,
 // modeling/quantization/awq.py:433-450).
 //
 // Kernels:
@@ -26,13 +34,13 @@
 //                         the K-major 64-byte-swizzled tile layout the MMA
 //                         reads (pre-swizzled, so a stage is one bulk copy),
 //                         and per (group, token) the scale a / 128 and the
-//                         integer sum of 128 x0 + x1.
+//                         integer sums of 128 x0 + x1 and 128 x2 + x3.
 //   awq_i8_kernel<BN>     persistent, one CTA per SM over (128-column tile,
 //                         K split) units; launched as a programmatic
 //                         dependent of the limb kernel so that its set-up and
 //                         code streaming overlap it:
 //     warp 0      bulk copies of the packed codes (16 KB per 256-k stage)
-//     warp 1      bulk copies of the limb tiles (2 BN rows x 256 k)
+//     warp 1      bulk copies of the limb tiles (4 BN rows x 256 k)
 //     warp 2      TMEM allocation and the tcgen05.mma.kind::i8 issuer of
 //                 even stages; warp 11 issues the odd stages
 //     warps 3..6  code expanders: q nibbles -> int8 A columns in TMEM
@@ -63,15 +71,35 @@ constexpr int kDrainWarp = 7;                         // first drain warp
 constexpr int kIssuer2Warp = 11;                      // second MMA issuer (odd stages)
 constexpr int kThreads = 12 * 32;
 constexpr int kTmemCols = 512;
+constexpr int kLimbs = 4;                             // int8 limbs per activation
+
+// x / a (exact in fp32: a power-of-two scaling of an fp16 value) into
+// kLimbs int8 limbs, x / a = sum_i l[i] / 128^i; each residual is exact.
+__device__ __forceinline__ void split_limbs(float r, int (&l)[kLimbs]) {
+#pragma unroll
+  for (int i = 0; i < kLimbs; ++i) {
+    const float li = rintf(r);
+    l[i] = static_cast<int>(li);
+    r = (r - li) * 128.f;
+  }
+}
+
+// Power-of-two exponent e of the limb scale a = 2^e: the smallest a with
+// amax / a <= 127 (a = 1 for an all-zero group).
+__device__ __forceinline__ int limb_exponent(float amax) {
+  int e = 0;
+  if (amax > 0.f) frexpf(amax / 127.f, &e);
+  return e;
+}
 
 // Groups of 128 or 256 k: a 256-k stage holds two groups or one, and the
 // MMA issuer, code expanders and drain synchronise once per stage.
 template <int BN>
 struct I8Config {
   // Stage accumulators in flight: the drain of stage s overlaps the MMAs of
-  // the next kDStages - 1 stages (as many as tensor memory holds).
-  static constexpr int kDStages = BN == 16 ? 4 : 2;
-  static constexpr int kLimbRows = 2 * BN;                   // (limb, token) rows of B
+  // the next stage (two fit beside the A stages in tensor memory).
+  static constexpr int kDStages = 2;
+  static constexpr int kLimbRows = kLimbs * BN;              // (limb, token) rows of B
   static constexpr int kLimbChunkBytes = kLimbRows * 64;     // one 64-k chunk of the limb tile
   static constexpr int kLimbStageBytes = kStageBlocks * kLimbChunkBytes;
   static constexpr int kQOff = kLimbStageBytes;              // limb tile first (1024-aligned)
@@ -84,15 +112,15 @@ struct I8Config {
   static constexpr int kNumBars = 3 * kStages + 2 * kDStages + 2;
   static_assert((kDStages & (kDStages - 1)) == 0, "power-of-two accumulator ring");
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;
-  // Per drain warp, two stage slots of per-token scalars (2 groups x BN x 8 bytes).
+  // Per drain warp, two stage slots of per-token scalars (2 groups x BN x 16 bytes).
   static constexpr int kScalOff = (kMiscOff + 64 + 15) / 16 * 16;
-  static constexpr int kScalSlotBytes = 2 * BN * 8;
+  static constexpr int kScalSlotBytes = 2 * BN * 16;
   static constexpr int kScalBytes = 4 * 2 * kScalSlotBytes;
   // Output tile [BN tokens][128 columns] fp16, written to y by one TMA store.
   static constexpr int kYOff = (kScalOff + kScalBytes + 127) / 128 * 128;
   static constexpr int kYBytes = BN * kTileN * 2;
   static constexpr int kSmemBytes = kYOff + kYBytes + 1024;
-  static_assert(BN == 16 || BN == 32, "int8 path covers 16- and 32-row token tiles");
+  static_assert(BN == 16, "int8 path covers 16-row token tiles (N = 4 limbs x 16 rows)");
   static_assert(kACol + kStages * kAStageCols <= kTmemCols, "tensor memory budget");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 };
@@ -100,8 +128,8 @@ struct I8Config {
 struct I8Params {
   const uint8_t *qpack;      // packed codes [n_tiles][k_chunks][128][16 B]
   const uint32_t *szpack;    // [n_tiles][groups][128] (scale bits | zero << 16)
-  const int8_t *limbs;       // [K/64][2 BN][64 B], pre-swizzled
-  const int2 *scal;          // [groups][BN]: (bits of a / 128, sum of 128 x0 + x1)
+  const int8_t *limbs;       // [K/64][kLimbs BN][64 B], pre-swizzled
+  const int4 *scal;          // [groups][BN]: (bits of a / 128, sum of 128 x0 + x1, sum of 128 x2 + x3, 0)
   const uint16_t *bias;      // may be null
   uint16_t *y;
   uint32_t *semaphores;
@@ -126,13 +154,14 @@ __host__ __device__ __forceinline__ int sw64(int row, int byte) {
 
 // One warp per (group, token row t < BN); rows t >= M are written as zeros.
 // Each lane handles 4 consecutive k (one quad) per pass and stores the quad's
-// two limbs as one 32-bit word each, bytes in the (0, 2, 1, 3) order.
-// x rows are x_stride elements apart.  gated: x holds merged [gate | up] rows
-// of 2K values and the activation is fp16(silu(gate) * up), rounded exactly as
-// lvb_silu_mul rounds it (the SiLU-mul fused into the down projection).
+// limbs as one 32-bit word per limb, bytes in the (0, 2, 1, 3) order; limb l
+// of token t is row l * BN + t of the tile.  x rows are x_stride elements
+// apart.  gated: x holds merged [gate | up] rows of 2K values and the
+// activation is fp16(silu(gate) * up), rounded exactly as lvb_silu_mul
+// rounds it (the SiLU-mul fused into the down projection).
 template <int BN>
 __global__ void __launch_bounds__(32) awq_act_limbs_kernel(const uint16_t *__restrict__ x, int64_t x_stride, int gated,
-                                                           int8_t *__restrict__ limbs, int2 *__restrict__ scal,
+                                                           int8_t *__restrict__ limbs, int4 *__restrict__ scal,
                                                            int M, int K, int G) {
   // The AWQ kernel that reads these limbs may start now and overlap this
   // grid; it waits for its completion before touching the outputs.  This
@@ -167,36 +196,36 @@ __global__ void __launch_bounds__(32) awq_act_limbs_kernel(const uint16_t *__res
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-  // Smallest power of two a with amax / a <= 127 (a = 1 for an all-zero row).
-  int e = 0;
-  if (amax > 0.f) frexpf(amax / 127.f, &e);
+  const int e = limb_exponent(amax);
   const float inv_a = ldexpf(1.f, -e);
-  int isum = 0;
+  int s01 = 0, s23 = 0;
   for (int i = 4 * lane; i < G; i += 128) {
     const uint2 raw = load4(i);
     const __half2 h0 = *reinterpret_cast<const __half2 *>(&raw.x);
     const __half2 h1 = *reinterpret_cast<const __half2 *>(&raw.y);
     const float v[4] = {__low2float(h0), __high2float(h0), __low2float(h1), __high2float(h1)};
-    uint32_t w0 = 0, w1 = 0;
+    uint32_t w[kLimbs] = {};
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
-      const float r = v[q] * inv_a;                 // exact: power-of-two scaling of an fp16 value
-      const float x0 = rintf(r);
-      const float x1 = rintf((r - x0) * 128.f);     // r - x0 exact, |r - x0| <= 1/2
-      const int i0 = static_cast<int>(x0), i1 = static_cast<int>(x1);
-      isum += i0 * 128 + i1;
+      int l[kLimbs];
+      split_limbs(v[q] * inv_a, l);
+      s01 += l[0] * 128 + l[1];
+      s23 += l[2] * 128 + l[3];
       const int pos = ((q & 1) << 1) | (q >> 1);    // byte of k-offset q in the quad
-      w0 |= (static_cast<uint32_t>(i0) & 0xFFu) << (8 * pos);
-      w1 |= (static_cast<uint32_t>(i1) & 0xFFu) << (8 * pos);
+#pragma unroll
+      for (int j = 0; j < kLimbs; ++j) w[j] |= (static_cast<uint32_t>(l[j]) & 0xFFu) << (8 * pos);
     }
     const int k = g * G + i;
-    int8_t *tile = limbs + static_cast<size_t>(k >> 6) * (2 * BN * 64);
-    *reinterpret_cast<uint32_t *>(tile + sw64(t, k & 63)) = w0;
-    *reinterpret_cast<uint32_t *>(tile + sw64(BN + t, k & 63)) = w1;
+    int8_t *tile = limbs + static_cast<size_t>(k >> 6) * (kLimbs * BN * 64);
+#pragma unroll
+    for (int j = 0; j < kLimbs; ++j) *reinterpret_cast<uint32_t *>(tile + sw64(j * BN + t, k & 63)) = w[j];
   }
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) isum += __shfl_xor_sync(0xffffffffu, isum, o);
-  if (lane == 0) scal[static_cast<size_t>(g) * BN + t] = make_int2(__float_as_int(ldexpf(1.f, e - 7)), isum);
+  for (int o = 16; o > 0; o >>= 1) {
+    s01 += __shfl_xor_sync(0xffffffffu, s01, o);
+    s23 += __shfl_xor_sync(0xffffffffu, s23, o);
+  }
+  if (lane == 0) scal[static_cast<size_t>(g) * BN + t] = make_int4(__float_as_int(ldexpf(1.f, e - 7)), s01, s23, 0);
 }
 
 // y tile store: shared [BN][128] fp16 -> global y at (column n0, row 0);
@@ -374,7 +403,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // accumulator ds = parity and A stages s = gs % 4 are private to one
     // issuer, and tcgen05.commit tracks only the issuing thread's MMAs.
     if (lane == 0) {
-      constexpr uint32_t idesc = umma_idesc_i8(kTileN, 2 * BN);
+      constexpr uint32_t idesc = umma_idesc_i8(kTileN, kLimbs * BN);
       const int parity = warp == 2 ? 0 : 1;
       bool ok = true;
       int gs = 0;
@@ -465,7 +494,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     auto fetch_scal = [&](const Unit &w, int ls, int gs_) {
       const int g0 = w.g_begin + ls * gps_full;
       const int ng = min(kStageBlocks, w.nblocks - ls * kStageBlocks) >> p.bpg_shift;
-      if (lane < ng * BN / 2)
+      if (lane < ng * BN)
         cp_async_16(smem_u32(scal_sm + (gs_ & 1) * C::kScalSlotBytes + lane * 16),
                     reinterpret_cast<const uint8_t *>(p.scal + static_cast<size_t>(g0) * BN) + lane * 16, 16u);
       cp_async_commit();
@@ -512,7 +541,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           fetch_scal(wn, 0, gs + 1);
           sz_next = sz_unit_next;
         }
-        const int4 *sc = reinterpret_cast<const int4 *>(scal_sm + (gs & 1) * C::kScalSlotBytes);
+        const int4 *sc = reinterpret_cast<const int4 *>(scal_sm + (gs & 1) * C::kScalSlotBytes);  // one per token
         const int ds = gs & (C::kDStages - 1);
         if (!__all_sync(0xffffffffu, mbar_wait(&d_full[ds], (gs / C::kDStages) & 1, abort_flag))) { ok = false; break; }
         tc_fence_after();
@@ -524,17 +553,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t dcol = tmem + lane_base + ds * C::kDStageCols + j * C::kGroupCols;
 #pragma unroll
           for (int h = 0; h < BN / 16; ++h) {
-            uint32_t d0[16], d1[16];
+            uint32_t d0[16], d1[16], d2[16], d3[16];
             tmem_ld_32x32b_x16(dcol + h * 16, d0);
             tmem_ld_32x32b_x16(dcol + BN + h * 16, d1);
+            tmem_ld_32x32b_x16(dcol + 2 * BN + h * 16, d2);
+            tmem_ld_32x32b_x16(dcol + 3 * BN + h * 16, d3);
             tmem_wait_ld();
 #pragma unroll
-            for (int t = 0; t < 16; t += 2) {
-              const int4 two = sc[(j * BN + h * 16 + t) / 2];
-              const int v0 = static_cast<int>(d0[t]) * 128 + static_cast<int>(d1[t]) - z * two.y;
-              const int v1 = static_cast<int>(d0[t + 1]) * 128 + static_cast<int>(d1[t + 1]) - z * two.w;
-              acc[h * 16 + t] = fmaf(s * __int_as_float(two.x), static_cast<float>(v0), acc[h * 16 + t]);
-              acc[h * 16 + t + 1] = fmaf(s * __int_as_float(two.z), static_cast<float>(v1), acc[h * 16 + t + 1]);
+            for (int t = 0; t < 16; ++t) {
+              const int4 sc4 = sc[j * BN + h * 16 + t];
+              const int v_hi = static_cast<int>(d0[t]) * 128 + static_cast<int>(d1[t]) - z * sc4.y;
+              const int v_lo = static_cast<int>(d2[t]) * 128 + static_cast<int>(d3[t]) - z * sc4.z;
+              const float v = fmaf(static_cast<float>(v_lo), 1.f / 16384.f, static_cast<float>(v_hi));
+              acc[h * 16 + t] = fmaf(s * __int_as_float(sc4.x), v, acc[h * 16 + t]);
             }
           }
         }

@@ -16,6 +16,7 @@
 #include <cstring>
 #include <mutex>
 #include <utility>
+#include <vector>
 
 #include "../../include/lvb200.h"
 #include "awq_gemm.cuh"
@@ -30,7 +31,7 @@
 
 namespace {
 
-constexpr int kAbiVersion = 5;
+constexpr int kAbiVersion = 6;
 constexpr int kMaxDevices = 64;
 
 thread_local char g_last_error[512] = "";
@@ -318,7 +319,7 @@ int launch_awq_packed(const PackedPlan &plan, const PackedShape &sh, const uint1
   return LVB_OK;
 }
 
-// int8 tensor-core path for decode batches: m <= 32, groups of 128 or 256 k
+// int8 tensor-core path for decode batches: m <= 16, groups of 128 or 256 k
 // (one or two whole groups per 256-k stage).
 // The int8 path pays a limb prologue and a persistent-kernel start-up that
 // only large weights amortise: measured on B200 at m = 16 it ties the fp16
@@ -326,8 +327,11 @@ int launch_awq_packed(const PackedPlan &plan, const PackedShape &sh, const uint1
 // 68 MB: 26.9 vs 40.6 us) and loses below (config 1, 2.2 MB: 13.0 vs 8.2 us).
 constexpr int64_t kI8MinWeightBytes = int64_t(8) << 20;
 
+// 16-row token tiles only: four activation limbs x 16 rows make the MMA's
+// N = 64, and two stage accumulators of two groups fill the tensor memory
+// beside the A stages.  Batches of 17..32 rows run the fp16 packed kernel.
 bool i8_eligible(int64_t m, int64_t k, int64_t n, int64_t g) {
-  return m <= 32 && (g == 128 || g == 256) && k % g == 0 && n % 128 == 0 && k * n / 2 >= kI8MinWeightBytes;
+  return m <= 16 && (g == 128 || g == 256) && k % g == 0 && n % 128 == 0 && k * n / 2 >= kI8MinWeightBytes;
 }
 
 struct I8Plan {
@@ -342,9 +346,10 @@ size_t round256(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
 // whole groups; same cost model as the packed path.
 I8Plan i8_plan(int64_t m, int64_t k, const PackedShape &sh, int64_t g, int sms, size_t max_ws = SIZE_MAX) {
   I8Plan p;
-  const int bn = m <= 16 ? 16 : 32;
-  p.limb_bytes = round256(static_cast<size_t>(k) * 2 * bn);
-  p.scal_bytes = round256(static_cast<size_t>(sh.groups) * bn * 8);
+  (void)m;
+  const int bn = 16;
+  p.limb_bytes = round256(static_cast<size_t>(k) * lvb::awqi8::kLimbs * bn);
+  p.scal_bytes = round256(static_cast<size_t>(sh.groups) * bn * sizeof(int4));
   if (p.limb_bytes + p.scal_bytes > max_ws) return p;
   p.bn = bn;
   const int bpg = static_cast<int>(g / 64);
@@ -377,7 +382,7 @@ int launch_awq_i8(const I8Plan &plan, const PackedShape &sh, const uint16_t *x, 
   int rc = ensure_smem(kernel, C::kSmemBytes, dev, smem_done);
   if (rc != LVB_OK) return rc;
   int8_t *limbs = reinterpret_cast<int8_t *>(ws + plan.sem_bytes + plan.part_bytes);
-  int2 *scal = reinterpret_cast<int2 *>(ws + plan.sem_bytes + plan.part_bytes + plan.limb_bytes);
+  int4 *scal = reinterpret_cast<int4 *>(ws + plan.sem_bytes + plan.part_bytes + plan.limb_bytes);
   cudaError_t e = launch_pdl(lvb::awqi8::awq_act_limbs_kernel<BN>, dim3(sh.groups, BN), dim3(32), 0, stream, x,
                              x_stride, gated, limbs, scal, static_cast<int>(m), static_cast<int>(k),
                              static_cast<int>(g));
@@ -442,21 +447,20 @@ bool gemv_eligible(int64_t m, int64_t k, int64_t n, int64_t g) {
 
 struct GemvPlan {
   int mt = 0, splits = 1, gps = 1;
-  size_t smem = 0, sem_bytes = 0, part_bytes = 0, limb_bytes = 0, scal_bytes = 0;
-  size_t total() const { return sem_bytes + part_bytes + limb_bytes + scal_bytes; }
+  size_t smem = 0, sem_bytes = 0, part_bytes = 0;
+  size_t total() const { return sem_bytes + part_bytes; }
 };
 
 constexpr size_t kGemvMaxSmem = 96 * 1024;
 
 // About four 128-thread CTAs per SM, whole groups per split, shared memory
-// for the split's limbs within kGemvMaxSmem; mt == 0 when the limbs do not fit
-// in `max_ws`.
+// for the split's limbs within kGemvMaxSmem; mt == 0 when no plan fits in
+// `max_ws` (split-K partials and semaphores only: the limbs live in shared
+// memory).
 GemvPlan gemv_plan(int64_t m, int64_t k, const PackedShape &sh, int64_t g, int sms, size_t max_ws = SIZE_MAX) {
   GemvPlan p;
+  (void)k;
   const int mt = m <= 1 ? 1 : m <= 2 ? 2 : 4;
-  p.limb_bytes = round256(static_cast<size_t>(k) * 2 * lvb::awqg::kLimbBN);
-  p.scal_bytes = round256(static_cast<size_t>(sh.groups) * lvb::awqg::kLimbBN * 8);
-  if (p.limb_bytes + p.scal_bytes > max_ws) return p;
   const int rpg = static_cast<int>(g / 32);
   auto smem_of = [&](int gps) {
     return mt == 1 ? lvb::awqg::GemvSmem<1>::bytes(gps, rpg)
@@ -470,12 +474,13 @@ GemvPlan gemv_plan(int64_t m, int64_t k, const PackedShape &sh, int64_t g, int s
   if (splits > sh.groups) splits = sh.groups;
   int gps = (sh.groups + splits - 1) / splits;
   while (smem_of(gps) > kGemvMaxSmem && gps > 1) --gps;
+  if (smem_of(gps) > kGemvMaxSmem) return p;
   splits = (sh.groups + gps - 1) / gps;
   const size_t sem = round256(static_cast<size_t>(sh.n_tiles) * 4);
   // Fewer splits when the partials do not fit the caller's workspace.
   while (true) {
     const size_t part = splits > 1 ? static_cast<size_t>(sh.n_tiles) * splits * m * lvb::awqg::kThreads * 4 : 0;
-    if ((splits > 1 ? sem : 0) + part + p.limb_bytes + p.scal_bytes <= max_ws) {
+    if ((splits > 1 ? sem : 0) + part <= max_ws) {
       p.part_bytes = part;
       p.sem_bytes = splits > 1 ? sem : 0;
       break;
@@ -493,6 +498,9 @@ GemvPlan gemv_plan(int64_t m, int64_t k, const PackedShape &sh, int64_t g, int s
   return p;
 }
 
+// One launch: the GEMV builds its activation limbs itself and is a
+// programmatic dependent of the kernel that produced x (its producer warp
+// streams codes before that kernel has finished).
 template <int MT>
 int launch_awq_gemv(const GemvPlan &plan, const PackedShape &sh, const uint16_t *x, const uint8_t *codes,
                     const uint32_t *groups, const uint16_t *bias, uint16_t *y, int64_t m, int64_t k, int64_t n,
@@ -501,17 +509,12 @@ int launch_awq_gemv(const GemvPlan &plan, const PackedShape &sh, const uint16_t 
   auto kernel = lvb::awqg::awq_gemv_kernel<MT>;
   int rc = ensure_smem(kernel, static_cast<int>(kGemvMaxSmem), dev, smem_done);
   if (rc != LVB_OK) return rc;
-  int8_t *limbs = reinterpret_cast<int8_t *>(ws + plan.sem_bytes + plan.part_bytes);
-  int2 *scal = reinterpret_cast<int2 *>(ws + plan.sem_bytes + plan.part_bytes + plan.limb_bytes);
-  cudaError_t e = launch_pdl(lvb::awqi8::awq_act_limbs_kernel<lvb::awqg::kLimbBN>, dim3(sh.groups, lvb::awqg::kLimbBN),
-                             dim3(32), 0, stream, x, x_stride, gated, limbs, scal, static_cast<int>(m),
-                             static_cast<int>(k), static_cast<int>(g));
-  if (e != cudaSuccess) return cuda_fail(e, "awq_act_limbs_kernel launch");
   lvb::awqg::GemvParams p{};
   p.qpack = codes;
   p.szpack = groups;
-  p.limbs = limbs;
-  p.scal = scal;
+  p.x = x;
+  p.x_stride = x_stride;
+  p.gated = gated;
   p.bias = bias;
   p.y = y;
   p.semaphores = reinterpret_cast<uint32_t *>(ws);
@@ -526,19 +529,8 @@ int launch_awq_gemv(const GemvPlan &plan, const PackedShape &sh, const uint16_t 
   p.n_tiles = sh.n_tiles;
   p.splits = plan.splits;
   p.groups_per_split = plan.gps;
-  // A programmatic dependent of the limb kernel: it streams its first codes
-  // while the limbs are computed and waits for them in-kernel.
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(sh.n_tiles), static_cast<unsigned>(plan.splits));
-  cfg.blockDim = dim3(lvb::awqg::kCtaThreads);
-  cfg.dynamicSmemBytes = plan.smem;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  e = cudaLaunchKernelEx(&cfg, kernel, p);
+  cudaError_t e = launch_pdl(kernel, dim3(static_cast<unsigned>(sh.n_tiles), static_cast<unsigned>(plan.splits)),
+                             dim3(lvb::awqg::kCtaThreads), plan.smem, stream, p);
   if (e != cudaSuccess) return cuda_fail(e, "awq_gemv_kernel launch");
   return LVB_OK;
 }
@@ -666,6 +658,7 @@ int launch_general(const lvb::attn::AttnArgs &a, int64_t num_tokens, cudaStream_
 // rounded to 256 bytes).  It is part of the module image: every device that
 // loads the library holds it until the process exits.
 constexpr size_t kAwqStaticScratchBytes = (size_t(6) << 20) + 4096;
+constexpr size_t kKvMoveMaxSmem = 96 * 1024;  // rows staged by one KV-move CTA
 __device__ __align__(256) unsigned char g_awq_static_scratch[kAwqStaticScratchBytes];
 
 // Device address of the array on each device.  In host code the symbol is a
@@ -850,7 +843,6 @@ int lvb_awq_linear_packed(const uint16_t *x, const void *codes, const void *grou
     const uint32_t *g8 = static_cast<const uint32_t *>(groups);
     uint8_t *w8 = static_cast<uint8_t *>(workspace);
     if (ip.bn == 16) return launch_awq_i8<16>(ip, sh, x, c8, g8, bias, y, m, k, n, group_size, w8, dev, stream_, k, 0);
-    if (ip.bn == 32) return launch_awq_i8<32>(ip, sh, x, c8, g8, bias, y, m, k, n, group_size, w8, dev, stream_, k, 0);
   }
   // The plan never needs more split-K workspace than the caller passed.
   const int per_sm = packed_ctas_per_sm(packed_bn(m), sh, m, sm_count(dev));
@@ -904,9 +896,8 @@ int lvb_awq_silu_linear_packed(const uint16_t *gate_up, int64_t gate_up_stride, 
   if (i8_eligible(m, k, n, group_size) && aligned16(y)) {
     const I8Plan ip = i8_plan(m, k, sh, group_size, sm_count(dev), max_ws);
     if (ip.bn == 16) return launch_awq_i8<16>(ip, sh, gate_up, c8, g8, bias, y, m, k, n, group_size, w8, dev, st, gate_up_stride, 1);
-    if (ip.bn == 32) return launch_awq_i8<32>(ip, sh, gate_up, c8, g8, bias, y, m, k, n, group_size, w8, dev, st, gate_up_stride, 1);
   }
-  return fail(LVB_ERR_UNSUPPORTED, "fused SiLU-mul linear covers decode batches (m <= 32, groups of 128 / 256) only");
+  return fail(LVB_ERR_UNSUPPORTED, "fused SiLU-mul linear covers decode batches (m <= 16, groups of 128 / 256) only");
 }
 
 static int kv_write_common(const lvb::attn::KVWriteArgs &a, int dtype, lvb_stream_t stream) {
@@ -978,6 +969,80 @@ int lvb_kv_scatter(const uint16_t *key, int64_t key_token_stride, const uint16_t
   a.D = static_cast<int>(head_size);
   a.bs = 1;
   return kv_write_common(a, dtype, stream);
+}
+
+// Rules of PagedKVCache.compact (runtime/execution/paged_cache.py:257-326),
+// in the order that decides which message a caller sees; counts[] =
+// {computed, query, reserved, readonly prefix blocks}.  Non-integers reach
+// here as -1 (the Python shim maps them), so they fail the rule of the field
+// they are in.
+int lvb_kv_compact_plan(const int64_t *block_ids, int64_t num_table_blocks, const int64_t *counts,
+                        const int64_t *retained, int64_t num_retained, int64_t num_blocks, int64_t block_size,
+                        int32_t *src_slots, int32_t *dst_slots, int64_t *moved) {
+  if (!counts || !moved || (num_table_blocks > 0 && !block_ids) || (num_retained > 0 && (!retained || !src_slots || !dst_slots)))
+    return fail(LVB_ERR_INVALID, "KV compaction null pointer argument");
+  if (block_size <= 0 || num_blocks <= 0 || num_table_blocks < 0 || num_retained < 0)
+    return fail(LVB_ERR_INVALID, "invalid KV compaction geometry");
+  *moved = 0;
+  const int64_t computed = counts[0], queries = counts[1], reserved = counts[2], readonly = counts[3];
+  if (computed < 0 || queries < 0 || reserved < 0 || readonly < 0)
+    return fail(LVB_ERR_INVALID, "paged compact counts must be non-negative integers");
+  if (reserved < queries) return fail(LVB_ERR_INVALID, "reserved query tokens must cover every actual query");
+  std::vector<int64_t> sorted(retained, retained + num_retained);
+  for (int64_t v : sorted)
+    if (v < 0) return fail(LVB_ERR_INVALID, "retained query indices must be non-negative integers");
+  std::sort(sorted.begin(), sorted.end());
+  if (std::adjacent_find(sorted.begin(), sorted.end()) != sorted.end())
+    return fail(LVB_ERR_INVALID, "retained query indices must be unique");
+  if (!sorted.empty() && sorted.back() >= queries)
+    return fail(LVB_ERR_METADATA, "retained query index exceeds the paged KV tail");
+  if (num_table_blocks != (computed + reserved + block_size - 1) / block_size)
+    return fail(LVB_ERR_METADATA, "block table does not exactly cover the reserved query slots");
+  std::vector<int64_t> ids(block_ids, block_ids + num_table_blocks);
+  for (int64_t b : ids)
+    if (b < 0 || b >= num_blocks) return fail(LVB_ERR_METADATA, "block table contains an invalid physical block");
+  std::sort(ids.begin(), ids.end());
+  if (std::adjacent_find(ids.begin(), ids.end()) != ids.end())
+    return fail(LVB_ERR_METADATA, "block table aliases a physical block within one request");
+  if (readonly * block_size > computed)
+    return fail(LVB_ERR_METADATA, "readonly prefix blocks exceed the computed prefix");
+  if (num_blocks * block_size > INT_MAX) return fail(LVB_ERR_UNSUPPORTED, "KV slot index exceeds int32");
+  auto slot = [&](int64_t pos) { return block_ids[pos / block_size] * block_size + pos % block_size; };
+  int64_t changed = 0;
+  for (int64_t i = 0; i < num_retained; ++i) {
+    src_slots[i] = static_cast<int32_t>(slot(computed + retained[i]));
+    dst_slots[i] = static_cast<int32_t>(slot(computed + i));
+    changed += src_slots[i] != dst_slots[i];
+  }
+  *moved = changed;
+  return LVB_OK;
+}
+
+int lvb_kv_move_rows(uint16_t *key_cache, uint16_t *value_cache, const int32_t *src_slots,
+                     const int32_t *dst_slots, int64_t num_rows, int64_t num_kv_heads, int64_t head_size,
+                     int64_t num_slots, int dtype, lvb_stream_t stream) {
+  (void)num_slots;
+  if (dtype != LVB_DTYPE_F16 && dtype != LVB_DTYPE_BF16) return fail(LVB_ERR_INVALID, "unknown dtype %d", dtype);
+  if (num_rows < 0 || num_kv_heads <= 0 || head_size <= 0 || head_size % 8 != 0)
+    return fail(LVB_ERR_INVALID, "invalid KV move shape (head_size must be a multiple of 8)");
+  if (num_rows == 0) return LVB_OK;
+  if (!key_cache || !value_cache || !src_slots || !dst_slots) return fail(LVB_ERR_INVALID, "KV move null pointer argument");
+  if (!aligned16(key_cache) || !aligned16(value_cache)) return fail(LVB_ERR_INVALID, "KV caches must be 16-byte aligned");
+  const size_t smem = static_cast<size_t>(num_rows) * head_size * 2;
+  if (smem > kKvMoveMaxSmem)
+    return fail(LVB_ERR_UNSUPPORTED, "KV move of %lld rows x %lld values exceeds %zu bytes of shared memory",
+                (long long)num_rows, (long long)head_size, kKvMoveMaxSmem);
+  int dev = 0;
+  int rc = current_device(&dev);
+  if (rc != LVB_OK) return rc;
+  static bool smem_done[kMaxDevices] = {false};
+  rc = ensure_smem(lvb::attn::kv_move_rows_kernel, static_cast<int>(kKvMoveMaxSmem), dev, smem_done);
+  if (rc != LVB_OK) return rc;
+  cudaError_t e = launch_pdl(lvb::attn::kv_move_rows_kernel, dim3(static_cast<unsigned>(num_kv_heads), 2), dim3(128), smem,
+                             reinterpret_cast<cudaStream_t>(stream), key_cache, value_cache, src_slots, dst_slots,
+                             static_cast<int>(num_rows), static_cast<int>(num_kv_heads), static_cast<int>(head_size));
+  if (e != cudaSuccess) return cuda_fail(e, "kv_move_rows_kernel launch");
+  return LVB_OK;
 }
 
 size_t lvb_paged_attention_workspace_bytes(int64_t num_seqs, int64_t num_q_heads,

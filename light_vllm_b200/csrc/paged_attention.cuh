@@ -119,6 +119,32 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
+// KV compaction move (tree acceptance): rows of every (slot, head) listed in
+// src move to the matching dst slot.  One CTA per (KV head, K or V) stages all
+// of its source rows in shared memory before writing any target, so the moves
+// may overlap (a target slot that is also a later source).  head_size % 8 == 0.
+__global__ void __launch_bounds__(128) kv_move_rows_kernel(uint16_t *__restrict__ key_cache,
+                                                           uint16_t *__restrict__ value_cache,
+                                                           const int32_t *__restrict__ src,
+                                                           const int32_t *__restrict__ dst, int n, int hkv, int d) {
+  extern __shared__ __align__(16) uint8_t move_smem[];
+  pdl_entry();
+  uint4 *rows = reinterpret_cast<uint4 *>(move_smem);
+  uint16_t *base = blockIdx.y == 0 ? key_cache : value_cache;
+  const int head = blockIdx.x;
+  const int vec = d / 8;  // 16-byte vectors per row
+  const size_t slot_elems = static_cast<size_t>(hkv) * d;
+  for (int i = threadIdx.x; i < n * vec; i += blockDim.x) {
+    const int r = i / vec, c = i - r * vec;
+    rows[i] = *reinterpret_cast<const uint4 *>(base + static_cast<size_t>(src[r]) * slot_elems + head * d + c * 8);
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < n * vec; i += blockDim.x) {
+    const int r = i / vec, c = i - r * vec;
+    *reinterpret_cast<uint4 *>(base + static_cast<size_t>(dst[r]) * slot_elems + head * d + c * 8) = rows[i];
+  }
+}
+
 // ------------------------------------------------------------------------
 // General kernel
 // ------------------------------------------------------------------------

@@ -48,7 +48,7 @@ from light_vllm_b200.collectives import (
     awq_row_shard,
     partition_dimension,
 )
-from light_vllm_b200.kv_cache import AttentionLayerSpec, KVCacheError, ModelKVCacheSpec
+from light_vllm_b200.kv_cache import KVCacheError
 from light_vllm_b200.paged_attention import _heads_contiguous, _rope_write_kv
 
 
@@ -213,12 +213,14 @@ class Qwen2AWQRunner:
         self._lib = _native.library()
 
     # ------------------------------------------------------------------ specs
-    def kv_cache_spec(self) -> ModelKVCacheSpec:
-        """Per-layer K/V geometry of this rank (qwen2.py:597-611)."""
+    def kv_layers(self) -> tuple[tuple[str, int, int, int], ...]:
+        """Per-layer K/V geometry of this rank, (layer_id, query heads, KV
+        heads, head size) -- the fields of the reference's
+        ``AttentionLayerSpec`` entries of ``kv_cache_spec`` (qwen2.py:597-611);
+        build the cache's ``ModelKVCacheSpec`` from them."""
 
-        return ModelKVCacheSpec(tuple(
-            AttentionLayerSpec(L.layer_id, self.layout.q_heads, self.layout.kv_heads, self.shape.head_size)
-            for L in self.layers))
+        return tuple((L.layer_id, self.layout.q_heads, self.layout.kv_heads, self.shape.head_size)
+                     for L in self.layers)
 
     def close(self) -> None:
         self.workspace.close()

@@ -23,18 +23,16 @@ import numpy as np
 import pytest
 import torch
 
-from light_vllm_b200 import _native
-from light_vllm_b200.kv_cache import (
-    AttentionLayerSpec,
-    KVCacheError,
-    ModelKVCacheSpec,
-    PagedAttentionMetadata,
-    PagedKVCache,
-    PagedKVCacheConfig,
-    QueryLayout,
-    linear_query_layout,
-)
+from light_vllm_b200 import KVCacheError, _native, compact_kv
 from light_vllm_b200.paged_attention import B200PagedAttentionBackend
+from oracle.paged_cache import reference_types
+
+# light-vllm's own cache and metadata classes when importable, else the
+# oracle's stand-ins (same surface): the backend is driven through them.
+_T = reference_types()
+AttentionLayerSpec, ModelKVCacheSpec = _T.AttentionLayerSpec, _T.ModelKVCacheSpec
+PagedAttentionMetadata, QueryLayout, linear_query_layout = _T.PagedAttentionMetadata, _T.QueryLayout, _T.linear_query_layout
+PagedKVCache, PagedKVCacheConfig = _T.PagedKVCache, _T.PagedKVCacheConfig
 from oracle import awq as oawq
 from oracle import paged_attention as opa
 
@@ -394,9 +392,10 @@ def test_strided_qkv_views_are_accepted():
 
 def test_compaction_moves_retained_queries_like_the_reference():
     """The reference's compaction test (tests/test_paged_attention.py:178-228)
-    on the B200 cache (head size 8 instead of 4: the scatter kernel moves
-    16-byte rows): retained queries (0, 2, 4) land in slots (6, 7, 0) and the
-    readonly prefix block is untouched."""
+    through ``compact_kv`` (native plan + ``lvb_kv_move_rows``; head size 8
+    instead of 4: the kernel moves 16-byte rows): retained queries (0, 2, 4)
+    land in slots (6, 7, 0), the readonly prefix block is untouched, and the
+    cache equals the one the cache's own ``compact`` produces."""
 
     spec = ModelKVCacheSpec((AttentionLayerSpec("attention", 2, 2, 8),))
     device = torch.device("cuda", 0)
@@ -412,10 +411,17 @@ def test_compaction_moves_retained_queries_like_the_reference():
     query_keys = (torch.arange(80, dtype=torch.float32).reshape(5, 2, 8) + 40).half().to(device)
     query_values = query_keys + 200
     cache.write("attention", query_keys, query_values, md.slot_mapping(block_size=2, device=device))
-    moved = cache.compact(md.block_tables[0], num_computed_tokens=2, num_query_tokens=5, num_reserved_query_tokens=5,
-                          retained_query_indices=(0, 2, 4), num_readonly_prefix_blocks=1)
+    twin = PagedKVCache(spec, PagedKVCacheConfig(4, 2, dtype=torch.float16, device=device))
+    twin.layer("attention").keys.copy_(layer.keys)
+    twin.layer("attention").values.copy_(layer.values)
+    args = dict(num_computed_tokens=2, num_query_tokens=5, num_reserved_query_tokens=5,
+                retained_query_indices=(0, 2, 4), num_readonly_prefix_blocks=1)
+    moved = compact_kv(cache, md.block_tables[0], **args)
+    assert twin.compact(md.block_tables[0], **args) == moved
     torch.cuda.synchronize()
     assert moved == 2
+    assert torch.equal(layer.keys, twin.layer("attention").keys)
+    assert torch.equal(layer.values, twin.layer("attention").values)
     assert torch.equal(layer.keys[1], prefix_keys)
     flat_k = layer.keys.view(8, 2, 8)
     flat_v = layer.values.view(8, 2, 8)

@@ -38,8 +38,12 @@ def _fixture():
 
 
 def _generate(rank: int, world: int, graph: bool, group=None) -> np.ndarray:
-    from light_vllm_b200 import B200PagedAttentionBackend, PagedAttentionMetadata, PagedKVCache, PagedKVCacheConfig
-    from light_vllm_b200.kv_cache import linear_query_layout
+    from light_vllm_b200 import B200PagedAttentionBackend
+    from oracle.paged_cache import model_spec, reference_types
+
+    T = reference_types()
+    PagedAttentionMetadata, PagedKVCache, PagedKVCacheConfig = T.PagedAttentionMetadata, T.PagedKVCache, T.PagedKVCacheConfig
+    linear_query_layout = T.linear_query_layout
     from light_vllm_b200.qwen2 import Qwen2AWQRunner, Qwen2Shape, StaticDecodeAttention, shard_state_dict
 
     d, cfg, weights, prompts = _fixture()
@@ -49,7 +53,7 @@ def _generate(rank: int, world: int, graph: bool, group=None) -> np.ndarray:
                             rank=rank, world=world, group=group, max_tokens=64)
     bs = cfg["block_size"]
     tables = [[int(b) for b in t] for t in d["tables"]]
-    cache = PagedKVCache(runner.kv_cache_spec(), PagedKVCacheConfig(32, bs, dtype=torch.float16, device=device))
+    cache = PagedKVCache(model_spec(T, runner.kv_layers()), PagedKVCacheConfig(32, bs, dtype=torch.float16, device=device))
     backend = B200PagedAttentionBackend()
     steps = len(d["tokens"]) - 1
 

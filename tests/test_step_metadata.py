@@ -18,10 +18,15 @@ from types import SimpleNamespace
 import numpy as np
 import pytest
 
-from light_vllm_b200 import _native
-from light_vllm_b200.kv_cache import KVCacheError, PagedAttentionMetadata, QueryLayout, linear_query_layout
+from light_vllm_b200 import KVCacheError, _native
 from light_vllm_b200.paged_attention import StepMetadataPacker
 from oracle import paged_attention as opa
+from oracle.paged_cache import reference_types
+
+# The packer reads light-vllm's own PagedAttentionMetadata / QueryLayout
+# objects when light-vllm is importable, else the oracle's stand-ins.
+_T = reference_types()
+PagedAttentionMetadata, QueryLayout, linear_query_layout = _T.PagedAttentionMetadata, _T.QueryLayout, _T.linear_query_layout
 
 META = json.loads((Path(__file__).resolve().parent / "golden" / "paged_meta.json").read_text())
 
@@ -98,6 +103,35 @@ def test_golden_cases(case):
         check_payload(payload, case["tables"], case["computed"], qlens)
 
 
+@pytest.mark.parametrize("case", META, ids=[c["name"] for c in META])
+def test_golden_cases_through_the_metadata_objects(case):
+    """The product path over the metadata objects themselves (light-vllm's own
+    ``PagedAttentionMetadata`` when importable): gather + validate + pack give
+    the reference's validation message, or the packed payload."""
+
+    md = PagedAttentionMetadata(
+        block_tables=tuple(tuple(t) for t in case["tables"]),
+        num_computed_tokens=tuple(case["computed"]),
+        query_layouts=tuple(QueryLayout(tuple(p)) for p in case["layouts"]),
+        num_reserved_query_tokens=tuple(case.get("reserved") or ()),
+        num_readonly_prefix_blocks=tuple(case.get("readonly") or ()),
+    )
+    packer = StepMetadataPacker()
+    step = packer.gather(md)
+    out = np.zeros(step.packed_size, dtype=np.int32)
+    try:
+        packer.pack(case["num_blocks"], case["block_size"], out.ctypes.data, out.size)
+        error = None
+    except KVCacheError as exc:
+        if _T.source == "light_vllm":
+            assert isinstance(exc, _T.KVCacheError)  # the Worker's handlers catch it
+        error = str(exc)
+    assert error == case["validate_error"]
+    if error is None:
+        qlens = [len(p) for p in case["layouts"]]
+        check_payload((out, step.max_blocks, step.num_tokens), case["tables"], case["computed"], qlens)
+
+
 def _random_case(rng: random.Random):
     block_size = rng.choice((1, 2, 4, 16))
     num_blocks = rng.randint(4, 40)
@@ -165,7 +199,7 @@ def test_small_buffer_is_rejected():
 
 
 def test_packer_reads_the_metadata_objects():
-    """Gathering from the metadata mirror: tuples and lists, tree layouts
+    """Gathering from the metadata objects: tuples and lists, tree layouts
     (not linear), ids beyond int32 (reported as out of range, as the
     reference reports any id >= num_blocks), counts beyond int32 refused."""
 
