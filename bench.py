@@ -278,6 +278,120 @@ def awq_detail(torch, peaks, steps: int, shapes_arg: str | None = None) -> list[
 
 
 # ----------------------------------------------------------------------------
+# The reference's own GPU paths on this B200 (detail, when light-vllm is importable)
+# ----------------------------------------------------------------------------
+def _time_fn(torch, fn, iters: int) -> float:
+    """ms per call of fn: a CUDA graph of one call replayed when capturable,
+    else back-to-back eager calls; CUDA events on the current stream."""
+
+    try:
+        graph = capture(torch, fn)
+        return time_graph(torch, graph, iters, 3)
+    except Exception:  # not capturable: eager calls
+        torch.cuda.synchronize()
+        for _ in range(3):
+            fn()
+        stream = torch.cuda.current_stream()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(iters):
+            fn()
+        end.record(stream)
+        torch.cuda.synchronize()
+        return start.elapsed_time(end) / iters
+
+
+def reference_gpu_detail(torch, peaks, steps: int, cache, md, q, k, v, ctx, ours: dict) -> dict:
+    """light-vllm's own GPU paths on the same B200 -- the CUDA AWQ extension
+    (CudaAWQScheme: mma.sync K1 kernel below 256 rows, dequantise + cuBLAS
+    above; JIT-built for this GPU by the reference's loader) and the Triton
+    paged-attention backend -- on the same shapes and inputs as ours."""
+
+    T = cache_types()
+    if T.source != "light_vllm":
+        return {"unavailable": "light-vllm is not importable (no baseline/_ref, no LIGHT_VLLM_SRC)"}
+    import numpy as np
+
+    from oracle import awq as oawq  # input generator only
+    out: dict = {}
+    try:
+        from light_vllm.modeling.quantization.awq_schemes import CudaAWQScheme
+
+        t0 = time.perf_counter()
+        scheme = CudaAWQScheme()
+        rows = []
+        l2 = 126 * 1024 * 1024
+        for name, m, kk, n, g in (("config1 0.5B up-proj", 16, 896, 4864, 128), ("7B gate_up", 1, 3584, 37888, 128),
+                                  ("7B gate_up", 16, 3584, 37888, 128), ("7B gate_up", 64, 3584, 37888, 128),
+                                  ("7B down", 16, 18944, 3584, 128), ("7B gate_up prefill", 2048, 3584, 37888, 128)):
+            qweight, qzeros, scales = oawq.random_checkpoint(kk, n, g, seed=m + kk + n)
+            weight_bytes = qweight.nbytes + qzeros.nbytes + scales.nbytes
+            copies = max(1, math.ceil(2 * l2 / weight_bytes)) if m <= 256 else 1
+            dev = torch.device("cuda")
+            base = [torch.from_numpy(a).to(dev) for a in (qweight, qzeros, scales)]
+            ops = [scheme.prepare(*([t.clone() for t in base] if i else base), g, None) for i in range(copies)]
+            x = torch.randn(m, kk, dtype=torch.float16, device=dev)
+            if "build_s" not in out:
+                ops[0](x)
+                torch.cuda.synchronize()
+                out["build_s"] = round(time.perf_counter() - t0, 1)
+
+            def run():
+                for op in ops:
+                    op(x)
+
+            ms = _time_fn(torch, run, max(3, steps // 4)) / copies
+            io_bytes = weight_bytes + m * kk * 2 + m * n * 2
+            gbs = io_bytes / (ms * 1e-3) / 1e9
+            row = {"shape": name, "m": m, "k": kk, "n": n, "us_per_call": round(ms * 1e3, 2), "gbs": round(gbs, 1),
+                   "hbm_frac": round(gbs / peaks["hbm_gbs"], 3),
+                   "tflops": round(2.0 * m * kk * n / (ms * 1e-3) / 1e12, 2)}
+            mine = [r for r in ours.get("awq", []) if (r["m"], r["k"], r["n"]) == (m, kk, n)]
+            if mine:
+                row["b200_us_per_call"] = mine[0]["us_per_call"]
+                row["b200_speedup"] = round(ms * 1e3 / mine[0]["us_per_call"], 2)
+            rows.append(row)
+            del ops, base
+            torch.cuda.empty_cache()
+        out["awq_cuda_extension"] = rows
+    except Exception as exc:  # reported, not fatal
+        out["awq_cuda_extension"] = {"unavailable": f"{type(exc).__name__}: {exc}"[:300]}
+    try:
+        from light_vllm.runtime.execution.triton_paged_attention import TritonPagedAttentionBackend
+
+        backend = TritonPagedAttentionBackend()
+        scale = 1.0 / math.sqrt(CFG["d"])
+        backend.create(cache, md).forward("layer0", q, k, v, scale=scale)  # Triton JIT compile
+        torch.cuda.synchronize()
+        # Device time of the write + attention kernels: one context's forward
+        # captured and replayed (as our step graph); and the public API per
+        # step (create + forward), as our e2e without the host copies.
+        step_ctx = backend.create(cache, md)
+        ms_dev = _time_fn(torch, lambda: step_ctx.forward("layer0", q, k, v, scale=scale), steps)
+
+        def api_step():
+            backend.create(cache, md).forward("layer0", q, k, v, scale=scale)
+
+        stream = torch.cuda.current_stream()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(steps):
+            api_step()
+        end.record(stream)
+        torch.cuda.synchronize()
+        ms_api = start.elapsed_time(end) / steps
+        nbytes = algorithmic_bytes(ctx)["step"]
+        out["attention_triton_config2"] = {
+            "ms_per_step_device": round(ms_dev, 4), "gbs_device": round(nbytes / (ms_dev * 1e-3) / 1e9, 1),
+            "ms_per_step_api": round(ms_api, 4), "gbs_api": round(nbytes / (ms_api * 1e-3) / 1e9, 1),
+            "b200_ms_per_step_device": ours.get("ms_per_step"),
+            "b200_speedup_device": round(ms_dev / ours["ms_per_step"], 2) if ours.get("ms_per_step") else None}
+    except Exception as exc:
+        out["attention_triton_config2"] = {"unavailable": f"{type(exc).__name__}: {exc}"[:300]}
+    return out
+
+
+# ----------------------------------------------------------------------------
 # CPU baseline (the oracle restating the reference's Torch path)
 # ----------------------------------------------------------------------------
 def cpu_baseline(torch, cache, md, q, k, v, ctx, budget_s: float = 20.0) -> dict:
@@ -319,6 +433,93 @@ QWEN2_7B = dict(vocab_size=152064, hidden_size=3584, intermediate_size=18944, nu
 # Intermediate 29696 = 29568 padded to 232 groups of 128 so that every TP shard is group-aligned.
 QWEN2_72B = dict(vocab_size=152064, hidden_size=8192, intermediate_size=29696, num_hidden_layers=80,
                  num_attention_heads=64, num_key_value_heads=8, rms_norm_eps=1e-6, rope_theta=1e6)
+# Intermediate 13824 (108 groups); at TP = 8 it is padded to 14336 so every shard is group-aligned.
+QWEN2_14B = dict(vocab_size=152064, hidden_size=5120, intermediate_size=13824, num_hidden_layers=48,
+                 num_attention_heads=40, num_key_value_heads=8, rms_norm_eps=1e-6, rope_theta=1e6)
+
+
+def mixed_step_case(torch, shape, rank: int, world: int, device, steps: int, dist) -> dict:
+    """one step of a 2048-token prefill chunk (fresh
+    prompt) packed with 64 decode requests (contexts U[256, 8192]) through
+    the runner's eager forward and ``B200PagedAttentionBackend`` (the
+    reference's step-handler path: token-major batch, one create per step);
+    the same step repeated, CUDA events, max over ranks.  Prefill GEMMs at
+    M = 2112 run on tcgen05; attention runs the tile kernel for the chunk
+    and the split decode kernel for the 64 decodes."""
+
+    import gc
+
+    from light_vllm_b200 import B200PagedAttentionBackend
+    from light_vllm_b200.qwen2 import Qwen2AWQRunner, random_shard
+    from oracle.paged_cache import model_spec
+
+    T = cache_types()
+    gc.collect()
+    torch.cuda.empty_cache()
+    chunk, n_dec = 2048, 64
+    gen = torch.Generator().manual_seed(2026)
+    ctx = torch.randint(256, 8193, (n_dec,), generator=gen).tolist()
+    weights = random_shard(shape, rank, world, device, seed=11)
+    runner = Qwen2AWQRunner(shape, weights, device, rank=rank, world=world, max_tokens=chunk + n_dec)
+    del weights
+    torch.cuda.empty_cache()
+    try:
+        lengths = [chunk] + [1] * n_dec
+        computed = [0] + [c - 1 for c in ctx]
+        need = [-(-(c + n) // 16) for c, n in zip(computed, lengths)]
+        cache = T.PagedKVCache(model_spec(T, runner.kv_layers()),
+                               T.PagedKVCacheConfig(sum(need), 16, dtype=torch.float16, device=device))
+        for layer_id, *_ in runner.kv_layers():
+            cache.layer(layer_id).keys.zero_()
+            cache.layer(layer_id).values.zero_()
+        tables, off = [], 0
+        for n in need:
+            tables.append(tuple(range(off, off + n)))
+            off += n
+        md = T.PagedAttentionMetadata(block_tables=tuple(tables), num_computed_tokens=tuple(computed),
+                                      query_layouts=tuple(T.linear_query_layout(n) for n in lengths))
+        ids = torch.randint(0, shape.vocab_size, (chunk + n_dec,), device=device)
+        positions = torch.tensor([i for i in range(chunk)] + [c - 1 for c in ctx], dtype=torch.int32, device=device)
+        rows = torch.tensor([chunk - 1] + [chunk + i for i in range(n_dec)], device=device)
+        backend = B200PagedAttentionBackend()
+
+        def step():
+            return runner.forward(ids, positions, backend.create(cache, md), rows)
+
+        for _ in range(2):
+            step()
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+        stream = torch.cuda.current_stream()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record(stream)
+        for _ in range(steps):
+            step()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        ms = ev0.elapsed_time(ev1) / steps
+        if dist is not None:
+            t = torch.tensor([ms], device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        lay = runner.layout
+        h, d = shape.hidden_size, shape.head_size
+        qkv_n = (lay.q_heads + 2 * lay.kv_heads) * d
+        inter = lay.inter_part.local_size
+        m = chunk + n_dec
+        gemm_flops = 2.0 * m * shape.num_hidden_layers * (h * qkv_n + lay.q_heads * d * h + h * 2 * inter + inter * h)
+        attn_flops = 4.0 * shape.num_hidden_layers * lay.q_heads * d * (chunk * (chunk + 1) / 2 + sum(ctx))
+        return {"tp": world, "prefill_tokens": chunk, "decodes": n_dec, "decode_ctx": "U[256, 8192]",
+                "ms_per_step": round(ms, 3), "tok_s": round(m / ms * 1e3, 1),
+                "gemm_tflop_per_step_per_rank": round(gemm_flops / 1e12, 3),
+                "attention_tflop_per_step_per_rank": round(attn_flops / 1e12, 3),
+                "tflops_per_rank": round((gemm_flops + attn_flops) / (ms * 1e-3) / 1e12, 1),
+                "intermediate": shape.intermediate_size, "kv": "fp16 pages, zero-filled (timing only)",
+                "timing": "eager runner.forward over backend.create(cache, metadata), CUDA events, max over ranks"}
+    finally:
+        torch.cuda.synchronize()
+        runner.close()
 
 
 def decode_case(torch, shape, rank: int, world: int, device, batches, ctx: int, steps: int, warmup: int,
@@ -462,14 +663,14 @@ def decode_detail(torch, device, rank: int, world: int, dist, steps: int, warmup
     shape3 = Qwen2Shape(**QWEN2_7B)
     why = tp_layout_error(shape3)
     if why is None:
-        cfg3 = decode_case(torch, shape3, rank, world, device, (1, 16, 64), 1024, steps, warmup, dist,
+        cfg3 = decode_case(torch, shape3, rank, world, device, (1, 16, 64, 256), 1024, 128, warmup, dist,
                            random_kv=True)
-        out["config3_qwen2.5_7b_awq"] = {"tp": world, "steps": cfg3, "prompt_tokens": 1024,
-                                         "kv": "fp16 pages N(0,1)",
+        out["config3_qwen2.5_7b_awq"] = {"tp": world, "steps": cfg3, "prompt_tokens": 1024, "decode_steps": 128,
+                                         "kv": "fp16 pages N(0,1) standing in for the 1024-token prompt's K/V",
                                          "allocated_gb_after": round(torch.cuda.memory_allocated(device) / 1e9, 2)}
     else:
         out["config3_qwen2.5_7b_awq"] = {"tp": world, "skipped": f"no TP={world} layout: {why}"}
-    if world > 1:  # BASELINE config 4 is a TP = 2 / 4 / 8 configuration
+    if True:  # BASELINE config 4 (TP = 2 / 4 / 8); TP = 1 fits one B200 (~128 GB) and anchors the scaling curve
         shape4 = Qwen2Shape(**QWEN2_72B)
         why = tp_layout_error(shape4)
         if why is None:
@@ -479,6 +680,10 @@ def decode_detail(torch, device, rank: int, world: int, dist, steps: int, warmup
                                               "intermediate": 29696, "kv": "fp16 pages, zero-filled (timing only)"}
         else:
             out["config4_qwen2.5_72b_awq"] = {"tp": world, "skipped": f"no TP={world} layout: {why}"}
+    shape5 = Qwen2Shape(**dict(QWEN2_14B, intermediate_size=14336 if world == 8 else 13824))
+    why = tp_layout_error(shape5)
+    out["config5_qwen2.5_14b_awq_mixed"] = (mixed_step_case(torch, shape5, rank, world, device, 5, dist)
+                                            if why is None else {"tp": world, "skipped": f"no TP={world} layout: {why}"})
     out.update({
            "timing": "one CUDA graph per batch size: embedding, 4 AWQ projections, RoPE, K/V write, paged "
                      "attention, SiLU-mul, 2 fused all-reduce+add+RMSNorm per layer, lm_head, greedy pick; "
@@ -495,12 +700,14 @@ def main() -> int:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
     ap.add_argument("--no-awq", action="store_true", help="skip the AWQ detail measurements")
-    ap.add_argument("--only", choices=("all", "attention", "awq", "decode"), default="all",
+    ap.add_argument("--only", choices=("all", "attention", "awq", "decode", "mixed"), default="all",
                     help="run one part (profiling); 'awq' prints only the AWQ detail")
     ap.add_argument("--awq-shapes", default=None,
                     help="AWQ detail shapes as 'm,k,n[;m,k,n...]' (group 128)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline (profiling)")
     ap.add_argument("--no-decode", action="store_true", help="skip the Qwen2 decode-step detail")
+    ap.add_argument("--no-reference-gpu", action="store_true",
+                    help="skip timing light-vllm's own GPU paths (CUDA AWQ extension, Triton attention)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -532,6 +739,16 @@ def main() -> int:
         detail = decode_detail(torch, device, rank, world, dist, args.steps, args.warmup, with_cpu=not args.no_cpu)
         if rank == 0:
             print(json.dumps({"decode": detail}), flush=True)
+        if dist is not None:
+            dist.destroy_process_group()
+        return 0
+    if args.only == "mixed":  # BASELINE config 5 step alone (profiling the tile kernel)
+        from light_vllm_b200.qwen2 import Qwen2Shape
+
+        shape5 = Qwen2Shape(**dict(QWEN2_14B, intermediate_size=14336 if world == 8 else 13824))
+        detail = mixed_step_case(torch, shape5, rank, world, device, max(1, min(args.steps, 5)), dist)
+        if rank == 0:
+            print(json.dumps({"config5_qwen2.5_14b_awq_mixed": detail}), flush=True)
         if dist is not None:
             dist.destroy_process_group()
         return 0
@@ -652,9 +869,10 @@ def main() -> int:
         if not args.no_cpu:
             result["cpu_baseline"] = cpu_baseline(torch, cache, md, q, k, v, ctx)
         if not args.no_awq and args.only == "all":
-            cache = step_ctx = None
-            torch.cuda.empty_cache()
             result["awq"] = awq_detail(torch, peaks, args.steps, args.awq_shapes)
+        if not args.no_reference_gpu and args.only == "all":
+            result["reference_gpu"] = reference_gpu_detail(torch, peaks, args.steps, cache, md, q, k, v, ctx,
+                                                           {"awq": result.get("awq", []), "ms_per_step": step_ms})
     if args.only == "all" and not args.no_decode:
         cache = step_ctx = step_graph = attn_graph = None
         torch.cuda.empty_cache()

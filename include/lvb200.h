@@ -292,6 +292,13 @@ LVB_API size_t lvb_paged_attention_workspace_bytes(int64_t num_seqs, int64_t num
  * their num_computed in that order, as lvb_pack_step_metadata writes it) is
  * the order in which that path launches them: longest context first shortens
  * the tail of the launch.  The results do not depend on it.
+ * Other batches (prefill chunks, mixed prefill + decode, tree layouts) with
+ * head_size 64 or 128 and 16-token blocks run the tensor-core tile kernel;
+ * when request_order is given, its first num_decode_seqs requests are the
+ * batch's one-token requests (as lvb_pack_step_metadata orders them) and run
+ * the split-context decode path instead (it needs `workspace`), the rest the
+ * tile kernel.  With request_order NULL, num_decode_seqs is ignored.  Head
+ * sizes 32 / 80 / 256 and other block sizes run a scalar kernel.
  * Replaces the Triton attention launches
  * (runtime/execution/triton_paged_attention.py:106-391, 519-559). */
 LVB_API int lvb_paged_attention(const uint16_t *query, int64_t query_token_stride,
@@ -301,7 +308,7 @@ LVB_API int lvb_paged_attention(const uint16_t *query, int64_t query_token_strid
                         const int32_t *query_start_loc, const int32_t *request_indices,
                         const int32_t *request_order,
                         const uint8_t *visibility, const int32_t *visibility_start,
-                        int64_t num_seqs, int64_t num_tokens, int64_t max_query_len,
+                        int64_t num_seqs, int64_t num_decode_seqs, int64_t num_tokens, int64_t max_query_len,
                         int64_t max_seq_len, int64_t num_q_heads, int64_t num_kv_heads,
                         int64_t head_size, int64_t block_size, int64_t num_blocks, float scale,
                         int dtype, void *workspace, size_t workspace_bytes,
@@ -407,6 +414,31 @@ LVB_API int lvb_rope_kv_write(uint16_t *qkv, int64_t row_stride, int64_t tokens,
  * tensors 16-byte aligned. */
 LVB_API int lvb_silu_mul(const uint16_t *gate_up, int64_t in_stride, int64_t tokens, int64_t intermediate,
                          uint16_t *out, int64_t out_stride, lvb_stream_t stream);
+
+/* Greedy pick of the vocabulary head without writing logits: for each of
+ * tokens (1..4) hidden rows, logit[t][v] = fp16(fp32 sum_k hidden[t][k] *
+ * weight[v][k]) over this rank's vocab_rows rows of weight ([vocab_rows]
+ * [hidden_size] fp16, the nn.Linear layout), and out_index[t] = vocab_offset
+ * + the lowest row holding the maximum; out_value[t] (optional) = that
+ * maximum, for the cross-rank pick of a vocab-parallel head.  Replaces the
+ * lm_head F.linear + greedy argmax (modeling/models/qwen2.py:665-673,
+ * runtime/sampling.py:103-112) at decode batch sizes.  workspace:
+ * lvb_lm_head_workspace_bytes() bytes, zero-filled once; every call leaves
+ * it zero.  Calls sharing a workspace must not overlap on the GPU. */
+LVB_API size_t lvb_lm_head_workspace_bytes(void);
+LVB_API int lvb_lm_head_argmax(const uint16_t *hidden, int64_t hidden_stride, int64_t tokens,
+                               const uint16_t *weight, int64_t vocab_rows, int64_t hidden_size,
+                               int64_t vocab_offset, int64_t *out_index, float *out_value, void *workspace,
+                               lvb_stream_t stream);
+
+/* out[t] = table[ids[t] - vocab_start] for vocab_start <= ids[t] < vocab_end,
+ * else zeros (int64 ids; fp16 rows of hidden_size, a multiple of 8).  The
+ * masked lookup of `VocabParallelEmbedding.forward`
+ * (modeling/tensor_parallel.py:296-306); the cross-rank sum is the all-reduce
+ * that follows. */
+LVB_API int lvb_embedding(const int64_t *ids, int64_t tokens, const uint16_t *table, int64_t vocab_start,
+                          int64_t vocab_end, int64_t hidden_size, uint16_t *out, int64_t out_stride,
+                          lvb_stream_t stream);
 
 #ifdef __cplusplus
 } /* extern "C" */

@@ -104,6 +104,11 @@ PROTOTYPES: dict[str, tuple[object, tuple[object, ...]]] = {
         (_c_ptr, _i64, _i64, _i64, _i64, _i64, _c_ptr, _c_ptr, _c_ptr, _i64, _c_ptr),
     ),
     "lvb_silu_mul": (_int, (_c_ptr, _i64, _i64, _i64, _c_ptr, _i64, _c_ptr)),
+    "lvb_lm_head_workspace_bytes": (_size, ()),
+    "lvb_lm_head_argmax": (
+        _int, (_c_ptr, _i64, _i64, _c_ptr, _i64, _i64, _i64, _c_ptr, _c_ptr, _c_ptr, _c_ptr),
+    ),
+    "lvb_embedding": (_int, (_c_ptr, _i64, _c_ptr, _i64, _i64, _i64, _c_ptr, _i64, _c_ptr)),
     "lvb_rope_kv_write": (
         _int,
         (_c_ptr, _i64, _i64, _i64, _i64, _i64, _c_ptr, _c_ptr, _c_ptr, _i64, _c_ptr, _c_ptr, _c_ptr, _i64, _c_ptr,
@@ -112,7 +117,7 @@ PROTOTYPES: dict[str, tuple[object, tuple[object, ...]]] = {
     "lvb_paged_attention": (
         _int,
         (_c_ptr, _i64, _c_ptr, _c_ptr, _c_ptr, _i64, _c_ptr, _i64, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr,
-         _c_ptr, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _int, _c_ptr, _size,
+         _c_ptr, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _int, _c_ptr, _size,
          _c_ptr),
     ),
 }

@@ -19,7 +19,8 @@
  *           rows[4 n]         int32: computed | query lengths | reserved |
  *                             readonly prefix blocks
  *   returns (total_ids, max_blocks, num_tokens, max_query_len, max_seq_len,
- *            linear), linear = every layout is the causal chain
+ *            linear, num_single), linear = every layout is the causal chain,
+ *            num_single = requests with one query token
  *            (-1, 0, 1, ..., len - 2).
  * Counts that do not fit int32 raise OverflowError; ids_capacity too small
  * raises ValueError.  The caller owns the buffers (sizes n + 1, 4 n and
@@ -118,7 +119,7 @@ static PyObject *gather_step(PyObject *self, PyObject *args) {
   PyObject **trows = PySequence_Fast_ITEMS(tfast);
   PyObject *lfast = NULL;
   Py_ssize_t total = 0, max_blocks = 0;
-  long long num_tokens = 0, max_query = 0, max_seq = 0;
+  long long num_tokens = 0, max_query = 0, max_seq = 0, single = 0;
   int linear = 1;
 
   offsets[0] = 0;
@@ -164,6 +165,7 @@ static PyObject *gather_step(PyObject *self, PyObject *args) {
     }
     qlen[r] = (int32_t)len;
     num_tokens += len;
+    single += len == 1;
     if (len > max_query) max_query = len;
     if ((long long)comp[r] + len > max_seq) max_seq = (long long)comp[r] + len;
     if (linear) {
@@ -174,8 +176,8 @@ static PyObject *gather_step(PyObject *self, PyObject *args) {
   }
   Py_DECREF(lfast);
   Py_DECREF(tfast);
-  return Py_BuildValue("(nnLLLO)", total, max_blocks, num_tokens, max_query, max_seq,
-                       linear ? Py_True : Py_False);
+  return Py_BuildValue("(nnLLLOL)", total, max_blocks, num_tokens, max_query, max_seq,
+                       linear ? Py_True : Py_False, single);
 
 fail:
   Py_XDECREF(lfast);
@@ -186,7 +188,8 @@ fail:
 static PyMethodDef methods[] = {
     {"gather_step", gather_step, METH_VARARGS,
      "gather_step(tables, computed, layouts, reserved, readonly, ids_addr, ids_capacity, offsets_addr, "
-     "rows_addr) -> (total_ids, max_blocks, num_tokens, max_query_len, max_seq_len, linear)"},
+     "rows_addr) -> (total_ids, max_blocks, num_tokens, max_query_len, max_seq_len, linear, "
+     "num_single)"},
     {NULL, NULL, 0, NULL},
 };
 

@@ -603,6 +603,27 @@ bool decode_eligible(const uint8_t *vis, int64_t max_query_len, int64_t num_seqs
          (d == 64 || d == 128) && hq % hkv == 0 && hq / hkv <= 16;
 }
 
+bool decode_shape_ok(int64_t hq, int64_t hkv, int64_t d, int64_t bs) {
+  return bs == lvb::attn::kPageTokens && (d == 64 || d == 128) && hq % hkv == 0 && hq / hkv <= 16;
+}
+
+// Tensor-core tile kernel: head sizes 64 / 128, 16-token blocks, any GQA group.
+bool tile_eligible(int64_t hq, int64_t hkv, int64_t d, int64_t bs) {
+  return bs == lvb::attn::kPageTokens && (d == 64 || d == 128) && hq % hkv == 0;
+}
+
+template <bool kBf16, int D>
+int launch_prefill(const lvb::attn::AttnArgs &a, dim3 grid, int dev, cudaStream_t stream) {
+  using Cfg = lvb::attn::PrefillCfg<D>;
+  static bool smem_done[kMaxDevices] = {false};
+  auto kernel = lvb::attn::paged_prefill_kernel<kBf16, D>;
+  int rc = ensure_smem(kernel, Cfg::kSmemBytes, dev, smem_done);
+  if (rc != LVB_OK) return rc;
+  cudaError_t e = launch_pdl(kernel, grid, dim3(128), Cfg::kSmemBytes, stream, a);
+  if (e != cudaSuccess) return cuda_fail(e, "paged_prefill_kernel launch");
+  return LVB_OK;
+}
+
 template <bool kBf16, int D, int HPC, int KW = 1>
 int launch_decode(const lvb::attn::AttnArgs &a, int64_t num_seqs, int64_t num_blocks, int dev,
                   cudaStream_t stream) {
@@ -1062,7 +1083,7 @@ int lvb_paged_attention(const uint16_t *query, int64_t query_token_stride,
                         const int32_t *query_start_loc, const int32_t *request_indices,
                         const int32_t *request_order,
                         const uint8_t *visibility, const int32_t *visibility_start,
-                        int64_t num_seqs, int64_t num_tokens, int64_t max_query_len,
+                        int64_t num_seqs, int64_t num_decode_seqs, int64_t num_tokens, int64_t max_query_len,
                         int64_t max_seq_len, int64_t num_q_heads, int64_t num_kv_heads,
                         int64_t head_size, int64_t block_size, int64_t num_blocks, float scale,
                         int dtype, void *workspace, size_t workspace_bytes,
@@ -1112,8 +1133,18 @@ int lvb_paged_attention(const uint16_t *query, int64_t query_token_stride,
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const bool bf16 = dtype == LVB_DTYPE_BF16;
 
-  if (decode_eligible(visibility, max_query_len, num_seqs, num_tokens, num_q_heads, num_kv_heads, head_size,
-                      block_size)) {
+  const bool all_decode = decode_eligible(visibility, max_query_len, num_seqs, num_tokens, num_q_heads,
+                                         num_kv_heads, head_size, block_size);
+  const bool tiles = tile_eligible(num_q_heads, num_kv_heads, head_size, block_size);
+  // One-token requests of a mixed batch: listed first in request_order.
+  int64_t n_decode = all_decode ? num_seqs : 0;
+  if (!all_decode && tiles && request_order != nullptr && decode_shape_ok(num_q_heads, num_kv_heads, head_size, block_size)) {
+    if (num_decode_seqs < 0 || num_decode_seqs > num_seqs)
+      return fail(LVB_ERR_INVALID, "num_decode_seqs %lld outside [0, %lld]", (long long)num_decode_seqs,
+                  (long long)num_seqs);
+    n_decode = num_decode_seqs;
+  }
+  if (n_decode > 0) {
     const DecodePlan plan = decode_plan(num_seqs, num_q_heads, num_kv_heads, head_size, max_seq_len, sm_count(dev));
     if (workspace == nullptr || workspace_bytes < plan.total() || !aligned16(workspace))
       return fail(LVB_ERR_WORKSPACE, "paged attention workspace of %zu bytes is below the %zu required",
@@ -1124,13 +1155,25 @@ int lvb_paged_attention(const uint16_t *query, int64_t query_token_stride,
     a.max_splits = plan.max_splits;
     a.chunk_tokens = plan.chunk_tokens;
     if (bf16) {
-      return head_size == 128
-                 ? launch_decode_any<true, 128>(a, plan.heads_per_cta, plan.warps_per_head, num_seqs, num_blocks, dev, s)
-                 : launch_decode_any<true, 64>(a, plan.heads_per_cta, plan.warps_per_head, num_seqs, num_blocks, dev, s);
+      rc = head_size == 128
+               ? launch_decode_any<true, 128>(a, plan.heads_per_cta, plan.warps_per_head, n_decode, num_blocks, dev, s)
+               : launch_decode_any<true, 64>(a, plan.heads_per_cta, plan.warps_per_head, n_decode, num_blocks, dev, s);
+    } else {
+      rc = head_size == 128
+               ? launch_decode_any<false, 128>(a, plan.heads_per_cta, plan.warps_per_head, n_decode, num_blocks, dev, s)
+               : launch_decode_any<false, 64>(a, plan.heads_per_cta, plan.warps_per_head, n_decode, num_blocks, dev, s);
     }
-    return head_size == 128
-               ? launch_decode_any<false, 128>(a, plan.heads_per_cta, plan.warps_per_head, num_seqs, num_blocks, dev, s)
-               : launch_decode_any<false, 64>(a, plan.heads_per_cta, plan.warps_per_head, num_seqs, num_blocks, dev, s);
+    if (rc != LVB_OK || all_decode) return rc;
+  }
+  if (tiles) {
+    const int64_t tile_reqs = request_order != nullptr ? num_seqs - n_decode : num_seqs;
+    if (tile_reqs == 0) return LVB_OK;
+    a.first_tile_req = static_cast<int>(request_order != nullptr ? n_decode : 0);
+    const int64_t row_tiles = (max_query_len * (num_q_heads / num_kv_heads) + 63) / 64;
+    if (row_tiles > INT_MAX || tile_reqs > 65535) return fail(LVB_ERR_UNSUPPORTED, "prefill tile grid exceeds launch limits");
+    const dim3 grid(static_cast<unsigned>(row_tiles), static_cast<unsigned>(tile_reqs), static_cast<unsigned>(num_kv_heads));
+    if (bf16) return head_size == 128 ? launch_prefill<true, 128>(a, grid, dev, s) : launch_prefill<true, 64>(a, grid, dev, s);
+    return head_size == 128 ? launch_prefill<false, 128>(a, grid, dev, s) : launch_prefill<false, 64>(a, grid, dev, s);
   }
   return bf16 ? launch_general<true>(a, num_tokens, s) : launch_general<false>(a, num_tokens, s);
 }
@@ -1222,10 +1265,15 @@ int lvb_pack_step_metadata(const int32_t *block_ids, const int64_t *table_offset
     for (int32_t i = 0; i < query_lengths[r]; ++i) req[t++] = static_cast<int32_t>(r);
     order[r] = static_cast<int32_t>(r);
   }
-  // Launch order for the decode kernel: longest context first, ties by index;
-  // then the listed requests' computed counts.
-  std::stable_sort(order, order + num_seqs,
-                   [num_computed](int32_t x, int32_t y) { return num_computed[x] > num_computed[y]; });
+  // Launch order: the one-token (decode) requests first, longest context
+  // first, for the split decode kernel; then the others, longest context
+  // first, for the prefill tile kernel; ties by index.  Then the listed
+  // requests' computed counts.
+  std::stable_sort(order, order + num_seqs, [num_computed, query_lengths](int32_t x, int32_t y) {
+    const bool dx = query_lengths[x] == 1, dy = query_lengths[y] == 1;
+    if (dx != dy) return dx;
+    return num_computed[x] + query_lengths[x] > num_computed[y] + query_lengths[y];
+  });
   for (int64_t r = 0; r < num_seqs; ++r) order[num_seqs + r] = num_computed[order[r]];
   *table_stride_out = max_blocks;
   *num_tokens_out = num_tokens;
@@ -1549,6 +1597,82 @@ int lvb_rope_kv_write(uint16_t *qkv, int64_t row_stride, int64_t tokens, int64_t
   cudaError_t e = launch_pdl(lvb::q2::rope_kv_write_kernel, dim3(static_cast<unsigned>(tokens)),
                              dim3(lvb::q2::kRopeThreads), 0, reinterpret_cast<cudaStream_t>(stream), a);
   return e == cudaSuccess ? LVB_OK : cuda_fail(e, "rope_kv_write_kernel launch");
+}
+
+size_t lvb_lm_head_workspace_bytes(void) { return 256; }
+
+int lvb_lm_head_argmax(const uint16_t *hidden, int64_t hidden_stride, int64_t tokens, const uint16_t *weight,
+                       int64_t vocab_rows, int64_t hidden_size, int64_t vocab_offset, int64_t *out_index,
+                       float *out_value, void *workspace, lvb_stream_t stream) {
+  if (tokens < 1 || tokens > lvb::q2::kHeadMaxTokens)
+    return fail(LVB_ERR_UNSUPPORTED, "lm_head argmax covers 1..%d tokens, got %lld", lvb::q2::kHeadMaxTokens,
+                (long long)tokens);
+  if (vocab_rows <= 0 || vocab_rows > INT_MAX || hidden_size <= 0 || hidden_size % 8 || hidden_size > 16384 ||
+      hidden_stride < hidden_size || hidden_stride % 8)
+    return fail(LVB_ERR_INVALID, "lm_head argmax: invalid shape (hidden size a multiple of 8 up to 16384)");
+  if (!hidden || !weight || !out_index || !workspace || !aligned16(hidden) || !aligned16(weight) ||
+      !aligned16(workspace))
+    return fail(LVB_ERR_INVALID, "lm_head argmax: tensors must be non-null and 16-byte aligned");
+  int dev = 0;
+  int rc = current_device(&dev);
+  if (rc != LVB_OK) return rc;
+  lvb::q2::HeadArgs a{};
+  a.hidden = hidden;
+  a.hidden_stride = hidden_stride;
+  a.weight = weight;
+  a.tokens = static_cast<int>(tokens);
+  a.H = static_cast<int>(hidden_size);
+  a.V = static_cast<int>(vocab_rows);
+  a.vocab_offset = vocab_offset;
+  a.keys = static_cast<unsigned long long *>(workspace);
+  a.counter = reinterpret_cast<unsigned int *>(static_cast<uint8_t *>(workspace) + 8 * lvb::q2::kHeadMaxTokens);
+  a.out_index = out_index;
+  a.out_value = out_value;
+  const int tok = tokens <= 1 ? 1 : tokens <= 2 ? 2 : 4;
+  const size_t smem = static_cast<size_t>(tok) * hidden_size * 4;
+  // Up to four CTAs per SM, as many as the fp32 hidden rows let fit.
+  int per_sm = static_cast<int>((200 * 1024) / (smem + 4096));
+  if (per_sm > 4) per_sm = 4;
+  if (per_sm < 1) per_sm = 1;
+  const int64_t rows_per_cta = lvb::q2::kHeadThreads / 32;
+  int64_t ctas = static_cast<int64_t>(sm_count(dev)) * per_sm;
+  if (ctas > (vocab_rows + rows_per_cta - 1) / rows_per_cta) ctas = (vocab_rows + rows_per_cta - 1) / rows_per_cta;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  cudaError_t e;
+  if (tok == 1) {
+    static bool done[kMaxDevices] = {false};
+    rc = ensure_smem(lvb::q2::lm_head_argmax_kernel<1>, static_cast<int>(smem), dev, done);
+    if (rc != LVB_OK) return rc;
+    e = launch_pdl(lvb::q2::lm_head_argmax_kernel<1>, dim3(static_cast<unsigned>(ctas)), dim3(lvb::q2::kHeadThreads),
+                   smem, st, a);
+  } else if (tok == 2) {
+    static bool done[kMaxDevices] = {false};
+    rc = ensure_smem(lvb::q2::lm_head_argmax_kernel<2>, static_cast<int>(smem), dev, done);
+    if (rc != LVB_OK) return rc;
+    e = launch_pdl(lvb::q2::lm_head_argmax_kernel<2>, dim3(static_cast<unsigned>(ctas)), dim3(lvb::q2::kHeadThreads),
+                   smem, st, a);
+  } else {
+    static bool done[kMaxDevices] = {false};
+    rc = ensure_smem(lvb::q2::lm_head_argmax_kernel<4>, static_cast<int>(smem), dev, done);
+    if (rc != LVB_OK) return rc;
+    e = launch_pdl(lvb::q2::lm_head_argmax_kernel<4>, dim3(static_cast<unsigned>(ctas)), dim3(lvb::q2::kHeadThreads),
+                   smem, st, a);
+  }
+  return e == cudaSuccess ? LVB_OK : cuda_fail(e, "lm_head_argmax_kernel launch");
+}
+
+int lvb_embedding(const int64_t *ids, int64_t tokens, const uint16_t *table, int64_t vocab_start, int64_t vocab_end,
+                  int64_t hidden_size, uint16_t *out, int64_t out_stride, lvb_stream_t stream) {
+  if (tokens < 0 || tokens > INT_MAX || hidden_size <= 0 || hidden_size % 8 || out_stride < hidden_size ||
+      out_stride % 8 || vocab_end < vocab_start)
+    return fail(LVB_ERR_INVALID, "embedding: invalid shape (hidden size and row stride multiples of 8)");
+  if (tokens == 0) return LVB_OK;
+  if (!ids || !table || !out || !aligned16(table) || !aligned16(out))
+    return fail(LVB_ERR_INVALID, "embedding: tensors must be non-null and 16-byte aligned");
+  cudaError_t e = launch_pdl(lvb::q2::embedding_kernel, dim3(static_cast<unsigned>(tokens)), dim3(128), 0,
+                             reinterpret_cast<cudaStream_t>(stream), ids, table, vocab_start, vocab_end,
+                             static_cast<int>(hidden_size), out, out_stride);
+  return e == cudaSuccess ? LVB_OK : cuda_fail(e, "embedding_kernel launch");
 }
 
 int lvb_silu_mul(const uint16_t *gate_up, int64_t in_stride, int64_t tokens, int64_t intermediate, uint16_t *out,

@@ -105,6 +105,10 @@ struct AttnArgs {
   int max_splits;
   int chunk_tokens;  // multiple of 16
   int num_seqs;
+  // prefill tile kernel: requests order[first_tile_req + blockIdx.y] (the
+  // packer lists one-token requests first; the decode kernel serves those), or
+  // blockIdx.y itself when order is null
+  int first_tile_req;
 };
 
 __device__ __forceinline__ float warp_max(float v) {
@@ -246,6 +250,248 @@ __global__ void __launch_bounds__(128) paged_attn_general_kernel(const AttnArgs 
 #pragma unroll
     for (int w = 0; w < kWarps; ++w) o += wgt[w] * o_sm[w][d];
     a.out[t * a.o_stride + static_cast<int64_t>(h) * D + d] = from_float<kBf16>(o * inv);
+  }
+}
+
+// ------------------------------------------------------------------------
+// Prefill / mixed / tree attention on warp MMAs
+// ------------------------------------------------------------------------
+// One CTA per (64-row tile, request, KV head).  The rows of a request and KV
+// head are its (query token, query head of the GQA group) pairs, token-major:
+// row R is token R / G, head R % G.  Four warps take 16 rows each, so one CTA
+// covers the whole group for ~64 / G consecutive tokens and every K/V
+// position it needs is staged once in shared memory for all of them (the
+// reference's grouped Triton kernel shares pages across the group the same
+// way, runtime/execution/triton_paged_attention.py:248-391).  K/V stream in
+// tiles of 32 positions (two 16-token pages) through a 3-stage cp.async ring,
+// 128-byte-swizzled rows that ldmatrix reads without bank conflicts; S = Q K^T
+// and O += P V are m16n8k16 warp MMAs with an fp32 online softmax per row.  P
+// enters P V in the cache dtype, as a hi + lo pair for bf16 (as in the decode
+// kernel).  Visibility: the computed prefix always; inside the query block
+// the causal chain, or the request's visibility matrix (tree layouts).
+// Positions past a tile's last visible one are not read (zero-filled), so
+// never-written cache slots (possibly NaN) never enter P V.
+template <int D>
+struct PrefillCfg {
+  static constexpr int kWarps = 4;
+  static constexpr int kRows = 16 * kWarps;
+  static constexpr int kTilePos = 32;                     // K/V positions per stage
+  static constexpr int kStages = 3;
+  static constexpr int kHalfBytes = kTilePos * 128;       // one 64-dim half of a K or V tile
+  static constexpr int kKVBytes = (D / 64) * kHalfBytes;  // a K (or V) tile
+  static constexpr int kStageBytes = 2 * kKVBytes;        // K then V
+  static constexpr int kSmemBytes = kStages * kStageBytes + 1024;
+  static constexpr int kChunks = kTilePos * (D / 8);      // 16-byte chunks of a K (or V) tile
+};
+
+template <bool kBf16, int D>
+__global__ void __launch_bounds__(128) paged_prefill_kernel(const AttnArgs a) {
+  pdl_entry();
+  using Cfg = PrefillCfg<D>;
+  constexpr int kSteps = D / 16;  // k-steps of QK^T, dim pairs of PV
+  constexpr int kNTiles = D / 8;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const uint32_t ring = smem_u32(smem);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int seq = a.order != nullptr ? a.order[a.first_tile_req + blockIdx.y] : static_cast<int>(blockIdx.y);
+  const int kvh = blockIdx.z;
+  const int G = a.Hq / a.Hkv;
+  const int qs = a.qsl[seq];
+  const int qlen = a.qsl[seq + 1] - qs;
+  const int row0 = blockIdx.x * Cfg::kRows;
+  if (row0 >= qlen * G) return;  // uniform for the CTA
+  const int c = a.computed[seq];
+  const bool tree = a.vis != nullptr;
+  const uint8_t *vis = tree ? a.vis + a.vis_start[seq] : nullptr;
+  // Last query token of the tile, and the K/V range the tile reads.
+  const int last_tok = min(qlen * G, row0 + Cfg::kRows) - 1;
+  const int kv_end = c + (tree ? qlen : last_tok / G + 1);
+  const int ntiles = (kv_end + Cfg::kTilePos - 1) / Cfg::kTilePos;
+  const int32_t *table = a.tables + static_cast<int64_t>(seq) * a.table_stride;
+  const int64_t row_elems = static_cast<int64_t>(a.Hkv) * D;
+  const int64_t head_off = static_cast<int64_t>(kvh) * D;
+
+  // Stage loader: thread i copies 16-byte chunks i, i + 128, ... of the K and
+  // V tiles; positions at or past kv_end are zero-filled.
+  auto load_stage = [&](int tile, int slot) {
+    const uint32_t kdst = ring + slot * Cfg::kStageBytes;
+    const uint32_t vdst = kdst + Cfg::kKVBytes;
+#pragma unroll
+    for (int u = 0; u < Cfg::kChunks / 128; ++u) {
+      const int q = threadIdx.x + 128 * u;
+      const int tok = q / (D / 8);
+      const int c16 = q - tok * (D / 8);
+      const int pos = tile * Cfg::kTilePos + tok;
+      const uint32_t off = (c16 >> 3) * Cfg::kHalfBytes + tok * 128 + (((c16 & 7) ^ (tok & 7)) << 4);
+      const bool ok = pos < kv_end;
+      int64_t src = head_off;
+      if (ok) {
+        const int64_t block = table[pos >> 4];  // 16-token pages
+        src = (block * 16 + (pos & 15)) * row_elems + head_off + c16 * 8;
+      }
+      cp_async_16(kdst + off, a.kc + src, ok ? 16u : 0u);
+      cp_async_16(vdst + off, a.vc + src, ok ? 16u : 0u);
+    }
+  };
+#pragma unroll
+  for (int s = 0; s < Cfg::kStages - 1; ++s) {
+    if (s < ntiles) load_stage(s, s);
+    cp_async_commit();
+  }
+
+  // This warp's rows g and g + 8 of the MMA tile.
+  const int g = lane >> 2;
+  const int cq = lane & 3;
+  int tok_r[2], head_r[2];
+  bool row_ok[2];
+#pragma unroll
+  for (int hr = 0; hr < 2; ++hr) {
+    const int R = row0 + warp * 16 + g + 8 * hr;
+    row_ok[hr] = R < qlen * G;
+    tok_r[hr] = row_ok[hr] ? R / G : 0;
+    head_r[hr] = row_ok[hr] ? R - (R / G) * G : 0;
+  }
+  uint32_t qa[kSteps][4];
+  {
+    const uint16_t *q0 = a.q + static_cast<int64_t>(qs + tok_r[0]) * a.q_stride +
+                         static_cast<int64_t>(kvh * G + head_r[0]) * D;
+    const uint16_t *q1 = a.q + static_cast<int64_t>(qs + tok_r[1]) * a.q_stride +
+                         static_cast<int64_t>(kvh * G + head_r[1]) * D;
+#pragma unroll
+    for (int ks = 0; ks < kSteps; ++ks) {
+      const int d0 = ks * 16 + 2 * cq;
+      qa[ks][0] = row_ok[0] ? *reinterpret_cast<const uint32_t *>(q0 + d0) : 0u;
+      qa[ks][1] = row_ok[1] ? *reinterpret_cast<const uint32_t *>(q1 + d0) : 0u;
+      qa[ks][2] = row_ok[0] ? *reinterpret_cast<const uint32_t *>(q0 + d0 + 8) : 0u;
+      qa[ks][3] = row_ok[1] ? *reinterpret_cast<const uint32_t *>(q1 + d0 + 8) : 0u;
+    }
+  }
+  float o[kNTiles][4];
+#pragma unroll
+  for (int i = 0; i < kNTiles; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float m_run[2] = {-INFINITY, -INFINITY};
+  float l_run[2] = {0.f, 0.f};
+  const int mi = lane >> 3;
+  const int rr = lane & 7;
+
+  for (int it = 0; it < ntiles; ++it) {
+    cp_async_wait_group<Cfg::kStages - 2>();
+    __syncthreads();  // stage `it` landed for every thread; the slot of it - 1 is free
+    if (it + Cfg::kStages - 1 < ntiles) load_stage(it + Cfg::kStages - 1, (it + Cfg::kStages - 1) % Cfg::kStages);
+    cp_async_commit();
+    const uint32_t kbase = ring + (it % Cfg::kStages) * Cfg::kStageBytes;
+    const uint32_t vbase = kbase + Cfg::kKVBytes;
+
+    // S = Q K^T over the stage's 32 positions (four 8-position MMA tiles).
+    float sc[4][4];
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+#pragma unroll
+    for (int ks = 0; ks < kSteps; ++ks) {
+#pragma unroll
+      for (int pp = 0; pp < 2; ++pp) {
+        const int tok = pp * 16 + (mi >> 1) * 8 + rr;
+        const int chunk = (ks & 3) * 2 + (mi & 1);
+        const uint32_t addr = kbase + (ks >> 2) * Cfg::kHalfBytes + tok * 128 + ((chunk ^ (tok & 7)) << 4);
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(addr, b0, b1, b2, b3);
+        mma_16816<kBf16>(sc[2 * pp], qa[ks], b0, b1);
+        mma_16816<kBf16>(sc[2 * pp + 1], qa[ks], b2, b3);
+      }
+    }
+    // Visibility and the online softmax (rows g, g + 8).
+    const int pos0 = it * Cfg::kTilePos + 2 * cq;
+    float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int hr = e >> 1;
+        const int pos = pos0 + nt * 8 + (e & 1);
+        bool visible = row_ok[hr] && pos < kv_end;
+        if (visible && pos >= c) {
+          const int j = pos - c;
+          visible = tree ? (j < qlen && vis[static_cast<int64_t>(tok_r[hr]) * qlen + j] != 0) : j <= tok_r[hr];
+        }
+        const float v = visible ? sc[nt][e] * a.scale_log2 : -INFINITY;
+        sc[nt][e] = v;
+        mx[hr] = fmaxf(mx[hr], v);
+      }
+    }
+    float alpha[2], m_use[2];
+#pragma unroll
+    for (int hr = 0; hr < 2; ++hr) {
+      mx[hr] = fmaxf(mx[hr], __shfl_xor_sync(0xffffffffu, mx[hr], 1));
+      mx[hr] = fmaxf(mx[hr], __shfl_xor_sync(0xffffffffu, mx[hr], 2));
+      const float m_new = fmaxf(m_run[hr], mx[hr]);
+      m_use[hr] = m_new == -INFINITY ? 0.f : m_new;  // a row with nothing visible yet
+      alpha[hr] = exp2f(m_run[hr] - m_use[hr]);
+      m_run[hr] = m_new;
+      l_run[hr] *= alpha[hr];
+    }
+#pragma unroll
+    for (int n = 0; n < kNTiles; ++n) {
+      o[n][0] *= alpha[0];
+      o[n][1] *= alpha[0];
+      o[n][2] *= alpha[1];
+      o[n][3] *= alpha[1];
+    }
+    // O += P V, two 16-position k-steps.
+#pragma unroll
+    for (int kp = 0; kp < 2; ++kp) {
+      uint32_t pa_hi[4], pa_lo[4];
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const int nt = 2 * kp + half;
+#pragma unroll
+        for (int hr = 0; hr < 2; ++hr) {
+          const float p0 = exp2f(sc[nt][2 * hr] - m_use[hr]);
+          const float p1 = exp2f(sc[nt][2 * hr + 1] - m_use[hr]);
+          l_run[hr] += p0 + p1;
+          const uint32_t hi = pack2<kBf16>(p0, p1);
+          pa_hi[half * 2 + hr] = hi;
+          if constexpr (kBf16) {
+            const float h0 = __uint_as_float(hi << 16);
+            const float h1 = __uint_as_float(hi & 0xFFFF0000u);
+            pa_lo[half * 2 + hr] = pack2<kBf16>(p0 - h0, p1 - h1);
+          }
+        }
+      }
+#pragma unroll
+      for (int dp = 0; dp < kSteps; ++dp) {
+        const int tok = kp * 16 + (mi & 1) * 8 + rr;
+        const int chunk = (dp & 3) * 2 + (mi >> 1);
+        const uint32_t addr = vbase + (dp >> 2) * Cfg::kHalfBytes + tok * 128 + ((chunk ^ (tok & 7)) << 4);
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4_trans(addr, b0, b1, b2, b3);
+        mma_16816<kBf16>(o[2 * dp], pa_hi, b0, b1);
+        mma_16816<kBf16>(o[2 * dp + 1], pa_hi, b2, b3);
+        if constexpr (kBf16) {
+          mma_16816<kBf16>(o[2 * dp], pa_lo, b0, b1);
+          mma_16816<kBf16>(o[2 * dp + 1], pa_lo, b2, b3);
+        }
+      }
+    }
+  }
+  cp_async_wait_all();
+
+#pragma unroll
+  for (int hr = 0; hr < 2; ++hr) {
+    l_run[hr] += __shfl_xor_sync(0xffffffffu, l_run[hr], 1);
+    l_run[hr] += __shfl_xor_sync(0xffffffffu, l_run[hr], 2);
+  }
+#pragma unroll
+  for (int hr = 0; hr < 2; ++hr) {
+    if (!row_ok[hr]) continue;
+    const float inv = l_run[hr] > 0.f ? 1.f / l_run[hr] : 0.f;
+    uint16_t *dst = a.out + static_cast<int64_t>(qs + tok_r[hr]) * a.o_stride +
+                    static_cast<int64_t>(kvh * G + head_r[hr]) * D;
+#pragma unroll
+    for (int n = 0; n < kNTiles; ++n)
+      *reinterpret_cast<uint32_t *>(dst + n * 8 + 2 * cq) = pack2<kBf16>(o[n][2 * hr] * inv, o[n][2 * hr + 1] * inv);
   }
 }
 

@@ -190,5 +190,150 @@ __global__ void __launch_bounds__(kSiluThreads) silu_mul_kernel(const __grid_con
   }
 }
 
+// ------------------------------------------------------------------------
+// Greedy head and embedding
+// ------------------------------------------------------------------------
+// lm_head_argmax: for each of up to kHeadMaxTokens hidden rows, the greedy
+// pick over this rank's vocabulary rows: logit[t][v] = fp16(sum_k h[t][k] W[v][k])
+// (fp32 accumulation rounded to fp16, the value F.linear hands to argmax in
+// the reference, qwen2.py:665-673, sampling.py:103-112), its maximum and the
+// lowest vocabulary index holding it -- without writing the logits.  Each warp
+// streams one weight row at a time (16-byte loads, the row read once), the
+// hidden rows sit in shared memory as fp32; per token the best (value, index)
+// folds into one 64-bit key (orderable value bits, then the complemented
+// index so equal values keep the lowest index) by atomicMax, and the last
+// CTA to finish turns the keys into indices and values and clears them.
+constexpr int kHeadThreads = 256;
+constexpr int kHeadMaxTokens = 4;
+
+struct HeadArgs {
+  const uint16_t *hidden;  // [tokens][hidden_stride] fp16
+  int64_t hidden_stride;
+  const uint16_t *weight;  // [vocab][H] fp16 (nn.Linear layout)
+  int tokens, H, V;
+  int64_t vocab_offset;    // global index of local row 0
+  unsigned long long *keys;  // [kHeadMaxTokens], zero between calls
+  unsigned int *counter;     // zero between calls
+  int64_t *out_index;        // [tokens]
+  float *out_value;          // [tokens] or null
+};
+
+__device__ __forceinline__ unsigned long long head_key(float v, int row) {
+  uint32_t b = __float_as_uint(v);
+  b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+  return (static_cast<unsigned long long>(b) << 32) | (0xFFFFFFFFu - static_cast<uint32_t>(row));
+}
+
+__device__ __forceinline__ float head_value(unsigned long long key) {
+  uint32_t b = static_cast<uint32_t>(key >> 32);
+  b = (b & 0x80000000u) ? (b & 0x7FFFFFFFu) : ~b;
+  return __uint_as_float(b);
+}
+
+template <int TOK>
+__global__ void __launch_bounds__(kHeadThreads) lm_head_argmax_kernel(const __grid_constant__ HeadArgs a) {
+  extern __shared__ __align__(16) float head_sm[];  // [TOK][H] fp32
+  __shared__ unsigned long long best_sm[kHeadThreads / 32][TOK];
+  __shared__ int last_sm;
+  pdl_entry();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int chunks = a.H / 8;
+  for (int i = threadIdx.x; i < TOK * chunks; i += kHeadThreads) {
+    const int t = i / chunks, c = i - t * chunks;
+    const uint4 v = *reinterpret_cast<const uint4 *>(a.hidden + static_cast<size_t>(t) * a.hidden_stride + c * 8);
+    const __half2 *h = reinterpret_cast<const __half2 *>(&v);
+    float4 *dst = reinterpret_cast<float4 *>(head_sm + static_cast<size_t>(t) * a.H + c * 8);
+    const float2 f0 = __half22float2(h[0]), f1 = __half22float2(h[1]), f2 = __half22float2(h[2]),
+                 f3 = __half22float2(h[3]);
+    dst[0] = make_float4(f0.x, f0.y, f1.x, f1.y);
+    dst[1] = make_float4(f2.x, f2.y, f3.x, f3.y);
+  }
+  __syncthreads();
+  unsigned long long best[TOK];
+#pragma unroll
+  for (int t = 0; t < TOK; ++t) best[t] = 0ull;
+  const int warps = gridDim.x * (kHeadThreads / 32);
+  for (int row = blockIdx.x * (kHeadThreads / 32) + warp; row < a.V; row += warps) {
+    const uint4 *w = reinterpret_cast<const uint4 *>(a.weight + static_cast<size_t>(row) * a.H);
+    float acc[TOK];
+#pragma unroll
+    for (int t = 0; t < TOK; ++t) acc[t] = 0.f;
+#pragma unroll 4
+    for (int c = lane; c < chunks; c += 32) {
+      uint4 wv;
+      asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+                   : "=r"(wv.x), "=r"(wv.y), "=r"(wv.z), "=r"(wv.w)
+                   : "l"(w + c));
+      const __half2 *wh = reinterpret_cast<const __half2 *>(&wv);
+      float wf[8];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __half22float2(wh[e]);
+        wf[2 * e] = f.x;
+        wf[2 * e + 1] = f.y;
+      }
+#pragma unroll
+      for (int t = 0; t < TOK; ++t) {
+        const float4 *hp = reinterpret_cast<const float4 *>(head_sm + static_cast<size_t>(t) * a.H + c * 8);
+        const float4 h0 = hp[0], h1 = hp[1];
+        acc[t] = fmaf(wf[0], h0.x, acc[t]);
+        acc[t] = fmaf(wf[1], h0.y, acc[t]);
+        acc[t] = fmaf(wf[2], h0.z, acc[t]);
+        acc[t] = fmaf(wf[3], h0.w, acc[t]);
+        acc[t] = fmaf(wf[4], h1.x, acc[t]);
+        acc[t] = fmaf(wf[5], h1.y, acc[t]);
+        acc[t] = fmaf(wf[6], h1.z, acc[t]);
+        acc[t] = fmaf(wf[7], h1.w, acc[t]);
+      }
+    }
+#pragma unroll
+    for (int t = 0; t < TOK; ++t) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) acc[t] += __shfl_xor_sync(0xffffffffu, acc[t], o);
+      const unsigned long long k = head_key(__half2float(__float2half_rn(acc[t])), row);
+      best[t] = k > best[t] ? k : best[t];
+    }
+  }
+  if (lane == 0) {
+#pragma unroll
+    for (int t = 0; t < TOK; ++t) best_sm[warp][t] = best[t];
+  }
+  __syncthreads();
+  if (threadIdx.x < TOK && threadIdx.x < a.tokens) {
+    unsigned long long k = 0ull;
+    for (int w = 0; w < kHeadThreads / 32; ++w) k = best_sm[w][threadIdx.x] > k ? best_sm[w][threadIdx.x] : k;
+    atomicMax(a.keys + threadIdx.x, k);
+  }
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) last_sm = atomicAdd(a.counter, 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (!last_sm) return;
+  __threadfence();
+  if (threadIdx.x < a.tokens) {
+    const unsigned long long k = atomicExch(a.keys + threadIdx.x, 0ull);
+    a.out_index[threadIdx.x] = a.vocab_offset + static_cast<int64_t>(0xFFFFFFFFu - static_cast<uint32_t>(k));
+    if (a.out_value != nullptr) a.out_value[threadIdx.x] = head_value(k);
+  }
+  if (threadIdx.x == 0) *a.counter = 0u;
+}
+
+// Token embedding rows (one CTA per token, 16-byte copies): out[t] =
+// table[ids[t] - vocab_start] when vocab_start <= ids[t] < vocab_end, else
+// zeros (the masked lookup of a vocab-parallel shard, tensor_parallel.py:
+// 296-306; the row sum over ranks is the fused all-reduce that follows).
+__global__ void __launch_bounds__(128) embedding_kernel(const int64_t *__restrict__ ids,
+                                                        const uint16_t *__restrict__ table, int64_t vocab_start,
+                                                        int64_t vocab_end, int H, uint16_t *__restrict__ out,
+                                                        int64_t out_stride) {
+  pdl_entry();
+  const int t = blockIdx.x;
+  const int64_t id = ids[t];
+  const bool owned = id >= vocab_start && id < vocab_end;
+  const uint4 *src = reinterpret_cast<const uint4 *>(table + (owned ? (id - vocab_start) : 0) * H);
+  uint4 *dst = reinterpret_cast<uint4 *>(out + static_cast<int64_t>(t) * out_stride);
+  for (int c = threadIdx.x; c < H / 8; c += blockDim.x) dst[c] = owned ? src[c] : make_uint4(0u, 0u, 0u, 0u);
+}
+
 }  // namespace q2
 }  // namespace lvb

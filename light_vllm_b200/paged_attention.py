@@ -13,8 +13,9 @@ of ``lvb_paged_kv_write`` and ``lvb_paged_attention``:
   indices and the decode launch order (longest context first) go to the GPU
   in one pinned copy and are shared by every layer;
 * decode steps (one linear query per request) take the split-context kernel;
-  every other batch (prefill chunks, mixed batches, tree visibility) the
-  general kernel;
+  prefill chunks, mixed batches and tree layouts the tensor-core tile kernel,
+  with a mixed batch's one-token requests on the split-context kernel (head
+  sizes 32 / 80 / 256 run a scalar kernel);
 * errors follow the reference: ``KVCacheError`` for a repeated layer, a shape,
   dtype or device mismatch, and any block-table violation.
 
@@ -73,6 +74,7 @@ class StepShape(NamedTuple):
     max_query_len: int
     max_seq_len: int
     linear: bool
+    num_single: int  # requests with one query token (listed first in the launch order)
 
     @property
     def packed_size(self) -> int:
@@ -123,11 +125,11 @@ class StepMetadataPacker:
         tables = metadata.block_tables
         n = len(tables)
         self._reserve(n, sum(map(len, tables)))
-        total, max_blocks, ntok, max_q, max_seq, linear = self._hostpack.gather_step(
+        total, max_blocks, ntok, max_q, max_seq, linear, single = self._hostpack.gather_step(
             tables, metadata.num_computed_tokens, metadata.query_layouts,
             metadata.num_reserved_query_tokens, metadata.num_readonly_prefix_blocks,
             self._ids_ptr, self._ids.size, self._offsets_ptr, self._rows_ptr)
-        self._step = StepShape(n, total, max_blocks, ntok, max_q, max_seq, linear)
+        self._step = StepShape(n, total, max_blocks, ntok, max_q, max_seq, linear, single)
         return self._step
 
     def pack(self, num_blocks: int, block_size: int, out_ptr: int, out_capacity: int) -> None:
@@ -202,6 +204,7 @@ class B200PagedAttention:
         self._request_order = packed[req_end:]
         self._table_stride = max_blocks
         self._num_seqs = n
+        self._num_decode = step.num_single
         self._num_tokens = step.num_tokens
         self._max_query_len = step.max_query_len
         self._max_seq_len = step.max_seq_len
@@ -287,7 +290,7 @@ class B200PagedAttention:
                 self._request_indices.data_ptr(), self._request_order.data_ptr(),
                 None if self._visibility is None else self._visibility.data_ptr(),
                 None if self._visibility_start is None else self._visibility_start.data_ptr(),
-                self._num_seqs, self._num_tokens, self._max_query_len, self._max_seq_len,
+                self._num_seqs, self._num_decode, self._num_tokens, self._max_query_len, self._max_seq_len,
                 spec.num_query_heads, spec.num_kv_heads, spec.head_size, config.block_size,
                 config.num_blocks, float(scale), dtype_code, workspace, workspace_bytes, stream,
             ),

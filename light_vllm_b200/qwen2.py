@@ -8,7 +8,7 @@ out like the reference (column-parallel QKV and gate/up, row-parallel o/down,
 vocab-parallel embedding and lm_head, KV heads replicated when there are
 fewer than ranks: qwen2.py:290-318, tensor_parallel.py:248-330):
 
-  x = embed(ids)                          masked per vocab shard
+  x = embed(ids)                          lvb_embedding, masked per vocab shard
   x, residual = allreduce_add_rmsnorm(x, 0, input_layernorm)
   per layer:
     qkv  = AWQ(x) + bias                  B200AWQScheme, merged QKV
@@ -18,8 +18,9 @@ fewer than ranks: qwen2.py:290-318, tensor_parallel.py:248-330):
     x, residual = allreduce_add_rmsnorm(AWQ_down(silu(gate) * up), residual, next norm)
                                           (the SiLU-mul inside the down projection's
                                           activation prologue at decode sizes)
-  logits = x @ lm_head_shard^T            cuBLAS (plain fp16 GEMM)
-  next   = argmax over the full vocabulary (per-shard max + index, gathered)
+  next   = greedy over the full vocabulary   lvb_lm_head_argmax at <= 4 rows (no logits
+                                          written), else cuBLAS logits + argmax;
+                                          per-shard (max, index) gathered under TP
 
 Every row-parallel sum, the residual add and the following RMSNorm are one
 launch of ``lvb_allreduce_add_rmsnorm`` over NVLink peer memory (a single
@@ -37,7 +38,6 @@ from collections.abc import Mapping
 import torch
 import torch.distributed as dist
 from torch import Tensor
-from torch.nn import functional as F
 
 from light_vllm_b200 import _native
 from light_vllm_b200.awq import B200AWQScheme
@@ -211,6 +211,9 @@ class Qwen2AWQRunner:
                                        distributed=world > 1)
         self.scale = 1.0 / shape.head_size ** 0.5
         self._lib = _native.library()
+        # zero-filled once; every lvb_lm_head_argmax call leaves it zero
+        self.head_workspace = torch.zeros(int(self._lib.lvb_lm_head_workspace_bytes()), dtype=torch.uint8,
+                                          device=self.device)
 
     # ------------------------------------------------------------------ specs
     def kv_layers(self) -> tuple[tuple[str, int, int, int], ...]:
@@ -227,12 +230,17 @@ class Qwen2AWQRunner:
 
     # ---------------------------------------------------------------- forward
     def _embed(self, ids: Tensor) -> Tensor:
-        if self.world == 1:
-            return F.embedding(ids, self.embed)
+        """Masked lookup of this rank's vocabulary rows (``lvb_embedding``;
+        rows of other shards are zero and the following all-reduce sums
+        them, tensor_parallel.py:296-306)."""
+
         vp = self.layout.vocab_part
-        owned = (ids >= vp.start) & (ids < vp.end)
-        local = torch.where(owned, ids - vp.start, torch.zeros_like(ids))
-        return F.embedding(local, self.embed).masked_fill_(~owned.unsqueeze(-1), 0)
+        out = torch.empty((ids.shape[0], self.shape.hidden_size), dtype=torch.float16, device=self.device)
+        ids = ids if ids.dtype == torch.int64 else ids.to(torch.int64)
+        _native.check(self._lib.lvb_embedding(
+            ids.data_ptr(), ids.shape[0], self.embed.data_ptr(), vp.start, vp.end, self.shape.hidden_size,
+            out.data_ptr(), out.stride(0), _native.stream_handle(self.device)), "lvb_embedding")
+        return out
 
     def _rope(self, qkv: Tensor, positions: Tensor) -> None:
         s = self.shape
@@ -242,11 +250,29 @@ class Qwen2AWQRunner:
             _native.stream_handle(self.device)), "lvb_rope_qk")
 
     def _greedy(self, hidden: Tensor) -> Tensor:
-        logits = torch.mm(hidden, self.lm_head.t())
-        if self.world == 1:
-            return logits.argmax(dim=-1)
-        values, index = logits.max(dim=-1)
-        index = index + self.layout.vocab_part.start
+        """Greedy next token of each row (qwen2.py:665-673, sampling.py:103-112).
+        Up to four rows: ``lvb_lm_head_argmax`` streams the head once and
+        keeps per row the (maximum fp16 logit, lowest index) without writing
+        logits; larger batches: cuBLAS logits and argmax."""
+
+        t = hidden.shape[0]
+        vp = self.layout.vocab_part
+        if t <= 4:
+            index = torch.empty(t, dtype=torch.int64, device=self.device)
+            values = torch.empty(t, dtype=torch.float32, device=self.device) if self.world > 1 else None
+            hidden = hidden if hidden.is_contiguous() else hidden.contiguous()
+            _native.check(self._lib.lvb_lm_head_argmax(
+                hidden.data_ptr(), hidden.stride(0), t, self.lm_head.data_ptr(), self.lm_head.shape[0],
+                self.shape.hidden_size, vp.start, index.data_ptr(), None if values is None else values.data_ptr(),
+                self.head_workspace.data_ptr(), _native.stream_handle(self.device)), "lvb_lm_head_argmax")
+            if self.world == 1:
+                return index
+        else:
+            logits = torch.mm(hidden, self.lm_head.t())
+            if self.world == 1:
+                return logits.argmax(dim=-1)
+            values, index = logits.max(dim=-1)
+            index = index + vp.start
         gv = torch.empty((self.world,) + tuple(values.shape), dtype=values.dtype, device=self.device)
         gi = torch.empty((self.world,) + tuple(index.shape), dtype=index.dtype, device=self.device)
         dist.all_gather_into_tensor(gv, values, group=self.group)
@@ -415,7 +441,7 @@ class StaticDecodeAttention:
             query.data_ptr(), query.stride(0), layer.keys.data_ptr(), layer.values.data_ptr(),
             out.data_ptr(), out.stride(0), self.tables.data_ptr(), self.stride, self.computed.data_ptr(),
             self.query_start.data_ptr(), self.request_indices.data_ptr(), None, None, None,
-            self.num_seqs, self.num_seqs, 1, self.capacity, spec.num_query_heads, spec.num_kv_heads,
+            self.num_seqs, self.num_seqs, self.num_seqs, 1, self.capacity, spec.num_query_heads, spec.num_kv_heads,
             spec.head_size, config.block_size, config.num_blocks, float(scale), dtype_code,
             self.workspace.data_ptr(), self.workspace.numel(), stream), "lvb_paged_attention")
         return out

@@ -112,6 +112,37 @@ def linear_fp32(
     return y.reshape(*np.asarray(inputs).shape[:-1], w.shape[1])
 
 
+def linear_exact_weight(
+    inputs: np.ndarray,
+    qweight: np.ndarray,
+    qzeros: np.ndarray,
+    scales: np.ndarray,
+    group_size: int,
+    bias: np.ndarray | None,
+) -> tuple[np.ndarray, np.ndarray]:
+    """Not a reference function: the same product with the unrounded weight
+    (q - z) * s (float64), and sum_k |x_k W_k| with the reference's fp16 W.
+
+    The reference rounds W to fp16 before the product
+    (modeling/quantization/awq.py:433-450); a kernel that applies the zero
+    point and scale exactly (the integer-limb decode paths) differs from it
+    by at most 2^-11 * sum_k |x_k W_k| (half an fp16 ulp per weight).  Tests
+    use the first array to check such a kernel's own arithmetic and the second
+    to bound its distance from the reference.  Returns (y_exact, abs_sum).
+    """
+
+    codes = unpack(np.asarray(qweight)).astype(np.float64)
+    zeros = unpack(np.asarray(qzeros)).astype(np.float64)
+    group_ids = np.arange(codes.shape[0]) // group_size
+    w = (codes - zeros[group_ids]) * np.asarray(scales, dtype=np.float16).astype(np.float64)[group_ids]
+    x = np.asarray(inputs, dtype=np.float16).astype(np.float64).reshape(-1, w.shape[0])
+    y = x @ w
+    if bias is not None:
+        y = y + np.asarray(bias, dtype=np.float16).astype(np.float64)
+    w16 = dequantize(qweight, qzeros, scales, group_size).astype(np.float64)
+    return y, np.abs(x) @ np.abs(w16)
+
+
 def torch_linear(
     inputs: torch.Tensor,
     qweight: torch.Tensor,

@@ -61,7 +61,7 @@ def test_invalid_arguments_are_rejected_before_any_launch():
     with pytest.raises(ValueError, match="invalid AWQ shape"):
         _native.check(status, "lvb_awq_linear")
     status = lib.lvb_paged_attention(None, 0, None, None, None, 0, None, 0, None, None, None, None, None,
-                                     None, 1, 1, 1, 1, 4, 4, 8, 16, 1, 1.0, 7, None, 0, None)
+                                     None, 1, 1, 1, 1, 1, 4, 4, 8, 16, 1, 1.0, 7, None, 0, None)
     assert status == _native.LVB_ERR_INVALID
     assert b"unknown dtype" in lib.lvb_last_error()
 

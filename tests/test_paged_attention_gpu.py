@@ -444,3 +444,72 @@ def test_staging_ring_copies_groups_and_grows():
         assert torch.equal(rest.cpu(), torch.from_numpy(tail))
         packed = staging.copy_packed(5, lambda host: host[:5].copy_(torch.arange(5, dtype=torch.int32) + i).numel())
         assert packed.tolist() == [i, i + 1, i + 2, i + 3, i + 4]
+
+
+def _mixed_batch(requests, hq, hkv, d, dtype, *, seed, block_size=16):
+    """A packed batch of (computed tokens, query layout parents) requests over
+    tables carved from a random permutation of the pool."""
+
+    gen = torch.Generator().manual_seed(seed)
+    need = [-(-(c + len(p)) // block_size) for c, p in requests]
+    pages = sum(need)
+    perm = torch.randperm(pages + 5, generator=gen).tolist()
+    tables, offset = [], 0
+    for n in need:
+        tables.append(tuple(perm[offset:offset + n]))
+        offset += n
+    md = PagedAttentionMetadata(block_tables=tuple(tables), num_computed_tokens=tuple(c for c, _ in requests),
+                                query_layouts=tuple(QueryLayout(tuple(p)) for _, p in requests))
+    spec = ModelKVCacheSpec((AttentionLayerSpec("attention", hq, hkv, d),))
+    cache = PagedKVCache(spec, PagedKVCacheConfig(pages + 5, block_size, dtype=dtype, device=DEV))
+    layer = cache.layer("attention")
+    torch.manual_seed(seed)
+    layer.keys.normal_()
+    layer.values.normal_()
+    t = sum(len(p) for _, p in requests)
+    q = torch.randn(t, hq, d, device=DEV, dtype=dtype)
+    k = torch.randn(t, hkv, d, device=DEV, dtype=dtype)
+    v = torch.randn(t, hkv, d, device=DEV, dtype=dtype)
+    return cache, md, q, k, v
+
+
+def _linear(n):
+    return tuple(range(-1, n - 1))
+
+
+_MIXED_CASES = {
+    # a prefill chunk after a long prefix, a fresh short prompt, and decodes
+    "chunk_prompt_decodes": [(500, _linear(300)), (0, _linear(7)), (37, _linear(1)), (2999, _linear(1)),
+                             (16, _linear(1))],
+    # prefill only: ragged prompts, one of them a single token
+    "prefill_only": [(0, _linear(129)), (0, _linear(1)), (48, _linear(64)), (0, _linear(33))],
+    # tree (speculative) layouts beside a linear chunk and decodes
+    "tree": [(200, (-1, 0, 0, 1, 1, 2, 5, -1)), (63, _linear(1)), (10, _linear(20)), (0, (-1, 0, 1, 0))],
+}
+
+
+@pytest.mark.parametrize("dtype", (torch.bfloat16, torch.float16))
+@pytest.mark.parametrize("hq,hkv,d", [(28, 4, 128), (10, 2, 128), (16, 2, 64), (8, 8, 128)])
+@pytest.mark.parametrize("case", sorted(_MIXED_CASES))
+def test_prefill_tiles_and_mixed_batches(case, dtype, hq, hkv, d):
+    """Prefill chunks, mixed prefill + decode batches and tree layouts (16-token
+    pages, head sizes 64 / 128) run the tensor-core tile kernel, a mixed
+    batch's one-token requests the split decode kernel: against a float64
+    evaluation of the same visible positions, rounded to the cache dtype,
+    max-abs <= 2e-2 and rel-L2 <= 1e-3; this step's K/V rows bit-exact in
+    their slots."""
+
+    cache, md, q, k, v = _mixed_batch(_MIXED_CASES[case], hq, hkv, d, dtype, seed=hq * 7 + d + len(case))
+    _check_decode(cache, md, q, k, v)
+
+
+def test_config5_shaped_mixed_step():
+    """BASELINE config 5 per TP = 4 rank (10 query / 2 KV heads, D = 128): one
+    2048-token prefill chunk and 64 decodes with contexts in [256, 8192],
+    fp16 cache."""
+
+    gen = torch.Generator().manual_seed(5)
+    ctx = torch.randint(256, 8193, (64,), generator=gen).tolist()
+    requests = [(0, _linear(2048))] + [(c - 1, _linear(1)) for c in ctx]
+    cache, md, q, k, v = _mixed_batch(requests, 10, 2, 128, torch.float16, seed=55)
+    _check_decode(cache, md, q, k, v)

@@ -255,3 +255,62 @@ def test_rope_kv_write_equals_rope_then_write():
     assert torch.equal(outs[0], outs[1])
     assert torch.equal(caches[0][0], caches[1][0]) and torch.equal(caches[0][1], caches[1][1])
     assert bool(caches[1][0].abs().sum() > 0)
+
+
+@pytest.mark.parametrize("tokens,vocab,hidden", [(1, 152064, 3584), (2, 4099, 256), (3, 1000, 8192), (4, 77, 5120)])
+def test_lm_head_argmax_matches_fp16_logits(tokens, vocab, hidden):
+    """lvb_lm_head_argmax against argmax over fp16 logits computed in float64
+    (the reference's F.linear output rounded to fp16), including planted
+    exact ties (equal rows: the lowest index wins, as torch.argmax), twice in
+    a row on one workspace (it must be left zero)."""
+
+    from light_vllm_b200 import _native
+
+    g = torch.Generator().manual_seed(tokens * 7 + vocab)
+    w = (torch.randn(vocab, hidden, generator=g) * 0.05).half()
+    h = torch.randn(tokens, hidden, generator=g).half()
+    # tie: the best row of token 0 duplicated at a higher and a lower index
+    logits64 = h.double() @ w.double().t()
+    best0 = int(logits64[0].argmax())
+    lo = max(0, best0 - 3)
+    w[lo] = w[best0]
+    if best0 + 5 < vocab:
+        w[best0 + 5] = w[best0]
+    want = (h.double() @ w.double().t()).half().float()
+    want_idx = want.argmax(dim=-1)
+    want_val = want.max(dim=-1).values
+    lib = _native.library()
+    ws = torch.zeros(int(lib.lvb_lm_head_workspace_bytes()), dtype=torch.uint8, device="cuda")
+    wd, hd = w.cuda(), h.cuda()
+    for _ in range(2):
+        idx = torch.full((tokens,), -1, dtype=torch.int64, device="cuda")
+        val = torch.empty(tokens, dtype=torch.float32, device="cuda")
+        _native.check(lib.lvb_lm_head_argmax(hd.data_ptr(), hd.stride(0), tokens, wd.data_ptr(), vocab, hidden, 1000,
+                                             idx.data_ptr(), val.data_ptr(), ws.data_ptr(),
+                                             torch.cuda.current_stream().cuda_stream), "lm_head")
+        torch.cuda.synchronize()
+        assert _native.device_error() == 0
+        # fp32 accumulation may round a logit to the neighbouring fp16 value; the pick
+        # must then still hold the maximum up to one fp16 ulp
+        got = idx.cpu() - 1000
+        assert torch.equal(got, want_idx) or all(
+            float(want[t, got[t]]) >= float(want_val[t]) - float(want_val[t].abs()) * 2.0**-10 for t in range(tokens))
+        assert int(got[0]) == min(lo, int(want_idx[0]))  # exact tie of equal rows: the lowest index
+        assert torch.allclose(val.cpu(), want[torch.arange(tokens), got], rtol=0, atol=0)
+        assert int(ws.cpu().sum()) == 0
+
+
+def test_embedding_masks_rows_of_other_shards():
+    from light_vllm_b200 import _native
+
+    table = torch.randn(50, 64).half().cuda()
+    ids = torch.tensor([100, 149, 99, 150, 120], dtype=torch.int64, device="cuda")
+    out = torch.full((5, 64), 7.0, dtype=torch.float16, device="cuda")
+    _native.check(_native.library().lvb_embedding(ids.data_ptr(), 5, table.data_ptr(), 100, 150, 64, out.data_ptr(),
+                                                  out.stride(0), torch.cuda.current_stream().cuda_stream), "embed")
+    torch.cuda.synchronize()
+    want = torch.zeros(5, 64, dtype=torch.float16)
+    for i, v in enumerate(ids.tolist()):
+        if 100 <= v < 150:
+            want[i] = table[v - 100].cpu()
+    assert torch.equal(out.cpu(), want)

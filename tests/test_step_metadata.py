@@ -85,9 +85,10 @@ def check_payload(payload, tables, computed, qlens):
     assert list(out[base : base + n]) == list(computed)
     assert list(out[base + n : base + 2 * n + 1]) == list(opa.query_start_loc(qlens))
     assert list(out[base + 2 * n + 1 : base + 2 * n + 1 + ntok]) == list(opa.request_indices(qlens))
-    # Launch order for the decode kernel: descending computed count, ties by index.
+    # Launch order: one-token requests first, then the rest; each part by
+    # descending context length (computed + query tokens), ties by index.
     order = list(out[base + 2 * n + 1 + ntok : base + 3 * n + 1 + ntok])
-    assert order == sorted(range(n), key=lambda r: -computed[r])
+    assert order == sorted(range(n), key=lambda r: (qlens[r] != 1, -(computed[r] + qlens[r])))
     assert list(out[base + 3 * n + 1 + ntok : base + 4 * n + 1 + ntok]) == [computed[r] for r in order]
 
 
@@ -207,7 +208,7 @@ def test_packer_reads_the_metadata_objects():
     md = PagedAttentionMetadata(block_tables=((3, 1), (0,)), num_computed_tokens=(16, 3),
                                 query_layouts=(linear_query_layout(2), QueryLayout((-1, 0, 0))))
     step = packer.gather(md)
-    assert step == (2, 3, 2, 5, 3, 18, False)
+    assert step == (2, 3, 2, 5, 3, 18, False, 0)
     out = np.zeros(step.packed_size, dtype=np.int32)
     packer.pack(4, 16, out.ctypes.data, out.size)
     assert out.tolist() == [3, 1, 0, 0, 16, 3, 0, 2, 5, 0, 0, 1, 1, 1, 0, 1, 16, 3]
