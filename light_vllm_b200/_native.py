@@ -178,6 +178,10 @@ def hostpack():
     spec = importlib.util.spec_from_file_location("light_vllm_b200._hostpack", str(HOSTPACK_PATH), loader=loader)
     module = importlib.util.module_from_spec(spec)
     loader.exec_module(module)
+    # The call trampolines reach the library's entry points directly.
+    lib = library()
+    module.bind(*(ctypes.cast(getattr(lib, name), ctypes.c_void_p).value
+                  for name in ("lvb_paged_kv_write", "lvb_paged_attention", "lvb_stage_step_metadata")))
     return module
 
 

@@ -1,6 +1,7 @@
 /* CPython module light_vllm_b200._hostpack: reads one step's attention
  * metadata out of its Python objects into flat C arrays for
- * lvb_pack_step_metadata.
+ * lvb_pack_step_metadata, and calls the attention step's library entry
+ * points with C-API argument parsing (call trampolines, below).
  *
  * PagedAttentionMetadata (runtime/execution/paged_attention.py:18-95) holds
  * its block tables as tuples of Python ints and its query layouts as objects
@@ -185,7 +186,113 @@ fail:
   return NULL;
 }
 
+/* ------------------------------------------------------------------------
+ * Call trampolines.  The attention step's library calls (lvb_paged_kv_write,
+ * lvb_paged_attention) and the metadata staging call (lvb_stage_step_metadata)
+ * take 17-30 arguments; through ctypes each call costs several microseconds of
+ * argument conversion per layer and step.  bind() receives the three function
+ * addresses once (from the ctypes library object); the entry points below
+ * parse their arguments with the C API and call them directly.
+ * ------------------------------------------------------------------------ */
+typedef int (*kv_write_fn)(const void *, int64_t, const void *, int64_t, void *, void *, const void *, int64_t,
+                           const void *, const void *, const void *, int64_t, int64_t, int64_t, int64_t, int,
+                           void *);
+typedef int (*attention_fn)(const void *, int64_t, const void *, const void *, void *, int64_t, const void *,
+                            int64_t, const void *, const void *, const void *, const void *, const void *,
+                            const void *, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t,
+                            int64_t, int64_t, float, int, void *, size_t, void *);
+typedef int (*stage_fn)(const int32_t *, const int64_t *, const int32_t *, const int32_t *, const int32_t *,
+                        const int32_t *, int64_t, int64_t, int64_t, int32_t *, int64_t, int32_t *, int64_t, void *,
+                        void *, int64_t *, int64_t *);
+static kv_write_fn g_kv_write;
+static attention_fn g_attention;
+static stage_fn g_stage;
+
+static PyObject *bind(PyObject *self, PyObject *args) {
+  (void)self;
+  unsigned long long kv, attn, stage;
+  if (!PyArg_ParseTuple(args, "KKK", &kv, &attn, &stage)) return NULL;
+  g_kv_write = (kv_write_fn)(uintptr_t)kv;
+  g_attention = (attention_fn)(uintptr_t)attn;
+  g_stage = (stage_fn)(uintptr_t)stage;
+  Py_RETURN_NONE;
+}
+
+#define PTR(x) ((void *)(uintptr_t)(x))
+
+/* attention_step(step, layer, q, q_stride, k, k_stride, v, v_stride, out,
+ *                o_stride, write_kv, scale, workspace, workspace_bytes, stream)
+ *   step  = (tables, table_stride, computed, query_start, request_indices,
+ *            request_order, visibility, visibility_start, num_seqs,
+ *            num_decode_seqs, num_tokens, max_query_len, max_seq_len)
+ *   layer = (key_cache, value_cache, num_q_heads, num_kv_heads, head_size,
+ *            block_size, num_blocks, dtype)
+ * Runs lvb_paged_kv_write (when write_kv) then lvb_paged_attention; returns
+ * (status, 0) or (status, 1) for the call that failed (0 = kv write). */
+static PyObject *attention_step(PyObject *self, PyObject *args) {
+  (void)self;
+  unsigned long long tables, computed, qsl, req, order, vis, vis_start;
+  long long stride, n_seqs, n_decode, n_tokens, max_q, max_seq;
+  unsigned long long kc, vc;
+  long long hq, hkv, d, bs, num_blocks;
+  int dtype;
+  unsigned long long q, k, v, out, ws, stream;
+  long long q_stride, k_stride, v_stride, o_stride;
+  int write_kv;
+  float scale;
+  Py_ssize_t ws_bytes;
+  if (!PyArg_ParseTuple(args, "(KLKKKKKKLLLLL)(KKLLLLLi)KLKLKLKLpfKnK", &tables, &stride, &computed, &qsl, &req,
+                        &order, &vis, &vis_start, &n_seqs, &n_decode, &n_tokens, &max_q, &max_seq, &kc, &vc, &hq,
+                        &hkv, &d, &bs, &num_blocks, &dtype, &q, &q_stride, &k, &k_stride, &v, &v_stride, &out,
+                        &o_stride, &write_kv, &scale, &ws, &ws_bytes, &stream))
+    return NULL;
+  if (!g_kv_write || !g_attention) {
+    PyErr_SetString(PyExc_RuntimeError, "_hostpack.bind was not called");
+    return NULL;
+  }
+  if (write_kv) {
+    const int rc = g_kv_write(PTR(k), k_stride, PTR(v), v_stride, PTR(kc), PTR(vc), PTR(tables), stride,
+                              PTR(computed), PTR(qsl), PTR(req), n_tokens, hkv, d, bs, dtype, PTR(stream));
+    if (rc) return Py_BuildValue("(ii)", rc, 0);
+  }
+  const int rc = g_attention(PTR(q), q_stride, PTR(kc), PTR(vc), PTR(out), o_stride, PTR(tables), stride,
+                             PTR(computed), PTR(qsl), PTR(req), PTR(order), PTR(vis), PTR(vis_start), n_seqs,
+                             n_decode, n_tokens, max_q, max_seq, hq, hkv, d, bs, num_blocks, scale, dtype, PTR(ws),
+                             (size_t)ws_bytes, PTR(stream));
+  return Py_BuildValue("(ii)", rc, 1);
+}
+
+/* stage_step(ids, offsets, rows, num_seqs, num_blocks, block_size, pinned,
+ *            pinned_capacity, device, device_capacity, event, stream)
+ *   -> (status, table_stride, num_tokens): lvb_stage_step_metadata over the
+ *   buffers gather_step filled. */
+static PyObject *stage_step(PyObject *self, PyObject *args) {
+  (void)self;
+  unsigned long long ids, offsets, rows, pinned, device, event, stream;
+  long long n, num_blocks, block_size, pinned_cap, device_cap;
+  if (!PyArg_ParseTuple(args, "KKKLLLKLKLKK", &ids, &offsets, &rows, &n, &num_blocks, &block_size, &pinned,
+                        &pinned_cap, &device, &device_cap, &event, &stream))
+    return NULL;
+  if (!g_stage) {
+    PyErr_SetString(PyExc_RuntimeError, "_hostpack.bind was not called");
+    return NULL;
+  }
+  const int32_t *r = (const int32_t *)PTR(rows);
+  int64_t stride = 0, ntok = 0;
+  const int rc = g_stage((const int32_t *)PTR(ids), (const int64_t *)PTR(offsets), r, r + n, r + 2 * n, r + 3 * n, n,
+                         num_blocks, block_size, (int32_t *)PTR(pinned), pinned_cap, (int32_t *)PTR(device),
+                         device_cap, PTR(event), PTR(stream), &stride, &ntok);
+  return Py_BuildValue("(iLL)", rc, (long long)stride, (long long)ntok);
+}
+
 static PyMethodDef methods[] = {
+    {"bind", bind, METH_VARARGS, "bind(kv_write_addr, attention_addr, stage_addr): library entry points"},
+    {"attention_step", attention_step, METH_VARARGS,
+     "attention_step(step, layer, q, q_stride, k, k_stride, v, v_stride, out, o_stride, write_kv, scale, "
+     "workspace, workspace_bytes, stream) -> (status, failed_call)"},
+    {"stage_step", stage_step, METH_VARARGS,
+     "stage_step(ids, offsets, rows, n, num_blocks, block_size, pinned, pinned_capacity, device, "
+     "device_capacity, event, stream) -> (status, table_stride, num_tokens)"},
     {"gather_step", gather_step, METH_VARARGS,
      "gather_step(tables, computed, layouts, reserved, readonly, ids_addr, ids_capacity, offsets_addr, "
      "rows_addr) -> (total_ids, max_blocks, num_tokens, max_query_len, max_seq_len, linear, "

@@ -26,6 +26,7 @@ validates and stages the step metadata, in native code.
 from __future__ import annotations
 
 import ctypes
+import weakref
 from typing import NamedTuple
 
 import numpy as np
@@ -37,23 +38,6 @@ from light_vllm_b200.kv_cache import KVCacheError
 from light_vllm_b200.staging import SingleStepStaging
 
 _SUPPORTED_DTYPES = (torch.float16, torch.bfloat16)
-
-
-def _validate_tensors(cache, num_query_tokens: int, layer_id: str, query: Tensor, key: Tensor, value: Tensor):
-    """Shape rules shared with the reference backends (paged_attention.py:226-247)."""
-
-    spec = cache.layer_spec(layer_id)
-    if query.ndim != 3:
-        raise KVCacheError("paged attention query must have three dimensions")
-    if query.shape[0] != key.shape[0] or value.shape != key.shape:
-        raise KVCacheError("paged attention Q/K/V token dimensions must match")
-    if query.shape[0] != num_query_tokens:
-        raise KVCacheError("paged attention metadata token count does not match query")
-    if tuple(query.shape[1:]) != (spec.num_query_heads, spec.head_size):
-        raise KVCacheError("paged attention query shape does not match the layer spec")
-    if tuple(key.shape[1:]) != (spec.num_kv_heads, spec.head_size):
-        raise KVCacheError("paged attention K/V shape does not match the layer spec")
-    return spec
 
 
 def _heads_contiguous(t: Tensor, *, align: int) -> Tensor:
@@ -158,20 +142,29 @@ class StepMetadataPacker:
         if step is None:
             raise RuntimeError("StepMetadataPacker.stage before gather")
         n = step.num_seqs
-        rows = self._rows_ptr
-        lib = self._lib
+        hostpack = self._hostpack
 
         def run(host_ptr: int, host_capacity: int, dev_ptr: int, dev_capacity: int, event: int,
                 stream: int) -> int:
-            _native.check(
-                lib.lvb_stage_step_metadata(
-                    self._ids_ptr, self._offsets_ptr, rows, rows + 4 * n, rows + 8 * n, rows + 12 * n, n,
-                    num_blocks, block_size, host_ptr, host_capacity, dev_ptr, dev_capacity, event, stream,
-                    self._stride_ref, self._ntok_ref),
-                "lvb_stage_step_metadata")
+            status, _, _ = hostpack.stage_step(self._ids_ptr, self._offsets_ptr, self._rows_ptr, n, num_blocks,
+                                               block_size, host_ptr, host_capacity, dev_ptr, dev_capacity, event,
+                                               stream)
+            if status:
+                _native.check(status, "lvb_stage_step_metadata")
             return step.packed_size
 
         return staging.stage(step.packed_size, run)
+
+
+class _LayerInfo(NamedTuple):
+    """Per (cache, layer) constants of the attention launches."""
+
+    spec: object
+    q_tail: tuple[int, int]
+    kv_tail: tuple[int, int]
+    args: tuple  # (key_cache, value_cache, hq, hkv, head_size, block_size, num_blocks, dtype)
+    keys: Tensor
+    values: Tensor
 
 
 class B200PagedAttention:
@@ -179,15 +172,15 @@ class B200PagedAttention:
 
     def __init__(self, cache, metadata, staging: SingleStepStaging, backend: "B200PagedAttentionBackend"):
         config = cache.config
-        if torch.device(config.device).type != "cuda":
-            raise KVCacheError("B200 paged attention requires a CUDA KV cache")
+        device = backend._device_of(config)
         if config.dtype not in _SUPPORTED_DTYPES:
             raise KVCacheError("B200 paged attention supports fp16 and bf16 KV caches")
         self._cache = cache
         self._metadata = metadata
         self._backend = backend
         self._layer_ids: set[str] = set()
-        self._device = torch.device(config.device)
+        self._device = device
+        self._dtype = config.dtype
         # Gathering from the metadata objects, validation (the reference's
         # block-table rules, same order and messages), packing and the one
         # pinned host-to-device copy of the per-step int32 payload all run in
@@ -196,12 +189,13 @@ class B200PagedAttention:
         step = packer.gather(metadata)
         packed = packer.stage(staging, config.num_blocks, config.block_size)
         n, max_blocks = step.num_seqs, step.max_blocks
-        self._tables = packed[: n * max_blocks]
-        self._computed = packed[n * max_blocks : n * max_blocks + n]
-        self._query_start = packed[n * max_blocks + n : n * max_blocks + 2 * n + 1]
-        req_end = n * max_blocks + 2 * n + 1 + step.num_tokens
-        self._request_indices = packed[n * max_blocks + 2 * n + 1 : req_end]
-        self._request_order = packed[req_end:]
+        self._packed = packed  # keeps the device payload alive; the launches take raw addresses
+        base = packed.data_ptr()
+        self._tables_ptr = base
+        self._computed_ptr = base + 4 * n * max_blocks
+        self._query_start_ptr = self._computed_ptr + 4 * n
+        self._request_indices_ptr = self._query_start_ptr + 4 * (n + 1)
+        self._request_order_ptr = self._request_indices_ptr + 4 * step.num_tokens
         self._table_stride = max_blocks
         self._num_seqs = n
         self._num_decode = step.num_single
@@ -211,10 +205,40 @@ class B200PagedAttention:
         self._linear = step.linear
         self._visibility: Tensor | None = None
         self._visibility_start: Tensor | None = None
+        self._step_args = (self._tables_ptr, max_blocks, self._computed_ptr, self._query_start_ptr,
+                           self._request_indices_ptr, self._request_order_ptr, 0, 0, n, step.num_single,
+                           step.num_tokens, step.max_query_len, step.max_seq_len)
+        self._workspace: tuple | None = None
 
     @property
     def layer_ids(self) -> frozenset[str]:
         return frozenset(self._layer_ids)
+
+    # Tensors of the step's payload, for callers that want views (tests, the
+    # fused RoPE + K/V write).
+    def _view(self, offset_ptr: int, count: int) -> Tensor:
+        start = (offset_ptr - self._tables_ptr) // 4
+        return self._packed[start : start + count]
+
+    @property
+    def _tables(self) -> Tensor:
+        return self._view(self._tables_ptr, self._num_seqs * self._table_stride)
+
+    @property
+    def _computed(self) -> Tensor:
+        return self._view(self._computed_ptr, self._num_seqs)
+
+    @property
+    def _query_start(self) -> Tensor:
+        return self._view(self._query_start_ptr, self._num_seqs + 1)
+
+    @property
+    def _request_indices(self) -> Tensor:
+        return self._view(self._request_indices_ptr, self._num_tokens)
+
+    @property
+    def _request_order(self) -> Tensor:
+        return self._view(self._request_order_ptr, 2 * self._num_seqs)
 
     def forward(self, layer_id: str, query: Tensor, key: Tensor, value: Tensor, *, scale: float,
                 write_kv: bool = True) -> Tensor:
@@ -226,16 +250,26 @@ class B200PagedAttention:
         if layer_id in self._layer_ids:
             raise KVCacheError(f"paged attention layer {layer_id!r} ran more than once")
         self._layer_ids.add(layer_id)
-        spec = _validate_tensors(self._cache, self._num_tokens, layer_id, query, key, value)
-        config = self._cache.config
-        for t in (query, key, value):
-            if t.device != self._device or t.dtype != config.dtype:
-                raise KVCacheError("B200 query/key/value dtype and device must match the KV cache")
-        if spec.head_size % 8 or spec.head_size > 256:
+        info = self._backend._layer_info(self._cache, layer_id)
+        # Shape rules shared with the reference backends (paged_attention.py:226-247).
+        if query.ndim != 3:
+            raise KVCacheError("paged attention query must have three dimensions")
+        if query.shape[0] != key.shape[0] or value.shape != key.shape:
+            raise KVCacheError("paged attention Q/K/V token dimensions must match")
+        if query.shape[0] != self._num_tokens:
+            raise KVCacheError("paged attention metadata token count does not match query")
+        if query.shape[1:] != info.q_tail:
+            raise KVCacheError("paged attention query shape does not match the layer spec")
+        if key.shape[1:] != info.kv_tail:
+            raise KVCacheError("paged attention K/V shape does not match the layer spec")
+        dev, dt = self._device, self._dtype
+        if (query.dtype != dt or key.dtype != dt or value.dtype != dt or query.device != dev
+                or key.device != dev or value.device != dev):
+            raise KVCacheError("B200 query/key/value dtype and device must match the KV cache")
+        if info.kv_tail[1] % 8 or info.kv_tail[1] > 256:
             raise KVCacheError("B200 paged attention supports head sizes that are multiples of 8 up to 256")
-        out = torch.empty((query.shape[0], spec.num_query_heads, spec.head_size),
-                          dtype=query.dtype, device=self._device)
-        return self.launch(layer_id, query, key, value, scale=scale, out=out, write_kv=write_kv)
+        out = torch.empty(query.shape, dtype=dt, device=dev)
+        return self._launch(info, query, key, value, float(scale), out, write_kv)
 
     def rope_write_kv(self, layer_id: str, qkv: Tensor, q_heads: int, kv_heads: int, positions: Tensor,
                       cos: Tensor, sin: Tensor) -> None:
@@ -243,8 +277,8 @@ class B200PagedAttention:
         step's K/V write for ``layer_id`` (``lvb_rope_kv_write``); follow with
         ``forward(..., write_kv=False)``."""
 
-        _rope_write_kv(self._cache, layer_id, qkv, q_heads, kv_heads, positions, cos, sin, self._tables,
-                       self._table_stride, self._computed, self._query_start, self._request_indices,
+        _rope_write_kv(self._cache, layer_id, qkv, q_heads, kv_heads, positions, cos, sin, self._tables_ptr,
+                       self._table_stride, self._computed_ptr, self._query_start_ptr, self._request_indices_ptr,
                        self._device)
 
     def launch(self, layer_id: str, query: Tensor, key: Tensor, value: Tensor, *, scale: float,
@@ -254,53 +288,41 @@ class B200PagedAttention:
         synchronisation), so repeated steps can be captured in a CUDA graph.
         Shapes must already satisfy ``forward``'s checks."""
 
-        spec = self._cache.layer_spec(layer_id)
-        config = self._cache.config
-        lib = _native.library()
-        stream = _native.stream_handle(self._device)
-        dtype_code = _native.DTYPE_BF16 if config.dtype == torch.bfloat16 else _native.DTYPE_F16
-        layer = self._cache.layer(layer_id)
-        if write_kv:
-            key = _heads_contiguous(key, align=8)
-            value = _heads_contiguous(value, align=8)
-            _native.check(
-                lib.lvb_paged_kv_write(
-                    key.data_ptr(), key.stride(0), value.data_ptr(), value.stride(0),
-                    layer.keys.data_ptr(), layer.values.data_ptr(),
-                    self._tables.data_ptr(), self._table_stride, self._computed.data_ptr(),
-                    self._query_start.data_ptr(), self._request_indices.data_ptr(),
-                    self._num_tokens, spec.num_kv_heads, spec.head_size, config.block_size,
-                    dtype_code, stream,
-                ),
-                "lvb_paged_kv_write",
-            )
+        return self._launch(self._backend._layer_info(self._cache, layer_id), query, key, value, float(scale), out,
+                            write_kv)
+
+    def _launch(self, info: _LayerInfo, query: Tensor, key: Tensor, value: Tensor, scale: float, out: Tensor,
+                write_kv: bool) -> Tensor:
         if not self._linear and self._visibility is None:
             vis, starts = self._metadata.visibility_tensor(device=self._device)
             self._visibility = vis.to(torch.uint8)
             self._visibility_start = starts
+            self._step_args = self._step_args[:6] + (self._visibility.data_ptr(),
+                                                     self._visibility_start.data_ptr()) + self._step_args[8:]
+        if self._workspace is None or self._workspace[0] != info.args[2:5]:
+            spec = info.spec
+            ptr, nbytes = self._backend._workspace(self._device, self._num_seqs, spec.num_query_heads,
+                                                   spec.num_kv_heads, spec.head_size, self._max_seq_len)
+            self._workspace = (info.args[2:5], ptr, nbytes)
+        if write_kv:
+            key = _heads_contiguous(key, align=8)
+            value = _heads_contiguous(value, align=8)
         query = _heads_contiguous(query, align=2)
-        workspace, workspace_bytes = self._backend._workspace(
-            self._device, self._num_seqs, spec.num_query_heads, spec.num_kv_heads,
-            spec.head_size, self._max_seq_len)
-        _native.check(
-            lib.lvb_paged_attention(
-                query.data_ptr(), query.stride(0), layer.keys.data_ptr(), layer.values.data_ptr(),
-                out.data_ptr(), out.stride(0), self._tables.data_ptr(), self._table_stride,
-                self._computed.data_ptr(), self._query_start.data_ptr(),
-                self._request_indices.data_ptr(), self._request_order.data_ptr(),
-                None if self._visibility is None else self._visibility.data_ptr(),
-                None if self._visibility_start is None else self._visibility_start.data_ptr(),
-                self._num_seqs, self._num_decode, self._num_tokens, self._max_query_len, self._max_seq_len,
-                spec.num_query_heads, spec.num_kv_heads, spec.head_size, config.block_size,
-                config.num_blocks, float(scale), dtype_code, workspace, workspace_bytes, stream,
-            ),
-            "lvb_paged_attention",
-        )
+        _, ws_ptr, ws_bytes = self._workspace
+        status, which = self._backend._hostpack.attention_step(
+            self._step_args, info.args, query.data_ptr(), query.stride(0), key.data_ptr(), key.stride(0),
+            value.data_ptr(), value.stride(0), out.data_ptr(), out.stride(0), write_kv, scale, ws_ptr, ws_bytes,
+            _native.stream_handle(self._device))
+        if status:
+            _native.check(status, "lvb_paged_attention" if which else "lvb_paged_kv_write")
         return out
 
 
 def _rope_write_kv(cache, layer_id, qkv, q_heads, kv_heads, positions, cos, sin, tables, table_stride, computed,
                    query_start, request_indices, device) -> None:
+    """``lvb_rope_kv_write`` for one layer; the step metadata (tables,
+    computed counts, query starts, request indices) as device addresses."""
+
     spec = cache.layer_spec(layer_id)
     config = cache.config
     if config.dtype != torch.float16 or qkv.dtype != torch.float16:
@@ -311,32 +333,60 @@ def _rope_write_kv(cache, layer_id, qkv, q_heads, kv_heads, positions, cos, sin,
     _native.check(_native.library().lvb_rope_kv_write(
         qkv.data_ptr(), qkv.stride(0), qkv.shape[0], q_heads, kv_heads, spec.head_size, positions.data_ptr(),
         cos.data_ptr(), sin.data_ptr(), cos.shape[0], layer.keys.data_ptr(), layer.values.data_ptr(),
-        tables.data_ptr(), table_stride, computed.data_ptr(), query_start.data_ptr(), request_indices.data_ptr(),
+        tables, table_stride, computed, query_start, request_indices,
         config.block_size, _native.stream_handle(device)), "lvb_rope_kv_write")
 
 
 class B200PagedAttentionBackend:
     """Creates one ``B200PagedAttention`` per model step.
 
-    Owns the pinned metadata staging buffer and the split-context workspace;
-    both grow on demand and are reused by later steps.
+    Owns the pinned metadata staging buffer, the split-context workspace and
+    per-(cache, layer) launch constants; all are reused by later steps.
     """
 
     name = "b200"
 
     def __init__(self) -> None:
         _native.library()  # fail loudly at construction when the library is missing
+        self._hostpack = _native.hostpack()
         self._staging: SingleStepStaging | None = None
         self._packer = StepMetadataPacker()
         self._workspaces: dict[torch.device, Tensor] = {}
+        self._layers: "weakref.WeakKeyDictionary[object, dict[str, _LayerInfo]]" = weakref.WeakKeyDictionary()
+        self._devices: dict[object, torch.device] = {}
+
+    def _device_of(self, config) -> torch.device:
+        device = self._devices.get(config.device)
+        if device is None:
+            device = torch.device(config.device)
+            if device.type != "cuda":
+                raise KVCacheError("B200 paged attention requires a CUDA KV cache")
+            if device.index is None:
+                device = torch.device("cuda", torch.cuda.current_device())
+            self._devices[config.device] = device
+        return device
 
     def create(self, cache, metadata) -> B200PagedAttention:
-        device = torch.device(cache.config.device)
-        if device.type != "cuda":
-            raise KVCacheError("B200 paged attention requires a CUDA KV cache")
+        device = self._device_of(cache.config)
         if self._staging is None:
             self._staging = SingleStepStaging(device)
         return B200PagedAttention(cache, metadata, self._staging, self)
+
+    def _layer_info(self, cache, layer_id: str) -> _LayerInfo:
+        try:
+            return self._layers[cache][layer_id]
+        except KeyError:
+            pass
+        spec = cache.layer_spec(layer_id)  # the cache's own KVCacheError for an unknown layer
+        layer = cache.layer(layer_id)
+        config = cache.config
+        dtype = _native.DTYPE_BF16 if config.dtype == torch.bfloat16 else _native.DTYPE_F16
+        info = _LayerInfo(spec, (spec.num_query_heads, spec.head_size), (spec.num_kv_heads, spec.head_size),
+                          (layer.keys.data_ptr(), layer.values.data_ptr(), spec.num_query_heads, spec.num_kv_heads,
+                           spec.head_size, config.block_size, config.num_blocks, dtype),
+                          layer.keys, layer.values)
+        self._layers.setdefault(cache, {})[layer_id] = info
+        return info
 
     def _workspace(self, device: torch.device, num_seqs: int, hq: int, hkv: int, d: int,
                    max_seq_len: int) -> tuple[int, int]:

@@ -415,8 +415,9 @@ class StaticDecodeAttention:
                       cos: Tensor, sin: Tensor) -> None:
         """RoPE fused with this step's K/V write (``lvb_rope_kv_write``)."""
 
-        _rope_write_kv(self.cache, layer_id, qkv, q_heads, kv_heads, positions, cos, sin, self.tables, self.stride,
-                       self.computed, self.query_start, self.request_indices, self.device)
+        _rope_write_kv(self.cache, layer_id, qkv, q_heads, kv_heads, positions, cos, sin, self.tables.data_ptr(),
+                       self.stride, self.computed.data_ptr(), self.query_start.data_ptr(),
+                       self.request_indices.data_ptr(), self.device)
 
     def forward(self, layer_id: str, query: Tensor, key: Tensor, value: Tensor, *, scale: float,
                 write_kv: bool = True) -> Tensor:
