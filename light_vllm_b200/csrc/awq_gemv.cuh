@@ -10,8 +10,9 @@
 //
 //   x is split per (token, group) into four int8 limbs,
 //   x = a (x0 + x1 / 128 + x2 / 128^2 + x3 / 128^3), a a power of two
-//   (exact for every fp16 value within 2^17 of the group's largest); for
-//   each group
+//   (exact for every fp16 value within 2^17 of the group's largest); a group
+//   where at least G/8 elements exceed a sixteenth of its largest skips x2 and
+//   x3 (see awqi8::needs_four_limbs); for each group
 //     D_l  = sum q x_l                               (dp4a, exact in int32)
 //     v_hi = 128 D0 + D1 - z * sum(128 x0 + x1),  v_lo = 128 D2 + D3 - z * sum(128 x2 + x3)
 //     acc += s * (a / 128) * (v_hi + v_lo / 128^2)   (fp32)
@@ -186,13 +187,14 @@ __global__ void __launch_bounds__(kCtaThreads) awq_gemv_kernel(const __grid_cons
       for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
       const int e = awqi8::limb_exponent(amax);
       const float inv_a = ldexpf(1.f, -e);
-      int s01 = 0, s23 = 0;
+      int s01 = 0, s23 = 0, large = 0;
       uint32_t *trow = limb_sm + static_cast<size_t>(t) * kLimbs * range_quads;
       for (int i = 4 * lane; i < G; i += 128) {
         const uint2 raw = load4(i);
         const __half2 h0 = *reinterpret_cast<const __half2 *>(&raw.x);
         const __half2 h1 = *reinterpret_cast<const __half2 *>(&raw.y);
         const float v[4] = {__low2float(h0), __high2float(h0), __low2float(h1), __high2float(h1)};
+        large += awqi8::large_count(v, amax);
         uint32_t w[kLimbs] = {};
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
@@ -212,8 +214,10 @@ __global__ void __launch_bounds__(kCtaThreads) awq_gemv_kernel(const __grid_cons
       for (int o = 16; o > 0; o >>= 1) {
         s01 += __shfl_xor_sync(0xffffffffu, s01, o);
         s23 += __shfl_xor_sync(0xffffffffu, s23, o);
+        large += __shfl_xor_sync(0xffffffffu, large, o);
       }
-      if (lane == 0) scal_sm[pr] = make_int4(__float_as_int(ldexpf(1.f, e - 7)), s01, s23, 0);
+      if (lane == 0)
+        scal_sm[pr] = make_int4(__float_as_int(ldexpf(1.f, e - 7)), s01, s23, awqi8::needs_four_limbs(large, G));
     }
   }
   consumers_sync();
@@ -228,6 +232,10 @@ __global__ void __launch_bounds__(kCtaThreads) awq_gemv_kernel(const __grid_cons
   }
   int group = g0, run_in_group = 0;
   bool ok = mbar_wait(sz_bar, 0, abort_flag);
+  // Per token: whether the current group uses four limbs (uniform over the CTA).
+  int four[MT];
+#pragma unroll
+  for (int t = 0; t < MT; ++t) four[t] = scal_sm[t].w;
 
   for (int st = 0; st < nstages && ok; ++st) {
     const int slot = st % kStages;
@@ -253,6 +261,7 @@ __global__ void __launch_bounds__(kCtaThreads) awq_gemv_kernel(const __grid_cons
         for (int t = 0; t < MT; ++t) {
 #pragma unroll
           for (int j = 0; j < kLimbs; ++j) {
+            if (j >= 2 && !four[t]) break;  // two-limb group
             const uint4 *l = reinterpret_cast<const uint4 *>(limb_sm + (static_cast<size_t>(t) * kLimbs + j) * range_quads + q0);
             const uint4 a = l[0], b = l[1];
             int acc_l = d[t][j];
@@ -276,7 +285,7 @@ __global__ void __launch_bounds__(kCtaThreads) awq_gemv_kernel(const __grid_cons
           for (int t = 0; t < MT; ++t) {
             const int4 sc = scal_sm[(group - g0) * MT + t];
             const int v_hi = 128 * d[t][0] + d[t][1] - z * sc.y;
-            const int v_lo = 128 * d[t][2] + d[t][3] - z * sc.z;
+            const int v_lo = four[t] ? 128 * d[t][2] + d[t][3] - z * sc.z : 0;
             const float v = fmaf(static_cast<float>(v_lo), 1.f / 16384.f, static_cast<float>(v_hi));
             acc[t] = fmaf(s * __int_as_float(sc.x), v, acc[t]);
 #pragma unroll
@@ -284,6 +293,10 @@ __global__ void __launch_bounds__(kCtaThreads) awq_gemv_kernel(const __grid_cons
           }
           ++group;
           run_in_group = 0;
+          if (group < g1) {
+#pragma unroll
+            for (int t = 0; t < MT; ++t) four[t] = scal_sm[(group - g0) * MT + t].w;
+          }
         }
       }
     }

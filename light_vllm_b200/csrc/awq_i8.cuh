@@ -30,11 +30,15 @@
 // modeling/quantization/awq.py:433-450).
 //
 // Kernels:
-//   awq_act_limbs_kernel  one warp per (group, token row): the limbs of x, in
-//                         the K-major 64-byte-swizzled tile layout the MMA
-//                         reads (pre-swizzled, so a stage is one bulk copy),
-//                         and per (group, token) the scale a / 128 and the
-//                         integer sums of 128 x0 + x1 and 128 x2 + x3.
+//   awq_act_limbs_kernel  one CTA per group, one warp per token row: the
+//                         limbs of x, in the K-major 64-byte-swizzled tile
+//                         layout the MMA reads (pre-swizzled, so a stage is
+//                         one bulk copy), per (group, token) the scale a / 128
+//                         and the integer sums of 128 x0 + x1 and 128 x2 + x3,
+//                         and per group whether any token needs limbs 2-3.
+//                         Stages whose groups need only limbs 0-1 (ordinary
+//                         activations) copy half the limb tile, issue N = 32
+//                         MMAs and drain two accumulators per group.
 //   awq_i8_kernel<BN>     persistent, one CTA per SM over (128-column tile,
 //                         K split) units; launched as a programmatic
 //                         dependent of the limb kernel so that its set-up and
@@ -84,6 +88,23 @@ __device__ __forceinline__ void split_limbs(float r, int (&l)[kLimbs]) {
   }
 }
 
+// Whether a (token, group) needs all four limbs.  Two limbs keep 15 bits
+// relative to the group's largest element |x|max, an absolute rounding of at
+// most |x|max 2^-15 per element.  That is negligible against the group's
+// contribution unless the group's typical elements are much smaller than its
+// largest -- a massive activation (10^3-10^4 x the rest, as real Qwen2
+// checkpoints have in a few channels) beside ordinary values.  The test is
+// robust to a few such outliers: when fewer than G / 8 elements exceed
+// |x|max / 16, the bulk of the group is small next to |x|max and all four limbs
+// are used; otherwise (Gaussian-like groups: ~85 % of elements exceed a
+// sixteenth of the maximum) the last two limbs are skipped.
+__device__ __forceinline__ int large_count(const float (&v)[4], float amax) {
+  const float cut = amax * 0.0625f;
+  return (fabsf(v[0]) > cut) + (fabsf(v[1]) > cut) + (fabsf(v[2]) > cut) + (fabsf(v[3]) > cut);
+}
+
+__device__ __forceinline__ int needs_four_limbs(int large, int G) { return large * 8 < G ? 1 : 0; }
+
 // Power-of-two exponent e of the limb scale a = 2^e: the smallest a with
 // amax / a <= 127 (a = 1 for an all-zero group).
 __device__ __forceinline__ int limb_exponent(float amax) {
@@ -129,7 +150,8 @@ struct I8Params {
   const uint8_t *qpack;      // packed codes [n_tiles][k_chunks][128][16 B]
   const uint32_t *szpack;    // [n_tiles][groups][128] (scale bits | zero << 16)
   const int8_t *limbs;       // [K/64][kLimbs BN][64 B], pre-swizzled
-  const int4 *scal;          // [groups][BN]: (bits of a / 128, sum of 128 x0 + x1, sum of 128 x2 + x3, 0)
+  const int4 *scal;          // [groups][BN]: (bits of a / 128, sum of 128 x0 + x1, sum of 128 x2 + x3, four)
+  const int *four;           // [groups]: the group's stages use limbs 2 and 3
   const uint16_t *bias;      // may be null
   uint16_t *y;
   uint32_t *semaphores;
@@ -152,24 +174,28 @@ __host__ __device__ __forceinline__ int sw64(int row, int byte) {
   return row * 64 + ((((byte >> 4) ^ ((row >> 1) & 3)) & 3) << 4) + (byte & 15);
 }
 
-// One warp per (group, token row t < BN); rows t >= M are written as zeros.
-// Each lane handles 4 consecutive k (one quad) per pass and stores the quad's
-// limbs as one 32-bit word per limb, bytes in the (0, 2, 1, 3) order; limb l
-// of token t is row l * BN + t of the tile.  x rows are x_stride elements
-// apart.  gated: x holds merged [gate | up] rows of 2K values and the
-// activation is fp16(silu(gate) * up), rounded exactly as lvb_silu_mul
-// rounds it (the SiLU-mul fused into the down projection).
+// One CTA per group, one warp per token row t < BN; rows t >= M are written
+// as zeros.  Each lane handles 4 consecutive k (one quad) per pass and stores
+// the quad's limbs as one 32-bit word per limb, bytes in the (0, 2, 1, 3)
+// order; limb l of token t is row l * BN + t of the tile.  x rows are
+// x_stride elements apart.  gated: x holds merged [gate | up] rows of 2K
+// values and the activation is fp16(silu(gate) * up), rounded exactly as
+// lvb_silu_mul rounds it (the SiLU-mul fused into the down projection).
+// four[g] = whether any token of group g needs its last two limbs
+// (needs_four_limbs); stages whose groups need none copy and multiply only
+// limbs 0 and 1.
 template <int BN>
-__global__ void __launch_bounds__(32) awq_act_limbs_kernel(const uint16_t *__restrict__ x, int64_t x_stride, int gated,
-                                                           int8_t *__restrict__ limbs, int4 *__restrict__ scal,
-                                                           int M, int K, int G) {
+__global__ void __launch_bounds__(32 * BN) awq_act_limbs_kernel(const uint16_t *__restrict__ x, int64_t x_stride,
+                                                                int gated, int8_t *__restrict__ limbs,
+                                                                int4 *__restrict__ scal, int *__restrict__ four,
+                                                                int M, int K, int G) {
   // The AWQ kernel that reads these limbs may start now and overlap this
   // grid; it waits for its completion before touching the outputs.  This
   // grid waits for the kernel that produced x.
   pdl_entry();
   const int g = blockIdx.x;
-  const int t = blockIdx.y;
-  const int lane = threadIdx.x;
+  const int t = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
   const bool row_ok = t < M;
   const uint16_t *xrow = x + static_cast<size_t>(row_ok ? t : 0) * x_stride + static_cast<size_t>(g) * G;
   // Four consecutive activations at k = g * G + i.
@@ -198,12 +224,13 @@ __global__ void __launch_bounds__(32) awq_act_limbs_kernel(const uint16_t *__res
   for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
   const int e = limb_exponent(amax);
   const float inv_a = ldexpf(1.f, -e);
-  int s01 = 0, s23 = 0;
+  int s01 = 0, s23 = 0, large = 0;
   for (int i = 4 * lane; i < G; i += 128) {
     const uint2 raw = load4(i);
     const __half2 h0 = *reinterpret_cast<const __half2 *>(&raw.x);
     const __half2 h1 = *reinterpret_cast<const __half2 *>(&raw.y);
     const float v[4] = {__low2float(h0), __high2float(h0), __low2float(h1), __high2float(h1)};
+    large += large_count(v, amax);
     uint32_t w[kLimbs] = {};
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
@@ -224,8 +251,12 @@ __global__ void __launch_bounds__(32) awq_act_limbs_kernel(const uint16_t *__res
   for (int o = 16; o > 0; o >>= 1) {
     s01 += __shfl_xor_sync(0xffffffffu, s01, o);
     s23 += __shfl_xor_sync(0xffffffffu, s23, o);
+    large += __shfl_xor_sync(0xffffffffu, large, o);
   }
-  if (lane == 0) scal[static_cast<size_t>(g) * BN + t] = make_int4(__float_as_int(ldexpf(1.f, e - 7)), s01, s23, 0);
+  const int mine = row_ok ? needs_four_limbs(large, G) : 0;
+  if (lane == 0) scal[static_cast<size_t>(g) * BN + t] = make_int4(__float_as_int(ldexpf(1.f, e - 7)), s01, s23, mine);
+  const int any = __syncthreads_or(lane == 0 && mine);
+  if (threadIdx.x == 0) four[g] = any ? 1 : 0;
 }
 
 // y tile store: shared [BN][128] fp16 -> global y at (column n0, row 0);
@@ -383,9 +414,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                             p.qpack + (static_cast<size_t>(w.tile) * p.k_chunks + 2 * blk0) * kChunkBytes, bytes,
                             &full[slot]);
           } else {
-            const uint32_t bytes = static_cast<uint32_t>(nb * C::kLimbChunkBytes);
-            mbar_arrive_expect_tx(&full[slot], bytes);
-            awqd::bulk_load(stage, p.limbs + static_cast<size_t>(blk0) * C::kLimbChunkBytes, bytes, &full[slot]);
+            // Limbs 0-1 are the first half of each 64-k chunk (rows 0 .. 2 BN - 1):
+            // a two-limb stage copies only those halves.
+            const int g0 = blk0 >> p.bpg_shift;
+            const bool four = p.four[g0] || ((blk0 + nb - 1) >> p.bpg_shift) != g0 && p.four[g0 + 1];
+            if (four) {
+              const uint32_t bytes = static_cast<uint32_t>(nb * C::kLimbChunkBytes);
+              mbar_arrive_expect_tx(&full[slot], bytes);
+              awqd::bulk_load(stage, p.limbs + static_cast<size_t>(blk0) * C::kLimbChunkBytes, bytes, &full[slot]);
+            } else {
+              mbar_arrive_expect_tx(&full[slot], static_cast<uint32_t>(nb * C::kLimbChunkBytes / 2));
+              for (int b = 0; b < nb; ++b)
+                awqd::bulk_load(stage + b * C::kLimbChunkBytes,
+                                p.limbs + static_cast<size_t>(blk0 + b) * C::kLimbChunkBytes,
+                                static_cast<uint32_t>(C::kLimbChunkBytes / 2), &full[slot]);
+            }
           }
         }
       }
@@ -402,8 +445,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     // bookkeeping overlap the other issuer's MMAs in the tensor pipe.  Stage
     // accumulator ds = parity and A stages s = gs % 4 are private to one
     // issuer, and tcgen05.commit tracks only the issuing thread's MMAs.
+    // The limb kernel's flags are read below: wait for it (it precedes this grid).
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     if (lane == 0) {
-      constexpr uint32_t idesc = umma_idesc_i8(kTileN, kLimbs * BN);
+      constexpr uint32_t idesc4 = umma_idesc_i8(kTileN, kLimbs * BN);
+      constexpr uint32_t idesc2 = umma_idesc_i8(kTileN, 2 * BN);  // limbs 0 and 1 only
       const int parity = warp == 2 ? 0 : 1;
       bool ok = true;
       int gs = 0;
@@ -424,6 +470,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           tc_fence_after();
+          const int blk0 = w.b_begin + ls * kStageBlocks;
+          const int g0 = blk0 >> p.bpg_shift;
+          const bool four = p.four[g0] || ((blk0 + nb - 1) >> p.bpg_shift) != g0 && p.four[g0 + 1];
+          const uint32_t idesc = four ? idesc4 : idesc2;
           for (int b = 0; b < nb; ++b) {
             const uint32_t d = d0 + (b >> p.bpg_shift) * C::kGroupCols;
             const uint64_t bd = bdesc0 + static_cast<uint64_t>((b * C::kLimbChunkBytes) >> 4);
@@ -545,6 +595,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int ds = gs & (C::kDStages - 1);
         if (!__all_sync(0xffffffffu, mbar_wait(&d_full[ds], (gs / C::kDStages) & 1, abort_flag))) { ok = false; break; }
         tc_fence_after();
+        const int sg0 = w.g_begin + ls * gps_full;
+        const bool four = p.four[sg0] || (ng > 1 && p.four[sg0 + 1]);
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
           if (j >= ng) break;
@@ -553,19 +605,30 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t dcol = tmem + lane_base + ds * C::kDStageCols + j * C::kGroupCols;
 #pragma unroll
           for (int h = 0; h < BN / 16; ++h) {
-            uint32_t d0[16], d1[16], d2[16], d3[16];
+            uint32_t d0[16], d1[16];
             tmem_ld_32x32b_x16(dcol + h * 16, d0);
             tmem_ld_32x32b_x16(dcol + BN + h * 16, d1);
-            tmem_ld_32x32b_x16(dcol + 2 * BN + h * 16, d2);
-            tmem_ld_32x32b_x16(dcol + 3 * BN + h * 16, d3);
-            tmem_wait_ld();
+            if (four) {  // uniform over the warp
+              uint32_t d2[16], d3[16];
+              tmem_ld_32x32b_x16(dcol + 2 * BN + h * 16, d2);
+              tmem_ld_32x32b_x16(dcol + 3 * BN + h * 16, d3);
+              tmem_wait_ld();
 #pragma unroll
-            for (int t = 0; t < 16; ++t) {
-              const int4 sc4 = sc[j * BN + h * 16 + t];
-              const int v_hi = static_cast<int>(d0[t]) * 128 + static_cast<int>(d1[t]) - z * sc4.y;
-              const int v_lo = static_cast<int>(d2[t]) * 128 + static_cast<int>(d3[t]) - z * sc4.z;
-              const float v = fmaf(static_cast<float>(v_lo), 1.f / 16384.f, static_cast<float>(v_hi));
-              acc[h * 16 + t] = fmaf(s * __int_as_float(sc4.x), v, acc[h * 16 + t]);
+              for (int t = 0; t < 16; ++t) {
+                const int4 sc4 = sc[j * BN + h * 16 + t];
+                const int v_hi = static_cast<int>(d0[t]) * 128 + static_cast<int>(d1[t]) - z * sc4.y;
+                const int v_lo = static_cast<int>(d2[t]) * 128 + static_cast<int>(d3[t]) - z * sc4.z;
+                const float v = fmaf(static_cast<float>(v_lo), 1.f / 16384.f, static_cast<float>(v_hi));
+                acc[h * 16 + t] = fmaf(s * __int_as_float(sc4.x), v, acc[h * 16 + t]);
+              }
+            } else {
+              tmem_wait_ld();
+#pragma unroll
+              for (int t = 0; t < 16; ++t) {
+                const int4 sc4 = sc[j * BN + h * 16 + t];
+                const int v_hi = static_cast<int>(d0[t]) * 128 + static_cast<int>(d1[t]) - z * sc4.y;
+                acc[h * 16 + t] = fmaf(s * __int_as_float(sc4.x), static_cast<float>(v_hi), acc[h * 16 + t]);
+              }
             }
           }
         }

@@ -336,8 +336,8 @@ bool i8_eligible(int64_t m, int64_t k, int64_t n, int64_t g) {
 
 struct I8Plan {
   int bn = 0, splits = 1;
-  size_t sem_bytes = 0, part_bytes = 0, limb_bytes = 0, scal_bytes = 0;
-  size_t total() const { return sem_bytes + part_bytes + limb_bytes + scal_bytes; }
+  size_t sem_bytes = 0, part_bytes = 0, limb_bytes = 0, scal_bytes = 0, flag_bytes = 0;
+  size_t total() const { return sem_bytes + part_bytes + limb_bytes + scal_bytes + flag_bytes; }
 };
 
 size_t round256(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
@@ -350,7 +350,8 @@ I8Plan i8_plan(int64_t m, int64_t k, const PackedShape &sh, int64_t g, int sms, 
   const int bn = 16;
   p.limb_bytes = round256(static_cast<size_t>(k) * lvb::awqi8::kLimbs * bn);
   p.scal_bytes = round256(static_cast<size_t>(sh.groups) * bn * sizeof(int4));
-  if (p.limb_bytes + p.scal_bytes > max_ws) return p;
+  p.flag_bytes = round256(static_cast<size_t>(sh.groups) * sizeof(int));
+  if (p.limb_bytes + p.scal_bytes + p.flag_bytes > max_ws) return p;
   p.bn = bn;
   const int bpg = static_cast<int>(g / 64);
   const size_t sem = round256(static_cast<size_t>(sh.n_tiles) * 4);
@@ -358,7 +359,7 @@ I8Plan i8_plan(int64_t m, int64_t k, const PackedShape &sh, int64_t g, int sms, 
   const int max_splits = sh.groups < 16 ? sh.groups : 16;
   for (int sp = 1; sp <= max_splits; ++sp) {
     const size_t part = sp > 1 ? static_cast<size_t>(sh.n_tiles) * sp * bn * lvb::awqi8::kTileN * sizeof(float) : 0;
-    if ((sp > 1 ? sem : 0) + part + p.limb_bytes + p.scal_bytes > max_ws) continue;
+    if ((sp > 1 ? sem : 0) + part + p.limb_bytes + p.scal_bytes + p.flag_bytes > max_ws) continue;
     const long long ctas = static_cast<long long>(sh.n_tiles) * sp;
     const long long waves = (ctas + sms - 1) / sms;
     const long long cost = waves * ((sh.groups + sp - 1) / sp) * bpg;
@@ -383,8 +384,9 @@ int launch_awq_i8(const I8Plan &plan, const PackedShape &sh, const uint16_t *x, 
   if (rc != LVB_OK) return rc;
   int8_t *limbs = reinterpret_cast<int8_t *>(ws + plan.sem_bytes + plan.part_bytes);
   int4 *scal = reinterpret_cast<int4 *>(ws + plan.sem_bytes + plan.part_bytes + plan.limb_bytes);
-  cudaError_t e = launch_pdl(lvb::awqi8::awq_act_limbs_kernel<BN>, dim3(sh.groups, BN), dim3(32), 0, stream, x,
-                             x_stride, gated, limbs, scal, static_cast<int>(m), static_cast<int>(k),
+  int *four = reinterpret_cast<int *>(ws + plan.sem_bytes + plan.part_bytes + plan.limb_bytes + plan.scal_bytes);
+  cudaError_t e = launch_pdl(lvb::awqi8::awq_act_limbs_kernel<BN>, dim3(sh.groups), dim3(32 * BN), 0, stream, x,
+                             x_stride, gated, limbs, scal, four, static_cast<int>(m), static_cast<int>(k),
                              static_cast<int>(g));
   if (e != cudaSuccess) return cuda_fail(e, "awq_act_limbs_kernel launch");
   lvb::awqi8::I8Params p{};
@@ -392,6 +394,7 @@ int launch_awq_i8(const I8Plan &plan, const PackedShape &sh, const uint16_t *x, 
   p.szpack = groups;
   p.limbs = limbs;
   p.scal = scal;
+  p.four = four;
   p.bias = bias;
   p.y = y;
   p.semaphores = reinterpret_cast<uint32_t *>(ws);
@@ -1630,6 +1633,12 @@ int lvb_lm_head_argmax(const uint16_t *hidden, int64_t hidden_stride, int64_t to
   a.out_value = out_value;
   const int tok = tokens <= 1 ? 1 : tokens <= 2 ? 2 : 4;
   const size_t smem = static_cast<size_t>(tok) * hidden_size * 4;
+  // The kernels are opted in once to kHeadMaxSmem of dynamic shared memory
+  // (the attribute caps every later launch, so it is set to the largest).
+  constexpr size_t kHeadMaxSmem = 200 * 1024;
+  if (smem > kHeadMaxSmem)
+    return fail(LVB_ERR_UNSUPPORTED, "lm_head argmax: %d rows x %lld hidden values exceed shared memory", tok,
+                (long long)hidden_size);
   // Up to four CTAs per SM, as many as the fp32 hidden rows let fit.
   int per_sm = static_cast<int>((200 * 1024) / (smem + 4096));
   if (per_sm > 4) per_sm = 4;
@@ -1641,19 +1650,19 @@ int lvb_lm_head_argmax(const uint16_t *hidden, int64_t hidden_stride, int64_t to
   cudaError_t e;
   if (tok == 1) {
     static bool done[kMaxDevices] = {false};
-    rc = ensure_smem(lvb::q2::lm_head_argmax_kernel<1>, static_cast<int>(smem), dev, done);
+    rc = ensure_smem(lvb::q2::lm_head_argmax_kernel<1>, static_cast<int>(kHeadMaxSmem), dev, done);
     if (rc != LVB_OK) return rc;
     e = launch_pdl(lvb::q2::lm_head_argmax_kernel<1>, dim3(static_cast<unsigned>(ctas)), dim3(lvb::q2::kHeadThreads),
                    smem, st, a);
   } else if (tok == 2) {
     static bool done[kMaxDevices] = {false};
-    rc = ensure_smem(lvb::q2::lm_head_argmax_kernel<2>, static_cast<int>(smem), dev, done);
+    rc = ensure_smem(lvb::q2::lm_head_argmax_kernel<2>, static_cast<int>(kHeadMaxSmem), dev, done);
     if (rc != LVB_OK) return rc;
     e = launch_pdl(lvb::q2::lm_head_argmax_kernel<2>, dim3(static_cast<unsigned>(ctas)), dim3(lvb::q2::kHeadThreads),
                    smem, st, a);
   } else {
     static bool done[kMaxDevices] = {false};
-    rc = ensure_smem(lvb::q2::lm_head_argmax_kernel<4>, static_cast<int>(smem), dev, done);
+    rc = ensure_smem(lvb::q2::lm_head_argmax_kernel<4>, static_cast<int>(kHeadMaxSmem), dev, done);
     if (rc != LVB_OK) return rc;
     e = launch_pdl(lvb::q2::lm_head_argmax_kernel<4>, dim3(static_cast<unsigned>(ctas)), dim3(lvb::q2::kHeadThreads),
                    smem, st, a);
