@@ -654,7 +654,8 @@ def decode_cpu_baseline(torch, budget_s: float = 20.0) -> dict:
                                       f"extrapolated, plus the lm_head GEMV on 1/8 of the vocabulary x 8"}
 
 
-def decode_detail(torch, device, rank: int, world: int, dist, steps: int, warmup: int, with_cpu: bool) -> dict:
+def decode_detail(torch, device, rank: int, world: int, dist, steps: int, warmup: int, with_cpu: bool,
+                  batches: str | None = None) -> dict:
     from light_vllm_b200.qwen2 import Qwen2Shape
 
     from light_vllm_b200.qwen2 import RankLayout
@@ -673,14 +674,14 @@ def decode_detail(torch, device, rank: int, world: int, dist, steps: int, warmup
     shape3 = Qwen2Shape(**QWEN2_7B)
     why = tp_layout_error(shape3)
     if why is None:
-        cfg3 = decode_case(torch, shape3, rank, world, device, (1, 16, 64, 256), 1024, 128, warmup, dist,
-                           random_kv=True)
+        sizes = tuple(int(b) for b in batches.split(",")) if batches else (1, 16, 64, 256)
+        cfg3 = decode_case(torch, shape3, rank, world, device, sizes, 1024, 128, warmup, dist, random_kv=True)
         out["config3_qwen2.5_7b_awq"] = {"tp": world, "steps": cfg3, "prompt_tokens": 1024, "decode_steps": 128,
                                          "kv": "fp16 pages N(0,1) standing in for the 1024-token prompt's K/V",
                                          "allocated_gb_after": round(torch.cuda.memory_allocated(device) / 1e9, 2)}
     else:
         out["config3_qwen2.5_7b_awq"] = {"tp": world, "skipped": f"no TP={world} layout: {why}"}
-    if True:  # BASELINE config 4 (TP = 2 / 4 / 8); TP = 1 fits one B200 (~128 GB) and anchors the scaling curve
+    if not batches:  # BASELINE config 4 (TP = 2 / 4 / 8); TP = 1 fits one B200 (~128 GB) and anchors the scaling curve
         shape4 = Qwen2Shape(**QWEN2_72B)
         why = tp_layout_error(shape4)
         if why is None:
@@ -692,8 +693,9 @@ def decode_detail(torch, device, rank: int, world: int, dist, steps: int, warmup
             out["config4_qwen2.5_72b_awq"] = {"tp": world, "skipped": f"no TP={world} layout: {why}"}
     shape5 = Qwen2Shape(**dict(QWEN2_14B, intermediate_size=14336 if world == 8 else 13824))
     why = tp_layout_error(shape5)
-    out["config5_qwen2.5_14b_awq_mixed"] = (mixed_step_case(torch, shape5, rank, world, device, 5, dist)
-                                            if why is None else {"tp": world, "skipped": f"no TP={world} layout: {why}"})
+    if not batches:
+        out["config5_qwen2.5_14b_awq_mixed"] = (mixed_step_case(torch, shape5, rank, world, device, 5, dist)
+                                                if why is None else {"tp": world, "skipped": f"no TP={world} layout: {why}"})
     out.update({
            "timing": "one CUDA graph per batch size: embedding, 4 AWQ projections, RoPE, K/V write, paged "
                      "attention, SiLU-mul, 2 fused all-reduce+add+RMSNorm per layer, lm_head, greedy pick; "
@@ -716,6 +718,8 @@ def main() -> int:
                     help="AWQ detail shapes as 'm,k,n[;m,k,n...]' (group 128)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline (profiling)")
     ap.add_argument("--no-decode", action="store_true", help="skip the Qwen2 decode-step detail")
+    ap.add_argument("--decode-batches", default=None,
+                    help="config-3 batch sizes only, e.g. '1,16' (profiling; skips configs 4 and 5)")
     ap.add_argument("--no-reference-gpu", action="store_true",
                     help="skip timing light-vllm's own GPU paths (CUDA AWQ extension, Triton attention)")
     args = ap.parse_args()
@@ -746,7 +750,8 @@ def main() -> int:
 
     peaks = measured_peaks()
     if args.only == "decode":
-        detail = decode_detail(torch, device, rank, world, dist, args.steps, args.warmup, with_cpu=not args.no_cpu)
+        detail = decode_detail(torch, device, rank, world, dist, args.steps, args.warmup, with_cpu=not args.no_cpu,
+                               batches=args.decode_batches)
         if rank == 0:
             print(json.dumps({"decode": detail}), flush=True)
         if dist is not None:
