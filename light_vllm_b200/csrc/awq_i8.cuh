@@ -49,6 +49,10 @@
 //                 even stages; warp 11 issues the odd stages
 //     warps 3..6  code expanders: q nibbles -> int8 A columns in TMEM
 //     warps 7..10 drain: per group, int32 D -> fp32 accumulators; epilogue
+// Accumulators: a ring of four TMEM slots of one limb pair (N = 32) for two
+// groups each; a stage takes one slot (limbs 0-1), or two when it needs limbs
+// 2-3, which run as separate N = 32 MMAs over the upper half of each limb
+// chunk into the second slot.
 // The codes use the packed layout of awq_decode.cuh.  Within a 32-k run, word
 // w masked with 0x0F0F0F0F gives the bytes of k = 4w, 4w+2, 4w+1, 4w+3, and
 // the word shifted right by 4 those of k = 16+4w, 16+4w+2, 16+4w+1, 16+4w+3;
@@ -117,16 +121,19 @@ __device__ __forceinline__ int limb_exponent(float amax) {
 // MMA issuer, code expanders and drain synchronise once per stage.
 template <int BN>
 struct I8Config {
-  // Stage accumulators in flight: the drain of stage s overlaps the MMAs of
-  // the next stage (two fit beside the A stages in tensor memory).
-  static constexpr int kDStages = 2;
+  // Accumulator slots: a ring of four, each holding limbs 0-1 (N = 2 BN
+  // columns) of up to two groups.  A stage takes one slot, or two when it
+  // needs limbs 2-3 (the second slot holds those), so the drain of a stage
+  // overlaps the MMAs of the next several.
+  static constexpr int kDStages = 4;
   static constexpr int kLimbRows = kLimbs * BN;              // (limb, token) rows of B
   static constexpr int kLimbChunkBytes = kLimbRows * 64;     // one 64-k chunk of the limb tile
+  static constexpr int kLimbHiOffset = 2 * BN * 64;          // limbs 2-3: rows 2 BN .. 4 BN - 1 of a chunk
   static constexpr int kLimbStageBytes = kStageBlocks * kLimbChunkBytes;
   static constexpr int kQOff = kLimbStageBytes;              // limb tile first (1024-aligned)
   static constexpr int kStageBytes = ((kQOff + kQStageBytes) + 1023) / 1024 * 1024;
-  static constexpr int kGroupCols = kLimbRows;               // int32 accumulator columns per group
-  static constexpr int kDStageCols = 2 * kGroupCols;         // up to two groups per stage
+  static constexpr int kGroupCols = 2 * BN;                  // int32 accumulator columns per group and limb pair
+  static constexpr int kDStageCols = 2 * kGroupCols;         // one slot: up to two groups
   static constexpr int kACol = kDStages * kDStageCols;
   static constexpr int kBarOff = kStages * kStageBytes;
   // full, done, a_full (stages), d_full, d_empty (stage accumulators), fin (per issuer).
@@ -448,40 +455,49 @@ __global__ void __launch_bounds__(kThreads, 1)
     // The limb kernel's flags are read below: wait for it (it precedes this grid).
     asm volatile("griddepcontrol.wait;" ::: "memory");
     if (lane == 0) {
-      constexpr uint32_t idesc4 = umma_idesc_i8(kTileN, kLimbs * BN);
-      constexpr uint32_t idesc2 = umma_idesc_i8(kTileN, 2 * BN);  // limbs 0 and 1 only
+      constexpr uint32_t idesc = umma_idesc_i8(kTileN, 2 * BN);  // one limb pair: N = 2 BN
       const int parity = warp == 2 ? 0 : 1;
       bool ok = true;
       int gs = 0;
+      int sc = 0;  // accumulator slots taken by every stage so far (both issuers count all stages)
       for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
         const Unit w = unit_of(u, p);
         for (int ls = 0; ls < w.nstages; ++ls, ++gs) {
+          const int nb = min(kStageBlocks, w.nblocks - ls * kStageBlocks);
+          const int blk0 = w.b_begin + ls * kStageBlocks;
+          const int g0 = blk0 >> p.bpg_shift;
+          const bool four = p.four[g0] || ((blk0 + nb - 1) >> p.bpg_shift) != g0 && p.four[g0 + 1];
+          const int slot0 = sc;
+          sc += four ? 2 : 1;
           if ((gs & 1) != parity) continue;
           const int s = gs % kStages;
-          const int ds = gs & (C::kDStages - 1);
-          const int nb = min(kStageBlocks, w.nblocks - ls * kStageBlocks);
+          const int ds0 = slot0 & (C::kDStages - 1), ds1 = (slot0 + 1) & (C::kDStages - 1);
           const uint64_t bdesc0 = awqd::umma_desc_kmajor_sw64(smem_u32(smem + s * C::kStageBytes));
           const uint32_t a0 = tmem + C::kACol + s * kAStageCols;
-          const uint32_t d0 = tmem + ds * C::kDStageCols;
           if (!mbar_wait(&full[s], (gs / kStages) & 1, abort_flag) ||
               !mbar_wait(&a_full[s], (gs / kStages) & 1, abort_flag) ||
-              (gs >= C::kDStages && !mbar_wait(&d_empty[ds], ((gs / C::kDStages) - 1) & 1, abort_flag))) {
+              (slot0 >= C::kDStages && !mbar_wait(&d_empty[ds0], ((slot0 / C::kDStages) - 1) & 1, abort_flag)) ||
+              (four && slot0 + 1 >= C::kDStages &&
+               !mbar_wait(&d_empty[ds1], (((slot0 + 1) / C::kDStages) - 1) & 1, abort_flag))) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const int blk0 = w.b_begin + ls * kStageBlocks;
-          const int g0 = blk0 >> p.bpg_shift;
-          const bool four = p.four[g0] || ((blk0 + nb - 1) >> p.bpg_shift) != g0 && p.four[g0 + 1];
-          const uint32_t idesc = four ? idesc4 : idesc2;
           for (int b = 0; b < nb; ++b) {
-            const uint32_t d = d0 + (b >> p.bpg_shift) * C::kGroupCols;
+            const uint32_t dg = (b >> p.bpg_shift) * C::kGroupCols;
             const uint64_t bd = bdesc0 + static_cast<uint64_t>((b * C::kLimbChunkBytes) >> 4);
-            umma_i8_ts(d, a0 + b * 16, bd, idesc, (b & ((1 << p.bpg_shift) - 1)) == 0 ? 0u : 1u);
-            umma_i8_ts(d, a0 + b * 16 + 8, bd + 2, idesc, 1u);  // +32 bytes: the block's second 32-k run
+            const uint32_t first = (b & ((1 << p.bpg_shift) - 1)) == 0 ? 0u : 1u;
+            umma_i8_ts(tmem + ds0 * C::kDStageCols + dg, a0 + b * 16, bd, idesc, first);
+            umma_i8_ts(tmem + ds0 * C::kDStageCols + dg, a0 + b * 16 + 8, bd + 2, idesc, 1u);  // second 32-k run
+            if (four) {  // limbs 2-3 into the stage's second slot
+              const uint64_t bh = bd + static_cast<uint64_t>(C::kLimbHiOffset >> 4);
+              umma_i8_ts(tmem + ds1 * C::kDStageCols + dg, a0 + b * 16, bh, idesc, first);
+              umma_i8_ts(tmem + ds1 * C::kDStageCols + dg, a0 + b * 16 + 8, bh + 2, idesc, 1u);
+            }
           }
           umma_commit(&done[s]);
-          umma_commit(&d_full[ds]);
+          umma_commit(&d_full[ds0]);
+          if (four) umma_commit(&d_full[ds1]);
         }
       }
       // Tensor memory is freed only after every issued MMA has completed.
@@ -561,6 +577,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     asm volatile("griddepcontrol.wait;" ::: "memory");  // the scalars come from the prologue launch
     bool ok = true;
     int gs = 0;
+    int slots = 0;  // accumulator slots taken by the stages drained so far
     uint2 sz_next = make_uint2(0u, 0u);
     uint2 sz_unit_next = make_uint2(0u, 0u);  // first stage of the next unit, loaded a unit ahead
     int u = blockIdx.x;
@@ -592,17 +609,23 @@ __global__ void __launch_bounds__(kThreads, 1)
           sz_next = sz_unit_next;
         }
         const int4 *sc = reinterpret_cast<const int4 *>(scal_sm + (gs & 1) * C::kScalSlotBytes);  // one per token
-        const int ds = gs & (C::kDStages - 1);
-        if (!__all_sync(0xffffffffu, mbar_wait(&d_full[ds], (gs / C::kDStages) & 1, abort_flag))) { ok = false; break; }
-        tc_fence_after();
         const int sg0 = w.g_begin + ls * gps_full;
         const bool four = p.four[sg0] || (ng > 1 && p.four[sg0 + 1]);
+        const int ds0 = slots & (C::kDStages - 1), ds1 = (slots + 1) & (C::kDStages - 1);
+        if (!__all_sync(0xffffffffu, mbar_wait(&d_full[ds0], (slots / C::kDStages) & 1, abort_flag) &&
+                                         (!four || mbar_wait(&d_full[ds1], ((slots + 1) / C::kDStages) & 1,
+                                                             abort_flag)))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
           if (j >= ng) break;
           const float s = __half2float(__ushort_as_half(static_cast<uint16_t>(sz[j] & 0xFFFFu)));
           const int z = static_cast<int>(sz[j] >> 16);
-          const uint32_t dcol = tmem + lane_base + ds * C::kDStageCols + j * C::kGroupCols;
+          const uint32_t dcol = tmem + lane_base + ds0 * C::kDStageCols + j * C::kGroupCols;
+          const uint32_t dcol_hi = tmem + lane_base + ds1 * C::kDStageCols + j * C::kGroupCols;
 #pragma unroll
           for (int h = 0; h < BN / 16; ++h) {
             uint32_t d0[16], d1[16];
@@ -610,8 +633,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_ld_32x32b_x16(dcol + BN + h * 16, d1);
             if (four) {  // uniform over the warp
               uint32_t d2[16], d3[16];
-              tmem_ld_32x32b_x16(dcol + 2 * BN + h * 16, d2);
-              tmem_ld_32x32b_x16(dcol + 3 * BN + h * 16, d3);
+              tmem_ld_32x32b_x16(dcol_hi + h * 16, d2);
+              tmem_ld_32x32b_x16(dcol_hi + BN + h * 16, d3);
               tmem_wait_ld();
 #pragma unroll
               for (int t = 0; t < 16; ++t) {
@@ -634,7 +657,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&d_empty[ds]);
+        if (lane == 0) {
+          mbar_arrive(&d_empty[ds0]);
+          if (four) mbar_arrive(&d_empty[ds1]);
+        }
+        slots += four ? 2 : 1;
       }
       // ---- epilogue of the unit ----
       ok = __all_sync(0xffffffffu, ok) && !*abort_flag;
