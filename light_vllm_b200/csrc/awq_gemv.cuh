@@ -27,10 +27,11 @@
 // producer streams the range's codes -- contiguous in the packed layout --
 // into a ring of shared-memory stages with bulk async copies (mbarrier
 // complete_tx) from the moment the CTA starts; meanwhile the consumers wait
-// for the kernel that produced x (programmatic dependent launch), stage the
-// range's activations (a few KB, L2-resident, every load issued at once) in
-// shared memory and build their limbs there -- one warp per (group, token) --
-// so no separate prologue launch and no global limb buffer exist.  Consumers then read their
+// for the kernel that produced x (programmatic dependent launch), read the
+// range's activations (a few KB, L2-resident; a warp issues the loads of four
+// (group, token) pairs before using them) and build their limbs in shared
+// memory -- so no separate prologue launch and no global limb buffer exist.
+// Groups of up to 256 k.  Consumers then read their
 // column's 16 bytes per run from shared memory and the limbs as broadcasts.
 // Splits combine through per-split fp32 partials and a semaphore: the last
 // CTA of a tile sums them in split order (deterministic), adds the bias and
@@ -83,13 +84,7 @@ struct GemvSmem {
     return scal_off(gps, rpg) + static_cast<size_t>(gps) * MT * 16;
   }
   __host__ __device__ static size_t bar_off(int gps, int rpg) { return sz_off(gps, rpg) + static_cast<size_t>(gps) * kThreads * 4; }
-  // The range's activations as fp16 [MT][gps * rpg * 32], staged before the limbs are built.
-  __host__ __device__ static size_t xs_off(int gps, int rpg) {
-    return (bar_off(gps, rpg) + (2 * kStages + 1) * 8 + 16 + 15) / 16 * 16;
-  }
-  __host__ __device__ static size_t bytes(int gps, int rpg) {
-    return xs_off(gps, rpg) + static_cast<size_t>(MT) * gps * rpg * 32 * 2;
-  }
+  __host__ __device__ static size_t bytes(int gps, int rpg) { return bar_off(gps, rpg) + (2 * kStages + 1) * 8 + 16; }
 };
 
 __device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kThreads) : "memory"); }
@@ -162,82 +157,90 @@ __global__ void __launch_bounds__(kCtaThreads) awq_gemv_kernel(const __grid_cons
   // have started during its tail): wait for it, then build this range's limbs.
   pdl_wait();
   {
-    // Stage the range's activations (MT rows x range_k values, 16-byte loads,
-    // all issued before any is used), then build the limbs from shared memory.
+    // Limbs of the range, one warp per (group, token) pair.  A warp takes its
+    // pairs kPairBatch at a time and issues every activation load of a batch
+    // before using any (one L2 round trip per batch, not two per pair); each
+    // lane holds 4 consecutive k per 128 of the group (groups of up to 256).
+    constexpr int kPairBatch = 4;
+    constexpr int kWarpsC = kThreads / 32;
     const int G = p.G;
     const int ng = g1 - g0;
-    const int range_k = ng * G;
-    const int vecs = range_k / 8;
-    __half *xs = reinterpret_cast<__half *>(smem + S::xs_off(p.groups_per_split, rpg));
-    for (int i = tid; i < MT * vecs; i += kThreads) {
-      const int t = i / vecs, c = i - t * vecs;
-      uint4 v = make_uint4(0u, 0u, 0u, 0u);
-      if (t < p.M) {
-        const uint16_t *src = p.x + static_cast<size_t>(t) * p.x_stride + static_cast<size_t>(g0) * G + c * 8;
-        v = *reinterpret_cast<const uint4 *>(src);
-        if (p.gated) {
-          const uint4 u = *reinterpret_cast<const uint4 *>(src + p.K);
-          const __half2 *gh = reinterpret_cast<const __half2 *>(&v);
-          const __half2 *uh = reinterpret_cast<const __half2 *>(&u);
-          uint4 o;
-          __half2 *oh = reinterpret_cast<__half2 *>(&o);
+    const int pairs = ng * MT;
+    auto load4 = [&](int gg, int t, int i) -> uint2 {
+      if (t >= p.M || i >= G) return make_uint2(0u, 0u);
+      const uint16_t *src = p.x + static_cast<size_t>(t) * p.x_stride + static_cast<size_t>(g0 + gg) * G + i;
+      const uint2 gv = *reinterpret_cast<const uint2 *>(src);
+      if (!p.gated) return gv;
+      const uint2 uv = *reinterpret_cast<const uint2 *>(src + p.K);
+      const float2 ga = __half22float2(*reinterpret_cast<const __half2 *>(&gv.x));
+      const float2 gb = __half22float2(*reinterpret_cast<const __half2 *>(&gv.y));
+      const float2 ua = __half22float2(*reinterpret_cast<const __half2 *>(&uv.x));
+      const float2 ub = __half22float2(*reinterpret_cast<const __half2 *>(&uv.y));
+      const __half2 a0 = __floats2half2_rn(silu_times(ga.x, ua.x), silu_times(ga.y, ua.y));
+      const __half2 a1 = __floats2half2_rn(silu_times(gb.x, ub.x), silu_times(gb.y, ub.y));
+      return make_uint2(*reinterpret_cast<const uint32_t *>(&a0), *reinterpret_cast<const uint32_t *>(&a1));
+    };
+    for (int base = warp; base < pairs; base += kWarpsC * kPairBatch) {
+      uint2 xv[kPairBatch][2];
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float2 gf = __half22float2(gh[e]), uf = __half22float2(uh[e]);
-            oh[e] = __floats2half2_rn(silu_times(gf.x, uf.x), silu_times(gf.y, uf.y));
+      for (int b = 0; b < kPairBatch; ++b) {
+        const int pr = base + kWarpsC * b;
+        const int gg = pr / MT, t = pr - (pr / MT) * MT;
+#pragma unroll
+        for (int c = 0; c < 2; ++c) xv[b][c] = pr < pairs ? load4(gg, t, 4 * lane + 128 * c) : make_uint2(0u, 0u);
+      }
+#pragma unroll
+      for (int b = 0; b < kPairBatch; ++b) {
+        const int pr = base + kWarpsC * b;
+        if (pr >= pairs) break;  // uniform over the warp
+        const int gg = pr / MT, t = pr - gg * MT;
+        float v[2][4];
+        float amax = 0.f;
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          const __half2 h0 = *reinterpret_cast<const __half2 *>(&xv[b][c].x);
+          const __half2 h1 = *reinterpret_cast<const __half2 *>(&xv[b][c].y);
+          v[c][0] = __low2float(h0);
+          v[c][1] = __high2float(h0);
+          v[c][2] = __low2float(h1);
+          v[c][3] = __high2float(h1);
+          amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[c][0]), fabsf(v[c][1])), fmaxf(fabsf(v[c][2]), fabsf(v[c][3]))));
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        const int e = awqi8::limb_exponent(amax);
+        const float inv_a = ldexpf(1.f, -e);
+        int s01 = 0, s23 = 0, large = 0;
+        uint32_t *trow = limb_sm + static_cast<size_t>(t) * kLimbs * range_quads;
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          const int i = 4 * lane + 128 * c;
+          if (i >= G) break;
+          large += awqi8::large_count(v[c], amax);
+          uint32_t w[kLimbs] = {};
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            int l[kLimbs];
+            awqi8::split_limbs(v[c][q] * inv_a, l);
+            s01 += l[0] * 128 + l[1];
+            s23 += l[2] * 128 + l[3];
+            const int pos = ((q & 1) << 1) | (q >> 1);  // byte of k-offset q in the quad
+#pragma unroll
+            for (int j = 0; j < kLimbs; ++j) w[j] |= (static_cast<uint32_t>(l[j]) & 0xFFu) << (8 * pos);
           }
-          v = o;
+          const int quad = (gg * G + i) >> 2;
+#pragma unroll
+          for (int j = 0; j < kLimbs; ++j) trow[static_cast<size_t>(j) * range_quads + quad] = w[j];
         }
-      }
-      reinterpret_cast<uint4 *>(xs)[static_cast<size_t>(t) * vecs + c] = v;
-    }
-    consumers_sync();
-    for (int pr = warp; pr < ng * MT; pr += kThreads / 32) {
-      const int gg = pr / MT, t = pr - gg * MT;
-      const __half *xg = xs + static_cast<size_t>(t) * range_k + gg * G;
-      float amax = 0.f;
-      for (int i = 4 * lane; i < G; i += 128) {
-        const uint2 raw = *reinterpret_cast<const uint2 *>(xg + i);
-        const __half2 h0 = *reinterpret_cast<const __half2 *>(&raw.x);
-        const __half2 h1 = *reinterpret_cast<const __half2 *>(&raw.y);
-        amax = fmaxf(amax, fmaxf(fmaxf(fabsf(__low2float(h0)), fabsf(__high2float(h0))),
-                                 fmaxf(fabsf(__low2float(h1)), fabsf(__high2float(h1)))));
-      }
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-      const int e = awqi8::limb_exponent(amax);
-      const float inv_a = ldexpf(1.f, -e);
-      int s01 = 0, s23 = 0, large = 0;
-      uint32_t *trow = limb_sm + static_cast<size_t>(t) * kLimbs * range_quads;
-      for (int i = 4 * lane; i < G; i += 128) {
-        const uint2 raw = *reinterpret_cast<const uint2 *>(xg + i);
-        const __half2 h0 = *reinterpret_cast<const __half2 *>(&raw.x);
-        const __half2 h1 = *reinterpret_cast<const __half2 *>(&raw.y);
-        const float v[4] = {__low2float(h0), __high2float(h0), __low2float(h1), __high2float(h1)};
-        large += awqi8::large_count(v, amax);
-        uint32_t w[kLimbs] = {};
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          int l[kLimbs];
-          awqi8::split_limbs(v[q] * inv_a, l);
-          s01 += l[0] * 128 + l[1];
-          s23 += l[2] * 128 + l[3];
-          const int pos = ((q & 1) << 1) | (q >> 1);  // byte of k-offset q in the quad
-#pragma unroll
-          for (int j = 0; j < kLimbs; ++j) w[j] |= (static_cast<uint32_t>(l[j]) & 0xFFu) << (8 * pos);
+        for (int o = 16; o > 0; o >>= 1) {
+          s01 += __shfl_xor_sync(0xffffffffu, s01, o);
+          s23 += __shfl_xor_sync(0xffffffffu, s23, o);
+          large += __shfl_xor_sync(0xffffffffu, large, o);
         }
-        const int quad = (gg * G + i) >> 2;
-#pragma unroll
-        for (int j = 0; j < kLimbs; ++j) trow[static_cast<size_t>(j) * range_quads + quad] = w[j];
+        if (lane == 0)
+          scal_sm[pr] = make_int4(__float_as_int(ldexpf(1.f, e - 7)), s01, s23, awqi8::needs_four_limbs(large, G));
       }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        s01 += __shfl_xor_sync(0xffffffffu, s01, o);
-        s23 += __shfl_xor_sync(0xffffffffu, s23, o);
-        large += __shfl_xor_sync(0xffffffffu, large, o);
-      }
-      if (lane == 0)
-        scal_sm[pr] = make_int4(__float_as_int(ldexpf(1.f, e - 7)), s01, s23, awqi8::needs_four_limbs(large, G));
     }
   }
   consumers_sync();

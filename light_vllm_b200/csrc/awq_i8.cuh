@@ -80,6 +80,7 @@ constexpr int kIssuer2Warp = 11;                      // second MMA issuer (odd 
 constexpr int kThreads = 12 * 32;
 constexpr int kTmemCols = 512;
 constexpr int kLimbs = 4;                             // int8 limbs per activation
+constexpr int kMaxFlagGroups = 2048;                  // groups whose flags are staged in shared memory
 
 // x / a (exact in fp32: a power-of-two scaling of an fp16 value) into
 // kLimbs int8 limbs, x / a = sum_i l[i] / 128^i; each residual is exact.
@@ -137,7 +138,8 @@ struct I8Config {
   static constexpr int kACol = kDStages * kDStageCols;
   static constexpr int kBarOff = kStages * kStageBytes;
   // full, done, a_full (stages), d_full, d_empty (stage accumulators), fin (per issuer).
-  static constexpr int kNumBars = 3 * kStages + 2 * kDStages + 2;
+  // + flags: the per-group four-limb flags are in shared memory.
+  static constexpr int kNumBars = 3 * kStages + 2 * kDStages + 2 + 1;
   static_assert((kDStages & (kDStages - 1)) == 0, "power-of-two accumulator ring");
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;
   // Per drain warp, two stage slots of per-token scalars (2 groups x BN x 16 bytes).
@@ -147,7 +149,9 @@ struct I8Config {
   // Output tile [BN tokens][128 columns] fp16, written to y by one TMA store.
   static constexpr int kYOff = (kScalOff + kScalBytes + 127) / 128 * 128;
   static constexpr int kYBytes = BN * kTileN * 2;
-  static constexpr int kSmemBytes = kYOff + kYBytes + 1024;
+  // Four-limb flag of every group (one byte each), staged once per CTA.
+  static constexpr int kFlagOff = kYOff + kYBytes;
+  static constexpr int kSmemBytes = kFlagOff + kMaxFlagGroups + 1024;
   static_assert(BN == 16, "int8 path covers 16-row token tiles (N = 4 limbs x 16 rows)");
   static_assert(kACol + kStages * kAStageCols <= kTmemCols, "tensor memory budget");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
@@ -361,6 +365,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t *d_full = a_full + kStages;        // a stage accumulator holds finished groups
   uint64_t *d_empty = d_full + C::kDStages;      // the drain has read a stage accumulator
   uint64_t *fin = d_empty + C::kDStages;         // [2]: every MMA of each issuer has completed
+  uint64_t *flags_bar = fin + 2;                 // the group flags are in shared memory
+  const uint8_t *four_sm = smem + C::kFlagOff;
+  // Four-limb flag of group g (shared memory when every group fits there).
+  auto four_of = [&](int g) -> bool { return p.groups <= kMaxFlagGroups ? four_sm[g] != 0 : p.four[g] != 0; };
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + C::kMiscOff);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + C::kMiscOff + 8);
   volatile int *last_flag = reinterpret_cast<volatile int *>(smem + C::kMiscOff + 16);
@@ -381,6 +389,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     mbar_init(&fin[0], 1);
     mbar_init(&fin[1], 1);
+    mbar_init(flags_bar, 32);
     *abort_flag = 0;
     *last_flag = 0;
     fence_barrier_init();
@@ -396,11 +405,20 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0 || warp == 1) {
     // ---------------- producers ----------------
+    if (warp == 1) {
+      // The activation limbs and group flags come from the preceding prologue
+      // launch, which this grid may overlap (programmatic dependent launch):
+      // wait for it before the first limb copy; then stage the group flags.
+      // The codes do not depend on it.
+      asm volatile("griddepcontrol.wait;" ::: "memory");
+      if (p.groups <= kMaxFlagGroups) {
+        uint8_t *dst = smem + C::kFlagOff;
+        for (int g = lane; g < p.groups; g += 32) dst[g] = p.four[g] ? 1 : 0;
+      }
+      __syncwarp();
+      mbar_arrive(flags_bar);
+    }
     if (lane == 0) {
-      // The activation limbs come from the preceding prologue launch, which
-      // this grid may overlap (programmatic dependent launch): wait for it
-      // before the first limb copy.  The codes do not depend on it.
-      if (warp == 1) asm volatile("griddepcontrol.wait;" ::: "memory");
       bool ok = true;
       int gs = 0;
       for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
@@ -424,7 +442,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             // Limbs 0-1 are the first half of each 64-k chunk (rows 0 .. 2 BN - 1):
             // a two-limb stage copies only those halves.
             const int g0 = blk0 >> p.bpg_shift;
-            const bool four = p.four[g0] || ((blk0 + nb - 1) >> p.bpg_shift) != g0 && p.four[g0 + 1];
+            const bool four = four_of(g0) || ((blk0 + nb - 1) >> p.bpg_shift) != g0 && four_of(g0 + 1);
             if (four) {
               const uint32_t bytes = static_cast<uint32_t>(nb * C::kLimbChunkBytes);
               mbar_arrive_expect_tx(&full[slot], bytes);
@@ -457,7 +475,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       constexpr uint32_t idesc = umma_idesc_i8(kTileN, 2 * BN);  // one limb pair: N = 2 BN
       const int parity = warp == 2 ? 0 : 1;
-      bool ok = true;
+      bool ok = mbar_wait(flags_bar, 0, abort_flag);
       int gs = 0;
       int sc = 0;  // accumulator slots taken by every stage so far (both issuers count all stages)
       for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
@@ -466,7 +484,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int nb = min(kStageBlocks, w.nblocks - ls * kStageBlocks);
           const int blk0 = w.b_begin + ls * kStageBlocks;
           const int g0 = blk0 >> p.bpg_shift;
-          const bool four = p.four[g0] || ((blk0 + nb - 1) >> p.bpg_shift) != g0 && p.four[g0 + 1];
+          const bool four = four_of(g0) || ((blk0 + nb - 1) >> p.bpg_shift) != g0 && four_of(g0 + 1);
           const int slot0 = sc;
           sc += four ? 2 : 1;
           if ((gs & 1) != parity) continue;
@@ -575,7 +593,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         ng > 1 ? __ldg(szrow + static_cast<size_t>(g0 + 1) * kTileN) : 0u);
     };
     asm volatile("griddepcontrol.wait;" ::: "memory");  // the scalars come from the prologue launch
-    bool ok = true;
+    bool ok = __all_sync(0xffffffffu, mbar_wait(flags_bar, 0, abort_flag));
     int gs = 0;
     int slots = 0;  // accumulator slots taken by the stages drained so far
     uint2 sz_next = make_uint2(0u, 0u);
@@ -610,7 +628,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         const int4 *sc = reinterpret_cast<const int4 *>(scal_sm + (gs & 1) * C::kScalSlotBytes);  // one per token
         const int sg0 = w.g_begin + ls * gps_full;
-        const bool four = p.four[sg0] || (ng > 1 && p.four[sg0 + 1]);
+        const bool four = four_of(sg0) || (ng > 1 && four_of(sg0 + 1));
         const int ds0 = slots & (C::kDStages - 1), ds1 = (slots + 1) & (C::kDStages - 1);
         if (!__all_sync(0xffffffffu, mbar_wait(&d_full[ds0], (slots / C::kDStages) & 1, abort_flag) &&
                                          (!four || mbar_wait(&d_full[ds1], ((slots + 1) / C::kDStages) & 1,

@@ -444,7 +444,7 @@ int launch_awq_i8(const I8Plan &plan, const PackedShape &sh, const uint16_t *x, 
 constexpr int64_t kGemvFastRows = 1;
 
 bool gemv_eligible(int64_t m, int64_t k, int64_t n, int64_t g) {
-  return m >= 1 && m <= lvb::awqg::kMaxM && g % 32 == 0 && k % g == 0 && k % 64 == 0 && n % 128 == 0 &&
+  return m >= 1 && m <= lvb::awqg::kMaxM && g % 32 == 0 && g <= 256 && k % g == 0 && k % 64 == 0 && n % 128 == 0 &&
          (m <= kGemvFastRows || !(m <= 32 && (g == 128 || g == 256)));
 }
 
