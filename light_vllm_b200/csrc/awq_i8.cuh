@@ -44,7 +44,8 @@
 //                         dependent of the limb kernel so that its set-up and
 //                         code streaming overlap it:
 //     warp 0      bulk copies of the packed codes (16 KB per 256-k stage)
-//     warp 1      bulk copies of the limb tiles (4 BN rows x 256 k)
+//     warp 1      bulk copies of the limb tiles (limbs 0-1, and 2-3 when the
+//                 stage needs them: 2 BN rows x 256 k each)
 //     warp 2      TMEM allocation and the tcgen05.mma.kind::i8 issuer of
 //                 even stages; warp 11 issues the odd stages
 //     warps 3..6  code expanders: q nibbles -> int8 A columns in TMEM
@@ -128,8 +129,9 @@ struct I8Config {
   // overlaps the MMAs of the next several.
   static constexpr int kDStages = 4;
   static constexpr int kLimbRows = kLimbs * BN;              // (limb, token) rows of B
-  static constexpr int kLimbChunkBytes = kLimbRows * 64;     // one 64-k chunk of the limb tile
-  static constexpr int kLimbHiOffset = 2 * BN * 64;          // limbs 2-3: rows 2 BN .. 4 BN - 1 of a chunk
+  static constexpr int kLimbChunkBytes = kLimbRows * 64;     // the four limbs of one 64-k chunk
+  static constexpr int kPairChunkBytes = 2 * BN * 64;        // one limb pair of one 64-k chunk (2 BN rows)
+  static constexpr int kPairStageStride = kStageBlocks * kPairChunkBytes;  // limbs 2-3 of a stage in shared memory
   static constexpr int kLimbStageBytes = kStageBlocks * kLimbChunkBytes;
   static constexpr int kQOff = kLimbStageBytes;              // limb tile first (1024-aligned)
   static constexpr int kStageBytes = ((kQOff + kQStageBytes) + 1023) / 1024 * 1024;
@@ -160,7 +162,7 @@ struct I8Config {
 struct I8Params {
   const uint8_t *qpack;      // packed codes [n_tiles][k_chunks][128][16 B]
   const uint32_t *szpack;    // [n_tiles][groups][128] (scale bits | zero << 16)
-  const int8_t *limbs;       // [K/64][kLimbs BN][64 B], pre-swizzled
+  const int8_t *limbs;       // [2 limb pairs][K/64][2 BN][64 B], pre-swizzled
   const int4 *scal;          // [groups][BN]: (bits of a / 128, sum of 128 x0 + x1, sum of 128 x2 + x3, four)
   const int *four;           // [groups]: the group's stages use limbs 2 and 3
   const uint16_t *bias;      // may be null
@@ -254,9 +256,13 @@ __global__ void __launch_bounds__(32 * BN) awq_act_limbs_kernel(const uint16_t *
       for (int j = 0; j < kLimbs; ++j) w[j] |= (static_cast<uint32_t>(l[j]) & 0xFFu) << (8 * pos);
     }
     const int k = g * G + i;
-    int8_t *tile = limbs + static_cast<size_t>(k >> 6) * (kLimbs * BN * 64);
+    // Limb pair q = j / 2 of 64-k chunk c at q * (K / 64) * 2 KB + c * 2 KB;
+    // rows (j % 2) * BN + t of the pair's [2 BN][64 B] chunk tile.
+    const size_t pair_stride = static_cast<size_t>(K >> 6) * (2 * BN * 64);
+    int8_t *tile = limbs + static_cast<size_t>(k >> 6) * (2 * BN * 64);
 #pragma unroll
-    for (int j = 0; j < kLimbs; ++j) *reinterpret_cast<uint32_t *>(tile + sw64(j * BN + t, k & 63)) = w[j];
+    for (int j = 0; j < kLimbs; ++j)
+      *reinterpret_cast<uint32_t *>(tile + (j >> 1) * pair_stride + sw64((j & 1) * BN + t, k & 63)) = w[j];
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
@@ -439,21 +445,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                             p.qpack + (static_cast<size_t>(w.tile) * p.k_chunks + 2 * blk0) * kChunkBytes, bytes,
                             &full[slot]);
           } else {
-            // Limbs 0-1 are the first half of each 64-k chunk (rows 0 .. 2 BN - 1):
-            // a two-limb stage copies only those halves.
+            // Limb pair 0 (limbs 0-1) of the stage's chunks is one contiguous
+            // run of the limb tile, pair 1 another; a two-limb stage copies
+            // only the first.
             const int g0 = blk0 >> p.bpg_shift;
             const bool four = four_of(g0) || ((blk0 + nb - 1) >> p.bpg_shift) != g0 && four_of(g0 + 1);
-            if (four) {
-              const uint32_t bytes = static_cast<uint32_t>(nb * C::kLimbChunkBytes);
-              mbar_arrive_expect_tx(&full[slot], bytes);
-              awqd::bulk_load(stage, p.limbs + static_cast<size_t>(blk0) * C::kLimbChunkBytes, bytes, &full[slot]);
-            } else {
-              mbar_arrive_expect_tx(&full[slot], static_cast<uint32_t>(nb * C::kLimbChunkBytes / 2));
-              for (int b = 0; b < nb; ++b)
-                awqd::bulk_load(stage + b * C::kLimbChunkBytes,
-                                p.limbs + static_cast<size_t>(blk0 + b) * C::kLimbChunkBytes,
-                                static_cast<uint32_t>(C::kLimbChunkBytes / 2), &full[slot]);
-            }
+            const uint32_t bytes = static_cast<uint32_t>(nb * C::kPairChunkBytes);
+            mbar_arrive_expect_tx(&full[slot], four ? 2 * bytes : bytes);
+            const int8_t *src = p.limbs + static_cast<size_t>(blk0) * C::kPairChunkBytes;
+            awqd::bulk_load(stage, src, bytes, &full[slot]);
+            if (four)
+              awqd::bulk_load(stage + C::kPairStageStride, src + static_cast<size_t>(p.k_chunks / 2) * C::kPairChunkBytes,
+                              bytes, &full[slot]);
           }
         }
       }
@@ -503,12 +506,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_after();
           for (int b = 0; b < nb; ++b) {
             const uint32_t dg = (b >> p.bpg_shift) * C::kGroupCols;
-            const uint64_t bd = bdesc0 + static_cast<uint64_t>((b * C::kLimbChunkBytes) >> 4);
+            const uint64_t bd = bdesc0 + static_cast<uint64_t>((b * C::kPairChunkBytes) >> 4);
             const uint32_t first = (b & ((1 << p.bpg_shift) - 1)) == 0 ? 0u : 1u;
             umma_i8_ts(tmem + ds0 * C::kDStageCols + dg, a0 + b * 16, bd, idesc, first);
             umma_i8_ts(tmem + ds0 * C::kDStageCols + dg, a0 + b * 16 + 8, bd + 2, idesc, 1u);  // second 32-k run
             if (four) {  // limbs 2-3 into the stage's second slot
-              const uint64_t bh = bd + static_cast<uint64_t>(C::kLimbHiOffset >> 4);
+              const uint64_t bh = bd + static_cast<uint64_t>(C::kPairStageStride >> 4);
               umma_i8_ts(tmem + ds1 * C::kDStageCols + dg, a0 + b * 16, bh, idesc, first);
               umma_i8_ts(tmem + ds1 * C::kDStageCols + dg, a0 + b * 16 + 8, bh + 2, idesc, 1u);
             }
