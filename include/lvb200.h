@@ -119,6 +119,29 @@ LVB_API int lvb_awq_dequantize(const int32_t *qweight, const int32_t *qzeros, co
                        uint16_t *w, int64_t k, int64_t n, int64_t group_size,
                        lvb_stream_t stream);
 
+/* The QKV projection of a decode step with its epilogue: y = x W + bias over
+ * the packed layout (lvb_awq_linear_packed), and then, per token, the Qwen2
+ * half-rotation RoPE (lvb_rope_kv_write's arithmetic) applied to the query
+ * heads in y, the rotated key heads written to the token's paged cache slot
+ * and the value heads copied there -- the QKV epilogue of
+ * `Qwen2Attention.forward` (modeling/models/qwen2.py:380-411) with the K/V
+ * write of the attention step (runtime/execution/triton_paged_attention.py:
+ * 31-104, _qwen2_kernels.py:66-133), in the projection's own launch.  y holds
+ * merged [q | k | v] rows of (hq + 2 hkv) x head_size values (head size 64 or
+ * 128); its key and value heads are left unrotated.  Covers the one-row
+ * decode GEMV (m = 1); other shapes return LVB_ERR_UNSUPPORTED and the caller
+ * runs lvb_awq_linear_packed + lvb_rope_kv_write.  Positions outside the
+ * tables set LVB_DEVERR_INDEX. */
+LVB_API int lvb_awq_qkv_rope_packed(const uint16_t *x, const void *codes, const void *groups, const uint16_t *bias,
+                                    uint16_t *y, int64_t m, int64_t k, int64_t n, int64_t group_size,
+                                    void *workspace, size_t workspace_bytes, const int32_t *positions,
+                                    const uint16_t *cos_table, const uint16_t *sin_table, int64_t table_rows,
+                                    uint16_t *key_cache, uint16_t *value_cache, const int32_t *block_tables,
+                                    int64_t table_stride, const int32_t *num_computed,
+                                    const int32_t *query_start_loc, const int32_t *request_indices,
+                                    int64_t num_query_heads, int64_t num_kv_heads, int64_t head_size,
+                                    int64_t block_size, lvb_stream_t stream);
+
 /* Packed decode layout.  AWQScheme.prepare (modeling/quantization/awq.py:
  * 468-486) hands a backend the checkpoint once, after loading, so that it can
  * convert it (the protocol names Marlin-style backends, which repack); the

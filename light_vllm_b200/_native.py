@@ -56,6 +56,11 @@ PROTOTYPES: dict[str, tuple[object, tuple[object, ...]]] = {
     "lvb_awq_linear_packed": (
         _int, (_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _i64, _i64, _i64, _i64, _c_ptr, _size, _c_ptr),
     ),
+    "lvb_awq_qkv_rope_packed": (
+        _int,
+        (_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _i64, _i64, _i64, _i64, _c_ptr, _size, _c_ptr, _c_ptr, _c_ptr,
+         _i64, _c_ptr, _c_ptr, _c_ptr, _i64, _c_ptr, _c_ptr, _c_ptr, _i64, _i64, _i64, _i64, _c_ptr),
+    ),
     "lvb_awq_silu_linear_packed": (
         _int,
         (_c_ptr, _i64, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _i64, _i64, _i64, _i64, _c_ptr, _size, _c_ptr),

@@ -123,6 +123,37 @@ class B200AWQOperation:
         )
         return out.reshape(*inputs.shape[:-1], self.output_width)
 
+    def qkv_rope(self, inputs: Tensor, positions: Tensor, cos: Tensor, sin: Tensor, kv_args: tuple,
+                 q_heads: int, kv_heads: int, head_size: int) -> Tensor | None:
+        """The merged QKV projection with its decode epilogue in one launch
+        (``lvb_awq_qkv_rope_packed``): RoPE on the query heads of the output,
+        rotated keys and the values written to the tokens' paged cache slots.
+        ``kv_args`` = (key_cache, value_cache, block_tables, table_stride,
+        num_computed, query_start_loc, request_indices, block_size) as device
+        addresses.  Returns None when the shape is not covered (the caller
+        then runs the projection and ``lvb_rope_kv_write``)."""
+
+        if self.codes is None:
+            return None
+        flat = inputs.reshape(-1, self.inner)
+        if flat.dtype != torch.float16:
+            raise ValueError("B200 AWQ activations must be float16")
+        if not flat.is_contiguous() or flat.data_ptr() % 16:
+            flat = flat.contiguous()
+        rows = flat.shape[0]
+        out = torch.empty((rows, self.output_width), dtype=torch.float16, device=flat.device)
+        kc, vc, tables, stride, computed, qsl, req, block_size = kv_args
+        status = _native.library().lvb_awq_qkv_rope_packed(
+            flat.data_ptr(), self.codes.data_ptr(), self.groups.data_ptr(),
+            None if self.bias is None else self.bias.data_ptr(), out.data_ptr(), rows, self.inner,
+            self.output_width, self.group_size, self.workspace.data_ptr(), self.workspace.numel(),
+            positions.data_ptr(), cos.data_ptr(), sin.data_ptr(), cos.shape[0], kc, vc, tables, stride, computed,
+            qsl, req, q_heads, kv_heads, head_size, block_size, _native.stream_handle(flat.device))
+        if status == _native.LVB_ERR_UNSUPPORTED:
+            return None
+        _native.check(status, "lvb_awq_qkv_rope_packed")
+        return out
+
     def silu_mul_linear(self, gate_up: Tensor) -> Tensor:
         """``self(silu(gate) * up)`` for merged [gate | up] rows of 2 x inner
         values (the Qwen2 MLP's down projection after ``silu_and_mul``,

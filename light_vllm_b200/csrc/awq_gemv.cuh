@@ -53,6 +53,23 @@ constexpr int kStageBytes = kStageRuns * 128 * 16;
 constexpr int kMaxM = 4;
 using awqi8::kLimbs;
 
+// QKV epilogue (rope != 0): the output row is a merged QKV projection with
+// head size D (64 or 128, so a 128-column tile holds whole heads).  Query
+// heads are rotated (Qwen2 half rotation, fp32 from the fp16-rounded outputs,
+// one rounding: the arithmetic of rope_kv_write_kernel) and written to y;
+// key heads are rotated into the token's paged cache slot and value heads
+// copied there (y keeps them unrotated).
+struct GemvRope {
+  int rope;
+  const int32_t *positions;          // [M] RoPE position per token
+  const uint16_t *cos, *sin;         // [table_rows][D] fp16
+  uint16_t *key_cache, *value_cache;  // [blocks][bs][hkv][D]
+  const int32_t *tables;
+  int64_t table_stride;
+  const int32_t *computed, *qsl, *req;
+  int hq, hkv, D, bs, table_rows;
+};
+
 struct GemvParams {
   const uint8_t *qpack;    // [n_tiles][k_chunks][128][16 B]
   const uint32_t *szpack;  // [n_tiles][groups][128]: scale bits | zero << 16
@@ -66,7 +83,65 @@ struct GemvParams {
   int M, K, N, G;
   int groups, k_chunks, runs_per_group;
   int n_tiles, splits, groups_per_split;
+  GemvRope r;
 };
+
+__device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kThreads) : "memory"); }
+
+// Final outputs of column n for the MT token rows: y, or the QKV epilogue.
+// All 128 consumer threads of the CTA call it together (RoPE exchanges the
+// two halves of a head through shared memory).
+template <int MT>
+__device__ __forceinline__ void gemv_store(const GemvParams &p, int n, const float (&v)[MT]) {
+  if (!p.r.rope) {
+#pragma unroll
+    for (int t = 0; t < MT; ++t)
+      if (t < p.M) p.y[static_cast<size_t>(t) * p.N + n] = __half_as_ushort(__float2half_rn(v[t]));
+    return;
+  }
+  __shared__ __half xch[MT][kThreads];
+  const int tid = threadIdx.x;
+  const GemvRope &r = p.r;
+  const int D = r.D, half = D / 2;
+  const int head = n / D, i = n - head * D;
+  __half h[MT];
+#pragma unroll
+  for (int t = 0; t < MT; ++t) {
+    h[t] = __float2half_rn(v[t]);
+    xch[t][tid] = h[t];
+  }
+  consumers_sync();
+#pragma unroll
+  for (int t = 0; t < MT; ++t) {
+    if (t >= p.M) continue;
+    const int pos = r.positions[t];
+    if (pos < 0 || pos >= r.table_rows) {
+      if (tid == 0) record_device_error(LVB_DEVERR_INDEX);
+      continue;
+    }
+    const int q = r.req[t];
+    const int lp = r.computed[q] + (t - r.qsl[q]);
+    const int64_t slot =
+        static_cast<int64_t>(r.tables[static_cast<int64_t>(q) * r.table_stride + lp / r.bs]) * r.bs + lp % r.bs;
+    if (head < r.hq + r.hkv) {
+      const float self = __half2float(h[t]);
+      const float other = __half2float(xch[t][tid ^ half]);
+      const float c = __half2float(reinterpret_cast<const __half *>(r.cos)[static_cast<size_t>(pos) * D + i]);
+      const float sn = __half2float(reinterpret_cast<const __half *>(r.sin)[static_cast<size_t>(pos) * D + i]);
+      // Lower half x1 c1 + (-x2) s1, upper x2 c2 + x1 s2 (the standalone kernels' rope_rotate).
+      const __half o = __float2half_rn(rope_rotate(self, c, i < half ? -other : other, sn));
+      if (head < r.hq) {
+        p.y[static_cast<size_t>(t) * p.N + n] = __half_as_ushort(o);
+      } else {
+        r.key_cache[(static_cast<size_t>(slot) * r.hkv + (head - r.hq)) * D + i] = __half_as_ushort(o);
+        p.y[static_cast<size_t>(t) * p.N + n] = __half_as_ushort(h[t]);
+      }
+    } else {
+      r.value_cache[(static_cast<size_t>(slot) * r.hkv + (head - r.hq - r.hkv)) * D + i] = __half_as_ushort(h[t]);
+      p.y[static_cast<size_t>(t) * p.N + n] = __half_as_ushort(h[t]);
+    }
+  }
+}
 
 // Shared memory: code stages, limb words [MT][kLimbs][range_quads] (quad q =
 // k offset 4q of the range, bytes in the (0, 2, 1, 3) order), per [group][MT]
@@ -86,8 +161,6 @@ struct GemvSmem {
   __host__ __device__ static size_t bar_off(int gps, int rpg) { return sz_off(gps, rpg) + static_cast<size_t>(gps) * kThreads * 4; }
   __host__ __device__ static size_t bytes(int gps, int rpg) { return bar_off(gps, rpg) + (2 * kStages + 1) * 8 + 16; }
 };
-
-__device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kThreads) : "memory"); }
 
 template <int MT>
 __global__ void __launch_bounds__(kCtaThreads) awq_gemv_kernel(const __grid_constant__ GemvParams p) {
@@ -334,9 +407,10 @@ __global__ void __launch_bounds__(kCtaThreads) awq_gemv_kernel(const __grid_cons
   const int n = tile * kThreads + tid;
   if (p.splits == 1) {
     const float b = p.bias ? __half2float(__ushort_as_half(p.bias[n])) : 0.f;
+    float v[MT];
 #pragma unroll
-    for (int t = 0; t < MT; ++t)
-      if (t < p.M) p.y[static_cast<size_t>(t) * p.N + n] = __half_as_ushort(__float2half_rn(acc[t] + b));
+    for (int t = 0; t < MT; ++t) v[t] = acc[t] + b;
+    gemv_store<MT>(p, n, v);
     return;
   }
   float *part = p.partials + (static_cast<size_t>(tile) * p.splits + split) * p.M * kThreads;
@@ -373,9 +447,10 @@ __global__ void __launch_bounds__(kCtaThreads) awq_gemv_kernel(const __grid_cons
     }
   }
   const float b = p.bias ? __half2float(__ushort_as_half(p.bias[n])) : 0.f;
+  float v[MT];
 #pragma unroll
-  for (int t = 0; t < MT; ++t)
-    if (t < p.M) p.y[static_cast<size_t>(t) * p.N + n] = __half_as_ushort(__float2half_rn(sum[t] + b));
+  for (int t = 0; t < MT; ++t) v[t] = sum[t] + b;
+  gemv_store<MT>(p, n, v);
   if (tid == 0) p.semaphores[tile] = 0u;  // ready for the next call
 }
 

@@ -507,7 +507,8 @@ GemvPlan gemv_plan(int64_t m, int64_t k, const PackedShape &sh, int64_t g, int s
 template <int MT>
 int launch_awq_gemv(const GemvPlan &plan, const PackedShape &sh, const uint16_t *x, const uint8_t *codes,
                     const uint32_t *groups, const uint16_t *bias, uint16_t *y, int64_t m, int64_t k, int64_t n,
-                    int64_t g, uint8_t *ws, int dev, cudaStream_t stream, int64_t x_stride, int gated) {
+                    int64_t g, uint8_t *ws, int dev, cudaStream_t stream, int64_t x_stride, int gated,
+                    const lvb::awqg::GemvRope *rope = nullptr) {
   static bool smem_done[kMaxDevices] = {false};
   auto kernel = lvb::awqg::awq_gemv_kernel<MT>;
   int rc = ensure_smem(kernel, static_cast<int>(kGemvMaxSmem), dev, smem_done);
@@ -532,6 +533,7 @@ int launch_awq_gemv(const GemvPlan &plan, const PackedShape &sh, const uint16_t 
   p.n_tiles = sh.n_tiles;
   p.splits = plan.splits;
   p.groups_per_split = plan.gps;
+  if (rope != nullptr) p.r = *rope;
   cudaError_t e = launch_pdl(kernel, dim3(static_cast<unsigned>(sh.n_tiles), static_cast<unsigned>(plan.splits)),
                              dim3(lvb::awqg::kCtaThreads), plan.smem, stream, p);
   if (e != cudaSuccess) return cuda_fail(e, "awq_gemv_kernel launch");
@@ -895,6 +897,59 @@ int lvb_awq_linear_packed(const uint16_t *x, const void *codes, const void *grou
     default:
       return launch_awq_packed<256, 2, 2, false, 512, 224>(plan, sh, x, c, g, bias, y, m, k, n, group_size, ws, dev, s);
   }
+}
+
+int lvb_awq_qkv_rope_packed(const uint16_t *x, const void *codes, const void *groups, const uint16_t *bias,
+                            uint16_t *y, int64_t m, int64_t k, int64_t n, int64_t group_size, void *workspace,
+                            size_t workspace_bytes, const int32_t *positions, const uint16_t *cos_table,
+                            const uint16_t *sin_table, int64_t table_rows, uint16_t *key_cache,
+                            uint16_t *value_cache, const int32_t *block_tables, int64_t table_stride,
+                            const int32_t *num_computed, const int32_t *query_start_loc,
+                            const int32_t *request_indices, int64_t num_query_heads, int64_t num_kv_heads,
+                            int64_t head_size, int64_t block_size, lvb_stream_t stream) {
+  int rc = check_awq_shape(m, k, n, group_size);
+  if (rc != LVB_OK) return rc;
+  if (m == 0) return LVB_OK;
+  if (!x || !codes || !groups || !y || !positions || !cos_table || !sin_table || !key_cache || !value_cache ||
+      !block_tables || !num_computed || !query_start_loc || !request_indices)
+    return fail(LVB_ERR_INVALID, "QKV epilogue null pointer argument");
+  if (!aligned16(x) || !aligned16(codes) || !aligned16(groups) || (workspace && !aligned16(workspace)))
+    return fail(LVB_ERR_INVALID, "AWQ x, packed buffers and workspace must be 16-byte aligned");
+  if ((head_size != 64 && head_size != 128) || num_query_heads <= 0 || num_kv_heads <= 0 || block_size <= 0 ||
+      n != (num_query_heads + 2 * num_kv_heads) * head_size || table_rows <= 0)
+    return fail(LVB_ERR_UNSUPPORTED, "QKV epilogue covers head sizes 64 / 128 over merged [q | k | v] rows");
+  if (!gemv_eligible(m, k, n, group_size))
+    return fail(LVB_ERR_UNSUPPORTED, "QKV epilogue covers the one-row decode GEMV (m = 1)");
+  int dev = 0;
+  rc = current_device(&dev);
+  if (rc != LVB_OK) return rc;
+  const PackedShape sh = packed_shape(k, n, group_size);
+  const GemvPlan gp = gemv_plan(m, k, sh, group_size, sm_count(dev), workspace != nullptr ? workspace_bytes : 0);
+  if (gp.mt == 0) return fail(LVB_ERR_UNSUPPORTED, "QKV epilogue: the GEMV plan does not fit the workspace");
+  lvb::awqg::GemvRope r{};
+  r.rope = 1;
+  r.positions = positions;
+  r.cos = cos_table;
+  r.sin = sin_table;
+  r.key_cache = key_cache;
+  r.value_cache = value_cache;
+  r.tables = block_tables;
+  r.table_stride = table_stride;
+  r.computed = num_computed;
+  r.qsl = query_start_loc;
+  r.req = request_indices;
+  r.hq = static_cast<int>(num_query_heads);
+  r.hkv = static_cast<int>(num_kv_heads);
+  r.D = static_cast<int>(head_size);
+  r.bs = static_cast<int>(block_size);
+  r.table_rows = static_cast<int>(table_rows);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const uint8_t *c8 = static_cast<const uint8_t *>(codes);
+  const uint32_t *g8 = static_cast<const uint32_t *>(groups);
+  uint8_t *w8 = static_cast<uint8_t *>(workspace);
+  if (gp.mt == 1) return launch_awq_gemv<1>(gp, sh, x, c8, g8, bias, y, m, k, n, group_size, w8, dev, st, k, 0, &r);
+  if (gp.mt == 2) return launch_awq_gemv<2>(gp, sh, x, c8, g8, bias, y, m, k, n, group_size, w8, dev, st, k, 0, &r);
+  return launch_awq_gemv<4>(gp, sh, x, c8, g8, bias, y, m, k, n, group_size, w8, dev, st, k, 0, &r);
 }
 
 int lvb_awq_silu_linear_packed(const uint16_t *gate_up, int64_t gate_up_stride, const void *codes,

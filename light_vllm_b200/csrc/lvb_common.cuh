@@ -164,6 +164,15 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
+// One RoPE output element: x c + y s with the product y s rounded first and
+// x c added by one fused multiply-add (y is the partner element, negated for
+// the lower half).  Every RoPE path uses this one form, so that the fused
+// epilogues and the standalone kernels agree bit for bit whatever the
+// compiler would contract on its own.
+__device__ __forceinline__ float rope_rotate(float x, float c, float y, float s) {
+  return __fmaf_rn(x, c, __fmul_rn(y, s));
+}
+
 // Wait until at most N of this thread's committed cp.async groups are pending.
 template <int N>
 __device__ __forceinline__ void cp_async_wait_group() {

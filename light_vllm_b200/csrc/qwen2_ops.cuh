@@ -64,8 +64,8 @@ __global__ void __launch_bounds__(kRopeThreads) rope_qk_kernel(const __grid_cons
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
         const float v1 = __half2float(x1[e]), v2 = __half2float(x2[e]);
-        o1[e] = __float2half_rn(v1 * __half2float(c1[e]) + (-v2) * __half2float(s1[e]));
-        o2[e] = __float2half_rn(v2 * __half2float(c2[e]) + v1 * __half2float(s2[e]));
+        o1[e] = __float2half_rn(rope_rotate(v1, __half2float(c1[e]), -v2, __half2float(s1[e])));
+        o2[e] = __float2half_rn(rope_rotate(v2, __half2float(c2[e]), v1, __half2float(s2[e])));
       }
       *reinterpret_cast<uint4 *>(x + i) = oa;
       *reinterpret_cast<uint4 *>(x + i + half) = ob;
@@ -77,8 +77,8 @@ __global__ void __launch_bounds__(kRopeThreads) rope_qk_kernel(const __grid_cons
       __half *x = row + static_cast<size_t>(head) * a.D;
       const float x1 = __half2float(x[i]);
       const float x2 = __half2float(x[i + half]);
-      const float o1 = x1 * __half2float(cs[i]) + (-x2) * __half2float(sn[i]);
-      const float o2 = x2 * __half2float(cs[i + half]) + x1 * __half2float(sn[i + half]);
+      const float o1 = rope_rotate(x1, __half2float(cs[i]), -x2, __half2float(sn[i]));
+      const float o2 = rope_rotate(x2, __half2float(cs[i + half]), x1, __half2float(sn[i + half]));
       x[i] = __float2half_rn(o1);
       x[i + half] = __float2half_rn(o2);
     }
@@ -113,8 +113,8 @@ __device__ __forceinline__ void rope8(const uint4 xa, const uint4 xb, const uint
 #pragma unroll
   for (int e = 0; e < 8; ++e) {
     const float v1 = __half2float(x1[e]), v2 = __half2float(x2[e]);
-    o1[e] = __float2half_rn(v1 * __half2float(c1[e]) + (-v2) * __half2float(s1[e]));
-    o2[e] = __float2half_rn(v2 * __half2float(c2[e]) + v1 * __half2float(s2[e]));
+    o1[e] = __float2half_rn(rope_rotate(v1, __half2float(c1[e]), -v2, __half2float(s1[e])));
+    o2[e] = __float2half_rn(rope_rotate(v2, __half2float(c2[e]), v1, __half2float(s2[e])));
   }
 }
 

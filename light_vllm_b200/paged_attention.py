@@ -281,6 +281,17 @@ class B200PagedAttention:
                        self._table_stride, self._computed_ptr, self._query_start_ptr, self._request_indices_ptr,
                        self._device)
 
+    def kv_write_args(self, layer_id: str) -> tuple | None:
+        """Device addresses a projection epilogue needs to write this step's
+        K/V of ``layer_id`` (``lvb_awq_qkv_rope_packed``); None when the
+        fused write does not cover the cache (fp16 caches only)."""
+
+        if self._dtype != torch.float16:
+            return None
+        info = self._backend._layer_info(self._cache, layer_id)
+        return (info.args[0], info.args[1], self._tables_ptr, self._table_stride, self._computed_ptr,
+                self._query_start_ptr, self._request_indices_ptr, info.args[5])
+
     def launch(self, layer_id: str, query: Tensor, key: Tensor, value: Tensor, *, scale: float,
                out: Tensor, write_kv: bool = True) -> Tensor:
         """Enqueue the K/V write and the attention into ``out`` without the

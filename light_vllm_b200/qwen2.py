@@ -11,8 +11,10 @@ fewer than ranks: qwen2.py:290-318, tensor_parallel.py:248-330):
   x = embed(ids)                          lvb_embedding, masked per vocab shard
   x, residual = allreduce_add_rmsnorm(x, 0, input_layernorm)
   per layer:
-    qkv  = AWQ(x) + bias                  B200AWQScheme, merged QKV
-    rope(q, k) + K/V write                lvb_rope_kv_write (q in place, k, v to the pages)
+    qkv  = AWQ(x) + bias                  B200AWQScheme, merged QKV; at one row the
+    rope(q, k) + K/V write                RoPE and K/V write run in the QKV GEMV's
+                                          epilogue (lvb_awq_qkv_rope_packed), else
+                                          lvb_rope_kv_write (q in place, k, v to the pages)
     attn = attention.forward(q, ...)      B200PagedAttention (K/V already written)
     x, residual = allreduce_add_rmsnorm(AWQ_o(attn), residual, post_norm)
     x, residual = allreduce_add_rmsnorm(AWQ_down(silu(gate) * up), residual, next norm)
@@ -300,13 +302,27 @@ class Qwen2AWQRunner:
         residual = torch.zeros((t, s.hidden_size), dtype=torch.float16, device=self.device)
         x, residual = all_reduce_add_rms_norm(ws, self._embed(input_ids), residual, self.layers[0].ln_in, eps)
         for i, L in enumerate(self.layers):
-            qkv = L.qkv(x)
+            qkv = None
+            if fused_rope and t == 1 and hasattr(attention, "kv_write_args"):
+                # One-row decode: RoPE and the K/V write run in the QKV
+                # projection's own epilogue (qwen2.py:380-411).
+                kv_args = attention.kv_write_args(L.layer_id)
+                if kv_args is not None:
+                    qkv = L.qkv.qkv_rope(x, positions, self.cos, self.sin, kv_args, lay.q_heads, lay.kv_heads,
+                                         s.head_size)
+                rope_done = qkv is not None
+            else:
+                rope_done = False
+            if qkv is None:
+                qkv = L.qkv(x)
             q = qkv[:, :qd].view(t, lay.q_heads, s.head_size)
             k = qkv[:, qd:qd + kd].view(t, lay.kv_heads, s.head_size)
             v = qkv[:, qd + kd:qd + 2 * kd].view(t, lay.kv_heads, s.head_size)
             if fused_rope:
                 # RoPE fused with the K/V write (the QKV epilogue of qwen2.py:380-411)
-                attention.rope_write_kv(L.layer_id, qkv, lay.q_heads, lay.kv_heads, positions, self.cos, self.sin)
+                if not rope_done:
+                    attention.rope_write_kv(L.layer_id, qkv, lay.q_heads, lay.kv_heads, positions, self.cos,
+                                            self.sin)
                 attn = attention.forward(L.layer_id, q, k, v, scale=self.scale, write_kv=False)
             else:
                 self._rope(qkv, positions)
@@ -410,6 +426,16 @@ class StaticDecodeAttention:
 
     def advance(self) -> None:
         self.computed.add_(1)
+
+    def kv_write_args(self, layer_id: str) -> tuple | None:
+        """Device addresses for a projection epilogue's K/V write (fp16 caches)."""
+
+        if self.cache.config.dtype != torch.float16:
+            return None
+        layer = self.cache.layer(layer_id)
+        return (layer.keys.data_ptr(), layer.values.data_ptr(), self.tables.data_ptr(), self.stride,
+                self.computed.data_ptr(), self.query_start.data_ptr(), self.request_indices.data_ptr(),
+                self.cache.config.block_size)
 
     def rope_write_kv(self, layer_id: str, qkv: Tensor, q_heads: int, kv_heads: int, positions: Tensor,
                       cos: Tensor, sin: Tensor) -> None:

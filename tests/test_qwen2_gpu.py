@@ -257,6 +257,70 @@ def test_rope_kv_write_equals_rope_then_write():
     assert bool(caches[1][0].abs().sum() > 0)
 
 
+@pytest.mark.parametrize("hidden,hq,hkv,d,position", [(3584, 28, 4, 128, 1037), (896, 14, 2, 64, 5), (2048, 16, 2, 128, 0)])
+def test_qkv_rope_gemv_equals_projection_then_rope_kv_write(hidden, hq, hkv, d, position):
+    """lvb_awq_qkv_rope_packed (one-row QKV GEMV with the RoPE / K/V-write
+    epilogue) is bit-identical to lvb_awq_linear_packed followed by
+    lvb_rope_kv_write: rotated queries in y, unrotated keys and values in y,
+    rotated keys and the values in the token's cache slot, nothing else of
+    the cache touched (Qwen2.5-7B, 0.5B and the pinned model's shapes)."""
+
+    from light_vllm_b200 import _native
+    from light_vllm_b200.awq import pack_awq_decode_layout
+    from oracle import awq as oawq
+    from oracle.qwen2 import rope_tables
+
+    lib = _native.library()
+    n, g, bs, nb = (hq + 2 * hkv) * d, 128, 16, 80
+    qweight, qzeros, scales = oawq.random_checkpoint(hidden, n, g, seed=hidden + d)
+    rng = np.random.default_rng(position)
+    x = torch.from_numpy(rng.standard_normal((1, hidden)).astype(np.float16)).cuda()
+    bias = torch.from_numpy(rng.standard_normal(n).astype(np.float16)).cuda()
+    codes, groups = pack_awq_decode_layout(*(torch.from_numpy(a).cuda() for a in (qweight, qzeros, scales)), g)
+    cos, sin = (t.cuda() for t in rope_tables(2048, d, 1e6))
+    # one request whose token sits at `position` in its table
+    tables = torch.tensor([list(range(nb - 1, -1, -1))], dtype=torch.int32, device="cuda")
+    computed = torch.tensor([position], dtype=torch.int32, device="cuda")
+    qsl = torch.tensor([0, 1], dtype=torch.int32, device="cuda")
+    req = torch.zeros(1, dtype=torch.int32, device="cuda")
+    positions = torch.tensor([position], dtype=torch.int32, device="cuda")
+    ws = torch.zeros(max(int(lib.lvb_awq_workspace_bytes(1, hidden, n, g)), 256), dtype=torch.uint8, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    results = []
+    for fused in (False, True):
+        kc = torch.full((nb, bs, hkv, d), 7.0, dtype=torch.float16, device="cuda")
+        vc = torch.full_like(kc, -3.0)
+        y = torch.empty(1, n, dtype=torch.float16, device="cuda")
+        if fused:
+            _native.check(lib.lvb_awq_qkv_rope_packed(
+                x.data_ptr(), codes.data_ptr(), groups.data_ptr(), bias.data_ptr(), y.data_ptr(), 1, hidden, n, g,
+                ws.data_ptr(), ws.numel(), positions.data_ptr(), cos.data_ptr(), sin.data_ptr(), cos.shape[0],
+                kc.data_ptr(), vc.data_ptr(), tables.data_ptr(), nb, computed.data_ptr(), qsl.data_ptr(),
+                req.data_ptr(), hq, hkv, d, bs, stream), "qkv_rope")
+            plain = y
+        else:
+            _native.check(lib.lvb_awq_linear_packed(x.data_ptr(), codes.data_ptr(), groups.data_ptr(),
+                                                    bias.data_ptr(), y.data_ptr(), 1, hidden, n, g, ws.data_ptr(),
+                                                    ws.numel(), stream), "linear")
+            plain = y.clone()  # the projection before RoPE: its k and v columns
+            _native.check(lib.lvb_rope_kv_write(y.data_ptr(), n, 1, hq, hkv, d, positions.data_ptr(), cos.data_ptr(),
+                                                sin.data_ptr(), cos.shape[0], kc.data_ptr(), vc.data_ptr(),
+                                                tables.data_ptr(), nb, computed.data_ptr(), qsl.data_ptr(),
+                                                req.data_ptr(), bs, stream), "rope_kv_write")
+        torch.cuda.synchronize()
+        results.append((y[:, :hq * d].clone(), plain[:, hq * d:].clone(), kc, vc))
+    assert _native.device_error() == 0
+    (q0, kv0, k0, v0), (q1, kv1, k1, v1) = results
+    assert torch.equal(q0, q1), "rotated queries differ"
+    assert torch.equal(kv0, kv1), "unrotated k/v columns differ"
+    assert torch.equal(k0, k1) and torch.equal(v0, v1), "cache contents differ"
+    slot_block = int(tables[0, position // bs])
+    assert int((k1 != 7.0).sum()) > 0 and bool((k1[slot_block, position % bs] != 7.0).any())
+    others = torch.ones(nb, bs, dtype=torch.bool, device="cuda")
+    others[slot_block, position % bs] = False
+    assert bool((k1[others] == 7.0).all()) and bool((v1[others] == -3.0).all())
+
+
 @pytest.mark.parametrize("tokens,vocab,hidden", [(1, 152064, 3584), (2, 4099, 256), (3, 1000, 8192), (4, 77, 5120)])
 def test_lm_head_argmax_matches_fp16_logits(tokens, vocab, hidden):
     """lvb_lm_head_argmax against argmax over fp16 logits computed in float64
