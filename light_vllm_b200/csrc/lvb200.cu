@@ -479,6 +479,13 @@ GemvPlan gemv_plan(int64_t m, int64_t k, const PackedShape &sh, int64_t g, int s
   while (smem_of(gps) > kGemvMaxSmem && gps > 1) --gps;
   if (smem_of(gps) > kGemvMaxSmem) return p;
   splits = (sh.groups + gps - 1) / gps;
+  // One wave: whole groups per split can round the CTA count past the four
+  // resident per SM (7B down, 28 tiles: 7 groups per split gives 22 splits =
+  // 616 CTAs, and the 24 of a second wave doubled the launch's time).
+  while (static_cast<long long>(sh.n_tiles) * splits > target && gps < sh.groups && smem_of(gps + 1) <= kGemvMaxSmem) {
+    ++gps;
+    splits = (sh.groups + gps - 1) / gps;
+  }
   const size_t sem = round256(static_cast<size_t>(sh.n_tiles) * 4);
   // Fewer splits when the partials do not fit the caller's workspace.
   while (true) {
@@ -557,6 +564,7 @@ int check_awq_shape(int64_t m, int64_t k, int64_t n, int64_t group_size) {
 // ------------------------------------------------------------------------
 struct DecodePlan {
   int max_splits, chunk_tokens, heads_per_cta, warps_per_head;
+  bool flat;  // balanced schedule (paged_decode_flat_kernel): max_splits bounds the pieces per request
   size_t o_bytes, lse_bytes, count_bytes;
   size_t total() const { return o_bytes + lse_bytes + count_bytes; }
 };
@@ -596,6 +604,20 @@ DecodePlan decode_plan(int64_t num_seqs, int64_t hq, int64_t hkv, int64_t d, int
   p.chunk_tokens = static_cast<int>(chunk_pages * lvb::attn::kPageTokens);
   p.heads_per_cta = static_cast<int>(hpc);
   p.warps_per_head = static_cast<int>(kw);
+  // Large batches run the balanced schedule when its tables and merge
+  // weights fit in shared memory (one CTA's page rings hold the weights).
+  p.flat = false;
+  if (!small && num_seqs <= lvb::attn::kFlatMaxSeqs && max_pages <= INT_MAX / 2) {
+    const int pieces = lvb::attn::flat_max_pieces(static_cast<int>(max_pages));
+    const int ring_bytes = hpc == 4   ? (d == 128 ? lvb::attn::DecodeCfg<128, 4>::kBarOff : lvb::attn::DecodeCfg<64, 4>::kBarOff)
+                           : hpc == 2 ? (d == 128 ? lvb::attn::DecodeCfg<128, 2>::kBarOff : lvb::attn::DecodeCfg<64, 2>::kBarOff)
+                                      : (d == 128 ? lvb::attn::DecodeCfg<128, 1>::kBarOff : lvb::attn::DecodeCfg<64, 1>::kBarOff);
+    if (static_cast<int64_t>(hpc) * (hq / hkv) * pieces * 4 <= ring_bytes) {
+      p.flat = true;
+      splits = pieces;
+      p.max_splits = pieces;
+    }
+  }
   p.o_bytes = (static_cast<size_t>(num_seqs * hq * splits * d) * 4 + 255) & ~static_cast<size_t>(255);
   p.lse_bytes = (static_cast<size_t>(num_seqs * hq * splits) * 4 + 255) & ~static_cast<size_t>(255);
   p.count_bytes = (static_cast<size_t>(num_seqs * hkv) * 4 + 255) & ~static_cast<size_t>(255);
@@ -644,9 +666,44 @@ int launch_decode(const lvb::attn::AttnArgs &a, int64_t num_seqs, int64_t num_bl
   return LVB_OK;
 }
 
+// Balanced schedule: one wave of CTAs (the occupancy calculator's resident
+// count per SM x the SM count, over the KV head groups).
+template <bool kBf16, int D, int HPC>
+int launch_decode_flat(lvb::attn::AttnArgs a, int64_t num_seqs, int dev, cudaStream_t stream) {
+  using Cfg = lvb::attn::FlatCfg<D, HPC>;
+  auto kernel = lvb::attn::paged_decode_flat_kernel<kBf16, D, HPC>;
+  static bool smem_done[kMaxDevices] = {false};
+  static int resident[kMaxDevices] = {0};
+  const int max_smem = Cfg::smem_bytes(lvb::attn::kFlatMaxSeqs);
+  int rc = ensure_smem(kernel, max_smem, dev, smem_done);
+  if (rc != LVB_OK) return rc;
+  if (resident[dev] == 0) {
+    int nb = 0;
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kernel, HPC * 32, max_smem);
+    if (e != cudaSuccess) return cuda_fail(e, "paged_decode_flat_kernel occupancy");
+    resident[dev] = nb > 0 ? nb : 1;
+  }
+  a.decode_seqs = static_cast<int>(num_seqs);
+  const int groups = a.Hkv / HPC;
+  int ctas = resident[dev] * sm_count(dev) / groups;
+  if (ctas < 1) ctas = 1;
+  const dim3 grid(static_cast<unsigned>(ctas), static_cast<unsigned>(groups));
+  cudaError_t e = launch_pdl(kernel, grid, dim3(HPC * 32), Cfg::smem_bytes(static_cast<int>(num_seqs)), stream, a);
+  if (e != cudaSuccess) return cuda_fail(e, "paged_decode_flat_kernel launch");
+  return LVB_OK;
+}
+
 template <bool kBf16, int D>
-int launch_decode_any(const lvb::attn::AttnArgs &a, int heads_per_cta, int warps_per_head, int64_t num_seqs,
-                      int64_t num_blocks, int dev, cudaStream_t stream) {
+int launch_decode_any(const lvb::attn::AttnArgs &a, const DecodePlan &plan, int64_t num_seqs, int64_t num_blocks,
+                      int dev, cudaStream_t stream) {
+  const int heads_per_cta = plan.heads_per_cta, warps_per_head = plan.warps_per_head;
+  if (plan.flat) {
+    switch (heads_per_cta) {
+      case 4: return launch_decode_flat<kBf16, D, 4>(a, num_seqs, dev, stream);
+      case 2: return launch_decode_flat<kBf16, D, 2>(a, num_seqs, dev, stream);
+      default: return launch_decode_flat<kBf16, D, 1>(a, num_seqs, dev, stream);
+    }
+  }
   if (warps_per_head == 4) return launch_decode<kBf16, D, 1, 4>(a, num_seqs, num_blocks, dev, stream);
   switch (heads_per_cta) {
     case 4: return launch_decode<kBf16, D, 4>(a, num_seqs, num_blocks, dev, stream);
@@ -1220,13 +1277,11 @@ int lvb_paged_attention(const uint16_t *query, int64_t query_token_stride,
     a.max_splits = plan.max_splits;
     a.chunk_tokens = plan.chunk_tokens;
     if (bf16) {
-      rc = head_size == 128
-               ? launch_decode_any<true, 128>(a, plan.heads_per_cta, plan.warps_per_head, n_decode, num_blocks, dev, s)
-               : launch_decode_any<true, 64>(a, plan.heads_per_cta, plan.warps_per_head, n_decode, num_blocks, dev, s);
+      rc = head_size == 128 ? launch_decode_any<true, 128>(a, plan, n_decode, num_blocks, dev, s)
+                            : launch_decode_any<true, 64>(a, plan, n_decode, num_blocks, dev, s);
     } else {
-      rc = head_size == 128
-               ? launch_decode_any<false, 128>(a, plan.heads_per_cta, plan.warps_per_head, n_decode, num_blocks, dev, s)
-               : launch_decode_any<false, 64>(a, plan.heads_per_cta, plan.warps_per_head, n_decode, num_blocks, dev, s);
+      rc = head_size == 128 ? launch_decode_any<false, 128>(a, plan, n_decode, num_blocks, dev, s)
+                            : launch_decode_any<false, 64>(a, plan, n_decode, num_blocks, dev, s);
     }
     if (rc != LVB_OK || all_decode) return rc;
   }

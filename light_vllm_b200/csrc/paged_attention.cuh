@@ -105,6 +105,7 @@ struct AttnArgs {
   int max_splits;
   int chunk_tokens;  // multiple of 16
   int num_seqs;
+  int decode_seqs;   // balanced decode schedule: requests (launch order slots 0 .. decode_seqs - 1)
   // prefill tile kernel: requests order[first_tile_req + blockIdx.y] (the
   // packer lists one-token requests first; the decode kernel serves those), or
   // blockIdx.y itself when order is null
@@ -527,6 +528,183 @@ struct DecodeCfg {
   static_assert(KW == 1 || kMergeObufOff + KW * 16 * D * 4 <= kBarOff, "merge scratch fits in the ring");
 };
 
+// One 16-token page of a warp's (request, KV head) pass: S = Q K^T for the
+// page's tokens (two 8-token MMA tiles over the GQA group's rows), the online
+// softmax update (positions >= end masked) and O += P V.  K and V sit in
+// shared memory as two 64-dim boxes each, 16-byte chunks XOR-swizzled by the
+// token row; pos0 is the position of the lane's first score column.
+template <bool kBf16, int D>
+__device__ __forceinline__ void decode_page(uint32_t kbase, uint32_t vbase, const uint32_t (&qa)[D / 16][4],
+                                            float (&o)[D / 8][4], float (&m_run)[2], float (&l_run)[2], int pos0,
+                                            int end, float scale_log2) {
+  constexpr int kSteps = D / 16;
+  constexpr int kNTiles = D / 8;
+  const int lane = threadIdx.x & 31;
+  const int mi = lane >> 3;
+  const int rr = lane & 7;
+  // S = Q K^T for the 16 tokens of the page (two 8-token MMA tiles).
+  float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+  for (int ks = 0; ks < kSteps; ++ks) {
+    const int tok = (mi >> 1) * 8 + rr;
+    const int chunk = (ks & 3) * 2 + (mi & 1);
+    const uint32_t addr = kbase + (ks >> 2) * kBoxBytes + tok * 128 + ((chunk ^ (tok & 7)) << 4);
+    uint32_t b0, b1, b2, b3;
+    ldsm_x4(addr, b0, b1, b2, b3);
+    mma_16816<kBf16>(sc[0], qa[ks], b0, b1);
+    mma_16816<kBf16>(sc[1], qa[ks], b2, b3);
+  }
+  // Online softmax (rows g and g + 8; columns = tokens 8 * nt + 2 * cq + {0, 1}).
+  float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int pos = pos0 + nt * 8 + (e & 1);
+      const float v = pos < end ? sc[nt][e] * scale_log2 : -INFINITY;
+      sc[nt][e] = v;
+      mx[e >> 1] = fmaxf(mx[e >> 1], v);
+    }
+  }
+  float alpha[2];
+#pragma unroll
+  for (int hr = 0; hr < 2; ++hr) {
+    mx[hr] = fmaxf(mx[hr], __shfl_xor_sync(0xffffffffu, mx[hr], 1));
+    mx[hr] = fmaxf(mx[hr], __shfl_xor_sync(0xffffffffu, mx[hr], 2));
+    const float m_new = fmaxf(m_run[hr], mx[hr]);
+    alpha[hr] = exp2f(m_run[hr] - m_new);
+    m_run[hr] = m_new;
+    l_run[hr] *= alpha[hr];
+  }
+  // P enters the MMA in the cache dtype.  bf16 keeps 8 mantissa bits, so its
+  // rounding error is carried by a second MMA on the remainder (hi + lo ~ 16
+  // bits); fp16 P (11 bits) is used as is, as the reference's Triton kernel
+  // does (tl.dot on fp16 p), one MMA per tile.
+  uint32_t pa_hi[4], pa_lo[4];
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+    for (int hr = 0; hr < 2; ++hr) {
+      const float p0 = exp2f(sc[nt][2 * hr] - m_run[hr]);
+      const float p1 = exp2f(sc[nt][2 * hr + 1] - m_run[hr]);
+      l_run[hr] += p0 + p1;
+      const uint32_t hi = pack2<kBf16>(p0, p1);
+      pa_hi[nt * 2 + hr] = hi;
+      if constexpr (kBf16) {
+        const float h0 = __uint_as_float(hi << 16);
+        const float h1 = __uint_as_float(hi & 0xFFFF0000u);
+        pa_lo[nt * 2 + hr] = pack2<kBf16>(p0 - h0, p1 - h1);
+      }
+    }
+  }
+#pragma unroll
+  for (int n = 0; n < kNTiles; ++n) {
+    o[n][0] *= alpha[0];
+    o[n][1] *= alpha[0];
+    o[n][2] *= alpha[1];
+    o[n][3] *= alpha[1];
+  }
+  // O += P V: A = P (rows = heads, k = the page's 16 tokens).
+#pragma unroll
+  for (int dp = 0; dp < kSteps; ++dp) {
+    const int tok = (mi & 1) * 8 + rr;
+    const int chunk = (dp & 3) * 2 + (mi >> 1);
+    const uint32_t addr = vbase + (dp >> 2) * kBoxBytes + tok * 128 + ((chunk ^ (tok & 7)) << 4);
+    uint32_t b0, b1, b2, b3;
+    ldsm_x4_trans(addr, b0, b1, b2, b3);
+    mma_16816<kBf16>(o[2 * dp], pa_hi, b0, b1);
+    mma_16816<kBf16>(o[2 * dp + 1], pa_hi, b2, b3);
+    if constexpr (kBf16) {
+      mma_16816<kBf16>(o[2 * dp], pa_lo, b0, b1);
+      mma_16816<kBf16>(o[2 * dp + 1], pa_lo, b2, b3);
+    }
+  }
+}
+
+// Combines the nsplit partial results of `rows` consecutive query heads
+// (head0 = request * Hq + first head) into out_row: each split's normalised
+// output and log2-sum-exp sit in part_o / part_lse at split index 0 ..
+// nsplit - 1.  All kThreads threads of the CTA call it; w_sm holds rows x
+// nsplit floats of shared memory.
+template <bool kBf16, int D, int kThreads>
+__device__ __forceinline__ void merge_partials(const AttnArgs &a, int64_t head0, int rows, int nsplit, float *w_sm,
+                                               uint16_t *out_row) {
+  const int tid = threadIdx.x;
+  // Split weights first (log2-sum-exp -> normalised weights, in shared memory
+  // reused from the ring), then the weighted sum with independent loads.
+  for (int idx = tid; idx < rows * nsplit; idx += kThreads) {
+    const int row = idx / nsplit;
+    const int sp = idx - row * nsplit;
+    w_sm[idx] = __ldcg(a.part_lse + (head0 + row) * a.max_splits + sp);
+  }
+  asm volatile("bar.sync 2, %0;" ::"n"(kThreads) : "memory");
+  for (int row = tid; row < rows; row += kThreads) {
+    float m_all = -INFINITY;
+    for (int sp = 0; sp < nsplit; ++sp) m_all = fmaxf(m_all, w_sm[row * nsplit + sp]);
+    float wsum = 0.f;
+    for (int sp = 0; sp < nsplit; ++sp) {
+      const float wt = exp2f(w_sm[row * nsplit + sp] - m_all);
+      w_sm[row * nsplit + sp] = wt;
+      wsum += wt;
+    }
+    const float inv = 1.f / wsum;
+    for (int sp = 0; sp < nsplit; ++sp) w_sm[row * nsplit + sp] *= inv;
+  }
+  asm volatile("bar.sync 2, %0;" ::"n"(kThreads) : "memory");
+  // Weighted sum over the splits.  The partials sit in L2 (written moments
+  // ago), so the cost is round trips, not bytes: each thread keeps
+  // kMergeOuts float4 outputs x kMergeSplits splits = 16 independent loads in
+  // flight per round trip.  Splits are summed in order for every output, so
+  // the result does not depend on the thread mapping.
+  constexpr int kMergeOuts = 4;
+  constexpr int kMergeSplits = 4;
+  constexpr int kQuads = D / 4;
+  const int total4 = rows * kQuads;
+  for (int base = tid; base < total4; base += kThreads * kMergeOuts) {
+    float4 acc[kMergeOuts];
+    const float4 *src[kMergeOuts];
+    const float *wrow[kMergeOuts];
+#pragma unroll
+    for (int j = 0; j < kMergeOuts; ++j) {
+      acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+      const int idx = base + j * kThreads;
+      const int row = (idx < total4 ? idx : 0) / kQuads;
+      const int q4 = (idx < total4 ? idx : 0) - row * kQuads;
+      src[j] = reinterpret_cast<const float4 *>(a.part_o + (head0 + row) * a.max_splits * D) + q4;
+      wrow[j] = w_sm + row * nsplit;
+    }
+    for (int sp0 = 0; sp0 < nsplit; sp0 += kMergeSplits) {
+      float4 v[kMergeOuts][kMergeSplits];
+#pragma unroll
+      for (int j = 0; j < kMergeOuts; ++j)
+#pragma unroll
+        for (int s = 0; s < kMergeSplits; ++s)
+          v[j][s] = (sp0 + s < nsplit && base + j * kThreads < total4) ? __ldcg(src[j] + (sp0 + s) * kQuads)
+                                                                          : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int j = 0; j < kMergeOuts; ++j)
+#pragma unroll
+        for (int s = 0; s < kMergeSplits; ++s) {
+          const float wt = sp0 + s < nsplit ? wrow[j][sp0 + s] : 0.f;
+          acc[j].x = fmaf(wt, v[j][s].x, acc[j].x);
+          acc[j].y = fmaf(wt, v[j][s].y, acc[j].y);
+          acc[j].z = fmaf(wt, v[j][s].z, acc[j].z);
+          acc[j].w = fmaf(wt, v[j][s].w, acc[j].w);
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < kMergeOuts; ++j) {
+      const int idx = base + j * kThreads;
+      if (idx >= total4) continue;
+      const int row = idx / kQuads;
+      const int q4 = idx - row * kQuads;
+      uint32_t *dst = reinterpret_cast<uint32_t *>(out_row + row * D + 4 * q4);
+      dst[0] = pack2<kBf16>(acc[j].x, acc[j].y);
+      dst[1] = pack2<kBf16>(acc[j].z, acc[j].w);
+    }
+  }
+}
+
 template <bool kBf16, int D, int HPC, int KW = 1>
 __global__ void __launch_bounds__(DecodeCfg<D, HPC, KW>::kThreads, 2)
     paged_decode_kernel(const AttnArgs a) {
@@ -649,8 +827,6 @@ __global__ void __launch_bounds__(DecodeCfg<D, HPC, KW>::kThreads, 2)
   for (int i = 0; i < kNTiles; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
   float m_run[2] = {-INFINITY, -INFINITY};
   float l_run[2] = {0.f, 0.f};
-  const int mi = lane >> 3;  // ldmatrix: matrix index and row within it
-  const int rr = lane & 7;
   bool ok = true;
 
   for (int i = 0; i < my_pages; ++i) {
@@ -665,86 +841,8 @@ __global__ void __launch_bounds__(DecodeCfg<D, HPC, KW>::kThreads, 2)
     const uint32_t ph = (i / kStages) & 1;
     if (!__all_sync(0xffffffffu, mbar_wait(&ready[s], ph, abort_flag))) { ok = false; break; }
     const uint32_t kbase = ring + s * Cfg::kPageBytes;
-    const uint32_t vbase = kbase + Cfg::kHeadBytes;
-
-    // S = Q K^T for the 16 tokens of the page (two 8-token MMA tiles).
-    float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-#pragma unroll
-    for (int ks = 0; ks < kSteps; ++ks) {
-      const int tok = (mi >> 1) * 8 + rr;
-      const int chunk = (ks & 3) * 2 + (mi & 1);
-      const uint32_t addr = kbase + (ks >> 2) * kBoxBytes + tok * 128 + ((chunk ^ (tok & 7)) << 4);
-      uint32_t b0, b1, b2, b3;
-      ldsm_x4(addr, b0, b1, b2, b3);
-      mma_16816<kBf16>(sc[0], qa[ks], b0, b1);
-      mma_16816<kBf16>(sc[1], qa[ks], b2, b3);
-    }
-    // Online softmax (rows g and g + 8; columns = tokens 8 * nt + 2 * cq + {0, 1}).
-    const int pos0 = (p_begin + pg) * kPageTokens + 2 * cq;
-    float mx[2] = {-INFINITY, -INFINITY};
-#pragma unroll
-    for (int nt = 0; nt < 2; ++nt) {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int pos = pos0 + nt * 8 + (e & 1);
-        const float v = pos < end ? sc[nt][e] * a.scale_log2 : -INFINITY;
-        sc[nt][e] = v;
-        mx[e >> 1] = fmaxf(mx[e >> 1], v);
-      }
-    }
-    float alpha[2];
-#pragma unroll
-    for (int hr = 0; hr < 2; ++hr) {
-      mx[hr] = fmaxf(mx[hr], __shfl_xor_sync(0xffffffffu, mx[hr], 1));
-      mx[hr] = fmaxf(mx[hr], __shfl_xor_sync(0xffffffffu, mx[hr], 2));
-      const float m_new = fmaxf(m_run[hr], mx[hr]);
-      alpha[hr] = exp2f(m_run[hr] - m_new);
-      m_run[hr] = m_new;
-      l_run[hr] *= alpha[hr];
-    }
-    // P enters the MMA in the cache dtype.  bf16 keeps 8 mantissa bits, so its
-    // rounding error is carried by a second MMA on the remainder (hi + lo ~ 16
-    // bits); fp16 P (11 bits) is used as is, as the reference's Triton kernel
-    // does (tl.dot on fp16 p), one MMA per tile.
-    uint32_t pa_hi[4], pa_lo[4];
-#pragma unroll
-    for (int nt = 0; nt < 2; ++nt) {
-#pragma unroll
-      for (int hr = 0; hr < 2; ++hr) {
-        const float p0 = exp2f(sc[nt][2 * hr] - m_run[hr]);
-        const float p1 = exp2f(sc[nt][2 * hr + 1] - m_run[hr]);
-        l_run[hr] += p0 + p1;
-        const uint32_t hi = pack2<kBf16>(p0, p1);
-        pa_hi[nt * 2 + hr] = hi;
-        if constexpr (kBf16) {
-          const float h0 = __uint_as_float(hi << 16);
-          const float h1 = __uint_as_float(hi & 0xFFFF0000u);
-          pa_lo[nt * 2 + hr] = pack2<kBf16>(p0 - h0, p1 - h1);
-        }
-      }
-    }
-#pragma unroll
-    for (int n = 0; n < kNTiles; ++n) {
-      o[n][0] *= alpha[0];
-      o[n][1] *= alpha[0];
-      o[n][2] *= alpha[1];
-      o[n][3] *= alpha[1];
-    }
-    // O += P V: A = P (rows = heads, k = the page's 16 tokens).
-#pragma unroll
-    for (int dp = 0; dp < kSteps; ++dp) {
-      const int tok = (mi & 1) * 8 + rr;
-      const int chunk = (dp & 3) * 2 + (mi >> 1);
-      const uint32_t addr = vbase + (dp >> 2) * kBoxBytes + tok * 128 + ((chunk ^ (tok & 7)) << 4);
-      uint32_t b0, b1, b2, b3;
-      ldsm_x4_trans(addr, b0, b1, b2, b3);
-      mma_16816<kBf16>(o[2 * dp], pa_hi, b0, b1);
-      mma_16816<kBf16>(o[2 * dp + 1], pa_hi, b2, b3);
-      if constexpr (kBf16) {
-        mma_16816<kBf16>(o[2 * dp], pa_lo, b0, b1);
-        mma_16816<kBf16>(o[2 * dp + 1], pa_lo, b2, b3);
-      }
-    }
+    decode_page<kBf16, D>(kbase, kbase + Cfg::kHeadBytes, qa, o, m_run, l_run,
+                          (p_begin + pg) * kPageTokens + 2 * cq, end, a.scale_log2);
     __syncwarp();
   }
   cp_async_wait_all();
@@ -860,84 +958,301 @@ __global__ void __launch_bounds__(DecodeCfg<D, HPC, KW>::kThreads, 2)
   asm volatile("bar.sync 2, %0;" ::"n"(kConsumers) : "memory");
   if (!*last_flag) return;
   __threadfence();
-  // Split weights first (log2-sum-exp -> normalised weights, in shared memory
-  // reused from the ring), then the weighted sum with independent loads.
-  const int rows = HPC * group;
-  float *w_sm = reinterpret_cast<float *>(smem);  // [rows][nsplit]
-  const int64_t head0 = static_cast<int64_t>(seq) * a.Hq + hg * HPC * group;
-  for (int idx = tid; idx < rows * nsplit; idx += kConsumers) {
-    const int row = idx / nsplit;
-    const int sp = idx - row * nsplit;
-    w_sm[idx] = __ldcg(a.part_lse + (head0 + row) * a.max_splits + sp);
-  }
-  asm volatile("bar.sync 2, %0;" ::"n"(kConsumers) : "memory");
-  for (int row = tid; row < rows; row += kConsumers) {
-    float m_all = -INFINITY;
-    for (int sp = 0; sp < nsplit; ++sp) m_all = fmaxf(m_all, w_sm[row * nsplit + sp]);
-    float wsum = 0.f;
-    for (int sp = 0; sp < nsplit; ++sp) {
-      const float wt = exp2f(w_sm[row * nsplit + sp] - m_all);
-      w_sm[row * nsplit + sp] = wt;
-      wsum += wt;
-    }
-    const float inv = 1.f / wsum;
-    for (int sp = 0; sp < nsplit; ++sp) w_sm[row * nsplit + sp] *= inv;
-  }
-  asm volatile("bar.sync 2, %0;" ::"n"(kConsumers) : "memory");
-  // Weighted sum over the splits.  The partials sit in L2 (written moments
-  // ago), so the cost is round trips, not bytes: each thread keeps
-  // kMergeOuts float4 outputs x kMergeSplits splits = 16 independent loads in
-  // flight per round trip.  Splits are summed in order for every output, so
-  // the result does not depend on the thread mapping.
-  constexpr int kMergeOuts = 4;
-  constexpr int kMergeSplits = 4;
-  constexpr int kQuads = D / 4;
-  const int total4 = rows * kQuads;
-  uint16_t *out_row = a.out + t * a.o_stride + static_cast<int64_t>(hg) * HPC * group * D;
-  for (int base = tid; base < total4; base += kConsumers * kMergeOuts) {
-    float4 acc[kMergeOuts];
-    const float4 *src[kMergeOuts];
-    const float *wrow[kMergeOuts];
-#pragma unroll
-    for (int j = 0; j < kMergeOuts; ++j) {
-      acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-      const int idx = base + j * kConsumers;
-      const int row = (idx < total4 ? idx : 0) / kQuads;
-      const int q4 = (idx < total4 ? idx : 0) - row * kQuads;
-      src[j] = reinterpret_cast<const float4 *>(a.part_o + (head0 + row) * a.max_splits * D) + q4;
-      wrow[j] = w_sm + row * nsplit;
-    }
-    for (int sp0 = 0; sp0 < nsplit; sp0 += kMergeSplits) {
-      float4 v[kMergeOuts][kMergeSplits];
-#pragma unroll
-      for (int j = 0; j < kMergeOuts; ++j)
-#pragma unroll
-        for (int s = 0; s < kMergeSplits; ++s)
-          v[j][s] = (sp0 + s < nsplit && base + j * kConsumers < total4) ? __ldcg(src[j] + (sp0 + s) * kQuads)
-                                                                          : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-      for (int j = 0; j < kMergeOuts; ++j)
-#pragma unroll
-        for (int s = 0; s < kMergeSplits; ++s) {
-          const float wt = sp0 + s < nsplit ? wrow[j][sp0 + s] : 0.f;
-          acc[j].x = fmaf(wt, v[j][s].x, acc[j].x);
-          acc[j].y = fmaf(wt, v[j][s].y, acc[j].y);
-          acc[j].z = fmaf(wt, v[j][s].z, acc[j].z);
-          acc[j].w = fmaf(wt, v[j][s].w, acc[j].w);
-        }
-    }
-#pragma unroll
-    for (int j = 0; j < kMergeOuts; ++j) {
-      const int idx = base + j * kConsumers;
-      if (idx >= total4) continue;
-      const int row = idx / kQuads;
-      const int q4 = idx - row * kQuads;
-      uint32_t *dst = reinterpret_cast<uint32_t *>(out_row + row * D + 4 * q4);
-      dst[0] = pack2<kBf16>(acc[j].x, acc[j].y);
-      dst[1] = pack2<kBf16>(acc[j].z, acc[j].w);
-    }
-  }
+  merge_partials<kBf16, D, kConsumers>(a, static_cast<int64_t>(seq) * a.Hq + hg * HPC * group, HPC * group, nsplit,
+                                       reinterpret_cast<float *>(smem),
+                                       a.out + t * a.o_stride + static_cast<int64_t>(hg) * HPC * group * D);
   if (tid == 0) *counter = 0u;
+}
+
+
+// ------------------------------------------------------------------------
+// Balanced decode schedule
+// ------------------------------------------------------------------------
+// The split kernel above gives every request the same number of fixed-size
+// splits, so a batch of ragged contexts launches many empty CTAs and runs in
+// uneven waves.  Here the requests' pages are laid end to end in launch order
+// (request z owns flat pages prefix[z] .. prefix[z + 1] - 1) and CTA c takes
+// the L flat pages from c L, crossing request boundaries: every CTA but the
+// last streams the same number of pages, and the grid is one wave.  A request
+// whose pages span several CTAs leaves one partial result per CTA ("piece",
+// numbered from the CTA holding its first page); the last piece to finish
+// merges them.  One warp per KV head of the CTA's head group.
+constexpr int kFlatMinPages = 8;    // fewest pages per CTA: bounds the pieces per request
+constexpr int kFlatMaxSeqs = 512;   // requests whose page prefix fits beside the page rings
+
+template <int D, int HPC>
+struct FlatCfg {
+  using Base = DecodeCfg<D, HPC, 1>;
+  // prefix[n + 1], ctx[n], seq[n] (int32) after the barriers and flags
+  static constexpr int kTableOff = Base::kBarOff + HPC * Base::kStages * 8 + 16;
+  __host__ __device__ static int smem_bytes(int n) { return kTableOff + 12 * (n + 1) + 1024; }
+};
+
+// Most pieces a request of max_pages pages can have: a piece holds at least
+// one page and every CTA but one holds kFlatMinPages or more.
+__host__ __device__ inline int flat_max_pieces(int max_pages) {
+  return (max_pages + kFlatMinPages - 1) / kFlatMinPages + 1;
+}
+
+template <bool kBf16, int D, int HPC>
+__global__ void __launch_bounds__(HPC * 32, 2) paged_decode_flat_kernel(const AttnArgs a) {
+  pdl_entry();
+  using Base = DecodeCfg<D, HPC, 1>;
+  using Cfg = FlatCfg<D, HPC>;
+  constexpr int kStages = Base::kStages;
+  constexpr int kSteps = D / 16;
+  constexpr int kNTiles = D / 8;
+  constexpr int kThreads = HPC * 32;
+  constexpr int kChunksPerLane = Base::kHeadBytes / 16 / 32;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + Base::kBarOff);
+  uint64_t *ready = bars + warp * kStages;
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(bars + HPC * kStages);
+  volatile int *last_flag = abort_flag + 1;
+  const int n = a.decode_seqs;
+  int *prefix = reinterpret_cast<int *>(smem + Cfg::kTableOff);  // [n + 1]
+  int *ctx_sm = prefix + n + 1;                                   // [n]
+  int *seq_sm = ctx_sm + n;                                       // [n]
+
+  for (int z = tid; z < n; z += kThreads) {
+    seq_sm[z] = a.order != nullptr ? a.order[z] : z;
+    ctx_sm[z] = (a.order != nullptr ? a.order[a.num_seqs + z] : a.computed[z]) + 1;
+  }
+  if (tid == 0) {
+    for (int s = 0; s < HPC * kStages; ++s) mbar_init(bars + s, 32);
+    *abort_flag = 0;
+    *last_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  // Exclusive prefix of the page counts: lane l of warp 0 sums a run of
+  // requests, one warp scan combines the runs.
+  if (warp == 0) {
+    const int per = (n + 31) / 32;
+    const int z0 = min(n, lane * per);
+    const int z1 = min(n, z0 + per);
+    int sum = 0;
+    for (int z = z0; z < z1; ++z) sum += (ctx_sm[z] + kPageTokens - 1) / kPageTokens;
+    int incl = sum;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    int run = incl - sum;
+    for (int z = z0; z < z1; ++z) {
+      prefix[z] = run;
+      run += (ctx_sm[z] + kPageTokens - 1) / kPageTokens;
+    }
+    if (lane == 31) prefix[n] = incl;
+  }
+  __syncthreads();
+  const int total = prefix[n];
+  const int per_cta = max(kFlatMinPages, (total + static_cast<int>(gridDim.x) - 1) / static_cast<int>(gridDim.x));
+  const int g0 = static_cast<int>(blockIdx.x) * per_cta;
+  if (g0 >= total) return;  // uniform for the whole CTA
+  const int npg = min(total, g0 + per_cta) - g0;
+  const int hg = blockIdx.y;
+  const int kvh = hg * HPC + warp;
+  const int group = a.Hq / a.Hkv;
+  const uint32_t ring = smem_u32(smem) + warp * Base::kWarpRing;
+  const int64_t head_off = static_cast<int64_t>(kvh) * D;
+  const int64_t row_elems = static_cast<int64_t>(a.Hkv) * D;
+
+  // Request slot holding flat page gp (largest z with prefix[z] <= gp; every
+  // request has at least one page).
+  auto find_req = [&](int gp) {
+    int lo = 0, hi = n - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (prefix[mid] <= gp) lo = mid; else hi = mid - 1;
+    }
+    return lo;
+  };
+  // Per lane: block id and rows in use of the CTA's page base + lane, for a
+  // batch of 32 pages and the batch after it.
+  auto fetch = [&](int base, int &blk, int &valid) {
+    const int i = base + lane;
+    blk = 0;
+    valid = 0;
+    if (i < npg) {
+      const int gp = g0 + i;
+      const int z = find_req(gp);
+      const int j = gp - prefix[z];
+      blk = a.tables[static_cast<int64_t>(seq_sm[z]) * a.table_stride + j];
+      valid = ctx_sm[z] - j * kPageTokens;
+    }
+  };
+  int blk_cur, valid_cur, blk_next, valid_next;
+  fetch(0, blk_cur, valid_cur);
+  fetch(32, blk_next, valid_next);
+  int batch_base = 0;
+
+  // Same copy pattern as the split kernel: lane l copies 16-byte chunks l,
+  // l + 32, ... of the head's 16 token rows; rows past the request's context
+  // are zero-filled (their V rows enter P V with weight 0).
+  auto load_page = [&](int i, int slot) {
+    while (i >= batch_base + 32) {
+      blk_cur = blk_next;
+      valid_cur = valid_next;
+      batch_base += 32;
+      fetch(batch_base + 32, blk_next, valid_next);
+    }
+    const int block = __shfl_sync(0xffffffffu, blk_cur, i - batch_base);
+    const int valid = __shfl_sync(0xffffffffu, valid_cur, i - batch_base);
+    const uint32_t kdst = ring + slot * Base::kPageBytes;
+    const uint32_t vdst = kdst + Base::kHeadBytes;
+    const int64_t base = static_cast<int64_t>(block) * kPageTokens * row_elems + head_off;
+#pragma unroll
+    for (int u = 0; u < kChunksPerLane; ++u) {
+      const int q = lane + 32 * u;
+      const int tok = q / (D / 8);
+      const int c16 = q - tok * (D / 8);
+      const int half = c16 >> 3;
+      const int c = c16 & 7;
+      const uint32_t off = half * kBoxBytes + tok * 128 + ((c ^ (tok & 7)) << 4);
+      const int64_t src = base + tok * row_elems + c16 * 8;
+      const uint32_t bytes = tok < valid ? 16u : 0u;
+      cp_async_16(kdst + off, a.kc + (bytes ? src : head_off), bytes);
+      cp_async_16(vdst + off, a.vc + (bytes ? src : head_off), bytes);
+    }
+    cp_async_arrive_noinc(&ready[slot]);
+  };
+
+#pragma unroll 1
+  for (int j = 0; j < kStages - 1 && j < npg; ++j) load_page(j, j);
+
+  const int g = lane >> 2;
+  const int cq = lane & 3;
+  uint32_t qa[kSteps][4];
+  float o[kNTiles][4];
+  float m_run[2], l_run[2];
+  int z = find_req(g0);
+  int seg_first = prefix[z] - g0;  // CTA page index of the request's page 0 (<= 0 for the first segment)
+  int seg_end = prefix[z + 1] - g0;
+  // Pieces of this CTA that another CTA may have to merge: at most the first
+  // and the last segment (a middle segment lies wholly in this CTA).
+  int pend_seq0 = -1, pend_n0 = 0, pend_seq1 = -1, pend_n1 = 0;
+
+  auto start_segment = [&]() {
+    const int seq = seq_sm[z];
+    const uint16_t *qrow = a.q + static_cast<int64_t>(a.qsl[seq]) * a.q_stride + static_cast<int64_t>(kvh) * group * D;
+#pragma unroll
+    for (int ks = 0; ks < kSteps; ++ks) {
+      const int d0 = ks * 16 + 2 * cq;
+      qa[ks][0] = g < group ? *reinterpret_cast<const uint32_t *>(qrow + g * D + d0) : 0u;
+      qa[ks][1] = g + 8 < group ? *reinterpret_cast<const uint32_t *>(qrow + (g + 8) * D + d0) : 0u;
+      qa[ks][2] = g < group ? *reinterpret_cast<const uint32_t *>(qrow + g * D + d0 + 8) : 0u;
+      qa[ks][3] = g + 8 < group ? *reinterpret_cast<const uint32_t *>(qrow + (g + 8) * D + d0 + 8) : 0u;
+    }
+#pragma unroll
+    for (int i = 0; i < kNTiles; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+    m_run[0] = m_run[1] = -INFINITY;
+    l_run[0] = l_run[1] = 0.f;
+  };
+  // The segment's output: final rows when the request lies wholly in this
+  // CTA, else this CTA's piece (normalised output and log2-sum-exp).
+  auto finish_segment = [&]() {
+    const int seq = seq_sm[z];
+    const int first_cta = prefix[z] / per_cta;
+    const int pieces = (prefix[z + 1] - 1) / per_cta - first_cta + 1;
+    const int piece = static_cast<int>(blockIdx.x) - first_cta;
+#pragma unroll
+    for (int hr = 0; hr < 2; ++hr) {
+      l_run[hr] += __shfl_xor_sync(0xffffffffu, l_run[hr], 1);
+      l_run[hr] += __shfl_xor_sync(0xffffffffu, l_run[hr], 2);
+    }
+    if (pieces > a.max_splits) {
+      if (tid == 0) record_device_error(LVB_DEVERR_INDEX);
+      return;
+    }
+#pragma unroll
+    for (int hr = 0; hr < 2; ++hr) {
+      const int row = g + 8 * hr;
+      if (row >= group) continue;
+      const int h = kvh * group + row;
+      const float inv = 1.f / l_run[hr];
+      if (pieces == 1) {
+        uint16_t *dst = a.out + static_cast<int64_t>(a.qsl[seq]) * a.o_stride + static_cast<int64_t>(h) * D;
+#pragma unroll
+        for (int nt = 0; nt < kNTiles; ++nt)
+          *reinterpret_cast<uint32_t *>(dst + nt * 8 + 2 * cq) =
+              pack2<kBf16>(o[nt][2 * hr] * inv, o[nt][2 * hr + 1] * inv);
+      } else {
+        const int64_t base = (static_cast<int64_t>(seq) * a.Hq + h) * a.max_splits + piece;
+        float *dst = a.part_o + base * D;
+#pragma unroll
+        for (int nt = 0; nt < kNTiles; ++nt)
+          __stcg(reinterpret_cast<float2 *>(dst + nt * 8 + 2 * cq),
+                 make_float2(o[nt][2 * hr] * inv, o[nt][2 * hr + 1] * inv));
+        if (cq == 0) __stcg(a.part_lse + base, m_run[hr] + log2f(l_run[hr]));
+      }
+    }
+    if (pieces > 1) {
+      if (pend_seq0 < 0) {
+        pend_seq0 = seq;
+        pend_n0 = pieces;
+      } else {
+        pend_seq1 = seq;
+        pend_n1 = pieces;
+      }
+    }
+  };
+
+  start_segment();
+  bool ok = true;
+  for (int i = 0; i < npg; ++i) {
+    if (i + kStages - 1 < npg) load_page(i + kStages - 1, (i + kStages - 1) % kStages);
+    if (i == seg_end) {
+      finish_segment();
+      ++z;
+      seg_first = seg_end;
+      seg_end = prefix[z + 1] - g0;
+      start_segment();
+    }
+    const int s = i % kStages;
+    const uint32_t ph = (i / kStages) & 1;
+    if (!__all_sync(0xffffffffu, mbar_wait(&ready[s], ph, abort_flag))) { ok = false; break; }
+    const uint32_t kbase = ring + s * Base::kPageBytes;
+    decode_page<kBf16, D>(kbase, kbase + Base::kHeadBytes, qa, o, m_run, l_run,
+                          (i - seg_first) * kPageTokens + 2 * cq, ctx_sm[z], a.scale_log2);
+    __syncwarp();
+  }
+  cp_async_wait_all();
+  if (ok) finish_segment();
+  asm volatile("bar.sync 1, %0;" ::"n"(kThreads) : "memory");
+  if (!ok || *abort_flag) return;  // a failed wait raised the (CTA-wide) abort flag
+
+  // The CTA's pieces of requests shared with other CTAs: the last piece of a
+  // request to arrive merges all of them.
+#pragma unroll 1
+  for (int pi = 0; pi < 2; ++pi) {
+    const int seq = pi == 0 ? pend_seq0 : pend_seq1;
+    const int pieces = pi == 0 ? pend_n0 : pend_n1;
+    if (seq < 0) break;
+    __threadfence();
+    asm volatile("bar.sync 2, %0;" ::"n"(kThreads) : "memory");
+    uint32_t *counter = a.merge_count + static_cast<int64_t>(seq) * (a.Hkv / HPC) + hg;
+    if (tid == 0) {
+      const unsigned int prev = atomicAdd(counter, 1u);
+      *last_flag = prev == static_cast<unsigned int>(pieces - 1) ? 1 : 0;
+    }
+    asm volatile("bar.sync 2, %0;" ::"n"(kThreads) : "memory");
+    if (*last_flag) {
+      __threadfence();
+      merge_partials<kBf16, D, kThreads>(a, static_cast<int64_t>(seq) * a.Hq + hg * HPC * group, HPC * group, pieces,
+                                         reinterpret_cast<float *>(smem),
+                                         a.out + static_cast<int64_t>(a.qsl[seq]) * a.o_stride +
+                                             static_cast<int64_t>(hg) * HPC * group * D);
+      if (tid == 0) *counter = 0u;
+    }
+    asm volatile("bar.sync 2, %0;" ::"n"(kThreads) : "memory");  // last_flag and the scratch free again
+  }
 }
 
 }  // namespace attn
