@@ -794,36 +794,21 @@ def main() -> int:
 
     # End to end through the public API with host buffers, as a serving loop
     # runs it: the step's q | k | v sit in one pinned buffer (as the rows of a
-    # merged QKV projection would) and reach the device in one copy on a copy
-    # stream; the API gets views of the device copy; the output goes back to
-    # pinned memory on a second copy stream.  Two device input buffers let
-    # step i + 1's upload overlap step i's attention (events order each
-    # buffer's reuse after the attention that read it).
+    # merged QKV projection would) and reach the device in one copy; the API
+    # gets views of the device copy; the output goes back to pinned memory.
+    # Everything is enqueued on one stream without host synchronisation, so
+    # the host prepares step i + 1 while the device runs step i.
     sizes = [t.numel() for t in (q, k, v)]
     pinned = torch.cat([t.reshape(-1) for t in (q, k, v)]).cpu().pin_memory()
-    host_outs = [torch.empty(q.shape, dtype=q.dtype, pin_memory=True) for _ in range(2)]
-    staged_flat = [torch.empty_like(pinned, device=device) for _ in range(2)]
-    staged = [[part.view(t.shape) for part, t in zip(buf.split(sizes), (q, k, v))] for buf in staged_flat]
+    host_out = torch.empty(q.shape, dtype=q.dtype, pin_memory=True)
+    staged_flat = torch.empty_like(pinned, device=device)
+    staged = [part.view(t.shape) for part, t in zip(staged_flat.split(sizes), (q, k, v))]
     stream = torch.cuda.current_stream()
-    copy_in, copy_out = torch.cuda.Stream(device), torch.cuda.Stream(device)
-    in_ready = [torch.cuda.Event() for _ in range(2)]
-    buf_free = [torch.cuda.Event() for _ in range(2)]
-    for ev in buf_free:
-        ev.record(stream)
 
     def e2e_step(i):
-        b = i & 1
-        copy_in.wait_event(buf_free[b])
-        with torch.cuda.stream(copy_in):
-            staged_flat[b].copy_(pinned, non_blocking=True)
-        in_ready[b].record(copy_in)
-        stream.wait_event(in_ready[b])
-        o = backend.create(cache, md).forward("layer0", *staged[b], scale=scale)
-        buf_free[b].record(stream)
-        copy_out.wait_stream(stream)
-        with torch.cuda.stream(copy_out):
-            host_outs[b].copy_(o, non_blocking=True)
-        o.record_stream(copy_out)
+        staged_flat.copy_(pinned, non_blocking=True)
+        o = backend.create(cache, md).forward("layer0", *staged, scale=scale)
+        host_out.copy_(o, non_blocking=True)
 
     for i in range(args.warmup):
         e2e_step(i)
@@ -837,7 +822,6 @@ def main() -> int:
     for i in range(e2e_steps):
         e2e_step(i)
     host_ms = (time.perf_counter() - host_t0) * 1e3 / e2e_steps
-    stream.wait_stream(copy_out)
     ev1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = ev0.elapsed_time(ev1) / e2e_steps
@@ -897,8 +881,8 @@ def main() -> int:
         "e2e": {"value": round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4),
                 "host_ms_per_step": round(host_ms, 4),
-                "path": "backend.create(cache, metadata).forward(...) with pinned host q/k/v and output; "
-                        "uploads and read-backs on two copy streams, overlapping the neighbouring steps"},
+                "path": "backend.create(cache, metadata).forward(...) with pinned host q/k/v and output, "
+                        "one stream, no host synchronisation between steps"},
         "gpu_launches": 3 * args.steps,
         "clocks": clock_summary,
     }

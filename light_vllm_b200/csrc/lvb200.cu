@@ -651,13 +651,13 @@ int launch_prefill(const lvb::attn::AttnArgs &a, dim3 grid, int dev, cudaStream_
   return LVB_OK;
 }
 
-template <bool kBf16, int D, int HPC, int KW = 1>
+template <bool kBf16, int D, int HPC, int KW = 1, int NT = 1>
 int launch_decode(const lvb::attn::AttnArgs &a, int64_t num_seqs, int64_t num_blocks, int dev,
                   cudaStream_t stream) {
   (void)num_blocks;
   using Cfg = lvb::attn::DecodeCfg<D, HPC, KW>;
   static bool smem_done[kMaxDevices] = {false};
-  auto kernel = lvb::attn::paged_decode_kernel<kBf16, D, HPC, KW>;
+  auto kernel = lvb::attn::paged_decode_kernel<kBf16, D, HPC, KW, NT>;
   int rc = ensure_smem(kernel, Cfg::kSmemBytes, dev, smem_done);
   if (rc != LVB_OK) return rc;
   dim3 grid(a.max_splits, a.Hkv / HPC, static_cast<unsigned>(num_seqs));
@@ -668,10 +668,10 @@ int launch_decode(const lvb::attn::AttnArgs &a, int64_t num_seqs, int64_t num_bl
 
 // Balanced schedule: one wave of CTAs (the occupancy calculator's resident
 // count per SM x the SM count, over the KV head groups).
-template <bool kBf16, int D, int HPC>
+template <bool kBf16, int D, int HPC, int NT>
 int launch_decode_flat(lvb::attn::AttnArgs a, int64_t num_seqs, int dev, cudaStream_t stream) {
   using Cfg = lvb::attn::FlatCfg<D, HPC>;
-  auto kernel = lvb::attn::paged_decode_flat_kernel<kBf16, D, HPC>;
+  auto kernel = lvb::attn::paged_decode_flat_kernel<kBf16, D, HPC, NT>;
   static bool smem_done[kMaxDevices] = {false};
   static int resident[kMaxDevices] = {0};
   const int max_smem = Cfg::smem_bytes(lvb::attn::kFlatMaxSeqs);
@@ -693,23 +693,31 @@ int launch_decode_flat(lvb::attn::AttnArgs a, int64_t num_seqs, int dev, cudaStr
   return LVB_OK;
 }
 
-template <bool kBf16, int D>
-int launch_decode_any(const lvb::attn::AttnArgs &a, const DecodePlan &plan, int64_t num_seqs, int64_t num_blocks,
-                      int dev, cudaStream_t stream) {
+// NT = 8-head tiles of the GQA group (groups of up to 8 heads: one).
+template <bool kBf16, int D, int NT>
+int launch_decode_nt(const lvb::attn::AttnArgs &a, const DecodePlan &plan, int64_t num_seqs, int64_t num_blocks,
+                     int dev, cudaStream_t stream) {
   const int heads_per_cta = plan.heads_per_cta, warps_per_head = plan.warps_per_head;
   if (plan.flat) {
     switch (heads_per_cta) {
-      case 4: return launch_decode_flat<kBf16, D, 4>(a, num_seqs, dev, stream);
-      case 2: return launch_decode_flat<kBf16, D, 2>(a, num_seqs, dev, stream);
-      default: return launch_decode_flat<kBf16, D, 1>(a, num_seqs, dev, stream);
+      case 4: return launch_decode_flat<kBf16, D, 4, NT>(a, num_seqs, dev, stream);
+      case 2: return launch_decode_flat<kBf16, D, 2, NT>(a, num_seqs, dev, stream);
+      default: return launch_decode_flat<kBf16, D, 1, NT>(a, num_seqs, dev, stream);
     }
   }
-  if (warps_per_head == 4) return launch_decode<kBf16, D, 1, 4>(a, num_seqs, num_blocks, dev, stream);
+  if (warps_per_head == 4) return launch_decode<kBf16, D, 1, 4, NT>(a, num_seqs, num_blocks, dev, stream);
   switch (heads_per_cta) {
-    case 4: return launch_decode<kBf16, D, 4>(a, num_seqs, num_blocks, dev, stream);
-    case 2: return launch_decode<kBf16, D, 2>(a, num_seqs, num_blocks, dev, stream);
-    default: return launch_decode<kBf16, D, 1>(a, num_seqs, num_blocks, dev, stream);
+    case 4: return launch_decode<kBf16, D, 4, 1, NT>(a, num_seqs, num_blocks, dev, stream);
+    case 2: return launch_decode<kBf16, D, 2, 1, NT>(a, num_seqs, num_blocks, dev, stream);
+    default: return launch_decode<kBf16, D, 1, 1, NT>(a, num_seqs, num_blocks, dev, stream);
   }
+}
+
+template <bool kBf16, int D>
+int launch_decode_any(const lvb::attn::AttnArgs &a, const DecodePlan &plan, int64_t num_seqs, int64_t num_blocks,
+                      int dev, cudaStream_t stream) {
+  return a.Hq / a.Hkv <= 8 ? launch_decode_nt<kBf16, D, 1>(a, plan, num_seqs, num_blocks, dev, stream)
+                           : launch_decode_nt<kBf16, D, 2>(a, plan, num_seqs, num_blocks, dev, stream);
 }
 
 template <bool kBf16>

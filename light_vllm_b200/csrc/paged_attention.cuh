@@ -523,103 +523,196 @@ struct DecodeCfg {
   static constexpr int kBarOff = kWarps * kWarpRing;
   static constexpr int kSmemBytes = kBarOff + kWarps * kStages * 8 + 16 + 1024;
   // Cross-warp merge scratch (KW > 1), reusing the ring: (m, l) per warp and
-  // row, then the scaled outputs [KW][16 rows][D] fp32.
+  // head, then the scaled outputs [KW][up to 16 heads][D] fp32.
   static constexpr int kMergeObufOff = 1024;
-  static_assert(KW == 1 || kMergeObufOff + KW * 16 * D * 4 <= kBarOff, "merge scratch fits in the ring");
+  static_assert(KW == 1 || kMergeObufOff + KW * 16 * D * 4 <= kBarOff, "merge scratch (16 heads) fits in the ring");
 };
 
-// One 16-token page of a warp's (request, KV head) pass: S = Q K^T for the
-// page's tokens (two 8-token MMA tiles over the GQA group's rows), the online
-// softmax update (positions >= end masked) and O += P V.  K and V sit in
-// shared memory as two 64-dim boxes each, 16-byte chunks XOR-swizzled by the
-// token row; pos0 is the position of the lane's first score column.
-template <bool kBf16, int D>
-__device__ __forceinline__ void decode_page(uint32_t kbase, uint32_t vbase, const uint32_t (&qa)[D / 16][4],
-                                            float (&o)[D / 8][4], float (&m_run)[2], float (&l_run)[2], int pos0,
-                                            int end, float scale_log2) {
-  constexpr int kSteps = D / 16;
-  constexpr int kNTiles = D / 8;
-  const int lane = threadIdx.x & 31;
-  const int mi = lane >> 3;
-  const int rr = lane & 7;
-  // S = Q K^T for the 16 tokens of the page (two 8-token MMA tiles).
-  float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+// Decode math of one warp over one (request, KV head): the page's 16 tokens
+// on the MMA's M dimension and the GQA group's query heads on N (NT tiles of
+// 8 heads), so a group of up to 8 heads fills the N = 8 tile instead of
+// padding M = 16 rows:
+//   S^T = K Q^T      A = K (16 tokens x 16 dims, ldmatrix), B = Q^T (registers)
+//   O^T += V^T P^T   A = V^T (ldmatrix.trans), B = P^T
+// P^T leaves the first MMA in the accumulator layout (lane 4 r + c: tokens r
+// and r + 8, heads 2 c and 2 c + 1) and enters the second as the B operand
+// (tokens 2 c, 2 c + 1, head r): one movmatrix.trans per 8 x 8 block.
+// Per 16-token page and 8 heads: kSteps MMAs for S and kSteps (fp16) or
+// 2 kSteps (bf16: P as hi + lo) for O.  Each lane holds two heads' running
+// max / sum (its partial sum over its tokens; summed over the lanes with the
+// same column by finish()) and O^T rows g and g + 8 of every 16-dim m-tile.
+template <bool kBf16, int D, int NT>
+struct TokMath {
+  static constexpr int kSteps = D / 16;  // k-steps of K Q^T; 16-dim m-tiles of V^T P^T
+  uint32_t qb[kSteps][NT][2];
+  float o[kSteps][NT][4];
+  float m_run[NT][2], l_run[NT][2];
+
+  // q_head0: the group's first query head (heads are D apart).
+  __device__ __forceinline__ void load_q(const uint16_t *q_head0, int group) {
+    const int lane = threadIdx.x & 31;
+    const int g = lane >> 2, cq = lane & 3;
 #pragma unroll
-  for (int ks = 0; ks < kSteps; ++ks) {
-    const int tok = (mi >> 1) * 8 + rr;
-    const int chunk = (ks & 3) * 2 + (mi & 1);
-    const uint32_t addr = kbase + (ks >> 2) * kBoxBytes + tok * 128 + ((chunk ^ (tok & 7)) << 4);
-    uint32_t b0, b1, b2, b3;
-    ldsm_x4(addr, b0, b1, b2, b3);
-    mma_16816<kBf16>(sc[0], qa[ks], b0, b1);
-    mma_16816<kBf16>(sc[1], qa[ks], b2, b3);
-  }
-  // Online softmax (rows g and g + 8; columns = tokens 8 * nt + 2 * cq + {0, 1}).
-  float mx[2] = {-INFINITY, -INFINITY};
+    for (int nt = 0; nt < NT; ++nt) {
+      const int h = nt * 8 + g;
+      const uint16_t *qr = q_head0 + static_cast<int64_t>(h) * D + 2 * cq;
 #pragma unroll
-  for (int nt = 0; nt < 2; ++nt) {
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const int pos = pos0 + nt * 8 + (e & 1);
-      const float v = pos < end ? sc[nt][e] * scale_log2 : -INFINITY;
-      sc[nt][e] = v;
-      mx[e >> 1] = fmaxf(mx[e >> 1], v);
-    }
-  }
-  float alpha[2];
-#pragma unroll
-  for (int hr = 0; hr < 2; ++hr) {
-    mx[hr] = fmaxf(mx[hr], __shfl_xor_sync(0xffffffffu, mx[hr], 1));
-    mx[hr] = fmaxf(mx[hr], __shfl_xor_sync(0xffffffffu, mx[hr], 2));
-    const float m_new = fmaxf(m_run[hr], mx[hr]);
-    alpha[hr] = exp2f(m_run[hr] - m_new);
-    m_run[hr] = m_new;
-    l_run[hr] *= alpha[hr];
-  }
-  // P enters the MMA in the cache dtype.  bf16 keeps 8 mantissa bits, so its
-  // rounding error is carried by a second MMA on the remainder (hi + lo ~ 16
-  // bits); fp16 P (11 bits) is used as is, as the reference's Triton kernel
-  // does (tl.dot on fp16 p), one MMA per tile.
-  uint32_t pa_hi[4], pa_lo[4];
-#pragma unroll
-  for (int nt = 0; nt < 2; ++nt) {
-#pragma unroll
-    for (int hr = 0; hr < 2; ++hr) {
-      const float p0 = exp2f(sc[nt][2 * hr] - m_run[hr]);
-      const float p1 = exp2f(sc[nt][2 * hr + 1] - m_run[hr]);
-      l_run[hr] += p0 + p1;
-      const uint32_t hi = pack2<kBf16>(p0, p1);
-      pa_hi[nt * 2 + hr] = hi;
-      if constexpr (kBf16) {
-        const float h0 = __uint_as_float(hi << 16);
-        const float h1 = __uint_as_float(hi & 0xFFFF0000u);
-        pa_lo[nt * 2 + hr] = pack2<kBf16>(p0 - h0, p1 - h1);
+      for (int ks = 0; ks < kSteps; ++ks) {
+        qb[ks][nt][0] = h < group ? *reinterpret_cast<const uint32_t *>(qr + ks * 16) : 0u;
+        qb[ks][nt][1] = h < group ? *reinterpret_cast<const uint32_t *>(qr + ks * 16 + 8) : 0u;
       }
     }
   }
+
+  __device__ __forceinline__ void reset() {
 #pragma unroll
-  for (int n = 0; n < kNTiles; ++n) {
-    o[n][0] *= alpha[0];
-    o[n][1] *= alpha[0];
-    o[n][2] *= alpha[1];
-    o[n][3] *= alpha[1];
-  }
-  // O += P V: A = P (rows = heads, k = the page's 16 tokens).
+    for (int mt = 0; mt < kSteps; ++mt)
 #pragma unroll
-  for (int dp = 0; dp < kSteps; ++dp) {
-    const int tok = (mi & 1) * 8 + rr;
-    const int chunk = (dp & 3) * 2 + (mi >> 1);
-    const uint32_t addr = vbase + (dp >> 2) * kBoxBytes + tok * 128 + ((chunk ^ (tok & 7)) << 4);
-    uint32_t b0, b1, b2, b3;
-    ldsm_x4_trans(addr, b0, b1, b2, b3);
-    mma_16816<kBf16>(o[2 * dp], pa_hi, b0, b1);
-    mma_16816<kBf16>(o[2 * dp + 1], pa_hi, b2, b3);
-    if constexpr (kBf16) {
-      mma_16816<kBf16>(o[2 * dp], pa_lo, b0, b1);
-      mma_16816<kBf16>(o[2 * dp + 1], pa_lo, b2, b3);
+      for (int nt = 0; nt < NT; ++nt) o[mt][nt][0] = o[mt][nt][1] = o[mt][nt][2] = o[mt][nt][3] = 0.f;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      m_run[nt][0] = m_run[nt][1] = -INFINITY;
+      l_run[nt][0] = l_run[nt][1] = 0.f;
     }
   }
-}
+
+  // One page: K and V as two 64-dim boxes each in shared memory (16-byte
+  // chunks XOR-swizzled by the token row); pos0 = position of token row 0;
+  // positions >= end are masked.  Every page holds at least one position
+  // below end, so each head's running max is finite after it.
+  __device__ __forceinline__ void page(uint32_t kbase, uint32_t vbase, int pos0, int end, float scale_log2) {
+    const int lane = threadIdx.x & 31;
+    const int g = lane >> 2;
+    const int mi = lane >> 3, rr = lane & 7;
+    float s[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
+#pragma unroll
+    for (int ks = 0; ks < kSteps; ++ks) {
+      // a0: tokens 0-7 of the k-step's low 8 dims, a1: tokens 8-15, a2 / a3: the high 8 dims.
+      const int tok = (mi & 1) * 8 + rr;
+      const int chunk = (ks & 3) * 2 + (mi >> 1);
+      uint32_t a[4];
+      ldsm_x4(kbase + (ks >> 2) * kBoxBytes + tok * 128 + ((chunk ^ (tok & 7)) << 4), a[0], a[1], a[2], a[3]);
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) mma_16816_nv<kBf16>(s[nt], a, qb[ks][nt][0], qb[ks][nt][1]);
+    }
+    const bool ok0 = pos0 + g < end, ok1 = pos0 + g + 8 < end;
+    uint32_t bh[NT][2], bl[NT][2];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      float p[4];
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const float v0 = ok0 ? s[nt][j] * scale_log2 : -INFINITY;      // token g, head 2 cq + j
+        const float v1 = ok1 ? s[nt][2 + j] * scale_log2 : -INFINITY;  // token g + 8
+        float mx = fmaxf(v0, v1);
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+        const float m_new = fmaxf(m_run[nt][j], mx);
+        const float alpha = exp2f(m_run[nt][j] - m_new);
+        m_run[nt][j] = m_new;
+        p[j] = exp2f(v0 - m_new);
+        p[2 + j] = exp2f(v1 - m_new);
+        l_run[nt][j] = l_run[nt][j] * alpha + p[j] + p[2 + j];
+#pragma unroll
+        for (int mt = 0; mt < kSteps; ++mt) {
+          o[mt][nt][j] *= alpha;
+          o[mt][nt][2 + j] *= alpha;
+        }
+      }
+      // P enters the MMA in the cache dtype.  bf16 keeps 8 mantissa bits, so
+      // its rounding error is carried by a second MMA on the remainder (hi +
+      // lo ~ 16 bits); fp16 P (11 bits) is used as is, as the reference's
+      // Triton kernel does (tl.dot on fp16 p).
+      const uint32_t h0 = pack2<kBf16>(p[0], p[1]);  // tokens 0-7 block, row g
+      const uint32_t h1 = pack2<kBf16>(p[2], p[3]);  // tokens 8-15 block
+      bh[nt][0] = movmatrix_trans(h0);
+      bh[nt][1] = movmatrix_trans(h1);
+      if constexpr (kBf16) {
+        const uint32_t l0 = pack2<kBf16>(p[0] - __uint_as_float(h0 << 16), p[1] - __uint_as_float(h0 & 0xFFFF0000u));
+        const uint32_t l1 = pack2<kBf16>(p[2] - __uint_as_float(h1 << 16), p[3] - __uint_as_float(h1 & 0xFFFF0000u));
+        bl[nt][0] = movmatrix_trans(l0);
+        bl[nt][1] = movmatrix_trans(l1);
+      }
+    }
+#pragma unroll
+    for (int mt = 0; mt < kSteps; ++mt) {
+      // a0: dims 0-7 of the m-tile x tokens 0-7 (transposed), a1: dims 8-15,
+      // a2 / a3: tokens 8-15.
+      const int tok = (mi >> 1) * 8 + rr;
+      const int chunk = (mt & 3) * 2 + (mi & 1);
+      uint32_t a[4];
+      ldsm_x4_trans(vbase + (mt >> 2) * kBoxBytes + tok * 128 + ((chunk ^ (tok & 7)) << 4), a[0], a[1], a[2], a[3]);
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        mma_16816_nv<kBf16>(o[mt][nt], a, bh[nt][0], bh[nt][1]);
+        if constexpr (kBf16) mma_16816_nv<kBf16>(o[mt][nt], a, bl[nt][0], bl[nt][1]);
+      }
+    }
+  }
+
+  // Sum the lanes' partial softmax denominators (lanes 4 r + c, same c).
+  __device__ __forceinline__ void finish() {
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        float l = l_run[nt][j];
+        l += __shfl_xor_sync(0xffffffffu, l, 4);
+        l += __shfl_xor_sync(0xffffffffu, l, 8);
+        l += __shfl_xor_sync(0xffffffffu, l, 16);
+        l_run[nt][j] = l;
+      }
+  }
+
+  // Normalised output rows of the group's heads (after finish()): out_head0
+  // is head 0's row, heads D apart.
+  __device__ __forceinline__ void store(uint16_t *out_head0, int group) const {
+    const int lane = threadIdx.x & 31;
+    const int g = lane >> 2, cq = lane & 3;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int h = nt * 8 + 2 * cq + j;
+        if (h >= group) continue;
+        const float inv = 1.f / l_run[nt][j];
+        uint16_t *dst = out_head0 + static_cast<int64_t>(h) * D + g;
+#pragma unroll
+        for (int mt = 0; mt < kSteps; ++mt) {
+          dst[mt * 16] = from_float<kBf16>(o[mt][nt][j] * inv);
+          dst[mt * 16 + 8] = from_float<kBf16>(o[mt][nt][2 + j] * inv);
+        }
+      }
+  }
+
+  // A split's normalised output and log2-sum-exp: head h's row at
+  // part_o + (head_base + h) * stride * D, its lse at part_lse + (head_base +
+  // h) * stride (stride = the workspace's splits per head, offset by split).
+  __device__ __forceinline__ void store_partial(float *part_o, float *part_lse, int64_t head_base, int64_t stride,
+                                                int group) const {
+    const int lane = threadIdx.x & 31;
+    const int g = lane >> 2, cq = lane & 3;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int h = nt * 8 + 2 * cq + j;
+        if (h >= group) continue;
+        const float inv = 1.f / l_run[nt][j];
+        const int64_t row = (head_base + h) * stride;
+        float *dst = part_o + row * D + g;
+#pragma unroll
+        for (int mt = 0; mt < kSteps; ++mt) {
+          __stcg(dst + mt * 16, o[mt][nt][j] * inv);
+          __stcg(dst + mt * 16 + 8, o[mt][nt][2 + j] * inv);
+        }
+        if (g == 0) __stcg(part_lse + row, m_run[nt][j] + log2f(l_run[nt][j]));
+      }
+  }
+};
 
 // Combines the nsplit partial results of `rows` consecutive query heads
 // (head0 = request * Hq + first head) into out_row: each split's normalised
@@ -705,14 +798,13 @@ __device__ __forceinline__ void merge_partials(const AttnArgs &a, int64_t head0,
   }
 }
 
-template <bool kBf16, int D, int HPC, int KW = 1>
+template <bool kBf16, int D, int HPC, int KW = 1, int NT = 1>
 __global__ void __launch_bounds__(DecodeCfg<D, HPC, KW>::kThreads, 2)
     paged_decode_kernel(const AttnArgs a) {
   pdl_entry();
   using Cfg = DecodeCfg<D, HPC, KW>;
   constexpr int kStages = Cfg::kStages;
-  constexpr int kSteps = D / 16;  // k-steps of QK^T, and dim pairs of PV
-  constexpr int kNTiles = D / 8;  // 8-dim output tiles
+  constexpr int kSteps = D / 16;  // 16-dim m-tiles of the output
   constexpr int kConsumers = Cfg::kThreads;
   constexpr int kChunksPerLane = Cfg::kHeadBytes / 16 / 32;  // 16-byte copies per lane for K (and V)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -809,24 +901,12 @@ __global__ void __launch_bounds__(DecodeCfg<D, HPC, KW>::kThreads, 2)
     load_page(pg, block_of(pg), j % kStages);
   }
 
-  const int g = lane >> 2;  // MMA row (query head within the group), and +8
+  const int g = lane >> 2;  // MMA row group
   const int cq = lane & 3;  // MMA column pair
   const int t = a.qsl[seq];
-  const uint16_t *qrow = a.q + t * a.q_stride + static_cast<int64_t>(kvh) * group * D;
-  uint32_t qa[kSteps][4];
-#pragma unroll
-  for (int ks = 0; ks < kSteps; ++ks) {
-    const int d0 = ks * 16 + 2 * cq;
-    qa[ks][0] = g < group ? *reinterpret_cast<const uint32_t *>(qrow + g * D + d0) : 0u;
-    qa[ks][1] = g + 8 < group ? *reinterpret_cast<const uint32_t *>(qrow + (g + 8) * D + d0) : 0u;
-    qa[ks][2] = g < group ? *reinterpret_cast<const uint32_t *>(qrow + g * D + d0 + 8) : 0u;
-    qa[ks][3] = g + 8 < group ? *reinterpret_cast<const uint32_t *>(qrow + (g + 8) * D + d0 + 8) : 0u;
-  }
-  float o[kNTiles][4];
-#pragma unroll
-  for (int i = 0; i < kNTiles; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-  float m_run[2] = {-INFINITY, -INFINITY};
-  float l_run[2] = {0.f, 0.f};
+  TokMath<kBf16, D, NT> mth;
+  mth.load_q(a.q + t * a.q_stride + static_cast<int64_t>(kvh) * group * D, group);
+  mth.reset();
   bool ok = true;
 
   for (int i = 0; i < my_pages; ++i) {
@@ -841,81 +921,75 @@ __global__ void __launch_bounds__(DecodeCfg<D, HPC, KW>::kThreads, 2)
     const uint32_t ph = (i / kStages) & 1;
     if (!__all_sync(0xffffffffu, mbar_wait(&ready[s], ph, abort_flag))) { ok = false; break; }
     const uint32_t kbase = ring + s * Cfg::kPageBytes;
-    decode_page<kBf16, D>(kbase, kbase + Cfg::kHeadBytes, qa, o, m_run, l_run,
-                          (p_begin + pg) * kPageTokens + 2 * cq, end, a.scale_log2);
+    mth.page(kbase, kbase + Cfg::kHeadBytes, (p_begin + pg) * kPageTokens, end, a.scale_log2);
     __syncwarp();
   }
   cp_async_wait_all();
-
-  // Row sums are spread over the 4 lanes of a row group.
-#pragma unroll
-  for (int hr = 0; hr < 2; ++hr) {
-    l_run[hr] += __shfl_xor_sync(0xffffffffu, l_run[hr], 1);
-    l_run[hr] += __shfl_xor_sync(0xffffffffu, l_run[hr], 2);
-  }
+  mth.finish();
   asm volatile("bar.sync 1, %0;" ::"n"(kConsumers) : "memory");
   if (!ok || *abort_flag) return;  // a failed wait raised the (CTA-wide) abort flag
 
   if constexpr (KW > 1) {
-    // Merge the warps' partial softmax results: rescale each to the rows'
+    // Merge the warps' partial softmax results: rescale each to the heads'
     // common maximum, sum in shared memory; warp 0 carries the result.
-    float *ml = reinterpret_cast<float *>(smem);  // [KW][16][2]: (m, l)
-    float *obuf = reinterpret_cast<float *>(smem + Cfg::kMergeObufOff);
-    if (cq == 0) {
+    constexpr int kHeads = NT * 8;
+    float *ml = reinterpret_cast<float *>(smem);  // [KW][kHeads][2]: (m, l)
+    float *obuf = reinterpret_cast<float *>(smem + Cfg::kMergeObufOff);  // [KW][kHeads][D]
+    if (g == 0) {
 #pragma unroll
-      for (int hr = 0; hr < 2; ++hr) {
-        ml[(warp * 16 + g + 8 * hr) * 2] = m_run[hr];
-        ml[(warp * 16 + g + 8 * hr) * 2 + 1] = l_run[hr];
-      }
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const int h = nt * 8 + 2 * cq + j;
+          ml[(warp * kHeads + h) * 2] = mth.m_run[nt][j];
+          ml[(warp * kHeads + h) * 2 + 1] = mth.l_run[nt][j];
+        }
     }
     asm volatile("bar.sync 1, %0;" ::"n"(kConsumers) : "memory");
-    float scale[2], m_all[2], l_all[2];
 #pragma unroll
-    for (int hr = 0; hr < 2; ++hr) {
-      const int row = g + 8 * hr;
-      m_all[hr] = -INFINITY;
+    for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-      for (int w = 0; w < KW; ++w) m_all[hr] = fmaxf(m_all[hr], ml[(w * 16 + row) * 2]);
-      l_all[hr] = 0.f;
+      for (int j = 0; j < 2; ++j) {
+        const int h = nt * 8 + 2 * cq + j;
+        float m_all = -INFINITY;
 #pragma unroll
-      for (int w = 0; w < KW; ++w) {
-        const float mw = ml[(w * 16 + row) * 2];
-        l_all[hr] += mw == -INFINITY ? 0.f : ml[(w * 16 + row) * 2 + 1] * exp2f(mw - m_all[hr]);
+        for (int w = 0; w < KW; ++w) m_all = fmaxf(m_all, ml[(w * kHeads + h) * 2]);
+        float l_all = 0.f;
+#pragma unroll
+        for (int w = 0; w < KW; ++w) {
+          const float mw = ml[(w * kHeads + h) * 2];
+          l_all += mw == -INFINITY ? 0.f : ml[(w * kHeads + h) * 2 + 1] * exp2f(mw - m_all);
+        }
+        const float sc = mth.m_run[nt][j] == -INFINITY ? 0.f : exp2f(mth.m_run[nt][j] - m_all);
+        float *ob = obuf + static_cast<int64_t>(warp * kHeads + h) * D + g;
+#pragma unroll
+        for (int mt = 0; mt < kSteps; ++mt) {
+          ob[mt * 16] = mth.o[mt][nt][j] * sc;
+          ob[mt * 16 + 8] = mth.o[mt][nt][2 + j] * sc;
+        }
+        mth.m_run[nt][j] = m_all;
+        mth.l_run[nt][j] = l_all;
       }
-      scale[hr] = m_run[hr] == -INFINITY ? 0.f : exp2f(m_run[hr] - m_all[hr]);
-    }
-#pragma unroll
-    for (int n = 0; n < kNTiles; ++n) {
-      const int col = n * 8 + 2 * cq;
-      *reinterpret_cast<float2 *>(obuf + (warp * 16 + g) * D + col) = make_float2(o[n][0] * scale[0], o[n][1] * scale[0]);
-      *reinterpret_cast<float2 *>(obuf + (warp * 16 + g + 8) * D + col) =
-          make_float2(o[n][2] * scale[1], o[n][3] * scale[1]);
-    }
     asm volatile("bar.sync 1, %0;" ::"n"(kConsumers) : "memory");
     if (warp == 0) {
 #pragma unroll
-      for (int n = 0; n < kNTiles; ++n) {
-        const int col = n * 8 + 2 * cq;
-        float2 s0 = make_float2(0.f, 0.f), s1 = make_float2(0.f, 0.f);
+      for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-        for (int w = 0; w < KW; ++w) {
-          const float2 v0 = *reinterpret_cast<const float2 *>(obuf + (w * 16 + g) * D + col);
-          const float2 v1 = *reinterpret_cast<const float2 *>(obuf + (w * 16 + g + 8) * D + col);
-          s0.x += v0.x;
-          s0.y += v0.y;
-          s1.x += v1.x;
-          s1.y += v1.y;
+        for (int j = 0; j < 2; ++j) {
+          const int h = nt * 8 + 2 * cq + j;
+#pragma unroll
+          for (int mt = 0; mt < kSteps; ++mt) {
+            float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+            for (int w = 0; w < KW; ++w) {
+              const float *ob = obuf + static_cast<int64_t>(w * kHeads + h) * D + g;
+              s0 += ob[mt * 16];
+              s1 += ob[mt * 16 + 8];
+            }
+            mth.o[mt][nt][j] = s0;
+            mth.o[mt][nt][2 + j] = s1;
+          }
         }
-        o[n][0] = s0.x;
-        o[n][1] = s0.y;
-        o[n][2] = s1.x;
-        o[n][3] = s1.y;
-      }
-#pragma unroll
-      for (int hr = 0; hr < 2; ++hr) {
-        m_run[hr] = m_all[hr];
-        l_run[hr] = l_all[hr];
-      }
     }
     asm volatile("bar.sync 1, %0;" ::"n"(kConsumers) : "memory");  // scratch free again
   }
@@ -924,27 +998,12 @@ __global__ void __launch_bounds__(DecodeCfg<D, HPC, KW>::kThreads, 2)
   // split, else this split's normalised output and log2-sum-exp; the last split
   // to finish (per-(request, head group) semaphore) combines the splits.
   const int nsplit = (ctx + a.chunk_tokens - 1) / a.chunk_tokens;
-#pragma unroll
-  for (int hr = 0; hr < 2; ++hr) {
-    const int row = g + 8 * hr;
-    if (row >= group || (KW > 1 && warp != 0)) continue;
-    const int h = kvh * group + row;
-    const float inv = 1.f / l_run[hr];
-    if (nsplit == 1) {
-      uint16_t *dst = a.out + t * a.o_stride + static_cast<int64_t>(h) * D;
-#pragma unroll
-      for (int n = 0; n < kNTiles; ++n)
-        *reinterpret_cast<uint32_t *>(dst + n * 8 + 2 * cq) =
-            pack2<kBf16>(o[n][2 * hr] * inv, o[n][2 * hr + 1] * inv);
-    } else {
-      const int64_t base = (static_cast<int64_t>(seq) * a.Hq + h) * a.max_splits + split;
-      float *dst = a.part_o + base * D;
-#pragma unroll
-      for (int n = 0; n < kNTiles; ++n)
-        __stcg(reinterpret_cast<float2 *>(dst + n * 8 + 2 * cq),
-               make_float2(o[n][2 * hr] * inv, o[n][2 * hr + 1] * inv));
-      if (cq == 0) __stcg(a.part_lse + base, m_run[hr] + log2f(l_run[hr]));
-    }
+  if (KW == 1 || warp == 0) {
+    if (nsplit == 1)
+      mth.store(a.out + t * a.o_stride + static_cast<int64_t>(kvh) * group * D, group);
+    else
+      mth.store_partial(a.part_o + static_cast<int64_t>(split) * D, a.part_lse + split,
+                        static_cast<int64_t>(seq) * a.Hq + kvh * group, a.max_splits, group);
   }
   if (nsplit == 1) return;
   __threadfence();
@@ -994,14 +1053,12 @@ __host__ __device__ inline int flat_max_pieces(int max_pages) {
   return (max_pages + kFlatMinPages - 1) / kFlatMinPages + 1;
 }
 
-template <bool kBf16, int D, int HPC>
+template <bool kBf16, int D, int HPC, int NT = 1>
 __global__ void __launch_bounds__(HPC * 32, 2) paged_decode_flat_kernel(const AttnArgs a) {
   pdl_entry();
   using Base = DecodeCfg<D, HPC, 1>;
   using Cfg = FlatCfg<D, HPC>;
   constexpr int kStages = Base::kStages;
-  constexpr int kSteps = D / 16;
-  constexpr int kNTiles = D / 8;
   constexpr int kThreads = HPC * 32;
   constexpr int kChunksPerLane = Base::kHeadBytes / 16 / 32;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -1127,11 +1184,7 @@ __global__ void __launch_bounds__(HPC * 32, 2) paged_decode_flat_kernel(const At
 #pragma unroll 1
   for (int j = 0; j < kStages - 1 && j < npg; ++j) load_page(j, j);
 
-  const int g = lane >> 2;
-  const int cq = lane & 3;
-  uint32_t qa[kSteps][4];
-  float o[kNTiles][4];
-  float m_run[2], l_run[2];
+  TokMath<kBf16, D, NT> mth;
   int z = find_req(g0);
   int seg_first = prefix[z] - g0;  // CTA page index of the request's page 0 (<= 0 for the first segment)
   int seg_end = prefix[z + 1] - g0;
@@ -1141,19 +1194,8 @@ __global__ void __launch_bounds__(HPC * 32, 2) paged_decode_flat_kernel(const At
 
   auto start_segment = [&]() {
     const int seq = seq_sm[z];
-    const uint16_t *qrow = a.q + static_cast<int64_t>(a.qsl[seq]) * a.q_stride + static_cast<int64_t>(kvh) * group * D;
-#pragma unroll
-    for (int ks = 0; ks < kSteps; ++ks) {
-      const int d0 = ks * 16 + 2 * cq;
-      qa[ks][0] = g < group ? *reinterpret_cast<const uint32_t *>(qrow + g * D + d0) : 0u;
-      qa[ks][1] = g + 8 < group ? *reinterpret_cast<const uint32_t *>(qrow + (g + 8) * D + d0) : 0u;
-      qa[ks][2] = g < group ? *reinterpret_cast<const uint32_t *>(qrow + g * D + d0 + 8) : 0u;
-      qa[ks][3] = g + 8 < group ? *reinterpret_cast<const uint32_t *>(qrow + (g + 8) * D + d0 + 8) : 0u;
-    }
-#pragma unroll
-    for (int i = 0; i < kNTiles; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-    m_run[0] = m_run[1] = -INFINITY;
-    l_run[0] = l_run[1] = 0.f;
+    mth.load_q(a.q + static_cast<int64_t>(a.qsl[seq]) * a.q_stride + static_cast<int64_t>(kvh) * group * D, group);
+    mth.reset();
   };
   // The segment's output: final rows when the request lies wholly in this
   // CTA, else this CTA's piece (normalised output and log2-sum-exp).
@@ -1162,38 +1204,17 @@ __global__ void __launch_bounds__(HPC * 32, 2) paged_decode_flat_kernel(const At
     const int first_cta = prefix[z] / per_cta;
     const int pieces = (prefix[z + 1] - 1) / per_cta - first_cta + 1;
     const int piece = static_cast<int>(blockIdx.x) - first_cta;
-#pragma unroll
-    for (int hr = 0; hr < 2; ++hr) {
-      l_run[hr] += __shfl_xor_sync(0xffffffffu, l_run[hr], 1);
-      l_run[hr] += __shfl_xor_sync(0xffffffffu, l_run[hr], 2);
-    }
+    mth.finish();
     if (pieces > a.max_splits) {
       if (tid == 0) record_device_error(LVB_DEVERR_INDEX);
       return;
     }
-#pragma unroll
-    for (int hr = 0; hr < 2; ++hr) {
-      const int row = g + 8 * hr;
-      if (row >= group) continue;
-      const int h = kvh * group + row;
-      const float inv = 1.f / l_run[hr];
-      if (pieces == 1) {
-        uint16_t *dst = a.out + static_cast<int64_t>(a.qsl[seq]) * a.o_stride + static_cast<int64_t>(h) * D;
-#pragma unroll
-        for (int nt = 0; nt < kNTiles; ++nt)
-          *reinterpret_cast<uint32_t *>(dst + nt * 8 + 2 * cq) =
-              pack2<kBf16>(o[nt][2 * hr] * inv, o[nt][2 * hr + 1] * inv);
-      } else {
-        const int64_t base = (static_cast<int64_t>(seq) * a.Hq + h) * a.max_splits + piece;
-        float *dst = a.part_o + base * D;
-#pragma unroll
-        for (int nt = 0; nt < kNTiles; ++nt)
-          __stcg(reinterpret_cast<float2 *>(dst + nt * 8 + 2 * cq),
-                 make_float2(o[nt][2 * hr] * inv, o[nt][2 * hr + 1] * inv));
-        if (cq == 0) __stcg(a.part_lse + base, m_run[hr] + log2f(l_run[hr]));
-      }
-    }
-    if (pieces > 1) {
+    if (pieces == 1) {
+      mth.store(a.out + static_cast<int64_t>(a.qsl[seq]) * a.o_stride + static_cast<int64_t>(kvh) * group * D,
+                group);
+    } else {
+      mth.store_partial(a.part_o + static_cast<int64_t>(piece) * D, a.part_lse + piece,
+                        static_cast<int64_t>(seq) * a.Hq + kvh * group, a.max_splits, group);
       if (pend_seq0 < 0) {
         pend_seq0 = seq;
         pend_n0 = pieces;
@@ -1219,8 +1240,7 @@ __global__ void __launch_bounds__(HPC * 32, 2) paged_decode_flat_kernel(const At
     const uint32_t ph = (i / kStages) & 1;
     if (!__all_sync(0xffffffffu, mbar_wait(&ready[s], ph, abort_flag))) { ok = false; break; }
     const uint32_t kbase = ring + s * Base::kPageBytes;
-    decode_page<kBf16, D>(kbase, kbase + Base::kHeadBytes, qa, o, m_run, l_run,
-                          (i - seg_first) * kPageTokens + 2 * cq, ctx_sm[z], a.scale_log2);
+    mth.page(kbase, kbase + Base::kHeadBytes, (i - seg_first) * kPageTokens, ctx_sm[z], a.scale_log2);
     __syncwarp();
   }
   cp_async_wait_all();
