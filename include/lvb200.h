@@ -291,6 +291,15 @@ LVB_API int lvb_event_destroy(void *event);
 LVB_API int lvb_event_record(void *event, lvb_stream_t stream);
 LVB_API int lvb_event_wait_host(void *event);
 
+/* Stream plumbing for callers that overlap their own host<->device copies
+ * with the attention and projection launches (no counterpart in the
+ * reference, whose Python callers use torch.cuda streams): make `stream`
+ * wait for `event` (cudaStreamWaitEvent), and copy `bytes` bytes between any
+ * two addresses on `stream` (cudaMemcpyAsync, direction inferred; host
+ * memory should be pinned for the copy to be asynchronous). */
+LVB_API int lvb_stream_wait_event(lvb_stream_t stream, void *event);
+LVB_API int lvb_copy_async(void *dst, const void *src, size_t bytes, lvb_stream_t stream);
+
 /* Bytes of workspace `lvb_paged_attention` needs: split-context partial
  * outputs and log-sum-exps, then one merge semaphore per (request, KV head).
  * A workspace must be zero-filled once before its first use; every call

@@ -19,7 +19,7 @@ from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().parent / "_lib" / "liblvb200.so"
 HOSTPACK_PATH = Path(__file__).resolve().parent / "_lib" / ("_hostpack" + sysconfig.get_config_var("EXT_SUFFIX"))
-ABI_VERSION = 6
+ABI_VERSION = 7
 
 LVB_OK = 0
 LVB_ERR_INVALID = 1
@@ -93,6 +93,8 @@ PROTOTYPES: dict[str, tuple[object, tuple[object, ...]]] = {
     "lvb_event_destroy": (_int, (_c_ptr,)),
     "lvb_event_record": (_int, (_c_ptr, _c_ptr)),
     "lvb_event_wait_host": (_int, (_c_ptr,)),
+    "lvb_stream_wait_event": (_int, (_c_ptr, _c_ptr)),
+    "lvb_copy_async": (_int, (_c_ptr, _c_ptr, _size, _c_ptr)),
     "lvb_ipc_alloc": (_int, (_size, ctypes.POINTER(_c_ptr), _c_ptr)),
     "lvb_ipc_open": (_int, (_c_ptr, ctypes.POINTER(_c_ptr))),
     "lvb_ipc_close": (_int, (_c_ptr,)),

@@ -79,27 +79,33 @@ static int row_values(PyObject *seq, Py_ssize_t n, int32_t *dst, const char *wha
   return 0;
 }
 
-/* 1 if layout.parent_indices is (-1, 0, ..., len - 2), 0 if not, -1 on error. */
-static int is_linear(PyObject *layout) {
+/* The query count of a layout, len(layout.parent_indices), and when
+ * `linear` is given whether the parents are (-1, 0, ..., len - 2).  Returns
+ * 0 with an exception set on error. */
+static int layout_shape(PyObject *layout, Py_ssize_t *len, int *linear) {
   PyObject *parents = PyObject_GetAttr(layout, parent_indices_name);
-  if (!parents) return -1;
+  if (!parents) return 0;
   PyObject *fast = PySequence_Fast(parents, "parent_indices");
   Py_DECREF(parents);
-  if (!fast) return -1;
+  if (!fast) return 0;
   const Py_ssize_t n = PySequence_Fast_GET_SIZE(fast);
-  PyObject **items = PySequence_Fast_ITEMS(fast);
-  int linear = 1;
-  for (Py_ssize_t j = 0; j < n && linear; ++j) {
-    int overflow = 0;
-    long long v = PyLong_AsLongLongAndOverflow(items[j], &overflow);
-    if (v == -1 && PyErr_Occurred()) {
-      Py_DECREF(fast);
-      return -1;
+  *len = n;
+  if (linear) {
+    PyObject **items = PySequence_Fast_ITEMS(fast);
+    int lin = 1;
+    for (Py_ssize_t j = 0; j < n && lin; ++j) {
+      int overflow = 0;
+      long long v = PyLong_AsLongLongAndOverflow(items[j], &overflow);
+      if (v == -1 && PyErr_Occurred()) {
+        Py_DECREF(fast);
+        return 0;
+      }
+      lin = !overflow && v == (long long)j - 1;
     }
-    linear = !overflow && v == (long long)j - 1;
+    *linear = lin;
   }
   Py_DECREF(fast);
-  return linear;
+  return 1;
 }
 
 static PyObject *gather_step(PyObject *self, PyObject *args) {
@@ -134,8 +140,19 @@ static PyObject *gather_step(PyObject *self, PyObject *args) {
       goto fail;
     }
     PyObject **items = PySequence_Fast_ITEMS(row);
+    int32_t *dst = ids + total;
     for (Py_ssize_t i = 0; i < len; ++i) {
-      if (to_i32(items[i], &ids[total + i], 1) < 0) {
+#if PY_VERSION_HEX >= 0x030C0000
+      /* Inline fast path: exact one-digit ints (every block id in practice). */
+      PyObject *o = items[i];
+      if (i + 8 < len) __builtin_prefetch(items[i + 8]);
+      if (PyLong_CheckExact(o) && PyUnstable_Long_IsCompact((PyLongObject *)o)) {
+        const Py_ssize_t v = PyUnstable_Long_CompactValue((PyLongObject *)o);
+        dst[i] = v >= INT32_MIN && v <= INT32_MAX ? (int32_t)v : -1;
+        continue;
+      }
+#endif
+      if (to_i32(items[i], &dst[i], 1) < 0) {
         Py_DECREF(row);
         goto fail;
       }
@@ -158,8 +175,12 @@ static PyObject *gather_step(PyObject *self, PyObject *args) {
   }
   PyObject **litems = PySequence_Fast_ITEMS(lfast);
   for (Py_ssize_t r = 0; r < n; ++r) {
-    const Py_ssize_t len = PyObject_Size(litems[r]);
-    if (len < 0) goto fail;
+    /* A layout's length is that of its parent_indices (QueryLayout.__len__,
+     * runtime/execution/interfaces.py:96-97); reading the tuple directly
+     * avoids one Python-level call per request. */
+    Py_ssize_t len;
+    int l = 1;
+    if (!layout_shape(litems[r], &len, linear ? &l : NULL)) goto fail;
     if (len > INT32_MAX) {
       PyErr_SetString(PyExc_OverflowError, "step metadata count does not fit int32");
       goto fail;
@@ -169,11 +190,7 @@ static PyObject *gather_step(PyObject *self, PyObject *args) {
     single += len == 1;
     if (len > max_query) max_query = len;
     if ((long long)comp[r] + len > max_seq) max_seq = (long long)comp[r] + len;
-    if (linear) {
-      const int l = is_linear(litems[r]);
-      if (l < 0) goto fail;
-      linear = l;
-    }
+    linear = linear && l;
   }
   Py_DECREF(lfast);
   Py_DECREF(tfast);

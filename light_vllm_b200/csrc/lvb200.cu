@@ -31,7 +31,7 @@
 
 namespace {
 
-constexpr int kAbiVersion = 6;
+constexpr int kAbiVersion = 7;
 constexpr int kMaxDevices = 64;
 
 thread_local char g_last_error[512] = "";
@@ -1435,6 +1435,19 @@ int lvb_event_wait_host(void *event) {
   cudaError_t err = cudaEventQuery(e);
   if (err == cudaErrorNotReady) err = cudaEventSynchronize(e);
   return err == cudaSuccess ? LVB_OK : cuda_fail(err, "waiting for a staging copy");
+}
+
+int lvb_stream_wait_event(lvb_stream_t stream, void *event) {
+  if (!event) return fail(LVB_ERR_INVALID, "lvb_stream_wait_event: null event");
+  cudaError_t err = cudaStreamWaitEvent(reinterpret_cast<cudaStream_t>(stream), static_cast<cudaEvent_t>(event), 0);
+  return err == cudaSuccess ? LVB_OK : cuda_fail(err, "cudaStreamWaitEvent");
+}
+
+int lvb_copy_async(void *dst, const void *src, size_t bytes, lvb_stream_t stream) {
+  if (bytes == 0) return LVB_OK;
+  if (!dst || !src) return fail(LVB_ERR_INVALID, "lvb_copy_async: null pointer");
+  cudaError_t err = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, reinterpret_cast<cudaStream_t>(stream));
+  return err == cudaSuccess ? LVB_OK : cuda_fail(err, "cudaMemcpyAsync");
 }
 
 int lvb_stage_step_metadata(const int32_t *block_ids, const int64_t *table_offsets,

@@ -180,6 +180,7 @@ class B200PagedAttention:
         self._backend = backend
         self._layer_ids: set[str] = set()
         self._device = device
+        self._device_index = device.index
         self._dtype = config.dtype
         # Gathering from the metadata objects, validation (the reference's
         # block-table rules, same order and messages), packing and the one
@@ -252,23 +253,24 @@ class B200PagedAttention:
         self._layer_ids.add(layer_id)
         info = self._backend._layer_info(self._cache, layer_id)
         # Shape rules shared with the reference backends (paged_attention.py:226-247).
-        if query.ndim != 3:
+        qs, ks = query.shape, key.shape
+        if len(qs) != 3:
             raise KVCacheError("paged attention query must have three dimensions")
-        if query.shape[0] != key.shape[0] or value.shape != key.shape:
+        if qs[0] != ks[0] or value.shape != ks:
             raise KVCacheError("paged attention Q/K/V token dimensions must match")
-        if query.shape[0] != self._num_tokens:
+        if qs[0] != self._num_tokens:
             raise KVCacheError("paged attention metadata token count does not match query")
-        if query.shape[1:] != info.q_tail:
+        if qs[1:] != info.q_tail:
             raise KVCacheError("paged attention query shape does not match the layer spec")
-        if key.shape[1:] != info.kv_tail:
+        if ks[1:] != info.kv_tail:
             raise KVCacheError("paged attention K/V shape does not match the layer spec")
-        dev, dt = self._device, self._dtype
-        if (query.dtype != dt or key.dtype != dt or value.dtype != dt or query.device != dev
-                or key.device != dev or value.device != dev):
+        dt, index = self._dtype, self._device_index
+        if (query.dtype != dt or key.dtype != dt or value.dtype != dt or query.get_device() != index
+                or key.get_device() != index or value.get_device() != index):
             raise KVCacheError("B200 query/key/value dtype and device must match the KV cache")
         if info.kv_tail[1] % 8 or info.kv_tail[1] > 256:
             raise KVCacheError("B200 paged attention supports head sizes that are multiples of 8 up to 256")
-        out = torch.empty(query.shape, dtype=dt, device=dev)
+        out = torch.empty_like(query, memory_format=torch.contiguous_format)
         return self._launch(info, query, key, value, float(scale), out, write_kv)
 
     def rope_write_kv(self, layer_id: str, qkv: Tensor, q_heads: int, kv_heads: int, positions: Tensor,
