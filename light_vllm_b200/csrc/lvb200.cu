@@ -576,6 +576,11 @@ constexpr int64_t kMinSplitPagesSmall = 8;
 constexpr int64_t kMinSplitPagesLarge = 16;
 // Batches below this many requests run one KV head per CTA.
 constexpr int64_t kAttnSmallBatch = 32;
+// The balanced schedule (paged_decode_flat_kernel) measured slower than the
+// split kernel on the decode batches tried on B200 (config 2: 65.7 vs
+// 59.9 us; uniform 2304-token contexts 69.1 vs 69.1), so large batches take
+// the split kernel.
+constexpr bool kBalancedDecode = false;
 
 DecodePlan decode_plan(int64_t num_seqs, int64_t hq, int64_t hkv, int64_t d, int64_t max_seq_len,
                        int sms) {
@@ -607,7 +612,7 @@ DecodePlan decode_plan(int64_t num_seqs, int64_t hq, int64_t hkv, int64_t d, int
   // Large batches run the balanced schedule when its tables and merge
   // weights fit in shared memory (one CTA's page rings hold the weights).
   p.flat = false;
-  if (!small && num_seqs <= lvb::attn::kFlatMaxSeqs && max_pages <= INT_MAX / 2) {
+  if (kBalancedDecode && !small && num_seqs <= lvb::attn::kFlatMaxSeqs && max_pages <= INT_MAX / 2) {
     const int pieces = lvb::attn::flat_max_pieces(static_cast<int>(max_pages));
     const int ring_bytes = hpc == 4   ? (d == 128 ? lvb::attn::DecodeCfg<128, 4>::kBarOff : lvb::attn::DecodeCfg<64, 4>::kBarOff)
                            : hpc == 2 ? (d == 128 ? lvb::attn::DecodeCfg<128, 2>::kBarOff : lvb::attn::DecodeCfg<64, 2>::kBarOff)

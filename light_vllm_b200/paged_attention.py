@@ -136,24 +136,19 @@ class StepMetadataPacker:
     def stage(self, staging: SingleStepStaging, num_blocks: int, block_size: int) -> Tensor:
         """Validate, pack and copy the gathered step to the device in one
         native call (``lvb_stage_step_metadata``) through a staging slot;
-        returns the device payload (``packed_size`` int32 values)."""
+        returns the device buffer whose first ``packed_size`` int32 values
+        are the payload."""
 
         step = self._step
         if step is None:
             raise RuntimeError("StepMetadataPacker.stage before gather")
-        n = step.num_seqs
-        hostpack = self._hostpack
-
-        def run(host_ptr: int, host_capacity: int, dev_ptr: int, dev_capacity: int, event: int,
-                stream: int) -> int:
-            status, _, _ = hostpack.stage_step(self._ids_ptr, self._offsets_ptr, self._rows_ptr, n, num_blocks,
-                                               block_size, host_ptr, host_capacity, dev_ptr, dev_capacity, event,
-                                               stream)
-            if status:
-                _native.check(status, "lvb_stage_step_metadata")
-            return step.packed_size
-
-        return staging.stage(step.packed_size, run)
+        dev, host_ptr, host_cap, dev_ptr, dev_cap, event, stream = staging.slot(step.packed_size)
+        status, _, _ = self._hostpack.stage_step(self._ids_ptr, self._offsets_ptr, self._rows_ptr, step.num_seqs,
+                                                 num_blocks, block_size, host_ptr, host_cap, dev_ptr, dev_cap,
+                                                 event, stream)
+        if status:
+            _native.check(status, "lvb_stage_step_metadata")
+        return dev
 
 
 class _LayerInfo(NamedTuple):

@@ -127,3 +127,12 @@ class SingleStepStaging:
         total = int(run(host.data_ptr(), host.numel(), dev.data_ptr(), dev.numel(), self._event(slot),
                         self._stream()))
         return dev[:total]
+
+    def slot(self, capacity: int) -> tuple[Tensor, int, int, int, int, int, int]:
+        """The next ring slot for a native stager: (device buffer, pinned
+        address, pinned capacity, device address, device capacity, slot
+        event, stream).  The device buffer is returned whole (the payload
+        starts at its first value); keep it alive while launches read it."""
+
+        slot, host, dev = self._next_slot(capacity)
+        return dev, host.data_ptr(), host.numel(), dev.data_ptr(), dev.numel(), self._event(slot), self._stream()
