@@ -668,6 +668,11 @@ int launch_decode(const lvb::attn::AttnArgs &a, int64_t num_seqs, int64_t num_bl
   dim3 grid(a.max_splits, a.Hkv / HPC, static_cast<unsigned>(num_seqs));
   cudaError_t e = launch_pdl(kernel, grid, dim3(Cfg::kThreads), Cfg::kSmemBytes, stream, a);
   if (e != cudaSuccess) return cuda_fail(e, "paged_decode_kernel launch");
+  if (a.max_splits > 1) {
+    e = launch_pdl(lvb::attn::decode_merge_kernel<kBf16, D>, dim3((a.Hq + 3) / 4, static_cast<unsigned>(num_seqs)),
+                   dim3(128), 0, stream, a);
+    if (e != cudaSuccess) return cuda_fail(e, "decode_merge_kernel launch");
+  }
   return LVB_OK;
 }
 
@@ -689,12 +694,16 @@ int launch_decode_flat(lvb::attn::AttnArgs a, int64_t num_seqs, int dev, cudaStr
     resident[dev] = nb > 0 ? nb : 1;
   }
   a.decode_seqs = static_cast<int>(num_seqs);
+  a.heads_per_cta = HPC;
   const int groups = a.Hkv / HPC;
   int ctas = resident[dev] * sm_count(dev) / groups;
   if (ctas < 1) ctas = 1;
   const dim3 grid(static_cast<unsigned>(ctas), static_cast<unsigned>(groups));
   cudaError_t e = launch_pdl(kernel, grid, dim3(HPC * 32), Cfg::smem_bytes(static_cast<int>(num_seqs)), stream, a);
   if (e != cudaSuccess) return cuda_fail(e, "paged_decode_flat_kernel launch");
+  e = launch_pdl(lvb::attn::decode_merge_kernel<kBf16, D, true>, dim3((a.Hq + 3) / 4, static_cast<unsigned>(num_seqs)),
+                 dim3(128), 0, stream, a);
+  if (e != cudaSuccess) return cuda_fail(e, "decode_merge_kernel launch");
   return LVB_OK;
 }
 

@@ -106,6 +106,7 @@ struct AttnArgs {
   int chunk_tokens;  // multiple of 16
   int num_seqs;
   int decode_seqs;   // balanced decode schedule: requests (launch order slots 0 .. decode_seqs - 1)
+  int heads_per_cta; // balanced decode schedule: KV heads per CTA (merge_count holds pieces per head group)
   // prefill tile kernel: requests order[first_tile_req + blockIdx.y] (the
   // packer lists one-token requests first; the decode kernel serves those), or
   // blockIdx.y itself when order is null
@@ -526,6 +527,7 @@ struct DecodeCfg {
   // head, then the scaled outputs [KW][up to 16 heads][D] fp32.
   static constexpr int kMergeObufOff = 1024;
   static_assert(KW == 1 || kMergeObufOff + KW * 16 * D * 4 <= kBarOff, "merge scratch (16 heads) fits in the ring");
+  static_assert(kWarps * 16 * (D + 4) * 4 <= kBarOff, "output staging (16 heads per warp) fits in the ring");
 };
 
 // Decode math of one warp over one (request, KV head): the page's 16 tokens
@@ -686,6 +688,60 @@ struct TokMath {
           dst[mt * 16 + 8] = from_float<kBf16>(o[mt][nt][2 + j] * inv);
         }
       }
+  }
+
+  // Rows of the staging area used by store_staged: D floats plus 4 of
+  // padding, so the lanes' fragment writes (heads 2 c + j, dims g) hit 32
+  // distinct banks.
+  static constexpr int kStageRow = D + 4;
+  static constexpr int kStageBytes = NT * 8 * kStageRow * 4;
+
+  // The normalised output of the group's heads (after finish()) through this
+  // warp's `stage` (kStageBytes of shared memory, 16-byte aligned): written
+  // as fragments, read back as rows, stored with 16-byte stores -- fp32
+  // partial rows at part_o + (head_base + h) * stride * D (kPartial; the
+  // log2-sum-exp at part_lse + (head_base + h) * stride), else the output
+  // rows in the cache dtype at out_head0 + h * D.
+  template <bool kPartial>
+  __device__ __forceinline__ void store_staged(float *stage, uint16_t *out_head0, float *part_o, float *part_lse,
+                                               int64_t head_base, int64_t stride, int group) const {
+    const int lane = threadIdx.x & 31;
+    const int g = lane >> 2, cq = lane & 3;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int h = nt * 8 + 2 * cq + j;
+        const float inv = h < group ? 1.f / l_run[nt][j] : 0.f;
+        float *row = stage + h * kStageRow + g;
+#pragma unroll
+        for (int mt = 0; mt < kSteps; ++mt) {
+          row[mt * 16] = o[mt][nt][j] * inv;
+          row[mt * 16 + 8] = o[mt][nt][2 + j] * inv;
+        }
+        if (kPartial && g == 0 && h < group) __stcg(part_lse + (head_base + h) * stride, m_run[nt][j] + log2f(l_run[nt][j]));
+      }
+    __syncwarp();
+    constexpr int kPer = kPartial ? 4 : 8;  // values per 16-byte store
+    constexpr int kChunks = D / kPer;
+    for (int idx = lane; idx < group * kChunks; idx += 32) {
+      const int h = idx / kChunks;
+      const int c = idx - h * kChunks;
+      const float *src = stage + h * kStageRow + c * kPer;
+      if constexpr (kPartial) {
+        __stcg(reinterpret_cast<float4 *>(part_o + (head_base + h) * stride * D) + c,
+               *reinterpret_cast<const float4 *>(src));
+      } else {
+        const float4 v0 = *reinterpret_cast<const float4 *>(src);
+        const float4 v1 = *reinterpret_cast<const float4 *>(src + 4);
+        uint4 w;
+        w.x = pack2<kBf16>(v0.x, v0.y);
+        w.y = pack2<kBf16>(v0.z, v0.w);
+        w.z = pack2<kBf16>(v1.x, v1.y);
+        w.w = pack2<kBf16>(v1.z, v1.w);
+        *reinterpret_cast<uint4 *>(out_head0 + static_cast<int64_t>(h) * D + c * 8) = w;
+      }
+    }
   }
 
   // A split's normalised output and log2-sum-exp: head h's row at
@@ -995,34 +1051,126 @@ __global__ void __launch_bounds__(DecodeCfg<D, HPC, KW>::kThreads, 2)
   }
 
   // Each warp writes its own heads: the final output when the request has one
-  // split, else this split's normalised output and log2-sum-exp; the last split
-  // to finish (per-(request, head group) semaphore) combines the splits.
+  // split, else this split's normalised output and log2-sum-exp, which
+  // decode_merge_kernel (the next launch) combines.  The CTA then ends: a
+  // fence, a semaphore and a merge here held the CTA's SM slot, with no page
+  // in flight, for about a fifth of the kernel's time on B200 (config 2,
+  // pages streamed without the math: 45.2 us without them, 57.3 with).
   const int nsplit = (ctx + a.chunk_tokens - 1) / a.chunk_tokens;
   if (KW == 1 || warp == 0) {
-    if (nsplit == 1)
-      mth.store(a.out + t * a.o_stride + static_cast<int64_t>(kvh) * group * D, group);
+    // Staged through the warp's part of the (now idle) page ring.
+    float *stage = reinterpret_cast<float *>(smem + warp * TokMath<kBf16, D, NT>::kStageBytes);
+    uint16_t *out_head0 = a.out + t * a.o_stride + static_cast<int64_t>(kvh) * group * D;
+    // 16-byte output stores need 16-byte aligned rows (the API asks for 4).
+    const bool out16 = ((reinterpret_cast<uintptr_t>(a.out) | static_cast<uintptr_t>(a.o_stride * 2)) & 15u) == 0;
+    if (nsplit == 1 && out16)
+      mth.template store_staged<false>(stage, out_head0, nullptr, nullptr, 0, 0, group);
+    else if (nsplit == 1)
+      mth.store(out_head0, group);
     else
-      mth.store_partial(a.part_o + static_cast<int64_t>(split) * D, a.part_lse + split,
-                        static_cast<int64_t>(seq) * a.Hq + kvh * group, a.max_splits, group);
+      mth.template store_staged<true>(stage, nullptr, a.part_o + static_cast<int64_t>(split) * D, a.part_lse + split,
+                                      static_cast<int64_t>(seq) * a.Hq + kvh * group, a.max_splits, group);
   }
-  if (nsplit == 1) return;
-  __threadfence();
-  asm volatile("bar.sync 2, %0;" ::"n"(kConsumers) : "memory");
-  const int tid = threadIdx.x;
-  uint32_t *counter = a.merge_count + seq * (a.Hkv / HPC) + hg;
-  if (tid == 0) {
-    const unsigned int prev = atomicAdd(counter, 1u);
-    *last_flag = prev == static_cast<unsigned int>(nsplit - 1) ? 1 : 0;
-  }
-  asm volatile("bar.sync 2, %0;" ::"n"(kConsumers) : "memory");
-  if (!*last_flag) return;
-  __threadfence();
-  merge_partials<kBf16, D, kConsumers>(a, static_cast<int64_t>(seq) * a.Hq + hg * HPC * group, HPC * group, nsplit,
-                                       reinterpret_cast<float *>(smem),
-                                       a.out + t * a.o_stride + static_cast<int64_t>(hg) * HPC * group * D);
-  if (tid == 0) *counter = 0u;
 }
 
+// Combines the split kernel's partial results: one warp per (query head,
+// request in launch order), four heads per CTA (requests with one split were
+// written whole).  Lane l holds the log2-sum-exp of splits l, l + 32, ... and
+// D / 32 consecutive output values; the weights come from two warp
+// reductions and the splits' rows are read eight at a time, summed in split
+// order (the result does not depend on the launch shape).  A programmatic
+// dependent of the split kernel: it waits for that grid to complete first.
+constexpr int kMergeMaxSplits = 256;  // decode_plan's cap
+template <bool kBf16, int D, bool kFlat = false>
+__global__ void __launch_bounds__(128) decode_merge_kernel(const AttnArgs a) {
+  pdl_entry();
+  constexpr int kPer = D / 32;  // output values per lane: 4 (D = 128) or 2 (D = 64)
+  constexpr int kLse = kMergeMaxSplits / 32;
+  const int lane = threadIdx.x & 31;
+  const int h = blockIdx.x * 4 + (threadIdx.x >> 5);
+  const int z = blockIdx.y;
+  if (h >= a.Hq) return;
+  const int seq = a.order != nullptr ? a.order[z] : z;
+  const int ctx = (a.order != nullptr ? a.order[a.num_seqs + z] : a.computed[z]) + 1;
+  // The balanced kernel records each request's piece count (one per KV
+  // head group; every group has the same pieces).
+  const int nsplit = kFlat ? static_cast<int>(a.merge_count[static_cast<int64_t>(seq) * (a.Hkv / a.heads_per_cta)])
+                           : (ctx + a.chunk_tokens - 1) / a.chunk_tokens;
+  if (nsplit <= 1) return;
+  if (nsplit > a.max_splits || nsplit > kMergeMaxSplits) {
+    if (lane == 0) record_device_error(LVB_DEVERR_INDEX);
+    return;
+  }
+  const int64_t row0 = (static_cast<int64_t>(seq) * a.Hq + h) * a.max_splits;
+  const float *src = a.part_o + row0 * D + lane * kPer;
+  // One round trip for up to kBatch splits: their rows are loaded together
+  // with the log2-sum-exps, before the weights are known.
+  constexpr int kBatch = 16;
+  float v[kBatch][kPer];
+  auto load_rows = [&](int s0) {
+#pragma unroll
+    for (int b = 0; b < kBatch; ++b) {
+      const int sp = s0 + b;
+      if (sp < nsplit) {
+        if constexpr (kPer == 4) {
+          const float4 t = __ldcg(reinterpret_cast<const float4 *>(src + static_cast<int64_t>(sp) * D));
+          v[b][0] = t.x; v[b][1] = t.y; v[b][2] = t.z; v[b][3] = t.w;
+        } else {
+          const float2 t = __ldcg(reinterpret_cast<const float2 *>(src + static_cast<int64_t>(sp) * D));
+          v[b][0] = t.x; v[b][1] = t.y;
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < kPer; ++e) v[b][e] = 0.f;
+      }
+    }
+  };
+  float w[kLse];
+#pragma unroll
+  for (int k = 0; k < kLse; ++k) {
+    const int sp = k * 32 + lane;
+    w[k] = sp < nsplit ? __ldcg(a.part_lse + row0 + sp) : -INFINITY;
+  }
+  load_rows(0);
+  float m = -INFINITY;
+#pragma unroll
+  for (int k = 0; k < kLse; ++k) m = fmaxf(m, w[k]);
+  m = warp_max(m);
+  float sum = 0.f;
+#pragma unroll
+  for (int k = 0; k < kLse; ++k) {
+    w[k] = w[k] == -INFINITY ? 0.f : exp2f(w[k] - m);
+    sum += w[k];
+  }
+  const float inv = 1.f / warp_sum(sum);
+#pragma unroll
+  for (int k = 0; k < kLse; ++k) w[k] *= inv;
+  float acc[kPer];
+#pragma unroll
+  for (int e = 0; e < kPer; ++e) acc[e] = 0.f;
+  // Splits summed in order: s0 = 0, 16, 32, ... (weights by shuffle from
+  // lane sp % 32 of register sp / 32).
+  for (int s0 = 0; s0 < nsplit; s0 += kBatch) {
+    if (s0 > 0) load_rows(s0);
+#pragma unroll
+    for (int k = 0; k < kLse; ++k) {
+      if (k * 32 + 31 < s0 || k * 32 >= s0 + kBatch) continue;
+#pragma unroll
+      for (int b = 0; b < kBatch; ++b) {
+        const int sp = s0 + b;
+        if (sp / 32 != k) continue;
+        const float wt = __shfl_sync(0xffffffffu, w[k], sp & 31);
+        if (sp < nsplit) {
+#pragma unroll
+          for (int e = 0; e < kPer; ++e) acc[e] = fmaf(wt, v[b][e], acc[e]);
+        }
+      }
+    }
+  }
+  uint16_t *dst = a.out + static_cast<int64_t>(a.qsl[seq]) * a.o_stride + static_cast<int64_t>(h) * D + lane * kPer;
+#pragma unroll
+  for (int e = 0; e < kPer; e += 2) *reinterpret_cast<uint32_t *>(dst + e) = pack2<kBf16>(acc[e], acc[e + 1]);
+}
 
 // ------------------------------------------------------------------------
 // Balanced decode schedule
@@ -1188,17 +1336,15 @@ __global__ void __launch_bounds__(HPC * 32, 2) paged_decode_flat_kernel(const At
   int z = find_req(g0);
   int seg_first = prefix[z] - g0;  // CTA page index of the request's page 0 (<= 0 for the first segment)
   int seg_end = prefix[z + 1] - g0;
-  // Pieces of this CTA that another CTA may have to merge: at most the first
-  // and the last segment (a middle segment lies wholly in this CTA).
-  int pend_seq0 = -1, pend_n0 = 0, pend_seq1 = -1, pend_n1 = 0;
-
   auto start_segment = [&]() {
     const int seq = seq_sm[z];
     mth.load_q(a.q + static_cast<int64_t>(a.qsl[seq]) * a.q_stride + static_cast<int64_t>(kvh) * group * D, group);
     mth.reset();
   };
   // The segment's output: final rows when the request lies wholly in this
-  // CTA, else this CTA's piece (normalised output and log2-sum-exp).
+  // CTA, else this CTA's piece (normalised output and log2-sum-exp), which
+  // decode_merge_kernel combines.  The CTA holding the request's first page
+  // records the request's piece count for it.
   auto finish_segment = [&]() {
     const int seq = seq_sm[z];
     const int first_cta = prefix[z] / per_cta;
@@ -1209,20 +1355,13 @@ __global__ void __launch_bounds__(HPC * 32, 2) paged_decode_flat_kernel(const At
       if (tid == 0) record_device_error(LVB_DEVERR_INDEX);
       return;
     }
-    if (pieces == 1) {
+    if (piece == 0 && tid == 0) a.merge_count[seq * (a.Hkv / HPC) + hg] = static_cast<uint32_t>(pieces);
+    if (pieces == 1)
       mth.store(a.out + static_cast<int64_t>(a.qsl[seq]) * a.o_stride + static_cast<int64_t>(kvh) * group * D,
                 group);
-    } else {
+    else
       mth.store_partial(a.part_o + static_cast<int64_t>(piece) * D, a.part_lse + piece,
                         static_cast<int64_t>(seq) * a.Hq + kvh * group, a.max_splits, group);
-      if (pend_seq0 < 0) {
-        pend_seq0 = seq;
-        pend_n0 = pieces;
-      } else {
-        pend_seq1 = seq;
-        pend_n1 = pieces;
-      }
-    }
   };
 
   start_segment();
@@ -1245,34 +1384,6 @@ __global__ void __launch_bounds__(HPC * 32, 2) paged_decode_flat_kernel(const At
   }
   cp_async_wait_all();
   if (ok) finish_segment();
-  asm volatile("bar.sync 1, %0;" ::"n"(kThreads) : "memory");
-  if (!ok || *abort_flag) return;  // a failed wait raised the (CTA-wide) abort flag
-
-  // The CTA's pieces of requests shared with other CTAs: the last piece of a
-  // request to arrive merges all of them.
-#pragma unroll 1
-  for (int pi = 0; pi < 2; ++pi) {
-    const int seq = pi == 0 ? pend_seq0 : pend_seq1;
-    const int pieces = pi == 0 ? pend_n0 : pend_n1;
-    if (seq < 0) break;
-    __threadfence();
-    asm volatile("bar.sync 2, %0;" ::"n"(kThreads) : "memory");
-    uint32_t *counter = a.merge_count + static_cast<int64_t>(seq) * (a.Hkv / HPC) + hg;
-    if (tid == 0) {
-      const unsigned int prev = atomicAdd(counter, 1u);
-      *last_flag = prev == static_cast<unsigned int>(pieces - 1) ? 1 : 0;
-    }
-    asm volatile("bar.sync 2, %0;" ::"n"(kThreads) : "memory");
-    if (*last_flag) {
-      __threadfence();
-      merge_partials<kBf16, D, kThreads>(a, static_cast<int64_t>(seq) * a.Hq + hg * HPC * group, HPC * group, pieces,
-                                         reinterpret_cast<float *>(smem),
-                                         a.out + static_cast<int64_t>(a.qsl[seq]) * a.o_stride +
-                                             static_cast<int64_t>(hg) * HPC * group * D);
-      if (tid == 0) *counter = 0u;
-    }
-    asm volatile("bar.sync 2, %0;" ::"n"(kThreads) : "memory");  // last_flag and the scratch free again
-  }
 }
 
 }  // namespace attn
