@@ -906,8 +906,8 @@ def main() -> int:
             "traffic": profiled_traffic("paged_decode_cfg2.txt"),
             "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch "
                               "of this workload (profiles/paged_decode_cfg2.txt)",
-            "kernel": "paged_decode_kernel (split-context decode with in-kernel merge; one "
-                      "lvb_paged_attention call)",
+            "kernel": "paged_decode_kernel (split-context decode) + decode_merge_kernel (split merge); "
+                      "one lvb_paged_attention call",
             "peak_source": peaks["source"],
             "algorithmic_bytes_per_launch": nbytes["attention"],
             "launch_us": round(attn_ms * 1e3, 2),
