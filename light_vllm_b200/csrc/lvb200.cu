@@ -573,6 +573,10 @@ struct DecodePlan {
 // measured best on B200 at 8 pages for small batches and 16 from 32 requests
 // up (B = 64, ctx 1024: 38.5 -> 34.1 us).
 constexpr int64_t kMinSplitPagesSmall = 8;
+// Four warps per head (a handful of requests): 4-page splits put more CTAs on
+// the context (B200, 7B heads, one request, ctx 1024: 10.3 -> 8.2 us with the
+// merge launch; 2-page splits 10.3).
+constexpr int64_t kMinSplitPagesTiny = 4;
 constexpr int64_t kMinSplitPagesLarge = 16;
 // Batches below this many requests run one KV head per CTA.
 constexpr int64_t kAttnSmallBatch = 32;
@@ -601,7 +605,8 @@ DecodePlan decode_plan(int64_t num_seqs, int64_t hq, int64_t hkv, int64_t d, int
   if (splits > max_pages) splits = max_pages > 0 ? max_pages : 1;
   if (splits > 256) splits = 256;  // merge weights: (heads per CTA) x splits floats in shared memory
   int64_t chunk_pages = (max_pages + splits - 1) / splits > 0 ? (max_pages + splits - 1) / splits : 1;
-  const int64_t min_pages = num_seqs < kAttnSmallBatch ? kMinSplitPagesSmall : kMinSplitPagesLarge;
+  const int64_t min_pages =
+      kw > 1 ? kMinSplitPagesTiny : num_seqs < kAttnSmallBatch ? kMinSplitPagesSmall : kMinSplitPagesLarge;
   if (chunk_pages < min_pages) chunk_pages = min_pages;
   splits = (max_pages + chunk_pages - 1) / chunk_pages;
   if (splits < 1) splits = 1;
