@@ -301,9 +301,8 @@ LVB_API int lvb_stream_wait_event(lvb_stream_t stream, void *event);
 LVB_API int lvb_copy_async(void *dst, const void *src, size_t bytes, lvb_stream_t stream);
 
 /* Bytes of workspace `lvb_paged_attention` needs: split-context partial
- * outputs and log-sum-exps, then one merge semaphore per (request, KV head).
- * A workspace must be zero-filled once before its first use; every call
- * leaves its semaphores zero again. */
+ * outputs and log-sum-exps, then one word per (request, KV head) (the
+ * balanced schedule's piece counts).  Zero-fill it once before first use. */
 LVB_API size_t lvb_paged_attention_workspace_bytes(int64_t num_seqs, int64_t num_q_heads,
                                            int64_t num_kv_heads, int64_t head_size,
                                            int64_t max_seq_len);
@@ -323,7 +322,13 @@ LVB_API size_t lvb_paged_attention_workspace_bytes(int64_t num_seqs, int64_t num
  * index order: 2 * num_seqs int32, a permutation of the requests followed by
  * their num_computed in that order, as lvb_pack_step_metadata writes it) is
  * the order in which that path launches them: longest context first shortens
- * the tail of the launch.  The results do not depend on it.
+ * the tail of the launch.  The results do not depend on it.  That path is
+ * two launches (the split kernel, then the merge of the splits) and starts
+ * reading each request's pages wholly before its newest position before the
+ * previous kernel of the stream has finished: rows of those positions must
+ * not be written by work still running when the call is made (this
+ * library's own K/V writers that let the next launch start early write only
+ * the step's new positions; lvb_kv_scatter and lvb_kv_move_rows do not).
  * Other batches (prefill chunks, mixed prefill + decode, tree layouts) with
  * head_size 64 or 128 and 16-token blocks run the tensor-core tile kernel;
  * when request_order is given, its first num_decode_seqs requests are the

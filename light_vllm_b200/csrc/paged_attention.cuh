@@ -52,7 +52,11 @@ struct KVWriteArgs {
 };
 
 __global__ void paged_kv_write_kernel(const KVWriteArgs a) {
-  pdl_entry();
+  // Writes of the step's new positions let the attention launch early (it
+  // reads older positions before waiting); explicit slots may be any
+  // positions, so then the next launch starts only after this one ends.
+  if (a.slots == nullptr) pdl_launch_dependents();
+  pdl_wait();
   const int t = blockIdx.x;
   int64_t slot;
   if (a.slots != nullptr) {
@@ -134,7 +138,9 @@ __global__ void __launch_bounds__(128) kv_move_rows_kernel(uint16_t *__restrict_
                                                            const int32_t *__restrict__ src,
                                                            const int32_t *__restrict__ dst, int n, int hkv, int d) {
   extern __shared__ __align__(16) uint8_t move_smem[];
-  pdl_entry();
+  // Moves rows to older positions: no early launch of the next kernel (the
+  // decode attention reads older positions before its dependency wait).
+  pdl_wait();
   uint4 *rows = reinterpret_cast<uint4 *>(move_smem);
   uint16_t *base = blockIdx.y == 0 ? key_cache : value_cache;
   const int head = blockIdx.x;
@@ -857,7 +863,13 @@ __device__ __forceinline__ void merge_partials(const AttnArgs &a, int64_t head0,
 template <bool kBf16, int D, int HPC, int KW = 1, int NT = 1>
 __global__ void __launch_bounds__(DecodeCfg<D, HPC, KW>::kThreads, 2)
     paged_decode_kernel(const AttnArgs a) {
-  pdl_entry();
+  // The previous kernel of the stream may still run: this CTA reads the step
+  // metadata and the pages wholly before the request's newest position
+  // (written by earlier steps, never by a kernel still running -- this
+  // library's K/V writers that let the next launch start early write only
+  // the step's new positions) before waiting for it; q, the page holding the
+  // newest position and the outputs come after the wait.
+  pdl_launch_dependents();
   using Cfg = DecodeCfg<D, HPC, KW>;
   constexpr int kStages = Cfg::kStages;
   constexpr int kSteps = D / 16;  // 16-dim m-tiles of the output
@@ -951,11 +963,17 @@ __global__ void __launch_bounds__(DecodeCfg<D, HPC, KW>::kThreads, 2)
     return __shfl_sync(0xffffffffu, blk_cur, pg - blk_base);
   };
 
+  bool waited = false;
 #pragma unroll 1
   for (int j = 0; j < kStages - 1 && j < my_pages; ++j) {
     const int pg = wsub + j * KW;
+    if (!waited && (p_begin + pg + 1) * kPageTokens >= ctx) {
+      pdl_wait();
+      waited = true;
+    }
     load_page(pg, block_of(pg), j % kStages);
   }
+  if (!waited) pdl_wait();
 
   const int g = lane >> 2;  // MMA row group
   const int cq = lane & 3;  // MMA column pair
