@@ -44,7 +44,11 @@ def _heads_contiguous(t: Tensor, *, align: int) -> Tensor:
     """A [tokens, heads, dim] view usable by the kernels without a copy when
     heads and dims are dense and rows keep ``align``-element alignment."""
 
-    if (t.stride(2) == 1 and t.stride(1) == t.shape[2] and t.stride(0) % align == 0
+    if t.is_contiguous():
+        # Dense rows: row stride heads x dim; only alignment to check.
+        if t.data_ptr() % (2 * align) == 0 and (t.shape[1] * t.shape[2]) % align == 0:
+            return t
+    elif (t.stride(2) == 1 and t.stride(1) == t.shape[2] and t.stride(0) % align == 0
             and t.data_ptr() % (2 * align) == 0):
         return t
     return t.contiguous()
@@ -108,11 +112,23 @@ class StepMetadataPacker:
     def gather(self, metadata) -> StepShape:
         tables = metadata.block_tables
         n = len(tables)
-        self._reserve(n, sum(map(len, tables)))
-        total, max_blocks, ntok, max_q, max_seq, linear, single = self._hostpack.gather_step(
-            tables, metadata.num_computed_tokens, metadata.query_layouts,
-            metadata.num_reserved_query_tokens, metadata.num_readonly_prefix_blocks,
-            self._ids_ptr, self._ids.size, self._offsets_ptr, self._rows_ptr)
+        if self._offsets.size < n + 1:
+            self._reserve(n, sum(map(len, tables)))
+        try:
+            total, max_blocks, ntok, max_q, max_seq, linear, single = self._hostpack.gather_step(
+                tables, metadata.num_computed_tokens, metadata.query_layouts,
+                metadata.num_reserved_query_tokens, metadata.num_readonly_prefix_blocks,
+                self._ids_ptr, self._ids.size, self._offsets_ptr, self._rows_ptr)
+        except ValueError:
+            # The block-id buffer is too small for this step: grow it, retry.
+            needed = sum(map(len, tables))
+            if needed <= self._ids.size:
+                raise
+            self._reserve(n, needed)
+            total, max_blocks, ntok, max_q, max_seq, linear, single = self._hostpack.gather_step(
+                tables, metadata.num_computed_tokens, metadata.query_layouts,
+                metadata.num_reserved_query_tokens, metadata.num_readonly_prefix_blocks,
+                self._ids_ptr, self._ids.size, self._offsets_ptr, self._rows_ptr)
         self._step = StepShape(n, total, max_blocks, ntok, max_q, max_seq, linear, single)
         return self._step
 
