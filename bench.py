@@ -918,7 +918,9 @@ def main() -> int:
                 "path": "backend.create(cache, metadata).forward(...) with pinned host q/k/v and output; "
                         "uploads and read-backs on two copy streams overlapping the neighbouring steps' kernels, "
                         "no host synchronisation between steps"},
-        "gpu_launches": 3 * args.steps,
+        # per timed step: the split decode kernel (which also stores the
+        # step's K/V rows) and the split merge
+        "gpu_launches": 2 * args.steps,
         "clocks": clock_summary,
     }
     if rank == 0 and world == 1:

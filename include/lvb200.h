@@ -351,6 +351,25 @@ LVB_API int lvb_paged_attention(const uint16_t *query, int64_t query_token_strid
                         int dtype, void *workspace, size_t workspace_bytes,
                         lvb_stream_t stream);
 
+/* lvb_paged_kv_write of this step's key / value rows followed by
+ * lvb_paged_attention, in fewer launches: a decode batch on the
+ * split-context path stores each request's new row from the warp that loads
+ * the page holding it (the rows then need 16-byte aligned starts and token
+ * strides that are multiples of 8 elements); other batches run the write
+ * first.  The write + attention of the reference's attention step
+ * (runtime/execution/triton_paged_attention.py:498-517, 519-559). */
+LVB_API int lvb_paged_attention_kv(const uint16_t *key, int64_t key_token_stride, const uint16_t *value,
+                                   int64_t value_token_stride, const uint16_t *query, int64_t query_token_stride,
+                                   uint16_t *key_cache, uint16_t *value_cache, uint16_t *out,
+                                   int64_t out_token_stride, const int32_t *block_tables, int64_t table_stride,
+                                   const int32_t *num_computed, const int32_t *query_start_loc,
+                                   const int32_t *request_indices, const int32_t *request_order,
+                                   const uint8_t *visibility, const int32_t *visibility_start, int64_t num_seqs,
+                                   int64_t num_decode_seqs, int64_t num_tokens, int64_t max_query_len,
+                                   int64_t max_seq_len, int64_t num_q_heads, int64_t num_kv_heads,
+                                   int64_t head_size, int64_t block_size, int64_t num_blocks, float scale,
+                                   int dtype, void *workspace, size_t workspace_bytes, lvb_stream_t stream);
+
 /* ------------------------------------------------------------------------ */
 /* Tensor-parallel all-reduce + residual add + RMSNorm                        */
 /* ------------------------------------------------------------------------ */

@@ -19,7 +19,7 @@ from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().parent / "_lib" / "liblvb200.so"
 HOSTPACK_PATH = Path(__file__).resolve().parent / "_lib" / ("_hostpack" + sysconfig.get_config_var("EXT_SUFFIX"))
-ABI_VERSION = 7
+ABI_VERSION = 8
 
 LVB_OK = 0
 LVB_ERR_INVALID = 1
@@ -127,6 +127,12 @@ PROTOTYPES: dict[str, tuple[object, tuple[object, ...]]] = {
          _c_ptr, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _int, _c_ptr, _size,
          _c_ptr),
     ),
+    "lvb_paged_attention_kv": (
+        _int,
+        (_c_ptr, _i64, _c_ptr, _i64, _c_ptr, _i64, _c_ptr, _c_ptr, _c_ptr, _i64, _c_ptr, _i64, _c_ptr, _c_ptr,
+         _c_ptr, _c_ptr, _c_ptr, _c_ptr, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _int,
+         _c_ptr, _size, _c_ptr),
+    ),
 }
 
 
@@ -188,7 +194,8 @@ def hostpack():
     # The call trampolines reach the library's entry points directly.
     lib = library()
     module.bind(*(ctypes.cast(getattr(lib, name), ctypes.c_void_p).value
-                  for name in ("lvb_paged_kv_write", "lvb_paged_attention", "lvb_stage_step_metadata")))
+                  for name in ("lvb_paged_kv_write", "lvb_paged_attention", "lvb_stage_step_metadata",
+                               "lvb_paged_attention_kv")))
     return module
 
 

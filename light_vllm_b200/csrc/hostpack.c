@@ -218,20 +218,27 @@ typedef int (*attention_fn)(const void *, int64_t, const void *, const void *, v
                             int64_t, const void *, const void *, const void *, const void *, const void *,
                             const void *, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t,
                             int64_t, int64_t, float, int, void *, size_t, void *);
+typedef int (*attention_kv_fn)(const void *, int64_t, const void *, int64_t, const void *, int64_t, void *, void *,
+                               void *, int64_t, const void *, int64_t, const void *, const void *, const void *,
+                               const void *, const void *, const void *, int64_t, int64_t, int64_t, int64_t,
+                               int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, float, int, void *, size_t,
+                               void *);
 typedef int (*stage_fn)(const int32_t *, const int64_t *, const int32_t *, const int32_t *, const int32_t *,
                         const int32_t *, int64_t, int64_t, int64_t, int32_t *, int64_t, int32_t *, int64_t, void *,
                         void *, int64_t *, int64_t *);
 static kv_write_fn g_kv_write;
 static attention_fn g_attention;
 static stage_fn g_stage;
+static attention_kv_fn g_attention_kv;
 
 static PyObject *bind(PyObject *self, PyObject *args) {
   (void)self;
-  unsigned long long kv, attn, stage;
-  if (!PyArg_ParseTuple(args, "KKK", &kv, &attn, &stage)) return NULL;
+  unsigned long long kv, attn, stage, attn_kv;
+  if (!PyArg_ParseTuple(args, "KKKK", &kv, &attn, &stage, &attn_kv)) return NULL;
   g_kv_write = (kv_write_fn)(uintptr_t)kv;
   g_attention = (attention_fn)(uintptr_t)attn;
   g_stage = (stage_fn)(uintptr_t)stage;
+  g_attention_kv = (attention_kv_fn)(uintptr_t)attn_kv;
   Py_RETURN_NONE;
 }
 
@@ -244,8 +251,9 @@ static PyObject *bind(PyObject *self, PyObject *args) {
  *            num_decode_seqs, num_tokens, max_query_len, max_seq_len)
  *   layer = (key_cache, value_cache, num_q_heads, num_kv_heads, head_size,
  *            block_size, num_blocks, dtype)
- * Runs lvb_paged_kv_write (when write_kv) then lvb_paged_attention; returns
- * (status, 0) or (status, 1) for the call that failed (0 = kv write). */
+ * Runs lvb_paged_attention_kv (when write_kv: the step's K/V write and the
+ * attention) or lvb_paged_attention; returns (status, 1) on failure.  The
+ * failed_call value 0 (the K/V write) is kept for callers that name it. */
 static PyObject *attention_step(PyObject *self, PyObject *args) {
   (void)self;
   unsigned long long tables, computed, qsl, req, order, vis, vis_start;
@@ -263,14 +271,17 @@ static PyObject *attention_step(PyObject *self, PyObject *args) {
                         &hkv, &d, &bs, &num_blocks, &dtype, &q, &q_stride, &k, &k_stride, &v, &v_stride, &out,
                         &o_stride, &write_kv, &scale, &ws, &ws_bytes, &stream))
     return NULL;
-  if (!g_kv_write || !g_attention) {
+  if (!g_kv_write || !g_attention || !g_attention_kv) {
     PyErr_SetString(PyExc_RuntimeError, "_hostpack.bind was not called");
     return NULL;
   }
   if (write_kv) {
-    const int rc = g_kv_write(PTR(k), k_stride, PTR(v), v_stride, PTR(kc), PTR(vc), PTR(tables), stride,
-                              PTR(computed), PTR(qsl), PTR(req), n_tokens, hkv, d, bs, dtype, PTR(stream));
-    if (rc) return Py_BuildValue("(ii)", rc, 0);
+    /* One call: the decode path stores the step's rows itself. */
+    const int rc = g_attention_kv(PTR(k), k_stride, PTR(v), v_stride, PTR(q), q_stride, PTR(kc), PTR(vc), PTR(out),
+                                  o_stride, PTR(tables), stride, PTR(computed), PTR(qsl), PTR(req), PTR(order),
+                                  PTR(vis), PTR(vis_start), n_seqs, n_decode, n_tokens, max_q, max_seq, hq, hkv, d,
+                                  bs, num_blocks, scale, dtype, PTR(ws), (size_t)ws_bytes, PTR(stream));
+    return Py_BuildValue("(ii)", rc, 1);
   }
   const int rc = g_attention(PTR(q), q_stride, PTR(kc), PTR(vc), PTR(out), o_stride, PTR(tables), stride,
                              PTR(computed), PTR(qsl), PTR(req), PTR(order), PTR(vis), PTR(vis_start), n_seqs,
@@ -303,7 +314,8 @@ static PyObject *stage_step(PyObject *self, PyObject *args) {
 }
 
 static PyMethodDef methods[] = {
-    {"bind", bind, METH_VARARGS, "bind(kv_write_addr, attention_addr, stage_addr): library entry points"},
+    {"bind", bind, METH_VARARGS,
+     "bind(kv_write_addr, attention_addr, stage_addr, attention_kv_addr): library entry points"},
     {"attention_step", attention_step, METH_VARARGS,
      "attention_step(step, layer, q, q_stride, k, k_stride, v, v_stride, out, o_stride, write_kv, scale, "
      "workspace, workspace_bytes, stream) -> (status, failed_call)"},

@@ -31,7 +31,7 @@
 
 namespace {
 
-constexpr int kAbiVersion = 7;
+constexpr int kAbiVersion = 8;
 constexpr int kMaxDevices = 64;
 
 thread_local char g_last_error[512] = "";
@@ -1225,6 +1225,21 @@ size_t lvb_paged_attention_workspace_bytes(int64_t num_seqs, int64_t num_q_heads
   return p.total();
 }
 
+struct StepKV {  // the step's K/V rows for lvb_paged_attention_kv
+  const uint16_t *key, *value;
+  int64_t key_stride, value_stride;
+};
+
+int paged_attention_impl(const StepKV *kv, const uint16_t *query, int64_t query_token_stride,
+                         const uint16_t *key_cache, const uint16_t *value_cache, uint16_t *out,
+                         int64_t out_token_stride, const int32_t *block_tables, int64_t table_stride,
+                         const int32_t *num_computed, const int32_t *query_start_loc,
+                         const int32_t *request_indices, const int32_t *request_order, const uint8_t *visibility,
+                         const int32_t *visibility_start, int64_t num_seqs, int64_t num_decode_seqs,
+                         int64_t num_tokens, int64_t max_query_len, int64_t max_seq_len, int64_t num_q_heads,
+                         int64_t num_kv_heads, int64_t head_size, int64_t block_size, int64_t num_blocks,
+                         float scale, int dtype, void *workspace, size_t workspace_bytes, lvb_stream_t stream);
+
 int lvb_paged_attention(const uint16_t *query, int64_t query_token_stride,
                         const uint16_t *key_cache, const uint16_t *value_cache, uint16_t *out,
                         int64_t out_token_stride, const int32_t *block_tables,
@@ -1237,6 +1252,40 @@ int lvb_paged_attention(const uint16_t *query, int64_t query_token_stride,
                         int64_t head_size, int64_t block_size, int64_t num_blocks, float scale,
                         int dtype, void *workspace, size_t workspace_bytes,
                         lvb_stream_t stream) {
+  return paged_attention_impl(nullptr, query, query_token_stride, key_cache, value_cache, out, out_token_stride,
+                              block_tables, table_stride, num_computed, query_start_loc, request_indices,
+                              request_order, visibility, visibility_start, num_seqs, num_decode_seqs, num_tokens,
+                              max_query_len, max_seq_len, num_q_heads, num_kv_heads, head_size, block_size,
+                              num_blocks, scale, dtype, workspace, workspace_bytes, stream);
+}
+
+int lvb_paged_attention_kv(const uint16_t *key, int64_t key_token_stride, const uint16_t *value,
+                           int64_t value_token_stride, const uint16_t *query, int64_t query_token_stride,
+                           uint16_t *key_cache, uint16_t *value_cache, uint16_t *out, int64_t out_token_stride,
+                           const int32_t *block_tables, int64_t table_stride, const int32_t *num_computed,
+                           const int32_t *query_start_loc, const int32_t *request_indices,
+                           const int32_t *request_order, const uint8_t *visibility, const int32_t *visibility_start,
+                           int64_t num_seqs, int64_t num_decode_seqs, int64_t num_tokens, int64_t max_query_len,
+                           int64_t max_seq_len, int64_t num_q_heads, int64_t num_kv_heads, int64_t head_size,
+                           int64_t block_size, int64_t num_blocks, float scale, int dtype, void *workspace,
+                           size_t workspace_bytes, lvb_stream_t stream) {
+  const StepKV kv{key, value, key_token_stride, value_token_stride};
+  return paged_attention_impl(&kv, query, query_token_stride, key_cache, value_cache, out, out_token_stride,
+                              block_tables, table_stride, num_computed, query_start_loc, request_indices,
+                              request_order, visibility, visibility_start, num_seqs, num_decode_seqs, num_tokens,
+                              max_query_len, max_seq_len, num_q_heads, num_kv_heads, head_size, block_size,
+                              num_blocks, scale, dtype, workspace, workspace_bytes, stream);
+}
+
+int paged_attention_impl(const StepKV *kv, const uint16_t *query, int64_t query_token_stride,
+                         const uint16_t *key_cache, const uint16_t *value_cache, uint16_t *out,
+                         int64_t out_token_stride, const int32_t *block_tables, int64_t table_stride,
+                         const int32_t *num_computed, const int32_t *query_start_loc,
+                         const int32_t *request_indices, const int32_t *request_order, const uint8_t *visibility,
+                         const int32_t *visibility_start, int64_t num_seqs, int64_t num_decode_seqs,
+                         int64_t num_tokens, int64_t max_query_len, int64_t max_seq_len, int64_t num_q_heads,
+                         int64_t num_kv_heads, int64_t head_size, int64_t block_size, int64_t num_blocks,
+                         float scale, int dtype, void *workspace, size_t workspace_bytes, lvb_stream_t stream) {
   if (dtype != LVB_DTYPE_F16 && dtype != LVB_DTYPE_BF16) return fail(LVB_ERR_INVALID, "unknown dtype %d", dtype);
   if (num_tokens < 0 || num_seqs <= 0 || num_q_heads <= 0 || num_kv_heads <= 0 ||
       num_q_heads % num_kv_heads != 0 || block_size <= 0 || num_blocks <= 0)
@@ -1285,6 +1334,25 @@ int lvb_paged_attention(const uint16_t *query, int64_t query_token_stride,
   const bool all_decode = decode_eligible(visibility, max_query_len, num_seqs, num_tokens, num_q_heads,
                                          num_kv_heads, head_size, block_size);
   const bool tiles = tile_eligible(num_q_heads, num_kv_heads, head_size, block_size);
+  if (kv != nullptr && (!kv->key || !kv->value)) return fail(LVB_ERR_INVALID, "paged K/V write null pointer argument");
+  if (kv != nullptr) {
+    // Decode batches on the split kernel store the step's rows themselves;
+    // anything else writes them first with lvb_paged_kv_write.
+    const bool rows16 = aligned16(kv->key) && aligned16(kv->value) && kv->key_stride % 8 == 0 &&
+                        kv->value_stride % 8 == 0;
+    if (all_decode && rows16 && !kBalancedDecode) {
+      a.new_k = kv->key;
+      a.new_v = kv->value;
+      a.new_k_stride = kv->key_stride;
+      a.new_v_stride = kv->value_stride;
+    } else {
+      rc = lvb_paged_kv_write(kv->key, kv->key_stride, kv->value, kv->value_stride, const_cast<uint16_t *>(key_cache),
+                              const_cast<uint16_t *>(value_cache), block_tables, table_stride, num_computed,
+                              query_start_loc, request_indices, num_tokens, num_kv_heads, head_size, block_size,
+                              dtype, stream);
+      if (rc != LVB_OK) return rc;
+    }
+  }
   // One-token requests of a mixed batch: listed first in request_order.
   int64_t n_decode = all_decode ? num_seqs : 0;
   if (!all_decode && tiles && request_order != nullptr && decode_shape_ok(num_q_heads, num_kv_heads, head_size, block_size)) {

@@ -110,6 +110,11 @@ struct AttnArgs {
   int chunk_tokens;  // multiple of 16
   int num_seqs;
   int decode_seqs;   // balanced decode schedule: requests (launch order slots 0 .. decode_seqs - 1)
+  // split decode kernel: the step's K/V rows ([tokens][Hkv][D], token
+  // strides in elements), stored to the newest position's cache slot by the
+  // warp that loads that page; null = already in the cache
+  const uint16_t *new_k, *new_v;
+  int64_t new_k_stride, new_v_stride;
   int heads_per_cta; // balanced decode schedule: KV heads per CTA (merge_count holds pieces per head group)
   // prefill tile kernel: requests order[first_tile_req + blockIdx.y] (the
   // packer lists one-token requests first; the decode kernel serves those), or
@@ -937,6 +942,22 @@ __global__ void __launch_bounds__(DecodeCfg<D, HPC, KW>::kThreads, 2)
     const uint32_t kdst = ring + slot * Cfg::kPageBytes;
     const uint32_t vdst = kdst + Cfg::kHeadBytes;
     const int64_t base = static_cast<int64_t>(block) * kPageTokens * row_elems + head_off;
+    if (a.new_k != nullptr && valid <= kPageTokens && valid > 0 && end == ctx) {
+      // The page holds the request's newest position (ctx - 1): store this
+      // step's K/V row of the warp's head into its slot first (this page is
+      // only ever loaded after the dependency wait).  Lanes 0 .. D/8 - 1 copy
+      // K, the next D/8 lanes V, 16 bytes each.
+      const int64_t t = a.qsl[seq];
+      const int64_t row = base + static_cast<int64_t>(valid - 1) * row_elems;
+      if (lane < D / 8)
+        *reinterpret_cast<uint4 *>(const_cast<uint16_t *>(a.kc) + row + lane * 8) =
+            *reinterpret_cast<const uint4 *>(a.new_k + t * a.new_k_stride + head_off + lane * 8);
+      else if (lane < D / 4)
+        *reinterpret_cast<uint4 *>(const_cast<uint16_t *>(a.vc) + row + (lane - D / 8) * 8) =
+            *reinterpret_cast<const uint4 *>(a.new_v + t * a.new_v_stride + head_off + (lane - D / 8) * 8);
+      __threadfence_block();
+      __syncwarp();
+    }
 #pragma unroll
     for (int u = 0; u < kChunksPerLane; ++u) {
       const int q = lane + 32 * u;                  // chunk of this head's page
