@@ -21,6 +21,7 @@
 #include "../../include/lvb200.h"
 #include "awq_gemm.cuh"
 #include "awq_gemv.cuh"
+#include "awq_mma.cuh"
 #include "qwen2_ops.cuh"
 #include "awq_decode.cuh"
 #include "awq_i8.cuh"
@@ -547,6 +548,116 @@ int launch_awq_gemv(const GemvPlan &plan, const PackedShape &sh, const uint16_t 
   return LVB_OK;
 }
 
+// ------------------------------------------------------------------------
+// Warp-MMA plan (m <= 16, fp16 mma.sync over the packed layout)
+// ------------------------------------------------------------------------
+constexpr int64_t kMmaMinRows = 2;
+constexpr size_t kMmaMaxSmem = 72 * 1024;  // with the minimum ring: three CTAs per SM
+// Dynamic shared memory one SM offers its CTAs (228 KB less 1 KB reserved and
+// 1 KB of static shared memory per CTA, for up to four CTAs).
+constexpr size_t kMmaSmPool = 220 * 1024;
+
+// Measured on B200 (m = 2..16, against the GEMV / int8 / fp16 packed routes):
+// the warp-MMA kernel wins on layers of at most half an SM count of column
+// tiles, where K is split many ways (7B QKV m = 2: 11.4 -> 9.4 us, o 10.7 ->
+// 8.2, down 23.6 -> 20.9, BASELINE config 1 at m = 16: 8.3 -> 6.4); on wider
+// layers it is issue-bound and the int8 path stays ahead (3584 x 18944, 148
+// tiles, m = 16: 21.6 vs 18.8 us; 7B gate_up: 41 vs 31 us).
+bool mma_eligible(int64_t m, int64_t k, int64_t n, int64_t g, int sms) {
+  return m >= kMmaMinRows && m <= lvb::awqm::kMaxRows && g % 32 == 0 && k % g == 0 && k % 64 == 0 && n % 128 == 0 &&
+         n / 128 <= sms / 2;
+}
+
+struct MmaPlan {
+  int nt = 0, splits = 1, gps = 1, stages = lvb::awqm::kMinStages;
+  size_t smem = 0, sem_bytes = 0, part_bytes = 0;
+  size_t total() const { return sem_bytes + part_bytes; }
+};
+
+// About three CTAs per SM in one wave, whole groups per split; then the ring
+// takes the shared memory the resident CTAs leave (the kernel is bound by the
+// bytes it keeps in flight).  nt == 0 when no plan fits in `max_ws` (split-K
+// partials and semaphores).
+MmaPlan mma_plan(int64_t m, const PackedShape &sh, int64_t g, int sms, size_t max_ws = SIZE_MAX) {
+  MmaPlan p;
+  const int nt = m <= 8 ? 1 : 2;
+  auto smem_of = [&](int gps, int stages) {
+    return nt == 1 ? lvb::awqm::MmaCfg<1>::bytes(gps, stages) : lvb::awqm::MmaCfg<2>::bytes(gps, stages);
+  };
+  const int min_st = lvb::awqm::kMinStages;
+  (void)g;
+  const long long target = 3LL * sms;
+  int splits = static_cast<int>((target + sh.n_tiles - 1) / sh.n_tiles);
+  if (splits < 1) splits = 1;
+  if (splits > sh.groups) splits = sh.groups;
+  int gps = (sh.groups + splits - 1) / splits;
+  while (smem_of(gps, min_st) > kMmaMaxSmem && gps > 1) --gps;
+  if (smem_of(gps, min_st) > kMmaMaxSmem) return p;
+  splits = (sh.groups + gps - 1) / gps;
+  while (static_cast<long long>(sh.n_tiles) * splits > target && gps < sh.groups &&
+         smem_of(gps + 1, min_st) <= kMmaMaxSmem) {
+    ++gps;
+    splits = (sh.groups + gps - 1) / gps;
+  }
+  const size_t sem = round256(static_cast<size_t>(sh.n_tiles) * 4);
+  while (true) {
+    const size_t part = splits > 1 ? static_cast<size_t>(sh.n_tiles) * splits * m * lvb::awqm::kCols * 4 : 0;
+    if ((splits > 1 ? sem : 0) + part <= max_ws) {
+      p.part_bytes = part;
+      p.sem_bytes = splits > 1 ? sem : 0;
+      break;
+    }
+    if (splits == 1) return p;
+    if (smem_of(gps + 1, min_st) > kMmaMaxSmem) return p;
+    ++gps;
+    splits = (sh.groups + gps - 1) / gps;
+  }
+  long long per_sm = (static_cast<long long>(sh.n_tiles) * splits + sms - 1) / sms;
+  if (per_sm < 1) per_sm = 1;
+  if (per_sm > 4) per_sm = 4;
+  const size_t budget = kMmaSmPool / static_cast<size_t>(per_sm);
+  int stages = min_st;
+  while (stages < lvb::awqm::kMaxStages && smem_of(gps, stages + 1) <= budget) ++stages;
+  p.nt = nt;
+  p.splits = splits;
+  p.gps = gps;
+  p.stages = stages;
+  p.smem = smem_of(gps, stages);
+  return p;
+}
+
+template <int NT>
+int launch_awq_mma(const MmaPlan &plan, const PackedShape &sh, const uint16_t *x, const uint8_t *codes,
+                   const uint32_t *groups, const uint16_t *bias, uint16_t *y, int64_t m, int64_t n, int64_t g,
+                   uint8_t *ws, int dev, cudaStream_t stream, int64_t x_stride) {
+  static bool smem_done[kMaxDevices] = {false};
+  auto kernel = lvb::awqm::awq_mma_kernel<NT>;
+  int rc = ensure_smem(kernel, static_cast<int>(kMmaSmPool), dev, smem_done);
+  if (rc != LVB_OK) return rc;
+  lvb::awqm::MmaParams p{};
+  p.qpack = codes;
+  p.szpack = groups;
+  p.x = x;
+  p.x_stride = x_stride;
+  p.bias = bias;
+  p.y = y;
+  p.semaphores = reinterpret_cast<uint32_t *>(ws);
+  p.partials = plan.splits > 1 ? reinterpret_cast<float *>(ws + plan.sem_bytes) : nullptr;
+  p.M = static_cast<int>(m);
+  p.N = static_cast<int>(n);
+  p.groups = sh.groups;
+  p.k_chunks = sh.k_chunks;
+  p.runs_per_group = static_cast<int>(g / 32);
+  p.n_tiles = sh.n_tiles;
+  p.splits = plan.splits;
+  p.groups_per_split = plan.gps;
+  p.stages = plan.stages;
+  cudaError_t e = launch_pdl(kernel, dim3(static_cast<unsigned>(sh.n_tiles), static_cast<unsigned>(plan.splits)),
+                             dim3(lvb::awqm::kCtaThreads), plan.smem, stream, p);
+  if (e != cudaSuccess) return cuda_fail(e, "awq_mma_kernel launch");
+  return LVB_OK;
+}
+
 int check_awq_shape(int64_t m, int64_t k, int64_t n, int64_t group_size) {
   if (m < 0 || k <= 0 || n <= 0)
     return fail(LVB_ERR_INVALID, "invalid AWQ shape m=%lld k=%lld n=%lld", (long long)m, (long long)k, (long long)n);
@@ -833,6 +944,12 @@ size_t lvb_awq_workspace_bytes(int64_t m, int64_t k, int64_t n, int64_t group_si
       const GemvPlan gp = gemv_plan(m, k, sh, group_size, sm_count(dev));
       if (gp.total() > need) need = gp.total();
     }
+    if (mma_eligible(m, k, n, group_size, sm_count(dev))) {
+      // The fused SiLU-mul entry also keeps the m x k activation there.
+      const MmaPlan mp = mma_plan(m, sh, group_size, sm_count(dev));
+      const size_t with_act = round256(mp.total()) + round256(static_cast<size_t>(m) * k * 2) + 256;
+      if (with_act > need) need = with_act;
+    }
   }
   return need;
 }
@@ -938,6 +1055,14 @@ int lvb_awq_linear_packed(const uint16_t *x, const void *codes, const void *grou
   const PackedShape sh = packed_shape(k, n, group_size);
   const size_t max_ws = workspace != nullptr ? workspace_bytes : 0;
   cudaStream_t stream_ = reinterpret_cast<cudaStream_t>(stream);
+  if (mma_eligible(m, k, n, group_size, sm_count(dev))) {
+    const MmaPlan mp = mma_plan(m, sh, group_size, sm_count(dev), max_ws);
+    const uint8_t *c8 = static_cast<const uint8_t *>(codes);
+    const uint32_t *g8 = static_cast<const uint32_t *>(groups);
+    uint8_t *w8 = static_cast<uint8_t *>(workspace);
+    if (mp.nt == 1) return launch_awq_mma<1>(mp, sh, x, c8, g8, bias, y, m, n, group_size, w8, dev, stream_, k);
+    if (mp.nt == 2) return launch_awq_mma<2>(mp, sh, x, c8, g8, bias, y, m, n, group_size, w8, dev, stream_, k);
+  }
   if (gemv_eligible(m, k, n, group_size)) {
     const GemvPlan gp = gemv_plan(m, k, sh, group_size, sm_count(dev), max_ws);
     const uint8_t *c8 = static_cast<const uint8_t *>(codes);
@@ -1057,6 +1182,19 @@ int lvb_awq_silu_linear_packed(const uint16_t *gate_up, int64_t gate_up_stride, 
   const uint8_t *c8 = static_cast<const uint8_t *>(codes);
   const uint32_t *g8 = static_cast<const uint32_t *>(groups);
   uint8_t *w8 = static_cast<uint8_t *>(workspace);
+  if (mma_eligible(m, k, n, group_size, sm_count(dev))) {
+    // silu(gate) * up into the workspace behind the split-K buffers, then
+    // the warp-MMA projection of it (two launches, programmatic dependents).
+    const size_t act = round256(static_cast<size_t>(m) * k * 2);
+    const MmaPlan mp = max_ws > act + 256 ? mma_plan(m, sh, group_size, sm_count(dev), max_ws - act - 256) : MmaPlan{};
+    if (mp.nt != 0) {
+      uint16_t *a16 = reinterpret_cast<uint16_t *>(w8 + round256(mp.total()));
+      rc = lvb_silu_mul(gate_up, gate_up_stride, m, k, a16, k, stream);
+      if (rc != LVB_OK) return rc;
+      if (mp.nt == 1) return launch_awq_mma<1>(mp, sh, a16, c8, g8, bias, y, m, n, group_size, w8, dev, st, k);
+      return launch_awq_mma<2>(mp, sh, a16, c8, g8, bias, y, m, n, group_size, w8, dev, st, k);
+    }
+  }
   if (gemv_eligible(m, k, n, group_size)) {
     const GemvPlan gp = gemv_plan(m, k, sh, group_size, sm_count(dev), max_ws);
     if (gp.mt == 1) return launch_awq_gemv<1>(gp, sh, gate_up, c8, g8, bias, y, m, k, n, group_size, w8, dev, st, gate_up_stride, 1);

@@ -224,15 +224,17 @@ def test_ragged_shapes_keep_the_checkpoint_layout():
 
 
 def _integer_path(m: int, k: int, n: int, g: int) -> bool:
-    """Whether the packed scheme runs an integer-limb path for this shape (the
-    dispatch rules of lvb_awq_linear_packed): the one-row GEMV at m = 1, the
-    int8 tensor-core path at m <= 16 for groups of 128 / 256 and >= 8 MiB of
-    codes; the fp16 packed kernel otherwise."""
+    """Whether the packed scheme applies the zero point and scale exactly for
+    this shape (the dispatch rules of lvb_awq_linear_packed on a 148-SM
+    B200): the one-row GEMV at m = 1 and the int8 tensor-core path at m =
+    2..16 on layers of more than 74 column tiles (groups of 128 / 256, >= 8
+    MiB of codes).  The warp-MMA kernel (m = 2..16, narrower layers) and the
+    fp16 packed kernel multiply the reference's fp16-rounded weight."""
 
     packed = n % 128 == 0 and k % 64 == 0
     if packed and m == 1 and g % 32 == 0:
         return True
-    return packed and m <= 16 and g in (128, 256) and k * n // 2 >= 8 << 20
+    return packed and m <= 16 and n // 128 > 148 // 2 and g in (128, 256) and k * n // 2 >= 8 << 20
 
 
 def _assert_fp16_output_close(actual: np.ndarray, expected: np.ndarray, what, x=None, weights=None) -> None:
@@ -265,12 +267,10 @@ def _assert_fp16_output_close(actual: np.ndarray, expected: np.ndarray, what, x=
 
 
 @pytest.mark.parametrize("m", [5, 16, 32])
-def test_int8_path_with_activation_outliers(m):
-    """Decode batches (m <= 16, group 128 / 256, weights >= 8 MiB) run the
-    int8 tensor-core path, which splits each (token, group) of x into four
-    int8 limbs under a power-of-two scale; rows whose groups mix outliers 300x
-    the typical value keep the north-star tolerance (m = 32 runs the fp16
-    packed kernel)."""
+def test_decode_batches_with_activation_outliers(m):
+    """Decode batches with outliers 300x the typical value in the rows: m = 5
+    and 16 run the warp-MMA kernel, m = 32 the fp16 packed kernel; the
+    north-star tolerance holds."""
 
     k, n, g = 3584, 4736, 128  # 8.5 MB of packed weights: the int8 path
     qweight, qzeros, scales = oawq.random_checkpoint(k, n, g, seed=m + 77)
@@ -312,8 +312,8 @@ def _massive_outlier_case(m: int, k: int, n: int, g: int, seed: int):
 
 @pytest.mark.parametrize("m", [1, 4, 16])
 def test_decode_paths_keep_precision_beside_massive_outliers(m):
-    """m = 1 runs the dp4a GEMV, m = 4 and 16 the int8 tensor-core path (8.5
-    MB of weights).  Columns whose outlier weights are zero: max-abs <= 2e-2
+    """m = 1 runs the dp4a GEMV, m = 4 and 16 the warp-MMA kernel (fp16 x
+    unchanged, the reference's fp16 weight).  Columns whose outlier weights are zero: max-abs <= 2e-2
     and rel-L2 <= 1e-3 against the fp32 oracle, with no widened bound; all
     columns: the fp16-output tolerance."""
 
