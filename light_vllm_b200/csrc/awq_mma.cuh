@@ -56,9 +56,6 @@ namespace lvb {
 namespace awqm {
 
 constexpr int kCols = 128;                      // output columns per CTA (one packed tile)
-constexpr int kWarps = 8;                       // consumer warps, 16 columns each
-constexpr int kThreads = kWarps * 32;           // consumer threads
-constexpr int kCtaThreads = kThreads + 32;      // + one producer warp
 constexpr int kStageRuns = 4;                   // 32-k runs per stage
 constexpr int kMinStages = 4;                   // ring depth the plan guarantees
 constexpr int kMaxStages = 16;                  // the host fills shared memory up to this
@@ -98,8 +95,6 @@ struct MmaParams {
   int stages;              // ring depth, kMinStages..kMaxStages
 };
 
-__device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kThreads) : "memory"); }
-
 __device__ __forceinline__ uint32_t hsub2_bits(uint32_t a, uint32_t b) {
   uint32_t d;
   asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
@@ -112,10 +107,23 @@ __device__ __forceinline__ uint32_t hmul2_bits(uint32_t a, uint32_t b) {
   return d;
 }
 
-template <int NT>
-__global__ void __launch_bounds__(kCtaThreads, 3) awq_mma_kernel(const __grid_constant__ MmaParams p) {
+// Consumer warps of CPW columns (16: one A tile; 32: two A tiles sharing
+// each B fragment) over the 128 columns of a tile.
+template <int CPW>
+struct MmaWarps {
+  static constexpr int kWarps = kCols / CPW;
+  static constexpr int kThreads = kWarps * 32;
+  static constexpr int kCtaThreads = kThreads + 32;
+};
+
+template <int NT, int CPW>
+__global__ void __launch_bounds__(MmaWarps<CPW>::kCtaThreads, 3) awq_mma_kernel(const __grid_constant__ MmaParams p) {
   using C = MmaCfg<NT>;
   constexpr int R = C::kRows;
+  constexpr int kW = MmaWarps<CPW>::kWarps;
+  constexpr int kCT = MmaWarps<CPW>::kThreads;
+  constexpr int kCtaT = MmaWarps<CPW>::kCtaThreads;
+  constexpr int kTiles = CPW / 16;  // A tiles per warp
   extern __shared__ __align__(1024) uint8_t smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int tile = blockIdx.x, split = blockIdx.y;
@@ -125,20 +133,21 @@ __global__ void __launch_bounds__(kCtaThreads, 3) awq_mma_kernel(const __grid_co
   const int run0 = g0 * rpg;
   const int nruns = (g1 - g0) * rpg;
   const int nstages = (nruns + kStageRuns - 1) / kStageRuns;
-  const int kStages = p.stages;
-  const uint32_t *sz_sm = reinterpret_cast<const uint32_t *>(smem + C::sz_off(kStages));
-  uint64_t *full = reinterpret_cast<uint64_t *>(smem + C::bar_off(p.groups_per_split, kStages));
-  uint64_t *empty = full + kStages;
-  uint64_t *sz_bar = empty + kStages;
+  const int stages = p.stages;
+  const uint32_t *sz_sm = reinterpret_cast<const uint32_t *>(smem + C::sz_off(stages));
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + C::bar_off(p.groups_per_split, stages));
+  uint64_t *empty = full + stages;
+  uint64_t *sz_bar = empty + stages;
   volatile int *abort_flag = reinterpret_cast<volatile int *>(sz_bar + 1);
+  auto csync = [] { asm volatile("bar.sync 1, %0;" ::"n"(kCT) : "memory"); };
 
   // The next kernel of the stream may launch now; it waits for this grid's
   // completion before touching y.
   pdl_launch_dependents();
   if (tid == 0) {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < stages; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kWarps);
+      mbar_init(&empty[s], kW);
     }
     mbar_init(sz_bar, 1);
     *abort_flag = 0;
@@ -148,9 +157,9 @@ __global__ void __launch_bounds__(kCtaThreads, 3) awq_mma_kernel(const __grid_co
   // never stored, and zeros keep them finite).
   if (p.M < R) {
     const int row_words = kXRow / 16;
-    const int words = kStages * (R - p.M) * row_words;
-    for (int i = tid; i < words; i += kCtaThreads) {
-      const int s = i / ((R - p.M) * row_words), rem = i - s * (R - p.M) * row_words;
+    const int per_stage = (R - p.M) * row_words;
+    for (int i = tid; i < stages * per_stage; i += kCtaT) {
+      const int s = i / per_stage, rem = i - s * per_stage;
       const int row = p.M + rem / row_words, w = rem - (rem / row_words) * row_words;
       *reinterpret_cast<int4 *>(smem + static_cast<size_t>(s) * C::kStageBytes + kCodeBytes + row * kXRow + w * 16) =
           make_int4(0, 0, 0, 0);
@@ -158,63 +167,61 @@ __global__ void __launch_bounds__(kCtaThreads, 3) awq_mma_kernel(const __grid_co
   }
   __syncthreads();
 
-  if (warp == kWarps) {
+  if (warp == kW) {
     // Producer.  Lane 0 sets each stage's byte count and copies its codes;
     // lane t < M copies token row t's slice of the stage.
     const uint8_t *codes = p.qpack + (static_cast<size_t>(tile) * p.k_chunks + run0) * kCols * 16;
     const bool xrow = lane < p.M;
     const uint16_t *xs = p.x + static_cast<size_t>(xrow ? lane : 0) * p.x_stride + static_cast<size_t>(run0) * 32;
     auto stage_runs = [&](int st) { return min(kStageRuns, nruns - st * kStageRuns); };
-    auto stage_bytes = [&](int st) {
+    auto copy_codes = [&](int st, int slot) {
       const uint32_t runs = static_cast<uint32_t>(stage_runs(st));
-      return runs * kCols * 16 + runs * 64 * static_cast<uint32_t>(p.M);
+      mbar_arrive_expect_tx(&full[slot], runs * kCols * 16 + runs * 64 * static_cast<uint32_t>(p.M));
+      awqd::bulk_load(smem + static_cast<size_t>(slot) * C::kStageBytes, codes + static_cast<size_t>(st) * kCodeBytes,
+                      runs * kCols * 16, &full[slot]);
     };
-    auto copy_x = [&](int st) {
+    auto copy_x = [&](int st, int slot) {
       if (xrow)
-        awqd::bulk_load(smem + static_cast<size_t>(st % kStages) * C::kStageBytes + kCodeBytes + lane * kXRow,
+        awqd::bulk_load(smem + static_cast<size_t>(slot) * C::kStageBytes + kCodeBytes + lane * kXRow,
                         xs + static_cast<size_t>(st) * kStageRuns * 32, static_cast<uint32_t>(stage_runs(st)) * 64,
-                        &full[st % kStages]);
+                        &full[slot]);
     };
     if (lane == 0) {
       // The range's (scale, zero) rows are contiguous: one copy.
       const uint32_t sz_bytes = static_cast<uint32_t>(g1 - g0) * kCols * 4;
       mbar_arrive_expect_tx(sz_bar, sz_bytes);
-      awqd::bulk_load(smem + C::sz_off(kStages), p.szpack + (static_cast<size_t>(tile) * p.groups + g0) * kCols, sz_bytes,
-                      sz_bar);
+      awqd::bulk_load(smem + C::sz_off(stages), p.szpack + (static_cast<size_t>(tile) * p.groups + g0) * kCols,
+                      sz_bytes, sz_bar);
     }
     // The codes do not depend on the previous kernel: the first stages' copies
     // start at once; x does, so its rows follow the wait.
-    const int pre = min(nstages, kStages);
-    if (lane == 0) {
-      for (int st = 0; st < pre; ++st) {
-        mbar_arrive_expect_tx(&full[st], stage_bytes(st));
-        awqd::bulk_load(smem + static_cast<size_t>(st) * C::kStageBytes, codes + static_cast<size_t>(st) * kCodeBytes,
-                        static_cast<uint32_t>(stage_runs(st)) * kCols * 16, &full[st]);
-      }
-    }
+    const int pre = min(nstages, stages);
+    if (lane == 0)
+      for (int st = 0; st < pre; ++st) copy_codes(st, st);
     pdl_wait();
     __syncwarp();
-    for (int st = 0; st < pre; ++st) copy_x(st);
+    for (int st = 0; st < pre; ++st) copy_x(st, st);
     int issued = pre;
+    int slot = 0;
+    uint32_t phase = 0;  // parity of the empty phase to wait for at `slot`
     for (int st = pre; st < nstages; ++st) {
-      const int slot = st % kStages;
       bool ok = true;
-      if (lane == 0) ok = mbar_wait(&empty[slot], ((st / kStages) - 1) & 1, abort_flag);
+      if (lane == 0) ok = mbar_wait(&empty[slot], phase, abort_flag);
       if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) break;
-      if (lane == 0) {
-        mbar_arrive_expect_tx(&full[slot], stage_bytes(st));
-        awqd::bulk_load(smem + static_cast<size_t>(slot) * C::kStageBytes, codes + static_cast<size_t>(st) * kCodeBytes,
-                        static_cast<uint32_t>(stage_runs(st)) * kCols * 16, &full[slot]);
-      }
+      if (lane == 0) copy_codes(st, slot);
       __syncwarp();
-      copy_x(st);
+      copy_x(st, slot);
       issued = st + 1;
+      if (++slot == stages) {
+        slot = 0;
+        phase ^= 1u;
+      }
     }
     // Leave only once every copy issued has landed (shared memory must not
     // be written after the CTA ends).
     if (lane == 0) {
-      for (int st = max(0, issued - kStages); st < issued; ++st)
-        mbar_wait(&full[st % kStages], (st / kStages) & 1, nullptr, kDrainBudgetCycles);
+      for (int st = max(0, issued - stages); st < issued; ++st)
+        mbar_wait(&full[st % stages], (st / stages) & 1, nullptr, kDrainBudgetCycles);
       mbar_wait(sz_bar, 0, nullptr, kDrainBudgetCycles);
     }
     return;
@@ -223,27 +230,32 @@ __global__ void __launch_bounds__(kCtaThreads, 3) awq_mma_kernel(const __grid_co
   // y and the partials may still be read by the previous kernel of the stream.
   pdl_wait();
   const int g = lane >> 2, t4 = lane & 3;
-  const int c0 = warp * 16;
-  // Two accumulators per token tile (k = 0..15 and 16..31 of each run), so
-  // consecutive MMAs do not wait on one another; summed at the end.
-  float acc[NT][4], acc2[NT][4];
+  const int c0 = warp * CPW;
+  // Two accumulators per (A tile, token tile): k = 0..15 and 16..31 of each
+  // run, so consecutive MMAs do not wait on one another; summed at the end.
+  float acc[kTiles][NT][4], acc2[kTiles][NT][4];
 #pragma unroll
-  for (int nt = 0; nt < NT; ++nt)
+  for (int ct = 0; ct < kTiles; ++ct)
 #pragma unroll
-    for (int i = 0; i < 4; ++i) acc[nt][i] = acc2[nt][i] = 0.f;
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[ct][nt][i] = acc2[ct][nt][i] = 0.f;
   bool ok = mbar_wait(sz_bar, 0, abort_flag);
-  // Columns c0 + g and c0 + g + 8 of the current group: the half2 (1024 + z)
+  // Columns c0 + 16 ct + g and + 8 of the current group: the half2 (1024 + z)
   // subtracted from the codes and the half2 scale.
-  uint32_t z_lo = 0, z_hi = 0, s_lo = 0, s_hi = 0;
+  uint32_t z_lo[kTiles], z_hi[kTiles], s_lo[kTiles], s_hi[kTiles];
   auto load_group = [&](int gr) {
-    const uint32_t w0 = sz_sm[(gr - g0) * kCols + c0 + g];
-    const uint32_t w1 = sz_sm[(gr - g0) * kCols + c0 + g + 8];
-    z_lo = (0x6400u + (w0 >> 16)) * 0x10001u;
-    z_hi = (0x6400u + (w1 >> 16)) * 0x10001u;
-    s_lo = (w0 & 0xFFFFu) * 0x10001u;
-    s_hi = (w1 & 0xFFFFu) * 0x10001u;
+#pragma unroll
+    for (int ct = 0; ct < kTiles; ++ct) {
+      const uint32_t w0 = sz_sm[(gr - g0) * kCols + c0 + 16 * ct + g];
+      const uint32_t w1 = sz_sm[(gr - g0) * kCols + c0 + 16 * ct + g + 8];
+      z_lo[ct] = (0x6400u + (w0 >> 16)) * 0x10001u;
+      z_hi[ct] = (0x6400u + (w1 >> 16)) * 0x10001u;
+      s_lo[ct] = (w0 & 0xFFFFu) * 0x10001u;
+      s_hi[ct] = (w1 & 0xFFFFu) * 0x10001u;
+    }
   };
-  // W = fp16((q - z) * s) for the four k of each half2 (q - z exact, one
+  // W = fp16((q - z) * s) for the two k of each half2 (q - z exact, one
   // rounding: the reference's dequantised weight).
   auto weight = [](uint32_t bits, uint32_t z, uint32_t sc) {
     return hmul2_bits(hsub2_bits((bits & 0x000F000Fu) | 0x64006400u, z), sc);
@@ -251,9 +263,10 @@ __global__ void __launch_bounds__(kCtaThreads, 3) awq_mma_kernel(const __grid_co
   int group = g0, run_in_group = 0;
   if (ok) load_group(group);
 
+  int slot = 0;
+  uint32_t phase = 0;
   for (int st = 0; st < nstages && ok; ++st) {
-    const int slot = st % kStages;
-    if (!mbar_wait(&full[slot], (st / kStages) & 1, abort_flag)) {
+    if (!mbar_wait(&full[slot], phase, abort_flag)) {
       ok = false;
       break;
     }
@@ -264,22 +277,29 @@ __global__ void __launch_bounds__(kCtaThreads, 3) awq_mma_kernel(const __grid_co
 #pragma unroll
     for (int r = 0; r < kStageRuns; ++r) {
       if (r < runs) {
-        const uint32_t w0 = cw[r * kCols * 4], w1 = cw[r * kCols * 4 + 32];
-        uint32_t a0[4], a1[4];
-        a0[0] = weight(w0, z_lo, s_lo);         // column g,     k 4 t4, 4 t4 + 1
-        a0[1] = weight(w1, z_hi, s_hi);         // column g + 8
-        a0[2] = weight(w0 >> 8, z_lo, s_lo);    // column g,     k 4 t4 + 2, 4 t4 + 3
-        a0[3] = weight(w1 >> 8, z_hi, s_hi);
-        a1[0] = weight(w0 >> 4, z_lo, s_lo);    // k 16 + 4 t4, 16 + 4 t4 + 1
-        a1[1] = weight(w1 >> 4, z_hi, s_hi);
-        a1[2] = weight(w0 >> 12, z_lo, s_lo);   // k 16 + 4 t4 + 2, 16 + 4 t4 + 3
-        a1[3] = weight(w1 >> 12, z_hi, s_hi);
+        uint32_t a0[kTiles][4], a1[kTiles][4];
+#pragma unroll
+        for (int ct = 0; ct < kTiles; ++ct) {
+          // Word t4 of columns c0 + 16 ct + g and + 8 (column stride 4 words).
+          const uint32_t w0 = cw[r * kCols * 4 + ct * 64], w1 = cw[r * kCols * 4 + ct * 64 + 32];
+          a0[ct][0] = weight(w0, z_lo[ct], s_lo[ct]);        // column g,     k 4 t4, 4 t4 + 1
+          a0[ct][1] = weight(w1, z_hi[ct], s_hi[ct]);        // column g + 8
+          a0[ct][2] = weight(w0 >> 8, z_lo[ct], s_lo[ct]);   // column g,     k 4 t4 + 2, 4 t4 + 3
+          a0[ct][3] = weight(w1 >> 8, z_hi[ct], s_hi[ct]);
+          a1[ct][0] = weight(w0 >> 4, z_lo[ct], s_lo[ct]);   // k 16 + 4 t4, 16 + 4 t4 + 1
+          a1[ct][1] = weight(w1 >> 4, z_hi[ct], s_hi[ct]);
+          a1[ct][2] = weight(w0 >> 12, z_lo[ct], s_lo[ct]);  // k 16 + 4 t4 + 2, 16 + 4 t4 + 3
+          a1[ct][3] = weight(w1 >> 12, z_hi[ct], s_hi[ct]);
+        }
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
           const uint2 b0 = *reinterpret_cast<const uint2 *>(xb + nt * 8 * kXRow + r * 64);
           const uint2 b1 = *reinterpret_cast<const uint2 *>(xb + nt * 8 * kXRow + r * 64 + 32);
-          mma_16816_nv<false>(acc[nt], a0, b0.x, b0.y);
-          mma_16816_nv<false>(acc2[nt], a1, b1.x, b1.y);
+#pragma unroll
+          for (int ct = 0; ct < kTiles; ++ct) {
+            mma_16816_nv<false>(acc[ct][nt], a0[ct], b0.x, b0.y);
+            mma_16816_nv<false>(acc2[ct][nt], a1[ct], b1.x, b1.y);
+          }
         }
         if (++run_in_group == rpg) {
           ++group;
@@ -290,49 +310,60 @@ __global__ void __launch_bounds__(kCtaThreads, 3) awq_mma_kernel(const __grid_co
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[slot]);
+    if (++slot == stages) {
+      slot = 0;
+      phase ^= 1u;
+    }
   }
 #pragma unroll
-  for (int nt = 0; nt < NT; ++nt)
+  for (int ct = 0; ct < kTiles; ++ct)
 #pragma unroll
-    for (int i = 0; i < 4; ++i) acc[nt][i] += acc2[nt][i];
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[ct][nt][i] += acc2[ct][nt][i];
   // A wait that gave up raised the abort flag (and set the error word): the
   // CTA then leaves without output.
-  consumers_sync();
+  csync();
   if (*abort_flag) return;
 
-  // Fragment element i of token tile nt: column c0 + g (+ 8 for i >= 2),
-  // token 8 nt + 2 t4 (+ 1 for odd i).
-  const int n_lo = tile * kCols + c0 + g;
+  // Fragment element i of (A tile ct, token tile nt): column c0 + 16 ct + g
+  // (+ 8 for i >= 2), token 8 nt + 2 t4 (+ 1 for odd i).
   if (p.splits == 1) {
-    const float b_lo = p.bias ? __half2float(__ushort_as_half(p.bias[n_lo])) : 0.f;
-    const float b_hi = p.bias ? __half2float(__ushort_as_half(p.bias[n_lo + 8])) : 0.f;
+#pragma unroll
+    for (int ct = 0; ct < kTiles; ++ct) {
+      const int n_lo = tile * kCols + c0 + 16 * ct + g;
+      const float b_lo = p.bias ? __half2float(__ushort_as_half(p.bias[n_lo])) : 0.f;
+      const float b_hi = p.bias ? __half2float(__ushort_as_half(p.bias[n_lo + 8])) : 0.f;
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int t = nt * 8 + 2 * t4 + (i & 1);
+          if (t < p.M)
+            p.y[static_cast<size_t>(t) * p.N + n_lo + (i >> 1) * 8] =
+                __half_as_ushort(__float2half_rn(acc[ct][nt][i] + (i < 2 ? b_lo : b_hi)));
+        }
+    }
+    return;
+  }
+  float *part = p.partials + (static_cast<size_t>(tile) * p.splits + split) * p.M * kCols;
+#pragma unroll
+  for (int ct = 0; ct < kTiles; ++ct)
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const int t = nt * 8 + 2 * t4 + (i & 1);
-        if (t < p.M)
-          p.y[static_cast<size_t>(t) * p.N + n_lo + (i >> 1) * 8] =
-              __half_as_ushort(__float2half_rn(acc[nt][i] + (i < 2 ? b_lo : b_hi)));
+        if (t < p.M) part[static_cast<size_t>(t) * kCols + c0 + 16 * ct + g + (i >> 1) * 8] = acc[ct][nt][i];
       }
-    return;
-  }
-  float *part = p.partials + (static_cast<size_t>(tile) * p.splits + split) * p.M * kCols;
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int t = nt * 8 + 2 * t4 + (i & 1);
-      if (t < p.M) part[static_cast<size_t>(t) * kCols + c0 + g + (i >> 1) * 8] = acc[nt][i];
-    }
   __shared__ int last_sm;
   __threadfence();
-  consumers_sync();
+  csync();
   if (tid == 0) {
     const unsigned prev = atomicAdd(p.semaphores + tile, 1u);
     last_sm = prev == static_cast<unsigned>(p.splits - 1);
   }
-  consumers_sync();
+  csync();
   if (!last_sm) return;
   __threadfence();
   // Last CTA of the tile: each thread sums up to two 4-column slots of the
@@ -341,8 +372,8 @@ __global__ void __launch_bounds__(kCtaThreads, 3) awq_mma_kernel(const __grid_co
   const int slots = p.M * (kCols / 4);
   const float4 *tp = reinterpret_cast<const float4 *>(p.partials + static_cast<size_t>(tile) * p.splits * p.M * kCols);
   constexpr int kBatch = 4;
-  for (int s0 = tid; s0 < slots; s0 += 2 * kThreads) {
-    const int s1 = s0 + kThreads;
+  for (int s0 = tid; s0 < slots; s0 += 2 * kCT) {
+    const int s1 = s0 + kCT;
     const bool two = s1 < slots;
     float4 sum0 = make_float4(0.f, 0.f, 0.f, 0.f), sum1 = sum0;
     for (int sp0 = 0; sp0 < p.splits; sp0 += kBatch) {
@@ -361,8 +392,8 @@ __global__ void __launch_bounds__(kCtaThreads, 3) awq_mma_kernel(const __grid_co
         }
       }
     }
-    auto store4 = [&](int slot, const float4 &v) {
-      const int t = slot / (kCols / 4), c = tile * kCols + (slot % (kCols / 4)) * 4;
+    auto store4 = [&](int sl, const float4 &v) {
+      const int t = sl / (kCols / 4), c = tile * kCols + (sl % (kCols / 4)) * 4;
       const float o[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
       for (int j = 0; j < 4; ++j) {

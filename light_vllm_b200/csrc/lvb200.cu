@@ -552,20 +552,23 @@ int launch_awq_gemv(const GemvPlan &plan, const PackedShape &sh, const uint16_t 
 // Warp-MMA plan (m <= 16, fp16 mma.sync over the packed layout)
 // ------------------------------------------------------------------------
 constexpr int64_t kMmaMinRows = 2;
+constexpr int kMmaColsPerWarp = 16;  // consumer warps of one 16-column A tile
 constexpr size_t kMmaMaxSmem = 72 * 1024;  // with the minimum ring: three CTAs per SM
 // Dynamic shared memory one SM offers its CTAs (228 KB less 1 KB reserved and
 // 1 KB of static shared memory per CTA, for up to four CTAs).
 constexpr size_t kMmaSmPool = 220 * 1024;
 
-// Measured on B200 (m = 2..16, against the GEMV / int8 / fp16 packed routes):
-// the warp-MMA kernel wins on layers of at most half an SM count of column
-// tiles, where K is split many ways (7B QKV m = 2: 11.4 -> 9.4 us, o 10.7 ->
-// 8.2, down 23.6 -> 20.9, BASELINE config 1 at m = 16: 8.3 -> 6.4); on wider
-// layers it is issue-bound and the int8 path stays ahead (3584 x 18944, 148
-// tiles, m = 16: 21.6 vs 18.8 us; 7B gate_up: 41 vs 31 us).
+// Measured on B200 (m = 2..16, against the int8 / fp16 packed routes): the
+// warp-MMA kernel wins on layers of at most half an SM count of column tiles,
+// where K is split many ways (7B QKV m = 2: 11.4 -> 9.4 us, o 10.7 -> 8.2,
+// down 23.6 -> 19.4, BASELINE config 1 at m = 16: 8.3 -> 6.3), and on wider
+// layers with one token tile (7B gate_up m = 2: 31.4 -> 30.2 us); with two
+// token tiles it is issue-bound there and the int8 path stays ahead
+// (3584 x 18944, 148 tiles, m = 16: 20.4 vs 18.7 us; 7B gate_up: 36.7 vs
+// 31.6 us).
 bool mma_eligible(int64_t m, int64_t k, int64_t n, int64_t g, int sms) {
   return m >= kMmaMinRows && m <= lvb::awqm::kMaxRows && g % 32 == 0 && k % g == 0 && k % 64 == 0 && n % 128 == 0 &&
-         n / 128 <= sms / 2;
+         (n / 128 <= sms / 2 || m <= 8);
 }
 
 struct MmaPlan {
@@ -631,7 +634,7 @@ int launch_awq_mma(const MmaPlan &plan, const PackedShape &sh, const uint16_t *x
                    const uint32_t *groups, const uint16_t *bias, uint16_t *y, int64_t m, int64_t n, int64_t g,
                    uint8_t *ws, int dev, cudaStream_t stream, int64_t x_stride) {
   static bool smem_done[kMaxDevices] = {false};
-  auto kernel = lvb::awqm::awq_mma_kernel<NT>;
+  auto kernel = lvb::awqm::awq_mma_kernel<NT, kMmaColsPerWarp>;
   int rc = ensure_smem(kernel, static_cast<int>(kMmaSmPool), dev, smem_done);
   if (rc != LVB_OK) return rc;
   lvb::awqm::MmaParams p{};
@@ -653,7 +656,7 @@ int launch_awq_mma(const MmaPlan &plan, const PackedShape &sh, const uint16_t *x
   p.groups_per_split = plan.gps;
   p.stages = plan.stages;
   cudaError_t e = launch_pdl(kernel, dim3(static_cast<unsigned>(sh.n_tiles), static_cast<unsigned>(plan.splits)),
-                             dim3(lvb::awqm::kCtaThreads), plan.smem, stream, p);
+                             dim3(lvb::awqm::MmaWarps<kMmaColsPerWarp>::kCtaThreads), plan.smem, stream, p);
   if (e != cudaSuccess) return cuda_fail(e, "awq_mma_kernel launch");
   return LVB_OK;
 }

@@ -227,14 +227,15 @@ def _integer_path(m: int, k: int, n: int, g: int) -> bool:
     """Whether the packed scheme applies the zero point and scale exactly for
     this shape (the dispatch rules of lvb_awq_linear_packed on a 148-SM
     B200): the one-row GEMV at m = 1 and the int8 tensor-core path at m =
-    2..16 on layers of more than 74 column tiles (groups of 128 / 256, >= 8
-    MiB of codes).  The warp-MMA kernel (m = 2..16, narrower layers) and the
-    fp16 packed kernel multiply the reference's fp16-rounded weight."""
+    9..16 on layers of more than 74 column tiles (groups of 128 / 256, >= 8
+    MiB of codes).  The warp-MMA kernel (m = 2..8, and m = 9..16 on narrower
+    layers) and the fp16 packed kernel multiply the reference's fp16-rounded
+    weight."""
 
     packed = n % 128 == 0 and k % 64 == 0
     if packed and m == 1 and g % 32 == 0:
         return True
-    return packed and m <= 16 and n // 128 > 148 // 2 and g in (128, 256) and k * n // 2 >= 8 << 20
+    return packed and 9 <= m <= 16 and n // 128 > 148 // 2 and g in (128, 256) and k * n // 2 >= 8 << 20
 
 
 def _assert_fp16_output_close(actual: np.ndarray, expected: np.ndarray, what, x=None, weights=None) -> None:
@@ -399,6 +400,26 @@ def test_silu_mul_linear_matches_oracle(m):
     qw, qz, sc, gu_dev = _gpu(qweight, qzeros, scales, gate_up)
     op = B200AWQScheme().prepare(qw, qz, sc, g, None)
     y = op.silu_mul_linear(gu_dev)
+    torch.cuda.synchronize()
+    assert _native.device_error() == 0
+    _assert_fp16_output_close(y.float().cpu().numpy(), expected, m, act, (qweight, qzeros, scales, g))
+
+
+@pytest.mark.parametrize("m", [9, 16])
+def test_silu_mul_linear_on_the_int8_route(m):
+    """A down projection wider than 74 column tiles with 9..16 rows (10 MB of
+    codes, groups of 128) takes the int8 path with the SiLU-mul in its limb
+    prologue; against the fp32 oracle on the fp16-rounded activation."""
+
+    k, n, g = 2048, 9728, 128
+    qweight, qzeros, scales = oawq.random_checkpoint(k, n, g, seed=m + 401)
+    rng = np.random.default_rng(m + 19)
+    gate_up = rng.standard_normal((m, 2 * k)).astype(np.float16)
+    gu = torch.from_numpy(gate_up).float()
+    act = (torch.nn.functional.silu(gu[:, :k]) * gu[:, k:]).half().numpy()
+    expected = oawq.linear_fp32(act, qweight, qzeros, scales, g, None)
+    qw, qz, sc, gu_dev = _gpu(qweight, qzeros, scales, gate_up)
+    y = B200AWQScheme().prepare(qw, qz, sc, g, None).silu_mul_linear(gu_dev)
     torch.cuda.synchronize()
     assert _native.device_error() == 0
     _assert_fp16_output_close(y.float().cpu().numpy(), expected, m, act, (qweight, qzeros, scales, g))

@@ -72,7 +72,7 @@ def _check(m, k, n, g, seed):
 
 SHAPES = [
     (3584, 4608, 128),   # 7B merged QKV: many splits
-    (3584, 37888, 128),  # 7B merged gate_up: wider than 74 tiles, so the int8 path / GEMV (dispatch boundary)
+    (3584, 37888, 128),  # 7B merged gate_up: wider than 74 tiles, the int8 path from m = 9 (dispatch boundary)
     (18944, 3584, 128),  # 7B down: 28 tiles, long k
     (896, 4864, 128),
     (512, 1024, 64),
