@@ -165,8 +165,7 @@ LVB_API int lvb_awq_pack(const int32_t *qweight, const int32_t *qzeros, const ui
 /* y[m, n] = x[m, :k] @ W + bias from the packed layout, any m.  Same
  * arithmetic and requirements as lvb_awq_linear (the one-row GEMV and the
  * int8 decode path apply the zero point and scale exactly instead of rounding
- * W to fp16).  Decode batches of 2..8 rows, and of 9..16 rows on layers of
- * at most half an SM count of 128-column tiles, run the warp-MMA kernel.  The split-K plan uses at
+ * W to fp16).  Decode batches of 2..16 rows run the warp-MMA kernel.  The split-K plan uses at
  * most `workspace_bytes` of workspace (NULL or 0: no split), so a smaller
  * workspace only costs speed; lvb_awq_workspace_bytes gives the size of the
  * fastest plan.  `codes` may be the checkpoint's own qweight buffer
@@ -187,8 +186,9 @@ LVB_API int lvb_awq_linear_packed(const uint16_t *x, const void *codes, const vo
  * _qwen2_kernels.py:45-64).  Covers the decode batches: one row (the GEMV
  * builds fp16(silu(gate) * up) in its prologue), the shapes of the warp-MMA
  * kernel (the activation goes through the workspace: lvb_silu_mul, then the
- * warp-MMA projection), and the int8 path
- * (m <= 16, groups of 128 / 256); other shapes return LVB_ERR_UNSUPPORTED and
+ * warp-MMA projection), and the int8 path when the workspace cannot hold
+ * the warp-MMA plan (m <= 16, groups of 128 / 256); other shapes return
+ * LVB_ERR_UNSUPPORTED and
  * the caller runs lvb_silu_mul + lvb_awq_linear_packed. */
 LVB_API int lvb_awq_silu_linear_packed(const uint16_t *gate_up, int64_t gate_up_stride, const void *codes,
                                        const void *groups, const uint16_t *bias, uint16_t *y, int64_t m, int64_t k,

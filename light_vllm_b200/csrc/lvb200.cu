@@ -558,17 +558,16 @@ constexpr size_t kMmaMaxSmem = 72 * 1024;  // with the minimum ring: three CTAs 
 // 1 KB of static shared memory per CTA, for up to four CTAs).
 constexpr size_t kMmaSmPool = 220 * 1024;
 
-// Measured on B200 (m = 2..16, against the int8 / fp16 packed routes): the
-// warp-MMA kernel wins on layers of at most half an SM count of column tiles,
-// where K is split many ways (7B QKV m = 2: 11.4 -> 9.4 us, o 10.7 -> 8.2,
-// down 23.6 -> 19.4, BASELINE config 1 at m = 16: 8.3 -> 6.3), and on wider
-// layers with one token tile (7B gate_up m = 2: 31.4 -> 30.2 us); with two
-// token tiles it is issue-bound there and the int8 path stays ahead
-// (3584 x 18944, 148 tiles, m = 16: 20.4 vs 18.7 us; 7B gate_up: 36.7 vs
-// 31.6 us).
+// Measured on B200 (m = 2..16, rotating weight copies > L2), against the
+// int8 tensor-core path and the fp16 packed kernel: 7B QKV m = 2 11.4 -> 9.1
+// us, o 10.7 -> 8.0, down 23.6 -> 18.3 (m = 16: 24.0 -> 21.0), gate_up
+// 31.4 -> 27.4 (m = 16: a tie, 31.6), BASELINE config 1 at m = 16 8.3 ->
+// 6.4; in the 7B B = 16 decode step, where the int8 path also needs its limb
+// launch, 2.84 -> 2.76 ms.  The int8 path remains the fallback when the
+// caller's workspace cannot hold this kernel's split-K buffers.
 bool mma_eligible(int64_t m, int64_t k, int64_t n, int64_t g, int sms) {
-  return m >= kMmaMinRows && m <= lvb::awqm::kMaxRows && g % 32 == 0 && k % g == 0 && k % 64 == 0 && n % 128 == 0 &&
-         (n / 128 <= sms / 2 || m <= 8);
+  (void)sms;
+  return m >= kMmaMinRows && m <= lvb::awqm::kMaxRows && g % 32 == 0 && k % g == 0 && k % 64 == 0 && n % 128 == 0;
 }
 
 struct MmaPlan {

@@ -225,17 +225,11 @@ def test_ragged_shapes_keep_the_checkpoint_layout():
 
 def _integer_path(m: int, k: int, n: int, g: int) -> bool:
     """Whether the packed scheme applies the zero point and scale exactly for
-    this shape (the dispatch rules of lvb_awq_linear_packed on a 148-SM
-    B200): the one-row GEMV at m = 1 and the int8 tensor-core path at m =
-    9..16 on layers of more than 74 column tiles (groups of 128 / 256, >= 8
-    MiB of codes).  The warp-MMA kernel (m = 2..8, and m = 9..16 on narrower
-    layers) and the fp16 packed kernel multiply the reference's fp16-rounded
-    weight."""
+    this shape (the dispatch rules of lvb_awq_linear_packed): the one-row GEMV
+    at m = 1.  The warp-MMA kernel (m = 2..16) and the fp16 packed kernel
+    multiply the reference's fp16-rounded weight."""
 
-    packed = n % 128 == 0 and k % 64 == 0
-    if packed and m == 1 and g % 32 == 0:
-        return True
-    return packed and 9 <= m <= 16 and n // 128 > 148 // 2 and g in (128, 256) and k * n // 2 >= 8 << 20
+    return n % 128 == 0 and k % 64 == 0 and m == 1 and g % 32 == 0
 
 
 def _assert_fp16_output_close(actual: np.ndarray, expected: np.ndarray, what, x=None, weights=None) -> None:
@@ -406,10 +400,10 @@ def test_silu_mul_linear_matches_oracle(m):
 
 
 @pytest.mark.parametrize("m", [9, 16])
-def test_silu_mul_linear_on_the_int8_route(m):
-    """A down projection wider than 74 column tiles with 9..16 rows (10 MB of
-    codes, groups of 128) takes the int8 path with the SiLU-mul in its limb
-    prologue; against the fp32 oracle on the fp16-rounded activation."""
+def test_silu_mul_linear_on_a_wide_layer(m):
+    """A down projection of 76 column tiles with 9..16 rows (10 MB of codes,
+    groups of 128): lvb_silu_mul into the workspace, then the warp-MMA
+    projection; against the fp32 oracle on the fp16-rounded activation."""
 
     k, n, g = 2048, 9728, 128
     qweight, qzeros, scales = oawq.random_checkpoint(k, n, g, seed=m + 401)

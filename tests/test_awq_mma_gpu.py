@@ -4,7 +4,7 @@ CPU oracle.
 lvb_awq_linear_packed runs it for 2..16 token rows over the packed layout:
 one token tile (m <= 8) or two (m <= 16), one split or many, groups of 32 /
 64 / 128 / 256 and per-column groups, stages cut short at the end of a range
-(runs per range not a multiple of four), with and without bias.  The kernel
+(runs per range not a multiple of eight), with and without bias.  The kernel
 multiplies the reference's fp16-rounded weight (modeling/quantization/
 awq.py:433-450) by the fp16 x with fp32 accumulation, so the tolerance is
 the north-star max-abs 2e-2 and rel-L2 1e-3 against the fp64-accumulated
@@ -72,13 +72,13 @@ def _check(m, k, n, g, seed):
 
 SHAPES = [
     (3584, 4608, 128),   # 7B merged QKV: many splits
-    (3584, 37888, 128),  # 7B merged gate_up: wider than 74 tiles, the int8 path from m = 9 (dispatch boundary)
+    (3584, 37888, 128),  # 7B merged gate_up: one split per tile
     (18944, 3584, 128),  # 7B down: 28 tiles, long k
     (896, 4864, 128),
     (512, 1024, 64),
     (1024, 256, 256),
     (896, 256, 896),     # per-column groups
-    (192, 384, 32),      # six runs per range: the last stage holds two
+    (192, 384, 32),      # six runs per range: one stage cut short
 ]
 
 

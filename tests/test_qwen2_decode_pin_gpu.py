@@ -13,7 +13,7 @@ Its MLP projections hold 16 and 8 MiB of int4 codes, so the runner's decode
 steps take the paths of the large models: one request runs the one-row dp4a
 GEMV for every projection (the down projection with the SiLU-mul fused into
 it); four requests run the warp-MMA kernel for every projection (the down
-projection after lvb_silu_mul), the routes of the 7B model at 2..8 rows.
+projection after lvb_silu_mul), the routes of the 7B model at 2..16 rows.
 
 The runner is fed the reference's tokens (teacher forcing) and must pick the
 reference's token at every step whose reference top-2 logit margin is at
