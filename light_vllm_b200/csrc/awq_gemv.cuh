@@ -46,9 +46,9 @@ namespace awqg {
 
 constexpr int kThreads = 128;      // consumer threads: one output column each
 constexpr int kCtaThreads = 160;   // + one producer warp
-constexpr int kStageRuns = 4;      // 32-k runs per stage (8 KB of codes)
-constexpr int kStages = 5;         // 40 KB ring: 4 CTAs still fit an SM; measured best of 4 / 5 / 6
-                                   // (7B gate_up m = 1: 19.0 / 17.7 / 24.7 us)
+constexpr int kStageRuns = 8;      // 32-k runs per stage (16 KB of codes)
+constexpr int kStages = 2;         // 32 KB ring.  B200, 7B B = 1 decode step: 2.15 ms with five
+                                   // 8 KB stages, 2.10 with two 16 KB stages, 2.30 with three
 constexpr int kStageBytes = kStageRuns * 128 * 16;
 constexpr int kMaxM = 4;
 using awqi8::kLimbs;
